@@ -1,0 +1,263 @@
+"""Benchmark: TGN train events/sec on N GPUs of one node.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+    torchrun --nnodes=1 --nproc-per-node N --master-addr 127.0.0.1 --master-port P bench.py --gpus N ...
+
+Workload: synthetic unipartite event stream of the config's shape (1,140,149 nodes,
+7,833,140 events, Zipf(1.2) endpoints, 20% repeat interactions, sorted uniform
+timestamps over [0, 1.9e8] s, 16-dim N(0,1) edge features), random-init TGN
+(memory/time/embedding 100, 2 heads, 10 most-recent neighbours, 1 mailbox slot,
+1 negative per positive), 600 events per rank per step (weak scaling).
+
+Every step is a full training step (sampling, memory update, mailbox write,
+attention forward/backward, link loss, gradient all-reduce for N > 1, Adam).
+``value`` is device-timed (CUDA events, W untimed warm-up steps, barrier +
+synchronize on both sides, max over ranks); ``e2e`` times the public
+``train_step`` API including the host->device copy of each batch from pinned
+memory and the device->host read of the loss, metrics and predictions.
+Rank 0 prints one JSON line.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import sys
+import threading
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+METRIC = "TGN train events/sec & MPNN-LSTM snapshots/sec, 1/2/4/8 B200, max over ranks"
+MODEL_NAME = "TGN (1-layer temporal attention, 2 heads), CTDG online + async_sync"
+
+
+def _args():
+    p = argparse.ArgumentParser()
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=200)
+    p.add_argument("--warmup", type=int, default=10)
+    p.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    p.add_argument("--events", type=int, default=7833140, help="stream length (config: 7,833,140)")
+    p.add_argument("--batch", type=int, default=600, help="events per rank per step")
+    return p.parse_args()
+
+
+class ClockSampler:
+    """Samples SM clock and throttle reasons of this process's GPU through NVML."""
+
+    def __init__(self, device_index: int):
+        self.samples: list[tuple[int, int]] = []
+        self.reasons: set[str] = set()
+        self.max_mhz = None
+        self._stop = threading.Event()
+        self._h = None
+        try:
+            import pynvml
+            import torch
+
+            pynvml.nvmlInit()
+            props = torch.cuda.get_device_properties(device_index)
+            bus = f"{props.pci_domain_id:08X}:{props.pci_bus_id:02X}:{props.pci_device_id:02X}.0"
+            self._h = pynvml.nvmlDeviceGetHandleByPciBusId(bus)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self._h, pynvml.NVML_CLOCK_SM)
+            self._nv = pynvml
+        except Exception:
+            self._h = None
+
+    def _run(self):
+        nv = self._nv
+        names = {
+            "hw_slowdown": getattr(nv, "nvmlClocksEventReasonHwSlowdown", 0x8),
+            "sw_thermal_slowdown": getattr(nv, "nvmlClocksEventReasonSwThermalSlowdown", 0x20),
+            "hw_thermal_slowdown": getattr(nv, "nvmlClocksEventReasonHwThermalSlowdown", 0x40),
+            "sw_power_cap": getattr(nv, "nvmlClocksEventReasonSwPowerCap", 0x4),
+        }
+        while not self._stop.is_set():
+            try:
+                mhz = nv.nvmlDeviceGetClockInfo(self._h, nv.NVML_CLOCK_SM)
+                mask = nv.nvmlDeviceGetCurrentClocksEventReasons(self._h)
+                self.samples.append((mhz, mask))
+                for n, bit in names.items():
+                    if mask & bit:
+                        self.reasons.add(n)
+            except Exception:
+                pass
+            time.sleep(0.05)
+
+    def __enter__(self):
+        if self._h is not None:
+            self._t = threading.Thread(target=self._run, daemon=True)
+            self._t.start()
+        return self
+
+    def __exit__(self, *exc):
+        self._stop.set()
+        if self._h is not None:
+            self._t.join(timeout=2)
+
+    def summary(self) -> dict:
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": ["unavailable"]}
+        return {"sm_mhz": statistics.median(s[0] for s in self.samples), "sm_max_mhz": self.max_mhz,
+                "reasons": sorted(self.reasons)}
+
+
+def _reference_arm(args):
+    """Run the unmodified reference from baseline/_ref through its own API."""
+    ref = ROOT / "baseline" / "_ref"
+    reason = None
+    if not (ref / "starry_unigraph").exists():
+        reason = "reference not installed under baseline/_ref"
+    else:
+        try:
+            import dgl  # noqa: F401
+        except Exception:
+            reason = ("reference requires DGL (its package import chain imports dgl), which is not "
+                      "installed and cannot be installed offline on this image")
+    if reason is None:
+        reason = "reference CTDG benchmark driver not wired"
+    if int(os.environ.get("RANK", "0")) == 0:
+        print(json.dumps({"impl": "reference", "unavailable": reason}), flush=True)
+    return 0
+
+
+def main():
+    args = _args()
+    if args.impl == "reference":
+        return _reference_arm(args)
+    sys.path.insert(0, str(ROOT))
+    import torch
+    import torch.distributed as dist
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local_rank)
+    from starry_unigraph import SchedulerSession
+    from starry_unigraph.ops import check_status
+
+    cfg = {
+        "model": {"name": "tgn", "family": "tgn", "task": "temporal_link_prediction", "hidden_dim": 100},
+        "data": {"root": "./data", "name": "tgn_large", "format": "synthetic",
+                 "synthetic": {"preset": "tgn_large", "num_events": args.events, "seed": 0}},
+        "train": {"epochs": 1, "batch_size": args.batch, "lr": 1e-4},
+        "runtime": {"device": "cuda", "cuda_graphs": True},
+        "ctdg": {"mailbox_slots": 1, "dim_time": 100, "num_head": 2, "dropout": 0.1, "att_dropout": 0.1,
+                 "async_sync": True},
+        "sampling": {"neighbor_limit": [10], "strategy": "recent", "history": 1},
+        "graph": {"partition": "round_robin"},
+        "dist": {"backend": "nccl", "timeout_s": 300},
+    }
+    session = SchedulerSession.from_config(cfg)
+    session.ctx.artifact_root = Path(os.environ.get("TMPDIR", "/tmp")) / f"su_bench_w{world}_r{rank}"
+    if world > 1:
+        from starry_unigraph.distributed import initialize_distributed
+
+        initialize_distributed(session.ctx.dist)
+    t_prep = time.perf_counter()
+    session.prepare_data()
+    session.build_runtime()
+    prep_s = time.perf_counter() - t_prep
+    rt = session.ctdg_session.online_runtime
+    eng = rt.engine
+    need = args.warmup + 2 * args.steps
+    batches = []
+    for b in rt.iter_batches("train", args.batch):
+        batches.append(b)
+        if len(batches) >= need:
+            break
+    if len(batches) < need:
+        raise SystemExit(f"stream too short: {len(batches)} batches < {need}")
+    for b in batches:  # the loader hands out pinned batches (one H2D copy each)
+        b.src, b.dst, b.ts, b.event_ids = (t.pin_memory() for t in (b.src, b.dst, b.ts, b.event_ids))
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    # warm-up (includes CUDA-graph capture)
+    for b in batches[: args.warmup]:
+        rt._engine_step(b, "train", True, want_outputs=False)
+    torch.cuda.synchronize()
+    check_status()
+
+    # ---- device-timed region
+    timed = batches[args.warmup: args.warmup + args.steps]
+    events = sum(b.size for b in timed)
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier()
+    torch.cuda.synchronize()
+    with ClockSampler(local_rank) as clocks:
+        start.record()
+        for b in timed:
+            rt._engine_step(b, "train", True, want_outputs=False)
+        end.record()
+        torch.cuda.synchronize()
+    barrier()
+    dev_ms = start.elapsed_time(end)
+    check_status()
+
+    # ---- end-to-end through the public per-step API (H2D of inputs, D2H of loss/metrics/predictions)
+    e2e_batches = batches[args.warmup + args.steps: args.warmup + 2 * args.steps]
+    e2e_events = sum(b.size for b in e2e_batches)
+    barrier()
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    last = None
+    for b in e2e_batches:
+        last = session.ctdg_session.train_step(b)
+    torch.cuda.synchronize()
+    e2e_s = time.perf_counter() - t0
+    barrier()
+
+    stats = torch.tensor([dev_ms, e2e_s, float(events), float(e2e_events)], dtype=torch.float64, device="cuda")
+    if world > 1:
+        mx = stats[:2].clone()
+        dist.all_reduce(mx, op=dist.ReduceOp.MAX)
+        sm = stats[2:].clone()
+        dist.all_reduce(sm, op=dist.ReduceOp.SUM)
+        stats = torch.cat([mx, sm])
+    dev_ms, e2e_s, events_all, e2e_events_all = stats.tolist()
+    value = events_all / (dev_ms / 1000.0)
+    e2e = e2e_events_all / e2e_s
+    per_step_launches = eng.launches_per_step(train=True) if hasattr(eng, "launches_per_step") else None
+    if rank == 0:
+        bpe = 8 + 8 + 4 + 8  # src, dst, ts, eid per event
+        line = {
+            "metric": "TGN train events/sec",
+            "value": value,
+            "unit": "events/s",
+            "n_gpus": world,
+            "steps": args.steps,
+            "warmup": args.warmup,
+            "ms_per_step": dev_ms / args.steps,
+            "higher_is_better": True,
+            "scaling": "weak",
+            "vs_baseline": None,
+            "dtype": "bf16",
+            "data": "synthetic (random-init weights)",
+            "config": {"model": MODEL_NAME, "global_batch": args.batch * world, "seq_len": None,
+                       "parallelism": f"dp{world}+memory-partition", "events": args.events, "nodes": 1140149,
+                       "fanout": 10, "mailbox_slots": 1, "dims": "memory=time=embed=100",
+                       "l2": "working set (memory 456 MB, mailbox 985 MB, edge features 500 MB) > 126 MB L2",
+                       "baseline_metric": METRIC},
+            "clocks": clocks.summary(),
+            "e2e": {"value": e2e, "unit": "events/s", "h2d_bytes_per_step": args.batch * bpe + 4,
+                    "d2h_bytes_per_step": 16 + 4 * args.batch},
+            "gpu_launches": (per_step_launches * args.steps) if per_step_launches else None,
+            "prep_s": prep_s,
+            "last_loss": last["loss"] if last else None,
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        eng.reset_graphs()
+        from starry_unigraph.distributed import finalize_distributed
+
+        finalize_distributed(session.ctx.dist)
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

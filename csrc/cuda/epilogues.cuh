@@ -1,0 +1,170 @@
+// Model-specific GEMM epilogues (TGN memory updater, output projection with
+// LayerNorm, time-encoder gradient). Data members are host-visible so the
+// torch-side wrappers can fill them; device code is compiled by nvcc only.
+#pragma once
+
+#include "tc_gemm.cuh"
+
+namespace su {
+
+constexpr uint32_t kStreamAttDrop = 0xA77D0u;
+constexpr uint32_t kStreamOutDrop = 0x0D7D0u;
+
+// ---------------------------------------------------------------------------
+// GRU gates epilogue. Accumulator columns hold four blocks of DP columns:
+//   [ x W_ir^T + h W_hr^T | x W_iz^T + h W_hz^T | x W_in^T | h W_hn^T ]
+// (PyTorch GRU gate convention). Produces h' = (1 - z) * n + z * h.
+// ---------------------------------------------------------------------------
+struct EpiGRU {
+  int D = 0, DP = 0;
+  const float* b_ih = nullptr;   // [3D]
+  const float* b_hh = nullptr;   // [3D]
+  const float* hprev = nullptr;  // previous hidden rows (nullptr -> zeros)
+  const int64_t* hprev_index = nullptr;
+  int hprev_ld = 0;
+  float* hout = nullptr;         // dense output rows (optional)
+  int hout_ld = 0;
+  float* save_prev = nullptr;    // copy of the previous hidden rows (optional)
+  float* scatter = nullptr;      // memory table written at rows scatter_index[row] (optional)
+  const int64_t* scatter_index = nullptr;
+  int scatter_ld = 0;
+  float* scatter_ts = nullptr;   // memory_ts[scatter_index[row]] = *ts_value
+  const float* ts_value = nullptr;
+
+#ifdef __CUDACC__
+  __device__ __forceinline__ void operator()(int row, bool valid, int n0, uint32_t taddr, int /*tile_cols*/) const {
+    const float* hp = nullptr;
+    if (valid && hprev != nullptr) {
+      const int64_t hr = hprev_index ? hprev_index[row] : row;
+      if (hr >= 0) hp = hprev + hr * hprev_ld;
+    }
+    int64_t srow = -1;
+    if (valid && scatter != nullptr) srow = scatter_index[row];
+    for (int c0 = 0; c0 < DP; c0 += 16) {
+      float r[16], z[16], ni[16], nh[16];
+      tmem_ld16(taddr + c0, r);
+      tmem_ld16(taddr + DP + c0, z);
+      tmem_ld16(taddr + 2 * DP + c0, ni);
+      tmem_ld16(taddr + 3 * DP + c0, nh);
+      if (!valid) continue;
+#pragma unroll
+      for (int i = 0; i < 16; ++i) {
+        const int c = c0 + i;
+        if (c >= D) break;
+        const float h = hp ? hp[c] : 0.f;
+        const float rg = sigmoidf_(r[i] + b_ih[c] + b_hh[c]);
+        const float zg = sigmoidf_(z[i] + b_ih[D + c] + b_hh[D + c]);
+        const float ng = tanhf(ni[i] + b_ih[2 * D + c] + rg * (nh[i] + b_hh[2 * D + c]));
+        const float hn = (1.f - zg) * ng + zg * h;
+        if (save_prev) save_prev[(int64_t)row * D + c] = h;
+        if (hout) hout[(int64_t)row * hout_ld + c] = hn;
+        if (srow >= 0) scatter[srow * scatter_ld + c] = hn;
+      }
+    }
+    if (valid && srow >= 0 && scatter_ts != nullptr && n0 == 0) scatter_ts[srow] = *ts_value;
+  }
+#endif
+};
+
+
+// ---------------------------------------------------------------------------
+// output projection epilogue: dropout -> ReLU -> LayerNorm (row owned by thread)
+// ---------------------------------------------------------------------------
+struct EpiOutLN {
+  int Do = 0;
+  const float* bias = nullptr;
+  const float* gamma = nullptr;
+  const float* beta = nullptr;
+  float drop = 0.f;
+  uint64_t seed = 0;
+  const int64_t* step_ctr = nullptr;
+  const int* edge_total = nullptr;  // no sampled edge in the whole block -> zero output
+  float* out = nullptr;    // [rows, Do]
+  float* xsave = nullptr;  // post-ReLU pre-LN activations [rows, Do]
+  float* mean = nullptr;   // [rows]
+  float* rstd = nullptr;   // [rows]
+
+#ifdef __CUDACC__
+  __device__ __forceinline__ void operator()(int row, bool valid, int /*n0*/, uint32_t taddr, int /*tile_cols*/) const {
+    const uint64_t dseed = seed ^ (static_cast<uint64_t>(*step_ctr) * 0x9E3779B97F4A7C15ull);
+    float s1 = 0.f, s2 = 0.f;
+    float* xs = xsave + (int64_t)row * Do;
+    for (int c0 = 0; c0 < Do; c0 += 16) {
+      float v[16];
+      tmem_ld16(taddr + c0, v);
+      if (!valid) continue;
+#pragma unroll
+      for (int i = 0; i < 16; ++i) {
+        const int c = c0 + i;
+        if (c >= Do) break;
+        float x = v[i] + bias[c];
+        if (drop > 0.f) x = dropout_keep(dseed, (uint64_t)row * Do + c, kStreamOutDrop, drop) ? x / (1.f - drop) : 0.f;
+        x = fmaxf(x, 0.f);
+        xs[c] = x;
+        s1 += x;
+        s2 += x * x;
+      }
+    }
+    if (!valid) return;
+    if (edge_total != nullptr && *edge_total == 0) {
+      float* o = out + (int64_t)row * Do;
+      for (int c = 0; c < Do; ++c) o[c] = 0.f;
+      mean[row] = 0.f;
+      rstd[row] = 0.f;
+      return;
+    }
+    const float mu = s1 / Do;
+    const float var = fmaxf(s2 / Do - mu * mu, 0.f);
+    const float rs = rsqrtf(var + 1e-5f);
+    mean[row] = mu;
+    rstd[row] = rs;
+    float* o = out + (int64_t)row * Do;
+    for (int c = 0; c < Do; ++c) o[c] = (xs[c] - mu) * rs * gamma[c] + beta[c];
+  }
+#endif
+};
+
+
+// Time-encoder gradient epilogue: rows are edges (or roots with t = 0), columns
+// the time-encoding dims; acc = d(cos(w t + b)). Accumulates
+//   dw[c] += sum_rows -sin(w t + b) * t * acc,   db[c] += sum_rows -sin(w t + b) * acc.
+struct EpiTimeGrad {
+  int T = 0;
+  const float* w = nullptr;
+  const float* b = nullptr;
+  const float* t = nullptr;   // per-row time (nullptr -> 0)
+  const int* gcount = nullptr;
+  int group = 1;
+  const int* nrows_dev = nullptr;
+  float* dw = nullptr;
+  float* db = nullptr;
+
+#ifdef __CUDACC__
+  __device__ __forceinline__ void operator()(int row, bool valid, int n0, uint32_t taddr, int tile_cols) const {
+    if (valid && nrows_dev != nullptr && row >= *nrows_dev) valid = false;
+    if (valid && gcount != nullptr && (row % group) >= gcount[row / group]) valid = false;
+    const float tt = (valid && t != nullptr) ? t[row] : 0.f;
+    const int lim = min(T - n0, tile_cols);
+    for (int c0 = 0; c0 < lim; c0 += 16) {
+      float v[16];
+      tmem_ld16(taddr + c0, v);
+#pragma unroll
+      for (int i = 0; i < 16; ++i) {
+        const int c = n0 + c0 + i;
+        float gb = 0.f;
+        if (valid && c < T) gb = -sinf(fmaf(w[c], tt, b[c])) * v[i];
+        float gw = gb * tt;
+        gb = warp_sum(gb);
+        gw = warp_sum(gw);
+        if ((threadIdx.x & 31) == 0 && c < T) {
+          atomicAdd(&db[c], gb);
+          if (t != nullptr) atomicAdd(&dw[c], gw);
+        }
+      }
+    }
+  }
+#endif
+};
+
+
+}  // namespace su

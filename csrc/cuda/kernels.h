@@ -1,0 +1,99 @@
+// Declarations shared by the CUDA translation units (nvcc) and the torch-side
+// wrappers (g++). Nothing here depends on torch headers.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "epilogues.cuh"
+#include "tc_gemm.cuh"
+
+namespace su {
+
+// ---- device bookkeeping -----------------------------------------------------
+int* device_status_ptr(int device);  // per-device status word (bounded waits, bad indices)
+int num_sms(int device);
+
+// ---- tcgen05 GEMM entry points (one overload per producer/epilogue combo) ---
+void gemm(const SegSource& a, const WeightSource& b, const EpiLinear& e, const GemmShape& sh, cudaStream_t st);
+void gemm(const SegSource& a, const WeightTSource& b, const EpiLinear& e, const GemmShape& sh, cudaStream_t st);
+void gemm(const TransposedSource& a, const TransposedSource& b, const EpiWeightGrad& e, const GemmShape& sh,
+          cudaStream_t st);
+void gemm(const SegSource& a, const WeightSource& b, const EpiGRU& e, const GemmShape& sh, cudaStream_t st);
+void gemm(const SegSource& a, const WeightSource& b, const EpiOutLN& e, const GemmShape& sh, cudaStream_t st);
+void gemm(const SegSource& a, const WeightTSource& b, const EpiTimeGrad& e, const GemmShape& sh, cudaStream_t st);
+
+// ---- TGN step kernels --------------------------------------------------------
+struct PrepArgs {
+  const int64_t* src;
+  const int64_t* dst;
+  const float* ts;
+  const int* n_ev;
+  int bmax;
+  int rmax;
+  const int64_t* neg_pool;
+  int64_t pool_size;
+  int* stamp;          // [num_nodes]
+  int* node2root;      // [num_nodes]
+  int64_t* step_ctr;   // [1]
+  uint64_t seed;
+  int64_t* roots;      // [rmax]
+  int* n_roots;        // [1]
+  int* src_idx;        // [bmax]
+  int* dst_idx;        // [bmax]
+  int64_t* neg;        // [bmax]
+  int* neg_idx;        // [bmax]
+  float* ts_max;       // [1]
+  int64_t* root_ts;    // [1]  (int64-truncated max timestamp, sampler query time)
+  unsigned long long* win_key;  // [2 * rmax]
+  int* win;            // [2 * rmax]  event index of the last message (src pass, dst pass)
+  int* cnt;            // [2 * rmax]
+  int* status;
+};
+
+void launch_tgn_prep(dim3 grid, dim3 block, cudaStream_t st, PrepArgs a);
+void launch_tgn_sample(dim3 grid, dim3 block, cudaStream_t st, const int64_t* __restrict__ roots, const int* __restrict__ n_roots, int rmax,
+                                  const int64_t* __restrict__ root_ts_scalar, const int64_t* __restrict__ root_ts_vec,
+                                  const int64_t* __restrict__ rowptr, const int64_t* __restrict__ nbr,
+                                  const int64_t* __restrict__ eid, const int64_t* __restrict__ ets, int k, int policy,
+                                  uint64_t seed, const int64_t* __restrict__ step_ctr, int64_t* __restrict__ out_nbr,
+                                  int64_t* __restrict__ out_eid, float* __restrict__ out_dt,
+                                  int* __restrict__ out_cnt, int* __restrict__ edge_total);
+void launch_tgn_mailbox(dim3 grid, dim3 block, cudaStream_t st, const int64_t* __restrict__ roots, const int* __restrict__ n_roots, int rmax,
+                                   const int* __restrict__ win, const int* __restrict__ cnt,
+                                   const int* __restrict__ src_idx, const int* __restrict__ dst_idx,
+                                   const int64_t* __restrict__ ev_eid, const float* __restrict__ ev_ts,
+                                   const float* __restrict__ mem_prev, int D, const float* __restrict__ efeat,
+                                   int efeat_ld, int e_raw, int E, float* __restrict__ mailbox,
+                                   float* __restrict__ mailbox_ts, int64_t* __restrict__ next_pos, int K);
+void launch_tgn_attn_fwd(dim3 grid, dim3 block, cudaStream_t st, const float* __restrict__ Q, const float* __restrict__ KV,
+                                    const int* __restrict__ cnt, const int* __restrict__ n_roots, int rmax, int k,
+                                    int Do, int H, float att_drop, uint64_t seed, const int64_t* __restrict__ step_ctr,
+                                    float* __restrict__ att_p, float* __restrict__ agg);
+void launch_tgn_attn_bwd(dim3 grid, dim3 block, cudaStream_t st, const float* __restrict__ Q, const float* __restrict__ KV,
+                                    const float* __restrict__ att_p, const float* __restrict__ dagg,
+                                    const int* __restrict__ cnt, const int* __restrict__ n_roots, int rmax, int k,
+                                    int Do, int H, float att_drop, uint64_t seed, const int64_t* __restrict__ step_ctr,
+                                    float* __restrict__ dKV, float* __restrict__ dQ);
+void launch_tgn_out_bwd(dim3 grid, dim3 block, cudaStream_t st, const float* __restrict__ dout, const float* __restrict__ xsave,
+                                   const float* __restrict__ mean, const float* __restrict__ rstd,
+                                   const float* __restrict__ gamma, const int* __restrict__ n_roots, int rmax, int Do,
+                                   float drop, uint64_t seed, const int64_t* __restrict__ step_ctr,
+                                   const int* __restrict__ edge_total, float* __restrict__ dpre,
+                                   float* __restrict__ dgamma, float* __restrict__ dbeta);
+void launch_tgn_link(dim3 grid, dim3 block, cudaStream_t st, const float* __restrict__ P, const int* __restrict__ src_idx,
+                                const int* __restrict__ dst_idx, const int* __restrict__ neg_idx,
+                                const int* __restrict__ n_ev, int bmax, int D, const float* __restrict__ b_dst,
+                                const float* __restrict__ w_out, const float* __restrict__ b_out, int need_grad,
+                                float* __restrict__ scores, float* __restrict__ loss, float* __restrict__ dP,
+                                float* __restrict__ g_w_out, float* __restrict__ g_b_out, float* __restrict__ g_b_dst);
+void launch_tgn_metrics(dim3 grid, dim3 block, cudaStream_t st, const float* __restrict__ scores,
+                                                           const int* __restrict__ n_ev, int bmax,
+                                                           float* __restrict__ out);
+
+// ---- optimiser ---------------------------------------------------------------
+void launch_adam_flat(cudaStream_t st, int blocks, float* p, const float* g, float* m, float* v, int64_t n,
+                      int64_t* step, unsigned int* done, float lr, float b1, float b2, float eps, float wd,
+                      float grad_scale);
+
+}  // namespace su

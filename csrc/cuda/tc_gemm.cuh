@@ -1,0 +1,600 @@
+// Generic tcgen05 (5th-generation tensor core) GEMM for sm_100a with fused
+// operand producers and pluggable epilogues.
+//
+//   D[M, N] = A[M, K] . B[N, K]^T      (bf16 operands, fp32 accumulate in TMEM)
+//
+// Operands are never materialised in global memory in bf16: producer warps
+// evaluate them on the fly from "sources" (gather by index, concatenation of
+// column segments, cosine time encoding, peer-GPU shards, transposed views)
+// and write them into shared memory in the canonical K-major no-swizzle UMMA
+// layout (core matrices of 8 rows x 16 bytes). One elected thread issues
+// tcgen05.mma (M = 128, N = BN per instruction, NSUB instructions side by side)
+// accumulating into TMEM; tcgen05.commit releases shared-memory stages and
+// signals the accumulator. The four producer warps then act as the epilogue:
+// each thread owns one TMEM lane (= one output row), reads its accumulator
+// columns with tcgen05.ld and applies the epilogue functor (bias, activation,
+// recurrent-cell gates, scatter, atomic split-K accumulation, ...).
+//
+// Warp roles (160 threads):
+//   warps 0-3 : operand producers, then epilogue for the same tile
+//   warp  4   : TMEM allocator + MMA issuer (lane 0)
+//
+// Every wait is bounded (common.cuh); on timeout the CTA records a status code,
+// drains its in-flight tensor-core work and frees TMEM before returning.
+#pragma once
+
+#include "common.cuh"
+
+namespace su {
+
+constexpr int kBM = 128;          // rows per tile (UMMA M)
+constexpr int kBK = 64;           // K elements per pipeline stage (4 UMMA k-steps of 16)
+constexpr int kStages = 2;
+constexpr int kGemmThreads = 160;
+constexpr int kMaxSeg = 4;
+constexpr int kMaxBlk = 4;
+
+// Byte offset of the 16-byte vector (row r, K-vector kv) inside a stage tile
+// laid out as 8-row groups of (kBK / 8) core matrices of 128 bytes each.
+#ifdef __CUDACC__
+__device__ __forceinline__ uint32_t tile_vec_off(int r, int kv) {
+  return static_cast<uint32_t>((r >> 3) * 1024 + kv * 128 + (r & 7) * 16);
+}
+
+#endif  // __CUDACC__
+
+// ---------------------------------------------------------------------------
+// Activation sources: row-wise concatenation of column segments
+// ---------------------------------------------------------------------------
+enum SegKind : int {
+  kSegF32 = 0,      // fp32 matrix rows (optionally gathered through an int64 index)
+  kSegBF16 = 1,     // bf16 matrix rows (optionally gathered)
+  kSegTime = 2,     // cos(w[c] * t[row] + b[c]) time encoding (t == nullptr -> t = 0)
+  kSegOnes = 3,     // a single constant-1 column (bias trick for weight gradients)
+  kSegSharded = 4,  // fp32 rows owned by peer GPUs: peers[owner[id]] + lrow[id] * ld
+  kSegZero = 5,     // zero padding
+};
+
+struct ASeg {
+  int kind = kSegZero;
+  int kpad = 0;    // padded width in the K space (multiple of 8)
+  int width = 0;   // valid columns
+  int ld = 0;      // row stride (elements)
+  int col0 = 0;    // first column
+  int vec = 0;     // 1 if 16-byte vector loads are legal for this segment
+  const void* ptr = nullptr;
+  const int64_t* index = nullptr;    // row -> source row (nullptr: identity); < 0 -> zeros
+  const float* tdt = nullptr;        // time-encoding input per row
+  const float* tw = nullptr;
+  const float* tb = nullptr;
+  const float* const* peers = nullptr;  // sharded: per-rank base pointers
+  const int* owner = nullptr;           // sharded: owning rank per global id
+  const int64_t* lrow = nullptr;        // sharded: row inside the owner's shard
+};
+
+#ifdef __CUDACC__
+__device__ __forceinline__ const float* seg_row_f32(const ASeg& g, int row) {
+  int64_t r = g.index ? g.index[row] : row;
+  if (r < 0) return nullptr;
+  if (g.kind == kSegSharded) {
+    const int o = g.owner ? g.owner[r] : 0;
+    const int64_t lr = g.lrow ? g.lrow[r] : r;
+    return g.peers[o] + lr * g.ld + g.col0;
+  }
+  return static_cast<const float*>(g.ptr) + r * g.ld + g.col0;
+}
+
+__device__ __forceinline__ void seg_fill8(const ASeg& g, int row, int c, float (&f)[8]) {
+  switch (g.kind) {
+    case kSegF32:
+    case kSegSharded: {
+      const float* p = seg_row_f32(g, row);
+      if (p == nullptr) return;
+      if (g.vec && c + 8 <= g.width) {
+        const float4 a = *reinterpret_cast<const float4*>(p + c);
+        const float4 b = *reinterpret_cast<const float4*>(p + c + 4);
+        f[0] = a.x; f[1] = a.y; f[2] = a.z; f[3] = a.w;
+        f[4] = b.x; f[5] = b.y; f[6] = b.z; f[7] = b.w;
+      } else {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) f[i] = (c + i < g.width) ? p[c + i] : 0.f;
+      }
+      break;
+    }
+    case kSegBF16: {
+      int64_t r = g.index ? g.index[row] : row;
+      if (r < 0) return;
+      const __nv_bfloat16* p = static_cast<const __nv_bfloat16*>(g.ptr) + r * g.ld + g.col0;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) f[i] = (c + i < g.width) ? __bfloat162float(p[c + i]) : 0.f;
+      break;
+    }
+    case kSegTime: {
+      const float t = g.tdt ? g.tdt[row] : 0.f;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) f[i] = (c + i < g.width) ? cosf(fmaf(g.tw[c + i], t, g.tb[c + i])) : 0.f;
+      break;
+    }
+    case kSegOnes:
+      if (c == 0) f[0] = 1.f;
+      break;
+    default:
+      break;
+  }
+}
+
+__device__ __forceinline__ float seg_load1(const ASeg& g, int row, int c) {
+  if (c >= g.width) return 0.f;
+  switch (g.kind) {
+    case kSegF32:
+    case kSegSharded: {
+      const float* p = seg_row_f32(g, row);
+      return p ? p[c] : 0.f;
+    }
+    case kSegBF16: {
+      int64_t r = g.index ? g.index[row] : row;
+      if (r < 0) return 0.f;
+      return __bfloat162float(static_cast<const __nv_bfloat16*>(g.ptr)[r * g.ld + g.col0 + c]);
+    }
+    case kSegTime: {
+      const float t = g.tdt ? g.tdt[row] : 0.f;
+      return cosf(fmaf(g.tw[c], t, g.tb[c]));
+    }
+    case kSegOnes:
+      return c == 0 ? 1.f : 0.f;
+    default:
+      return 0.f;
+  }
+}
+
+#endif  // __CUDACC__
+
+struct SegSource {
+  ASeg seg[kMaxSeg];
+  int nseg = 0;
+  int group = 1;                 // rows come in groups (edges of one root) ...
+  const int* gcount = nullptr;   // ... of which only the first gcount[g] are valid
+  const int* nrows_dev = nullptr;  // optional device-side row count
+
+#ifdef __CUDACC__
+  __device__ __forceinline__ bool row_valid(int row, int nrows) const {
+    if (row >= nrows) return false;
+    if (nrows_dev != nullptr && row >= *nrows_dev) return false;
+    if (gcount != nullptr && (row % group) >= gcount[row / group]) return false;
+    return true;
+  }
+#endif
+  // 8 consecutive K elements [kv*8, kv*8+8) of row `row`.
+#ifdef __CUDACC__
+  __device__ __forceinline__ uint4 load8(int row, int kv, int nrows) const {
+    float f[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    if (row_valid(row, nrows)) {
+      int k = kv * 8;
+#pragma unroll
+      for (int s = 0; s < kMaxSeg; ++s) {
+        if (s >= nseg) break;
+        if (k < seg[s].kpad) {
+          seg_fill8(seg[s], row, k, f);
+          break;
+        }
+        k -= seg[s].kpad;
+      }
+    }
+    return pack_bf16x8(f);
+  }
+#endif
+#ifdef __CUDACC__
+  __device__ __forceinline__ float load1(int row, int k, int nrows) const {
+    if (!row_valid(row, nrows)) return 0.f;
+#pragma unroll
+    for (int s = 0; s < kMaxSeg; ++s) {
+      if (s >= nseg) break;
+      if (k < seg[s].kpad) return seg_load1(seg[s], row, k);
+      k -= seg[s].kpad;
+    }
+    return 0.f;
+  }
+#endif
+};
+
+// A[n, m] = inner(m, n): used for weight gradients (reduction over rows m).
+struct TransposedSource {
+  SegSource inner;
+  int inner_rows = 0;  // static row bound of the inner source (the GEMM K extent)
+#ifdef __CUDACC__
+  __device__ __forceinline__ uint4 load8(int row, int kv, int /*nrows*/) const {
+    float f[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) f[i] = inner.load1(kv * 8 + i, row, inner_rows);
+    return pack_bf16x8(f);
+  }
+#endif
+};
+
+// ---------------------------------------------------------------------------
+// Weight sources: rows = concatenated output blocks, K = concatenated input
+// segments; each (block, segment) cell maps to an fp32 nn.Linear weight
+// region or to zeros. Weights are read in fp32 and rounded to bf16 on the fly.
+// ---------------------------------------------------------------------------
+struct WCell {
+  const float* ptr = nullptr;  // nullptr -> zero block
+  int ld = 0;
+  int row0 = 0;
+  int col0 = 0;
+  int width = 0;
+};
+
+struct WeightLayout {
+  int nblk = 0, nseg = 0;
+  int blk_rows[kMaxBlk] = {0, 0, 0, 0};  // valid rows of each output block
+  int blk_pad[kMaxBlk] = {0, 0, 0, 0};   // padded rows of each output block
+  int seg_kpad[kMaxSeg] = {0, 0, 0, 0};  // padded K width of each input segment
+  WCell cell[kMaxBlk][kMaxSeg];
+
+#ifdef __CUDACC__
+  __device__ __forceinline__ bool find_blk(int n, int& b, int& r) const {
+#pragma unroll
+    for (int i = 0; i < kMaxBlk; ++i) {
+      if (i >= nblk) break;
+      if (n < blk_pad[i]) {
+        b = i;
+        r = n;
+        return r < blk_rows[i];
+      }
+      n -= blk_pad[i];
+    }
+    return false;
+  }
+#endif
+#ifdef __CUDACC__
+  __device__ __forceinline__ bool find_seg(int k, int& s, int& c) const {
+#pragma unroll
+    for (int i = 0; i < kMaxSeg; ++i) {
+      if (i >= nseg) break;
+      if (k < seg_kpad[i]) {
+        s = i;
+        c = k;
+        return true;
+      }
+      k -= seg_kpad[i];
+    }
+    return false;
+  }
+#endif
+};
+
+// B[n, k] = W[n, k] (forward projection; n = output feature).
+struct WeightSource {
+  WeightLayout L;
+#ifdef __CUDACC__
+  __device__ __forceinline__ uint4 load8(int row, int kv, int /*nrows*/) const {
+    float f[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    int b, r, s, c;
+    if (L.find_blk(row, b, r) && L.find_seg(kv * 8, s, c)) {
+      const WCell& e = L.cell[b][s];
+      if (e.ptr != nullptr) {
+        const float* p = e.ptr + (int64_t)(e.row0 + r) * e.ld + e.col0;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) f[i] = (c + i < e.width) ? p[c + i] : 0.f;
+      }
+    }
+    return pack_bf16x8(f);
+  }
+#endif
+};
+
+// B[n, k] = W[k, n] (data gradient: n = input feature, k = output feature).
+struct WeightTSource {
+  WeightLayout L;
+#ifdef __CUDACC__
+  __device__ __forceinline__ uint4 load8(int row, int kv, int /*nrows*/) const {
+    float f[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    int s, c;
+    if (L.find_seg(row, s, c)) {
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        int b, r;
+        if (L.find_blk(kv * 8 + i, b, r)) {
+          const WCell& e = L.cell[b][s];
+          if (e.ptr != nullptr && c < e.width) f[i] = e.ptr[(int64_t)(e.row0 + r) * e.ld + e.col0 + c];
+        }
+      }
+    }
+    return pack_bf16x8(f);
+  }
+#endif
+};
+
+// ---------------------------------------------------------------------------
+// Generic epilogues
+// ---------------------------------------------------------------------------
+enum Act : int { kActNone = 0, kActRelu = 1, kActSigmoid = 2, kActTanh = 3 };
+
+#ifdef __CUDACC__
+__device__ __forceinline__ float apply_act(float v, int act) {
+  switch (act) {
+    case kActRelu: return fmaxf(v, 0.f);
+    case kActSigmoid: return sigmoidf_(v);
+    case kActTanh: return tanhf(v);
+    default: return v;
+  }
+}
+
+#endif  // __CUDACC__
+
+// out[row, col] (=|+=) act(scale * acc + bias[col]); optional row scatter.
+struct EpiLinear {
+  float* out = nullptr;
+  __nv_bfloat16* out_bf16 = nullptr;
+  int ldo = 0;
+  int ncols = 0;         // valid output columns
+  const float* bias = nullptr;
+  const float* bias2 = nullptr;  // bias of the columns >= bias_split (two fused projections)
+  int bias_split = 1 << 30;
+  int act = kActNone;
+  float scale = 1.f;
+  int accumulate = 0;    // 1: out += value (non-atomic), 2: atomicAdd
+  const int64_t* scatter = nullptr;  // row -> output row
+
+#ifdef __CUDACC__
+  __device__ __forceinline__ void operator()(int row, bool valid, int n0, uint32_t taddr, int tile_cols) const {
+    int64_t orow = row;
+    if (valid && scatter != nullptr) {
+      orow = scatter[row];
+      if (orow < 0) valid = false;
+    }
+    const int lim = min(ncols - n0, tile_cols);
+    for (int c0 = 0; c0 < lim; c0 += 16) {
+      float v[16];
+      tmem_ld16(taddr + c0, v);  // warp-uniform
+      if (!valid) continue;
+#pragma unroll
+      for (int i = 0; i < 16; ++i) {
+        const int col = n0 + c0 + i;
+        if (col >= ncols) break;
+        const float bv = col < bias_split ? (bias ? bias[col] : 0.f) : (bias2 ? bias2[col - bias_split] : 0.f);
+        float x = scale * v[i] + bv;
+        x = apply_act(x, act);
+        float* o = out ? out + orow * ldo + col : nullptr;
+        if (o) {
+          if (accumulate == 2) atomicAdd(o, x);
+          else if (accumulate == 1) *o += x;
+          else *o = x;
+        }
+        if (out_bf16) out_bf16[orow * ldo + col] = __float2bfloat16(x);
+      }
+    }
+  }
+#endif
+};
+
+// Weight gradient accumulation: rows = output features (blocks of the layout),
+// columns = padded input K space (segments). Segment kinds flagged as bias
+// accumulate into the bias gradient of the block.
+struct EpiWeightGrad {
+  WeightLayout L;                 // cell ptrs point at gradient buffers
+  float* bias_grad[kMaxBlk] = {nullptr, nullptr, nullptr, nullptr};
+  int bias_seg = -1;              // segment index carrying the ones column
+  int ncols = 0;                  // total K space width of the inner source
+
+#ifdef __CUDACC__
+  __device__ __forceinline__ void operator()(int row, bool valid, int n0, uint32_t taddr, int tile_cols) const {
+    int b = 0, r = 0;
+    if (valid) valid = L.find_blk(row, b, r);
+    const int lim = min(ncols - n0, tile_cols);
+    for (int c0 = 0; c0 < lim; c0 += 16) {
+      float v[16];
+      tmem_ld16(taddr + c0, v);
+      if (!valid) continue;
+#pragma unroll
+      for (int i = 0; i < 16; ++i) {
+        const int n = n0 + c0 + i;
+        int s, c;
+        if (!L.find_seg(n, s, c)) continue;
+        if (s == bias_seg) {
+          if (c == 0 && bias_grad[b] != nullptr) atomicAdd(bias_grad[b] + r, v[i]);
+          continue;
+        }
+        const WCell& e = L.cell[b][s];
+        if (e.ptr != nullptr && c < e.width)
+          atomicAdd(const_cast<float*>(e.ptr) + (int64_t)(e.row0 + r) * e.ld + e.col0 + c, v[i]);
+      }
+    }
+  }
+#endif
+};
+
+struct GemmShape {
+  int M = 0;                  // static row bound (grid sizing)
+  const int* m_dev = nullptr; // optional device row count (<= M)
+  int N = 0;                  // columns of D (rows of B)
+  int K = 0;                  // reduction extent
+  int ksplit = 1;             // split-K factor (epilogue must accumulate atomically)
+};
+
+constexpr int tmem_cols_for(int n) {
+  return n <= 32 ? 32 : n <= 64 ? 64 : n <= 128 ? 128 : n <= 256 ? 256 : 512;
+}
+
+template <int BN, int NSUB>
+constexpr int gemm_smem_bytes() {
+  return kStages * (kBM * kBK * 2 + BN * NSUB * kBK * 2) + 1024 /*barriers*/ + 1024 /*align slack*/;
+}
+
+#ifdef __CUDACC__
+template <int BN, int NSUB, class ASrc, class BSrc, class Epi>
+__global__ void __launch_bounds__(kGemmThreads, 1)
+    tc_gemm_kernel(const __grid_constant__ ASrc asrc, const __grid_constant__ BSrc bsrc,
+                   const __grid_constant__ Epi epi, const GemmShape shape, int* status) {
+  static_assert(BN % 16 == 0 && BN >= 16 && BN <= 256, "UMMA N for M=128 must be a multiple of 16 in [16, 256]");
+  static_assert(NSUB >= 1 && BN * NSUB <= 512, "accumulator exceeds TMEM");
+  constexpr int A_BYTES = kBM * kBK * 2;
+  constexpr int B_ROWS = BN * NSUB;
+  constexpr int B_BYTES = B_ROWS * kBK * 2;
+  constexpr uint32_t TMEM_COLS = tmem_cols_for(B_ROWS);
+  constexpr uint32_t IDESC = umma_idesc_bf16_f32(kBM, BN);
+
+  extern __shared__ uint8_t smem_dyn[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_dyn) + 1023) & ~uintptr_t(1023));
+  uint8_t* smemA = smem;
+  uint8_t* smemB = smem + kStages * A_BYTES;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smemB + kStages * B_BYTES);
+  uint64_t* full = bars;                  // [kStages] producers -> MMA
+  uint64_t* empty = bars + kStages;       // [kStages] MMA -> producers
+  uint64_t* acc_full = bars + 2 * kStages;
+  uint64_t* acc_empty = acc_full + 1;
+  uint64_t* drain = acc_full + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(&full[s], 128);
+      mbar_init(&empty[s], 1);
+    }
+    mbar_init(acc_full, 1);
+    mbar_init(acc_empty, 128);
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 4) {
+    tmem_alloc(tmem_slot, TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  int M = shape.M;
+  if (shape.m_dev != nullptr) M = min(M, *shape.m_dev);
+  const int tiles_m = (M + kBM - 1) / kBM;
+  const int tiles_n = (shape.N + B_ROWS - 1) / B_ROWS;
+  const int nchunks = (shape.K + kBK - 1) / kBK;
+  const int ksplit = max(1, shape.ksplit);
+  const int cps = (nchunks + ksplit - 1) / ksplit;
+  const int total = tiles_m * tiles_n * ksplit;
+
+  if (warp < 4) {
+    // ------------------------- producers + epilogue -------------------------
+    int cg = 0;
+    int tl = 0;
+    bool ok = true;
+    for (int tile = blockIdx.x; tile < total && ok; tile += gridDim.x, ++tl) {
+      const int ks = tile % ksplit;
+      const int mn = tile / ksplit;
+      const int nt = mn % tiles_n;
+      const int mt = mn / tiles_n;
+      const int kc0 = ks * cps;
+      const int kc1 = min(nchunks, kc0 + cps);
+      for (int kc = kc0; kc < kc1; ++kc, ++cg) {
+        const int s = cg % kStages;
+        const uint32_t ph = (cg / kStages) & 1;
+        if (!mbar_wait_bounded(&empty[s], ph ^ 1) || *abort_flag) {
+          record_status(status, kTimeoutEmpty);
+          *abort_flag = 1;
+          ok = false;
+          break;
+        }
+        uint8_t* a = smemA + s * A_BYTES;
+        uint8_t* b = smemB + s * B_BYTES;
+        const int row = mt * kBM + threadIdx.x;
+#pragma unroll 2
+        for (int kv = 0; kv < kBK / 8; ++kv) {
+          const uint4 v = asrc.load8(row, kc * (kBK / 8) + kv, M);
+          *reinterpret_cast<uint4*>(a + tile_vec_off(threadIdx.x, kv)) = v;
+        }
+        for (int r = threadIdx.x; r < B_ROWS; r += 128) {
+          const int n = nt * B_ROWS + r;
+#pragma unroll 2
+          for (int kv = 0; kv < kBK / 8; ++kv) {
+            uint4 v = make_uint4(0, 0, 0, 0);
+            if (n < shape.N) v = bsrc.load8(n, kc * (kBK / 8) + kv, shape.N);
+            *reinterpret_cast<uint4*>(b + tile_vec_off(r, kv)) = v;
+          }
+        }
+        fence_proxy_async_smem();
+        mbar_arrive(&full[s]);
+      }
+      if (!ok) break;
+      // epilogue for this tile
+      if (!mbar_wait_bounded(acc_full, tl & 1) || *abort_flag) {
+        record_status(status, kTimeoutAccum);
+        *abort_flag = 1;
+        break;
+      }
+      tc_fence_after();
+      const int row = mt * kBM + warp * 32 + lane;
+      const uint32_t taddr = tmem_base + (static_cast<uint32_t>(warp * 32) << 16);
+      epi(row, row < M, nt * B_ROWS, taddr, B_ROWS);
+      tc_fence_before();
+      mbar_arrive(acc_empty);
+    }
+  } else {
+    // ------------------------------ MMA issuer ------------------------------
+    if (lane == 0) {
+      int cg = 0;
+      int tl = 0;
+      bool ok = true;
+      bool issued = false;
+      for (int tile = blockIdx.x; tile < total && ok; tile += gridDim.x, ++tl) {
+        const int ks = tile % ksplit;
+        const int kc0 = ks * cps;
+        const int kc1 = min(nchunks, kc0 + cps);
+        if (!mbar_wait_bounded(acc_empty, (tl & 1) ^ 1) || *abort_flag) {
+          record_status(status, kTimeoutTmemFree);
+          *abort_flag = 1;
+          break;
+        }
+        tc_fence_after();
+        for (int kc = kc0; kc < kc1; ++kc, ++cg) {
+          const int s = cg % kStages;
+          const uint32_t ph = (cg / kStages) & 1;
+          if (!mbar_wait_bounded(&full[s], ph) || *abort_flag) {
+            record_status(status, kTimeoutFull);
+            *abort_flag = 1;
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a_base = smem_u32(smemA + s * A_BYTES);
+          const uint32_t b_base = smem_u32(smemB + s * B_BYTES);
+          const int ksteps = min(kBK / 16, (shape.K - kc * kBK + 15) / 16);
+          for (int kk = 0; kk < ksteps; ++kk) {
+            const uint64_t adesc = umma_desc_kmajor_noswizzle(a_base + kk * 256, 128, 1024);
+#pragma unroll
+            for (int sub = 0; sub < NSUB; ++sub) {
+              const uint64_t bdesc = umma_desc_kmajor_noswizzle(b_base + sub * (BN / 8) * 1024 + kk * 256, 128, 1024);
+              umma_bf16(tmem_base + sub * BN, adesc, bdesc, IDESC, (kc > kc0 || kk > 0) ? 1u : 0u);
+            }
+            issued = true;
+          }
+          umma_commit(&empty[s]);
+        }
+        if (!ok) break;
+        umma_commit(acc_full);
+      }
+      // make sure no tensor-core work is in flight before TMEM is released
+      if (issued) {
+        umma_commit(drain);
+        if (!mbar_wait_bounded(drain, 0)) record_status(status, kTimeoutAccum);
+      }
+    }
+    __syncwarp();
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 4) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, TMEM_COLS);
+  }
+}
+
+#endif  // __CUDACC__
+
+}  // namespace su

@@ -1,0 +1,563 @@
+// TGN / CTDG training-step kernels for sm_100a.
+//
+// The step follows the reference online runtime (backends/ctdg/runtime/runtime.py:225-328):
+//   prep      : unique roots of src ∪ dst, root index of every event, uniform
+//               negatives from the destination pool (+1 shift on collision), the
+//               per-root mailbox winners of the src and dst passes and ts_max.
+//   sample    : most-recent / uniform-before-t neighbours from a T-CSR keyed by
+//               destination (vendor/bts_sampler/sampler/include/sampler.h:213-261).
+//   gru       : GRU over the K mailbox slots, then GRUCell(agg, mem) with the
+//               result scattered straight into the memory table (fused epilogue).
+//   mailbox   : [mem_prev(self) || mem_prev(other) || edge_feat] written at the
+//               circular slot position (backends/ctdg/runtime/memory.py:183-248).
+//   attention : per-root softmax over the sampled neighbours, dropout, weighted
+//               sum of V (backends/ctdg/runtime/models.py:77-137), fwd and bwd.
+//   out/LN    : W_out [agg || h] -> dropout -> ReLU -> LayerNorm, fused epilogue.
+//   link/BCE  : src_fc/dst_fc/out_fc scoring and the two BCE terms with their
+//               gradients (models.py:313-324, runtime.py:290-292), plus AP/AUC.
+#include "kernels.h"
+
+namespace su {
+
+// ---------------------------------------------------------------------------
+// prep
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ uint32_t orderable_f32(float f) {
+  uint32_t u = __float_as_uint(f);
+  return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+
+
+
+__global__ void __launch_bounds__(1024) tgn_prep_kernel(PrepArgs a) {
+  __shared__ int s_R;
+  __shared__ float s_tsmax;
+  __shared__ int s_tag;
+  const int n = min(*a.n_ev, a.bmax);
+  if (threadIdx.x == 0) {
+    s_R = 0;
+    s_tsmax = -INFINITY;
+    s_tag = static_cast<int>((*a.step_ctr) & 0x3FFFFFFF) + 1;
+  }
+  for (int r = threadIdx.x; r < 2 * a.rmax; r += blockDim.x) {
+    a.win_key[r] = 0ull;
+    a.cnt[r] = 0;
+  }
+  __syncthreads();
+  const int tag = s_tag;
+  // phase 1: claim unique roots
+  float local_max = -INFINITY;
+  for (int j = threadIdx.x; j < 2 * n; j += blockDim.x) {
+    const int64_t v = j < n ? a.src[j] : a.dst[j - n];
+    if (j < n) local_max = fmaxf(local_max, a.ts[j]);
+    int cur = a.stamp[v];
+    bool claimed = false;
+    while (cur != tag) {
+      const int prev = atomicCAS(&a.stamp[v], cur, tag);
+      if (prev == cur) {
+        claimed = true;
+        break;
+      }
+      cur = prev;
+    }
+    if (claimed) {
+      const int r = atomicAdd(&s_R, 1);
+      if (r < a.rmax) {
+        a.node2root[v] = r;
+        a.roots[r] = v;
+      } else {
+        record_status(a.status, kTooLarge);
+      }
+    }
+  }
+  local_max = warp_max(local_max);
+  __shared__ float s_wmax[32];
+  if ((threadIdx.x & 31) == 0) s_wmax[threadIdx.x >> 5] = local_max;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float m = -INFINITY;
+    for (int w = 0; w < (blockDim.x >> 5); ++w) m = fmaxf(m, s_wmax[w]);
+    s_tsmax = n > 0 ? m : 0.f;
+  }
+  __syncthreads();
+  const int R = min(s_R, a.rmax);
+  // phase 2: event -> root indices, negatives, mailbox winners
+  for (int i = threadIdx.x; i < a.bmax; i += blockDim.x) {
+    if (i < n) {
+      const int si = a.node2root[a.src[i]];
+      const int di = a.node2root[a.dst[i]];
+      a.src_idx[i] = si;
+      a.dst_idx[i] = di;
+      // negative: pool[randint(P)], shifted by one on collision with the true dst
+      const uint4 rr = Philox::gen(a.seed, static_cast<uint64_t>(*a.step_ctr) * (uint64_t)a.bmax + i, 0x4E4547u);
+      int64_t idx = static_cast<int64_t>(((static_cast<uint64_t>(rr.x) << 32) | rr.y) % (uint64_t)a.pool_size);
+      int64_t ng = a.neg_pool[idx];
+      if (ng == a.dst[i]) {
+        idx = (idx + 1) % a.pool_size;
+        ng = a.neg_pool[idx];
+      }
+      a.neg[i] = ng;
+      a.neg_idx[i] = (a.stamp[ng] == tag) ? a.node2root[ng] : -1;
+      const unsigned long long key =
+          (static_cast<unsigned long long>(orderable_f32(a.ts[i])) << 32) | static_cast<unsigned int>(i);
+      atomicMax(&a.win_key[si], key);
+      atomicAdd(&a.cnt[si], 1);
+      atomicMax(&a.win_key[a.rmax + di], key);
+      atomicAdd(&a.cnt[a.rmax + di], 1);
+    } else {
+      a.src_idx[i] = -1;
+      a.dst_idx[i] = -1;
+      a.neg[i] = -1;
+      a.neg_idx[i] = -1;
+    }
+  }
+  __syncthreads();
+  for (int r = threadIdx.x; r < a.rmax; r += blockDim.x) {
+    if (r >= R) a.roots[r] = -1;
+    for (int p = 0; p < 2; ++p) {
+      const unsigned long long k = a.win_key[p * a.rmax + r];
+      a.win[p * a.rmax + r] = (r < R && a.cnt[p * a.rmax + r] > 0) ? static_cast<int>(k & 0xFFFFFFFFull) : -1;
+    }
+  }
+  if (threadIdx.x == 0) {
+    *a.n_roots = R;
+    *a.ts_max = s_tsmax;
+    *a.root_ts = static_cast<int64_t>(s_tsmax);
+    *a.step_ctr += 1;
+  }
+}
+
+// ---------------------------------------------------------------------------
+// temporal neighbour sampling (warp per root)
+// ---------------------------------------------------------------------------
+__global__ void tgn_sample_kernel(const int64_t* __restrict__ roots, const int* __restrict__ n_roots, int rmax,
+                                  const int64_t* __restrict__ root_ts_scalar, const int64_t* __restrict__ root_ts_vec,
+                                  const int64_t* __restrict__ rowptr, const int64_t* __restrict__ nbr,
+                                  const int64_t* __restrict__ eid, const int64_t* __restrict__ ets, int k, int policy,
+                                  uint64_t seed, const int64_t* __restrict__ step_ctr, int64_t* __restrict__ out_nbr,
+                                  int64_t* __restrict__ out_eid, float* __restrict__ out_dt,
+                                  int* __restrict__ out_cnt, int* __restrict__ edge_total) {
+  const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (warp >= rmax) return;
+  const int R = *n_roots;
+  const int r = warp;
+  if (r >= R) {
+    if (lane == 0) out_cnt[r] = 0;
+    for (int j = lane; j < k; j += 32) {
+      out_nbr[(int64_t)r * k + j] = -1;
+      out_eid[(int64_t)r * k + j] = -1;
+      out_dt[(int64_t)r * k + j] = 0.f;
+    }
+    return;
+  }
+  const int64_t v = roots[r];
+  const int64_t rts = root_ts_vec ? root_ts_vec[r] : *root_ts_scalar;
+  const int64_t lo = rowptr[v], hi = rowptr[v + 1];
+  // lower_bound(ts[lo:hi], rts): first position with ts >= rts (strictly-earlier neighbours)
+  int64_t a = lo, b = hi;
+  while (a < b) {
+    const int64_t m = (a + b) >> 1;
+    if (ets[m] < rts) a = m + 1;
+    else b = m;
+  }
+  const int64_t end = a;
+  const int64_t avail = end - lo;
+  int cnt;
+  if (policy == 0 || avail <= k) {
+    // recent: the last min(k, avail) entries in list (time) order
+    cnt = static_cast<int>(avail < (int64_t)k ? avail : (int64_t)k);
+    const int64_t start = end - cnt;
+    for (int j = lane; j < k; j += 32) {
+      const int64_t o = (int64_t)r * k + j;
+      if (j < cnt) {
+        const int64_t p = start + j;
+        out_nbr[o] = nbr[p];
+        out_eid[o] = eid[p];
+        out_dt[o] = static_cast<float>(rts - ets[p]);
+      } else {
+        out_nbr[o] = -1;
+        out_eid[o] = -1;
+        out_dt[o] = 0.f;
+      }
+    }
+  } else {
+    // uniform with replacement over the avail strictly-earlier neighbours
+    cnt = k;
+    for (int j = lane; j < k; j += 32) {
+      const uint4 rr = Philox::gen(seed, (static_cast<uint64_t>(*step_ctr) << 32) ^ ((uint64_t)r * k + j), 0x534D50u);
+      const int64_t p = lo + static_cast<int64_t>(rr.x % static_cast<uint64_t>(avail));
+      const int64_t o = (int64_t)r * k + j;
+      out_nbr[o] = nbr[p];
+      out_eid[o] = eid[p];
+      out_dt[o] = static_cast<float>(rts - ets[p]);
+    }
+  }
+  if (lane == 0) {
+    out_cnt[r] = cnt;
+    if (cnt > 0) atomicAdd(edge_total, cnt);
+  }
+}
+
+
+// ---------------------------------------------------------------------------
+// mailbox write (block of 128 threads per root, two passes in order src, dst)
+// ---------------------------------------------------------------------------
+__global__ void tgn_mailbox_kernel(const int64_t* __restrict__ roots, const int* __restrict__ n_roots, int rmax,
+                                   const int* __restrict__ win, const int* __restrict__ cnt,
+                                   const int* __restrict__ src_idx, const int* __restrict__ dst_idx,
+                                   const int64_t* __restrict__ ev_eid, const float* __restrict__ ev_ts,
+                                   const float* __restrict__ mem_prev, int D, const float* __restrict__ efeat,
+                                   int efeat_ld, int e_raw, int E, float* __restrict__ mailbox,
+                                   float* __restrict__ mailbox_ts, int64_t* __restrict__ next_pos, int K) {
+  const int r = blockIdx.x;
+  if (r >= *n_roots || r >= rmax) return;
+  const int64_t v = roots[r];
+  const int SW = 2 * D + E;
+  const int64_t pos0 = next_pos[v];
+  const int csrc = cnt[r], cdst = cnt[rmax + r];
+  for (int p = 0; p < 2; ++p) {
+    const int i = win[p * rmax + r];
+    if (i < 0) continue;
+    const int64_t pos = (p == 0 ? pos0 : (pos0 + csrc)) % K;
+    const int self = p == 0 ? src_idx[i] : dst_idx[i];
+    const int other = p == 0 ? dst_idx[i] : src_idx[i];
+    float* slot = mailbox + (v * K + pos) * SW;
+    const int64_t e = ev_eid[i];
+    for (int c = threadIdx.x; c < SW; c += blockDim.x) {
+      float x;
+      if (c < D) x = mem_prev[(int64_t)self * D + c];
+      else if (c < 2 * D) x = mem_prev[(int64_t)other * D + (c - D)];
+      else {
+        const int ce = c - 2 * D;
+        x = (ce < e_raw) ? efeat[e * efeat_ld + ce] : 0.f;
+      }
+      slot[c] = x;
+    }
+    if (threadIdx.x == 0) mailbox_ts[v * K + pos] = ev_ts[i];
+    __syncthreads();
+  }
+  if (threadIdx.x == 0) next_pos[v] = (pos0 + csrc + cdst) % K;
+}
+
+// ---------------------------------------------------------------------------
+// temporal attention forward (warp per root; edges of a root on lanes)
+// KV: [rmax*k, 2*Do] (K cols [0,Do), V cols [Do,2Do)); Q: [rmax, Do]
+// ---------------------------------------------------------------------------
+
+__global__ void tgn_attn_fwd_kernel(const float* __restrict__ Q, const float* __restrict__ KV,
+                                    const int* __restrict__ cnt, const int* __restrict__ n_roots, int rmax, int k,
+                                    int Do, int H, float att_drop, uint64_t seed, const int64_t* __restrict__ step_ctr,
+                                    float* __restrict__ att_p, float* __restrict__ agg) {
+  const int r = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (r >= rmax) return;
+  const int dh = Do / H;
+  float* ag = agg + (int64_t)r * Do;
+  const int nv = (r < *n_roots) ? cnt[r] : 0;
+  if (nv == 0) {
+    for (int d = lane; d < Do; d += 32) ag[d] = 0.f;
+    return;
+  }
+  const uint64_t dseed = seed ^ (static_cast<uint64_t>(*step_ctr) * 0x9E3779B97F4A7C15ull);
+  const float* q = Q + (int64_t)r * Do;
+  const int64_t e = (int64_t)r * k + lane;
+  // scores (lane j = edge j), up to 4 heads
+  float att[4] = {0.f, 0.f, 0.f, 0.f};
+  const bool on = lane < nv;
+  for (int h = 0; h < H && h < 4; ++h) {
+    float s = -INFINITY;
+    if (on) {
+      const float* kr = KV + e * (2 * Do) + h * dh;
+      float acc = 0.f;
+      for (int d = 0; d < dh; ++d) acc = fmaf(q[h * dh + d], kr[d], acc);
+      s = acc > 0.f ? acc : 0.2f * acc;  // LeakyReLU(0.2)
+    }
+    const float m = warp_max(s);
+    const float ex = on ? expf(s - m) : 0.f;
+    const float sum = warp_sum(ex);
+    const float p = ex / sum;
+    if (on) att_p[e * H + h] = p;
+    float a = p;
+    if (on && att_drop > 0.f)
+      a = dropout_keep(dseed, (uint64_t)(e * H + h), kStreamAttDrop, att_drop) ? p / (1.f - att_drop) : 0.f;
+    att[h] = on ? a : 0.f;
+  }
+  // aggregate: lanes over feature columns
+  for (int d = lane; d < Do; d += 32) {
+    const int h = d / dh;
+    float acc = 0.f;
+    for (int j = 0; j < nv; ++j) {
+      const float a = __shfl_sync(0xffffffffu, att[h < 4 ? h : 0], j);
+      acc = fmaf(a, KV[((int64_t)r * k + j) * (2 * Do) + Do + d], acc);
+    }
+    ag[d] = acc;
+  }
+}
+
+// Backward of the attention: dagg -> dKV (rows of invalid edges stay zero), dQ.
+__global__ void tgn_attn_bwd_kernel(const float* __restrict__ Q, const float* __restrict__ KV,
+                                    const float* __restrict__ att_p, const float* __restrict__ dagg,
+                                    const int* __restrict__ cnt, const int* __restrict__ n_roots, int rmax, int k,
+                                    int Do, int H, float att_drop, uint64_t seed, const int64_t* __restrict__ step_ctr,
+                                    float* __restrict__ dKV, float* __restrict__ dQ) {
+  const int r = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (r >= rmax) return;
+  const int dh = Do / H;
+  const int nv = (r < *n_roots) ? cnt[r] : 0;
+  float* dq = dQ + (int64_t)r * Do;
+  // zero rows of padded edges
+  for (int j = nv; j < k; ++j)
+    for (int d = lane; d < 2 * Do; d += 32) dKV[((int64_t)r * k + j) * (2 * Do) + d] = 0.f;
+  if (nv == 0) {
+    for (int d = lane; d < Do; d += 32) dq[d] = 0.f;
+    return;
+  }
+  // step_ctr was already advanced by this step's prep kernel, use the same value as forward
+  const uint64_t dseed = seed ^ (static_cast<uint64_t>(*step_ctr) * 0x9E3779B97F4A7C15ull);
+  const float* q = Q + (int64_t)r * Do;
+  const float* g = dagg + (int64_t)r * Do;
+  const int64_t e = (int64_t)r * k + lane;
+  const bool on = lane < nv;
+  float att[4] = {0.f, 0.f, 0.f, 0.f};
+  float dsc[4] = {0.f, 0.f, 0.f, 0.f};
+  for (int h = 0; h < H && h < 4; ++h) {
+    float p = 0.f, keep = 0.f, datt = 0.f, s = 0.f;
+    if (on) {
+      p = att_p[e * H + h];
+      keep = 1.f;
+      if (att_drop > 0.f)
+        keep = dropout_keep(dseed, (uint64_t)(e * H + h), kStreamAttDrop, att_drop) ? 1.f / (1.f - att_drop) : 0.f;
+      const float* vr = KV + e * (2 * Do) + Do + h * dh;
+      const float* kr = KV + e * (2 * Do) + h * dh;
+      float acc = 0.f, sacc = 0.f;
+      for (int d = 0; d < dh; ++d) {
+        acc = fmaf(g[h * dh + d], vr[d], acc);
+        sacc = fmaf(q[h * dh + d], kr[d], sacc);
+      }
+      datt = acc;
+      s = sacc;
+    }
+    att[h] = p * keep;
+    const float dp = datt * keep;               // through dropout
+    const float dot = warp_sum(on ? p * dp : 0.f);
+    const float ds = on ? p * (dp - dot) : 0.f;  // softmax backward
+    dsc[h] = on ? ds * (s > 0.f ? 1.f : 0.2f) : 0.f;  // LeakyReLU backward
+  }
+  for (int d = lane; d < Do; d += 32) {
+    const int h = d / dh;
+    float dqa = 0.f;
+    for (int j = 0; j < nv; ++j) {
+      const float a = __shfl_sync(0xffffffffu, att[h < 4 ? h : 0], j);
+      const float sj = __shfl_sync(0xffffffffu, dsc[h < 4 ? h : 0], j);
+      float* row = dKV + ((int64_t)r * k + j) * (2 * Do);
+      row[Do + d] = a * g[d];                               // dV
+      row[d] = sj * q[d];                                   // dK
+      dqa = fmaf(sj, KV[((int64_t)r * k + j) * (2 * Do) + d], dqa);  // dQ
+    }
+    dq[d] = dqa;
+  }
+}
+
+
+// LayerNorm + ReLU + dropout backward (warp per row).
+__global__ void tgn_out_bwd_kernel(const float* __restrict__ dout, const float* __restrict__ xsave,
+                                   const float* __restrict__ mean, const float* __restrict__ rstd,
+                                   const float* __restrict__ gamma, const int* __restrict__ n_roots, int rmax, int Do,
+                                   float drop, uint64_t seed, const int64_t* __restrict__ step_ctr,
+                                   const int* __restrict__ edge_total, float* __restrict__ dpre,
+                                   float* __restrict__ dgamma, float* __restrict__ dbeta) {
+  const int r = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (r >= rmax) return;
+  float* dp = dpre + (int64_t)r * Do;
+  if (r >= *n_roots || *edge_total == 0) {
+    for (int c = lane; c < Do; c += 32) dp[c] = 0.f;
+    return;
+  }
+  const uint64_t dseed = seed ^ (static_cast<uint64_t>(*step_ctr) * 0x9E3779B97F4A7C15ull);
+  const float mu = mean[r], rs = rstd[r];
+  const float* x = xsave + (int64_t)r * Do;
+  const float* dy = dout + (int64_t)r * Do;
+  float sa = 0.f, sb = 0.f;
+  for (int c = lane; c < Do; c += 32) {
+    const float xh = (x[c] - mu) * rs;
+    const float dxh = dy[c] * gamma[c];
+    sa += dxh;
+    sb += dxh * xh;
+    atomicAdd(&dgamma[c], dy[c] * xh);
+    atomicAdd(&dbeta[c], dy[c]);
+  }
+  sa = warp_sum(sa) / Do;
+  sb = warp_sum(sb) / Do;
+  for (int c = lane; c < Do; c += 32) {
+    const float xh = (x[c] - mu) * rs;
+    const float dxh = dy[c] * gamma[c];
+    float dx = rs * (dxh - sa - xh * sb);
+    dx = x[c] > 0.f ? dx : 0.f;  // ReLU
+    if (drop > 0.f)
+      dx = dropout_keep(dseed, (uint64_t)r * Do + c, kStreamOutDrop, drop) ? dx / (1.f - drop) : 0.f;
+    dp[c] = dx;
+  }
+}
+
+// ---------------------------------------------------------------------------
+// link predictor scoring + BCE loss + gradients (warp per event)
+// P: [rmax, 2D] per-root projections (src_fc | dst_fc incl. bias)
+// ---------------------------------------------------------------------------
+__global__ void tgn_link_kernel(const float* __restrict__ P, const int* __restrict__ src_idx,
+                                const int* __restrict__ dst_idx, const int* __restrict__ neg_idx,
+                                const int* __restrict__ n_ev, int bmax, int D, const float* __restrict__ b_dst,
+                                const float* __restrict__ w_out, const float* __restrict__ b_out, int need_grad,
+                                float* __restrict__ scores, float* __restrict__ loss, float* __restrict__ dP,
+                                float* __restrict__ g_w_out, float* __restrict__ g_b_out, float* __restrict__ g_b_dst) {
+  const int i = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  const int n = *n_ev;
+  if (i >= bmax || i >= n) return;
+  const int si = src_idx[i], di = dst_idx[i], ni = neg_idx[i];
+  const float* ps = P + (int64_t)si * 2 * D;
+  const float* pd = P + (int64_t)di * 2 * D + D;
+  const float* pn = ni >= 0 ? P + (int64_t)ni * 2 * D + D : nullptr;
+  float sp = 0.f, sn = 0.f;
+  for (int d = lane; d < D; d += 32) {
+    const float a = ps[d] + pd[d];
+    const float bneg = ps[d] + (pn ? pn[d] : b_dst[d]);
+    sp = fmaf(w_out[d], fmaxf(a, 0.f), sp);
+    sn = fmaf(w_out[d], fmaxf(bneg, 0.f), sn);
+  }
+  sp = warp_sum(sp) + b_out[0];
+  sn = warp_sum(sn) + b_out[0];
+  if (lane == 0) {
+    scores[i] = sp;
+    scores[bmax + i] = sn;
+    // BCE-with-logits: softplus(-x) for label 1, softplus(x) for label 0 (means over events)
+    const float lp = fmaxf(-sp, 0.f) + log1pf(expf(-fabsf(sp)));
+    const float ln = fmaxf(sn, 0.f) + log1pf(expf(-fabsf(sn)));
+    atomicAdd(loss, (lp + ln) / n);
+  }
+  if (!need_grad) return;
+  const float dpos = (sigmoidf_(sp) - 1.f) / n;
+  const float dneg = sigmoidf_(sn) / n;
+  float* dps = dP + (int64_t)si * 2 * D;
+  float* dpd = dP + (int64_t)di * 2 * D + D;
+  float* dpn = ni >= 0 ? dP + (int64_t)ni * 2 * D + D : nullptr;
+  for (int d = lane; d < D; d += 32) {
+    const float a = ps[d] + pd[d];
+    const float bneg = ps[d] + (pn ? pn[d] : b_dst[d]);
+    atomicAdd(&g_w_out[d], dpos * fmaxf(a, 0.f) + dneg * fmaxf(bneg, 0.f));
+    const float da = a > 0.f ? dpos * w_out[d] : 0.f;
+    const float db = bneg > 0.f ? dneg * w_out[d] : 0.f;
+    atomicAdd(&dps[d], da + db);
+    atomicAdd(&dpd[d], da);
+    if (dpn) atomicAdd(&dpn[d], db);
+    else atomicAdd(&g_b_dst[d], db);
+  }
+  if (lane == 0) atomicAdd(g_b_out, dpos + dneg);
+}
+
+// AP (sklearn semantics), ROC-AUC (ties count 1/2) and the pairwise "mrr" of the reference.
+__global__ void __launch_bounds__(1024) tgn_metrics_kernel(const float* __restrict__ scores,
+                                                           const int* __restrict__ n_ev, int bmax,
+                                                           float* __restrict__ out) {
+  __shared__ float s_ap, s_auc, s_gt;
+  const int n = *n_ev;
+  if (threadIdx.x == 0) { s_ap = 0.f; s_auc = 0.f; s_gt = 0.f; }
+  __syncthreads();
+  float ap = 0.f, auc = 0.f, gt = 0.f;
+  for (int i = threadIdx.x; i < n; i += blockDim.x) {
+    const float sp = scores[i];
+    int pos_ge = 0, all_ge = 0;
+    float a = 0.f, g = 0.f;
+    for (int j = 0; j < n; ++j) {
+      const float p2 = scores[j], n2 = scores[bmax + j];
+      pos_ge += p2 >= sp;
+      all_ge += (p2 >= sp) + (n2 >= sp);
+      a += sp > n2 ? 1.f : (sp == n2 ? 0.5f : 0.f);
+      g += sp > n2 ? 1.f : 0.f;
+    }
+    ap += static_cast<float>(pos_ge) / static_cast<float>(all_ge);
+    auc += a;
+    gt += g;
+  }
+  ap = warp_sum(ap); auc = warp_sum(auc); gt = warp_sum(gt);
+  if ((threadIdx.x & 31) == 0) { atomicAdd(&s_ap, ap); atomicAdd(&s_auc, auc); atomicAdd(&s_gt, gt); }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    const float nn = fmaxf(1.f, static_cast<float>(n));
+    out[0] = s_ap / nn;
+    out[1] = s_auc / (nn * nn);
+    out[2] = s_gt / (nn * nn);
+  }
+}
+
+
+// ---------------------------------------------------------------------------
+// launchers (called from the torch-side wrappers)
+// ---------------------------------------------------------------------------
+void launch_tgn_prep(dim3 grid, dim3 block, cudaStream_t st, PrepArgs a) {
+  tgn_prep_kernel<<<grid, block, 0, st>>>(a);
+}
+
+void launch_tgn_sample(dim3 grid, dim3 block, cudaStream_t st, const int64_t* __restrict__ roots, const int* __restrict__ n_roots, int rmax,
+                                  const int64_t* __restrict__ root_ts_scalar, const int64_t* __restrict__ root_ts_vec,
+                                  const int64_t* __restrict__ rowptr, const int64_t* __restrict__ nbr,
+                                  const int64_t* __restrict__ eid, const int64_t* __restrict__ ets, int k, int policy,
+                                  uint64_t seed, const int64_t* __restrict__ step_ctr, int64_t* __restrict__ out_nbr,
+                                  int64_t* __restrict__ out_eid, float* __restrict__ out_dt,
+                                  int* __restrict__ out_cnt, int* __restrict__ edge_total) {
+  tgn_sample_kernel<<<grid, block, 0, st>>>(roots, n_roots, rmax, root_ts_scalar, root_ts_vec, rowptr, nbr, eid, ets, k, policy, seed, step_ctr, out_nbr, out_eid, out_dt, out_cnt, edge_total);
+}
+
+void launch_tgn_mailbox(dim3 grid, dim3 block, cudaStream_t st, const int64_t* __restrict__ roots, const int* __restrict__ n_roots, int rmax,
+                                   const int* __restrict__ win, const int* __restrict__ cnt,
+                                   const int* __restrict__ src_idx, const int* __restrict__ dst_idx,
+                                   const int64_t* __restrict__ ev_eid, const float* __restrict__ ev_ts,
+                                   const float* __restrict__ mem_prev, int D, const float* __restrict__ efeat,
+                                   int efeat_ld, int e_raw, int E, float* __restrict__ mailbox,
+                                   float* __restrict__ mailbox_ts, int64_t* __restrict__ next_pos, int K) {
+  tgn_mailbox_kernel<<<grid, block, 0, st>>>(roots, n_roots, rmax, win, cnt, src_idx, dst_idx, ev_eid, ev_ts, mem_prev, D, efeat, efeat_ld, e_raw, E, mailbox, mailbox_ts, next_pos, K);
+}
+
+void launch_tgn_attn_fwd(dim3 grid, dim3 block, cudaStream_t st, const float* __restrict__ Q, const float* __restrict__ KV,
+                                    const int* __restrict__ cnt, const int* __restrict__ n_roots, int rmax, int k,
+                                    int Do, int H, float att_drop, uint64_t seed, const int64_t* __restrict__ step_ctr,
+                                    float* __restrict__ att_p, float* __restrict__ agg) {
+  tgn_attn_fwd_kernel<<<grid, block, 0, st>>>(Q, KV, cnt, n_roots, rmax, k, Do, H, att_drop, seed, step_ctr, att_p, agg);
+}
+
+void launch_tgn_attn_bwd(dim3 grid, dim3 block, cudaStream_t st, const float* __restrict__ Q, const float* __restrict__ KV,
+                                    const float* __restrict__ att_p, const float* __restrict__ dagg,
+                                    const int* __restrict__ cnt, const int* __restrict__ n_roots, int rmax, int k,
+                                    int Do, int H, float att_drop, uint64_t seed, const int64_t* __restrict__ step_ctr,
+                                    float* __restrict__ dKV, float* __restrict__ dQ) {
+  tgn_attn_bwd_kernel<<<grid, block, 0, st>>>(Q, KV, att_p, dagg, cnt, n_roots, rmax, k, Do, H, att_drop, seed, step_ctr, dKV, dQ);
+}
+
+void launch_tgn_out_bwd(dim3 grid, dim3 block, cudaStream_t st, const float* __restrict__ dout, const float* __restrict__ xsave,
+                                   const float* __restrict__ mean, const float* __restrict__ rstd,
+                                   const float* __restrict__ gamma, const int* __restrict__ n_roots, int rmax, int Do,
+                                   float drop, uint64_t seed, const int64_t* __restrict__ step_ctr,
+                                   const int* __restrict__ edge_total, float* __restrict__ dpre,
+                                   float* __restrict__ dgamma, float* __restrict__ dbeta) {
+  tgn_out_bwd_kernel<<<grid, block, 0, st>>>(dout, xsave, mean, rstd, gamma, n_roots, rmax, Do, drop, seed, step_ctr, edge_total, dpre, dgamma, dbeta);
+}
+
+void launch_tgn_link(dim3 grid, dim3 block, cudaStream_t st, const float* __restrict__ P, const int* __restrict__ src_idx,
+                                const int* __restrict__ dst_idx, const int* __restrict__ neg_idx,
+                                const int* __restrict__ n_ev, int bmax, int D, const float* __restrict__ b_dst,
+                                const float* __restrict__ w_out, const float* __restrict__ b_out, int need_grad,
+                                float* __restrict__ scores, float* __restrict__ loss, float* __restrict__ dP,
+                                float* __restrict__ g_w_out, float* __restrict__ g_b_out, float* __restrict__ g_b_dst) {
+  tgn_link_kernel<<<grid, block, 0, st>>>(P, src_idx, dst_idx, neg_idx, n_ev, bmax, D, b_dst, w_out, b_out, need_grad, scores, loss, dP, g_w_out, g_b_out, g_b_dst);
+}
+
+void launch_tgn_metrics(dim3 grid, dim3 block, cudaStream_t st, const float* __restrict__ scores,
+                                                           const int* __restrict__ n_ev, int bmax,
+                                                           float* __restrict__ out) {
+  tgn_metrics_kernel<<<grid, block, 0, st>>>(scores, n_ev, bmax, out);
+}
+
+}  // namespace su
+

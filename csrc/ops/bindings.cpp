@@ -1,0 +1,92 @@
+// Python bindings of the sm_100a kernels (module starry_unigraph._C).
+#include <torch/extension.h>
+
+int64_t status_read(bool clear);
+at::Tensor linear_fwd(const at::Tensor& x, const at::Tensor& w, const c10::optional<at::Tensor>& bias, int64_t act);
+at::Tensor linear_dgrad(const at::Tensor& dy, const at::Tensor& w);
+void linear_wgrad(const at::Tensor& dy, const at::Tensor& x, at::Tensor& dw, const c10::optional<at::Tensor>& db);
+
+void tgn_prep(const at::Tensor& src, const at::Tensor& dst, const at::Tensor& ts, const at::Tensor& n_ev,
+              const at::Tensor& neg_pool, at::Tensor& stamp, at::Tensor& node2root, at::Tensor& step_ctr, int64_t seed,
+              at::Tensor& roots, at::Tensor& n_roots, at::Tensor& src_idx, at::Tensor& dst_idx, at::Tensor& neg,
+              at::Tensor& neg_idx, at::Tensor& ts_max, at::Tensor& root_ts, at::Tensor& win_key, at::Tensor& win,
+              at::Tensor& cnt);
+void tgn_sample(const at::Tensor& roots, const at::Tensor& n_roots, const at::Tensor& root_ts,
+                const at::Tensor& rowptr, const at::Tensor& nbr, const at::Tensor& eid, const at::Tensor& ets,
+                int64_t k, int64_t policy, int64_t seed, const at::Tensor& step_ctr, at::Tensor& out_nbr,
+                at::Tensor& out_eid, at::Tensor& out_dt, at::Tensor& out_cnt, at::Tensor& edge_total);
+void tgn_memory_update(const at::Tensor& roots, const at::Tensor& n_roots, const at::Tensor& mailbox, int64_t K,
+                       at::Tensor& memory, at::Tensor& memory_ts, const at::Tensor& ts_max, const at::Tensor& gru_w_ih,
+                       const at::Tensor& gru_w_hh, const at::Tensor& gru_b_ih, const at::Tensor& gru_b_hh,
+                       const at::Tensor& cell_w_ih, const at::Tensor& cell_w_hh, const at::Tensor& cell_b_ih,
+                       const at::Tensor& cell_b_hh, at::Tensor& agg_buf, at::Tensor& agg_buf2, at::Tensor& mem_prev);
+void tgn_mailbox_write(const at::Tensor& roots, const at::Tensor& n_roots, const at::Tensor& win,
+                       const at::Tensor& cnt, const at::Tensor& src_idx, const at::Tensor& dst_idx,
+                       const at::Tensor& ev_eid, const at::Tensor& ev_ts, const at::Tensor& mem_prev,
+                       const at::Tensor& efeat, int64_t E, at::Tensor& mailbox, at::Tensor& mailbox_ts,
+                       at::Tensor& next_pos);
+void tgn_attn_proj(const at::Tensor& memory, const at::Tensor& roots, const at::Tensor& n_roots,
+                   const at::Tensor& nbr, const at::Tensor& nbr_eid, const at::Tensor& nbr_dt,
+                   const at::Tensor& nbr_cnt, const at::Tensor& efeat, int64_t E, const at::Tensor& te_w,
+                   const at::Tensor& te_b, const at::Tensor& wq, const at::Tensor& bq, const at::Tensor& wk,
+                   const at::Tensor& bk, const at::Tensor& wv, const at::Tensor& bv, at::Tensor& Q, at::Tensor& KV);
+void tgn_attn_fwd(const at::Tensor& Q, const at::Tensor& KV, const at::Tensor& nbr_cnt, const at::Tensor& n_roots,
+                  int64_t H, double att_drop, int64_t seed, const at::Tensor& step_ctr, at::Tensor& att_p,
+                  at::Tensor& agg);
+void tgn_attn_bwd(const at::Tensor& Q, const at::Tensor& KV, const at::Tensor& att_p, const at::Tensor& dagg,
+                  const at::Tensor& nbr_cnt, const at::Tensor& n_roots, int64_t H, double att_drop, int64_t seed,
+                  const at::Tensor& step_ctr, at::Tensor& dKV, at::Tensor& dQ);
+void tgn_out_fwd(const at::Tensor& agg, const at::Tensor& memory, const at::Tensor& roots, const at::Tensor& n_roots,
+                 const at::Tensor& w_out, const at::Tensor& b_out, const at::Tensor& gamma, const at::Tensor& beta,
+                 double drop, int64_t seed, const at::Tensor& step_ctr, const at::Tensor& edge_total, at::Tensor& out,
+                 at::Tensor& xsave, at::Tensor& mean, at::Tensor& rstd);
+void tgn_out_bwd(const at::Tensor& dout, const at::Tensor& xsave, const at::Tensor& mean, const at::Tensor& rstd,
+                 const at::Tensor& gamma, const at::Tensor& n_roots, double drop, int64_t seed,
+                 const at::Tensor& step_ctr, const at::Tensor& edge_total, at::Tensor& dpre, at::Tensor& dgamma,
+                 at::Tensor& dbeta);
+void tgn_attn_proj_bwd(const at::Tensor& memory, const at::Tensor& roots, const at::Tensor& n_roots,
+                       const at::Tensor& nbr, const at::Tensor& nbr_eid, const at::Tensor& nbr_dt,
+                       const at::Tensor& nbr_cnt, const at::Tensor& efeat, int64_t E, const at::Tensor& te_w,
+                       const at::Tensor& te_b, const at::Tensor& wq, const at::Tensor& wk, const at::Tensor& wv,
+                       const at::Tensor& dQ, const at::Tensor& dKV, at::Tensor& g_wq, at::Tensor& g_bq,
+                       at::Tensor& g_wk, at::Tensor& g_bk, at::Tensor& g_wv, at::Tensor& g_bv, at::Tensor& g_tw,
+                       at::Tensor& g_tb);
+void tgn_out_proj_bwd(const at::Tensor& dpre, const at::Tensor& agg, const at::Tensor& memory,
+                      const at::Tensor& roots, const at::Tensor& n_roots, const at::Tensor& w_out, at::Tensor& g_wout,
+                      at::Tensor& g_bout, at::Tensor& dagg);
+void tgn_link_proj(const at::Tensor& out, const at::Tensor& n_roots, const at::Tensor& w_src, const at::Tensor& b_src,
+                   const at::Tensor& w_dst, const at::Tensor& b_dst, at::Tensor& P);
+void tgn_link_loss(const at::Tensor& P, const at::Tensor& src_idx, const at::Tensor& dst_idx,
+                   const at::Tensor& neg_idx, const at::Tensor& n_ev, const at::Tensor& b_dst,
+                   const at::Tensor& w_out, const at::Tensor& b_out, bool need_grad, at::Tensor& scores,
+                   at::Tensor& loss, at::Tensor& dP, at::Tensor& g_w_out, at::Tensor& g_b_out, at::Tensor& g_b_dst);
+void tgn_metrics(const at::Tensor& scores, const at::Tensor& n_ev, at::Tensor& out);
+void tgn_link_proj_bwd(const at::Tensor& dP, const at::Tensor& out, const at::Tensor& n_roots,
+                       const at::Tensor& w_src, const at::Tensor& w_dst, at::Tensor& g_wsrc, at::Tensor& g_bsrc,
+                       at::Tensor& g_wdst, at::Tensor& g_bdst, at::Tensor& dout);
+void adam_flat(at::Tensor& p, const at::Tensor& g, at::Tensor& m, at::Tensor& v, at::Tensor& step, at::Tensor& done,
+               double lr, double b1, double b2, double eps, double wd, double grad_scale);
+
+PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
+  m.doc() = "starry_unigraph sm_100a kernels (tcgen05 GEMMs, TGN step, DTDG ops, collectives)";
+  m.def("status_read", &status_read, "read (and clear) the device status word", py::arg("clear") = true);
+  m.def("linear_fwd", &linear_fwd);
+  m.def("linear_dgrad", &linear_dgrad);
+  m.def("linear_wgrad", &linear_wgrad);
+  m.def("tgn_prep", &tgn_prep);
+  m.def("tgn_sample", &tgn_sample);
+  m.def("tgn_memory_update", &tgn_memory_update);
+  m.def("tgn_mailbox_write", &tgn_mailbox_write);
+  m.def("tgn_attn_proj", &tgn_attn_proj);
+  m.def("tgn_attn_fwd", &tgn_attn_fwd);
+  m.def("tgn_attn_bwd", &tgn_attn_bwd);
+  m.def("tgn_out_fwd", &tgn_out_fwd);
+  m.def("tgn_out_bwd", &tgn_out_bwd);
+  m.def("tgn_attn_proj_bwd", &tgn_attn_proj_bwd);
+  m.def("tgn_out_proj_bwd", &tgn_out_proj_bwd);
+  m.def("tgn_link_proj", &tgn_link_proj);
+  m.def("tgn_link_loss", &tgn_link_loss);
+  m.def("tgn_metrics", &tgn_metrics);
+  m.def("tgn_link_proj_bwd", &tgn_link_proj_bwd);
+  m.def("adam_flat", &adam_flat);
+}

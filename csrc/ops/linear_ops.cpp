@@ -1,0 +1,120 @@
+// nn.Linear forward / data-gradient / weight-gradient on the tcgen05 GEMM.
+//
+//   linear_fwd     : Y = act(X W^T + b)
+//   linear_dgrad   : dX = dY W              (B operand = W^T evaluated on the fly)
+//   linear_wgrad   : dW += dY^T X, db += sum_rows dY   (split-K, atomic epilogue;
+//                    the bias gradient comes from a constant-1 column appended
+//                    to X inside the producer)
+#include "host_common.h"
+
+using namespace su;
+
+// Reads (and optionally clears) the device status word. Synchronises the stream.
+int64_t status_read(bool clear) {
+  const int dev = at::cuda::current_device();
+  int h = 0;
+  int* p = device_status_ptr(dev);
+  C10_CUDA_CHECK(cudaMemcpyAsync(&h, p, sizeof(int), cudaMemcpyDeviceToHost, cur_stream()));
+  C10_CUDA_CHECK(cudaStreamSynchronize(cur_stream()));
+  if (clear) C10_CUDA_CHECK(cudaMemsetAsync(p, 0, sizeof(int), cur_stream()));
+  return h;
+}
+
+static WeightLayout single_weight_layout(const at::Tensor& w) {
+  const int N = static_cast<int>(w.size(0)), K = static_cast<int>(w.size(1));
+  WeightLayout L;
+  L.nblk = 1;
+  L.nseg = 1;
+  L.blk_rows[0] = N;
+  L.blk_pad[0] = N;
+  L.seg_kpad[0] = pad8(K);
+  L.cell[0][0] = wcell(w, 0, 0, K);
+  return L;
+}
+
+at::Tensor linear_fwd(const at::Tensor& x, const at::Tensor& w, const c10::optional<at::Tensor>& bias, int64_t act) {
+  SU_CHECK_CUDA(x); SU_CHECK_F32(x); SU_CHECK_F32(w); SU_CHECK_CONTIG(w);
+  TORCH_CHECK(x.dim() == 2 && x.stride(1) == 1, "x must be a row-major matrix");
+  const int M = static_cast<int>(x.size(0)), K = static_cast<int>(x.size(1)), N = static_cast<int>(w.size(0));
+  TORCH_CHECK(w.size(1) == K, "shape mismatch");
+  auto y = at::empty({M, N}, x.options());
+  if (M == 0) return y;
+  SegSource a;
+  a.nseg = 1;
+  a.seg[0] = seg_f32(x, K, pad8(K));
+  WeightSource b;
+  b.L = single_weight_layout(w);
+  EpiLinear e;
+  e.out = y.data_ptr<float>();
+  e.ldo = N;
+  e.ncols = N;
+  e.bias = opt_ptr<float>(bias);
+  e.act = static_cast<int>(act);
+  GemmShape sh;
+  sh.M = M;
+  sh.N = N;
+  sh.K = pad8(K);
+  gemm(a, b, e, sh, cur_stream());
+  SU_LAUNCH_CHECK();
+  return y;
+}
+
+at::Tensor linear_dgrad(const at::Tensor& dy, const at::Tensor& w) {
+  SU_CHECK_CUDA(dy); SU_CHECK_F32(dy); SU_CHECK_CONTIG(dy); SU_CHECK_F32(w); SU_CHECK_CONTIG(w);
+  const int M = static_cast<int>(dy.size(0)), N = static_cast<int>(w.size(0)), K = static_cast<int>(w.size(1));
+  auto dx = at::empty({M, K}, dy.options());
+  if (M == 0) return dx;
+  SegSource a;
+  a.nseg = 1;
+  a.seg[0] = seg_f32(dy, N, pad8(N));
+  WeightTSource b;
+  b.L = single_weight_layout(w);
+  b.L.blk_pad[0] = pad8(N);
+  EpiLinear e;
+  e.out = dx.data_ptr<float>();
+  e.ldo = K;
+  e.ncols = K;
+  GemmShape sh;
+  sh.M = M;
+  sh.N = K;
+  sh.K = pad8(N);
+  gemm(a, b, e, sh, cur_stream());
+  SU_LAUNCH_CHECK();
+  return dx;
+}
+
+void linear_wgrad(const at::Tensor& dy, const at::Tensor& x, at::Tensor& dw, const c10::optional<at::Tensor>& db) {
+  SU_CHECK_CUDA(dy); SU_CHECK_F32(dy); SU_CHECK_CONTIG(dy); SU_CHECK_F32(x); SU_CHECK_F32(dw); SU_CHECK_CONTIG(dw);
+  const int M = static_cast<int>(dy.size(0)), N = static_cast<int>(dy.size(1)), K = static_cast<int>(x.size(1));
+  if (M == 0) return;
+  TransposedSource a;  // A[n, m] = dY[m, n]
+  a.inner.nseg = 1;
+  a.inner.seg[0] = seg_f32(dy, N, pad8(N));
+  a.inner_rows = M;
+  TransposedSource b;  // B[k, m] = X[m, k] (+ ones column for the bias gradient)
+  b.inner.nseg = 2;
+  b.inner.seg[0] = seg_f32(x, K, pad8(K));
+  b.inner.seg[1] = seg_ones();
+  b.inner_rows = M;
+  EpiWeightGrad e;
+  e.L.nblk = 1;
+  e.L.nseg = 2;
+  e.L.blk_rows[0] = N;
+  e.L.blk_pad[0] = N;
+  e.L.seg_kpad[0] = pad8(K);
+  e.L.seg_kpad[1] = 8;
+  e.L.cell[0][0] = wcell(dw, 0, 0, K);
+  e.bias_grad[0] = (db.has_value() && db->defined()) ? db->data_ptr<float>() : nullptr;
+  e.bias_seg = 1;
+  e.ncols = pad8(K) + 8;
+  GemmShape sh;
+  sh.M = N;
+  sh.N = pad8(K) + 8;
+  sh.K = M;
+  const int nchunks = (M + kBK - 1) / kBK;
+  const int tiles = ((N + kBM - 1) / kBM) * ((sh.N + 255) / 256);
+  const int want = std::max(1, (2 * num_sms(at::cuda::current_device())) / std::max(1, tiles));
+  sh.ksplit = std::max(1, std::min(nchunks, want));
+  gemm(a, b, e, sh, cur_stream());
+  SU_LAUNCH_CHECK();
+}

@@ -1,0 +1,296 @@
+"""Raw temporal event loading and the event -> snapshot conversion.
+
+Formats (reference data/raw_temporal.py:175-439):
+  * ``mock``: deterministic ring stream (src = i mod N, dst = i+1 mod N).
+  * ``<root>/<name>/edges.csv`` with ``src,dst,time|ts[,w|weight]`` columns, optional
+    ``edge_features.pt`` and ``node_temporal_features.csv`` / ``node_features.csv``.
+  * ``<name>.edges`` / ``edges.txt``: whitespace or comma separated rows
+    ``u v ts`` | ``u v w ts`` | ``idx u v ts ...``; node ids are compacted.
+  * ``synthetic``: generated from ``data.synthetic`` (see data/synthetic.py).
+  Unknown/missing data falls back to the mock stream, as the reference does.
+
+``build_snapshot_dataset_from_events`` cuts the stream into equal-count
+snapshots; features are [in_deg, out_deg] (or the temporal node features),
+labels log(in_deg + 1) of the same snapshot, the last snapshot unlabeled.
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass
+from pathlib import Path
+from typing import Any
+
+import numpy as np
+import torch
+
+NODE_FEATURE_FILE_CANDIDATES = ("node_temporal_features.csv", "node_features.csv")
+
+
+@dataclass
+class NodeTemporalFeatureTable:
+    node_ids: torch.Tensor
+    ts: torch.Tensor
+    values: torch.Tensor
+    feature_names: tuple[str, ...]
+    source: str
+
+    @property
+    def dim(self) -> int:
+        return int(self.values.size(-1)) if self.values.dim() == 2 else 0
+
+    @property
+    def size(self) -> int:
+        return int(self.node_ids.numel())
+
+
+@dataclass
+class RawTemporalEvents:
+    src: torch.Tensor
+    dst: torch.Tensor
+    ts: torch.Tensor
+    weight: torch.Tensor
+    edge_feat: torch.Tensor
+    num_nodes: int
+    num_edges: int
+    source: str
+    node_temporal_features: NodeTemporalFeatureTable | None = None
+
+
+def _as_int(value: Any, default: int) -> int:
+    try:
+        return int(value)
+    except (TypeError, ValueError):
+        return default
+
+
+def _parse_edge_row(parts: list[str]) -> tuple[int, int, float, float] | None:
+    if len(parts) == 3:
+        u, v, ts = parts
+        w = 1.0
+    elif len(parts) == 4:
+        u, v, w, ts = parts
+    elif len(parts) >= 5:
+        _, u, v, ts = parts[:4]
+        w = 1.0
+    else:
+        return None
+    return int(float(u)), int(float(v)), float(ts), float(w)
+
+
+def _load_node_temporal_features(dataset_dir: Path) -> NodeTemporalFeatureTable | None:
+    path = next((dataset_dir / n for n in NODE_FEATURE_FILE_CANDIDATES if (dataset_dir / n).exists()), None)
+    if path is None:
+        return None
+    import pandas as pd
+
+    frame = pd.read_csv(path)
+    if frame.empty:
+        return NodeTemporalFeatureTable(torch.empty(0, dtype=torch.long), torch.empty(0), torch.empty(0, 0), (), str(path))
+    node_col = next((c for c in ("node_id", "node", "id") if c in frame.columns), None)
+    if node_col is None:
+        raise ValueError(f"Node feature file {path} must contain one of: node_id, node, id")
+    ts_col = next((c for c in ("time", "ts", "timestamp") if c in frame.columns), None)
+    reserved = {node_col} | ({ts_col} if ts_col else set())
+    feat_cols = [c for c in frame.columns if c not in reserved and pd.api.types.is_numeric_dtype(frame[c])]
+    if not feat_cols:
+        raise ValueError(f"Node feature file {path} must contain at least one numeric feature column")
+    node_ids = torch.as_tensor(frame[node_col].to_numpy(dtype="int64"))
+    ts = torch.zeros(node_ids.numel()) if ts_col is None else torch.as_tensor(frame[ts_col].to_numpy(dtype="float32"))
+    values = torch.as_tensor(frame[feat_cols].to_numpy(dtype="float32"))
+    order = torch.argsort(ts, stable=True)
+    return NodeTemporalFeatureTable(node_ids[order], ts[order], values[order], tuple(feat_cols), str(path))
+
+
+def _mock_events(dataset_name: str, config: dict[str, Any]) -> RawTemporalEvents:
+    snaps = max(1, _as_int(config.get("train", {}).get("snaps"), 8))
+    event_count = max(16, snaps * 4)
+    num_nodes = max(8, min(128, event_count // 2))
+    idx = torch.arange(event_count, dtype=torch.long)
+    return RawTemporalEvents(
+        src=idx % num_nodes,
+        dst=(idx + 1) % num_nodes,
+        ts=torch.arange(event_count, dtype=torch.float32),
+        weight=torch.ones(event_count),
+        edge_feat=torch.ones(event_count, 1),
+        num_nodes=num_nodes,
+        num_edges=event_count,
+        source=f"mock:{dataset_name}",
+    )
+
+
+def _synthetic_events(dataset_name: str, config: dict[str, Any]) -> RawTemporalEvents:
+    from .synthetic import CTDG_PRESETS, zipf_event_stream
+
+    spec = dict(config.get("data", {}).get("synthetic") or {})
+    preset = spec.pop("preset", None)
+    seed = int(spec.pop("seed", 0))
+    params = dict(CTDG_PRESETS[preset]) if preset else {}
+    params.update(spec)
+    stream = zipf_event_stream(**params, seed=seed)
+    n = int(stream["src"].numel())
+    return RawTemporalEvents(
+        src=stream["src"],
+        dst=stream["dst"],
+        ts=stream["ts"],
+        weight=torch.ones(n),
+        edge_feat=stream["edge_feat"],
+        num_nodes=int(stream["num_nodes"]),
+        num_edges=n,
+        source=f"synthetic:{preset or dataset_name}",
+    )
+
+
+def _load_from_ctdg_csv(dataset_dir: Path) -> RawTemporalEvents | None:
+    edges_path = dataset_dir / "edges.csv"
+    if not edges_path.exists():
+        return None
+    import pandas as pd
+
+    nfeat = _load_node_temporal_features(dataset_dir)
+    frame = pd.read_csv(edges_path)
+    if frame.empty or "src" not in frame.columns:
+        if frame.empty:
+            return RawTemporalEvents(torch.empty(0, dtype=torch.long), torch.empty(0, dtype=torch.long), torch.empty(0),
+                                     torch.empty(0), torch.empty(0, 1), nfeat.size if nfeat else 0, 0, str(edges_path), nfeat)
+        return None
+    src = torch.as_tensor(frame["src"].to_numpy(dtype="int64"))
+    dst = torch.as_tensor(frame["dst"].to_numpy(dtype="int64"))
+    ts_col = "time" if "time" in frame.columns else ("ts" if "ts" in frame.columns else frame.columns[-1])
+    ts = torch.as_tensor(frame[ts_col].to_numpy(dtype="float32"))
+    wcol = "w" if "w" in frame.columns else ("weight" if "weight" in frame.columns else None)
+    weight = torch.ones(src.numel()) if wcol is None else torch.as_tensor(frame[wcol].to_numpy(dtype="float32"))
+    num_nodes = int(max(int(src.max()), int(dst.max())) + 1) if src.numel() else 0
+    if nfeat is not None and nfeat.size > 0:
+        num_nodes = max(num_nodes, int(nfeat.node_ids.max()) + 1)
+    feat_path = dataset_dir / "edge_features.pt"
+    if feat_path.exists():
+        edge_feat = torch.load(feat_path, map_location="cpu").float()
+        if edge_feat.dim() == 1:
+            edge_feat = edge_feat.view(-1, 1)
+    else:
+        edge_feat = torch.ones(src.numel(), 1)
+    return RawTemporalEvents(src.long(), dst.long(), ts.float(), weight.float(), edge_feat, num_nodes,
+                             int(src.numel()), str(edges_path), nfeat)
+
+
+def _load_from_edge_file(dataset_dir: Path, dataset_name: str) -> RawTemporalEvents | None:
+    candidates = (dataset_dir / f"{dataset_name}.edges", dataset_dir / "edges.txt", dataset_dir / "edges.csv")
+    edge_path = next((c for c in candidates if c.exists()), None)
+    if edge_path is None:
+        return None
+    nfeat = _load_node_temporal_features(dataset_dir)
+    rows = []
+    with edge_path.open("r", encoding="utf-8") as handle:
+        for raw in handle:
+            line = raw.strip()
+            if not line or line.startswith(("%", "#")):
+                continue
+            parts = [p.strip() for p in line.split(",")] if "," in line else line.split()
+            try:
+                parsed = _parse_edge_row(parts)
+            except ValueError:
+                continue
+            if parsed is not None:
+                rows.append(parsed)
+    if not rows:
+        return None
+    arr = np.asarray(rows, dtype=np.float64)
+    order = np.argsort(arr[:, 2], kind="stable")
+    arr = arr[order]
+    src_raw = arr[:, 0].astype(np.int64)
+    dst_raw = arr[:, 1].astype(np.int64)
+    extra = nfeat.node_ids.numpy() if (nfeat is not None and nfeat.size > 0) else np.empty(0, np.int64)
+    unique, inverse = np.unique(np.concatenate([src_raw, dst_raw, extra]), return_inverse=True)
+    n = src_raw.size
+    src = torch.from_numpy(inverse[:n].astype(np.int64))
+    dst = torch.from_numpy(inverse[n:2 * n].astype(np.int64))
+    if nfeat is not None and nfeat.size > 0:
+        nfeat = NodeTemporalFeatureTable(torch.from_numpy(inverse[2 * n:].astype(np.int64)), nfeat.ts, nfeat.values,
+                                         nfeat.feature_names, nfeat.source)
+    return RawTemporalEvents(src, dst, torch.from_numpy(arr[:, 2].astype(np.float32)),
+                             torch.from_numpy(arr[:, 3].astype(np.float32)), torch.ones(n, 1), int(unique.size), n,
+                             str(edge_path), nfeat)
+
+
+def load_raw_temporal_events(root: Path | str, dataset_name: str, config: dict[str, Any]) -> RawTemporalEvents:
+    fmt = str(config.get("data", {}).get("format", "auto")).lower()
+    if fmt == "mock":
+        return _mock_events(dataset_name, config)
+    if fmt == "synthetic":
+        return _synthetic_events(dataset_name, config)
+    dataset_dir = Path(root).expanduser().resolve() / dataset_name
+    events = _load_from_ctdg_csv(dataset_dir)
+    if events is None:
+        events = _load_from_edge_file(dataset_dir, dataset_name)
+    if events is None:
+        return _mock_events(dataset_name, config)
+    return events
+
+
+def _compute_degrees(edge_index: torch.Tensor, edge_weight: torch.Tensor, num_nodes: int):
+    in_deg = torch.zeros(num_nodes)
+    out_deg = torch.zeros(num_nodes)
+    if edge_index.numel():
+        in_deg.index_add_(0, edge_index[1].long(), edge_weight.float())
+        out_deg.index_add_(0, edge_index[0].long(), edge_weight.float())
+    return in_deg, out_deg
+
+
+def _snapshot_end_timestamps(events: RawTemporalEvents, snaps: int) -> list[float]:
+    if events.num_edges == 0:
+        return [0.0] * snaps
+    per = max(1, (events.num_edges + snaps - 1) // snaps)
+    out, prev = [], float(events.ts[0])
+    for i in range(snaps):
+        start, end = i * per, min(events.num_edges, (i + 1) * per)
+        if start < end:
+            prev = float(events.ts[end - 1])
+            out.append(prev)
+        else:
+            out.append(prev if out else float(events.ts[-1]))
+    return out
+
+
+def _build_snapshot_node_features(events: RawTemporalEvents, snaps: int) -> list[torch.Tensor] | None:
+    table = events.node_temporal_features
+    if table is None or table.size == 0 or table.dim == 0:
+        return None
+    order = torch.argsort(table.ts, stable=True)
+    ids, ts, vals = table.node_ids[order], table.ts[order], table.values[order]
+    current = torch.zeros(events.num_nodes, table.dim)
+    cursor, out = 0, []
+    for end_ts in _snapshot_end_timestamps(events, snaps):
+        while cursor < ts.numel() and float(ts[cursor]) <= end_ts:
+            current[int(ids[cursor])] = vals[cursor]
+            cursor += 1
+        out.append(current.clone())
+    return out
+
+
+def build_snapshot_dataset_from_events(events: RawTemporalEvents, snaps: int, input_x=None, input_y=None) -> dict[str, Any]:
+    snaps = max(1, int(snaps))
+    num_edges = int(events.num_edges)
+    feats = input_x if input_x is not None else _build_snapshot_node_features(events, snaps)
+    per = max(1, (num_edges + snaps - 1) // snaps) if num_edges > 0 else 1
+    dataset = []
+    for i in range(snaps):
+        start, end = i * per, min(num_edges, (i + 1) * per)
+        if start >= end:
+            ei, ew = torch.empty((2, 0), dtype=torch.long), torch.empty(0)
+        else:
+            ei = torch.stack([events.src[start:end], events.dst[start:end]]).long()
+            ew = events.weight[start:end].float()
+        in_deg, out_deg = _compute_degrees(ei, ew, events.num_nodes)
+        labels = None if i == snaps - 1 else torch.log(in_deg + 1.0)
+        x = torch.stack([in_deg, out_deg], dim=1) if feats is None else feats[i]
+        dataset.append({"edge_index": ei, "edge_weight": ew, "x": x, "y": labels if input_y is None else input_y[i]})
+    return {
+        "num_nodes": int(events.num_nodes),
+        "num_edges": num_edges,
+        "num_snapshots": len(dataset),
+        "num_life_edges": int(sum(int(d["edge_weight"].numel()) for d in dataset)),
+        "dataset": dataset,
+        "source": events.source,
+        "node_feat_dim": int(dataset[0]["x"].size(-1)) if dataset else 0,
+        "node_feature_source": "temporal_node_features" if feats is not None and input_x is None else
+        ("input" if input_x is not None else "degree_fallback"),
+    }

@@ -1,0 +1,300 @@
+"""Fused sm_100a TGN training / evaluation step.
+
+One step (reference backends/ctdg/runtime/runtime.py:225-328) is a fixed
+sequence of kernel launches over static device buffers, so it can be captured
+once per (split, mode) in a CUDA graph and replayed:
+
+  prep -> sample -> GRU memory update (fused scatter) -> mailbox write ->
+  Q/KV projections (gather + time encoding fused into the GEMM producers) ->
+  attention -> W_out + dropout + ReLU + LayerNorm -> link projections ->
+  BCE loss + logits gradient (+ AP/AUC) -> [backward GEMMs -> gradient sync ->
+  fused Adam].
+
+Shapes are padded to ``bmax`` events and ``rmax = 2 * bmax`` roots; the real
+counts live on the device, so the host never synchronises inside a step.
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass
+from typing import Any, Callable
+
+import torch
+
+from starry_unigraph.ops import cuda_ext
+from starry_unigraph.ops.flat import FlatParams, FusedAdam
+
+
+@dataclass
+class TGNShapes:
+    bmax: int
+    k: int
+    D: int
+    E: int
+    T: int
+    Do: int
+    H: int
+    K: int
+
+    @property
+    def rmax(self) -> int:
+        return 2 * self.bmax
+
+    @property
+    def slot_width(self) -> int:
+        return 2 * self.D + self.E
+
+
+class TGNCudaEngine:
+    def __init__(
+        self,
+        *,
+        model: torch.nn.Module,
+        updater: torch.nn.Module,
+        memory: Any,
+        edge_feat: torch.Tensor,
+        neg_pool: torch.Tensor,
+        csr_provider: Callable[[str], Any],
+        bmax: int,
+        fanout: int,
+        policy: str,
+        lr: float,
+        dropout: float,
+        att_dropout: float,
+        num_head: int,
+        seed: int = 0,
+        use_graphs: bool = True,
+        grad_sync: Callable[[torch.Tensor], float] | None = None,
+    ) -> None:
+        self.C = cuda_ext()
+        self.model = model
+        self.updater = updater
+        self.memory = memory
+        dev = memory.memory.device
+        self.device = dev
+        conv = model.conv
+        D = memory.hidden_dim
+        E = memory.edge_feat_dim
+        self.s = TGNShapes(bmax=int(bmax), k=int(fanout), D=D, E=E, T=conv.dim_time, Do=conv.dim_out,
+                           H=int(num_head), K=memory.mailbox_slots)
+        if self.s.T <= 0:
+            raise ValueError("the fused TGN step requires dim_time > 0")
+        self.policy = 0 if policy == "recent" else 1
+        self.dropout = float(dropout)
+        self.att_dropout = float(att_dropout)
+        self.seed = int(seed)
+        self.use_graphs = bool(use_graphs)
+        self.csr_provider = csr_provider
+        self.grad_sync = grad_sync
+        ef = edge_feat.to(dev, dtype=torch.float32)
+        if ef.dim() == 1:
+            ef = ef.view(-1, 1)
+        self.efeat = ef.contiguous()
+        self.neg_pool = neg_pool.to(dev).long().contiguous()
+        # parameters live in one flat buffer (fused Adam, one-buffer gradient sync)
+        self.flat = FlatParams([model], dev)
+        self.opt = FusedAdam(self.flat, lr=lr)
+        self._alloc()
+        self._graphs: dict[tuple[str, bool], torch.cuda.CUDAGraph] = {}
+        self._warm: dict[tuple[str, bool], int] = {}
+
+    # ------------------------------------------------------------------ buffers
+    def _alloc(self) -> None:
+        s, dev = self.s, self.device
+        f32 = dict(dtype=torch.float32, device=dev)
+        i64 = dict(dtype=torch.int64, device=dev)
+        i32 = dict(dtype=torch.int32, device=dev)
+        N = self.memory.num_nodes
+        B, R, k = s.bmax, s.rmax, s.k
+        self.ev_src = torch.zeros(B, **i64)
+        self.ev_dst = torch.zeros(B, **i64)
+        self.ev_ts = torch.zeros(B, **f32)
+        self.ev_eid = torch.zeros(B, **i64)
+        self.n_ev = torch.zeros(1, **i32)
+        self.stamp = torch.zeros(N, **i32)
+        self.node2root = torch.zeros(N, **i32)
+        self.step_ctr = torch.zeros(1, **i64)
+        self.roots = torch.full((R,), -1, **i64)
+        self.n_roots = torch.zeros(1, **i32)
+        self.src_idx = torch.zeros(B, **i32)
+        self.dst_idx = torch.zeros(B, **i32)
+        self.neg = torch.zeros(B, **i64)
+        self.neg_idx = torch.zeros(B, **i32)
+        self.ts_max = torch.zeros(1, **f32)
+        self.root_ts = torch.zeros(1, **i64)
+        self.win_key = torch.zeros(2 * R, **i64)
+        self.win = torch.zeros(2 * R, **i32)
+        self.cnt = torch.zeros(2 * R, **i32)
+        self.nbr = torch.zeros(R * k, **i64)
+        self.nbr_eid = torch.zeros(R * k, **i64)
+        self.nbr_dt = torch.zeros(R * k, **f32)
+        self.nbr_cnt = torch.zeros(R, **i32)
+        self.edge_total = torch.zeros(1, **i32)
+        self.agg_buf = torch.zeros(R, s.D, **f32)
+        self.agg_buf2 = torch.zeros(R, s.D, **f32)
+        self.mem_prev = torch.zeros(R, s.D, **f32)
+        self.Q = torch.zeros(R, s.Do, **f32)
+        self.KV = torch.zeros(R * k, 2 * s.Do, **f32)
+        self.att_p = torch.zeros(R * k, s.H, **f32)
+        self.agg = torch.zeros(R, s.Do, **f32)
+        self.out = torch.zeros(R, s.Do, **f32)
+        self.xsave = torch.zeros(R, s.Do, **f32)
+        self.mean = torch.zeros(R, **f32)
+        self.rstd = torch.zeros(R, **f32)
+        self.P = torch.zeros(R, 2 * s.D, **f32)
+        self.scores = torch.zeros(2 * B, **f32)
+        self.loss = torch.zeros(1, **f32)
+        self.metrics = torch.zeros(3, **f32)
+        self.dP = torch.zeros(R, 2 * s.D, **f32)
+        self.dout = torch.zeros(R, s.D, **f32)
+        self.dpre = torch.zeros(R, s.Do, **f32)
+        self.dagg = torch.zeros(R, s.Do, **f32)
+        self.dKV = torch.zeros(R * k, 2 * s.Do, **f32)
+        self.dQ = torch.zeros(R, s.Do, **f32)
+
+    # ------------------------------------------------------------------ inputs
+    def load_batch(self, src: torch.Tensor, dst: torch.Tensor, ts: torch.Tensor, eid: torch.Tensor) -> None:
+        """Copy one batch into the static input buffers (H2D when the inputs are on the host)."""
+        n = int(src.numel())
+        if n > self.s.bmax:
+            raise ValueError(f"batch of {n} events exceeds bmax={self.s.bmax}")
+        nb = src.device.type == "cpu" and src.is_pinned()
+        self.ev_src[:n].copy_(src, non_blocking=nb)
+        self.ev_dst[:n].copy_(dst, non_blocking=nb)
+        self.ev_ts[:n].copy_(ts, non_blocking=nb)
+        self.ev_eid[:n].copy_(eid, non_blocking=nb)
+        self.n_ev.fill_(n)
+
+    def load_packed(self, packed_host: torch.Tensor, n: int) -> None:
+        """Single H2D copy of a pinned int64 [4, bmax] pack (src, dst, ts-bits, eid) plus the count."""
+        self._packed_dev = getattr(self, "_packed_dev", None)
+        if self._packed_dev is None:
+            self._packed_dev = torch.zeros(4, self.s.bmax, dtype=torch.int64, device=self.device)
+        self._packed_dev.copy_(packed_host, non_blocking=True)
+        self.ev_src.copy_(self._packed_dev[0])
+        self.ev_dst.copy_(self._packed_dev[1])
+        self.ev_ts.copy_(self._packed_dev[2].to(torch.int32).view(torch.float32))
+        self.ev_eid.copy_(self._packed_dev[3])
+        self.n_ev.fill_(n)
+
+    # ------------------------------------------------------------------ step
+    def _params(self):
+        m, u = self.model, self.updater
+        c = m.conv
+        return m, u, c
+
+    def _forward(self, split: str, train: bool) -> None:
+        C, s = self.C, self.s
+        m, u, c = self._params()
+        mem = self.memory
+        csr = self.csr_provider(split)
+        drop = self.dropout if train else 0.0
+        adrop = self.att_dropout if train else 0.0
+        C.tgn_prep(self.ev_src, self.ev_dst, self.ev_ts, self.n_ev, self.neg_pool, self.stamp, self.node2root,
+                   self.step_ctr, self.seed, self.roots, self.n_roots, self.src_idx, self.dst_idx, self.neg,
+                   self.neg_idx, self.ts_max, self.root_ts, self.win_key, self.win, self.cnt)
+        C.tgn_sample(self.roots, self.n_roots, self.root_ts, csr.rowptr, csr.nbr, csr.eid, csr.ts, s.k, self.policy,
+                     self.seed, self.step_ctr, self.nbr, self.nbr_eid, self.nbr_dt, self.nbr_cnt, self.edge_total)
+        g = u.mail_aggregator
+        cell = u.memory_cell
+        C.tgn_memory_update(self.roots, self.n_roots, mem.mailbox, s.K, mem.memory, mem.memory_ts, self.ts_max,
+                            g.weight_ih_l0, g.weight_hh_l0, g.bias_ih_l0, g.bias_hh_l0, cell.weight_ih,
+                            cell.weight_hh, cell.bias_ih, cell.bias_hh, self.agg_buf, self.agg_buf2, self.mem_prev)
+        C.tgn_mailbox_write(self.roots, self.n_roots, self.win, self.cnt, self.src_idx, self.dst_idx, self.ev_eid,
+                            self.ev_ts, self.mem_prev, self.efeat, s.E, mem.mailbox, mem.mailbox_ts, mem.next_mail_pos)
+        te = c.time_enc.w
+        C.tgn_attn_proj(mem.memory, self.roots, self.n_roots, self.nbr, self.nbr_eid, self.nbr_dt, self.nbr_cnt,
+                        self.efeat, s.E, te.weight, te.bias, c.w_q.weight, c.w_q.bias, c.w_k.weight, c.w_k.bias,
+                        c.w_v.weight, c.w_v.bias, self.Q, self.KV)
+        C.tgn_attn_fwd(self.Q, self.KV, self.nbr_cnt, self.n_roots, s.H, adrop, self.seed, self.step_ctr, self.att_p,
+                       self.agg)
+        C.tgn_out_fwd(self.agg, mem.memory, self.roots, self.n_roots, c.w_out.weight, c.w_out.bias,
+                      c.layer_norm.weight, c.layer_norm.bias, drop, self.seed, self.step_ctr, self.edge_total,
+                      self.out, self.xsave, self.mean, self.rstd)
+        C.tgn_link_proj(self.out, self.n_roots, m.src_fc.weight, m.src_fc.bias, m.dst_fc.weight, m.dst_fc.bias,
+                        self.P)
+        self.loss.zero_()
+        if train:
+            self.flat.zero_grad()
+            self.dP.zero_()
+        G = self.flat.grad_views
+        gw = {n.split(".", 1)[1]: v for n, v in G.items()}
+        C.tgn_link_loss(self.P, self.src_idx, self.dst_idx, self.neg_idx, self.n_ev, m.dst_fc.bias, m.out_fc.weight,
+                        m.out_fc.bias, train, self.scores, self.loss, self.dP, gw["out_fc.weight"], gw["out_fc.bias"],
+                        gw["dst_fc.bias"])
+        C.tgn_metrics(self.scores, self.n_ev, self.metrics)
+        if train:
+            self._backward(gw)
+
+    def _backward(self, gw: dict[str, torch.Tensor]) -> None:
+        C, s = self.C, self.s
+        m, u, c = self._params()
+        mem = self.memory
+        C.tgn_link_proj_bwd(self.dP, self.out, self.n_roots, m.src_fc.weight, m.dst_fc.weight, gw["src_fc.weight"],
+                            gw["src_fc.bias"], gw["dst_fc.weight"], gw["dst_fc.bias"], self.dout)
+        C.tgn_out_bwd(self.dout, self.xsave, self.mean, self.rstd, c.layer_norm.weight, self.n_roots, self.dropout,
+                      self.seed, self.step_ctr, self.edge_total, self.dpre, gw["conv.layer_norm.weight"],
+                      gw["conv.layer_norm.bias"])
+        C.tgn_out_proj_bwd(self.dpre, self.agg, mem.memory, self.roots, self.n_roots, c.w_out.weight,
+                           gw["conv.w_out.weight"], gw["conv.w_out.bias"], self.dagg)
+        C.tgn_attn_bwd(self.Q, self.KV, self.att_p, self.dagg, self.nbr_cnt, self.n_roots, s.H, self.att_dropout,
+                       self.seed, self.step_ctr, self.dKV, self.dQ)
+        te = c.time_enc.w
+        C.tgn_attn_proj_bwd(mem.memory, self.roots, self.n_roots, self.nbr, self.nbr_eid, self.nbr_dt, self.nbr_cnt,
+                            self.efeat, s.E, te.weight, te.bias, c.w_q.weight, c.w_k.weight, c.w_v.weight, self.dQ,
+                            self.dKV, gw["conv.w_q.weight"], gw["conv.w_q.bias"], gw["conv.w_k.weight"],
+                            gw["conv.w_k.bias"], gw["conv.w_v.weight"], gw["conv.w_v.bias"],
+                            gw["conv.time_enc.w.weight"], gw["conv.time_enc.w.bias"])
+        scale = 1.0
+        if self.grad_sync is not None:
+            scale = self.grad_sync(self.flat.grad)
+        self.opt.step(grad_scale=scale)
+
+    def step(self, split: str, train: bool) -> None:
+        """Run one step on the batch in the static buffers (graph replay after warm-up)."""
+        key = (split, bool(train))
+        if not self.use_graphs:
+            self._forward(split, train)
+            return
+        g = self._graphs.get(key)
+        if g is not None:
+            g.replay()
+            return
+        warm = self._warm.get(key, 0)
+        if warm < 2:
+            self._forward(split, train)
+            self._warm[key] = warm + 1
+            return
+        # capture (the capture run itself does not execute the kernels): save and
+        # restore the mutable state the step touches, then replay once for real.
+        state = self._snapshot_state()
+        g = torch.cuda.CUDAGraph()
+        torch.cuda.synchronize(self.device)
+        with torch.cuda.graph(g):
+            self._forward(split, train)
+        self._restore_state(state)
+        self._graphs[key] = g
+        g.replay()
+
+    def _snapshot_state(self):
+        return None  # graph capture does not launch work; device state is untouched
+
+    def _restore_state(self, state) -> None:
+        return None
+
+    def launches_per_step(self, train: bool = True) -> int:
+        """Number of framework kernel launches in one step (memsets excluded)."""
+        fwd = 10 + self.s.K  # prep, sample, K+1 GRU GEMMs, mailbox, Q, KV, attention, out+LN, link proj, loss, metrics
+        bwd = 11             # link-proj (2), LN, out-proj (2), attention, W_q/W_kv/time-encoder (4), Adam
+        return fwd + (bwd if train else 0)
+
+    def reset_graphs(self) -> None:
+        self._graphs.clear()
+        self._warm.clear()
+
+    # ------------------------------------------------------------------ results
+    def read_scalars(self) -> tuple[float, dict[str, float]]:
+        vals = torch.cat([self.loss, self.metrics]).tolist()
+        return vals[0], {"ap": vals[1], "auc": vals[2], "mrr": vals[3]}
+
+    def pos_probs(self, n: int) -> torch.Tensor:
+        return torch.sigmoid(self.scores[:n])

@@ -1,0 +1,341 @@
+"""SchedulerSession: the public prepare / train / predict lifecycle
+(reference session.py:25-439).
+
+``from_config`` merges the YAML config over the defaults, applies torchrun
+variables, validates, resolves the model family and task; ``prepare_data``
+runs the mode's preprocessor; ``build_runtime`` loads the artifacts and builds
+the CTDG online runtime or the DTDG Flare runtime; ``run_epoch`` returns the
+reference's dict (split, steps, local_steps, loss, local_loss, metrics,
+elapsed_s = max over ranks, local_elapsed_s, outputs).
+"""
+from __future__ import annotations
+
+import time
+from pathlib import Path
+from typing import Any
+
+import torch
+import torch.distributed as dist
+
+from starry_unigraph.checkpoint import load_checkpoint, save_checkpoint
+from starry_unigraph.config.schema import detect_graph_mode, load_config, validate_config
+from starry_unigraph.distributed import apply_distributed_env, build_distributed_context
+from starry_unigraph.preprocess.base import load_prepared_from_disk, read_artifact_meta
+from starry_unigraph.registry import ModelRegistry, TaskRegistry
+from starry_unigraph.types import PredictionResult, PreparedArtifacts, RuntimeBundle, SessionContext
+
+ARTIFACT_VERSION = 1
+
+
+def validate_artifacts(prepared: PreparedArtifacts, expected_graph_mode: str,
+                       expected_num_parts: int | None = None) -> dict[str, Any]:
+    """Reference backends/dtdg/preprocess.py:27-53."""
+    if not prepared.meta_path.exists():
+        raise FileNotFoundError(f"Missing artifacts metadata: {prepared.meta_path}")
+    meta = read_artifact_meta(prepared.meta_path)
+    if meta.get("artifact_version") != ARTIFACT_VERSION:
+        raise RuntimeError(f"Artifact version mismatch: expected {ARTIFACT_VERSION}, got {meta.get('artifact_version')}")
+    if meta.get("graph_mode") != expected_graph_mode:
+        raise RuntimeError(f"Artifact graph_mode mismatch: expected {expected_graph_mode}, got {meta.get('graph_mode')}")
+    if expected_num_parts is not None and meta.get("num_parts") != expected_num_parts:
+        raise RuntimeError(f"Artifact num_parts mismatch: expected {expected_num_parts}, got {meta.get('num_parts')}")
+    for sub in ("partitions", "routes"):
+        path = prepared.directories.get(sub, prepared.meta_path.parent.parent / sub) / "manifest.json"
+        if not path.exists():
+            raise FileNotFoundError(f"Missing {sub[:-1]} manifest: {path}")
+    return meta
+
+
+class SchedulerSession:
+    def __init__(self, session_ctx: SessionContext, model_spec: Any, task_adapter: Any):
+        self.ctx = session_ctx
+        self.model_spec = model_spec
+        self.task_adapter = task_adapter
+        self.current_epoch = 0
+        self.global_step = 0
+        self.runtime = RuntimeBundle()
+        self.snapshot_core: Any = None
+        self.ctdg_session: Any = None
+        self.prepared: PreparedArtifacts | None = None
+        self.pipeline_engine: Any = None
+
+    # ------------------------------------------------------------------ construction
+    @classmethod
+    def from_config(cls, config_or_path: str | Path | dict[str, Any], dataset_path: str | Path | None = None,
+                    overrides: dict[str, Any] | None = None) -> "SchedulerSession":
+        config = apply_distributed_env(load_config(config_or_path, overrides=overrides))
+        warnings = validate_config(config)
+        model_spec = ModelRegistry.resolve(model_name=config["model"]["name"], family=config["model"]["family"])
+        task_cls = TaskRegistry.resolve(config["model"]["task"])
+        artifact_root = (Path("artifacts") / config["data"]["name"]).resolve()
+        ctx = SessionContext(config=config, project_root=Path.cwd(),
+                             dataset_path=Path(dataset_path).expanduser().resolve() if dataset_path else None,
+                             artifact_root=artifact_root, dist=build_distributed_context(config), warnings=warnings)
+        return cls(session_ctx=ctx, model_spec=model_spec, task_adapter=task_cls())
+
+    @property
+    def graph_mode(self) -> str:
+        return detect_graph_mode(self.ctx.config)
+
+    def _device(self) -> str:
+        base = str(self.ctx.config["runtime"]["device"])
+        if base == "cuda" and dist.is_available() and dist.is_initialized():
+            return f"cuda:{self.ctx.dist.local_rank}"
+        if base.startswith("cuda") and not torch.cuda.is_available():
+            return "cpu"
+        return base
+
+    # ------------------------------------------------------------------ prepare
+    def prepare_data(self) -> PreparedArtifacts:
+        mode = self.graph_mode
+        if mode == "ctdg":
+            from starry_unigraph.backends.ctdg.preprocess import CTDGPreprocessor
+
+            pre = CTDGPreprocessor()
+        elif mode == "dtdg":
+            from starry_unigraph.backends.dtdg.preprocess import FlareDTDGPreprocessor
+
+            pre = FlareDTDGPreprocessor()
+        elif mode == "chunk":
+            from starry_unigraph.preprocess.chunk import ChunkPreprocessor
+
+            pre = ChunkPreprocessor()
+        else:
+            raise ValueError(f"Unknown graph_mode for preprocessing: {mode!r}")
+        self.prepared = pre.run(self.ctx)
+        self.ctx.prepared_artifacts = self.prepared
+        return self.prepared
+
+    # ------------------------------------------------------------------ runtime
+    def _load_partition(self):
+        flare_dir = self.prepared.directories.get("flare", self.ctx.artifact_root / "flare")
+        if not (flare_dir / "manifest.json").exists():
+            raise FileNotFoundError(f"Missing flare manifest: {flare_dir / 'manifest.json'}")
+        part_id = min(self.ctx.dist.rank, self.ctx.dist.world_size - 1)
+        path = flare_dir / f"part_{part_id:03d}.pth"
+        if not path.exists():
+            raise FileNotFoundError(f"Missing flare partition artifact: {path}")
+        return path, torch.load(path, weights_only=False)
+
+    def build_runtime(self) -> RuntimeBundle:
+        if self.prepared is None:
+            self.prepared = load_prepared_from_disk(self.ctx.artifact_root)
+        self.ctx.prepared_artifacts = self.prepared
+        mode = self.prepared.provider_meta.get("graph_mode")
+        device = self._device()
+        if mode == "ctdg":
+            from starry_unigraph.backends.ctdg.runtime.session import CTDGSession
+
+            if "max_local_batch" in self.prepared.provider_meta:
+                self.ctx.provider_state["max_local_batch"] = self.prepared.provider_meta["max_local_batch"]
+            self.ctdg_session = CTDGSession()
+            self.ctdg_session.build_runtime(self.ctx)
+            self.runtime = self.ctdg_session._runtime
+        elif mode == "dtdg":
+            from starry_unigraph.backends.dtdg import FlareRuntimeLoader, init_flare_training
+
+            validate_artifacts(self.prepared, "dtdg", self.ctx.dist.world_size)
+            path, part = self._load_partition()
+            self.snapshot_core = FlareRuntimeLoader.from_partition_data(
+                data=part, device=device, rank=self.ctx.dist.rank, world_size=self.ctx.dist.world_size,
+                config=self.ctx.config)
+            self.runtime = RuntimeBundle(state={"graph_mode": "dtdg"})
+            init_flare_training(runtime=self.runtime, session_ctx=self.ctx, partition_data=part, device=device)
+            self.runtime.state.update({"flare_partition_path": str(path),
+                                       "window_state": self.snapshot_core.describe_window_state(),
+                                       "snapshot_state": self.snapshot_core.dump_state(),
+                                       "route_cache": self.snapshot_core.describe_route_cache()})
+        elif mode == "chunk":
+            from starry_unigraph.runtime.chunk import ChunkRuntimeLoader
+
+            validate_artifacts(self.prepared, "chunk", self.ctx.dist.world_size)
+            self.snapshot_core = ChunkRuntimeLoader.from_prepared_artifacts(
+                prepared_dir=self.ctx.artifact_root, device=device, rank=self.ctx.dist.rank,
+                world_size=self.ctx.dist.world_size, config=self.ctx.config)
+            self.runtime = RuntimeBundle(state={"graph_mode": "chunk",
+                                                "chunk_manifest": self.snapshot_core.chunk_manifest})
+        else:
+            raise ValueError(f"Unknown graph_mode: {mode}")
+        return self.runtime
+
+    def build_pipeline_engine(self, model: Any = None):
+        from starry_unigraph.runtime.backend_adapters import (ChunkGraphBackend, CTDGGraphBackend,
+                                                              DummyStateManager, FlareGraphBackend)
+        from starry_unigraph.runtime.engine import PipelineEngine
+
+        if self.prepared is None:
+            self.prepared = load_prepared_from_disk(self.ctx.artifact_root)
+        if self.ctdg_session is None and self.snapshot_core is None:
+            self.build_runtime()
+        mode = self.prepared.provider_meta.get("graph_mode")
+        if mode == "ctdg":
+            backend = CTDGGraphBackend(self.ctdg_session)
+        elif mode == "dtdg":
+            backend = FlareGraphBackend(self.snapshot_core)
+        else:
+            backend = ChunkGraphBackend(self.snapshot_core)
+        self.pipeline_engine = PipelineEngine(backend=backend, state_manager=DummyStateManager(),
+                                              model=model or self.runtime.model or self.model_spec,
+                                              task_adapter=self.task_adapter, device=self._device(),
+                                              optimizer=self.runtime.optimizer)
+        return self.pipeline_engine
+
+    # ------------------------------------------------------------------ epochs
+    def _summarise(self, split: str, outputs: list[dict[str, Any]], losses: list[float], elapsed: float):
+        metric_acc: dict[str, list[float]] = {}
+        for item in outputs:
+            for k, v in item.get("meta", {}).get("metrics", {}).items():
+                metric_acc.setdefault(k, []).append(float(v))
+        loss_sum = float(sum(losses))
+        steps = len(losses) if split != "train" else len(outputs)
+        tot_loss, tot_steps, max_elapsed = self._distributed_epoch_stats(loss_sum, steps, elapsed)
+        return {"split": split, "steps": tot_steps, "local_steps": steps,
+                "loss": tot_loss / tot_steps if tot_steps else 0.0, "local_loss": loss_sum / steps if steps else 0.0,
+                "metrics": {k: float(sum(v) / len(v)) for k, v in metric_acc.items() if v},
+                "elapsed_s": max_elapsed, "local_elapsed_s": elapsed, "outputs": outputs}
+
+    def run_epoch(self, split: str = "train") -> dict[str, Any]:
+        if self.ctdg_session is not None:
+            rt = self.ctdg_session.online_runtime
+            train = split == "train"
+            start = time.perf_counter()
+            if rt.engine is not None:
+                res = rt.run_split_device(split, int(self.ctx.config["train"]["batch_size"]), train)
+                outputs = [{"loss": l, "meta": {"split": split, "batch_size": n,
+                                                "metrics": ({"ap": m[0], "auc": m[1], "mrr": m[2]} if n else {})}}
+                           for l, m, n in zip(res["losses"], res["metrics"], res["sizes"])]
+            else:
+                it = self.ctdg_session.iter_train(self.ctx) if train else self.ctdg_session.iter_eval(self.ctx, split)
+                outputs = [self.ctdg_session.train_step(b) if train else self.ctdg_session.eval_step(b) for b in it]
+            elapsed = time.perf_counter() - start
+            if train:
+                self.global_step += len(outputs)
+                self.current_epoch += 1
+            losses = [float(o["loss"]) for o in outputs if "loss" in o]
+            return self._summarise(split, outputs, losses, elapsed)
+        assert self.snapshot_core is not None, "Call build_runtime() first"
+        if split == "train":
+            iterator = self.snapshot_core.iter_train(split=split)
+        else:
+            self.runtime.state.pop("eval_rnn_state", None)
+            iterator = self.snapshot_core.iter_eval(split=split)
+        start = time.perf_counter()
+        outputs = []
+        for batch in iterator:
+            if split == "train":
+                outputs.append(self.snapshot_core.run_train_step(self.runtime, batch))
+                self.global_step += 1
+            else:
+                outputs.append(self.snapshot_core.run_eval_step(self.runtime, batch))
+        elapsed = time.perf_counter() - start
+        if split == "train":
+            self.current_epoch += 1
+        losses = [float(self.task_adapter.compute_loss(o)) for o in outputs if "loss" in o]
+        return self._summarise(split, outputs, losses, elapsed)
+
+    def run_task(self) -> dict[str, Any]:
+        self.build_runtime()
+        train_summary, eval_summary = [], []
+        t0 = time.perf_counter()
+        for epoch in range(int(self.ctx.config["train"]["epochs"])):
+            train_summary.append(self.run_epoch(split="train"))
+            if (epoch + 1) % int(self.ctx.config["train"]["eval_interval"]) == 0:
+                eval_summary.append(self.run_epoch(split="val"))
+        return {"epochs": self.current_epoch, "train": train_summary, "eval": eval_summary,
+                "train_total_s": sum(x.get("elapsed_s", 0.0) for x in train_summary),
+                "train_total_local_s": sum(x.get("local_elapsed_s", 0.0) for x in train_summary),
+                "run_task_total_s": time.perf_counter() - t0, "warnings": self.ctx.warnings}
+
+    def evaluate(self, split: str = "test") -> dict[str, Any]:
+        return self.run_epoch(split=split)
+
+    def predict(self, split: str = "test") -> PredictionResult:
+        if self.ctdg_session is not None:
+            rt = self.ctdg_session.online_runtime
+            preds: list[float] = []
+            targets: list[int] = []
+            if rt.engine is not None:
+                res = rt.run_split_device(split, int(self.ctx.config["train"]["batch_size"]), train=False,
+                                          collect_predictions=True)
+                for p in res["predictions"]:
+                    preds.extend(p)
+                    targets.extend([1] * len(p))
+            else:
+                for batch in self.ctdg_session.iter_predict(self.ctx, split=split):
+                    out = self.ctdg_session.predict_step(batch)
+                    preds.extend(out.get("predictions", []))
+                    targets.extend(out.get("targets", []) or [])
+            return PredictionResult(predictions=preds, targets=targets or None,
+                                    meta={"split": split, "graph_mode": self.model_spec.graph_mode})
+        assert self.snapshot_core is not None, "Call build_runtime() first"
+        self.runtime.state.pop("eval_rnn_state", None)
+        preds, targets = [], []
+        for batch in self.snapshot_core.iter_predict(split=split):
+            out = self.snapshot_core.run_predict_step(self.runtime, batch)
+            preds.extend(out.get("predictions", []))
+            if out.get("targets") is not None:
+                targets.extend(out["targets"])
+        return PredictionResult(predictions=preds, targets=targets or None,
+                                meta={"split": split, "graph_mode": self.model_spec.graph_mode})
+
+    def _distributed_epoch_stats(self, loss_sum: float, steps: int, elapsed: float) -> tuple[float, int, float]:
+        if not self.ctx.dist.is_distributed or not dist.is_initialized():
+            return loss_sum, steps, elapsed
+        dev = f"cuda:{self.ctx.dist.local_rank}" if dist.get_backend() == "nccl" else "cpu"
+        stats = torch.tensor([loss_sum, float(steps), elapsed], dtype=torch.float64, device=dev)
+        dist.all_reduce(stats[0:2], op=dist.ReduceOp.SUM)
+        dist.all_reduce(stats[2:3], op=dist.ReduceOp.MAX)
+        return float(stats[0]), int(stats[1]), float(stats[2])
+
+    # ------------------------------------------------------------------ checkpoints
+    def save_checkpoint(self, path: str | Path, *, exact_resume: bool = False) -> Path:
+        path = Path(path)
+        if self.ctx.dist.is_distributed and dist.is_initialized() and dist.get_rank() != 0:
+            return path  # one writer (all ranks hold identical parameters)
+        path.parent.mkdir(parents=True, exist_ok=True)
+        if self.ctdg_session is not None:
+            extra = None
+            if exact_resume:
+                mb = self.ctdg_session.online_runtime.memory
+                extra = {"memory_bank": {n: getattr(mb, n).cpu() for n in
+                                         ("memory", "memory_ts", "mailbox", "mailbox_ts", "next_mail_pos")},
+                         "optimizer": self.runtime.optimizer.state_dict(), "epoch": self.current_epoch,
+                         "global_step": self.global_step}
+            self.ctdg_session.save_checkpoint(path, extra)
+            return path
+        model = self.runtime.model.module if hasattr(self.runtime.model, "module") else self.runtime.model
+        opt = self.runtime.optimizer
+        payload = {"model_state": {k: v.detach().cpu() for k, v in model.state_dict().items()},
+                   "optimizer_state": opt.state_dict() if opt is not None else None,
+                   "scheduler_state": self.runtime.scheduler, "config": self.ctx.config,
+                   "epoch": self.current_epoch, "global_step": self.global_step}
+        return save_checkpoint(path, payload)
+
+    def load_checkpoint(self, path: str | Path) -> dict[str, Any]:
+        if self.ctdg_session is None and self.snapshot_core is None:
+            self.build_runtime()
+        if self.ctdg_session is not None:
+            ckpt = self.ctdg_session.load_checkpoint(path)
+            self.current_epoch = int(ckpt.get("epoch", self.current_epoch))
+            self.global_step = int(ckpt.get("global_step", self.global_step))
+            return ckpt
+        payload = load_checkpoint(path)
+        state = payload.get("model_state")
+        model = self.runtime.model.module if hasattr(self.runtime.model, "module") else self.runtime.model
+        if isinstance(state, torch.nn.Module):  # reference payloads pickle the live module
+            inner = state.module if hasattr(state, "module") else state
+            state = inner.state_dict()
+        if state is not None:
+            with torch.no_grad():
+                for k, v in model.state_dict().items():
+                    v.copy_(state[k])
+        opt_state = payload.get("optimizer_state")
+        if opt_state is not None and self.runtime.optimizer is not None and isinstance(opt_state, dict):
+            try:
+                self.runtime.optimizer.load_state_dict(opt_state)
+            except Exception:
+                pass
+        self.runtime.scheduler = payload.get("scheduler_state")
+        self.current_epoch = int(payload.get("epoch", 0))
+        self.global_step = int(payload.get("global_step", 0))
+        return payload

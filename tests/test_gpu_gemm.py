@@ -1,0 +1,85 @@
+"""tcgen05 GEMM numerics against a plain fp32 PyTorch reference (bf16 operands,
+fp32 accumulate: relative tolerance ~1e-2)."""
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+
+def _C():
+    from starry_unigraph.ops import cuda_ext
+
+    return cuda_ext()
+
+
+def _rel(a, b):
+    return float((a - b).norm() / (b.norm() + 1e-12))
+
+
+@pytest.mark.parametrize("M,K,N", [(1, 8, 16), (128, 64, 128), (300, 100, 100), (1000, 216, 200), (257, 33, 300),
+                                   (4096, 128, 512), (130, 256, 600)])
+def test_linear_fwd(M, K, N):
+    C = _C()
+    torch.manual_seed(0)
+    x = torch.randn(M, K, device="cuda")
+    w = torch.randn(N, K, device="cuda") / K ** 0.5
+    b = torch.randn(N, device="cuda")
+    y = C.linear_fwd(x, w, b, 0)
+    ref = x @ w.t() + b
+    torch.cuda.synchronize()
+    assert C.status_read(True) == 0
+    assert _rel(y, ref) < 1.5e-2, _rel(y, ref)
+
+
+@pytest.mark.parametrize("act", [1, 2, 3])
+def test_linear_act(act):
+    C = _C()
+    x = torch.randn(200, 64, device="cuda")
+    w = torch.randn(96, 64, device="cuda") / 8
+    y = C.linear_fwd(x, w, None, act)
+    z = x @ w.t()
+    ref = {1: torch.relu, 2: torch.sigmoid, 3: torch.tanh}[act](z)
+    assert _rel(y, ref) < 1.5e-2
+
+
+@pytest.mark.parametrize("M,K,N", [(64, 16, 32), (1000, 100, 200), (3000, 216, 100)])
+def test_linear_dgrad(M, K, N):
+    C = _C()
+    dy = torch.randn(M, N, device="cuda")
+    w = torch.randn(N, K, device="cuda") / N ** 0.5
+    dx = C.linear_dgrad(dy, w)
+    assert _rel(dx, dy @ w) < 1.5e-2
+
+
+@pytest.mark.parametrize("M,K,N", [(64, 16, 32), (1000, 100, 200), (12000, 216, 100)])
+def test_linear_wgrad(M, K, N):
+    C = _C()
+    dy = torch.randn(M, N, device="cuda")
+    x = torch.randn(M, K, device="cuda")
+    dw = torch.zeros(N, K, device="cuda")
+    db = torch.zeros(N, device="cuda")
+    C.linear_wgrad(dy, x, dw, db)
+    assert _rel(dw, dy.t() @ x) < 1.5e-2
+    assert _rel(db, dy.sum(0)) < 1.5e-2
+
+
+def test_adam_matches_torch():
+    from starry_unigraph.ops.flat import FlatParams, FusedAdam
+
+    torch.manual_seed(0)
+    m1 = torch.nn.Linear(37, 11).cuda()
+    m2 = torch.nn.Linear(37, 11).cuda()
+    m2.load_state_dict(m1.state_dict())
+    flat = FlatParams([m1], torch.device("cuda"))
+    opt = FusedAdam(flat, lr=1e-2, weight_decay=0.01)
+    ref = torch.optim.Adam(m2.parameters(), lr=1e-2, weight_decay=0.01)
+    for _ in range(5):
+        x = torch.randn(8, 37, device="cuda")
+        flat.zero_grad()
+        m1(x).pow(2).sum().backward()
+        opt.step()
+        ref.zero_grad()
+        m2(x).pow(2).sum().backward()
+        ref.step()
+    for a, b in zip(m1.parameters(), m2.parameters()):
+        assert torch.allclose(a, b, atol=1e-5, rtol=1e-4)

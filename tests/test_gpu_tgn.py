@@ -1,0 +1,99 @@
+"""Fused sm_100a TGN step against the PyTorch CPU path of the same runtime
+(reference semantics), with dropout disabled so both are deterministic."""
+import copy
+
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+
+def _cfg(device, **over):
+    cfg = {"model": {"name": "tgn", "family": "tgn", "task": "temporal_link_prediction", "hidden_dim": 32},
+           "data": {"root": "./data", "name": "gputest", "format": "synthetic",
+                    "synthetic": {"preset": "tgn_cpu", "num_events": 4000, "edge_dim": 8, "num_src": 300,
+                                  "num_dst": 100}},
+           "train": {"epochs": 1, "batch_size": 100, "lr": 1e-3},
+           "runtime": {"device": device, "cuda_graphs": False},
+           "ctdg": {"mailbox_slots": 1, "dim_time": 16, "num_head": 2, "dropout": 0.0, "att_dropout": 0.0},
+           "sampling": {"neighbor_limit": [5], "strategy": "recent", "history": 1}}
+    for k, v in over.items():
+        cfg[k].update(v)
+    return cfg
+
+
+def _session(device, tmp_path, **over):
+    from starry_unigraph import SchedulerSession
+
+    s = SchedulerSession.from_config(_cfg(device, **over))
+    s.ctx.artifact_root = tmp_path / device.replace(":", "_")
+    s.prepare_data()
+    s.build_runtime()
+    return s
+
+
+def test_sampler_kernel_matches_torch(tmp_path):
+    from starry_unigraph.ops import cuda_ext
+
+    C = cuda_ext()
+    s = _session("cuda", tmp_path)
+    rt = s.ctdg_session.online_runtime
+    csr = rt.sampler.csr("train")
+    R = 64
+    roots = torch.randperm(rt.dataset.num_nodes, device="cuda")[:R]
+    rts = torch.tensor([int(rt.dataset.ts[1500])], device="cuda", dtype=torch.int64)
+    ref = csr.sample_torch(roots, rts.expand(R), 5, "recent")
+    k = 5
+    out_nbr = torch.zeros(R * k, dtype=torch.int64, device="cuda")
+    out_eid = torch.zeros_like(out_nbr)
+    out_dt = torch.zeros(R * k, device="cuda")
+    out_cnt = torch.zeros(R, dtype=torch.int32, device="cuda")
+    tot = torch.zeros(1, dtype=torch.int32, device="cuda")
+    n_roots = torch.tensor([R], dtype=torch.int32, device="cuda")
+    step = torch.zeros(1, dtype=torch.int64, device="cuda")
+    C.tgn_sample(roots, n_roots, rts, csr.rowptr, csr.nbr, csr.eid, csr.ts, k, 0, 0, step, out_nbr, out_eid, out_dt,
+                 out_cnt, tot)
+    torch.cuda.synchronize()
+    assert torch.equal(out_cnt.long().cpu(), ref.count.long().cpu())
+    assert torch.equal(out_nbr.view(R, k).cpu(), ref.nbr.cpu())
+    assert torch.equal(out_eid.view(R, k).cpu(), ref.eid.cpu())
+    assert torch.allclose(out_dt.view(R, k).cpu(), ref.dt.cpu())
+    assert int(tot) == int(ref.count.sum())
+
+
+@pytest.mark.parametrize("slots", [1, 2])
+def test_fused_step_matches_cpu_oracle(tmp_path, slots):
+    g = _session("cuda", tmp_path, ctdg={"mailbox_slots": slots})
+    c = _session("cpu", tmp_path, ctdg={"mailbox_slots": slots})
+    rg, rc = g.ctdg_session.online_runtime, c.ctdg_session.online_runtime
+    for a, b in zip(rg.model.state_dict().values(), rc.model.state_dict().values()):
+        assert torch.allclose(a.cpu(), b)
+    eng = rg.engine
+    batches = list(rc.iter_batches("train", 100))[:6]
+    for i, batch in enumerate(batches):
+        res_g = rg.train_step(batch)
+        neg = eng.neg[: batch.size].cpu()
+        rc._negative_sample = lambda b, neg=neg: neg
+        res_c = rc.train_step(batch)
+        lg, lc = res_g["loss"], res_c["loss"]
+        assert abs(lg - lc) <= 2e-2 * max(1.0, abs(lc)), (i, lg, lc)
+    from starry_unigraph.ops import check_status
+
+    check_status()
+    mg, mc = rg.memory, rc.memory
+    assert torch.allclose(mg.memory.cpu(), mc.memory, atol=3e-2, rtol=3e-2)
+    assert torch.allclose(mg.mailbox.cpu(), mc.mailbox, atol=3e-2, rtol=3e-2)
+    assert torch.equal(mg.next_mail_pos.cpu(), mc.next_mail_pos)
+    for (n, a), b in zip(rg.model.state_dict().items(), rc.model.state_dict().values()):
+        err = float((a.cpu() - b).abs().max())
+        assert err < 5e-3, (n, err)
+
+
+def test_eval_and_predict_run(tmp_path):
+    s = _session("cuda", tmp_path, runtime={"cuda_graphs": True})
+    r = s.run_epoch("train")
+    assert r["steps"] > 0 and r["loss"] > 0
+    v = s.run_epoch("val")
+    assert 0.0 <= v["metrics"]["ap"] <= 1.0
+    p = s.predict("test")
+    assert len(p.predictions) > 0
