@@ -62,31 +62,47 @@ def test_sampler_kernel_matches_torch(tmp_path):
 
 
 @pytest.mark.parametrize("slots", [1, 2])
-def test_fused_step_matches_cpu_oracle(tmp_path, slots):
-    g = _session("cuda", tmp_path, ctdg={"mailbox_slots": slots})
-    c = _session("cpu", tmp_path, ctdg={"mailbox_slots": slots})
+def test_fused_forward_and_memory_match_cpu_oracle(tmp_path, slots):
+    """lr = 0: parameters stay fixed, so per-step losses, the memory table and the
+    mailbox isolate the forward pass and the memory/mailbox semantics."""
+    g = _session("cuda", tmp_path, ctdg={"mailbox_slots": slots}, train={"lr": 0.0})
+    c = _session("cpu", tmp_path, ctdg={"mailbox_slots": slots}, train={"lr": 0.0})
     rg, rc = g.ctdg_session.online_runtime, c.ctdg_session.online_runtime
     for a, b in zip(rg.model.state_dict().values(), rc.model.state_dict().values()):
         assert torch.allclose(a.cpu(), b)
     eng = rg.engine
-    batches = list(rc.iter_batches("train", 100))[:6]
-    for i, batch in enumerate(batches):
+    for i, batch in enumerate(list(rc.iter_batches("train", 100))[:8]):
         res_g = rg.train_step(batch)
         neg = eng.neg[: batch.size].cpu()
         rc._negative_sample = lambda b, neg=neg: neg
         res_c = rc.train_step(batch)
         lg, lc = res_g["loss"], res_c["loss"]
-        assert abs(lg - lc) <= 2e-2 * max(1.0, abs(lc)), (i, lg, lc)
+        assert abs(lg - lc) <= 1e-2 * max(1.0, abs(lc)), (i, lg, lc)
     from starry_unigraph.ops import check_status
 
     check_status()
     mg, mc = rg.memory, rc.memory
-    assert torch.allclose(mg.memory.cpu(), mc.memory, atol=3e-2, rtol=3e-2)
-    assert torch.allclose(mg.mailbox.cpu(), mc.mailbox, atol=3e-2, rtol=3e-2)
+    assert torch.allclose(mg.memory.cpu(), mc.memory, atol=2e-2, rtol=2e-2)
+    assert torch.allclose(mg.mailbox.cpu(), mc.mailbox, atol=2e-2, rtol=2e-2)
     assert torch.equal(mg.next_mail_pos.cpu(), mc.next_mail_pos)
-    for (n, a), b in zip(rg.model.state_dict().items(), rc.model.state_dict().values()):
-        err = float((a.cpu() - b).abs().max())
-        assert err < 5e-3, (n, err)
+
+
+def test_fused_gradients_match_autograd(tmp_path):
+    """Gradients of every trainable parameter after the same steps (lr = 0 keeps
+    both models identical; gradients of the last step are compared)."""
+    g = _session("cuda", tmp_path, train={"lr": 0.0})
+    c = _session("cpu", tmp_path, train={"lr": 0.0})
+    rg, rc = g.ctdg_session.online_runtime, c.ctdg_session.online_runtime
+    eng = rg.engine
+    for batch in list(rc.iter_batches("train", 100))[:5]:
+        rg.train_step(batch)
+        neg = eng.neg[: batch.size].cpu()
+        rc._negative_sample = lambda b, neg=neg: neg
+        rc.train_step(batch)
+    for (n, pg), pc in zip(rg.model.named_parameters(), rc.model.parameters()):
+        a, b = pg.grad.detach().cpu(), pc.grad.detach()
+        rel = float((a - b).norm() / (b.norm() + 1e-8))
+        assert rel < 5e-2, (n, rel)
 
 
 def test_eval_and_predict_run(tmp_path):
