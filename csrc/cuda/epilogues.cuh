@@ -168,3 +168,56 @@ struct EpiTimeGrad {
 
 
 }  // namespace su
+
+namespace su {
+
+// LSTM cell epilogue (reference runtime/modules/rnn_cells.py:92-116): the accumulator
+// holds four blocks of DP columns [x W_i^T + h ... | f | g | o] (one nn.Linear per gate
+// over [x || h]). i, f, o = sigmoid, g = tanh, c' = f c + i g, h' = o tanh(c').
+// Saves the post-activation gates for the backward pass.
+struct EpiLSTM {
+  int H = 0, DP = 0;
+  const float* b_i = nullptr;
+  const float* b_f = nullptr;
+  const float* b_g = nullptr;
+  const float* b_o = nullptr;
+  const float* c_prev = nullptr;  // [rows, H] (nullptr -> zeros)
+  float* h_out = nullptr;         // [rows, H]
+  float* c_out = nullptr;         // [rows, H]
+  float* gates = nullptr;         // [rows, 4H] (i, f, g, o) post-activation, optional
+
+#ifdef __CUDACC__
+  __device__ __forceinline__ void operator()(int row, bool valid, int /*n0*/, uint32_t taddr, int /*tc*/) const {
+    for (int c0 = 0; c0 < DP; c0 += 16) {
+      float gi[16], gf[16], gg[16], go[16];
+      tmem_ld16(taddr + c0, gi);
+      tmem_ld16(taddr + DP + c0, gf);
+      tmem_ld16(taddr + 2 * DP + c0, gg);
+      tmem_ld16(taddr + 3 * DP + c0, go);
+      if (!valid) continue;
+#pragma unroll
+      for (int j = 0; j < 16; ++j) {
+        const int c = c0 + j;
+        if (c >= H) break;
+        const float i = sigmoidf_(gi[j] + b_i[c]);
+        const float f = sigmoidf_(gf[j] + b_f[c]);
+        const float g = tanhf(gg[j] + b_g[c]);
+        const float o = sigmoidf_(go[j] + b_o[c]);
+        const float cp = c_prev ? c_prev[(int64_t)row * H + c] : 0.f;
+        const float cn = f * cp + i * g;
+        c_out[(int64_t)row * H + c] = cn;
+        h_out[(int64_t)row * H + c] = o * tanhf(cn);
+        if (gates) {
+          float* gr = gates + (int64_t)row * 4 * H;
+          gr[c] = i;
+          gr[H + c] = f;
+          gr[2 * H + c] = g;
+          gr[3 * H + c] = o;
+        }
+      }
+    }
+  }
+#endif
+};
+
+}  // namespace su

@@ -84,4 +84,9 @@ void gemm(const SegSource& a, const WeightTSource& b, const EpiTimeGrad& e, cons
   else launch_cfg<256, 1>(a, b, e, sh, st);
 }
 
+void gemm(const SegSource& a, const WeightSource& b, const EpiLSTM& e, const GemmShape& sh, cudaStream_t st) {
+  if (sh.N <= 256) launch_cfg<256, 1>(a, b, e, sh, st);
+  else launch_cfg<256, 2>(a, b, e, sh, st);
+}
+
 }  // namespace su

@@ -91,6 +91,13 @@ void launch_tgn_metrics(dim3 grid, dim3 block, cudaStream_t st, const float* __r
                                                            const int* __restrict__ n_ev, int bmax,
                                                            float* __restrict__ out);
 
+// ---- DTDG ---------------------------------------------------------------------
+void gemm(const SegSource& a, const WeightSource& b, const EpiLSTM& e, const GemmShape& sh, cudaStream_t st);
+void launch_spmm_csr(cudaStream_t st, const int64_t* rowptr, const int* col, const float* val, const float* x,
+                     int64_t n_rows, int F, float* out, int accumulate);
+void launch_lstm_bwd(cudaStream_t st, const float* gates, const float* c_prev, const float* c_new, const float* dh,
+                     const float* dc, int64_t rows, int H, float* dpre, float* dc_prev);
+
 // ---- optimiser ---------------------------------------------------------------
 void launch_adam_flat(cudaStream_t st, int blocks, float* p, const float* g, float* m, float* v, int64_t n,
                       int64_t* step, unsigned int* done, float lr, float b1, float b2, float eps, float wd,

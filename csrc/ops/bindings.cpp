@@ -67,6 +67,20 @@ void tgn_link_proj_bwd(const at::Tensor& dP, const at::Tensor& out, const at::Te
 void adam_flat(at::Tensor& p, const at::Tensor& g, at::Tensor& m, at::Tensor& v, at::Tensor& step, at::Tensor& done,
                double lr, double b1, double b2, double eps, double wd, double grad_scale);
 
+at::Tensor spmm_csr(const at::Tensor& rowptr, const at::Tensor& col, const at::Tensor& val, const at::Tensor& x,
+                    int64_t n_rows, const c10::optional<at::Tensor>& out_opt, bool accumulate);
+std::vector<at::Tensor> lstm_fwd(const at::Tensor& x, const c10::optional<at::Tensor>& h,
+                                 const c10::optional<at::Tensor>& c, const at::Tensor& wi, const at::Tensor& bi,
+                                 const at::Tensor& wf, const at::Tensor& bf, const at::Tensor& wg,
+                                 const at::Tensor& bg, const at::Tensor& wo, const at::Tensor& bo, bool save_gates);
+std::vector<at::Tensor> lstm_bwd(const at::Tensor& x, const c10::optional<at::Tensor>& h,
+                                 const c10::optional<at::Tensor>& c, const at::Tensor& c_new, const at::Tensor& gates,
+                                 const c10::optional<at::Tensor>& dh_opt, const c10::optional<at::Tensor>& dc_opt,
+                                 const at::Tensor& wi, const at::Tensor& wf, const at::Tensor& wg,
+                                 const at::Tensor& wo, at::Tensor& gwi, at::Tensor& gbi, at::Tensor& gwf,
+                                 at::Tensor& gbf, at::Tensor& gwg, at::Tensor& gbg, at::Tensor& gwo,
+                                 at::Tensor& gbo);
+
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "starry_unigraph sm_100a kernels (tcgen05 GEMMs, TGN step, DTDG ops, collectives)";
   m.def("status_read", &status_read, "read (and clear) the device status word", py::arg("clear") = true);
@@ -89,4 +103,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("tgn_metrics", &tgn_metrics);
   m.def("tgn_link_proj_bwd", &tgn_link_proj_bwd);
   m.def("adam_flat", &adam_flat);
+  m.def("spmm_csr", &spmm_csr);
+  m.def("lstm_fwd", &lstm_fwd);
+  m.def("lstm_bwd", &lstm_bwd);
 }

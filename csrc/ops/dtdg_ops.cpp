@@ -1,0 +1,182 @@
+// Torch-side wrappers of the DTDG kernels: CSR SpMM, fused LSTM cell (tcgen05
+// GEMM with a gate epilogue) and its backward (elementwise gate gradients, then
+// input and weight gradients on the tcgen05 GEMM).
+#include "host_common.h"
+
+using namespace su;
+
+at::Tensor spmm_csr(const at::Tensor& rowptr, const at::Tensor& col, const at::Tensor& val, const at::Tensor& x,
+                    int64_t n_rows, const c10::optional<at::Tensor>& out_opt, bool accumulate) {
+  SU_CHECK_I64(rowptr); SU_CHECK_I32(col); SU_CHECK_F32(val); SU_CHECK_F32(x); SU_CHECK_CONTIG(x);
+  const int F = static_cast<int>(x.size(1));
+  at::Tensor out = (out_opt.has_value() && out_opt->defined()) ? *out_opt : at::empty({n_rows, F}, x.options());
+  TORCH_CHECK(out.is_contiguous() && out.size(1) == F, "bad output buffer");
+  if (accumulate == false && n_rows > 0 && rowptr.numel() == n_rows + 1) {
+    // every row is written by the kernel
+  }
+  launch_spmm_csr(cur_stream(), rowptr.data_ptr<int64_t>(), col.data_ptr<int>(), val.data_ptr<float>(),
+                  x.data_ptr<float>(), n_rows, F, out.data_ptr<float>(), accumulate ? 1 : 0);
+  SU_LAUNCH_CHECK();
+  return out;
+}
+
+static WeightLayout lstm_layout(const std::vector<at::Tensor>& ws, int in_dim, int H, int DP) {
+  WeightLayout L;
+  L.nblk = 4;
+  L.nseg = 2;
+  L.seg_kpad[0] = pad8(in_dim);
+  L.seg_kpad[1] = pad8(H);
+  for (int i = 0; i < 4; ++i) {
+    L.blk_rows[i] = H;
+    L.blk_pad[i] = DP;
+    L.cell[i][0] = wcell(ws[i], 0, 0, in_dim);
+    L.cell[i][1] = wcell(ws[i], 0, in_dim, H);
+  }
+  return L;
+}
+
+// (h', c', gates) = LSTMCell(x, (h, c)); gates [rows, 4H] post-activation (i, f, g, o)
+std::vector<at::Tensor> lstm_fwd(const at::Tensor& x, const c10::optional<at::Tensor>& h,
+                                 const c10::optional<at::Tensor>& c, const at::Tensor& wi, const at::Tensor& bi,
+                                 const at::Tensor& wf, const at::Tensor& bf, const at::Tensor& wg,
+                                 const at::Tensor& bg, const at::Tensor& wo, const at::Tensor& bo, bool save_gates) {
+  SU_CHECK_F32(x); SU_CHECK_CONTIG(x);
+  const int rows = static_cast<int>(x.size(0));
+  const int in_dim = static_cast<int>(x.size(1));
+  const int H = static_cast<int>(wi.size(0));
+  const int DP = (H + 15) / 16 * 16;
+  TORCH_CHECK(4 * DP <= 512, "fused LSTM supports hidden size <= 128");
+  auto h_out = at::empty({rows, H}, x.options());
+  auto c_out = at::empty({rows, H}, x.options());
+  at::Tensor gates = save_gates ? at::empty({rows, 4 * H}, x.options()) : at::Tensor();
+  if (rows == 0) return {h_out, c_out, gates};
+  const bool has_h = h.has_value() && h->defined();
+  SegSource a;
+  a.nseg = 2;
+  a.seg[0] = seg_f32(x, in_dim, pad8(in_dim));
+  if (has_h) {
+    a.seg[1] = seg_f32(*h, H, pad8(H));
+  } else {
+    a.seg[1].kind = kSegZero;
+    a.seg[1].kpad = pad8(H);
+  }
+  WeightSource b;
+  b.L = lstm_layout({wi, wf, wg, wo}, in_dim, H, DP);
+  EpiLSTM e;
+  e.H = H;
+  e.DP = DP;
+  e.b_i = bi.data_ptr<float>();
+  e.b_f = bf.data_ptr<float>();
+  e.b_g = bg.data_ptr<float>();
+  e.b_o = bo.data_ptr<float>();
+  e.c_prev = (c.has_value() && c->defined()) ? c->data_ptr<float>() : nullptr;
+  e.h_out = h_out.data_ptr<float>();
+  e.c_out = c_out.data_ptr<float>();
+  e.gates = save_gates ? gates.data_ptr<float>() : nullptr;
+  GemmShape sh;
+  sh.M = rows;
+  sh.N = 4 * DP;
+  sh.K = pad8(in_dim) + pad8(H);
+  gemm(a, b, e, sh, cur_stream());
+  SU_LAUNCH_CHECK();
+  return {h_out, c_out, gates};
+}
+
+// Backward of lstm_fwd. Returns (dx, dh_prev, dc_prev) and accumulates weight/bias grads.
+std::vector<at::Tensor> lstm_bwd(const at::Tensor& x, const c10::optional<at::Tensor>& h,
+                                 const c10::optional<at::Tensor>& c, const at::Tensor& c_new, const at::Tensor& gates,
+                                 const c10::optional<at::Tensor>& dh_opt, const c10::optional<at::Tensor>& dc_opt,
+                                 const at::Tensor& wi, const at::Tensor& wf, const at::Tensor& wg,
+                                 const at::Tensor& wo, at::Tensor& gwi, at::Tensor& gbi, at::Tensor& gwf,
+                                 at::Tensor& gbf, at::Tensor& gwg, at::Tensor& gbg, at::Tensor& gwo,
+                                 at::Tensor& gbo) {
+  const int rows = static_cast<int>(x.size(0));
+  const int in_dim = static_cast<int>(x.size(1));
+  const int H = static_cast<int>(wi.size(0));
+  const bool has_h = h.has_value() && h->defined();
+  const bool has_c = c.has_value() && c->defined();
+  auto dpre = at::empty({rows, 4 * H}, x.options());
+  auto dc_prev = at::empty({rows, H}, x.options());
+  auto dxh = at::empty({rows, in_dim + H}, x.options());
+  if (rows == 0) return {dxh.narrow(1, 0, in_dim), dxh.narrow(1, in_dim, H), dc_prev};
+  const float* dh = (dh_opt.has_value() && dh_opt->defined()) ? dh_opt->contiguous().data_ptr<float>() : nullptr;
+  at::Tensor dh_c, dc_c;
+  if (dh_opt.has_value() && dh_opt->defined()) dh_c = dh_opt->contiguous();
+  if (dc_opt.has_value() && dc_opt->defined()) dc_c = dc_opt->contiguous();
+  launch_lstm_bwd(cur_stream(), gates.data_ptr<float>(), has_c ? c->data_ptr<float>() : nullptr,
+                  c_new.data_ptr<float>(), dh_c.defined() ? dh_c.data_ptr<float>() : nullptr,
+                  dc_c.defined() ? dc_c.data_ptr<float>() : nullptr, rows, H, dpre.data_ptr<float>(),
+                  dc_prev.data_ptr<float>());
+  (void)dh;
+  const int DP4 = 4 * H;
+  // d[x || h] = dpre [W_i; W_f; W_g; W_o]
+  {
+    SegSource a;
+    a.nseg = 1;
+    a.seg[0] = seg_f32(dpre, DP4, pad8(DP4));
+    WeightTSource b;
+    b.L = lstm_layout({wi, wf, wg, wo}, in_dim, H, H);
+    b.L.blk_pad[3] = pad8(DP4) - 3 * H;
+    EpiLinear e;
+    e.out = dxh.data_ptr<float>();
+    e.ldo = in_dim + H;
+    e.ncols = in_dim + H;
+    // B rows follow the padded K space of the forward (x then h segments)
+    GemmShape sh;
+    sh.M = rows;
+    sh.N = pad8(in_dim) + pad8(H);
+    sh.K = pad8(DP4);
+    // write into a padded buffer then compact (segment padding shifts the h columns)
+    if (pad8(in_dim) != in_dim) {
+      auto tmp = at::empty({rows, pad8(in_dim) + pad8(H)}, x.options());
+      e.out = tmp.data_ptr<float>();
+      e.ldo = pad8(in_dim) + pad8(H);
+      e.ncols = pad8(in_dim) + pad8(H);
+      gemm(a, b, e, sh, cur_stream());
+      dxh.narrow(1, 0, in_dim).copy_(tmp.narrow(1, 0, in_dim));
+      dxh.narrow(1, in_dim, H).copy_(tmp.narrow(1, pad8(in_dim), H));
+    } else {
+      gemm(a, b, e, sh, cur_stream());
+    }
+  }
+  // weight / bias gradients: dW_gate += dpre_gate^T [x || h]
+  {
+    SegSource dy;
+    dy.nseg = 1;
+    dy.seg[0] = seg_f32(dpre, DP4, pad8(DP4));
+    SegSource xs;
+    xs.nseg = 3;
+    xs.seg[0] = seg_f32(x, in_dim, pad8(in_dim));
+    if (has_h) xs.seg[1] = seg_f32(*h, H, pad8(H));
+    else {
+      xs.seg[1].kind = kSegZero;
+      xs.seg[1].kpad = pad8(H);
+    }
+    xs.seg[2] = seg_ones();
+    TransposedSource ta;
+    ta.inner = dy;
+    ta.inner_rows = rows;
+    TransposedSource tb;
+    tb.inner = xs;
+    tb.inner_rows = rows;
+    EpiWeightGrad e;
+    e.L = lstm_layout({gwi, gwf, gwg, gwo}, in_dim, H, H);
+    e.L.nseg = 3;
+    e.L.seg_kpad[2] = 8;
+    float* bgs[4] = {gbi.data_ptr<float>(), gbf.data_ptr<float>(), gbg.data_ptr<float>(), gbo.data_ptr<float>()};
+    for (int i = 0; i < 4; ++i) e.bias_grad[i] = bgs[i];
+    e.bias_seg = 2;
+    e.ncols = pad8(in_dim) + pad8(H) + 8;
+    GemmShape sh;
+    sh.M = DP4;
+    sh.N = e.ncols;
+    sh.K = rows;
+    const int nchunks = (rows + kBK - 1) / kBK;
+    const int tiles = ((DP4 + kBM - 1) / kBM) * ((sh.N + 255) / 256);
+    const int want = std::max(1, (2 * num_sms(at::cuda::current_device())) / std::max(1, tiles));
+    sh.ksplit = std::max(1, std::min(nchunks, want));
+    gemm(ta, tb, e, sh, cur_stream());
+  }
+  SU_LAUNCH_CHECK();
+  return {dxh.narrow(1, 0, in_dim), dxh.narrow(1, in_dim, H), dc_prev};
+}

@@ -53,6 +53,16 @@ if not SKIP_CUDA:
         )
     )
 
+def _omp_flags():
+    """Link libgomp explicitly: the active gcc prefix may ship omp.h without libgomp."""
+    for d in sorted(glob.glob("/usr/lib/gcc/x86_64-linux-gnu/*"), reverse=True):
+        if os.path.exists(os.path.join(d, "libgomp.so")):
+            return [], ["-L" + d, "-lgomp", "-Wl,-rpath,/usr/lib/x86_64-linux-gnu"]
+    return [], ["-fopenmp"]
+
+
+OMP_INC, OMP_LINK = _omp_flags()
+
 host_sources = sorted(glob.glob(os.path.join("csrc", "host", "*.cpp")))
 if host_sources:
     ext_modules.append(
@@ -60,8 +70,8 @@ if host_sources:
             name="starry_unigraph._native",
             sources=host_sources,
             include_dirs=[os.path.join(ROOT, "csrc", "host")],
-            extra_compile_args=CXX_FLAGS + ["-fopenmp"],
-            extra_link_args=["-fopenmp"],
+            extra_compile_args=CXX_FLAGS + ["-fopenmp"] + OMP_INC,
+            extra_link_args=OMP_LINK,
         )
     )
 

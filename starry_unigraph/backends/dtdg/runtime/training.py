@@ -1,0 +1,216 @@
+"""Flare DTDG training / eval / predict steps (reference backends/dtdg/runtime/training.py:31-295).
+
+Data parallelism: parameters live in one flat buffer; after backward the flat
+gradient is averaged across ranks in one collective (the peer-memory all-reduce
+kernel on CUDA with ``comm.path: p2p``, NCCL otherwise) and one fused Adam
+kernel updates everything. The loss is scaled by local/total nodes
+(``part_loss_scale``). Regression tasks use MSE (reference); classification
+tasks (``node_classification``) use BCE on one logit / CE on several.
+"""
+from __future__ import annotations
+
+from typing import Any
+
+import torch
+import torch.distributed as dist
+import torch.nn.functional as F
+
+from starry_unigraph.types import RuntimeBundle, SessionContext
+
+from .models import build_flare_model
+from .session_loader import DTDGBatch
+from .state import RNNStateManager, STGraphBlob
+
+
+def _infer_dims(partition_data: Any) -> tuple[int, int]:
+    input_size = int(partition_data.node_data["x"].data.size(-1))
+    labels = partition_data.node_data.get("y")
+    if labels is None:
+        return input_size, 1
+    y = labels.data
+    if y.dtype == torch.long:
+        return input_size, int(y.max().item() + 1 if y.dim() == 1 else y.size(-1))
+    return input_size, int(1 if y.dim() == 1 else y.size(-1))
+
+
+def _compute_part_loss_scale(local_nodes: int, device: str) -> float:
+    if not dist.is_available() or not dist.is_initialized():
+        return 1.0
+    dev = device if dist.get_backend() == "nccl" else "cpu"
+    t = torch.tensor([float(local_nodes)], device=dev)
+    dist.all_reduce(t)
+    total = float(t.item())
+    return local_nodes / total if total > 0 else 1.0
+
+
+class FlareOptimizer:
+    """Flat-buffer Adam with one gradient all-reduce per step."""
+
+    def __init__(self, model: torch.nn.Module, lr: float, device: torch.device, comm_path: str = "nccl"):
+        self.model = model
+        self.world = dist.get_world_size() if dist.is_available() and dist.is_initialized() else 1
+        self.cuda = device.type == "cuda"
+        self.comm_path = comm_path
+        self._allreduce = None
+        if self.cuda:
+            from starry_unigraph.ops.flat import FlatParams, FusedAdam
+
+            self.flat = FlatParams([model], device)
+            self.opt = FusedAdam(self.flat, lr=lr)
+            if self.world > 1 and comm_path == "p2p":
+                try:
+                    from starry_unigraph.parallel.allreduce import PeerAllReduce
+
+                    self._allreduce = PeerAllReduce(self.flat.grad.numel(), device)
+                except Exception as exc:  # symmetric memory unavailable -> NCCL baseline
+                    print(f"[starry_unigraph] peer all-reduce unavailable ({exc}); using NCCL")
+        else:
+            self.opt = torch.optim.Adam(model.parameters(), lr=lr)
+        self.param_groups = self.opt.param_groups
+
+    def zero_grad(self, set_to_none: bool = False) -> None:
+        if self.cuda:
+            self.flat.zero_grad()
+        else:
+            self.opt.zero_grad(set_to_none=set_to_none)
+
+    def step(self) -> None:
+        if self.cuda:
+            scale = 1.0
+            if self.world > 1:
+                if self._allreduce is not None:
+                    self._allreduce(self.flat.grad)
+                else:
+                    dist.all_reduce(self.flat.grad)
+                scale = 1.0 / self.world
+            self.opt.step(grad_scale=scale)
+        else:
+            if self.world > 1:
+                for p in self.model.parameters():
+                    if p.grad is None:
+                        p.grad = torch.zeros_like(p)
+                    dist.all_reduce(p.grad)
+                    p.grad /= self.world
+            self.opt.step()
+
+    def state_dict(self) -> dict:
+        return self.opt.state_dict()
+
+    def load_state_dict(self, state: dict) -> None:
+        self.opt.load_state_dict(state)
+
+
+def init_flare_training(runtime: RuntimeBundle, session_ctx: SessionContext, partition_data: Any,
+                        device: str | None = None) -> None:
+    input_size, output_size = _infer_dims(partition_data)
+    cfg = session_ctx.config
+    device = device or cfg["runtime"]["device"]
+    torch.manual_seed(int(cfg.get("train", {}).get("seed", 0)))
+    model = build_flare_model(cfg["model"]["name"], input_size, int(cfg["model"]["hidden_dim"]), output_size)
+    model = model.to(device)
+    opt = FlareOptimizer(model, float(cfg.get("train", {}).get("lr", 1e-3)), torch.device(device),
+                         str(cfg.get("comm", {}).get("path", "nccl")))
+    if dist.is_available() and dist.is_initialized():
+        for p in model.parameters():  # identical initial weights on every rank
+            dist.broadcast(p.data, src=0)
+    scale = _compute_part_loss_scale(int(partition_data.num_dst_nodes), device)
+    task = str(cfg["model"]["task"])
+    runtime.model = model
+    runtime.optimizer = opt
+    runtime.state["flare_model"] = {"name": cfg["model"]["name"], "input_size": input_size,
+                                    "hidden_size": int(cfg["model"]["hidden_dim"]), "output_size": output_size,
+                                    "part_loss_scale": scale, "task": task}
+    runtime.state["part_loss_scale"] = scale
+    runtime.state["task"] = task
+
+
+def _get_labels(graph: Any) -> torch.Tensor | None:
+    y = graph.dstdata.get("y")
+    if y is None:
+        y = graph.srcdata.get("y")
+        y = None if y is None else y[: graph.num_dst_nodes]
+    if y is None:
+        return None
+    return y.view(-1, 1) if y.dim() == 1 else y
+
+
+def _forward_single_graph(runtime: RuntimeBundle, graph: Any, state: Any):
+    graph = RNNStateManager.patch_dummy_methods(graph)
+    model = runtime.model.module if hasattr(runtime.model, "module") else runtime.model
+    return model(graph, state)
+
+
+def _loss_and_predictions(runtime: RuntimeBundle, blob_or_batch, training: bool, need_host: bool = True):
+    model = runtime.model
+    model.train(training)
+    if isinstance(blob_or_batch, STGraphBlob):
+        preds, _ = model(blob_or_batch)
+        last = blob_or_batch.current_graph
+    else:
+        graph = blob_or_batch.graph
+        if graph is None:
+            raise RuntimeError("flare_native batch.graph is not available")
+        preds, new_state = _forward_single_graph(runtime, graph, runtime.state.get("eval_rnn_state"))
+        runtime.state["eval_rnn_state"] = new_state
+        last = graph
+    pred = preds[-1] if isinstance(preds, list) else preds
+    labels = _get_labels(last)
+    pred_values = pred.detach().view(-1).cpu().tolist() if need_host else pred.detach()
+    if labels is None:
+        return None, pred_values, None
+    labels = labels.to(pred.device)
+    if pred.size(-1) != labels.size(-1):
+        labels = labels[..., : pred.size(-1)]
+    scale = float(runtime.state.get("part_loss_scale", 1.0))
+    if runtime.state.get("task") == "node_classification":
+        if pred.size(-1) == 1:
+            loss = F.binary_cross_entropy_with_logits(pred, labels.float()) * scale
+        else:
+            loss = F.cross_entropy(pred, labels.long().view(-1)) * scale
+    else:
+        loss = F.mse_loss(pred, labels.float()) * scale
+    targets = labels.detach().view(-1).cpu().tolist() if need_host else labels.detach()
+    return loss, pred_values, targets
+
+
+def run_flare_train_step(runtime: RuntimeBundle, batch: Any, kernel_output: dict[str, Any],
+                         need_host: bool = True) -> dict[str, Any]:
+    loss, preds, targets = _loss_and_predictions(runtime, batch, training=True, need_host=need_host)
+    if loss is None:
+        raise RuntimeError("Training labels are required for flare_native train_step")
+    runtime.optimizer.zero_grad(set_to_none=True)
+    loss.backward()
+    runtime.optimizer.step()
+    return {"loss": float(loss.detach().item()) if need_host else loss.detach(), "predictions": preds,
+            "targets": targets,
+            "meta": kernel_output.get("meta", {}) | {"model": runtime.state["flare_model"],
+                                                      "sequence_state": "updated"}}
+
+
+def run_flare_eval_step(runtime: RuntimeBundle, batch: Any, kernel_output: dict[str, Any]) -> dict[str, Any]:
+    with torch.no_grad():
+        if getattr(batch, "chain", "") == "snapshot_warmup":
+            _, new_state = _forward_single_graph(runtime, batch.graph, runtime.state.get("eval_rnn_state"))
+            runtime.state["eval_rnn_state"] = new_state
+            return {}
+        loss, preds, targets = _loss_and_predictions(runtime, batch, training=False)
+    out = {"predictions": preds, "targets": targets,
+           "meta": kernel_output.get("meta", {}) | {"model": runtime.state["flare_model"]}}
+    if loss is not None:
+        out["loss"] = float(loss.detach().item())
+        if targets is not None:
+            p = torch.tensor(preds)
+            t = torch.tensor(targets)
+            out["meta"]["metrics"] = {"mae": float((p - t).abs().mean()), "rmse": float((p - t).pow(2).mean().sqrt())}
+    return out
+
+
+def run_flare_predict_step(runtime: RuntimeBundle, batch: Any, kernel_output: dict[str, Any]) -> dict[str, Any]:
+    with torch.no_grad():
+        if getattr(batch, "chain", "") == "snapshot_warmup":
+            _, new_state = _forward_single_graph(runtime, batch.graph, runtime.state.get("eval_rnn_state"))
+            runtime.state["eval_rnn_state"] = new_state
+            return {}
+        _, preds, targets = _loss_and_predictions(runtime, batch, training=False)
+    return {"predictions": preds, "targets": targets,
+            "meta": kernel_output.get("meta", {}) | {"model": runtime.state["flare_model"]}}

@@ -1,0 +1,102 @@
+"""Autograd wrappers of the DTDG sm_100a kernels.
+
+* ``gcn_aggregate(block, x)``: normalised neighbour sum over the block's CSR
+  (forward over the destination-sorted CSR, backward over the source-sorted
+  one — no atomics).
+* ``linear(x, w, b, act)``: tcgen05 GEMM forward, data and weight gradients.
+* ``lstm_cell(x, state, cell)``: fused LSTM cell (one GEMM over [x || h] with a
+  gate epilogue) with a fused backward.
+
+On CPU tensors the same functions run the PyTorch reference math.
+"""
+from __future__ import annotations
+
+import torch
+import torch.nn.functional as F
+
+from starry_unigraph.ops import cuda_ext
+
+
+class _SpMM(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, x_src, rowptr, col, val, rowptr_t, col_t, val_t, n_dst):
+        C = cuda_ext()
+        ctx.save_for_backward(rowptr_t, col_t, val_t)
+        ctx.n_src = x_src.size(0)
+        return C.spmm_csr(rowptr, col, val, x_src.contiguous(), int(n_dst), None, False)
+
+    @staticmethod
+    def backward(ctx, g):
+        rowptr_t, col_t, val_t = ctx.saved_tensors
+        gx = cuda_ext().spmm_csr(rowptr_t, col_t, val_t, g.contiguous(), int(ctx.n_src), None, False)
+        return gx, None, None, None, None, None, None, None
+
+
+def gcn_aggregate(block, x_src: torch.Tensor) -> torch.Tensor:
+    if x_src.is_cuda:
+        c = block.csr()
+        return _SpMM.apply(x_src.float(), c["rowptr"], c["col"], c["val"], c["rowptr_t"], c["col_t"], c["val_t"],
+                           block.num_dst_nodes)
+    norm = block.edge_norm()
+    out = torch.zeros(block.num_dst_nodes, x_src.size(1), dtype=x_src.dtype, device=x_src.device)
+    return out.index_add(0, block.edge_dst.long(), x_src[block.edge_src.long()] * norm.unsqueeze(1))
+
+
+class _Linear(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, x, w, b, act):
+        y = cuda_ext().linear_fwd(x.contiguous(), w.contiguous(), b, int(act))
+        ctx.act = int(act)
+        ctx.has_b = b is not None
+        ctx.save_for_backward(x, w, y if act else None)
+        return y
+
+    @staticmethod
+    def backward(ctx, gy):
+        x, w, y = ctx.saved_tensors
+        C = cuda_ext()
+        gy = gy.contiguous()
+        if ctx.act == 1:
+            gy = gy * (y > 0)
+        elif ctx.act == 2:
+            gy = gy * y * (1 - y)
+        elif ctx.act == 3:
+            gy = gy * (1 - y * y)
+        gx = C.linear_dgrad(gy, w.contiguous()) if ctx.needs_input_grad[0] else None
+        gw = torch.zeros_like(w)
+        gb = torch.zeros(w.size(0), device=w.device) if ctx.has_b else None
+        C.linear_wgrad(gy, x.contiguous(), gw, gb)
+        return gx, gw, gb, None
+
+
+def linear(x: torch.Tensor, w: torch.Tensor, b: torch.Tensor | None = None, act: int = 0) -> torch.Tensor:
+    if x.is_cuda and x.dtype == torch.float32:
+        return _Linear.apply(x, w, b, act)
+    y = F.linear(x, w, b)
+    return {0: y, 1: F.relu(y), 2: torch.sigmoid(y), 3: torch.tanh(y)}[act]
+
+
+class _LSTMCell(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, x, h, c, wi, bi, wf, bf, wg, bg, wo, bo):
+        hn, cn, gates = cuda_ext().lstm_fwd(x.contiguous(), h, c, wi, bi, wf, bf, wg, bg, wo, bo, True)
+        ctx.save_for_backward(x, h, c, cn, gates, wi, wf, wg, wo)
+        ctx.has_h, ctx.has_c = h is not None, c is not None
+        return hn, cn
+
+    @staticmethod
+    def backward(ctx, dh, dc):
+        x, h, c, cn, gates, wi, wf, wg, wo = ctx.saved_tensors
+        gw = [torch.zeros_like(w) for w in (wi, wf, wg, wo)]
+        gb = [torch.zeros(w.size(0), device=w.device) for w in (wi, wf, wg, wo)]
+        dx, dhp, dcp = cuda_ext().lstm_bwd(x.contiguous(), h if ctx.has_h else None, c if ctx.has_c else None, cn,
+                                           gates, dh, dc, wi, wf, wg, wo, gw[0], gb[0], gw[1], gb[1], gw[2], gb[2],
+                                           gw[3], gb[3])
+        return (dx, dhp if ctx.has_h else None, dcp if ctx.has_c else None,
+                gw[0], gb[0], gw[1], gb[1], gw[2], gb[2], gw[3], gb[3])
+
+
+def lstm_cell(x: torch.Tensor, h, c, cell) -> tuple[torch.Tensor, torch.Tensor]:
+    """cell: module with i_t, f_t, g_t, o_t nn.Linear(in + hidden, hidden)."""
+    return _LSTMCell.apply(x.float(), h, c, cell.i_t.weight, cell.i_t.bias, cell.f_t.weight, cell.f_t.bias,
+                           cell.g_t.weight, cell.g_t.bias, cell.o_t.weight, cell.o_t.bias)

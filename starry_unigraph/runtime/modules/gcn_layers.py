@@ -1,0 +1,67 @@
+"""Multi-layer GCN over partitioned snapshot blocks
+(reference runtime/modules/gcn_layers.py:20-165).
+
+Per layer: normalised neighbour aggregation then ``Linear(bias=False)``, ReLU
+between layers. For a block, the first layer aggregates the stored source
+features (local rows + halo rows); later layers obtain halo rows through the
+block's ``Route`` (peer exchange) when running distributed, or zero-pad them.
+"""
+from __future__ import annotations
+
+import torch
+import torch.distributed as dist
+import torch.nn as nn
+
+from starry_unigraph.ops.dtdg import gcn_aggregate, linear
+
+
+def _graph_sequence(blob_or_graph):
+    if hasattr(blob_or_graph, "__iter__") and not hasattr(blob_or_graph, "edge_src"):
+        return list(blob_or_graph)
+    return [blob_or_graph]
+
+
+def _graph_input(graph) -> torch.Tensor:
+    if "x" in graph.dstdata:
+        return graph.dstdata["x"]
+    return graph.srcdata["x"]
+
+
+def _gcn_norm(graph) -> torch.Tensor:
+    return graph.edge_norm().unsqueeze(-1)
+
+
+def _gcn_message_pass(graph, x: torch.Tensor) -> torch.Tensor:
+    if x.size(0) == graph.num_src_nodes:
+        src_x = x
+    elif x.size(0) == graph.num_dst_nodes:
+        route = getattr(graph, "route", None)
+        if route is not None and route.send_index is not None and dist.is_available() and dist.is_initialized():
+            src_x = route.forward(x)
+        else:
+            extra = graph.num_src_nodes - graph.num_dst_nodes
+            src_x = torch.cat([x, x.new_zeros(extra, x.size(-1))], dim=0) if extra > 0 else x
+    else:
+        raise ValueError(f"Unexpected feature rows for block graph: got {x.size(0)}, expected "
+                         f"{graph.num_dst_nodes} or {graph.num_src_nodes}")
+    return gcn_aggregate(graph, src_x)
+
+
+class GCNStack(nn.Module):
+    def __init__(self, input_size: int, hidden_size: int, num_layers: int = 2) -> None:
+        super().__init__()
+        self.layers = nn.ModuleList()
+        d = input_size
+        for _ in range(num_layers):
+            self.layers.append(nn.Linear(d, hidden_size, bias=False))
+            d = hidden_size
+
+    def forward_graph(self, graph, x: torch.Tensor | None = None) -> torch.Tensor:
+        h = _graph_input(graph) if x is None else x
+        for i, layer in enumerate(self.layers):
+            h = _gcn_message_pass(graph, h.float())
+            h = linear(h, layer.weight, None, 1 if i < len(self.layers) - 1 else 0)
+        return h
+
+    def layerwise(self, blob_or_graph) -> list[torch.Tensor]:
+        return [self.forward_graph(g) for g in _graph_sequence(blob_or_graph)]
