@@ -16,7 +16,7 @@ constexpr uint32_t kStreamOutDrop = 0x0D7D0u;
 // (PyTorch GRU gate convention). Produces h' = (1 - z) * n + z * h.
 // ---------------------------------------------------------------------------
 struct EpiGRU {
-  int D = 0, DP = 0;
+  int D = 0, DP = 0;  // DP = gate group width G: tile columns are [r | z | n_i | n_h] x G units
   const float* b_ih = nullptr;   // [3D]
   const float* b_hh = nullptr;   // [3D]
   const float* hprev = nullptr;  // previous hidden rows (nullptr -> zeros)
@@ -33,6 +33,7 @@ struct EpiGRU {
 
 #ifdef __CUDACC__
   __device__ __forceinline__ void operator()(int row, bool valid, int n0, uint32_t taddr, int /*tile_cols*/) const {
+    const int u0 = (n0 / (4 * DP)) * DP;  // first hidden unit of this tile
     const float* hp = nullptr;
     if (valid && hprev != nullptr) {
       const int64_t hr = hprev_index ? hprev_index[row] : row;
@@ -49,7 +50,7 @@ struct EpiGRU {
       if (!valid) continue;
 #pragma unroll
       for (int i = 0; i < 16; ++i) {
-        const int c = c0 + i;
+        const int c = u0 + c0 + i;
         if (c >= D) break;
         const float h = hp ? hp[c] : 0.f;
         const float rg = sigmoidf_(r[i] + b_ih[c] + b_hh[c]);
@@ -61,7 +62,7 @@ struct EpiGRU {
         if (srow >= 0) scatter[srow * scatter_ld + c] = hn;
       }
     }
-    if (valid && srow >= 0 && scatter_ts != nullptr && n0 == 0) scatter_ts[srow] = *ts_value;
+    if (valid && srow >= 0 && scatter_ts != nullptr && u0 == 0) scatter_ts[srow] = *ts_value;
   }
 #endif
 };
@@ -125,46 +126,6 @@ struct EpiOutLN {
 };
 
 
-// Time-encoder gradient epilogue: rows are edges (or roots with t = 0), columns
-// the time-encoding dims; acc = d(cos(w t + b)). Accumulates
-//   dw[c] += sum_rows -sin(w t + b) * t * acc,   db[c] += sum_rows -sin(w t + b) * acc.
-struct EpiTimeGrad {
-  int T = 0;
-  const float* w = nullptr;
-  const float* b = nullptr;
-  const float* t = nullptr;   // per-row time (nullptr -> 0)
-  const int* gcount = nullptr;
-  int group = 1;
-  const int* nrows_dev = nullptr;
-  float* dw = nullptr;
-  float* db = nullptr;
-
-#ifdef __CUDACC__
-  __device__ __forceinline__ void operator()(int row, bool valid, int n0, uint32_t taddr, int tile_cols) const {
-    if (valid && nrows_dev != nullptr && row >= *nrows_dev) valid = false;
-    if (valid && gcount != nullptr && (row % group) >= gcount[row / group]) valid = false;
-    const float tt = (valid && t != nullptr) ? t[row] : 0.f;
-    const int lim = min(T - n0, tile_cols);
-    for (int c0 = 0; c0 < lim; c0 += 16) {
-      float v[16];
-      tmem_ld16(taddr + c0, v);
-#pragma unroll
-      for (int i = 0; i < 16; ++i) {
-        const int c = n0 + c0 + i;
-        float gb = 0.f;
-        if (valid && c < T) gb = -sinf(fmaf(w[c], tt, b[c])) * v[i];
-        float gw = gb * tt;
-        gb = warp_sum(gb);
-        gw = warp_sum(gw);
-        if ((threadIdx.x & 31) == 0 && c < T) {
-          atomicAdd(&db[c], gb);
-          if (t != nullptr) atomicAdd(&dw[c], gw);
-        }
-      }
-    }
-  }
-#endif
-};
 
 
 }  // namespace su
@@ -176,7 +137,7 @@ namespace su {
 // over [x || h]). i, f, o = sigmoid, g = tanh, c' = f c + i g, h' = o tanh(c').
 // Saves the post-activation gates for the backward pass.
 struct EpiLSTM {
-  int H = 0, DP = 0;
+  int H = 0, DP = 0;  // DP = gate group width G: tile columns are [i | f | g | o] x G units
   const float* b_i = nullptr;
   const float* b_f = nullptr;
   const float* b_g = nullptr;
@@ -187,7 +148,8 @@ struct EpiLSTM {
   float* gates = nullptr;         // [rows, 4H] (i, f, g, o) post-activation, optional
 
 #ifdef __CUDACC__
-  __device__ __forceinline__ void operator()(int row, bool valid, int /*n0*/, uint32_t taddr, int /*tc*/) const {
+  __device__ __forceinline__ void operator()(int row, bool valid, int n0, uint32_t taddr, int /*tc*/) const {
+    const int u0 = (n0 / (4 * DP)) * DP;
     for (int c0 = 0; c0 < DP; c0 += 16) {
       float gi[16], gf[16], gg[16], go[16];
       tmem_ld16(taddr + c0, gi);
@@ -197,7 +159,7 @@ struct EpiLSTM {
       if (!valid) continue;
 #pragma unroll
       for (int j = 0; j < 16; ++j) {
-        const int c = c0 + j;
+        const int c = u0 + c0 + j;
         if (c >= H) break;
         const float i = sigmoidf_(gi[j] + b_i[c]);
         const float f = sigmoidf_(gf[j] + b_f[c]);

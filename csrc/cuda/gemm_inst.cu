@@ -65,28 +65,24 @@ static void dispatch(const A& a, const B& b, const E& e, const GemmShape& sh, cu
 void gemm(const SegSource& a, const WeightSource& b, const EpiLinear& e, const GemmShape& sh, cudaStream_t st) {
   dispatch(a, b, e, sh, st);
 }
-void gemm(const SegSource& a, const WeightTSource& b, const EpiLinear& e, const GemmShape& sh, cudaStream_t st) {
+void gemm(const SegSource& a, const MNView<WeightSource>& b, const EpiLinear& e, const GemmShape& sh,
+          cudaStream_t st) {
   dispatch(a, b, e, sh, st);
 }
-void gemm(const TransposedSource& a, const TransposedSource& b, const EpiWeightGrad& e, const GemmShape& sh,
+void gemm(const MNView<SegSource>& a, const MNView<SegSource>& b, const EpiWeightGrad& e, const GemmShape& sh,
           cudaStream_t st) {
   dispatch(a, b, e, sh, st);
 }
 void gemm(const SegSource& a, const WeightSource& b, const EpiGRU& e, const GemmShape& sh, cudaStream_t st) {
-  launch_cfg<256, 2>(a, b, e, sh, st);  // four gate blocks side by side
+  launch_cfg<128, 1>(a, b, e, sh, st);  // one tile = four gates x 32 hidden units (gate-grouped rows)
 }
 void gemm(const SegSource& a, const WeightSource& b, const EpiOutLN& e, const GemmShape& sh, cudaStream_t st) {
   if (sh.N <= 128) launch_cfg<128, 1>(a, b, e, sh, st);
   else launch_cfg<256, 1>(a, b, e, sh, st);
 }
-void gemm(const SegSource& a, const WeightTSource& b, const EpiTimeGrad& e, const GemmShape& sh, cudaStream_t st) {
-  if (sh.N <= 128) launch_cfg<128, 1>(a, b, e, sh, st);
-  else launch_cfg<256, 1>(a, b, e, sh, st);
-}
 
 void gemm(const SegSource& a, const WeightSource& b, const EpiLSTM& e, const GemmShape& sh, cudaStream_t st) {
-  if (sh.N <= 256) launch_cfg<256, 1>(a, b, e, sh, st);
-  else launch_cfg<256, 2>(a, b, e, sh, st);
+  launch_cfg<128, 1>(a, b, e, sh, st);  // one tile = four gates x 32 hidden units (gate-grouped rows)
 }
 
 }  // namespace su

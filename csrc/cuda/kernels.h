@@ -16,12 +16,14 @@ int num_sms(int device);
 
 // ---- tcgen05 GEMM entry points (one overload per producer/epilogue combo) ---
 void gemm(const SegSource& a, const WeightSource& b, const EpiLinear& e, const GemmShape& sh, cudaStream_t st);
-void gemm(const SegSource& a, const WeightTSource& b, const EpiLinear& e, const GemmShape& sh, cudaStream_t st);
-void gemm(const TransposedSource& a, const TransposedSource& b, const EpiWeightGrad& e, const GemmShape& sh,
+void gemm(const SegSource& a, const MNView<WeightSource>& b, const EpiLinear& e, const GemmShape& sh,
+          cudaStream_t st);
+void gemm(const MNView<SegSource>& a, const MNView<SegSource>& b, const EpiWeightGrad& e, const GemmShape& sh,
           cudaStream_t st);
 void gemm(const SegSource& a, const WeightSource& b, const EpiGRU& e, const GemmShape& sh, cudaStream_t st);
 void gemm(const SegSource& a, const WeightSource& b, const EpiOutLN& e, const GemmShape& sh, cudaStream_t st);
-void gemm(const SegSource& a, const WeightTSource& b, const EpiTimeGrad& e, const GemmShape& sh, cudaStream_t st);
+void launch_time_grad_reduce(cudaStream_t st, const float* dT, int64_t rows, int T, const float* t, const float* w,
+                             const float* b, const int* gcount, int group, const int* nrows_dev, float* dw, float* db);
 
 // ---- TGN step kernels --------------------------------------------------------
 struct PrepArgs {

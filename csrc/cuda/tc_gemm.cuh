@@ -43,6 +43,22 @@ __device__ __forceinline__ uint32_t tile_vec_off(int r, int kv) {
 
 #endif  // __CUDACC__
 
+#ifdef __CUDACC__
+// cos / sin of w * t + b. For large phases (time deltas reach 1e8 s) the phase is
+// formed and reduced modulo 2*pi in double precision before the single-precision
+// call: exact to fp32 rounding of the reduced phase, and it keeps the trig
+// functions on their short-argument path.
+__device__ __forceinline__ float reduced_phase(float w, float t, float b) {
+  const float x = fmaf(w, t, b);
+  if (fabsf(x) < 8192.f) return x;
+  const double xd = fma(static_cast<double>(w), static_cast<double>(t), static_cast<double>(b));
+  const double two_pi = 6.283185307179586476925286766559;
+  return static_cast<float>(xd - two_pi * rint(xd / two_pi));
+}
+__device__ __forceinline__ float cos_phase(float w, float t, float b) { return cosf(reduced_phase(w, t, b)); }
+__device__ __forceinline__ float sin_phase(float w, float t, float b) { return sinf(reduced_phase(w, t, b)); }
+#endif
+
 // ---------------------------------------------------------------------------
 // Activation sources: row-wise concatenation of column segments
 // ---------------------------------------------------------------------------
@@ -112,7 +128,7 @@ __device__ __forceinline__ void seg_fill8(const ASeg& g, int row, int c, float (
     case kSegTime: {
       const float t = g.tdt ? g.tdt[row] : 0.f;
 #pragma unroll
-      for (int i = 0; i < 8; ++i) f[i] = (c + i < g.width) ? cosf(fmaf(g.tw[c + i], t, g.tb[c + i])) : 0.f;
+      for (int i = 0; i < 8; ++i) f[i] = (c + i < g.width) ? cos_phase(g.tw[c + i], t, g.tb[c + i]) : 0.f;
       break;
     }
     case kSegOnes:
@@ -138,7 +154,7 @@ __device__ __forceinline__ float seg_load1(const ASeg& g, int row, int c) {
     }
     case kSegTime: {
       const float t = g.tdt ? g.tdt[row] : 0.f;
-      return cosf(fmaf(g.tw[c], t, g.tb[c]));
+      return cos_phase(g.tw[c], t, g.tb[c]);
     }
     case kSegOnes:
       return c == 0 ? 1.f : 0.f;
@@ -150,6 +166,7 @@ __device__ __forceinline__ float seg_load1(const ASeg& g, int row, int c) {
 #endif  // __CUDACC__
 
 struct SegSource {
+  static constexpr bool kMN = false;
   ASeg seg[kMaxSeg];
   int nseg = 0;
   int group = 1;                 // rows come in groups (edges of one root) ...
@@ -166,8 +183,7 @@ struct SegSource {
 #endif
   // 8 consecutive K elements [kv*8, kv*8+8) of row `row`.
 #ifdef __CUDACC__
-  __device__ __forceinline__ uint4 load8(int row, int kv, int nrows) const {
-    float f[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+  __device__ __forceinline__ void load8f(int row, int kv, int nrows, float (&f)[8]) const {
     if (row_valid(row, nrows)) {
       int k = kv * 8;
 #pragma unroll
@@ -180,7 +196,6 @@ struct SegSource {
         k -= seg[s].kpad;
       }
     }
-    return pack_bf16x8(f);
   }
 #endif
 #ifdef __CUDACC__
@@ -197,16 +212,20 @@ struct SegSource {
 #endif
 };
 
-// A[n, m] = inner(m, n): used for weight gradients (reduction over rows m).
-struct TransposedSource {
-  SegSource inner;
-  int inner_rows = 0;  // static row bound of the inner source (the GEMM K extent)
+// MN-major view of a row source: the GEMM operand's MN index runs along the
+// inner source's K space and the GEMM's K index along the inner rows, i.e.
+// operand(mn, k) = inner(row = k, col = mn). The producer loads 8 consecutive mn
+// of one k (one 16-byte vector of the inner row) and the tile is consumed with
+// the MN-major bit of the instruction descriptor, so weight gradients
+// (reduction over samples) and data gradients (W^T) need no transposition.
+template <class Inner>
+struct MNView {
+  static constexpr bool kMN = true;
+  Inner inner;
+  int inner_rows = 0;  // static bound of the inner rows (the GEMM K extent)
 #ifdef __CUDACC__
-  __device__ __forceinline__ uint4 load8(int row, int kv, int /*nrows*/) const {
-    float f[8];
-#pragma unroll
-    for (int i = 0; i < 8; ++i) f[i] = inner.load1(kv * 8 + i, row, inner_rows);
-    return pack_bf16x8(f);
+  __device__ __forceinline__ void load8f(int mn_group, int k, int /*nrows*/, float (&f)[8]) const {
+    inner.load8f(k, mn_group, inner_rows, f);
   }
 #endif
 };
@@ -222,6 +241,7 @@ struct WCell {
   int row0 = 0;
   int col0 = 0;
   int width = 0;
+  int vec = 0;                 // 16-byte loads legal (ld, col0 multiples of 4, aligned base)
 };
 
 struct WeightLayout {
@@ -263,44 +283,42 @@ struct WeightLayout {
 #endif
 };
 
-// B[n, k] = W[n, k] (forward projection; n = output feature).
+// B[n, k] = W[n, k] (forward projection; n = output feature). MNView<WeightSource>
+// gives W^T (data gradients).
 struct WeightSource {
+  static constexpr bool kMN = false;
   WeightLayout L;
+  // gate_group > 0: rows are interleaved by gate in groups of gate_group units, so an
+  // N tile of 4 * gate_group rows holds all four gates of the same hidden units
+  // (recurrent-cell epilogues then need only one tile per unit group).
+  int gate_group = 0;
 #ifdef __CUDACC__
-  __device__ __forceinline__ uint4 load8(int row, int kv, int /*nrows*/) const {
-    float f[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+  __device__ __forceinline__ bool map_row(int row, int& b, int& r) const {
+    if (gate_group > 0) {
+      const int t = row / (L.nblk * gate_group), w = row % (L.nblk * gate_group);
+      b = w / gate_group;
+      r = t * gate_group + w % gate_group;
+      return r < L.blk_rows[b];
+    }
+    return L.find_blk(row, b, r);
+  }
+  __device__ __forceinline__ void load8f(int row, int kv, int /*nrows*/, float (&f)[8]) const {
     int b, r, s, c;
-    if (L.find_blk(row, b, r) && L.find_seg(kv * 8, s, c)) {
+    if (map_row(row, b, r) && L.find_seg(kv * 8, s, c)) {
       const WCell& e = L.cell[b][s];
       if (e.ptr != nullptr) {
         const float* p = e.ptr + (int64_t)(e.row0 + r) * e.ld + e.col0;
+        if (e.vec && c + 8 <= e.width) {
+          const float4 a = *reinterpret_cast<const float4*>(p + c);
+          const float4 b = *reinterpret_cast<const float4*>(p + c + 4);
+          f[0] = a.x; f[1] = a.y; f[2] = a.z; f[3] = a.w;
+          f[4] = b.x; f[5] = b.y; f[6] = b.z; f[7] = b.w;
+        } else {
 #pragma unroll
-        for (int i = 0; i < 8; ++i) f[i] = (c + i < e.width) ? p[c + i] : 0.f;
-      }
-    }
-    return pack_bf16x8(f);
-  }
-#endif
-};
-
-// B[n, k] = W[k, n] (data gradient: n = input feature, k = output feature).
-struct WeightTSource {
-  WeightLayout L;
-#ifdef __CUDACC__
-  __device__ __forceinline__ uint4 load8(int row, int kv, int /*nrows*/) const {
-    float f[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-    int s, c;
-    if (L.find_seg(row, s, c)) {
-#pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        int b, r;
-        if (L.find_blk(kv * 8 + i, b, r)) {
-          const WCell& e = L.cell[b][s];
-          if (e.ptr != nullptr && c < e.width) f[i] = e.ptr[(int64_t)(e.row0 + r) * e.ld + e.col0 + c];
+          for (int i = 0; i < 8; ++i) f[i] = (c + i < e.width) ? p[c + i] : 0.f;
         }
       }
     }
-    return pack_bf16x8(f);
   }
 #endif
 };
@@ -422,6 +440,52 @@ constexpr int gemm_smem_bytes() {
 }
 
 #ifdef __CUDACC__
+// Fill one stage tile of ROWS operand rows x kBK K elements. K-major sources give
+// 8 consecutive K of one row per 16-byte vector; MN-major sources give 8
+// consecutive MN of one K. Both canonical layouts use 128-byte core matrices,
+// LBO = 128 (K direction) and SBO = 1024 (MN direction).
+template <int ROWS, class Src>
+__device__ __forceinline__ void produce_tile(const Src& src, uint8_t* tile, int mn0, int kc, int nrows, int limit) {
+  // All global loads of a batch are issued before any conversion so that the
+  // producer keeps many requests in flight (memory-level parallelism).
+  if constexpr (!Src::kMN) {
+    for (int r = threadIdx.x; r < ROWS; r += 128) {
+      const int row = mn0 + r;
+      float f[kBK / 8][8];
+#pragma unroll
+      for (int kv = 0; kv < kBK / 8; ++kv) {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) f[kv][i] = 0.f;
+        if (row < limit) src.load8f(row, kc * (kBK / 8) + kv, nrows, f[kv]);
+      }
+#pragma unroll
+      for (int kv = 0; kv < kBK / 8; ++kv)
+        *reinterpret_cast<uint4*>(tile + tile_vec_off(r, kv)) = pack_bf16x8(f[kv]);
+    }
+  } else {
+    const int k = threadIdx.x & (kBK - 1);
+    const uint32_t koff = static_cast<uint32_t>((k >> 3) * 128 + (k & 7) * 16);
+    constexpr int G = ROWS / 8;          // MN groups in the tile
+    constexpr int STEP = 128 / kBK;      // threads per K index
+    constexpr int BATCH = 8;
+    for (int g0 = threadIdx.x / kBK; g0 < G; g0 += STEP * BATCH) {
+      float f[BATCH][8];
+#pragma unroll
+      for (int j = 0; j < BATCH; ++j) {
+        const int g = g0 + j * STEP;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) f[j][i] = 0.f;
+        if (g < G && mn0 + g * 8 < limit) src.load8f((mn0 >> 3) + g, kc * kBK + k, nrows, f[j]);
+      }
+#pragma unroll
+      for (int j = 0; j < BATCH; ++j) {
+        const int g = g0 + j * STEP;
+        if (g < G) *reinterpret_cast<uint4*>(tile + g * 1024 + koff) = pack_bf16x8(f[j]);
+      }
+    }
+  }
+}
+
 template <int BN, int NSUB, class ASrc, class BSrc, class Epi>
 __global__ void __launch_bounds__(kGemmThreads, 1)
     tc_gemm_kernel(const __grid_constant__ ASrc asrc, const __grid_constant__ BSrc bsrc,
@@ -432,7 +496,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   constexpr int B_ROWS = BN * NSUB;
   constexpr int B_BYTES = B_ROWS * kBK * 2;
   constexpr uint32_t TMEM_COLS = tmem_cols_for(B_ROWS);
-  constexpr uint32_t IDESC = umma_idesc_bf16_f32(kBM, BN);
+  constexpr uint32_t IDESC = umma_idesc_bf16_f32(kBM, BN) | (ASrc::kMN ? (1u << 15) : 0u) |
+                             (BSrc::kMN ? (1u << 16) : 0u);
 
   extern __shared__ uint8_t smem_dyn[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_dyn) + 1023) & ~uintptr_t(1023));
@@ -502,21 +567,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         }
         uint8_t* a = smemA + s * A_BYTES;
         uint8_t* b = smemB + s * B_BYTES;
-        const int row = mt * kBM + threadIdx.x;
-#pragma unroll 2
-        for (int kv = 0; kv < kBK / 8; ++kv) {
-          const uint4 v = asrc.load8(row, kc * (kBK / 8) + kv, M);
-          *reinterpret_cast<uint4*>(a + tile_vec_off(threadIdx.x, kv)) = v;
-        }
-        for (int r = threadIdx.x; r < B_ROWS; r += 128) {
-          const int n = nt * B_ROWS + r;
-#pragma unroll 2
-          for (int kv = 0; kv < kBK / 8; ++kv) {
-            uint4 v = make_uint4(0, 0, 0, 0);
-            if (n < shape.N) v = bsrc.load8(n, kc * (kBK / 8) + kv, shape.N);
-            *reinterpret_cast<uint4*>(b + tile_vec_off(r, kv)) = v;
-          }
-        }
+        produce_tile<kBM>(asrc, a, mt * kBM, kc, M, M);
+        produce_tile<B_ROWS>(bsrc, b, nt * B_ROWS, kc, shape.N, shape.N);
         fence_proxy_async_smem();
         mbar_arrive(&full[s]);
       }

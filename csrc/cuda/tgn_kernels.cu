@@ -458,28 +458,33 @@ __global__ void tgn_link_kernel(const float* __restrict__ P, const int* __restri
 }
 
 // AP (sklearn semantics), ROC-AUC (ties count 1/2) and the pairwise "mrr" of the reference.
+// Scores are staged in shared memory; each thread owns positives.
 __global__ void __launch_bounds__(1024) tgn_metrics_kernel(const float* __restrict__ scores,
                                                            const int* __restrict__ n_ev, int bmax,
                                                            float* __restrict__ out) {
+  extern __shared__ float sh_scores[];  // [2 * n]
   __shared__ float s_ap, s_auc, s_gt;
-  const int n = *n_ev;
+  const int n = min(*n_ev, bmax);
+  for (int i = threadIdx.x; i < n; i += blockDim.x) {
+    sh_scores[i] = scores[i];
+    sh_scores[n + i] = scores[bmax + i];
+  }
   if (threadIdx.x == 0) { s_ap = 0.f; s_auc = 0.f; s_gt = 0.f; }
   __syncthreads();
   float ap = 0.f, auc = 0.f, gt = 0.f;
   for (int i = threadIdx.x; i < n; i += blockDim.x) {
-    const float sp = scores[i];
-    int pos_ge = 0, all_ge = 0;
-    float a = 0.f, g = 0.f;
+    const float sp = sh_scores[i];
+    int pos_ge = 0, neg_ge = 0, neg_lt = 0, neg_eq = 0;
     for (int j = 0; j < n; ++j) {
-      const float p2 = scores[j], n2 = scores[bmax + j];
+      const float p2 = sh_scores[j], n2 = sh_scores[n + j];
       pos_ge += p2 >= sp;
-      all_ge += (p2 >= sp) + (n2 >= sp);
-      a += sp > n2 ? 1.f : (sp == n2 ? 0.5f : 0.f);
-      g += sp > n2 ? 1.f : 0.f;
+      neg_ge += n2 >= sp;
+      neg_lt += n2 < sp;
+      neg_eq += n2 == sp;
     }
-    ap += static_cast<float>(pos_ge) / static_cast<float>(all_ge);
-    auc += a;
-    gt += g;
+    ap += static_cast<float>(pos_ge) / static_cast<float>(pos_ge + neg_ge);
+    auc += neg_lt + 0.5f * neg_eq;
+    gt += neg_lt;
   }
   ap = warp_sum(ap); auc = warp_sum(auc); gt = warp_sum(gt);
   if ((threadIdx.x & 31) == 0) { atomicAdd(&s_ap, ap); atomicAdd(&s_auc, auc); atomicAdd(&s_gt, gt); }
@@ -556,8 +561,49 @@ void launch_tgn_link(dim3 grid, dim3 block, cudaStream_t st, const float* __rest
 void launch_tgn_metrics(dim3 grid, dim3 block, cudaStream_t st, const float* __restrict__ scores,
                                                            const int* __restrict__ n_ev, int bmax,
                                                            float* __restrict__ out) {
-  tgn_metrics_kernel<<<grid, block, 0, st>>>(scores, n_ev, bmax, out);
+  const int smem = 2 * bmax * static_cast<int>(sizeof(float));
+  if (smem > 48 * 1024) cudaFuncSetAttribute(tgn_metrics_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  tgn_metrics_kernel<<<grid, block, smem, st>>>(scores, n_ev, bmax, out);
 }
 
 }  // namespace su
 
+
+namespace su {
+
+// dw[c] += sum_rows -sin(w[c] t + b[c]) * t * dT[row, c];  db[c] += sum_rows -sin(w[c] t + b[c]) * dT[row, c]
+// (gradient of the cosine time encoding). Threads own columns, blocks own row ranges.
+__global__ void time_grad_reduce_kernel(const float* __restrict__ dT, int64_t rows, int T, const float* __restrict__ t,
+                                        const float* __restrict__ w, const float* __restrict__ b,
+                                        const int* __restrict__ gcount, int group, const int* __restrict__ nrows_dev,
+                                        float* __restrict__ dw, float* __restrict__ db) {
+  const int c = threadIdx.x;
+  if (c >= T) return;
+  const int64_t r0 = static_cast<int64_t>(blockIdx.x) * 64;
+  const int64_t r1 = (rows < r0 + 64) ? rows : (r0 + 64);
+  const int64_t nd = nrows_dev ? static_cast<int64_t>(*nrows_dev) : rows;
+  const int64_t limit = nd < rows ? nd : rows;
+  const float wc = w[c], bc = b[c];
+  float gw = 0.f, gb = 0.f;
+  for (int64_t r = r0; r < r1; ++r) {
+    if (r >= limit) break;
+    if (gcount != nullptr && (r % group) >= gcount[r / group]) continue;
+    const float tt = t ? t[r] : 0.f;
+    const float g = -sin_phase(wc, tt, bc) * dT[r * T + c];
+    gb += g;
+    gw = fmaf(g, tt, gw);
+  }
+  atomicAdd(&db[c], gb);
+  if (t) atomicAdd(&dw[c], gw);
+}
+
+void launch_time_grad_reduce(cudaStream_t st, const float* dT, int64_t rows, int T, const float* t, const float* w,
+                             const float* b, const int* gcount, int group, const int* nrows_dev, float* dw,
+                             float* db) {
+  if (rows == 0) return;
+  const int threads = (T + 31) / 32 * 32;
+  time_grad_reduce_kernel<<<(rows + 63) / 64, threads, 0, st>>>(dT, rows, T, t, w, b, gcount, group, nrows_dev,
+                                                                    dw, db);
+}
+
+}  // namespace su

@@ -44,8 +44,7 @@ std::vector<at::Tensor> lstm_fwd(const at::Tensor& x, const c10::optional<at::Te
   const int rows = static_cast<int>(x.size(0));
   const int in_dim = static_cast<int>(x.size(1));
   const int H = static_cast<int>(wi.size(0));
-  const int DP = (H + 15) / 16 * 16;
-  TORCH_CHECK(4 * DP <= 512, "fused LSTM supports hidden size <= 128");
+  constexpr int G = 32;  // gate group: an N tile holds [i | f | g | o] for 32 hidden units
   auto h_out = at::empty({rows, H}, x.options());
   auto c_out = at::empty({rows, H}, x.options());
   at::Tensor gates = save_gates ? at::empty({rows, 4 * H}, x.options()) : at::Tensor();
@@ -61,10 +60,11 @@ std::vector<at::Tensor> lstm_fwd(const at::Tensor& x, const c10::optional<at::Te
     a.seg[1].kpad = pad8(H);
   }
   WeightSource b;
-  b.L = lstm_layout({wi, wf, wg, wo}, in_dim, H, DP);
+  b.L = lstm_layout({wi, wf, wg, wo}, in_dim, H, H);
+  b.gate_group = G;
   EpiLSTM e;
   e.H = H;
-  e.DP = DP;
+  e.DP = G;
   e.b_i = bi.data_ptr<float>();
   e.b_f = bf.data_ptr<float>();
   e.b_g = bg.data_ptr<float>();
@@ -75,7 +75,7 @@ std::vector<at::Tensor> lstm_fwd(const at::Tensor& x, const c10::optional<at::Te
   e.gates = save_gates ? gates.data_ptr<float>() : nullptr;
   GemmShape sh;
   sh.M = rows;
-  sh.N = 4 * DP;
+  sh.N = 4 * G * ((H + G - 1) / G);
   sh.K = pad8(in_dim) + pad8(H);
   gemm(a, b, e, sh, cur_stream());
   SU_LAUNCH_CHECK();
@@ -114,9 +114,9 @@ std::vector<at::Tensor> lstm_bwd(const at::Tensor& x, const c10::optional<at::Te
     SegSource a;
     a.nseg = 1;
     a.seg[0] = seg_f32(dpre, DP4, pad8(DP4));
-    WeightTSource b;
-    b.L = lstm_layout({wi, wf, wg, wo}, in_dim, H, H);
-    b.L.blk_pad[3] = pad8(DP4) - 3 * H;
+    WeightLayout L = lstm_layout({wi, wf, wg, wo}, in_dim, H, H);
+    L.blk_pad[3] = pad8(DP4) - 3 * H;
+    WeightMN b = weight_mn(L, pad8(DP4));
     EpiLinear e;
     e.out = dxh.data_ptr<float>();
     e.ldo = in_dim + H;
@@ -153,12 +153,8 @@ std::vector<at::Tensor> lstm_bwd(const at::Tensor& x, const c10::optional<at::Te
       xs.seg[1].kpad = pad8(H);
     }
     xs.seg[2] = seg_ones();
-    TransposedSource ta;
-    ta.inner = dy;
-    ta.inner_rows = rows;
-    TransposedSource tb;
-    tb.inner = xs;
-    tb.inner_rows = rows;
+    SegMN ta = seg_mn(dy, rows);
+    SegMN tb = seg_mn(xs, rows);
     EpiWeightGrad e;
     e.L = lstm_layout({gwi, gwf, gwg, gwo}, in_dim, H, H);
     e.L.nseg = 3;

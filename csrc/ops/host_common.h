@@ -64,7 +64,24 @@ inline WCell wcell(const at::Tensor& w, int row0, int col0, int width) {
   c.row0 = row0;
   c.col0 = col0;
   c.width = width;
+  c.vec = ((c.ld % 4) == 0 && (col0 % 4) == 0 && (reinterpret_cast<uintptr_t>(c.ptr) % 16) == 0) ? 1 : 0;
   return c;
+}
+
+using WeightMN = MNView<WeightSource>;
+using SegMN = MNView<SegSource>;
+
+inline WeightMN weight_mn(const WeightLayout& L, int out_rows) {
+  WeightMN v;
+  v.inner.L = L;
+  v.inner_rows = out_rows;
+  return v;
+}
+inline SegMN seg_mn(const SegSource& s, int rows) {
+  SegMN v;
+  v.inner = s;
+  v.inner_rows = rows;
+  return v;
 }
 
 }  // namespace su

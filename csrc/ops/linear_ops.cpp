@@ -67,9 +67,9 @@ at::Tensor linear_dgrad(const at::Tensor& dy, const at::Tensor& w) {
   SegSource a;
   a.nseg = 1;
   a.seg[0] = seg_f32(dy, N, pad8(N));
-  WeightTSource b;
-  b.L = single_weight_layout(w);
-  b.L.blk_pad[0] = pad8(N);
+  WeightLayout L = single_weight_layout(w);
+  L.blk_pad[0] = pad8(N);
+  WeightMN b = weight_mn(L, pad8(N));
   EpiLinear e;
   e.out = dx.data_ptr<float>();
   e.ldo = K;
@@ -87,15 +87,15 @@ void linear_wgrad(const at::Tensor& dy, const at::Tensor& x, at::Tensor& dw, con
   SU_CHECK_CUDA(dy); SU_CHECK_F32(dy); SU_CHECK_CONTIG(dy); SU_CHECK_F32(x); SU_CHECK_F32(dw); SU_CHECK_CONTIG(dw);
   const int M = static_cast<int>(dy.size(0)), N = static_cast<int>(dy.size(1)), K = static_cast<int>(x.size(1));
   if (M == 0) return;
-  TransposedSource a;  // A[n, m] = dY[m, n]
-  a.inner.nseg = 1;
-  a.inner.seg[0] = seg_f32(dy, N, pad8(N));
-  a.inner_rows = M;
-  TransposedSource b;  // B[k, m] = X[m, k] (+ ones column for the bias gradient)
-  b.inner.nseg = 2;
-  b.inner.seg[0] = seg_f32(x, K, pad8(K));
-  b.inner.seg[1] = seg_ones();
-  b.inner_rows = M;
+  SegSource dys;  // A[n, m] = dY[m, n] (MN-major view)
+  dys.nseg = 1;
+  dys.seg[0] = seg_f32(dy, N, pad8(N));
+  SegSource xs;  // B[k, m] = X[m, k] (+ ones column for the bias gradient)
+  xs.nseg = 2;
+  xs.seg[0] = seg_f32(x, K, pad8(K));
+  xs.seg[1] = seg_ones();
+  SegMN a = seg_mn(dys, M);
+  SegMN b = seg_mn(xs, M);
   EpiWeightGrad e;
   e.L.nblk = 1;
   e.L.nseg = 2;

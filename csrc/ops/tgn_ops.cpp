@@ -64,18 +64,19 @@ void tgn_sample(const at::Tensor& roots, const at::Tensor& n_roots, const at::Te
 
 // One GRU step over rows `index` of `x_src` (gathered, column block col0..col0+width)
 // with previous hidden rows (or zeros); see EpiGRU for outputs.
+static constexpr int kGateGroup = 32;  // hidden units per gate group in an N tile (4 gates x 32 = 128 columns)
+
 static void gru_step(const SegSource& a, int kx, int kh, const at::Tensor& w_ih, const at::Tensor& w_hh,
                      const at::Tensor& b_ih, const at::Tensor& b_hh, EpiGRU e, int rmax, const int* m_dev) {
   const int D = static_cast<int>(w_hh.size(1));
-  const int DP = (D + 15) / 16 * 16;
-  TORCH_CHECK(4 * DP <= 512, "fused GRU epilogue supports hidden size <= 128");
   const int KX = static_cast<int>(w_ih.size(1));
   WeightSource b;
+  b.gate_group = kGateGroup;
   b.L.nblk = 4;
   b.L.nseg = kh > 0 ? 2 : 1;
   for (int i = 0; i < 4; ++i) {
     b.L.blk_rows[i] = D;
-    b.L.blk_pad[i] = DP;
+    b.L.blk_pad[i] = D;
   }
   b.L.seg_kpad[0] = kx;
   b.L.seg_kpad[1] = kh;
@@ -89,13 +90,13 @@ static void gru_step(const SegSource& a, int kx, int kh, const at::Tensor& w_ih,
     b.L.cell[3][1] = wcell(w_hh, 2 * D, 0, D);
   }
   e.D = D;
-  e.DP = DP;
+  e.DP = kGateGroup;
   e.b_ih = b_ih.data_ptr<float>();
   e.b_hh = b_hh.data_ptr<float>();
   GemmShape sh;
   sh.M = rmax;
   sh.m_dev = m_dev;
-  sh.N = 4 * DP;
+  sh.N = 4 * kGateGroup * ((D + kGateGroup - 1) / kGateGroup);
   sh.K = kx + kh;
   gemm(a, b, e, sh, cur_stream());
 }
@@ -338,12 +339,8 @@ void tgn_out_bwd(const at::Tensor& dout, const at::Tensor& xsave, const at::Tens
 // Weight gradients of a projection whose input is regenerated by a SegSource.
 static void proj_wgrad(const SegSource& dy_src, int dy_cols, const SegSource& x_src_with_ones, int x_kspace,
                        int rows_static, const WeightLayout& grad_layout, float* const* bias_grads, int bias_seg) {
-  TransposedSource a;
-  a.inner = dy_src;
-  a.inner_rows = rows_static;
-  TransposedSource b;
-  b.inner = x_src_with_ones;
-  b.inner_rows = rows_static;
+  SegMN a = seg_mn(dy_src, rows_static);
+  SegMN b = seg_mn(x_src_with_ones, rows_static);
   EpiWeightGrad e;
   e.L = grad_layout;
   for (int i = 0; i < kMaxBlk; ++i) e.bias_grad[i] = bias_grads ? bias_grads[i] : nullptr;
@@ -436,65 +433,68 @@ void tgn_attn_proj_bwd(const at::Tensor& memory, const at::Tensor& roots, const 
     float* bg[4] = {g_bk.data_ptr<float>(), g_bv.data_ptr<float>(), nullptr, nullptr};
     proj_wgrad(dy, 2 * Do, x, pad8(D) + pad8(Ei) + pad8(T) + 8, rmax * k, L, bg, 3);
   }
-  // ---------------- time encoder: d(time segment) = dKV [W_k; W_v][:, time] (edges), dQ W_q[:, time] (roots)
+  // ---------------- time encoder: d(time segment) = dKV [W_k; W_v][:, time] (edges), dQ W_q[:, time] (roots),
+  // then a column reduction with the derivative of cos(w t + b)
   {
+    at::Tensor dT = at::empty({static_cast<int64_t>(rmax) * k, T}, dKV.options());
     SegSource a;
     a.group = k;
     a.gcount = nbr_cnt.data_ptr<int>();
     a.nseg = 1;
     a.seg[0] = seg_f32(dKV, 2 * Do, pad8(2 * Do));
-    WeightTSource b;  // B[n = time col, k = output feature] = W[k, D + E + n]
-    b.L.nblk = 2;
-    b.L.nseg = 1;
-    b.L.blk_rows[0] = Do;
-    b.L.blk_pad[0] = Do;
-    b.L.blk_rows[1] = Do;
-    b.L.blk_pad[1] = pad8(2 * Do) - Do;
-    b.L.seg_kpad[0] = T;
-    b.L.cell[0][0] = wcell(wk, 0, D + Ei, T);
-    b.L.cell[1][0] = wcell(wv, 0, D + Ei, T);
-    EpiTimeGrad e;
-    e.T = T;
-    e.w = te_w.data_ptr<float>();
-    e.b = te_b.data_ptr<float>();
-    e.t = nbr_dt.data_ptr<float>();
-    e.gcount = nbr_cnt.data_ptr<int>();
-    e.group = k;
-    e.dw = g_tw.data_ptr<float>();
-    e.db = g_tb.data_ptr<float>();
+    WeightLayout L;  // rows (GEMM K) = output features of [W_k; W_v], columns (GEMM N) = time dims
+    L.nblk = 2;
+    L.nseg = 1;
+    L.blk_rows[0] = Do;
+    L.blk_pad[0] = Do;
+    L.blk_rows[1] = Do;
+    L.blk_pad[1] = pad8(2 * Do) - Do;
+    L.seg_kpad[0] = pad8(T);
+    L.cell[0][0] = wcell(wk, 0, D + Ei, T);
+    L.cell[1][0] = wcell(wv, 0, D + Ei, T);
+    WeightMN b = weight_mn(L, pad8(2 * Do));
+    EpiLinear e;
+    e.out = dT.data_ptr<float>();
+    e.ldo = T;
+    e.ncols = T;
     GemmShape sh;
     sh.M = rmax * k;
     sh.N = T;
     sh.K = pad8(2 * Do);
     gemm(a, b, e, sh, cur_stream());
+    launch_time_grad_reduce(cur_stream(), dT.data_ptr<float>(), static_cast<int64_t>(rmax) * k, T,
+                            nbr_dt.data_ptr<float>(), te_w.data_ptr<float>(), te_b.data_ptr<float>(),
+                            nbr_cnt.data_ptr<int>(), k, nullptr, g_tw.data_ptr<float>(), g_tb.data_ptr<float>());
   }
   {
+    at::Tensor dT = at::empty({rmax, T}, dQ.options());
     SegSource a;
     a.nrows_dev = n_roots.data_ptr<int>();
     a.nseg = 1;
     a.seg[0] = seg_f32(dQ, Do, pad8(Do));
-    WeightTSource b;
-    b.L.nblk = 1;
-    b.L.nseg = 1;
-    b.L.blk_rows[0] = Do;
-    b.L.blk_pad[0] = pad8(Do);
-    b.L.seg_kpad[0] = T;
-    b.L.cell[0][0] = wcell(wq, 0, D, T);
-    EpiTimeGrad e;
-    e.T = T;
-    e.w = te_w.data_ptr<float>();
-    e.b = te_b.data_ptr<float>();
-    e.t = nullptr;
-    e.nrows_dev = n_roots.data_ptr<int>();
-    e.dw = g_tw.data_ptr<float>();
-    e.db = g_tb.data_ptr<float>();
+    WeightLayout L;
+    L.nblk = 1;
+    L.nseg = 1;
+    L.blk_rows[0] = Do;
+    L.blk_pad[0] = pad8(Do);
+    L.seg_kpad[0] = pad8(T);
+    L.cell[0][0] = wcell(wq, 0, D, T);
+    WeightMN b = weight_mn(L, pad8(Do));
+    EpiLinear e;
+    e.out = dT.data_ptr<float>();
+    e.ldo = T;
+    e.ncols = T;
     GemmShape sh;
     sh.M = rmax;
     sh.m_dev = n_roots.data_ptr<int>();
     sh.N = T;
     sh.K = pad8(Do);
     gemm(a, b, e, sh, cur_stream());
+    launch_time_grad_reduce(cur_stream(), dT.data_ptr<float>(), rmax, T, nullptr, te_w.data_ptr<float>(),
+                            te_b.data_ptr<float>(), nullptr, 1, n_roots.data_ptr<int>(), g_tw.data_ptr<float>(),
+                            g_tb.data_ptr<float>());
   }
+  SU_LAUNCH_CHECK();
 }
 
 // Output projection backward: dW_out, db_out and d(agg) from dpre.
@@ -533,13 +533,14 @@ void tgn_out_proj_bwd(const at::Tensor& dpre, const at::Tensor& agg, const at::T
     a.nrows_dev = n_roots.data_ptr<int>();
     a.nseg = 1;
     a.seg[0] = seg_f32(dpre, Do, pad8(Do));
-    WeightTSource b;  // B[n = agg col, k = out feature] = W_out[k, n]
-    b.L.nblk = 1;
-    b.L.nseg = 1;
-    b.L.blk_rows[0] = Do;
-    b.L.blk_pad[0] = Do;
-    b.L.seg_kpad[0] = Do;
-    b.L.cell[0][0] = wcell(w_out, 0, 0, Do);
+    WeightLayout L;  // B[n = agg col, k = out feature] = W_out[k, n]
+    L.nblk = 1;
+    L.nseg = 1;
+    L.blk_rows[0] = Do;
+    L.blk_pad[0] = pad8(Do);
+    L.seg_kpad[0] = pad8(Do);
+    L.cell[0][0] = wcell(w_out, 0, 0, Do);
+    WeightMN b = weight_mn(L, pad8(Do));
     EpiLinear e;
     e.out = dagg.data_ptr<float>();
     e.ldo = Do;
@@ -648,16 +649,17 @@ void tgn_link_proj_bwd(const at::Tensor& dP, const at::Tensor& out, const at::Te
     a.nrows_dev = n_roots.data_ptr<int>();
     a.nseg = 1;
     a.seg[0] = seg_f32(dP, 2 * Dp, pad8(2 * Dp));
-    WeightTSource b;
-    b.L.nblk = 2;
-    b.L.nseg = 1;
-    b.L.blk_rows[0] = Dp;
-    b.L.blk_pad[0] = Dp;
-    b.L.blk_rows[1] = Dp;
-    b.L.blk_pad[1] = pad8(2 * Dp) - Dp;
-    b.L.seg_kpad[0] = D;
-    b.L.cell[0][0] = wcell(w_src, 0, 0, D);
-    b.L.cell[1][0] = wcell(w_dst, 0, 0, D);
+    WeightLayout L;
+    L.nblk = 2;
+    L.nseg = 1;
+    L.blk_rows[0] = Dp;
+    L.blk_pad[0] = Dp;
+    L.blk_rows[1] = Dp;
+    L.blk_pad[1] = pad8(2 * Dp) - Dp;
+    L.seg_kpad[0] = pad8(D);
+    L.cell[0][0] = wcell(w_src, 0, 0, D);
+    L.cell[1][0] = wcell(w_dst, 0, 0, D);
+    WeightMN b = weight_mn(L, pad8(2 * Dp));
     EpiLinear e;
     e.out = dout.data_ptr<float>();
     e.ldo = D;

@@ -1,0 +1,1 @@
+"""Graph-mode backends: ``ctdg`` (online event streams), ``dtdg`` (Flare snapshots), ``chunk``."""

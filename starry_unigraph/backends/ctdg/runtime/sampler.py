@@ -69,6 +69,10 @@ class TemporalCSR:
             take_all = end.unsqueeze(1) - cnt.unsqueeze(1) + j
             pos = torch.where((avail <= k).unsqueeze(1), take_all, draw)
         valid = j < cnt.unsqueeze(1)
+        if self.nbr.numel() == 0:  # no events at all: every slot is empty
+            none = torch.full(pos.shape, -1, dtype=torch.long, device=dev)
+            return DenseBlock(roots=roots, nbr=none, eid=none.clone(), dt=torch.zeros(pos.shape, device=dev),
+                              count=torch.zeros_like(cnt, dtype=torch.int32))
         pos = torch.where(valid, pos, torch.zeros_like(pos))
         nbr = torch.where(valid, self.nbr[pos], torch.full_like(pos, -1))
         eid = torch.where(valid, self.eid[pos], torch.full_like(pos, -1))

@@ -81,9 +81,8 @@ class STGraphLoader:
             ends_list = (ends_list + [None] * window)[:window]
         if ends_list is None:
             for i in range(len(self)):
-                g = RNNStateManager.patch_dummy_methods(self.fetch_graph(i, perm=perm))
                 states = RNNStateManager(ends_list=[None], mode="pad", disable_routes=disable_routes)
-                states.add(g)
+                states.add(self.fetch_graph(i, perm=perm))
                 yield STGraphBlob(states)
         else:
             states = RNNStateManager(ends_list=ends_list, mode="pad" if disable_states else "mix",

@@ -149,11 +149,15 @@ class SchedulerSession:
             from starry_unigraph.runtime.chunk import ChunkRuntimeLoader
 
             validate_artifacts(self.prepared, "chunk", self.ctx.dist.world_size)
+            from starry_unigraph.backends.ctdg.runtime.factory import build_ctdg_runtime
+
             self.snapshot_core = ChunkRuntimeLoader.from_prepared_artifacts(
                 prepared_dir=self.ctx.artifact_root, device=device, rank=self.ctx.dist.rank,
                 world_size=self.ctx.dist.world_size, config=self.ctx.config)
-            self.runtime = RuntimeBundle(state={"graph_mode": "chunk",
-                                                "chunk_manifest": self.snapshot_core.chunk_manifest})
+            online, bundle = build_ctdg_runtime(self.ctx)
+            self.snapshot_core.attach_ctdg(online)
+            self.runtime = bundle
+            self.runtime.state.update({"graph_mode": "chunk", "chunk_manifest": self.snapshot_core.chunk_manifest})
         else:
             raise ValueError(f"Unknown graph_mode: {mode}")
         return self.runtime

@@ -1,0 +1,159 @@
+"""SchedulerSession lifecycle on CPU (reference tests/test_session.py, rewritten for this API)."""
+import json
+import subprocess
+import sys
+from pathlib import Path
+
+import pytest
+import torch
+
+from starry_unigraph import SchedulerSession
+
+ROOT = Path(__file__).resolve().parents[1]
+
+
+def make_config(tmp_path, family="tgn", task=None, **over):
+    ctdg = family in ("tgn", "jodie", "dyrep", "tgat", "apan")
+    cfg = {"model": {"name": family, "family": family,
+                     "task": task or ("temporal_link_prediction" if ctdg else "snapshot_node_regression"),
+                     "hidden_dim": 16},
+           "data": {"root": str(tmp_path / "data"), "name": f"mock_{family}", "format": "mock"},
+           "train": {"epochs": 1, "batch_size": 8, "snaps": 12},
+           "runtime": {"device": "cpu", "checkpoint": str(tmp_path / "ckpt" / "latest.pt")},
+           "graph": {"storage": "events" if ctdg else "snapshots"},
+           "ctdg": {"dim_time": 8, "mailbox_slots": 2}}
+    for k, v in over.items():
+        cfg.setdefault(k, {}).update(v)
+    return cfg
+
+
+def _session(tmp_path, **kw):
+    s = SchedulerSession.from_config(make_config(tmp_path, **kw))
+    s.ctx.artifact_root = tmp_path / "artifacts"
+    return s
+
+
+@pytest.mark.parametrize("family", ["tgn", "jodie", "dyrep", "tgat", "apan"])
+def test_ctdg_prepare_train_eval_predict(tmp_path, family):
+    s = _session(tmp_path, family=family)
+    prepared = s.prepare_data()
+    meta = json.loads(prepared.meta_path.read_text())
+    assert meta["graph_mode"] == "ctdg" and meta["artifact_version"] == 1
+    for rel in ("partitions/manifest.json", "routes/manifest.json", "sampling/index.json"):
+        assert (s.ctx.artifact_root / rel).exists()
+    s.build_runtime()
+    r = s.run_epoch("train")
+    assert set(r) >= {"split", "steps", "local_steps", "loss", "local_loss", "metrics", "elapsed_s",
+                      "local_elapsed_s", "outputs"}
+    assert r["steps"] > 0 and r["loss"] > 0
+    v = s.evaluate("val")
+    assert v["steps"] > 0
+    p = s.predict("test")
+    assert len(p.predictions) > 0 and p.meta["graph_mode"] == "ctdg"
+
+
+@pytest.mark.parametrize("family", ["mpnn_lstm", "tgcn", "evolvegcn", "gcn"])
+def test_dtdg_prepare_train_eval_predict(tmp_path, family):
+    s = _session(tmp_path, family=family)
+    s.prepare_data()
+    for rel in ("flare/manifest.json", "flare/part_000.pth", "partitions/manifest.json", "routes/manifest.json"):
+        assert (s.ctx.artifact_root / rel).exists()
+    s.build_runtime()
+    assert s.runtime.state["graph_mode"] == "dtdg"
+    r = s.run_epoch("train")
+    assert r["steps"] > 0 and r["loss"] >= 0
+    v = s.run_epoch("val")
+    assert v["steps"] >= 1
+    p = s.predict("test")
+    assert len(p.predictions) > 0 and p.targets is not None
+
+
+def test_run_task(tmp_path):
+    s = _session(tmp_path, family="mpnn_lstm")
+    s.prepare_data()
+    out = s.run_task()
+    assert out["epochs"] == 1 and len(out["train"]) == 1 and len(out["eval"]) == 1
+
+
+def test_ctdg_checkpoint_roundtrip(tmp_path):
+    s = _session(tmp_path)
+    s.prepare_data()
+    s.build_runtime()
+    s.run_epoch("train")
+    path = s.save_checkpoint(tmp_path / "c.pt", exact_resume=True)
+    ck = torch.load(path, weights_only=False)
+    assert set(ck) >= {"model", "memory_updater", "memory_bank"}
+    s2 = _session(tmp_path)
+    s2.prepared = None
+    s2.ctx.artifact_root = s.ctx.artifact_root
+    s2.build_runtime()
+    s2.load_checkpoint(path)
+    for a, b in zip(s.runtime.model.state_dict().values(), s2.runtime.model.state_dict().values()):
+        assert torch.equal(a, b)
+
+
+def test_dtdg_checkpoint_roundtrip(tmp_path):
+    s = _session(tmp_path, family="tgcn")
+    s.prepare_data()
+    s.build_runtime()
+    s.run_epoch("train")
+    path = s.save_checkpoint(tmp_path / "d.pt")
+    payload = torch.load(path, weights_only=False)
+    assert set(payload) >= {"model_state", "optimizer_state", "scheduler_state", "config", "epoch", "global_step"}
+    s2 = _session(tmp_path, family="tgcn")
+    s2.ctx.artifact_root = s.ctx.artifact_root
+    s2.load_checkpoint(path)
+    assert s2.current_epoch == 1
+    for a, b in zip(s.runtime.model.state_dict().values(), s2.runtime.model.state_dict().values()):
+        assert torch.equal(a, b)
+
+
+def test_artifact_validation(tmp_path):
+    from starry_unigraph.session import validate_artifacts
+
+    s = _session(tmp_path, family="mpnn_lstm")
+    prepared = s.prepare_data()
+    validate_artifacts(prepared, "dtdg", 1)
+    with pytest.raises(RuntimeError):
+        validate_artifacts(prepared, "ctdg", 1)
+    with pytest.raises(RuntimeError):
+        validate_artifacts(prepared, "dtdg", 2)
+    meta = json.loads(prepared.meta_path.read_text())
+    meta["artifact_version"] = 99
+    prepared.meta_path.write_text(json.dumps(meta))
+    with pytest.raises(RuntimeError):
+        validate_artifacts(prepared, "dtdg", 1)
+
+
+def test_build_runtime_without_prepare_raises(tmp_path):
+    s = _session(tmp_path)
+    with pytest.raises(RuntimeError):
+        s.build_runtime()
+
+
+def test_node_classification_dtdg(tmp_path):
+    cfg = make_config(tmp_path, family="tgcn", task="node_classification")
+    cfg["data"] = {"root": str(tmp_path), "name": "cls", "format": "synthetic",
+                   "synthetic": {"num_nodes": 300, "num_snapshots": 6, "edges_per_snapshot": 1500, "churn": 0.1,
+                                 "feat_dim": 8, "label": "binary"}}
+    s = SchedulerSession.from_config(cfg)
+    s.ctx.artifact_root = tmp_path / "a"
+    s.prepare_data()
+    s.build_runtime()
+    r = s.run_epoch("train")
+    assert r["loss"] > 0
+
+
+def test_cli_prepare_train_predict(tmp_path):
+    import yaml
+
+    cfg = make_config(tmp_path, family="mpnn_lstm")
+    path = tmp_path / "cfg.yaml"
+    path.write_text(yaml.safe_dump(cfg))
+    env = {"PYTHONPATH": str(ROOT), "PATH": "/usr/bin:/bin"}
+    for phase in ("prepare", "train", "predict"):
+        out = subprocess.run([sys.executable, "-m", "starry_unigraph", "--config", str(path), "--phase", phase,
+                              "--artifact-root", str(tmp_path / "art")], capture_output=True, text=True,
+                             cwd=tmp_path, env=env, timeout=300)
+        assert out.returncode == 0, out.stderr[-2000:]
+    assert "MAE=" in out.stdout
