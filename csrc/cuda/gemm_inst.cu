@@ -55,6 +55,45 @@ static void launch_cfg(const A& a, const B& b, const E& e, const GemmShape& sh, 
   kern<<<grid, kGemmThreads, smem, st>>>(a, b, e, sh, device_status_ptr(device));
 }
 
+// launch_cfg with an explicit status word; setup (the shared-memory attribute,
+// the SM count) allocates nothing.
+template <int BN, int NSUB, class A, class B, class E>
+static void launch_cfg_status(const A& a, const B& b, const E& e, const GemmShape& sh, cudaStream_t st,
+                              int* status) {
+  constexpr int smem = gemm_smem_bytes<BN, NSUB>();
+  auto kern = tc_gemm_kernel<BN, NSUB, A, B, E>;
+  int device = 0;
+  cudaGetDevice(&device);
+  static unsigned long long configured = 0ull;
+  if (!(configured & (1ull << device))) {
+    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    configured |= (1ull << device);
+  }
+  const int tiles_m = (sh.M + kBM - 1) / kBM;
+  const int tiles_n = (sh.N + BN * NSUB - 1) / (BN * NSUB);
+  const int total = tiles_m * tiles_n * std::max(1, sh.ksplit);
+  if (total <= 0) return;
+  const int per_sm = (smem <= 100 * 1024) ? 2 : 1;
+  const int grid = std::min(total, num_sms(device) * per_sm);
+  kern<<<grid, kGemmThreads, smem, st>>>(a, b, e, sh, status);
+}
+
+template <class A, class B, class E>
+static void dispatch_status(const A& a, const B& b, const E& e, const GemmShape& sh, cudaStream_t st, int* status) {
+  if (sh.N <= 128) launch_cfg_status<128, 1>(a, b, e, sh, st, status);
+  else if (sh.N <= 256) launch_cfg_status<256, 1>(a, b, e, sh, st, status);
+  else launch_cfg_status<256, 2>(a, b, e, sh, st, status);
+}
+
+void gemm_with_status(const SegSource& a, const MNView<WeightSource>& b, const EpiLinear& e, const GemmShape& sh,
+                      cudaStream_t st, int* status) {
+  dispatch_status(a, b, e, sh, st, status);
+}
+void gemm_with_status(const MNView<SegSource>& a, const MNView<SegSource>& b, const EpiWeightGrad& e,
+                      const GemmShape& sh, cudaStream_t st, int* status) {
+  dispatch_status(a, b, e, sh, st, status);
+}
+
 template <class A, class B, class E>
 static void dispatch(const A& a, const B& b, const E& e, const GemmShape& sh, cudaStream_t st) {
   if (sh.N <= 128) launch_cfg<128, 1>(a, b, e, sh, st);
