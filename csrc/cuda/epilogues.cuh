@@ -22,6 +22,8 @@ struct EpiGRU {
   const float* hprev = nullptr;  // previous hidden rows (nullptr -> zeros)
   const int64_t* hprev_index = nullptr;
   int hprev_ld = 0;
+  const float* const* hprev_peers = nullptr;  // optional: hprev rows live in the owner rank's table
+  const int* hprev_owner = nullptr;
   float* hout = nullptr;         // dense output rows (optional)
   int hout_ld = 0;
   float* save_prev = nullptr;    // copy of the previous hidden rows (optional)
@@ -37,7 +39,7 @@ struct EpiGRU {
     const float* hp = nullptr;
     if (valid && hprev != nullptr) {
       const int64_t hr = hprev_index ? hprev_index[row] : row;
-      if (hr >= 0) hp = hprev + hr * hprev_ld;
+      if (hr >= 0) hp = (hprev_peers ? hprev_peers[hprev_owner[hr]] : hprev) + hr * hprev_ld;
     }
     int64_t srow = -1;
     if (valid && scatter != nullptr) srow = scatter_index[row];

@@ -106,6 +106,24 @@ void launch_spmm_csr(cudaStream_t st, const int64_t* rowptr, const int* col, con
 void launch_lstm_bwd(cudaStream_t st, const float* gates, const float* c_prev, const float* c_new, const float* dh,
                      const float* dc, int64_t rows, int H, float* dpre, float* dc_prev);
 
+// ---- peer (NVLink) kernels -----------------------------------------------------
+void launch_peer_barrier(cudaStream_t st, uint64_t* const* flag_ptrs, int rank, int W, int64_t* epoch, int* status,
+                         long long budget);
+void launch_peer_allreduce_adam(cudaStream_t st, int blocks, const float* const* grads, int W, float* p, float* m,
+                                float* v, int64_t n, int64_t* step, unsigned int* done, float lr, float b1, float b2,
+                                float eps, float wd, float scale);
+void launch_tgn_peer_writeback(cudaStream_t st, const int64_t* roots, const int* n_roots, int rmax,
+                               const float* mem_new, int D, const int* owner, float* const* mem_tables,
+                               float* const* ts_tables, const float* ts_max);
+void launch_tgn_peer_mail_claim(cudaStream_t st, const int64_t* roots, const int* n_roots, int rmax, const int* win,
+                                const int64_t* ev_eid, const float* ev_ts, const int* owner,
+                                unsigned long long* const* claim_tables);
+void launch_tgn_peer_mail_write(cudaStream_t st, const int64_t* roots, const int* n_roots, int rmax, const int* win,
+                                const int* src_idx, const int* dst_idx, const int64_t* ev_eid, const float* ev_ts,
+                                const float* mem_prev, int D, const float* efeat, int efeat_ld, int e_raw, int E,
+                                const int* owner, const unsigned long long* const* claim_tables,
+                                float* const* mail_tables, float* const* mail_ts_tables);
+
 // ---- optimiser ---------------------------------------------------------------
 void launch_adam_flat(cudaStream_t st, int blocks, float* p, const float* g, float* m, float* v, int64_t n,
                       int64_t* step, unsigned int* done, float lr, float b1, float b2, float eps, float wd,

@@ -85,7 +85,14 @@ struct ASeg {
   const float* tb = nullptr;
   const float* const* peers = nullptr;  // sharded: per-rank base pointers
   const int* owner = nullptr;           // sharded: owning rank per global id
-  const int64_t* lrow = nullptr;        // sharded: row inside the owner's shard
+  const int64_t* lrow = nullptr;        // sharded: row inside the owner's shard (nullptr: the global id)
+  // sharded, optional: rows of ids stamped in this step (stamp[id] == step tag)
+  // are read from the local `fresh` rows at node2root[id] instead of the owner
+  const int* stamp = nullptr;
+  const int* node2root = nullptr;
+  const int64_t* step_ctr = nullptr;    // the step tag is ((*step_ctr - 1) & 0x3FFFFFFF) + 1
+  const float* fresh = nullptr;
+  int fresh_ld = 0;
 };
 
 #ifdef __CUDACC__
@@ -93,6 +100,10 @@ __device__ __forceinline__ const float* seg_row_f32(const ASeg& g, int row) {
   int64_t r = g.index ? g.index[row] : row;
   if (r < 0) return nullptr;
   if (g.kind == kSegSharded) {
+    if (g.stamp != nullptr) {
+      const int tag = static_cast<int>(((*g.step_ctr) - 1) & 0x3FFFFFFF) + 1;
+      if (g.stamp[r] == tag) return g.fresh + static_cast<int64_t>(g.node2root[r]) * g.fresh_ld + g.col0;
+    }
     const int o = g.owner ? g.owner[r] : 0;
     const int64_t lr = g.lrow ? g.lrow[r] : r;
     return g.peers[o] + lr * g.ld + g.col0;

@@ -19,7 +19,8 @@ void tgn_memory_update(const at::Tensor& roots, const at::Tensor& n_roots, const
                        at::Tensor& memory, at::Tensor& memory_ts, const at::Tensor& ts_max, const at::Tensor& gru_w_ih,
                        const at::Tensor& gru_w_hh, const at::Tensor& gru_b_ih, const at::Tensor& gru_b_hh,
                        const at::Tensor& cell_w_ih, const at::Tensor& cell_w_hh, const at::Tensor& cell_b_ih,
-                       const at::Tensor& cell_b_hh, at::Tensor& agg_buf, at::Tensor& agg_buf2, at::Tensor& mem_prev);
+                       const at::Tensor& cell_b_hh, at::Tensor& agg_buf, at::Tensor& agg_buf2, at::Tensor& mem_prev,
+                       const c10::optional<at::Tensor>& peer);
 void tgn_mailbox_write(const at::Tensor& roots, const at::Tensor& n_roots, const at::Tensor& win,
                        const at::Tensor& cnt, const at::Tensor& src_idx, const at::Tensor& dst_idx,
                        const at::Tensor& ev_eid, const at::Tensor& ev_ts, const at::Tensor& mem_prev,
@@ -29,7 +30,8 @@ void tgn_attn_proj(const at::Tensor& memory, const at::Tensor& roots, const at::
                    const at::Tensor& nbr, const at::Tensor& nbr_eid, const at::Tensor& nbr_dt,
                    const at::Tensor& nbr_cnt, const at::Tensor& efeat, int64_t E, const at::Tensor& te_w,
                    const at::Tensor& te_b, const at::Tensor& wq, const at::Tensor& bq, const at::Tensor& wk,
-                   const at::Tensor& bk, const at::Tensor& wv, const at::Tensor& bv, at::Tensor& Q, at::Tensor& KV);
+                   const at::Tensor& bk, const at::Tensor& wv, const at::Tensor& bv, at::Tensor& Q, at::Tensor& KV,
+                   const c10::optional<at::Tensor>& peer);
 void tgn_attn_fwd(const at::Tensor& Q, const at::Tensor& KV, const at::Tensor& nbr_cnt, const at::Tensor& n_roots,
                   int64_t H, double att_drop, int64_t seed, const at::Tensor& step_ctr, at::Tensor& att_p,
                   at::Tensor& agg);
@@ -39,7 +41,7 @@ void tgn_attn_bwd(const at::Tensor& Q, const at::Tensor& KV, const at::Tensor& a
 void tgn_out_fwd(const at::Tensor& agg, const at::Tensor& memory, const at::Tensor& roots, const at::Tensor& n_roots,
                  const at::Tensor& w_out, const at::Tensor& b_out, const at::Tensor& gamma, const at::Tensor& beta,
                  double drop, int64_t seed, const at::Tensor& step_ctr, const at::Tensor& edge_total, at::Tensor& out,
-                 at::Tensor& xsave, at::Tensor& mean, at::Tensor& rstd);
+                 at::Tensor& xsave, at::Tensor& mean, at::Tensor& rstd, const c10::optional<at::Tensor>& peer);
 void tgn_out_bwd(const at::Tensor& dout, const at::Tensor& xsave, const at::Tensor& mean, const at::Tensor& rstd,
                  const at::Tensor& gamma, const at::Tensor& n_roots, double drop, int64_t seed,
                  const at::Tensor& step_ctr, const at::Tensor& edge_total, at::Tensor& dpre, at::Tensor& dgamma,
@@ -50,10 +52,10 @@ void tgn_attn_proj_bwd(const at::Tensor& memory, const at::Tensor& roots, const 
                        const at::Tensor& te_b, const at::Tensor& wq, const at::Tensor& wk, const at::Tensor& wv,
                        const at::Tensor& dQ, const at::Tensor& dKV, at::Tensor& g_wq, at::Tensor& g_bq,
                        at::Tensor& g_wk, at::Tensor& g_bk, at::Tensor& g_wv, at::Tensor& g_bv, at::Tensor& g_tw,
-                       at::Tensor& g_tb);
+                       at::Tensor& g_tb, const c10::optional<at::Tensor>& peer);
 void tgn_out_proj_bwd(const at::Tensor& dpre, const at::Tensor& agg, const at::Tensor& memory,
                       const at::Tensor& roots, const at::Tensor& n_roots, const at::Tensor& w_out, at::Tensor& g_wout,
-                      at::Tensor& g_bout, at::Tensor& dagg);
+                      at::Tensor& g_bout, at::Tensor& dagg, const c10::optional<at::Tensor>& peer);
 void tgn_link_proj(const at::Tensor& out, const at::Tensor& n_roots, const at::Tensor& w_src, const at::Tensor& b_src,
                    const at::Tensor& w_dst, const at::Tensor& b_dst, at::Tensor& P);
 void tgn_link_loss(const at::Tensor& P, const at::Tensor& src_idx, const at::Tensor& dst_idx,
@@ -81,6 +83,23 @@ std::vector<at::Tensor> lstm_bwd(const at::Tensor& x, const c10::optional<at::Te
                                  at::Tensor& gbf, at::Tensor& gwg, at::Tensor& gbg, at::Tensor& gwo,
                                  at::Tensor& gbo);
 
+// peer_ops.cpp
+void peer_barrier(const at::Tensor& flag_ptrs, int64_t rank, int64_t world, at::Tensor& epoch, int64_t budget);
+void peer_allreduce_adam(const at::Tensor& grad_ptrs, int64_t world, at::Tensor& p, at::Tensor& m, at::Tensor& v,
+                         at::Tensor& step, at::Tensor& done, double lr, double b1, double b2, double eps, double wd,
+                         double scale);
+void tgn_peer_writeback(const at::Tensor& roots, const at::Tensor& n_roots, const at::Tensor& mem_new,
+                        const at::Tensor& owner, const at::Tensor& mem_ptrs, const at::Tensor& ts_ptrs,
+                        const at::Tensor& ts_max);
+void tgn_peer_mail_claim(const at::Tensor& roots, const at::Tensor& n_roots, const at::Tensor& win,
+                         const at::Tensor& ev_eid, const at::Tensor& ev_ts, const at::Tensor& owner,
+                         const at::Tensor& claim_ptrs);
+void tgn_peer_mail_write(const at::Tensor& roots, const at::Tensor& n_roots, const at::Tensor& win,
+                         const at::Tensor& src_idx, const at::Tensor& dst_idx, const at::Tensor& ev_eid,
+                         const at::Tensor& ev_ts, const at::Tensor& mem_prev, const at::Tensor& efeat, int64_t E,
+                         const at::Tensor& owner, const at::Tensor& claim_ptrs, const at::Tensor& mail_ptrs,
+                         const at::Tensor& mail_ts_ptrs);
+
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "starry_unigraph sm_100a kernels (tcgen05 GEMMs, TGN step, DTDG ops, collectives)";
   m.def("status_read", &status_read, "read (and clear) the device status word", py::arg("clear") = true);
@@ -103,6 +122,11 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("tgn_metrics", &tgn_metrics);
   m.def("tgn_link_proj_bwd", &tgn_link_proj_bwd);
   m.def("adam_flat", &adam_flat);
+  m.def("peer_barrier", &peer_barrier);
+  m.def("peer_allreduce_adam", &peer_allreduce_adam);
+  m.def("tgn_peer_writeback", &tgn_peer_writeback);
+  m.def("tgn_peer_mail_claim", &tgn_peer_mail_claim);
+  m.def("tgn_peer_mail_write", &tgn_peer_mail_write);
   m.def("spmm_csr", &spmm_csr);
   m.def("lstm_fwd", &lstm_fwd);
   m.def("lstm_bwd", &lstm_bwd);

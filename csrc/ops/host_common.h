@@ -68,6 +68,61 @@ inline WCell wcell(const at::Tensor& w, int row0, int col0, int width) {
   return c;
 }
 
+// Multi-GPU view of the CTDG node tables: rows live in the owner rank's table
+// (peer pointers of symmetric allocations); rows of this step's roots are read
+// from the local `mem_new` buffer once the memory updater has produced them.
+// Passed from Python as a CPU int64 tensor of device addresses:
+//   [mem_peers, mail_peers, owner, stamp, node2root, step_ctr, mem_new]
+struct PeerDesc {
+  bool on = false;
+  const float* const* mem_peers = nullptr;
+  const float* const* mail_peers = nullptr;
+  const int* owner = nullptr;
+  const int* stamp = nullptr;
+  const int* node2root = nullptr;
+  const int64_t* step_ctr = nullptr;
+  float* mem_new = nullptr;
+};
+
+inline PeerDesc peer_desc(const c10::optional<at::Tensor>& t) {
+  PeerDesc d;
+  if (!t.has_value() || !t->defined()) return d;
+  TORCH_CHECK(t->device().is_cpu() && t->scalar_type() == at::kLong && t->numel() == 7, "bad peer descriptor");
+  const int64_t* v = t->data_ptr<int64_t>();
+  d.on = true;
+  d.mem_peers = reinterpret_cast<const float* const*>(v[0]);
+  d.mail_peers = reinterpret_cast<const float* const*>(v[1]);
+  d.owner = reinterpret_cast<const int*>(v[2]);
+  d.stamp = reinterpret_cast<const int*>(v[3]);
+  d.node2root = reinterpret_cast<const int*>(v[4]);
+  d.step_ctr = reinterpret_cast<const int64_t*>(v[5]);
+  d.mem_new = reinterpret_cast<float*>(v[6]);
+  return d;
+}
+
+// memory rows gathered through `index`: the local table, or (multi-GPU) the
+// owners' tables with this step's roots taken from mem_new when `fresh`
+inline ASeg seg_memory(const at::Tensor& memory, int D, const int64_t* index, const PeerDesc& pd, bool fresh) {
+  if (!pd.on) return seg_f32(memory, D, pad8(D), index);
+  ASeg s;
+  s.kind = kSegSharded;
+  s.peers = pd.mem_peers;
+  s.owner = pd.owner;
+  s.ld = D;
+  s.width = D;
+  s.kpad = pad8(D);
+  s.index = index;
+  s.vec = (D % 4) == 0 ? 1 : 0;
+  if (fresh) {
+    s.stamp = pd.stamp;
+    s.node2root = pd.node2root;
+    s.step_ctr = pd.step_ctr;
+    s.fresh = pd.mem_new;
+    s.fresh_ld = D;
+  }
+  return s;
+}
+
 using WeightMN = MNView<WeightSource>;
 using SegMN = MNView<SegSource>;
 

@@ -108,7 +108,9 @@ void tgn_memory_update(const at::Tensor& roots, const at::Tensor& n_roots, const
                        at::Tensor& memory, at::Tensor& memory_ts, const at::Tensor& ts_max, const at::Tensor& gru_w_ih,
                        const at::Tensor& gru_w_hh, const at::Tensor& gru_b_ih, const at::Tensor& gru_b_hh,
                        const at::Tensor& cell_w_ih, const at::Tensor& cell_w_hh, const at::Tensor& cell_b_ih,
-                       const at::Tensor& cell_b_hh, at::Tensor& agg_buf, at::Tensor& agg_buf2, at::Tensor& mem_prev) {
+                       const at::Tensor& cell_b_hh, at::Tensor& agg_buf, at::Tensor& agg_buf2, at::Tensor& mem_prev,
+                       const c10::optional<at::Tensor>& peer) {
+  const PeerDesc pd = peer_desc(peer);
   const int rmax = static_cast<int>(roots.numel());
   const int D = static_cast<int>(memory.size(1));
   const int SW = static_cast<int>(gru_w_ih.size(1));
@@ -120,6 +122,12 @@ void tgn_memory_update(const at::Tensor& roots, const at::Tensor& n_roots, const
     a.nrows_dev = m_dev;
     a.nseg = s == 0 ? 1 : 2;
     a.seg[0] = seg_f32(mailbox.view({mailbox.size(0), -1}), SW, pad8(SW), ridx, s * SW);
+    if (pd.on) {  // mailbox rows of the owner rank
+      a.seg[0].kind = kSegSharded;
+      a.seg[0].peers = pd.mail_peers;
+      a.seg[0].owner = pd.owner;
+      a.seg[0].vec = (a.seg[0].ld % 4 == 0 && (s * SW) % 4 == 0) ? 1 : 0;
+    }
     if (s > 0) a.seg[1] = seg_f32(cur, D, pad8(D));
     EpiGRU e;
     e.hprev = s == 0 ? nullptr : cur.data_ptr<float>();
@@ -134,17 +142,26 @@ void tgn_memory_update(const at::Tensor& roots, const at::Tensor& n_roots, const
   a.nrows_dev = m_dev;
   a.nseg = 2;
   a.seg[0] = seg_f32(cur, D, pad8(D));
-  a.seg[1] = seg_f32(memory, D, pad8(D), ridx);
+  a.seg[1] = seg_memory(memory, D, ridx, pd, false);
   EpiGRU e;
   e.hprev = memory.data_ptr<float>();
   e.hprev_index = ridx;
   e.hprev_ld = D;
   e.save_prev = mem_prev.data_ptr<float>();
-  e.scatter = memory.data_ptr<float>();
-  e.scatter_index = ridx;
-  e.scatter_ld = D;
-  e.scatter_ts = memory_ts.data_ptr<float>();
-  e.ts_value = ts_max.data_ptr<float>();
+  if (pd.on) {
+    // tables stay read-only during the step: new rows go to mem_new and are
+    // written back to the owners after the ranks' barrier
+    e.hprev_peers = pd.mem_peers;
+    e.hprev_owner = pd.owner;
+    e.hout = pd.mem_new;
+    e.hout_ld = D;
+  } else {
+    e.scatter = memory.data_ptr<float>();
+    e.scatter_index = ridx;
+    e.scatter_ld = D;
+    e.scatter_ts = memory_ts.data_ptr<float>();
+    e.ts_value = ts_max.data_ptr<float>();
+  }
   gru_step(a, pad8(D), pad8(D), cell_w_ih, cell_w_hh, cell_b_ih, cell_b_hh, e, rmax, m_dev);
 }
 
@@ -170,7 +187,9 @@ void tgn_attn_proj(const at::Tensor& memory, const at::Tensor& roots, const at::
                    const at::Tensor& nbr, const at::Tensor& nbr_eid, const at::Tensor& nbr_dt,
                    const at::Tensor& nbr_cnt, const at::Tensor& efeat, int64_t E, const at::Tensor& te_w,
                    const at::Tensor& te_b, const at::Tensor& wq, const at::Tensor& bq, const at::Tensor& wk,
-                   const at::Tensor& bk, const at::Tensor& wv, const at::Tensor& bv, at::Tensor& Q, at::Tensor& KV) {
+                   const at::Tensor& bk, const at::Tensor& wv, const at::Tensor& bv, at::Tensor& Q, at::Tensor& KV,
+    const c10::optional<at::Tensor>& peer) {
+  const PeerDesc pd = peer_desc(peer);
   const int rmax = static_cast<int>(roots.numel());
   const int k = static_cast<int>(nbr.numel() / rmax);
   const int D = static_cast<int>(memory.size(1));
@@ -183,7 +202,7 @@ void tgn_attn_proj(const at::Tensor& memory, const at::Tensor& roots, const at::
     SegSource a;
     a.nrows_dev = n_roots.data_ptr<int>();
     a.nseg = 2;
-    a.seg[0] = seg_f32(memory, D, pad8(D), roots.data_ptr<int64_t>());
+    a.seg[0] = seg_memory(memory, D, roots.data_ptr<int64_t>(), pd, true);
     a.seg[1] = seg_time(nullptr, te_w, te_b, pad8(T));
     WeightSource b;
     b.L.nblk = 1;
@@ -212,7 +231,7 @@ void tgn_attn_proj(const at::Tensor& memory, const at::Tensor& roots, const at::
     a.group = k;
     a.gcount = nbr_cnt.data_ptr<int>();
     a.nseg = 3;
-    a.seg[0] = seg_f32(memory, D, pad8(D), nbr.data_ptr<int64_t>());
+    a.seg[0] = seg_memory(memory, D, nbr.data_ptr<int64_t>(), pd, true);
     a.seg[1] = seg_f32(efeat, Ew, pad8(static_cast<int>(E)), nbr_eid.data_ptr<int64_t>());
     a.seg[2] = seg_time(nbr_dt.data_ptr<float>(), te_w, te_b, pad8(T));
     WeightSource b;
@@ -280,7 +299,9 @@ void tgn_attn_bwd(const at::Tensor& Q, const at::Tensor& KV, const at::Tensor& a
 void tgn_out_fwd(const at::Tensor& agg, const at::Tensor& memory, const at::Tensor& roots, const at::Tensor& n_roots,
                  const at::Tensor& w_out, const at::Tensor& b_out, const at::Tensor& gamma, const at::Tensor& beta,
                  double drop, int64_t seed, const at::Tensor& step_ctr, const at::Tensor& edge_total, at::Tensor& out,
-                 at::Tensor& xsave, at::Tensor& mean, at::Tensor& rstd) {
+                 at::Tensor& xsave, at::Tensor& mean, at::Tensor& rstd,
+    const c10::optional<at::Tensor>& peer) {
+  const PeerDesc pd = peer_desc(peer);
   const int rmax = static_cast<int>(roots.numel());
   const int Do = static_cast<int>(w_out.size(0));
   const int D = static_cast<int>(memory.size(1));
@@ -288,7 +309,7 @@ void tgn_out_fwd(const at::Tensor& agg, const at::Tensor& memory, const at::Tens
   a.nrows_dev = n_roots.data_ptr<int>();
   a.nseg = 2;
   a.seg[0] = seg_f32(agg, Do, pad8(Do));
-  a.seg[1] = seg_f32(memory, D, pad8(D), roots.data_ptr<int64_t>());
+  a.seg[1] = seg_memory(memory, D, roots.data_ptr<int64_t>(), pd, true);
   WeightSource b;
   b.L.nblk = 1;
   b.L.nseg = 2;
@@ -365,7 +386,9 @@ void tgn_attn_proj_bwd(const at::Tensor& memory, const at::Tensor& roots, const 
                        const at::Tensor& te_b, const at::Tensor& wq, const at::Tensor& wk, const at::Tensor& wv,
                        const at::Tensor& dQ, const at::Tensor& dKV, at::Tensor& g_wq, at::Tensor& g_bq,
                        at::Tensor& g_wk, at::Tensor& g_bk, at::Tensor& g_wv, at::Tensor& g_bv, at::Tensor& g_tw,
-                       at::Tensor& g_tb) {
+                       at::Tensor& g_tb,
+    const c10::optional<at::Tensor>& peer) {
+  const PeerDesc pd = peer_desc(peer);
   const int rmax = static_cast<int>(roots.numel());
   const int k = static_cast<int>(nbr.numel() / rmax);
   const int D = static_cast<int>(memory.size(1));
@@ -382,7 +405,7 @@ void tgn_attn_proj_bwd(const at::Tensor& memory, const at::Tensor& roots, const 
     SegSource x;
     x.nrows_dev = n_roots.data_ptr<int>();
     x.nseg = 3;
-    x.seg[0] = seg_f32(memory, D, pad8(D), roots.data_ptr<int64_t>());
+    x.seg[0] = seg_memory(memory, D, roots.data_ptr<int64_t>(), pd, true);
     x.seg[1] = seg_time(nullptr, te_w, te_b, pad8(T));
     x.seg[2] = seg_ones();
     WeightLayout L;
@@ -409,7 +432,7 @@ void tgn_attn_proj_bwd(const at::Tensor& memory, const at::Tensor& roots, const 
     x.group = k;
     x.gcount = nbr_cnt.data_ptr<int>();
     x.nseg = 4;
-    x.seg[0] = seg_f32(memory, D, pad8(D), nbr.data_ptr<int64_t>());
+    x.seg[0] = seg_memory(memory, D, nbr.data_ptr<int64_t>(), pd, true);
     x.seg[1] = seg_f32(efeat, Ew, pad8(Ei), nbr_eid.data_ptr<int64_t>());
     x.seg[2] = seg_time(nbr_dt.data_ptr<float>(), te_w, te_b, pad8(T));
     x.seg[3] = seg_ones();
@@ -500,7 +523,9 @@ void tgn_attn_proj_bwd(const at::Tensor& memory, const at::Tensor& roots, const 
 // Output projection backward: dW_out, db_out and d(agg) from dpre.
 void tgn_out_proj_bwd(const at::Tensor& dpre, const at::Tensor& agg, const at::Tensor& memory,
                       const at::Tensor& roots, const at::Tensor& n_roots, const at::Tensor& w_out, at::Tensor& g_wout,
-                      at::Tensor& g_bout, at::Tensor& dagg) {
+                      at::Tensor& g_bout, at::Tensor& dagg,
+    const c10::optional<at::Tensor>& peer) {
+  const PeerDesc pd = peer_desc(peer);
   const int rmax = static_cast<int>(roots.numel());
   const int Do = static_cast<int>(w_out.size(0));
   const int D = static_cast<int>(memory.size(1));
@@ -513,7 +538,7 @@ void tgn_out_proj_bwd(const at::Tensor& dpre, const at::Tensor& agg, const at::T
     x.nrows_dev = n_roots.data_ptr<int>();
     x.nseg = 3;
     x.seg[0] = seg_f32(agg, Do, pad8(Do));
-    x.seg[1] = seg_f32(memory, D, pad8(D), roots.data_ptr<int64_t>());
+    x.seg[1] = seg_memory(memory, D, roots.data_ptr<int64_t>(), pd, true);
     x.seg[2] = seg_ones();
     WeightLayout L;
     L.nblk = 1;

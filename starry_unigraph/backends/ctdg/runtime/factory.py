@@ -76,7 +76,18 @@ def build_ctdg_runtime(session_ctx: SessionContext, dataset: TGTemporalDataset |
         from starry_unigraph.ops.tgn import TGNCudaEngine
 
         grad_sync = None
-        if dctx.is_distributed:
+        peer = None
+        comm_path = str(cfg.get("comm", {}).get("path", "p2p"))
+        if dctx.is_distributed and comm_path == "p2p":
+            from starry_unigraph.parallel.ctdg_peer import PeerCTDGContext
+
+            owner = node_parts if node_parts is not None else \
+                torch.arange(dataset.num_nodes, dtype=torch.long) % dctx.world_size
+            peer = PeerCTDGContext(num_nodes=dataset.num_nodes, hidden_dim=hidden, slot_width=memory.slot_width,
+                                   mailbox_slots=slots, grad_numel=sum(p.numel() for p in model.parameters()),
+                                   owner=owner, device=torch.device(device))
+            peer.attach(memory)
+        elif dctx.is_distributed:
             import torch.distributed as dist
 
             world = dctx.world_size
@@ -93,7 +104,7 @@ def build_ctdg_runtime(session_ctx: SessionContext, dataset: TGTemporalDataset |
                                policy=str(sampling["strategy"]), lr=lr, dropout=float(c.get("dropout", 0.1)),
                                att_dropout=float(c.get("att_dropout", 0.1)), num_head=int(c.get("num_head", 2)),
                                seed=seed, use_graphs=bool(cfg["runtime"].get("cuda_graphs", True)),
-                               grad_sync=grad_sync)
+                               grad_sync=grad_sync, peer=peer)
         optimizer = engine.opt
     else:
         optimizer = torch.optim.Adam(list(model.parameters()) + [p for p in updater.parameters() if p.requires_grad],

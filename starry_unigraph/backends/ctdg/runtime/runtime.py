@@ -260,14 +260,17 @@ class CTDGOnlineRuntime:
     def _engine_step(self, batch: CTDGDataBatch, split: str, train: bool, want_outputs: bool = True) -> dict[str, Any]:
         eng = self.engine
         split = "test" if split == "predict" else split
-        self.memory.wait_pending_syncs()
-        if self.dist_ctx.is_distributed and self.memory.remote_fetch:
-            self.memory.pull_remote(self.dist_ctx, torch.cat([batch.src, batch.dst]))
+        nccl_sync = self.dist_ctx.is_distributed and eng.peer is None  # the NVLink path syncs inside the step
+        if nccl_sync:
+            self.memory.wait_pending_syncs()
+            if self.memory.remote_fetch:
+                self.memory.pull_remote(self.dist_ctx, torch.cat([batch.src, batch.dst]))
         eng.load_batch(batch.src, batch.dst, batch.ts, batch.event_ids)
         if train:
             self.model.train()
         eng.step(split, train)
-        self._submit_syncs(batch)
+        if nccl_sync:
+            self._submit_syncs(batch)
         if not want_outputs:
             return {}
         loss, metrics = eng.read_scalars()

@@ -46,6 +46,21 @@ class FlatParams:
         self.numel = total
         self.params = [p for _, p in params]
 
+    def rebind_grad(self, buffer: torch.Tensor) -> None:
+        """Move the gradient views onto `buffer` (e.g. a symmetric allocation that
+        peer GPUs read); its first ``grad.numel()`` elements are used."""
+        assert buffer.numel() >= self.grad.numel() and buffer.dtype == torch.float32
+        new = buffer.view(-1)[: self.grad.numel()]
+        new.copy_(self.grad)
+        self.grad = new
+        off = 0
+        for name, p in zip(self.names, self.params):
+            n = p.numel()
+            gview = self.grad[off:off + n].view_as(p)
+            p.grad = gview
+            self.grad_views[name] = gview
+            off += n
+
     def zero_grad(self) -> None:
         self.grad.zero_()
 

@@ -64,6 +64,7 @@ class TGNCudaEngine:
         seed: int = 0,
         use_graphs: bool = True,
         grad_sync: Callable[[torch.Tensor], float] | None = None,
+        peer: Any = None,
     ) -> None:
         self.C = cuda_ext()
         self.model = model
@@ -92,8 +93,16 @@ class TGNCudaEngine:
         self.neg_pool = neg_pool.to(dev).long().contiguous()
         # parameters live in one flat buffer (fused Adam, one-buffer gradient sync)
         self.flat = FlatParams([model], dev)
+        self.peer = peer
+        if peer is not None:
+            # gradients in the symmetric buffer: the fused all-reduce reads them from every rank
+            self.flat.rebind_grad(peer.arena["grad"])
         self.opt = FusedAdam(self.flat, lr=lr)
         self._alloc()
+        self._pd = None
+        if peer is not None:
+            self.mem_new = torch.zeros(self.s.rmax, self.s.D, dtype=torch.float32, device=dev)
+            self._pd = peer.descriptor(self.stamp, self.node2root, self.step_ctr, self.mem_new)
         self._graphs: dict[tuple[str, bool], torch.cuda.CUDAGraph] = {}
         self._warm: dict[tuple[str, bool], int] = {}
 
@@ -198,18 +207,20 @@ class TGNCudaEngine:
         cell = u.memory_cell
         C.tgn_memory_update(self.roots, self.n_roots, mem.mailbox, s.K, mem.memory, mem.memory_ts, self.ts_max,
                             g.weight_ih_l0, g.weight_hh_l0, g.bias_ih_l0, g.bias_hh_l0, cell.weight_ih,
-                            cell.weight_hh, cell.bias_ih, cell.bias_hh, self.agg_buf, self.agg_buf2, self.mem_prev)
-        C.tgn_mailbox_write(self.roots, self.n_roots, self.win, self.cnt, self.src_idx, self.dst_idx, self.ev_eid,
-                            self.ev_ts, self.mem_prev, self.efeat, s.E, mem.mailbox, mem.mailbox_ts, mem.next_mail_pos)
+                            cell.weight_hh, cell.bias_ih, cell.bias_hh, self.agg_buf, self.agg_buf2, self.mem_prev, self._pd)
+        if self.peer is None:  # multi-GPU: the mailbox is written to the owners after the step (_peer_sync)
+            C.tgn_mailbox_write(self.roots, self.n_roots, self.win, self.cnt, self.src_idx, self.dst_idx,
+                                self.ev_eid, self.ev_ts, self.mem_prev, self.efeat, s.E, mem.mailbox, mem.mailbox_ts,
+                                mem.next_mail_pos)
         te = c.time_enc.w
         C.tgn_attn_proj(mem.memory, self.roots, self.n_roots, self.nbr, self.nbr_eid, self.nbr_dt, self.nbr_cnt,
                         self.efeat, s.E, te.weight, te.bias, c.w_q.weight, c.w_q.bias, c.w_k.weight, c.w_k.bias,
-                        c.w_v.weight, c.w_v.bias, self.Q, self.KV)
+                        c.w_v.weight, c.w_v.bias, self.Q, self.KV, self._pd)
         C.tgn_attn_fwd(self.Q, self.KV, self.nbr_cnt, self.n_roots, s.H, adrop, self.seed, self.step_ctr, self.att_p,
                        self.agg)
         C.tgn_out_fwd(self.agg, mem.memory, self.roots, self.n_roots, c.w_out.weight, c.w_out.bias,
                       c.layer_norm.weight, c.layer_norm.bias, drop, self.seed, self.step_ctr, self.edge_total,
-                      self.out, self.xsave, self.mean, self.rstd)
+                      self.out, self.xsave, self.mean, self.rstd, self._pd)
         C.tgn_link_proj(self.out, self.n_roots, m.src_fc.weight, m.src_fc.bias, m.dst_fc.weight, m.dst_fc.bias,
                         self.P)
         self.loss.zero_()
@@ -224,6 +235,28 @@ class TGNCudaEngine:
         C.tgn_metrics(self.scores, self.n_ev, self.metrics)
         if train:
             self._backward(gw)
+        if self.peer is not None:
+            self._peer_sync(train)
+
+    def _peer_sync(self, train: bool) -> None:
+        """Multi-GPU end of step over NVLink: gradient all-reduce fused with Adam,
+        memory write-back and mailbox claim/write into the owner ranks' tables,
+        separated by device-side barriers (see starry_unigraph.parallel.ctdg_peer)."""
+        C, s, P = self.C, self.s, self.peer
+        P.barrier(C)
+        if train:
+            o = self.opt
+            C.peer_allreduce_adam(P.tables["grad"], P.world, self.flat.data, o.exp_avg, o.exp_avg_sq, o.step_ctr,
+                                  o.done, float(o.param_groups[0]["lr"]), float(o.betas[0]), float(o.betas[1]),
+                                  float(o.eps), float(o.weight_decay), 1.0 / P.world)
+        C.tgn_peer_writeback(self.roots, self.n_roots, self.mem_new, P.owner, P.tables["memory"],
+                             P.tables["memory_ts"], self.ts_max)
+        C.tgn_peer_mail_claim(self.roots, self.n_roots, self.win, self.ev_eid, self.ev_ts, P.owner, P.tables["claim"])
+        P.barrier(C)
+        C.tgn_peer_mail_write(self.roots, self.n_roots, self.win, self.src_idx, self.dst_idx, self.ev_eid, self.ev_ts,
+                              self.mem_prev, self.efeat, s.E, P.owner, P.tables["claim"], P.tables["mailbox"],
+                              P.tables["mailbox_ts"])
+        P.barrier(C)
 
     def _backward(self, gw: dict[str, torch.Tensor]) -> None:
         C, s = self.C, self.s
@@ -235,7 +268,7 @@ class TGNCudaEngine:
                       self.seed, self.step_ctr, self.edge_total, self.dpre, gw["conv.layer_norm.weight"],
                       gw["conv.layer_norm.bias"])
         C.tgn_out_proj_bwd(self.dpre, self.agg, mem.memory, self.roots, self.n_roots, c.w_out.weight,
-                           gw["conv.w_out.weight"], gw["conv.w_out.bias"], self.dagg)
+                           gw["conv.w_out.weight"], gw["conv.w_out.bias"], self.dagg, self._pd)
         C.tgn_attn_bwd(self.Q, self.KV, self.att_p, self.dagg, self.nbr_cnt, self.n_roots, s.H, self.att_dropout,
                        self.seed, self.step_ctr, self.dKV, self.dQ)
         te = c.time_enc.w
@@ -243,7 +276,9 @@ class TGNCudaEngine:
                             self.efeat, s.E, te.weight, te.bias, c.w_q.weight, c.w_k.weight, c.w_v.weight, self.dQ,
                             self.dKV, gw["conv.w_q.weight"], gw["conv.w_q.bias"], gw["conv.w_k.weight"],
                             gw["conv.w_k.bias"], gw["conv.w_v.weight"], gw["conv.w_v.bias"],
-                            gw["conv.time_enc.w.weight"], gw["conv.time_enc.w.bias"])
+                            gw["conv.time_enc.w.weight"], gw["conv.time_enc.w.bias"], self._pd)
+        if self.peer is not None:
+            return  # all-reduce + Adam run fused in _peer_sync
         scale = 1.0
         if self.grad_sync is not None:
             scale = self.grad_sync(self.flat.grad)
@@ -285,7 +320,11 @@ class TGNCudaEngine:
         """Number of framework kernel launches in one step (memsets excluded)."""
         fwd = 10 + self.s.K  # prep, sample, K+1 GRU GEMMs, mailbox, Q, KV, attention, out+LN, link proj, loss, metrics
         bwd = 11             # link-proj (2), LN, out-proj (2), attention, W_q/W_kv/time-encoder (4), Adam
-        return fwd + (bwd if train else 0)
+        n = fwd + (bwd if train else 0)
+        if self.peer is not None:
+            # - local mailbox; + 3 barriers, write-back, claim, mail write (Adam becomes the fused all-reduce + Adam)
+            n += -1 + 6
+        return n
 
     def reset_graphs(self) -> None:
         self._graphs.clear()

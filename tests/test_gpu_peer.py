@@ -1,0 +1,107 @@
+"""NVLink peer kernels on one GPU, with the ranks' buffers emulated as separate
+local allocations (no kernel waits on another kernel): barrier signalling and
+its bounded timeout, the fused all-reduce + Adam, CTDG memory write-back and
+the mailbox claim/write protocol."""
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+
+def _C():
+    from starry_unigraph.ops import cuda_ext
+
+    return cuda_ext()
+
+
+def _table(*ts):
+    return torch.tensor([t.data_ptr() for t in ts], dtype=torch.int64, device="cuda")
+
+
+def test_barrier_signals_peers_and_times_out_boundedly():
+    from starry_unigraph.ops import check_status
+
+    C = _C()
+    f0 = torch.zeros(32, dtype=torch.int64, device="cuda")  # rank 0's flag array
+    f1 = torch.zeros(32, dtype=torch.int64, device="cuda")  # "rank 1"'s flag array
+    f0[1] = 1  # rank 1 already reached barrier epoch 1
+    epoch = torch.zeros(1, dtype=torch.int64, device="cuda")
+    C.peer_barrier(_table(f0, f1), 0, 2, epoch, 50_000_000)
+    torch.cuda.synchronize()
+    check_status()
+    assert int(f1[0]) == 1 and int(epoch) == 1
+    # epoch 2: nothing ever sets f0[1] = 2 -> the wait gives up and reports
+    C.peer_barrier(_table(f0, f1), 0, 2, epoch, 2_000_000)
+    torch.cuda.synchronize()
+    with pytest.raises(RuntimeError, match="peer flag"):
+        check_status()
+    assert int(f1[0]) == 2
+
+
+def test_allreduce_adam_matches_torch():
+    C = _C()
+    n = 4096 + 4
+    torch.manual_seed(0)
+    g = [torch.randn(n, device="cuda") for _ in range(3)]
+    p = torch.randn(n, device="cuda")
+    m, v = torch.zeros_like(p), torch.zeros_like(p)
+    step = torch.zeros(1, dtype=torch.int64, device="cuda")
+    done = torch.zeros(1, dtype=torch.int32, device="cuda")
+    ref = p.clone().requires_grad_(True)
+    opt = torch.optim.Adam([ref], lr=1e-2)
+    for it in range(3):
+        C.peer_allreduce_adam(_table(*g), 3, p, m, v, step, done, 1e-2, 0.9, 0.999, 1e-8, 0.0, 1.0 / 3)
+        ref.grad = (g[0] + g[1] + g[2]) / 3
+        opt.step()
+        for x in g:
+            x.mul_(0.5)
+    torch.cuda.synchronize()
+    assert int(step) == 3
+    torch.testing.assert_close(p, ref.detach(), rtol=1e-5, atol=1e-6)
+
+
+def test_memory_writeback_and_mail_claims():
+    C = _C()
+    N, D, E = 10, 8, 4
+    SW = 2 * D + E
+    owner = (torch.arange(N, device="cuda") % 2).int()
+    mem = [torch.zeros(N, D, device="cuda") for _ in range(2)]
+    mts = [torch.full((N,), -1.0, device="cuda") for _ in range(2)]
+    mail = [torch.zeros(N, SW, device="cuda") for _ in range(2)]
+    mail_ts = [torch.zeros(N, device="cuda") for _ in range(2)]
+    claim = [torch.zeros(N, dtype=torch.int64, device="cuda") for _ in range(2)]
+    efeat = torch.randn(50, E, device="cuda")
+
+    def rank_step(roots, ts_max, ev, fill):
+        R = len(roots)
+        r = torch.tensor(roots, dtype=torch.int64, device="cuda")
+        nr = torch.tensor([R], dtype=torch.int32, device="cuda")
+        mem_new = torch.full((R, D), fill, device="cuda")
+        C.tgn_peer_writeback(r, nr, mem_new, owner, _table(*mem), _table(*mts),
+                             torch.tensor([ts_max], device="cuda"))
+        # one event per root: root i is the source of event i, its destination is root (i + 1) % R
+        win = torch.cat([torch.arange(R), torch.full((R,), -1)]).int().cuda()
+        src_idx = torch.arange(R, dtype=torch.int32, device="cuda")
+        dst_idx = ((torch.arange(R) + 1) % R).int().cuda()
+        eid = torch.tensor([e for e, _ in ev], dtype=torch.int64, device="cuda")
+        ets = torch.tensor([t for _, t in ev], dtype=torch.float32, device="cuda")
+        mem_prev = torch.full((R, D), fill, device="cuda")
+        return dict(r=r, nr=nr, win=win, src_idx=src_idx, dst_idx=dst_idx, eid=eid, ets=ets, mem_prev=mem_prev)
+
+    a = rank_step([0, 1, 2], 5.0, [(10, 4.0), (11, 5.0), (12, 5.0)], 1.0)
+    b = rank_step([1, 3], 7.0, [(20, 3.0), (21, 7.0)], 2.0)
+    for x in (a, b):
+        C.tgn_peer_mail_claim(x["r"], x["nr"], x["win"], x["eid"], x["ets"], owner, _table(*claim))
+    for x in (a, b):
+        C.tgn_peer_mail_write(x["r"], x["nr"], x["win"], x["src_idx"], x["dst_idx"], x["eid"], x["ets"],
+                              x["mem_prev"], efeat, E, owner, _table(*claim), _table(*mail), _table(*mail_ts))
+    torch.cuda.synchronize()
+    # memory rows land on the owner; memory_ts is the max over writers
+    assert torch.equal(mem[0][0], torch.ones(D, device="cuda")) and torch.equal(mem[0][2], torch.ones(D, device="cuda"))
+    assert float(mts[1][1]) == 7.0 and float(mts[1][3]) == 7.0 and float(mts[0][0]) == 5.0
+    assert float(mem[1][3][0]) == 2.0
+    # node 1: rank a proposes (ts 5, eid 11), rank b (ts 3, eid 20) -> a's mail wins
+    assert float(mail_ts[1][1]) == 5.0 and float(mail[1][1][0]) == 1.0
+    assert torch.equal(mail[1][1][2 * D:], efeat[11])
+    assert float(mail_ts[1][3]) == 7.0 and torch.equal(mail[1][3][2 * D:], efeat[21])
+    assert float(mail_ts[0][2]) == 5.0 and torch.equal(mail[0][2][2 * D:], efeat[12])
