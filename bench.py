@@ -41,6 +41,9 @@ def _args():
     p.add_argument("--impl", default="ours", choices=["ours", "reference"])
     p.add_argument("--events", type=int, default=7833140, help="stream length (config: 7,833,140)")
     p.add_argument("--batch", type=int, default=600, help="events per rank per step")
+    p.add_argument("--workload", default="tgn", choices=["tgn", "mpnn_lstm"],
+                   help="tgn: TGN train events/sec (default); mpnn_lstm: MPNN-LSTM train snapshots/sec")
+    p.add_argument("--snapshots", type=int, default=128, help="mpnn_lstm: snapshots generated (config: 128)")
     return p.parse_args()
 
 
@@ -123,10 +126,105 @@ def _reference_arm(args):
     return 0
 
 
+def _mpnn_main(args):
+    """MPNN-LSTM: 200,000 nodes, 128 Chung-Lu snapshots of ~2M edges with 30% churn,
+    64-dim features, window 8, two MPNN layers + two LSTMs of hidden 64, MSE. Nodes are partitioned over the
+    ranks (strong scaling: the same graph on every N). One step = one training window ending at the next
+    snapshot, so snapshots/sec = steps/sec."""
+    sys.path.insert(0, str(ROOT))
+    import torch
+    import torch.distributed as dist
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local_rank)
+    from starry_unigraph import SchedulerSession
+    from starry_unigraph.backends.dtdg.runtime.training import run_flare_train_step
+    from starry_unigraph.ops import check_status
+
+    def cfg(resident):
+        return {
+            "model": {"name": "mpnn_lstm", "family": "mpnn_lstm", "task": "snapshot_node_regression",
+                      "hidden_dim": 64, "window": {"size": 8}},
+            "data": {"root": "./data", "name": "mpnn_large", "format": "synthetic",
+                     "synthetic": {"preset": "mpnn_lstm_large", "num_snapshots": args.snapshots}},
+            "train": {"epochs": 1, "snaps": args.snapshots, "lr": 1e-3},
+            "runtime": {"device": "cuda"},
+            "dtdg": {"window_from_size": True, "chunk_order": None, "chunk_decay": None, "resident": resident},
+            "dist": {"backend": "nccl", "timeout_s": 600},
+        }
+
+    session = SchedulerSession.from_config(cfg(True))
+    session.ctx.artifact_root = Path(os.environ.get("TMPDIR", "/tmp")) / f"su_mpnn_w{world}_r{rank}"
+    if world > 1:
+        from starry_unigraph.distributed import initialize_distributed
+
+        initialize_distributed(session.ctx.dist)
+    t_prep = time.perf_counter()
+    session.prepare_data()
+    session.build_runtime()
+    prep_s = time.perf_counter() - t_prep
+    core, rt = session.snapshot_core, session.runtime
+    need = args.warmup + args.steps
+    blob_list = list(core.iter_train(max_steps=need))
+    if len(blob_list) < need:  # the train split holds ~70% of the snapshots
+        args.steps = len(blob_list) - args.warmup
+        if args.steps <= 0:
+            raise SystemExit(f"train split has only {len(blob_list)} windows")
+    blobs = iter(blob_list)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    for _ in range(args.warmup):
+        run_flare_train_step(rt, next(blobs), {"meta": {}}, need_host=False)
+    torch.cuda.synchronize()
+    check_status()
+    timed = [next(blobs) for _ in range(args.steps)]
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier()
+    torch.cuda.synchronize()
+    with ClockSampler(local_rank) as clocks:
+        start.record()
+        for b in timed:
+            run_flare_train_step(rt, b, {"meta": {}}, need_host=False)
+        end.record()
+        torch.cuda.synchronize()
+    barrier()
+    dev_ms = start.elapsed_time(end)
+    check_status()
+    stats = torch.tensor([dev_ms], dtype=torch.float64, device="cuda")
+    if world > 1:
+        dist.all_reduce(stats, op=dist.ReduceOp.MAX)
+    dev_ms = float(stats[0])
+    value = args.steps / (dev_ms / 1000.0)
+    if rank == 0:
+        print(json.dumps({
+            "metric": "MPNN-LSTM train snapshots/sec", "value": value, "unit": "snapshots/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": dev_ms / args.steps,
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "fp32+bf16-tensor-core",
+            "data": "synthetic (random-init weights)",
+            "config": {"model": "MPNN-LSTM (2 MPNN + 2 LSTM, hidden 64), flare_native", "global_batch": None,
+                       "seq_len": 8, "parallelism": f"graph-partition{world}", "nodes": 200000,
+                       "snapshots": args.snapshots, "edges_per_snapshot": 2000000, "window": 8,
+                       "l2": "per-snapshot working set (2M edges CSR ~24 MB + 200k x 64 fp32 features 51 MB) x 8 "
+                             "window graphs > 126 MB L2", "baseline_metric": METRIC},
+            "clocks": clocks.summary(), "prep_s": prep_s}), flush=True)
+    if world > 1:
+        from starry_unigraph.distributed import finalize_distributed
+
+        finalize_distributed(session.ctx.dist)
+    return 0
+
+
 def main():
     args = _args()
     if args.impl == "reference":
         return _reference_arm(args)
+    if args.workload == "mpnn_lstm":
+        return _mpnn_main(args)
     sys.path.insert(0, str(ROOT))
     import torch
     import torch.distributed as dist

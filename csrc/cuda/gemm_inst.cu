@@ -3,8 +3,10 @@
 // (status word, SM count). The N tile is chosen from the output width.
 #include <algorithm>
 #include <cstdio>
+#include <cstdlib>
 
 #include "kernels.h"
+#include "tc_gemm_packed.cuh"
 
 namespace su {
 
@@ -94,11 +96,95 @@ void gemm_with_status(const MNView<SegSource>& a, const MNView<SegSource>& b, co
   dispatch_status(a, b, e, sh, st, status);
 }
 
+// ---------------------------------------------------------------------------
+// packed-operand path: pack A, pack B (full-occupancy grids), then the
+// bulk-copy-fed tcgen05 GEMM. The packed images live in a per-device
+// workspace that grows outside stream capture only; a call that would need to
+// grow it during capture runs the fused-producer kernel instead.
+// ---------------------------------------------------------------------------
+static uint8_t* g_ws[64] = {nullptr};
+static size_t g_ws_bytes[64] = {0};
+
+static uint8_t* workspace(int device, size_t bytes, cudaStream_t st) {
+  if (bytes <= g_ws_bytes[device]) return g_ws[device];
+  cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+  cudaStreamIsCapturing(st, &cs);
+  if (cs != cudaStreamCaptureStatusNone) return nullptr;
+  if (g_ws[device] != nullptr) {
+    cudaDeviceSynchronize();  // earlier kernels may still read the old image
+    cudaFree(g_ws[device]);
+    g_ws[device] = nullptr;
+    g_ws_bytes[device] = 0;
+  }
+  const size_t want = bytes + bytes / 2;
+  void* p = nullptr;
+  if (cudaMalloc(&p, want) != cudaSuccess) {
+    cudaGetLastError();
+    return nullptr;
+  }
+  g_ws[device] = static_cast<uint8_t*>(p);
+  g_ws_bytes[device] = want;
+  return g_ws[device];
+}
+
+static bool packed_disabled() {
+  static int v = -1;
+  if (v < 0) {
+    const char* e = getenv("SU_GEMM_FUSED_PRODUCERS");
+    v = (e != nullptr && e[0] == '1') ? 1 : 0;
+  }
+  return v == 1;
+}
+
+template <int ROWS, class Src>
+static void launch_pack(const Src& src, uint8_t* out, int mn, const int* mn_dev, int k, int device, cudaStream_t st) {
+  const int tiles = (mn + ROWS - 1) / ROWS;
+  const int nchunks = (k + kBK - 1) / kBK;
+  const int64_t total = static_cast<int64_t>(tiles) * nchunks * ROWS * 8;
+  if (total <= 0) return;
+  const int64_t want = (total + 255) / 256;
+  const int blocks = static_cast<int>(std::min<int64_t>(want, static_cast<int64_t>(num_sms(device)) * 16));
+  pack_kernel<ROWS, Src><<<blocks, 256, 0, st>>>(src, out, tiles, nchunks, mn, mn_dev, mn);
+}
+
+template <int BN, int NSUB, class A, class B, class E>
+static bool launch_packed(const A& a, const B& b, const E& e, const GemmShape& sh, cudaStream_t st) {
+  constexpr int B_ROWS = BN * NSUB;
+  constexpr int smem = packed_smem_bytes<BN, NSUB>();
+  int device = 0;
+  cudaGetDevice(&device);
+  const size_t abytes = packed_bytes(sh.M, sh.K, kBM);
+  const size_t bbytes = packed_bytes(sh.N, sh.K, B_ROWS);
+  if (abytes == 0 || bbytes == 0) return true;
+  uint8_t* ws = workspace(device, abytes + bbytes, st);
+  if (ws == nullptr) return false;
+  auto kern = tc_gemm_packed_kernel<BN, NSUB, A::kMN, B::kMN, E>;
+  static unsigned long long configured = 0ull;
+  if (!(configured & (1ull << device))) {
+    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    configured |= (1ull << device);
+  }
+  launch_pack<kBM>(a, ws, sh.M, sh.m_dev, sh.K, device, st);
+  launch_pack<B_ROWS>(b, ws + abytes, sh.N, nullptr, sh.K, device, st);
+  const int tiles_m = (sh.M + kBM - 1) / kBM;
+  const int tiles_n = (sh.N + B_ROWS - 1) / B_ROWS;
+  const int total = tiles_m * tiles_n * std::max(1, sh.ksplit);
+  const int grid = std::min(total, num_sms(device));
+  kern<<<grid, kPackedThreads, smem, st>>>(ws, ws + abytes, e, sh, device_status_ptr(device));
+  return true;
+}
+
+template <int BN, int NSUB, class A, class B, class E>
+static void launch_any(const A& a, const B& b, const E& e, const GemmShape& sh, cudaStream_t st) {
+  if (!packed_disabled() && launch_packed<BN, NSUB>(a, b, e, sh, st)) return;
+  launch_cfg<BN, NSUB>(a, b, e, sh, st);
+}
+
 template <class A, class B, class E>
 static void dispatch(const A& a, const B& b, const E& e, const GemmShape& sh, cudaStream_t st) {
-  if (sh.N <= 128) launch_cfg<128, 1>(a, b, e, sh, st);
-  else if (sh.N <= 256) launch_cfg<256, 1>(a, b, e, sh, st);
-  else launch_cfg<256, 2>(a, b, e, sh, st);
+  if (sh.N <= 128) launch_any<128, 1>(a, b, e, sh, st);
+  else if (sh.N <= 256) launch_any<256, 1>(a, b, e, sh, st);
+  else launch_any<256, 2>(a, b, e, sh, st);
 }
 
 void gemm(const SegSource& a, const WeightSource& b, const EpiLinear& e, const GemmShape& sh, cudaStream_t st) {
@@ -113,15 +199,15 @@ void gemm(const MNView<SegSource>& a, const MNView<SegSource>& b, const EpiWeigh
   dispatch(a, b, e, sh, st);
 }
 void gemm(const SegSource& a, const WeightSource& b, const EpiGRU& e, const GemmShape& sh, cudaStream_t st) {
-  launch_cfg<128, 1>(a, b, e, sh, st);  // one tile = four gates x 32 hidden units (gate-grouped rows)
+  launch_any<128, 1>(a, b, e, sh, st);  // one tile = four gates x 32 hidden units (gate-grouped rows)
 }
 void gemm(const SegSource& a, const WeightSource& b, const EpiOutLN& e, const GemmShape& sh, cudaStream_t st) {
-  if (sh.N <= 128) launch_cfg<128, 1>(a, b, e, sh, st);
-  else launch_cfg<256, 1>(a, b, e, sh, st);
+  if (sh.N <= 128) launch_any<128, 1>(a, b, e, sh, st);
+  else launch_any<256, 1>(a, b, e, sh, st);
 }
 
 void gemm(const SegSource& a, const WeightSource& b, const EpiLSTM& e, const GemmShape& sh, cudaStream_t st) {
-  launch_cfg<128, 1>(a, b, e, sh, st);  // one tile = four gates x 32 hidden units (gate-grouped rows)
+  launch_any<128, 1>(a, b, e, sh, st);  // one tile = four gates x 32 hidden units (gate-grouped rows)
 }
 
 }  // namespace su

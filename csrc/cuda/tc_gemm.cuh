@@ -53,7 +53,8 @@ __device__ __forceinline__ float reduced_phase(float w, float t, float b) {
   if (fabsf(x) < 8192.f) return x;
   const double xd = fma(static_cast<double>(w), static_cast<double>(t), static_cast<double>(b));
   const double two_pi = 6.283185307179586476925286766559;
-  return static_cast<float>(xd - two_pi * rint(xd / two_pi));
+  const double inv_two_pi = 0.15915494309189533576888376337251;
+  return static_cast<float>(fma(-two_pi, rint(xd * inv_two_pi), xd));
 }
 __device__ __forceinline__ float cos_phase(float w, float t, float b) { return cosf(reduced_phase(w, t, b)); }
 __device__ __forceinline__ float sin_phase(float w, float t, float b) { return sinf(reduced_phase(w, t, b)); }

@@ -1,0 +1,269 @@
+// tcgen05 GEMM over pre-packed bf16 operands.
+//
+// The operands of the framework's GEMMs are gathers, concatenations and
+// on-the-fly time encodings of fp32 tensors (SegSource / WeightSource, see
+// tc_gemm.cuh). Building those tiles inside the GEMM leaves 4 producer warps
+// per SM latency-bound on dependent gathers. Here the work is split:
+//
+//   pack_kernel : a full-occupancy grid builds each operand once, as bf16, in
+//                 the exact shared-memory tile image the MMA reads (no-swizzle
+//                 core matrices; K-major or MN-major), block (tile, k-chunk)
+//                 after block, zero-padded to whole tiles.
+//   tc_gemm_packed_kernel : warp-specialised tcgen05 GEMM. One thread streams
+//                 the blocks into a multi-stage smem ring with bulk async
+//                 copies (cp.async.bulk, completion on an mbarrier, no
+//                 multicast), one thread issues tcgen05.mma into a TMEM
+//                 accumulator, four warps run the fused epilogue.
+//
+// Every wait is bounded; on expiry the kernel records a status code, waits
+// (bounded) for its copies in flight, frees TMEM and returns.
+#pragma once
+
+#include "tc_gemm.cuh"
+
+namespace su {
+
+constexpr int kPackedThreads = 192;  // warps 0-3 epilogue, warp 4 copy producer, warp 5 MMA (+ TMEM owner)
+
+template <int BN, int NSUB>
+constexpr int packed_stage_bytes() {
+  return kBM * kBK * 2 + BN * NSUB * kBK * 2;
+}
+template <int BN, int NSUB>
+constexpr int packed_stages() {
+  return (200 * 1024) / packed_stage_bytes<BN, NSUB>() >= 6 ? 6 : (200 * 1024) / packed_stage_bytes<BN, NSUB>();
+}
+template <int BN, int NSUB>
+constexpr int packed_smem_bytes() {
+  return packed_stages<BN, NSUB>() * packed_stage_bytes<BN, NSUB>() + 1024 /*barriers*/ + 1024 /*align*/;
+}
+
+// bytes of a packed operand with `mn` rows (MN extent) and K extent `k`
+inline size_t packed_bytes(int mn, int k, int rows_per_tile) {
+  const size_t tiles = (static_cast<size_t>(mn) + rows_per_tile - 1) / rows_per_tile;
+  const size_t chunks = (static_cast<size_t>(k) + kBK - 1) / kBK;
+  return tiles * chunks * static_cast<size_t>(rows_per_tile) * kBK * 2;
+}
+
+#ifdef __CUDACC__
+
+// One thread = one 16-byte vector (8 bf16) of the packed image.
+// Vector index -> (tile t, chunk kc, 8-row group g, k-vector kv, r8):
+//   K-major : row = t*ROWS + g*8 + r8, columns [kc*64 + kv*8, +8)
+//   MN-major: MN group t*ROWS/8 + g (8 consecutive MN indices), k = kc*64 + kv*8 + r8
+// both land at block(t, kc) + g*1024 + kv*128 + r8*16.
+template <int ROWS, class Src>
+__global__ void __launch_bounds__(256) pack_kernel(const __grid_constant__ Src src, uint8_t* __restrict__ out,
+                                                   int tiles, int nchunks, int limit, const int* limit_dev,
+                                                   int nrows) {
+  int lim = limit;
+  if (limit_dev != nullptr) lim = min(lim, *limit_dev);
+  (void)nrows;
+  const int64_t total = static_cast<int64_t>(tiles) * nchunks * (ROWS / 8) * 64;
+  const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+  for (int64_t idx = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; idx < total; idx += stride) {
+    const int r8 = static_cast<int>(idx & 7);
+    const int kv = static_cast<int>((idx >> 3) & 7);
+    int64_t rest = idx >> 6;
+    const int g = static_cast<int>(rest % (ROWS / 8));
+    rest /= (ROWS / 8);
+    const int kc = static_cast<int>(rest % nchunks);
+    const int t = static_cast<int>(rest / nchunks);
+    if (t * ROWS >= lim) continue;  // tiles past the (device-side) row count are never read
+    float f[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) f[i] = 0.f;
+    if constexpr (!Src::kMN) {
+      const int row = t * ROWS + g * 8 + r8;
+      if (row < lim) src.load8f(row, kc * (kBK / 8) + kv, lim, f);
+    } else {
+      const int mng = t * (ROWS / 8) + g;
+      if (mng * 8 < lim) src.load8f(mng, kc * kBK + kv * 8 + r8, lim, f);
+    }
+    *reinterpret_cast<uint4*>(out + (static_cast<int64_t>(t) * nchunks + kc) * (ROWS * 128) + g * 1024 + kv * 128 +
+                              r8 * 16) = pack_bf16x8(f);
+  }
+}
+
+template <int BN, int NSUB, bool AMN, bool BMN, class Epi>
+__global__ void __launch_bounds__(kPackedThreads, 1)
+    tc_gemm_packed_kernel(const uint8_t* __restrict__ pa, const uint8_t* __restrict__ pb,
+                          const __grid_constant__ Epi epi, const GemmShape shape, int* status) {
+  static_assert(BN % 16 == 0 && BN >= 16 && BN <= 256, "UMMA N for M=128 must be a multiple of 16 in [16, 256]");
+  static_assert(NSUB >= 1 && BN * NSUB <= 512, "accumulator exceeds TMEM");
+  constexpr int A_BYTES = kBM * kBK * 2;
+  constexpr int B_ROWS = BN * NSUB;
+  constexpr int B_BYTES = B_ROWS * kBK * 2;
+  constexpr int STAGES = packed_stages<BN, NSUB>();
+  constexpr uint32_t TMEM_COLS = tmem_cols_for(B_ROWS);
+  constexpr uint32_t IDESC =
+      umma_idesc_bf16_f32(kBM, BN) | (AMN ? (1u << 15) : 0u) | (BMN ? (1u << 16) : 0u);
+
+  extern __shared__ uint8_t smem_dyn[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_dyn) + 1023) & ~uintptr_t(1023));
+  uint8_t* smemA = smem;
+  uint8_t* smemB = smem + STAGES * A_BYTES;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smemB + STAGES * B_BYTES);
+  uint64_t* full = bars;                 // [STAGES] copies landed (1 arrival + tx bytes)
+  uint64_t* empty = bars + STAGES;       // [STAGES] MMA done with the stage
+  uint64_t* acc_full = bars + 2 * STAGES;
+  uint64_t* acc_empty = acc_full + 1;
+  uint64_t* drain = acc_full + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    mbar_init(acc_full, 1);
+    mbar_init(acc_empty, 128);
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 5) {
+    tmem_alloc(tmem_slot, TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  int M = shape.M;
+  if (shape.m_dev != nullptr) M = min(M, *shape.m_dev);
+  const int tiles_m = (M + kBM - 1) / kBM;
+  const int tiles_n = (shape.N + B_ROWS - 1) / B_ROWS;
+  const int nchunks = (shape.K + kBK - 1) / kBK;
+  const int ksplit = max(1, shape.ksplit);
+  const int cps = (nchunks + ksplit - 1) / ksplit;
+  const int total = tiles_m * tiles_n * ksplit;
+
+  if (warp < 4) {
+    // ------------------------------ epilogue ------------------------------
+    int tl = 0;  // tiles with work (the MMA warp counts the same ones)
+    for (int tile = blockIdx.x; tile < total; tile += gridDim.x) {
+      const int mn = tile / ksplit;
+      const int nt = mn % tiles_n;
+      const int mt = mn / tiles_n;
+      const int ks = tile % ksplit;
+      if (ks * cps >= nchunks) continue;  // empty split: nothing was accumulated
+      if (!mbar_wait_bounded(acc_full, tl & 1) || *abort_flag) {
+        record_status(status, kTimeoutAccum);
+        *abort_flag = 1;
+        break;
+      }
+      tc_fence_after();
+      const int row = mt * kBM + warp * 32 + lane;
+      const uint32_t taddr = tmem_base + (static_cast<uint32_t>(warp * 32) << 16);
+      epi(row, row < M, nt * B_ROWS, taddr, B_ROWS);
+      tc_fence_before();
+      mbar_arrive(acc_empty);
+      ++tl;
+    }
+  } else if (warp == 4) {
+    // --------------------------- copy producer ----------------------------
+    if (lane == 0) {
+      int cg = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; tile < total && ok; tile += gridDim.x) {
+        const int ks = tile % ksplit;
+        const int mn = tile / ksplit;
+        const int nt = mn % tiles_n;
+        const int mt = mn / tiles_n;
+        const int kc0 = ks * cps;
+        const int kc1 = min(nchunks, kc0 + cps);
+        for (int kc = kc0; kc < kc1; ++kc, ++cg) {
+          const int s = cg % STAGES;
+          const uint32_t ph = (cg / STAGES) & 1;
+          if (!mbar_wait_bounded(&empty[s], ph ^ 1) || *abort_flag) {
+            record_status(status, kTimeoutEmpty);
+            *abort_flag = 1;
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(&full[s], A_BYTES + B_BYTES);
+          bulk_g2s(smemA + s * A_BYTES, pa + (static_cast<size_t>(mt) * nchunks + kc) * A_BYTES, A_BYTES, &full[s]);
+          bulk_g2s(smemB + s * B_BYTES, pb + (static_cast<size_t>(nt) * nchunks + kc) * B_BYTES, B_BYTES, &full[s]);
+        }
+      }
+      // copies still in flight complete on their full barriers: wait for the
+      // last STAGES issued (bounded) so none targets smem of an exited CTA
+      for (int c = max(0, cg - STAGES); c < cg; ++c) {
+        if (!mbar_wait_bounded(&full[c % STAGES], (c / STAGES) & 1)) {
+          record_status(status, kTimeoutFull);
+          break;
+        }
+      }
+    }
+    __syncwarp();
+  } else {
+    // ------------------------------ MMA issuer ------------------------------
+    if (lane == 0) {
+      int cg = 0;
+      int tl = 0;
+      bool ok = true;
+      bool issued = false;
+      for (int tile = blockIdx.x; tile < total && ok; tile += gridDim.x) {
+        const int ks = tile % ksplit;
+        const int kc0 = ks * cps;
+        const int kc1 = min(nchunks, kc0 + cps);
+        if (kc0 >= kc1) continue;
+        if (!mbar_wait_bounded(acc_empty, (tl & 1) ^ 1) || *abort_flag) {
+          record_status(status, kTimeoutTmemFree);
+          *abort_flag = 1;
+          break;
+        }
+        tc_fence_after();
+        for (int kc = kc0; kc < kc1; ++kc, ++cg) {
+          const int s = cg % STAGES;
+          const uint32_t ph = (cg / STAGES) & 1;
+          if (!mbar_wait_bounded(&full[s], ph) || *abort_flag) {
+            record_status(status, kTimeoutFull);
+            *abort_flag = 1;
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a_base = smem_u32(smemA + s * A_BYTES);
+          const uint32_t b_base = smem_u32(smemB + s * B_BYTES);
+          const int ksteps = min(kBK / 16, (shape.K - kc * kBK + 15) / 16);
+          for (int kk = 0; kk < ksteps; ++kk) {
+            const uint64_t adesc = umma_desc_kmajor_noswizzle(a_base + kk * 256, 128, 1024);
+#pragma unroll
+            for (int sub = 0; sub < NSUB; ++sub) {
+              const uint64_t bdesc =
+                  umma_desc_kmajor_noswizzle(b_base + sub * (BN / 8) * 1024 + kk * 256, 128, 1024);
+              umma_bf16(tmem_base + sub * BN, adesc, bdesc, IDESC, (kc > kc0 || kk > 0) ? 1u : 0u);
+            }
+            issued = true;
+          }
+          umma_commit(&empty[s]);
+        }
+        if (!ok) break;
+        umma_commit(acc_full);
+        ++tl;
+      }
+      if (issued) {  // no tensor-core work may be in flight when TMEM is released
+        umma_commit(drain);
+        if (!mbar_wait_bounded(drain, 0)) record_status(status, kTimeoutAccum);
+      }
+    }
+    __syncwarp();
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 5) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, TMEM_COLS);
+  }
+}
+
+#endif  // __CUDACC__
+
+}  // namespace su

@@ -245,6 +245,17 @@ __global__ void tgn_mailbox_kernel(const int64_t* __restrict__ roots, const int*
 // KV: [rmax*k, 2*Do] (K cols [0,Do), V cols [Do,2Do)); Q: [rmax, Do]
 // ---------------------------------------------------------------------------
 
+// Value of head h's per-edge quantity held by lane j. __shfl_sync evaluates its
+// operand on the SOURCE lane, so every head is shuffled and the destination
+// lane picks its own head afterwards.
+__device__ __forceinline__ float shfl_head(const float (&v)[4], int H, int h, int j) {
+  const float v0 = __shfl_sync(0xffffffffu, v[0], j);
+  const float v1 = H > 1 ? __shfl_sync(0xffffffffu, v[1], j) : 0.f;
+  const float v2 = H > 2 ? __shfl_sync(0xffffffffu, v[2], j) : 0.f;
+  const float v3 = H > 3 ? __shfl_sync(0xffffffffu, v[3], j) : 0.f;
+  return h == 0 ? v0 : h == 1 ? v1 : h == 2 ? v2 : v3;
+}
+
 __global__ void tgn_attn_fwd_kernel(const float* __restrict__ Q, const float* __restrict__ KV,
                                     const int* __restrict__ cnt, const int* __restrict__ n_roots, int rmax, int k,
                                     int Do, int H, float att_drop, uint64_t seed, const int64_t* __restrict__ step_ctr,
@@ -283,15 +294,18 @@ __global__ void tgn_attn_fwd_kernel(const float* __restrict__ Q, const float* __
       a = dropout_keep(dseed, (uint64_t)(e * H + h), kStreamAttDrop, att_drop) ? p / (1.f - att_drop) : 0.f;
     att[h] = on ? a : 0.f;
   }
-  // aggregate: lanes over feature columns
-  for (int d = lane; d < Do; d += 32) {
-    const int h = d / dh;
+  // aggregate: lanes over feature columns (every lane runs every iteration so
+  // the shuffles see a full warp; columns past Do are masked)
+  for (int d0 = 0; d0 < Do; d0 += 32) {
+    const int d = d0 + lane;
+    const bool col = d < Do;
+    const int h = col ? d / dh : 0;
     float acc = 0.f;
     for (int j = 0; j < nv; ++j) {
-      const float a = __shfl_sync(0xffffffffu, att[h < 4 ? h : 0], j);
-      acc = fmaf(a, KV[((int64_t)r * k + j) * (2 * Do) + Do + d], acc);
+      const float a = shfl_head(att, H, h, j);
+      if (col) acc = fmaf(a, KV[((int64_t)r * k + j) * (2 * Do) + Do + d], acc);
     }
-    ag[d] = acc;
+    if (col) ag[d] = acc;
   }
 }
 
@@ -345,18 +359,21 @@ __global__ void tgn_attn_bwd_kernel(const float* __restrict__ Q, const float* __
     const float ds = on ? p * (dp - dot) : 0.f;  // softmax backward
     dsc[h] = on ? ds * (s > 0.f ? 1.f : 0.2f) : 0.f;  // LeakyReLU backward
   }
-  for (int d = lane; d < Do; d += 32) {
-    const int h = d / dh;
+  for (int d0 = 0; d0 < Do; d0 += 32) {
+    const int d = d0 + lane;
+    const bool col = d < Do;
+    const int h = col ? d / dh : 0;
     float dqa = 0.f;
     for (int j = 0; j < nv; ++j) {
-      const float a = __shfl_sync(0xffffffffu, att[h < 4 ? h : 0], j);
-      const float sj = __shfl_sync(0xffffffffu, dsc[h < 4 ? h : 0], j);
+      const float a = shfl_head(att, H, h, j);
+      const float sj = shfl_head(dsc, H, h, j);
+      if (!col) continue;
       float* row = dKV + ((int64_t)r * k + j) * (2 * Do);
       row[Do + d] = a * g[d];                               // dV
       row[d] = sj * q[d];                                   // dK
       dqa = fmaf(sj, KV[((int64_t)r * k + j) * (2 * Do) + d], dqa);  // dQ
     }
-    dq[d] = dqa;
+    if (col) dq[d] = dqa;
   }
 }
 

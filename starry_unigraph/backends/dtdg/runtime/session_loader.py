@@ -141,8 +141,9 @@ class FlareRuntimeLoader:
         part = data.node_data["partition_id"][0].item() if "partition_id" in data.node_data else None
         pid = int(part[0]) if part is not None and part.numel() else rank
         plan = SnapshotRoutePlan(str(config["graph"]["route"]), str(config["runtime"]["cache"]))
-        gl = STGraphLoader.from_partition_data(data, device, chunk_index, rank, world_size)
         d = config.get("dtdg", {})
+        gl = STGraphLoader.from_partition_data(data, device, chunk_index, rank, world_size,
+                                               resident=bool(d.get("resident", True)))
         return cls(partition_id=pid, route_plan=plan,
                    window_state=DTDGWindowState(int(config["model"]["window"]["size"])), partition_data=gl.data,
                    graph_loader=gl, device=device, rank=rank, world_size=world_size, chunk_index=chunk_index,

@@ -78,6 +78,8 @@ def test_fused_forward_and_memory_match_cpu_oracle(tmp_path, slots):
         res_c = rc.train_step(batch)
         lg, lc = res_g["loss"], res_c["loss"]
         assert abs(lg - lc) <= 1e-2 * max(1.0, abs(lc)), (i, lg, lc)
+        pg, pc = torch.tensor(res_g["predictions"]), torch.tensor(res_c["predictions"])
+        assert float((pg - pc).abs().max()) < 1e-2, (i, float((pg - pc).abs().max()))
     from starry_unigraph.ops import check_status
 
     check_status()
@@ -127,6 +129,11 @@ def test_fused_gradients_match_autograd(tmp_path):
     errs = {}
     for (n, pg), pc in zip(rg.model.named_parameters(), rc.model.parameters()):
         a, b = pg.grad.detach().cpu(), pc.grad.detach()
+        if n == "conv.w_k.bias":
+            # exact gradient is zero: the softmax over a root's edges is invariant to the shift q . b_k,
+            # which is the same for every edge; both sides hold rounding residue only
+            errs[n] = float(a.norm() / (dict(rg.model.named_parameters())["conv.w_k.weight"].grad.norm().cpu()))
+            continue
         if n == "conv.time_enc.w.weight":
             # high-frequency encodings: fp32 w * dt has an ulp of ~0.25 rad at dt ~ 1e6, so cos/sin there
             # differ between any two implementations; compare the low-frequency dims
@@ -134,7 +141,8 @@ def test_fused_gradients_match_autograd(tmp_path):
             errs[n] = float((a.view(-1)[ok] - b.view(-1)[ok]).norm() / scale[ok].norm().float())
         else:
             errs[n] = float((a - b).norm() / (b.norm() + 1e-8))
-    bad = {n: e for n, e in errs.items() if e > (2e-2 if n == "conv.time_enc.w.weight" else 5e-2)}
+    tol = {"conv.time_enc.w.weight": 2e-2, "conv.w_k.bias": 0.2}
+    bad = {n: e for n, e in errs.items() if e > tol.get(n, 5e-2)}
     assert not bad, errs
 
 
