@@ -216,6 +216,20 @@ __device__ __forceinline__ bool dropout_keep(uint64_t seed, uint64_t idx, uint32
   return Philox::uniform(w) >= p;
 }
 
+// Keep decisions of elements idx4 .. idx4+3 (idx4 a multiple of 4): one Philox
+// call, the same decisions dropout_keep gives element by element.
+__device__ __forceinline__ void dropout_keep4(uint64_t seed, uint64_t idx4, uint32_t stream, float p, bool (&k)[4]) {
+  if (p <= 0.f) {
+    k[0] = k[1] = k[2] = k[3] = true;
+    return;
+  }
+  const uint4 r = Philox::gen(seed, idx4 >> 2, stream);
+  k[0] = Philox::uniform(r.x) >= p;
+  k[1] = Philox::uniform(r.y) >= p;
+  k[2] = Philox::uniform(r.z) >= p;
+  k[3] = Philox::uniform(r.w) >= p;
+}
+
 __device__ __forceinline__ float warp_sum(float v) {
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);

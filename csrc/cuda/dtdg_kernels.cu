@@ -1,67 +1,107 @@
 // DTDG (Flare) kernels for sm_100a:
 //   * CSR SpMM for GCN aggregation: out[d] = sum_{e in row d} val[e] * x[col[e]]
-//     (warp per destination row, 16-byte vectors over features). The backward
-//     pass runs the same kernel over the source-sorted (transposed) CSR, so no
-//     atomics are needed and results are deterministic.
+//     (warps over fixed-size edge chunks, vectors over features). The backward
+//     pass runs the same kernel over the source-sorted (transposed) CSR. Rows
+//     inside one chunk are written directly; rows longer than a chunk (hubs)
+//     are combined with atomic adds.
 //   * LSTM cell backward (elementwise over the saved gates).
 #include "kernels.h"
 
 namespace su {
 
+// Work-balanced CSR SpMM. Power-law snapshots have hub rows with ~10^5 edges,
+// so a warp per row leaves one warp walking a hub while the rest of the GPU
+// idles. Instead every warp takes a fixed chunk of kChunk consecutive edges of
+// the CSR: it finds the row holding its first edge (binary search in rowptr),
+// accumulates row segment by row segment, and flushes each segment with a plain
+// store when the whole row lies inside the chunk, or an atomic add when the
+// row is shared with a neighbouring chunk (the output was zeroed first, or
+// holds the value to accumulate onto).
+constexpr int kSpmmChunk = 256;
+
 template <int VEC>
 __global__ void spmm_csr_kernel(const int64_t* __restrict__ rowptr, const int* __restrict__ col,
                                 const float* __restrict__ val, const float* __restrict__ x, int64_t n_rows, int F,
                                 float* __restrict__ out, int accumulate) {
-  const int64_t row = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
-  if (row >= n_rows) return;
-  const int64_t lo = rowptr[row], hi = rowptr[row + 1];
-  // every lane takes part in every shuffle; lanes beyond F only skip their loads
-  for (int fbase = 0; fbase < F; fbase += 32 * VEC) {
-    const int f0 = fbase + lane * VEC;
-    const bool active = f0 < F;
-    float acc[VEC];
+  const int64_t nnz = rowptr[n_rows];
+  const int64_t nchunks = (nnz + kSpmmChunk - 1) / kSpmmChunk;
+  const int64_t warps = (static_cast<int64_t>(gridDim.x) * blockDim.x) >> 5;
+  for (int64_t ch = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5; ch < nchunks;
+       ch += warps) {
+    const int64_t cb = ch * kSpmmChunk;
+    const int64_t ce = (cb + kSpmmChunk < nnz) ? cb + kSpmmChunk : nnz;
+    // row holding edge cb: last r with rowptr[r] <= cb
+    int64_t lo = 0, hi = n_rows;
+    while (hi - lo > 1) {
+      const int64_t mid = (lo + hi) >> 1;
+      if (rowptr[mid] <= cb) lo = mid;
+      else hi = mid;
+    }
+    int64_t row = lo;
+    int64_t e = cb;
+    while (e < ce) {
+      const int64_t rs = rowptr[row], re = rowptr[row + 1];
+      const int64_t se = re < ce ? re : ce;
+      const bool whole = rs >= cb && re <= ce;
+      // every lane takes part in every shuffle; lanes beyond F only skip their loads
+      for (int fbase = 0; fbase < F; fbase += 32 * VEC) {
+        const int f0 = fbase + lane * VEC;
+        const bool active = f0 < F;
+        float acc[VEC];
 #pragma unroll
-    for (int v = 0; v < VEC; ++v) acc[v] = 0.f;
-    for (int64_t e0 = lo; e0 < hi; e0 += 32) {
-      const int64_t my = e0 + lane;
-      const int mc = my < hi ? col[my] : 0;
-      const float mv = my < hi ? val[my] : 0.f;
-      const int cnt = static_cast<int>((hi - e0) < 32 ? (hi - e0) : 32);
-      for (int j = 0; j < cnt; ++j) {
-        const int c = __shfl_sync(0xffffffffu, mc, j);
-        const float w = __shfl_sync(0xffffffffu, mv, j);
-        if (!active) continue;
-        const float* xr = x + static_cast<int64_t>(c) * F + f0;
-        if (VEC == 4) {
-          const float4 t = *reinterpret_cast<const float4*>(xr);
-          acc[0] = fmaf(w, t.x, acc[0]);
-          acc[1] = fmaf(w, t.y, acc[1]);
-          acc[2] = fmaf(w, t.z, acc[2]);
-          acc[3] = fmaf(w, t.w, acc[3]);
-        } else if (VEC == 2) {
-          const float2 t = *reinterpret_cast<const float2*>(xr);
-          acc[0] = fmaf(w, t.x, acc[0]);
-          acc[1] = fmaf(w, t.y, acc[1]);
-        } else {
+        for (int v = 0; v < VEC; ++v) acc[v] = 0.f;
+        for (int64_t e0 = e; e0 < se; e0 += 32) {
+          const int64_t my = e0 + lane;
+          const int mc = my < se ? col[my] : 0;
+          const float mv = my < se ? val[my] : 0.f;
+          const int cnt = static_cast<int>((se - e0) < 32 ? (se - e0) : 32);
+          for (int j = 0; j < cnt; ++j) {
+            const int c = __shfl_sync(0xffffffffu, mc, j);
+            const float w = __shfl_sync(0xffffffffu, mv, j);
+            if (!active) continue;
+            const float* xr = x + static_cast<int64_t>(c) * F + f0;
+            if (VEC == 4) {
+              const float4 t = *reinterpret_cast<const float4*>(xr);
+              acc[0] = fmaf(w, t.x, acc[0]);
+              acc[1] = fmaf(w, t.y, acc[1]);
+              acc[2] = fmaf(w, t.z, acc[2]);
+              acc[3] = fmaf(w, t.w, acc[3]);
+            } else if (VEC == 2) {
+              const float2 t = *reinterpret_cast<const float2*>(xr);
+              acc[0] = fmaf(w, t.x, acc[0]);
+              acc[1] = fmaf(w, t.y, acc[1]);
+            } else {
 #pragma unroll
-          for (int v = 0; v < VEC; ++v) acc[v] = fmaf(w, xr[v], acc[v]);
+              for (int v = 0; v < VEC; ++v) acc[v] = fmaf(w, xr[v], acc[v]);
+            }
+          }
+        }
+        if (active) {
+          float* o = out + row * F + f0;
+#pragma unroll
+          for (int v = 0; v < VEC; ++v) {
+            if (whole) o[v] = accumulate ? o[v] + acc[v] : acc[v];
+            else atomicAdd(o + v, acc[v]);
+          }
         }
       }
-    }
-    if (active) {
-      float* o = out + row * F + f0;
-#pragma unroll
-      for (int v = 0; v < VEC; ++v) o[v] = accumulate ? o[v] + acc[v] : acc[v];
+      e = se;
+      ++row;
     }
   }
 }
 
 void launch_spmm_csr(cudaStream_t st, const int64_t* rowptr, const int* col, const float* val, const float* x,
                      int64_t n_rows, int F, float* out, int accumulate) {
+  if (n_rows == 0) return;
+  // rows without edges and rows shared between chunks start from zero
+  if (!accumulate) cudaMemsetAsync(out, 0, static_cast<size_t>(n_rows) * F * sizeof(float), st);
+  int dev = 0;
+  cudaGetDevice(&dev);
   const int threads = 256;
-  const int64_t blocks = (n_rows * 32 + threads - 1) / threads;
-  if (blocks == 0) return;
+  const int blocks = num_sms(dev) * 8;  // grid-stride over edge chunks (nnz is on the device)
+  count_launch();
   if (F % 128 == 0) spmm_csr_kernel<4><<<blocks, threads, 0, st>>>(rowptr, col, val, x, n_rows, F, out, accumulate);
   else if (F % 64 == 0) spmm_csr_kernel<2><<<blocks, threads, 0, st>>>(rowptr, col, val, x, n_rows, F, out, accumulate);
   else spmm_csr_kernel<1><<<blocks, threads, 0, st>>>(rowptr, col, val, x, n_rows, F, out, accumulate);
@@ -95,6 +135,7 @@ void launch_lstm_bwd(cudaStream_t st, const float* gates, const float* c_prev, c
                      const float* dc, int64_t rows, int H, float* dpre, float* dc_prev) {
   const int64_t n = rows * H;
   if (n == 0) return;
+  count_launch();
   lstm_bwd_kernel<<<(n + 255) / 256, 256, 0, st>>>(gates, c_prev, c_new, dh, dc, rows, H, dpre, dc_prev);
 }
 

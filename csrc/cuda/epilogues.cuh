@@ -16,6 +16,8 @@ constexpr uint32_t kStreamOutDrop = 0x0D7D0u;
 // (PyTorch GRU gate convention). Produces h' = (1 - z) * n + z * h.
 // ---------------------------------------------------------------------------
 struct EpiGRU {
+  static constexpr bool kSplitCols = false;  // a tile's gate groups of one unit must meet in one thread
+  static constexpr int kScratchBytes = 0;
   int D = 0, DP = 0;  // DP = gate group width G: tile columns are [r | z | n_i | n_h] x G units
   const float* b_ih = nullptr;   // [3D]
   const float* b_hh = nullptr;   // [3D]
@@ -74,6 +76,8 @@ struct EpiGRU {
 // output projection epilogue: dropout -> ReLU -> LayerNorm (row owned by thread)
 // ---------------------------------------------------------------------------
 struct EpiOutLN {
+  static constexpr bool kSplitCols = false;  // LayerNorm needs the whole row
+  static constexpr int kScratchBytes = 0;
   int Do = 0;
   const float* bias = nullptr;
   const float* gamma = nullptr;
@@ -90,27 +94,49 @@ struct EpiOutLN {
 #ifdef __CUDACC__
   __device__ __forceinline__ void operator()(int row, bool valid, int /*n0*/, uint32_t taddr, int /*tile_cols*/) const {
     const uint64_t dseed = seed ^ (static_cast<uint64_t>(*step_ctr) * 0x9E3779B97F4A7C15ull);
+    const float inv_keep = drop > 0.f ? 1.f / (1.f - drop) : 1.f;
     float s1 = 0.f, s2 = 0.f;
     float* xs = xsave + (int64_t)row * Do;
+    float* o = out + (int64_t)row * Do;
+    // 4-column groups: one Philox call and one 16-byte store each (Do % 4 == 0 keeps
+    // every row 16-byte aligned); a ragged tail goes element by element
+    const bool vec = (Do & 3) == 0 && (reinterpret_cast<uintptr_t>(xsave) & 15) == 0 &&
+                     (reinterpret_cast<uintptr_t>(out) & 15) == 0;
     for (int c0 = 0; c0 < Do; c0 += 16) {
       float v[16];
       tmem_ld16(taddr + c0, v);
       if (!valid) continue;
 #pragma unroll
-      for (int i = 0; i < 16; ++i) {
-        const int c = c0 + i;
+      for (int j = 0; j < 4; ++j) {
+        const int c = c0 + 4 * j;
         if (c >= Do) break;
-        float x = v[i] + bias[c];
-        if (drop > 0.f) x = dropout_keep(dseed, (uint64_t)row * Do + c, kStreamOutDrop, drop) ? x / (1.f - drop) : 0.f;
-        x = fmaxf(x, 0.f);
-        xs[c] = x;
-        s1 += x;
-        s2 += x * x;
+        if (vec) {
+          bool k[4];
+          dropout_keep4(dseed, (uint64_t)row * Do + c, kStreamOutDrop, drop, k);
+          float x[4];
+#pragma unroll
+          for (int u = 0; u < 4; ++u) {
+            const float t = (v[4 * j + u] + bias[c + u]) * inv_keep;
+            x[u] = k[u] ? fmaxf(t, 0.f) : 0.f;
+            s1 += x[u];
+            s2 += x[u] * x[u];
+          }
+          *reinterpret_cast<float4*>(xs + c) = make_float4(x[0], x[1], x[2], x[3]);
+        } else {
+          for (int u = 0; u < 4 && c + u < Do; ++u) {
+            float x = v[4 * j + u] + bias[c + u];
+            if (drop > 0.f)
+              x = dropout_keep(dseed, (uint64_t)row * Do + c + u, kStreamOutDrop, drop) ? x * inv_keep : 0.f;
+            x = fmaxf(x, 0.f);
+            xs[c + u] = x;
+            s1 += x;
+            s2 += x * x;
+          }
+        }
       }
     }
     if (!valid) return;
     if (edge_total != nullptr && *edge_total == 0) {
-      float* o = out + (int64_t)row * Do;
       for (int c = 0; c < Do; ++c) o[c] = 0.f;
       mean[row] = 0.f;
       rstd[row] = 0.f;
@@ -121,8 +147,16 @@ struct EpiOutLN {
     const float rs = rsqrtf(var + 1e-5f);
     mean[row] = mu;
     rstd[row] = rs;
-    float* o = out + (int64_t)row * Do;
-    for (int c = 0; c < Do; ++c) o[c] = (xs[c] - mu) * rs * gamma[c] + beta[c];
+    if (vec) {
+      for (int c = 0; c < Do; c += 4) {
+        const float4 x = *reinterpret_cast<const float4*>(xs + c);
+        *reinterpret_cast<float4*>(o + c) =
+            make_float4((x.x - mu) * rs * gamma[c] + beta[c], (x.y - mu) * rs * gamma[c + 1] + beta[c + 1],
+                        (x.z - mu) * rs * gamma[c + 2] + beta[c + 2], (x.w - mu) * rs * gamma[c + 3] + beta[c + 3]);
+      }
+    } else {
+      for (int c = 0; c < Do; ++c) o[c] = (xs[c] - mu) * rs * gamma[c] + beta[c];
+    }
   }
 #endif
 };
@@ -139,6 +173,8 @@ namespace su {
 // over [x || h]). i, f, o = sigmoid, g = tanh, c' = f c + i g, h' = o tanh(c').
 // Saves the post-activation gates for the backward pass.
 struct EpiLSTM {
+  static constexpr bool kSplitCols = false;
+  static constexpr int kScratchBytes = 0;
   int H = 0, DP = 0;  // DP = gate group width G: tile columns are [i | f | g | o] x G units
   const float* b_i = nullptr;
   const float* b_f = nullptr;
@@ -184,4 +220,93 @@ struct EpiLSTM {
 #endif
 };
 
+
+// ---------------------------------------------------------------------------
+// time-encoder gradient epilogue: the accumulator holds dT = d(loss)/d cos(w t + b)
+// for a tile of rows; the epilogue reduces it straight into the encoder's
+// parameter gradients (no dT buffer):
+//   db[c] += sum_rows -sin(w[c] t + b[c]) dT[row, c],   dw[c] += same * t
+// Rows are reduced over each warp with shuffles, then one atomic per warp.
+// ---------------------------------------------------------------------------
+struct EpiTimeGrad {
+  static constexpr bool kSplitCols = true;
+  // per 128-thread epilogue group: two [16 columns][132] fp32 staging arrays
+  static constexpr int kScratchStride = 132;
+  static constexpr int kScratchBytes = 2 * 16 * kScratchStride * 4;
+  int T = 0;
+  const float* t = nullptr;  // per-row time input (nullptr: t = 0, only db gets contributions)
+  const float* w = nullptr;
+  const float* b = nullptr;
+  float* dw = nullptr;
+  float* db = nullptr;
+
+#ifdef __CUDACC__
+  __device__ __forceinline__ void operator()(int row, bool valid, int n0, uint32_t taddr, int tile_cols) const {
+    const float tr = (valid && t != nullptr) ? t[row] : 0.f;
+    const int lane = threadIdx.x & 31;
+    const int lim = min(T - n0, tile_cols);
+    for (int c0 = 0; c0 < lim; c0 += 16) {
+      float v[16];
+      tmem_ld16(taddr + c0, v);
+#pragma unroll
+      for (int i = 0; i < 16; ++i) {
+        const int c = n0 + c0 + i;
+        if (c0 + i >= lim) break;  // uniform across the warp
+        const float g = valid ? -sin_phase(w[c], tr, b[c]) * v[i] : 0.f;
+        float gb = g, gw = g * tr;
+#pragma unroll
+        for (int off = 16; off > 0; off >>= 1) {
+          gb += __shfl_xor_sync(0xffffffffu, gb, off);
+          gw += __shfl_xor_sync(0xffffffffu, gw, off);
+        }
+        if (lane == 0) {
+          atomicAdd(&db[c], gb);
+          if (t != nullptr) atomicAdd(&dw[c], gw);
+        }
+      }
+    }
+  }
+
+  // Same result with the 128 rows of a tile reduced through shared memory
+  // (16 columns at a time; 8 threads per column) instead of per-column warp
+  // shuffles. All 128 threads of the group (barrier `bar_id`) take part.
+  __device__ __forceinline__ void run(int row, bool valid, int n0, uint32_t taddr, int tile_cols, float* scr,
+                                      int bar_id) const {
+    const float tr = (valid && t != nullptr) ? t[row] : 0.f;
+    const int tid = threadIdx.x & 127;  // row within the tile
+    float* sb = scr;
+    float* sw = scr + 16 * kScratchStride;
+    const int lim = min(T - n0, tile_cols);
+    for (int c0 = 0; c0 < lim; c0 += 16) {
+      float v[16];
+      tmem_ld16(taddr + c0, v);
+#pragma unroll
+      for (int i = 0; i < 16; ++i) {
+        const int c = n0 + c0 + i;
+        const float g = (valid && c0 + i < lim) ? -sin_phase(w[c], tr, b[c]) * v[i] : 0.f;
+        sb[i * kScratchStride + tid] = g;
+        sw[i * kScratchStride + tid] = g * tr;
+      }
+      asm volatile("bar.sync %0, 128;" ::"r"(bar_id) : "memory");
+      const int i = tid >> 3, part = tid & 7;
+      float gb = 0.f, gw = 0.f;
+#pragma unroll
+      for (int r = 0; r < 16; ++r) {
+        gb += sb[i * kScratchStride + r * 8 + part];
+        gw += sw[i * kScratchStride + r * 8 + part];
+      }
+#pragma unroll
+      for (int off = 4; off > 0; off >>= 1) {
+        gb += __shfl_xor_sync(0xffffffffu, gb, off);
+        gw += __shfl_xor_sync(0xffffffffu, gw, off);
+      }
+      if (part == 0 && c0 + i < lim) {
+        atomicAdd(&db[n0 + c0 + i], gb);
+        if (t != nullptr) atomicAdd(&dw[n0 + c0 + i], gw);
+      }
+      asm volatile("bar.sync %0, 128;" ::"r"(bar_id) : "memory");
+    }
+  }
+#endif
+};
 }  // namespace su

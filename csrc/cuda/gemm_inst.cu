@@ -2,6 +2,7 @@
 // combination used by the framework, and the per-device bookkeeping
 // (status word, SM count). The N tile is chosen from the output width.
 #include <algorithm>
+#include <atomic>
 #include <cstdio>
 #include <cstdlib>
 
@@ -29,6 +30,10 @@ int* device_status_ptr(int device) {
   return g_status[device];
 }
 
+static std::atomic<long long> g_launches{0};
+void count_launch() { g_launches.fetch_add(1, std::memory_order_relaxed); }
+long long launch_count() { return g_launches.load(std::memory_order_relaxed); }
+
 int num_sms(int device) {
   if (g_sms[device] == 0) {
     cudaDeviceGetAttribute(&g_sms[device], cudaDevAttrMultiProcessorCount, device);
@@ -54,6 +59,7 @@ static void launch_cfg(const A& a, const B& b, const E& e, const GemmShape& sh, 
   if (total <= 0) return;
   const int per_sm = (smem <= 100 * 1024) ? 2 : 1;
   const int grid = std::min(total, num_sms(device) * per_sm);
+  count_launch();
   kern<<<grid, kGemmThreads, smem, st>>>(a, b, e, sh, device_status_ptr(device));
 }
 
@@ -77,6 +83,7 @@ static void launch_cfg_status(const A& a, const B& b, const E& e, const GemmShap
   if (total <= 0) return;
   const int per_sm = (smem <= 100 * 1024) ? 2 : 1;
   const int grid = std::min(total, num_sms(device) * per_sm);
+  count_launch();
   kern<<<grid, kGemmThreads, smem, st>>>(a, b, e, sh, status);
 }
 
@@ -144,13 +151,14 @@ static void launch_pack(const Src& src, uint8_t* out, int mn, const int* mn_dev,
   if (total <= 0) return;
   const int64_t want = (total + 255) / 256;
   const int blocks = static_cast<int>(std::min<int64_t>(want, static_cast<int64_t>(num_sms(device)) * 16));
+  count_launch();
   pack_kernel<ROWS, Src><<<blocks, 256, 0, st>>>(src, out, tiles, nchunks, mn, mn_dev, mn);
 }
 
 template <int BN, int NSUB, class A, class B, class E>
 static bool launch_packed(const A& a, const B& b, const E& e, const GemmShape& sh, cudaStream_t st) {
   constexpr int B_ROWS = BN * NSUB;
-  constexpr int smem = packed_smem_bytes<BN, NSUB>();
+  constexpr int smem = packed_smem_bytes<BN, NSUB, E>();
   int device = 0;
   cudaGetDevice(&device);
   const size_t abytes = packed_bytes(sh.M, sh.K, kBM);
@@ -170,6 +178,7 @@ static bool launch_packed(const A& a, const B& b, const E& e, const GemmShape& s
   const int tiles_n = (sh.N + B_ROWS - 1) / B_ROWS;
   const int total = tiles_m * tiles_n * std::max(1, sh.ksplit);
   const int grid = std::min(total, num_sms(device));
+  count_launch();
   kern<<<grid, kPackedThreads, smem, st>>>(ws, ws + abytes, e, sh, device_status_ptr(device));
   return true;
 }
@@ -204,6 +213,11 @@ void gemm(const SegSource& a, const WeightSource& b, const EpiGRU& e, const Gemm
 void gemm(const SegSource& a, const WeightSource& b, const EpiOutLN& e, const GemmShape& sh, cudaStream_t st) {
   if (sh.N <= 128) launch_any<128, 1>(a, b, e, sh, st);
   else launch_any<256, 1>(a, b, e, sh, st);
+}
+
+void gemm(const SegSource& a, const MNView<WeightSource>& b, const EpiTimeGrad& e, const GemmShape& sh,
+          cudaStream_t st) {
+  dispatch(a, b, e, sh, st);
 }
 
 void gemm(const SegSource& a, const WeightSource& b, const EpiLSTM& e, const GemmShape& sh, cudaStream_t st) {

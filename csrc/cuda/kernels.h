@@ -12,6 +12,9 @@ namespace su {
 
 // ---- device bookkeeping -----------------------------------------------------
 int* device_status_ptr(int device);  // per-device status word (bounded waits, bad indices)
+// Host-side count of kernel launches issued by this library (all devices).
+void count_launch();
+long long launch_count();
 int num_sms(int device);
 
 // ---- tcgen05 GEMM entry points (one overload per producer/epilogue combo) ---
@@ -22,6 +25,8 @@ void gemm(const MNView<SegSource>& a, const MNView<SegSource>& b, const EpiWeigh
           cudaStream_t st);
 void gemm(const SegSource& a, const WeightSource& b, const EpiGRU& e, const GemmShape& sh, cudaStream_t st);
 void gemm(const SegSource& a, const WeightSource& b, const EpiOutLN& e, const GemmShape& sh, cudaStream_t st);
+void gemm(const SegSource& a, const MNView<WeightSource>& b, const EpiTimeGrad& e, const GemmShape& sh,
+          cudaStream_t st);
 // Same kernels, reporting into a caller-given device status word instead of the
 // lazily allocated per-device one (used by entry points that must not allocate).
 void gemm_with_status(const SegSource& a, const MNView<WeightSource>& b, const EpiLinear& e, const GemmShape& sh,

@@ -63,6 +63,7 @@ __global__ void adam_flat_kernel(float* __restrict__ p, const float* __restrict_
 void launch_adam_flat(cudaStream_t st, int blocks, float* p, const float* g, float* m, float* v, int64_t n,
                       int64_t* step, unsigned int* done, float lr, float b1, float b2, float eps, float wd,
                       float grad_scale) {
+  count_launch();
   adam_flat_kernel<<<blocks, 256, 0, st>>>(p, g, m, v, n, step, done, lr, b1, b2, eps, wd, grad_scale);
 }
 

@@ -66,6 +66,7 @@ __global__ void peer_barrier_kernel(uint64_t* const* __restrict__ flag_ptrs, int
 
 void launch_peer_barrier(cudaStream_t st, uint64_t* const* flag_ptrs, int rank, int W, int64_t* epoch, int* status,
                          long long budget) {
+  count_launch();
   peer_barrier_kernel<<<1, 32, 0, st>>>(flag_ptrs, rank, W, epoch, status, budget);
 }
 
@@ -124,6 +125,7 @@ __global__ void peer_allreduce_adam_kernel(const float* const* __restrict__ grad
 void launch_peer_allreduce_adam(cudaStream_t st, int blocks, const float* const* grads, int W, float* p, float* m,
                                 float* v, int64_t n, int64_t* step, unsigned int* done, float lr, float b1, float b2,
                                 float eps, float wd, float scale) {
+  count_launch();
   peer_allreduce_adam_kernel<<<blocks, 256, 0, st>>>(grads, W, p, m, v, n, step, done, lr, b1, b2, eps, wd, scale);
 }
 
@@ -156,6 +158,7 @@ void launch_tgn_peer_writeback(cudaStream_t st, const int64_t* roots, const int*
                                const float* mem_new, int D, const int* owner, float* const* mem_tables,
                                float* const* ts_tables, const float* ts_max) {
   if (rmax <= 0) return;
+  count_launch();
   tgn_peer_writeback_kernel<<<rmax, 64, 0, st>>>(roots, n_roots, rmax, mem_new, D, owner, mem_tables, ts_tables,
                                                  ts_max);
 }
@@ -234,6 +237,7 @@ void launch_tgn_peer_mail_claim(cudaStream_t st, const int64_t* roots, const int
                                 const int64_t* ev_eid, const float* ev_ts, const int* owner,
                                 unsigned long long* const* claim_tables) {
   if (rmax <= 0) return;
+  count_launch();
   tgn_peer_mail_claim_kernel<<<(rmax + 127) / 128, 128, 0, st>>>(roots, n_roots, rmax, win, ev_eid, ev_ts, owner,
                                                                   claim_tables);
 }
@@ -244,6 +248,7 @@ void launch_tgn_peer_mail_write(cudaStream_t st, const int64_t* roots, const int
                                 const int* owner, const unsigned long long* const* claim_tables,
                                 float* const* mail_tables, float* const* mail_ts_tables) {
   if (rmax <= 0) return;
+  count_launch();
   tgn_peer_mail_write_kernel<<<rmax, 128, 0, st>>>(roots, n_roots, rmax, win, src_idx, dst_idx, ev_eid, ev_ts,
                                                    mem_prev, D, efeat, efeat_ld, e_raw, E, owner, claim_tables,
                                                    mail_tables, mail_ts_tables);

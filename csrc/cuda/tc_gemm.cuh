@@ -354,6 +354,8 @@ __device__ __forceinline__ float apply_act(float v, int act) {
 
 // out[row, col] (=|+=) act(scale * acc + bias[col]); optional row scatter.
 struct EpiLinear {
+  static constexpr bool kSplitCols = true;  // columns are independent: two warps may share a row
+  static constexpr int kScratchBytes = 0;
   float* out = nullptr;
   __nv_bfloat16* out_bf16 = nullptr;
   int ldo = 0;
@@ -374,10 +376,29 @@ struct EpiLinear {
       if (orow < 0) valid = false;
     }
     const int lim = min(ncols - n0, tile_cols);
+    // plain stores of whole 16-column groups go out as four 16-byte vectors
+    const bool vec_ok = out != nullptr && accumulate == 0 && out_bf16 == nullptr && (ldo & 3) == 0 &&
+                        (reinterpret_cast<uintptr_t>(out) & 15) == 0;
     for (int c0 = 0; c0 < lim; c0 += 16) {
       float v[16];
       tmem_ld16(taddr + c0, v);  // warp-uniform
       if (!valid) continue;
+      const int cb = n0 + c0;
+      if (vec_ok && cb + 16 <= ncols && (cb & 3) == 0) {
+        float4* o = reinterpret_cast<float4*>(out + orow * ldo + cb);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          float x[4];
+#pragma unroll
+          for (int u = 0; u < 4; ++u) {
+            const int col = cb + 4 * j + u;
+            const float bv = col < bias_split ? (bias ? bias[col] : 0.f) : (bias2 ? bias2[col - bias_split] : 0.f);
+            x[u] = apply_act(scale * v[4 * j + u] + bv, act);
+          }
+          o[j] = make_float4(x[0], x[1], x[2], x[3]);
+        }
+        continue;
+      }
 #pragma unroll
       for (int i = 0; i < 16; ++i) {
         const int col = n0 + c0 + i;
@@ -402,6 +423,8 @@ struct EpiLinear {
 // columns = padded input K space (segments). Segment kinds flagged as bias
 // accumulate into the bias gradient of the block.
 struct EpiWeightGrad {
+  static constexpr bool kSplitCols = true;
+  static constexpr int kScratchBytes = 0;
   WeightLayout L;                 // cell ptrs point at gradient buffers
   float* bias_grad[kMaxBlk] = {nullptr, nullptr, nullptr, nullptr};
   int bias_seg = -1;              // segment index carrying the ones column

@@ -23,20 +23,43 @@
 
 namespace su {
 
-constexpr int kPackedThreads = 192;  // warps 0-3 epilogue, warp 4 copy producer, warp 5 MMA (+ TMEM owner)
+// warps 0-7 epilogue (warp w reads TMEM lanes 32*(w%4).. and, for epilogues with
+// independent columns, column half w/4), warp 8 copy producer, warp 9 MMA + TMEM owner
+constexpr int kPackedThreads = 320;
+constexpr int kProducerWarp = 8;
+constexpr int kMmaWarp = 9;
 
 template <int BN, int NSUB>
 constexpr int packed_stage_bytes() {
   return kBM * kBK * 2 + BN * NSUB * kBK * 2;
 }
-template <int BN, int NSUB>
+// ring depth: as many stages as fit (at most 6) next to the barriers, the
+// epilogue scratch and the alignment slack, within 224 KB of dynamic smem
+template <int BN, int NSUB, int SCRATCH>
 constexpr int packed_stages() {
-  return (200 * 1024) / packed_stage_bytes<BN, NSUB>() >= 6 ? 6 : (200 * 1024) / packed_stage_bytes<BN, NSUB>();
+  return (224 * 1024 - 2048 - 2 * SCRATCH) / packed_stage_bytes<BN, NSUB>() >= 6
+             ? 6
+             : (224 * 1024 - 2048 - 2 * SCRATCH) / packed_stage_bytes<BN, NSUB>();
 }
-template <int BN, int NSUB>
+template <int BN, int NSUB, class Epi>
 constexpr int packed_smem_bytes() {
-  return packed_stages<BN, NSUB>() * packed_stage_bytes<BN, NSUB>() + 1024 /*barriers*/ + 1024 /*align*/;
+  return packed_stages<BN, NSUB, Epi::kScratchBytes>() * packed_stage_bytes<BN, NSUB>() + 1024 /*barriers*/ +
+         2 * Epi::kScratchBytes + 1024 /*align*/;
 }
+
+#ifdef __CUDACC__
+// Epilogues with staging scratch reduce through shared memory with a named
+// barrier per 128-thread group; the rest take the plain call.
+template <class Epi>
+__device__ __forceinline__ void call_epilogue(const Epi& e, int row, bool valid, int n0, uint32_t taddr, int cols,
+                                              uint8_t* scratch, int group) {
+  if constexpr (Epi::kScratchBytes > 0) {
+    e.run(row, valid, n0, taddr, cols, reinterpret_cast<float*>(scratch + group * Epi::kScratchBytes), 1 + group);
+  } else {
+    e(row, valid, n0, taddr, cols);
+  }
+}
+#endif
 
 // bytes of a packed operand with `mn` rows (MN extent) and K extent `k`
 inline size_t packed_bytes(int mn, int k, int rows_per_tile) {
@@ -94,8 +117,12 @@ __global__ void __launch_bounds__(kPackedThreads, 1)
   constexpr int A_BYTES = kBM * kBK * 2;
   constexpr int B_ROWS = BN * NSUB;
   constexpr int B_BYTES = B_ROWS * kBK * 2;
-  constexpr int STAGES = packed_stages<BN, NSUB>();
-  constexpr uint32_t TMEM_COLS = tmem_cols_for(B_ROWS);
+  constexpr int STAGES = packed_stages<BN, NSUB, Epi::kScratchBytes>();
+  static_assert(STAGES >= 2, "shared memory too small for a two-stage ring");
+  static_assert(packed_smem_bytes<BN, NSUB, Epi>() <= 227 * 1024, "dynamic shared memory above the sm_100 limit");
+  // two accumulators when they fit in TMEM: the epilogue of tile i overlaps the MMA of tile i+1
+  constexpr int NACC = (2 * B_ROWS <= 512) ? 2 : 1;
+  constexpr uint32_t TMEM_COLS = tmem_cols_for(NACC * B_ROWS);
   constexpr uint32_t IDESC =
       umma_idesc_bf16_f32(kBM, BN) | (AMN ? (1u << 15) : 0u) | (BMN ? (1u << 16) : 0u);
 
@@ -106,11 +133,12 @@ __global__ void __launch_bounds__(kPackedThreads, 1)
   uint64_t* bars = reinterpret_cast<uint64_t*>(smemB + STAGES * B_BYTES);
   uint64_t* full = bars;                 // [STAGES] copies landed (1 arrival + tx bytes)
   uint64_t* empty = bars + STAGES;       // [STAGES] MMA done with the stage
-  uint64_t* acc_full = bars + 2 * STAGES;
-  uint64_t* acc_empty = acc_full + 1;
-  uint64_t* drain = acc_full + 2;
+  uint64_t* acc_full = bars + 2 * STAGES;  // [NACC]
+  uint64_t* acc_empty = acc_full + 2;      // [NACC]
+  uint64_t* drain = acc_full + 4;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  uint8_t* epi_scratch = reinterpret_cast<uint8_t*>(bars) + 1024;  // 2 * Epi::kScratchBytes
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -119,13 +147,15 @@ __global__ void __launch_bounds__(kPackedThreads, 1)
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
     }
-    mbar_init(acc_full, 1);
-    mbar_init(acc_empty, 128);
+    for (int a = 0; a < NACC; ++a) {
+      mbar_init(&acc_full[a], 1);
+      mbar_init(&acc_empty[a], Epi::kSplitCols ? 256 : 128);
+    }
     mbar_init(drain, 1);
     *abort_flag = 0;
     fence_mbar_init();
   }
-  if (warp == 5) {
+  if (warp == kMmaWarp) {
     tmem_alloc(tmem_slot, TMEM_COLS);
     tmem_relinquish();
   }
@@ -143,29 +173,36 @@ __global__ void __launch_bounds__(kPackedThreads, 1)
   const int cps = (nchunks + ksplit - 1) / ksplit;
   const int total = tiles_m * tiles_n * ksplit;
 
-  if (warp < 4) {
+  if (warp < 8) {
     // ------------------------------ epilogue ------------------------------
+    const int q = warp & 3;       // TMEM lane quarter
+    const int half = warp >> 2;   // column half (epilogues with independent columns)
+    const bool active = Epi::kSplitCols || half == 0;
     int tl = 0;  // tiles with work (the MMA warp counts the same ones)
-    for (int tile = blockIdx.x; tile < total; tile += gridDim.x) {
+    for (int tile = blockIdx.x; active && tile < total; tile += gridDim.x) {
       const int mn = tile / ksplit;
       const int nt = mn % tiles_n;
       const int mt = mn / tiles_n;
       const int ks = tile % ksplit;
       if (ks * cps >= nchunks) continue;  // empty split: nothing was accumulated
-      if (!mbar_wait_bounded(acc_full, tl & 1) || *abort_flag) {
+      const int slot = tl % NACC;
+      if (!mbar_wait_bounded(&acc_full[slot], (tl / NACC) & 1) || *abort_flag) {
         record_status(status, kTimeoutAccum);
         *abort_flag = 1;
         break;
       }
       tc_fence_after();
-      const int row = mt * kBM + warp * 32 + lane;
-      const uint32_t taddr = tmem_base + (static_cast<uint32_t>(warp * 32) << 16);
-      epi(row, row < M, nt * B_ROWS, taddr, B_ROWS);
+      const int row = mt * kBM + q * 32 + lane;
+      constexpr int kCols = Epi::kSplitCols ? B_ROWS / 2 : B_ROWS;
+      const int c0 = Epi::kSplitCols ? half * kCols : 0;
+      const uint32_t taddr = tmem_base + (static_cast<uint32_t>(q * 32) << 16) +
+                             static_cast<uint32_t>(slot * B_ROWS + c0);
+      call_epilogue(epi, row, row < M, nt * B_ROWS + c0, taddr, kCols, epi_scratch, half);
       tc_fence_before();
-      mbar_arrive(acc_empty);
+      mbar_arrive(&acc_empty[slot]);
       ++tl;
     }
-  } else if (warp == 4) {
+  } else if (warp == kProducerWarp) {
     // --------------------------- copy producer ----------------------------
     if (lane == 0) {
       int cg = 0;
@@ -213,12 +250,14 @@ __global__ void __launch_bounds__(kPackedThreads, 1)
         const int kc0 = ks * cps;
         const int kc1 = min(nchunks, kc0 + cps);
         if (kc0 >= kc1) continue;
-        if (!mbar_wait_bounded(acc_empty, (tl & 1) ^ 1) || *abort_flag) {
+        const int slot = tl % NACC;
+        if (!mbar_wait_bounded(&acc_empty[slot], ((tl / NACC) & 1) ^ 1) || *abort_flag) {
           record_status(status, kTimeoutTmemFree);
           *abort_flag = 1;
           break;
         }
         tc_fence_after();
+        const uint32_t acc = tmem_base + static_cast<uint32_t>(slot * B_ROWS);
         for (int kc = kc0; kc < kc1; ++kc, ++cg) {
           const int s = cg % STAGES;
           const uint32_t ph = (cg / STAGES) & 1;
@@ -238,14 +277,14 @@ __global__ void __launch_bounds__(kPackedThreads, 1)
             for (int sub = 0; sub < NSUB; ++sub) {
               const uint64_t bdesc =
                   umma_desc_kmajor_noswizzle(b_base + sub * (BN / 8) * 1024 + kk * 256, 128, 1024);
-              umma_bf16(tmem_base + sub * BN, adesc, bdesc, IDESC, (kc > kc0 || kk > 0) ? 1u : 0u);
+              umma_bf16(acc + sub * BN, adesc, bdesc, IDESC, (kc > kc0 || kk > 0) ? 1u : 0u);
             }
             issued = true;
           }
           umma_commit(&empty[s]);
         }
         if (!ok) break;
-        umma_commit(acc_full);
+        umma_commit(&acc_full[slot]);
         ++tl;
       }
       if (issued) {  // no tensor-core work may be in flight when TMEM is released
@@ -258,7 +297,7 @@ __global__ void __launch_bounds__(kPackedThreads, 1)
 
   tc_fence_before();
   __syncthreads();
-  if (warp == 5) {
+  if (warp == kMmaWarp) {
     tc_fence_after();
     tmem_dealloc(tmem_base, TMEM_COLS);
   }

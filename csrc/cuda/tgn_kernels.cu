@@ -519,6 +519,7 @@ __global__ void __launch_bounds__(1024) tgn_metrics_kernel(const float* __restri
 // launchers (called from the torch-side wrappers)
 // ---------------------------------------------------------------------------
 void launch_tgn_prep(dim3 grid, dim3 block, cudaStream_t st, PrepArgs a) {
+  count_launch();
   tgn_prep_kernel<<<grid, block, 0, st>>>(a);
 }
 
@@ -529,6 +530,7 @@ void launch_tgn_sample(dim3 grid, dim3 block, cudaStream_t st, const int64_t* __
                                   uint64_t seed, const int64_t* __restrict__ step_ctr, int64_t* __restrict__ out_nbr,
                                   int64_t* __restrict__ out_eid, float* __restrict__ out_dt,
                                   int* __restrict__ out_cnt, int* __restrict__ edge_total) {
+  count_launch();
   tgn_sample_kernel<<<grid, block, 0, st>>>(roots, n_roots, rmax, root_ts_scalar, root_ts_vec, rowptr, nbr, eid, ets, k, policy, seed, step_ctr, out_nbr, out_eid, out_dt, out_cnt, edge_total);
 }
 
@@ -539,6 +541,7 @@ void launch_tgn_mailbox(dim3 grid, dim3 block, cudaStream_t st, const int64_t* _
                                    const float* __restrict__ mem_prev, int D, const float* __restrict__ efeat,
                                    int efeat_ld, int e_raw, int E, float* __restrict__ mailbox,
                                    float* __restrict__ mailbox_ts, int64_t* __restrict__ next_pos, int K) {
+  count_launch();
   tgn_mailbox_kernel<<<grid, block, 0, st>>>(roots, n_roots, rmax, win, cnt, src_idx, dst_idx, ev_eid, ev_ts, mem_prev, D, efeat, efeat_ld, e_raw, E, mailbox, mailbox_ts, next_pos, K);
 }
 
@@ -546,6 +549,7 @@ void launch_tgn_attn_fwd(dim3 grid, dim3 block, cudaStream_t st, const float* __
                                     const int* __restrict__ cnt, const int* __restrict__ n_roots, int rmax, int k,
                                     int Do, int H, float att_drop, uint64_t seed, const int64_t* __restrict__ step_ctr,
                                     float* __restrict__ att_p, float* __restrict__ agg) {
+  count_launch();
   tgn_attn_fwd_kernel<<<grid, block, 0, st>>>(Q, KV, cnt, n_roots, rmax, k, Do, H, att_drop, seed, step_ctr, att_p, agg);
 }
 
@@ -554,6 +558,7 @@ void launch_tgn_attn_bwd(dim3 grid, dim3 block, cudaStream_t st, const float* __
                                     const int* __restrict__ cnt, const int* __restrict__ n_roots, int rmax, int k,
                                     int Do, int H, float att_drop, uint64_t seed, const int64_t* __restrict__ step_ctr,
                                     float* __restrict__ dKV, float* __restrict__ dQ) {
+  count_launch();
   tgn_attn_bwd_kernel<<<grid, block, 0, st>>>(Q, KV, att_p, dagg, cnt, n_roots, rmax, k, Do, H, att_drop, seed, step_ctr, dKV, dQ);
 }
 
@@ -563,6 +568,7 @@ void launch_tgn_out_bwd(dim3 grid, dim3 block, cudaStream_t st, const float* __r
                                    float drop, uint64_t seed, const int64_t* __restrict__ step_ctr,
                                    const int* __restrict__ edge_total, float* __restrict__ dpre,
                                    float* __restrict__ dgamma, float* __restrict__ dbeta) {
+  count_launch();
   tgn_out_bwd_kernel<<<grid, block, 0, st>>>(dout, xsave, mean, rstd, gamma, n_roots, rmax, Do, drop, seed, step_ctr, edge_total, dpre, dgamma, dbeta);
 }
 
@@ -572,6 +578,7 @@ void launch_tgn_link(dim3 grid, dim3 block, cudaStream_t st, const float* __rest
                                 const float* __restrict__ w_out, const float* __restrict__ b_out, int need_grad,
                                 float* __restrict__ scores, float* __restrict__ loss, float* __restrict__ dP,
                                 float* __restrict__ g_w_out, float* __restrict__ g_b_out, float* __restrict__ g_b_dst) {
+  count_launch();
   tgn_link_kernel<<<grid, block, 0, st>>>(P, src_idx, dst_idx, neg_idx, n_ev, bmax, D, b_dst, w_out, b_out, need_grad, scores, loss, dP, g_w_out, g_b_out, g_b_dst);
 }
 
@@ -580,6 +587,7 @@ void launch_tgn_metrics(dim3 grid, dim3 block, cudaStream_t st, const float* __r
                                                            float* __restrict__ out) {
   const int smem = 2 * bmax * static_cast<int>(sizeof(float));
   if (smem > 48 * 1024) cudaFuncSetAttribute(tgn_metrics_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  count_launch();
   tgn_metrics_kernel<<<grid, block, smem, st>>>(scores, n_ev, bmax, out);
 }
 
@@ -619,6 +627,7 @@ void launch_time_grad_reduce(cudaStream_t st, const float* dT, int64_t rows, int
                              float* db) {
   if (rows == 0) return;
   const int threads = (T + 31) / 32 * 32;
+  count_launch();
   time_grad_reduce_kernel<<<(rows + 63) / 64, threads, 0, st>>>(dT, rows, T, t, w, b, gcount, group, nrows_dev,
                                                                     dw, db);
 }

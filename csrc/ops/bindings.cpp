@@ -2,6 +2,9 @@
 #include <torch/extension.h>
 
 int64_t status_read(bool clear);
+namespace su {
+long long launch_count();
+}
 at::Tensor linear_fwd(const at::Tensor& x, const at::Tensor& w, const c10::optional<at::Tensor>& bias, int64_t act);
 at::Tensor linear_dgrad(const at::Tensor& dy, const at::Tensor& w);
 void linear_wgrad(const at::Tensor& dy, const at::Tensor& x, at::Tensor& dw, const c10::optional<at::Tensor>& db);
@@ -103,6 +106,7 @@ void tgn_peer_mail_write(const at::Tensor& roots, const at::Tensor& n_roots, con
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "starry_unigraph sm_100a kernels (tcgen05 GEMMs, TGN step, DTDG ops, collectives)";
   m.def("status_read", &status_read, "read (and clear) the device status word", py::arg("clear") = true);
+  m.def("launch_count", &su::launch_count, "kernel launches issued by this library so far (host-side count)");
   m.def("linear_fwd", &linear_fwd);
   m.def("linear_dgrad", &linear_dgrad);
   m.def("linear_wgrad", &linear_wgrad);

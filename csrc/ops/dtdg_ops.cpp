@@ -169,8 +169,7 @@ std::vector<at::Tensor> lstm_bwd(const at::Tensor& x, const c10::optional<at::Te
     sh.K = rows;
     const int nchunks = (rows + kBK - 1) / kBK;
     const int tiles = ((DP4 + kBM - 1) / kBM) * ((sh.N + 255) / 256);
-    const int want = std::max(1, (2 * num_sms(at::cuda::current_device())) / std::max(1, tiles));
-    sh.ksplit = std::max(1, std::min(nchunks, want));
+    sh.ksplit = wgrad_ksplit(nchunks, tiles);
     gemm(ta, tb, e, sh, cur_stream());
   }
   SU_LAUNCH_CHECK();

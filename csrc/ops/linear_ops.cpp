@@ -113,8 +113,7 @@ void linear_wgrad(const at::Tensor& dy, const at::Tensor& x, at::Tensor& dw, con
   sh.K = M;
   const int nchunks = (M + kBK - 1) / kBK;
   const int tiles = ((N + kBM - 1) / kBM) * ((sh.N + 255) / 256);
-  const int want = std::max(1, (2 * num_sms(at::cuda::current_device())) / std::max(1, tiles));
-  sh.ksplit = std::max(1, std::min(nchunks, want));
+  sh.ksplit = wgrad_ksplit(nchunks, tiles);
   gemm(a, b, e, sh, cur_stream());
   SU_LAUNCH_CHECK();
 }

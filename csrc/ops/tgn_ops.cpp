@@ -373,8 +373,7 @@ static void proj_wgrad(const SegSource& dy_src, int dy_cols, const SegSource& x_
   sh.K = rows_static;
   const int nchunks = (rows_static + kBK - 1) / kBK;
   const int tiles = ((dy_cols + kBM - 1) / kBM) * ((x_kspace + 255) / 256);
-  const int want = std::max(1, (2 * num_sms(at::cuda::current_device())) / std::max(1, tiles));
-  sh.ksplit = std::max(1, std::min(nchunks, want));
+  sh.ksplit = wgrad_ksplit(nchunks, tiles);
   gemm(a, b, e, sh, cur_stream());
 }
 
@@ -459,7 +458,6 @@ void tgn_attn_proj_bwd(const at::Tensor& memory, const at::Tensor& roots, const 
   // ---------------- time encoder: d(time segment) = dKV [W_k; W_v][:, time] (edges), dQ W_q[:, time] (roots),
   // then a column reduction with the derivative of cos(w t + b)
   {
-    at::Tensor dT = at::empty({static_cast<int64_t>(rmax) * k, T}, dKV.options());
     SegSource a;
     a.group = k;
     a.gcount = nbr_cnt.data_ptr<int>();
@@ -476,21 +474,20 @@ void tgn_attn_proj_bwd(const at::Tensor& memory, const at::Tensor& roots, const 
     L.cell[0][0] = wcell(wk, 0, D + Ei, T);
     L.cell[1][0] = wcell(wv, 0, D + Ei, T);
     WeightMN b = weight_mn(L, pad8(2 * Do));
-    EpiLinear e;
-    e.out = dT.data_ptr<float>();
-    e.ldo = T;
-    e.ncols = T;
+    EpiTimeGrad e;  // reduces dT straight into the encoder gradients
+    e.T = T;
+    e.t = nbr_dt.data_ptr<float>();
+    e.w = te_w.data_ptr<float>();
+    e.b = te_b.data_ptr<float>();
+    e.dw = g_tw.data_ptr<float>();
+    e.db = g_tb.data_ptr<float>();
     GemmShape sh;
     sh.M = rmax * k;
     sh.N = T;
     sh.K = pad8(2 * Do);
     gemm(a, b, e, sh, cur_stream());
-    launch_time_grad_reduce(cur_stream(), dT.data_ptr<float>(), static_cast<int64_t>(rmax) * k, T,
-                            nbr_dt.data_ptr<float>(), te_w.data_ptr<float>(), te_b.data_ptr<float>(),
-                            nbr_cnt.data_ptr<int>(), k, nullptr, g_tw.data_ptr<float>(), g_tb.data_ptr<float>());
   }
   {
-    at::Tensor dT = at::empty({rmax, T}, dQ.options());
     SegSource a;
     a.nrows_dev = n_roots.data_ptr<int>();
     a.nseg = 1;
@@ -503,19 +500,18 @@ void tgn_attn_proj_bwd(const at::Tensor& memory, const at::Tensor& roots, const 
     L.seg_kpad[0] = pad8(T);
     L.cell[0][0] = wcell(wq, 0, D, T);
     WeightMN b = weight_mn(L, pad8(Do));
-    EpiLinear e;
-    e.out = dT.data_ptr<float>();
-    e.ldo = T;
-    e.ncols = T;
+    EpiTimeGrad e;  // roots encode t = 0: only the bias gradient gets contributions
+    e.T = T;
+    e.w = te_w.data_ptr<float>();
+    e.b = te_b.data_ptr<float>();
+    e.dw = g_tw.data_ptr<float>();
+    e.db = g_tb.data_ptr<float>();
     GemmShape sh;
     sh.M = rmax;
     sh.m_dev = n_roots.data_ptr<int>();
     sh.N = T;
     sh.K = pad8(Do);
     gemm(a, b, e, sh, cur_stream());
-    launch_time_grad_reduce(cur_stream(), dT.data_ptr<float>(), rmax, T, nullptr, te_w.data_ptr<float>(),
-                            te_b.data_ptr<float>(), nullptr, 1, n_roots.data_ptr<int>(), g_tw.data_ptr<float>(),
-                            g_tb.data_ptr<float>());
   }
   SU_LAUNCH_CHECK();
 }

@@ -283,7 +283,7 @@ class CTDGOnlineRuntime:
                          "memory": self.memory.describe()}}
 
     def run_split_device(self, split: str, batch_size: int, train: bool, max_steps: int | None = None,
-                         collect_predictions: bool = False) -> dict[str, Any]:
+                         collect_predictions: bool = False, on_step: Any = None) -> dict[str, Any]:
         """Epoch over a split without per-step host synchronisation (CUDA engine only):
         losses and metrics accumulate on the device and are read once at the end."""
         eng = self.engine
@@ -291,6 +291,8 @@ class CTDGOnlineRuntime:
         for i, batch in enumerate(self.iter_batches(split, batch_size)):
             if max_steps is not None and i >= max_steps:
                 break
+            if on_step is not None:
+                on_step(i)
             self._engine_step(batch, split, train, want_outputs=False)
             losses.append(eng.loss.clone())
             mets.append(eng.metrics.clone())

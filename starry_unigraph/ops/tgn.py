@@ -105,6 +105,7 @@ class TGNCudaEngine:
             self._pd = peer.descriptor(self.stamp, self.node2root, self.step_ctr, self.mem_new)
         self._graphs: dict[tuple[str, bool], torch.cuda.CUDAGraph] = {}
         self._warm: dict[tuple[str, bool], int] = {}
+        self._launches: dict[tuple[str, bool], int] = {}  # library kernel launches per step, counted eagerly
 
     # ------------------------------------------------------------------ buffers
     def _alloc(self) -> None:
@@ -288,7 +289,9 @@ class TGNCudaEngine:
         """Run one step on the batch in the static buffers (graph replay after warm-up)."""
         key = (split, bool(train))
         if not self.use_graphs:
+            n0 = self.C.launch_count()
             self._forward(split, train)
+            self._launches[key] = self.C.launch_count() - n0
             return
         g = self._graphs.get(key)
         if g is not None:
@@ -296,7 +299,9 @@ class TGNCudaEngine:
             return
         warm = self._warm.get(key, 0)
         if warm < 2:
+            n0 = self.C.launch_count()
             self._forward(split, train)
+            self._launches[key] = self.C.launch_count() - n0
             self._warm[key] = warm + 1
             return
         # capture (the capture run itself does not execute the kernels): save and
@@ -317,7 +322,11 @@ class TGNCudaEngine:
         return None
 
     def launches_per_step(self, train: bool = True) -> int:
-        """Number of framework kernel launches in one step (memsets excluded)."""
+        """Framework kernel launches in one step (torch memsets excluded): the count
+        measured on an eager warm-up step when there was one, else an estimate."""
+        for (split, tr), n in self._launches.items():
+            if tr == bool(train):
+                return int(n)
         fwd = 10 + self.s.K  # prep, sample, K+1 GRU GEMMs, mailbox, Q, KV, attention, out+LN, link proj, loss, metrics
         bwd = 11             # link-proj (2), LN, out-proj (2), attention, W_q/W_kv/time-encoder (4), Adam
         n = fwd + (bwd if train else 0)

@@ -58,6 +58,12 @@ class SchedulerSession:
         self.ctdg_session: Any = None
         self.prepared: PreparedArtifacts | None = None
         self.pipeline_engine: Any = None
+        from starry_unigraph.utils import FaultInjector
+
+        self._faults = FaultInjector.from_env()
+        self._heartbeat = None
+        self._hb_last = 0.0
+        self._metrics = None
 
     # ------------------------------------------------------------------ construction
     @classmethod
@@ -184,8 +190,45 @@ class SchedulerSession:
                                               optimizer=self.runtime.optimizer)
         return self.pipeline_engine
 
+    # ------------------------------------------------------------------ step hooks
+    def _between_steps(self, step: int) -> None:
+        """Runs on the host before every step: injected faults (SU_FAULT) and the
+        peer heartbeat (dist.heartbeat_s > 0), so a rank learns that a peer is gone
+        before it enters the next collective."""
+        rank = self.ctx.dist.rank
+        if self._faults:
+            self._faults.maybe_inject(rank, step)
+        hb_s = float(self.ctx.config.get("dist", {}).get("heartbeat_s", 0) or 0)
+        if hb_s > 0 and self.ctx.dist.is_distributed and dist.is_initialized():
+            now = time.time()
+            if self._heartbeat is None:
+                from starry_unigraph.utils import Heartbeat
+
+                store = dist.distributed_c10d._get_default_store()
+                self._heartbeat = Heartbeat(store, rank, self.ctx.dist.world_size, timeout_s=hb_s)
+            if now - self._hb_last >= min(1.0, hb_s / 4):
+                self._heartbeat.beat(step)
+                self._heartbeat.check()
+                self._hb_last = now
+
+    def _log_metrics(self, **record: Any) -> None:
+        path = self.ctx.config.get("runtime", {}).get("metrics_path")
+        if not path:
+            return
+        if self._metrics is None:
+            from starry_unigraph.utils import MetricsLogger
+
+            self._metrics = MetricsLogger(path, rank=self.ctx.dist.rank)
+        self._metrics.log(**record)
+
     # ------------------------------------------------------------------ epochs
     def _summarise(self, split: str, outputs: list[dict[str, Any]], losses: list[float], elapsed: float):
+        res = self._summarise_impl(split, outputs, losses, elapsed)
+        self._log_metrics(epoch=self.current_epoch, split=split, steps=res["steps"], loss=res["loss"],
+                          metrics=res["metrics"], elapsed_s=res["elapsed_s"])
+        return res
+
+    def _summarise_impl(self, split: str, outputs: list[dict[str, Any]], losses: list[float], elapsed: float):
         metric_acc: dict[str, list[float]] = {}
         for item in outputs:
             for k, v in item.get("meta", {}).get("metrics", {}).items():
@@ -204,13 +247,18 @@ class SchedulerSession:
             train = split == "train"
             start = time.perf_counter()
             if rt.engine is not None:
-                res = rt.run_split_device(split, int(self.ctx.config["train"]["batch_size"]), train)
+                base = self.global_step
+                res = rt.run_split_device(split, int(self.ctx.config["train"]["batch_size"]), train,
+                                          on_step=lambda i: self._between_steps(base + i))
                 outputs = [{"loss": l, "meta": {"split": split, "batch_size": n,
                                                 "metrics": ({"ap": m[0], "auc": m[1], "mrr": m[2]} if n else {})}}
                            for l, m, n in zip(res["losses"], res["metrics"], res["sizes"])]
             else:
                 it = self.ctdg_session.iter_train(self.ctx) if train else self.ctdg_session.iter_eval(self.ctx, split)
-                outputs = [self.ctdg_session.train_step(b) if train else self.ctdg_session.eval_step(b) for b in it]
+                outputs = []
+                for i, b in enumerate(it):
+                    self._between_steps(self.global_step + i)
+                    outputs.append(self.ctdg_session.train_step(b) if train else self.ctdg_session.eval_step(b))
             elapsed = time.perf_counter() - start
             if train:
                 self.global_step += len(outputs)
@@ -225,7 +273,8 @@ class SchedulerSession:
             iterator = self.snapshot_core.iter_eval(split=split)
         start = time.perf_counter()
         outputs = []
-        for batch in iterator:
+        for i, batch in enumerate(iterator):
+            self._between_steps(self.global_step if split == "train" else i)
             if split == "train":
                 outputs.append(self.snapshot_core.run_train_step(self.runtime, batch))
                 self.global_step += 1

@@ -1,0 +1,78 @@
+"""Two-rank runs on CPU (gloo) through the public session API: DTDG halo
+exchange and data-parallel gradients, CTDG memory partitioning, and failure
+detection on the host (a rank that exits between steps)."""
+import json
+import os
+import socket
+import subprocess
+import sys
+from pathlib import Path
+
+import torch
+
+ROOT = Path(__file__).resolve().parents[1]
+WORKER = ROOT / "tests" / "workers" / "dist_cpu_worker.py"
+
+
+def _port() -> int:
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _launch(out, family, extra_env=None, *args, wall=240):
+    env = dict(os.environ)
+    env.pop("CUDA_VISIBLE_DEVICES", None)
+    env.update(extra_env or {})
+    cmd = ["timeout", "-k", "10", str(wall), sys.executable, "-m", "torch.distributed.run", "--nnodes=1",
+           "--nproc-per-node=2", "--master-addr", "127.0.0.1", "--master-port", str(_port()), str(WORKER),
+           "--family", family, "--out", str(out), *args]
+    return subprocess.run(cmd, cwd=ROOT, env=env, capture_output=True, text=True, timeout=wall + 30)
+
+
+def _outcome(out, r):
+    return json.loads((Path(out) / f"outcome_r{r}.json").read_text())
+
+
+def test_dtdg_two_ranks_halo_and_gradients(tmp_path):
+    res = _launch(tmp_path, "mpnn_lstm")
+    assert res.returncode == 0, res.stdout[-2000:] + res.stderr[-4000:]
+    o0, o1 = _outcome(tmp_path, 0), _outcome(tmp_path, 1)
+    assert o0["error"] is None and o1["error"] is None
+    assert o0["steps"] == o1["steps"] > 0
+    p0, p1 = torch.load(tmp_path / "r0.pt"), torch.load(tmp_path / "r1.pt")
+    # one all-reduced gradient buffer per step: replicas stay identical
+    for a, b in zip(p0["params"], p1["params"]):
+        assert torch.allclose(a, b, atol=1e-6)
+
+
+def test_ctdg_two_ranks_memory_partition(tmp_path):
+    res = _launch(tmp_path, "tgn")
+    assert res.returncode == 0, res.stdout[-2000:] + res.stderr[-4000:]
+    o0, o1 = _outcome(tmp_path, 0), _outcome(tmp_path, 1)
+    assert o0["error"] is None and o1["error"] is None
+    p0, p1 = torch.load(tmp_path / "r0.pt"), torch.load(tmp_path / "r1.pt")
+    for a, b in zip(p0["params"], p1["params"]):
+        assert torch.allclose(a, b, atol=1e-6)
+
+
+def test_rank_exit_between_steps_is_detected(tmp_path):
+    """Rank 1 exits before step 2; rank 0 must stop with an error (heartbeat or
+    collective timeout) instead of waiting forever."""
+    res = _launch(tmp_path, "mpnn_lstm", {"SU_FAULT": "1:2:exit"}, "--timeout", "20", "--heartbeat", "3",
+                  wall=120)
+    assert res.returncode != 0
+    o0 = _outcome(tmp_path, 0)
+    assert o0["error"] is not None, o0
+    assert o0["elapsed_s"] < 90
+    assert not (tmp_path / "outcome_r1.json").exists()  # rank 1 left without a word
+
+
+def test_injected_exception_surfaces(tmp_path):
+    res = _launch(tmp_path, "mpnn_lstm", {"SU_FAULT": "0:1:raise"}, "--timeout", "20", "--heartbeat", "3",
+                  wall=120)
+    assert res.returncode != 0
+    o0 = _outcome(tmp_path, 0)
+    assert o0["error"] == "InjectedFault"
+    o1 = _outcome(tmp_path, 1)
+    assert o1["error"] is not None  # the peer stops too (heartbeat or collective timeout)
