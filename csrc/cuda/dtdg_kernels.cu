@@ -19,10 +19,49 @@ namespace su {
 // holds the value to accumulate onto).
 constexpr int kSpmmChunk = 256;
 
-template <int VEC>
-__global__ void spmm_csr_kernel(const int64_t* __restrict__ rowptr, const int* __restrict__ col,
-                                const float* __restrict__ val, const float* __restrict__ x, int64_t n_rows, int F,
-                                float* __restrict__ out, int accumulate) {
+// where a source row lives: one local matrix, or any rank's copy of a symmetric
+// staging buffer (owner / row per source row, for the NVLink halo path)
+struct LocalRows {
+  const float* x;
+  int F;
+  __device__ __forceinline__ const float* row(int c) const { return x + static_cast<int64_t>(c) * F; }
+};
+struct PeerRows {
+  const float* const* peers;
+  const int* owner;
+  const int* lrow;
+  int F;
+  __device__ __forceinline__ const float* row(int c) const {
+    return peers[owner[c]] + static_cast<int64_t>(lrow[c]) * F;
+  }
+};
+// where a finished row segment goes: this rank's output (plain store for rows
+// inside the chunk, atomic add for rows shared with another chunk), or pushed
+// into the owner rank's buffer with a remote atomic add
+struct LocalOut {
+  float* out;
+  int F;
+  int accumulate;
+  __device__ __forceinline__ void put(int64_t row, int f, float v, bool whole) const {
+    float* o = out + row * F + f;
+    if (whole) *o = accumulate ? *o + v : v;
+    else atomicAdd(o, v);
+  }
+};
+struct PeerPush {
+  float* const* peers;
+  const int* owner;
+  const int* lrow;
+  int F;
+  __device__ __forceinline__ void put(int64_t row, int f, float v, bool /*whole*/) const {
+    atomicAdd(peers[owner[row]] + static_cast<int64_t>(lrow[row]) * F + f, v);
+  }
+};
+
+template <int VEC, class Rows, class Out>
+__global__ void spmm_chunked_kernel(const int64_t* __restrict__ rowptr, const int* __restrict__ col,
+                                    const float* __restrict__ val, const Rows rows, int64_t n_rows, int F,
+                                    const Out out) {
   const int lane = threadIdx.x & 31;
   const int64_t nnz = rowptr[n_rows];
   const int64_t nchunks = (nnz + kSpmmChunk - 1) / kSpmmChunk;
@@ -60,7 +99,7 @@ __global__ void spmm_csr_kernel(const int64_t* __restrict__ rowptr, const int* _
             const int c = __shfl_sync(0xffffffffu, mc, j);
             const float w = __shfl_sync(0xffffffffu, mv, j);
             if (!active) continue;
-            const float* xr = x + static_cast<int64_t>(c) * F + f0;
+            const float* xr = rows.row(c) + f0;
             if (VEC == 4) {
               const float4 t = *reinterpret_cast<const float4*>(xr);
               acc[0] = fmaf(w, t.x, acc[0]);
@@ -78,12 +117,8 @@ __global__ void spmm_csr_kernel(const int64_t* __restrict__ rowptr, const int* _
           }
         }
         if (active) {
-          float* o = out + row * F + f0;
 #pragma unroll
-          for (int v = 0; v < VEC; ++v) {
-            if (whole) o[v] = accumulate ? o[v] + acc[v] : acc[v];
-            else atomicAdd(o + v, acc[v]);
-          }
+          for (int v = 0; v < VEC; ++v) out.put(row, f0 + v, acc[v], whole);
         }
       }
       e = se;
@@ -92,19 +127,45 @@ __global__ void spmm_csr_kernel(const int64_t* __restrict__ rowptr, const int* _
   }
 }
 
-void launch_spmm_csr(cudaStream_t st, const int64_t* rowptr, const int* col, const float* val, const float* x,
-                     int64_t n_rows, int F, float* out, int accumulate) {
-  if (n_rows == 0) return;
-  // rows without edges and rows shared between chunks start from zero
-  if (!accumulate) cudaMemsetAsync(out, 0, static_cast<size_t>(n_rows) * F * sizeof(float), st);
+template <class Rows, class Out>
+static void launch_chunked(cudaStream_t st, const int64_t* rowptr, const int* col, const float* val, const Rows& rows,
+                           int64_t n_rows, int F, const Out& out) {
   int dev = 0;
   cudaGetDevice(&dev);
   const int threads = 256;
   const int blocks = num_sms(dev) * 8;  // grid-stride over edge chunks (nnz is on the device)
   count_launch();
-  if (F % 128 == 0) spmm_csr_kernel<4><<<blocks, threads, 0, st>>>(rowptr, col, val, x, n_rows, F, out, accumulate);
-  else if (F % 64 == 0) spmm_csr_kernel<2><<<blocks, threads, 0, st>>>(rowptr, col, val, x, n_rows, F, out, accumulate);
-  else spmm_csr_kernel<1><<<blocks, threads, 0, st>>>(rowptr, col, val, x, n_rows, F, out, accumulate);
+  if (F % 128 == 0) spmm_chunked_kernel<4><<<blocks, threads, 0, st>>>(rowptr, col, val, rows, n_rows, F, out);
+  else if (F % 64 == 0) spmm_chunked_kernel<2><<<blocks, threads, 0, st>>>(rowptr, col, val, rows, n_rows, F, out);
+  else spmm_chunked_kernel<1><<<blocks, threads, 0, st>>>(rowptr, col, val, rows, n_rows, F, out);
+}
+
+void launch_spmm_csr(cudaStream_t st, const int64_t* rowptr, const int* col, const float* val, const float* x,
+                     int64_t n_rows, int F, float* out, int accumulate) {
+  if (n_rows == 0) return;
+  // rows without edges and rows shared between chunks start from zero
+  if (!accumulate) cudaMemsetAsync(out, 0, static_cast<size_t>(n_rows) * F * sizeof(float), st);
+  launch_chunked(st, rowptr, col, val, LocalRows{x, F}, n_rows, F, LocalOut{out, F, accumulate});
+}
+
+// Halo-fused aggregation: source rows are read from the owners' staging
+// buffers over NVLink (local rows from this rank's own buffer).
+void launch_spmm_peer_gather(cudaStream_t st, const int64_t* rowptr, const int* col, const float* val,
+                             const float* const* peers, const int* src_owner, const int* src_row, int64_t n_rows,
+                             int F, float* out) {
+  if (n_rows == 0) return;
+  cudaMemsetAsync(out, 0, static_cast<size_t>(n_rows) * F * sizeof(float), st);
+  launch_chunked(st, rowptr, col, val, PeerRows{peers, src_owner, src_row, F}, n_rows, F, LocalOut{out, F, 0});
+}
+
+// Its backward over the transposed CSR (rows = source rows): each source row's
+// gradient is pushed into the owner's gradient buffer with remote atomic adds.
+void launch_spmm_peer_push(cudaStream_t st, const int64_t* rowptr_t, const int* col_t, const float* val_t,
+                           const float* grad_dst, int64_t n_src, int F, float* const* peers, const int* src_owner,
+                           const int* src_row) {
+  if (n_src == 0) return;
+  launch_chunked(st, rowptr_t, col_t, val_t, LocalRows{grad_dst, F}, n_src, F,
+                 PeerPush{peers, src_owner, src_row, F});
 }
 
 // d(pre-activation) of the four gates and dc_prev from dh', dc' and the saved gates.

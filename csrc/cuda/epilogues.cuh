@@ -195,6 +195,40 @@ struct EpiLSTM {
       tmem_ld16(taddr + 2 * DP + c0, gg);
       tmem_ld16(taddr + 3 * DP + c0, go);
       if (!valid) continue;
+      const int cb = u0 + c0;
+      if ((H & 3) == 0 && cb + 16 <= H) {
+        // whole group of 16 units: 16-byte loads and stores (rows are 16-byte aligned when H % 4 == 0)
+        const int64_t rb = (int64_t)row * H + cb;
+        float* gr = gates ? gates + (int64_t)row * 4 * H + cb : nullptr;
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          float cpv[4] = {0.f, 0.f, 0.f, 0.f};
+          if (c_prev) {
+            const float4 t = *reinterpret_cast<const float4*>(c_prev + rb + 4 * q);
+            cpv[0] = t.x; cpv[1] = t.y; cpv[2] = t.z; cpv[3] = t.w;
+          }
+          float iv[4], fv[4], gv[4], ov[4], cn[4], hn[4];
+#pragma unroll
+          for (int u = 0; u < 4; ++u) {
+            const int j = 4 * q + u, c = cb + j;
+            iv[u] = sigmoidf_(gi[j] + b_i[c]);
+            fv[u] = sigmoidf_(gf[j] + b_f[c]);
+            gv[u] = tanhf(gg[j] + b_g[c]);
+            ov[u] = sigmoidf_(go[j] + b_o[c]);
+            cn[u] = fv[u] * cpv[u] + iv[u] * gv[u];
+            hn[u] = ov[u] * tanhf(cn[u]);
+          }
+          *reinterpret_cast<float4*>(c_out + rb + 4 * q) = make_float4(cn[0], cn[1], cn[2], cn[3]);
+          *reinterpret_cast<float4*>(h_out + rb + 4 * q) = make_float4(hn[0], hn[1], hn[2], hn[3]);
+          if (gr) {
+            *reinterpret_cast<float4*>(gr + 4 * q) = make_float4(iv[0], iv[1], iv[2], iv[3]);
+            *reinterpret_cast<float4*>(gr + H + 4 * q) = make_float4(fv[0], fv[1], fv[2], fv[3]);
+            *reinterpret_cast<float4*>(gr + 2 * H + 4 * q) = make_float4(gv[0], gv[1], gv[2], gv[3]);
+            *reinterpret_cast<float4*>(gr + 3 * H + 4 * q) = make_float4(ov[0], ov[1], ov[2], ov[3]);
+          }
+        }
+        continue;
+      }
 #pragma unroll
       for (int j = 0; j < 16; ++j) {
         const int c = u0 + c0 + j;

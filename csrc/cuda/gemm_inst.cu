@@ -172,14 +172,36 @@ static bool launch_packed(const A& a, const B& b, const E& e, const GemmShape& s
     cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     configured |= (1ull << device);
   }
-  launch_pack<kBM>(a, ws, sh.M, sh.m_dev, sh.K, device, st);
-  launch_pack<B_ROWS>(b, ws + abytes, sh.N, nullptr, sh.K, device, st);
-  const int tiles_m = (sh.M + kBM - 1) / kBM;
-  const int tiles_n = (sh.N + B_ROWS - 1) / B_ROWS;
-  const int total = tiles_m * tiles_n * std::max(1, sh.ksplit);
-  const int grid = std::min(total, num_sms(device));
+  // one launch packs both operands; the GEMM is launched with programmatic
+  // stream serialisation so its prologue (barriers, TMEM) overlaps the packing
+  const int nchunks = (sh.K + kBK - 1) / kBK;
+  const int tiles_a = (sh.M + kBM - 1) / kBM;
+  const int tiles_b = (sh.N + B_ROWS - 1) / B_ROWS;
+  const int64_t va = static_cast<int64_t>(tiles_a) * nchunks * kBM * 8;
+  const int64_t vb = static_cast<int64_t>(tiles_b) * nchunks * B_ROWS * 8;
+  const int cap = num_sms(device) * 16;
+  const int blocks_a = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>((va + 255) / 256, cap)));
+  const int blocks_b = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>((vb + 255) / 256, cap / 2)));
   count_launch();
-  kern<<<grid, kPackedThreads, smem, st>>>(ws, ws + abytes, e, sh, device_status_ptr(device));
+  pack2_kernel<kBM, A, B_ROWS, B><<<blocks_a + blocks_b, 256, 0, st>>>(a, b, ws, ws + abytes, tiles_a, tiles_b, nchunks,
+                                                                      sh.M, sh.m_dev, sh.N, blocks_a);
+  const int total = tiles_a * tiles_b * std::max(1, sh.ksplit);
+  const int grid = std::min(total, num_sms(device));
+  const uint8_t* pa = ws;
+  const uint8_t* pb = ws + abytes;
+  int* status = device_status_ptr(device);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(kPackedThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  count_launch();
+  cudaLaunchKernelEx(&cfg, kern, pa, pb, e, sh, status);
   return true;
 }
 

@@ -108,6 +108,12 @@ void launch_tgn_metrics(dim3 grid, dim3 block, cudaStream_t st, const float* __r
 void gemm(const SegSource& a, const WeightSource& b, const EpiLSTM& e, const GemmShape& sh, cudaStream_t st);
 void launch_spmm_csr(cudaStream_t st, const int64_t* rowptr, const int* col, const float* val, const float* x,
                      int64_t n_rows, int F, float* out, int accumulate);
+void launch_spmm_peer_gather(cudaStream_t st, const int64_t* rowptr, const int* col, const float* val,
+                             const float* const* peers, const int* src_owner, const int* src_row, int64_t n_rows,
+                             int F, float* out);
+void launch_spmm_peer_push(cudaStream_t st, const int64_t* rowptr_t, const int* col_t, const float* val_t,
+                           const float* grad_dst, int64_t n_src, int F, float* const* peers, const int* src_owner,
+                           const int* src_row);
 void launch_lstm_bwd(cudaStream_t st, const float* gates, const float* c_prev, const float* c_new, const float* dh,
                      const float* dc, int64_t rows, int H, float* dpre, float* dc_prev);
 

@@ -75,16 +75,18 @@ inline size_t packed_bytes(int mn, int k, int rows_per_tile) {
 //   K-major : row = t*ROWS + g*8 + r8, columns [kc*64 + kv*8, +8)
 //   MN-major: MN group t*ROWS/8 + g (8 consecutive MN indices), k = kc*64 + kv*8 + r8
 // both land at block(t, kc) + g*1024 + kv*128 + r8*16.
+// Programmatic dependent launch: a kernel launched with the programmatic-
+// serialisation attribute may start while its predecessor drains; it waits
+// here before touching anything the predecessor writes. Kernels let their
+// dependents start early once their last loads are issued.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" :::); }
+
 template <int ROWS, class Src>
-__global__ void __launch_bounds__(256) pack_kernel(const __grid_constant__ Src src, uint8_t* __restrict__ out,
-                                                   int tiles, int nchunks, int limit, const int* limit_dev,
-                                                   int nrows) {
-  int lim = limit;
-  if (limit_dev != nullptr) lim = min(lim, *limit_dev);
-  (void)nrows;
+__device__ __forceinline__ void pack_range(const Src& src, uint8_t* __restrict__ out, int tiles, int nchunks,
+                                           int lim, int64_t first, int64_t stride) {
   const int64_t total = static_cast<int64_t>(tiles) * nchunks * (ROWS / 8) * 64;
-  const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
-  for (int64_t idx = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; idx < total; idx += stride) {
+  for (int64_t idx = first; idx < total; idx += stride) {
     const int r8 = static_cast<int>(idx & 7);
     const int kv = static_cast<int>((idx >> 3) & 7);
     int64_t rest = idx >> 6;
@@ -106,6 +108,46 @@ __global__ void __launch_bounds__(256) pack_kernel(const __grid_constant__ Src s
     *reinterpret_cast<uint4*>(out + (static_cast<int64_t>(t) * nchunks + kc) * (ROWS * 128) + g * 1024 + kv * 128 +
                               r8 * 16) = pack_bf16x8(f);
   }
+}
+
+// One thread = one 16-byte vector (8 bf16) of the packed image.
+// Vector index -> (tile t, chunk kc, 8-row group g, k-vector kv, r8):
+//   K-major : row = t*ROWS + g*8 + r8, columns [kc*64 + kv*8, +8)
+//   MN-major: MN group t*ROWS/8 + g (8 consecutive MN indices), k = kc*64 + kv*8 + r8
+// both land at block(t, kc) + g*1024 + kv*128 + r8*16.
+template <int ROWS, class Src>
+__global__ void __launch_bounds__(256) pack_kernel(const __grid_constant__ Src src, uint8_t* __restrict__ out,
+                                                   int tiles, int nchunks, int limit, const int* limit_dev,
+                                                   int nrows) {
+  pdl_wait();
+  int lim = limit;
+  if (limit_dev != nullptr) lim = min(lim, *limit_dev);
+  (void)nrows;
+  pack_range<ROWS>(src, out, tiles, nchunks, lim,
+                   static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x,
+                   static_cast<int64_t>(gridDim.x) * blockDim.x);
+  pdl_launch_dependents();
+}
+
+// Both operands of one GEMM in one launch: blocks [0, blocks_a) pack A, the rest pack B.
+template <int ROWS_A, class SrcA, int ROWS_B, class SrcB>
+__global__ void __launch_bounds__(256) pack2_kernel(const __grid_constant__ SrcA a, const __grid_constant__ SrcB b,
+                                                    uint8_t* __restrict__ out_a, uint8_t* __restrict__ out_b,
+                                                    int tiles_a, int tiles_b, int nchunks, int lim_a,
+                                                    const int* lim_a_dev, int lim_b, int blocks_a) {
+  pdl_wait();
+  if (static_cast<int>(blockIdx.x) < blocks_a) {
+    int lim = lim_a;
+    if (lim_a_dev != nullptr) lim = min(lim, *lim_a_dev);
+    pack_range<ROWS_A>(a, out_a, tiles_a, nchunks, lim, static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x,
+                       static_cast<int64_t>(blocks_a) * blockDim.x);
+  } else {
+    const int bb = static_cast<int>(blockIdx.x) - blocks_a;
+    const int nb = static_cast<int>(gridDim.x) - blocks_a;
+    pack_range<ROWS_B>(b, out_b, tiles_b, nchunks, lim_b, static_cast<int64_t>(bb) * blockDim.x + threadIdx.x,
+                       static_cast<int64_t>(nb) * blockDim.x);
+  }
+  pdl_launch_dependents();
 }
 
 template <int BN, int NSUB, bool AMN, bool BMN, class Epi>
@@ -163,6 +205,7 @@ __global__ void __launch_bounds__(kPackedThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  pdl_wait();  // the prologue above overlapped the pack kernel; its images are complete from here on
 
   int M = shape.M;
   if (shape.m_dev != nullptr) M = min(M, *shape.m_dev);

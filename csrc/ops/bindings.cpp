@@ -103,6 +103,13 @@ void tgn_peer_mail_write(const at::Tensor& roots, const at::Tensor& n_roots, con
                          const at::Tensor& owner, const at::Tensor& claim_ptrs, const at::Tensor& mail_ptrs,
                          const at::Tensor& mail_ts_ptrs);
 
+at::Tensor spmm_peer_gather(const at::Tensor& rowptr, const at::Tensor& col, const at::Tensor& val,
+                            const at::Tensor& peers, const at::Tensor& src_owner, const at::Tensor& src_row,
+                            int64_t n_rows, int64_t F);
+void spmm_peer_push(const at::Tensor& rowptr_t, const at::Tensor& col_t, const at::Tensor& val_t,
+                    const at::Tensor& grad_dst, int64_t n_src, const at::Tensor& peers, const at::Tensor& src_owner,
+                    const at::Tensor& src_row);
+
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "starry_unigraph sm_100a kernels (tcgen05 GEMMs, TGN step, DTDG ops, collectives)";
   m.def("status_read", &status_read, "read (and clear) the device status word", py::arg("clear") = true);
@@ -132,6 +139,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("tgn_peer_mail_claim", &tgn_peer_mail_claim);
   m.def("tgn_peer_mail_write", &tgn_peer_mail_write);
   m.def("spmm_csr", &spmm_csr);
+  m.def("spmm_peer_gather", &spmm_peer_gather);
+  m.def("spmm_peer_push", &spmm_peer_push);
   m.def("lstm_fwd", &lstm_fwd);
   m.def("lstm_bwd", &lstm_bwd);
 }

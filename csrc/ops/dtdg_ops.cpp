@@ -175,3 +175,34 @@ std::vector<at::Tensor> lstm_bwd(const at::Tensor& x, const c10::optional<at::Te
   SU_LAUNCH_CHECK();
   return {dxh.narrow(1, 0, in_dim), dxh.narrow(1, in_dim, H), dc_prev};
 }
+
+// ---------------------------------------------------------------------------
+// NVLink halo path (see starry_unigraph/parallel/halo.py): aggregation whose
+// source rows are read from the owners' staging buffers, and its backward
+// pushing source-row gradients into the owners' gradient buffers.
+// ---------------------------------------------------------------------------
+at::Tensor spmm_peer_gather(const at::Tensor& rowptr, const at::Tensor& col, const at::Tensor& val,
+                            const at::Tensor& peers, const at::Tensor& src_owner, const at::Tensor& src_row,
+                            int64_t n_rows, int64_t F) {
+  SU_CHECK_I64(rowptr); SU_CHECK_I32(col); SU_CHECK_F32(val); SU_CHECK_I32(src_owner); SU_CHECK_I32(src_row);
+  TORCH_CHECK(peers.is_cuda() && peers.scalar_type() == at::kLong, "peer table must be cuda int64");
+  at::Tensor out = at::empty({n_rows, F}, val.options());
+  launch_spmm_peer_gather(cur_stream(), rowptr.data_ptr<int64_t>(), col.data_ptr<int>(), val.data_ptr<float>(),
+                          reinterpret_cast<const float* const*>(peers.data_ptr<int64_t>()),
+                          src_owner.data_ptr<int>(), src_row.data_ptr<int>(), n_rows, static_cast<int>(F),
+                          out.data_ptr<float>());
+  SU_LAUNCH_CHECK();
+  return out;
+}
+
+void spmm_peer_push(const at::Tensor& rowptr_t, const at::Tensor& col_t, const at::Tensor& val_t,
+                    const at::Tensor& grad_dst, int64_t n_src, const at::Tensor& peers, const at::Tensor& src_owner,
+                    const at::Tensor& src_row) {
+  SU_CHECK_F32(grad_dst); SU_CHECK_CONTIG(grad_dst);
+  TORCH_CHECK(peers.is_cuda() && peers.scalar_type() == at::kLong, "peer table must be cuda int64");
+  launch_spmm_peer_push(cur_stream(), rowptr_t.data_ptr<int64_t>(), col_t.data_ptr<int>(), val_t.data_ptr<float>(),
+                        grad_dst.data_ptr<float>(), n_src, static_cast<int>(grad_dst.size(1)),
+                        reinterpret_cast<float* const*>(peers.data_ptr<int64_t>()), src_owner.data_ptr<int>(),
+                        src_row.data_ptr<int>());
+  SU_LAUNCH_CHECK();
+}

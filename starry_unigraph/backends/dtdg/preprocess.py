@@ -95,7 +95,12 @@ class FlareDTDGPreprocessor(BaseDTDGPreprocessor):
                    ArtifactOutput("flare/manifest.json", {"pipeline": "flare_native", "num_parts": len(parts),
                                                           "files": [f"part_{i:03d}.pth" for i in range(len(parts))]})]
         outputs += [ArtifactOutput(f"flare/part_{i:03d}.pth", p, serializer="torch") for i, p in enumerate(parts)]
-        return self.emit_artifacts(ctx, ArtifactPayload(provider_meta=self._provider_meta(ctx, plan), outputs=outputs))
+        # global node -> partition map (the NVLink halo path addresses peer rows with it)
+        outputs.append(ArtifactOutput("partitions/node_parts.pt",
+                                      ctx.provider_state["partition_result"]["node_parts"].long(), "torch"))
+        meta = self._provider_meta(ctx, plan)
+        meta["has_node_parts"] = True
+        return self.emit_artifacts(ctx, ArtifactPayload(provider_meta=meta, outputs=outputs))
 
 
 __all__ = ["FlareDTDGPreprocessor", "BaseDTDGPreprocessor", "validate_artifacts", "load_prepared_from_disk",

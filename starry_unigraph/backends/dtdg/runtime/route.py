@@ -7,12 +7,11 @@ many halo rows arrive from each peer (``recv_sizes``). ``forward(x)`` returns
 ``[x ; received halo rows]``; its backward sends the halo-row gradients back
 and scatter-adds them into the owners' rows.
 
-Two transports:
-  * ``nccl``: ``all_to_all_single`` (the reference's collective; baseline),
-  * ``p2p``: the peer-memory kernels of ``starry_unigraph.parallel.halo``
-    (peers read the rows they need straight from the owner's HBM over NVLink
-    and push gradients back with remote atomic adds), selected by
-    ``comm.path: p2p`` when symmetric memory is available.
+``Route.forward`` is the collective transport (``all_to_all_single``, the
+reference's; the baseline). With ``comm.path: p2p`` on CUDA the GCN layers do
+not call it: ``starry_unigraph.parallel.halo.halo_aggregate`` reads the halo
+rows from the owners' memory inside the aggregation kernel and pushes their
+gradients back with remote atomic adds.
 
 ``Route.from_graph`` partitions a global edge list into per-partition blocks
 (edges owned by the destination's partition, halo = remote sources).
@@ -143,10 +142,6 @@ class RouteExchange(autograd.Function):
         if not dist.is_available() or not dist.is_initialized():
             raise RuntimeError("torch.distributed must be initialized before using Route.forward")
         ctx.route, ctx.reverse, ctx.group = route, reverse, group
-        if _TRANSPORT["path"] == "p2p":
-            from starry_unigraph.parallel.halo import halo_forward
-
-            return halo_forward(x.detach(), route, group)
         send = x.detach()[route.send_index]
         recv = torch.empty(route.recv_len, *x.shape[1:], dtype=x.dtype, device=x.device)
         _a2a(recv, send.contiguous(), route.recv_sizes, route.send_sizes, group)
@@ -155,10 +150,6 @@ class RouteExchange(autograd.Function):
     @staticmethod
     def backward(ctx, grad: torch.Tensor):
         route = ctx.route
-        if _TRANSPORT["path"] == "p2p":
-            from starry_unigraph.parallel.halo import halo_backward
-
-            return halo_backward(grad, route, ctx.group), None, None, None
         n_local = grad.size(0) - route.recv_len
         gx = grad[:n_local].clone()
         back = torch.empty(route.send_len, *grad.shape[1:], dtype=grad.dtype, device=grad.device)

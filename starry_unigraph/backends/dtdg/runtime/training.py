@@ -58,12 +58,9 @@ class FlareOptimizer:
             self.flat = FlatParams([model], device)
             self.opt = FusedAdam(self.flat, lr=lr)
             if self.world > 1 and comm_path == "p2p":
-                try:
-                    from starry_unigraph.parallel.allreduce import PeerAllReduce
+                from starry_unigraph.parallel.allreduce import PeerAllReduceAdam
 
-                    self._allreduce = PeerAllReduce(self.flat.grad.numel(), device)
-                except Exception as exc:  # symmetric memory unavailable -> NCCL baseline
-                    print(f"[starry_unigraph] peer all-reduce unavailable ({exc}); using NCCL")
+                self._allreduce = PeerAllReduceAdam(self.flat, self.opt, device)
         else:
             self.opt = torch.optim.Adam(model.parameters(), lr=lr)
         self.param_groups = self.opt.param_groups
@@ -76,12 +73,12 @@ class FlareOptimizer:
 
     def step(self) -> None:
         if self.cuda:
+            if self._allreduce is not None:  # fused NVLink all-reduce + Adam
+                self._allreduce.step()
+                return
             scale = 1.0
             if self.world > 1:
-                if self._allreduce is not None:
-                    self._allreduce(self.flat.grad)
-                else:
-                    dist.all_reduce(self.flat.grad)
+                dist.all_reduce(self.flat.grad)
                 scale = 1.0 / self.world
             self.opt.step(grad_scale=scale)
         else:

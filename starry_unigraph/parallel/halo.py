@@ -1,0 +1,126 @@
+"""DTDG halo exchange fused into the neighbour aggregation over NVLink
+(reference: Route.forward = all_to_all of boundary rows, then DGL SpMM,
+backends/dtdg/runtime/route.py:297-322, runtime/modules/gcn_layers.py:62-94).
+
+Every rank copies its layer input rows into a symmetric staging buffer; after a
+bounded device barrier the aggregation kernel reads each source row from its
+owner's buffer directly (local rows from its own), so no halo tensor is ever
+materialised and no collective runs. Backward runs the transposed aggregation
+and pushes each source row's gradient into the owner's gradient buffer with
+remote atomic adds; after a barrier each rank takes its rows out.
+
+Staging and gradient buffers alternate between two copies, so a rank may start
+writing call k+1 while a slower peer still reads call k: a buffer is reused
+two calls later, after a barrier that every peer passes only once it finished
+reading it.
+"""
+from __future__ import annotations
+
+import torch
+import torch.autograd as autograd
+import torch.distributed as dist
+
+from starry_unigraph.data.partition import NID
+from starry_unigraph.ops import cuda_ext
+from starry_unigraph.parallel.ctdg_peer import DEFAULT_BARRIER_BUDGET
+from starry_unigraph.parallel.symmetric import SymmetricArena
+
+
+class PeerHaloContext:
+    def __init__(self, node_parts: torch.Tensor, features: int, device: torch.device,
+                 group: dist.ProcessGroup | None = None, barrier_budget: int = DEFAULT_BARRIER_BUDGET):
+        self.device = torch.device(device)
+        node_parts = node_parts.long().cpu()
+        world = dist.get_world_size(group)
+        counts = torch.bincount(node_parts, minlength=world)
+        max_rows = int(counts.max()) if counts.numel() else 1
+        self.F = int(features)
+        specs = {f"x{i}": ((max_rows, self.F), torch.float32) for i in range(2)}
+        specs.update({f"g{i}": ((max_rows, self.F), torch.float32) for i in range(2)})
+        specs["flags"] = ((32,), torch.int64)
+        self.arena = SymmetricArena(specs, self.device, group)
+        self.rank, self.world = self.arena.rank, self.arena.world_size
+        for n in ("x0", "x1", "g0", "g1", "flags"):
+            self.arena[n].zero_()
+        self.tables = {n: self.arena.peer_table(n) for n in specs}
+        # owner and row-in-owner of every global node (rows of a partition follow ascending node id)
+        local_index = torch.empty_like(node_parts)
+        for q in range(world):
+            ids = torch.nonzero(node_parts == q).view(-1)
+            local_index[ids] = torch.arange(ids.numel())
+        self.owner = node_parts.to(self.device, torch.int32)
+        self.local_index = local_index.to(self.device, torch.int32)
+        self.epoch = torch.zeros(1, dtype=torch.int64, device=self.device)
+        self.budget = int(barrier_budget)
+        self.fwd_calls = 0
+        self.bwd_calls = 0
+        self._C = cuda_ext()
+        torch.cuda.synchronize(self.device)
+        self.arena.barrier_host()
+
+    def barrier(self) -> None:
+        self._C.peer_barrier(self.tables["flags"], self.rank, self.world, self.epoch, self.budget)
+
+    def src_maps(self, graph) -> tuple[torch.Tensor, torch.Tensor]:
+        gid = graph.srcdata[NID].to(self.device).long()
+        return self.owner[gid].contiguous(), self.local_index[gid].contiguous()
+
+
+class _HaloAggregate(autograd.Function):
+    @staticmethod
+    def forward(ctx, x_local: torch.Tensor, graph, hc: PeerHaloContext):
+        C = hc._C
+        buf = f"x{hc.fwd_calls % 2}"
+        hc.fwd_calls += 1
+        n_local, F = x_local.shape
+        if F > hc.F:
+            raise ValueError(f"halo staging holds {hc.F} features, got {F}")
+        stage = hc.arena[buf]
+        if F == hc.F:
+            stage[:n_local].copy_(x_local)
+        else:  # narrower layer: rows of F values at the buffer's stride would break the kernel's row math
+            raise ValueError("halo staging buffers are sized for one feature width")
+        hc.barrier()
+        csr = graph.csr()
+        owner, row = hc.src_maps(graph)
+        out = C.spmm_peer_gather(csr["rowptr"], csr["col"], csr["val"], hc.tables[buf], owner, row,
+                                 graph.num_dst_nodes, F)
+        ctx.hc, ctx.graph, ctx.n_local = hc, graph, n_local
+        ctx.save_for_backward(owner, row)
+        return out
+
+    @staticmethod
+    def backward(ctx, grad: torch.Tensor):
+        hc = ctx.hc
+        C = hc._C
+        owner, row = ctx.saved_tensors
+        buf = f"g{hc.bwd_calls % 2}"
+        hc.bwd_calls += 1
+        csr = ctx.graph.csr()
+        C.spmm_peer_push(csr["rowptr_t"], csr["col_t"], csr["val_t"], grad.contiguous(), ctx.graph.num_src_nodes,
+                         hc.tables[buf], owner, row)
+        hc.barrier()
+        g = hc.arena[buf]
+        gx = g[: ctx.n_local].clone()
+        g[: ctx.n_local].zero_()  # ready for its next use, two calls later
+        return gx, None, None
+
+
+_CONTEXT: dict[str, PeerHaloContext | None] = {"ctx": None}
+
+
+def set_halo_context(hc: PeerHaloContext | None) -> None:
+    _CONTEXT["ctx"] = hc
+
+
+def get_halo_context() -> PeerHaloContext | None:
+    return _CONTEXT["ctx"]
+
+
+def halo_aggregate(graph, x_local: torch.Tensor) -> torch.Tensor:
+    """Normalised neighbour sum of `graph` whose halo source rows come from the
+    peers' staging buffers (requires an active PeerHaloContext)."""
+    hc = _CONTEXT["ctx"]
+    if hc is None:
+        raise RuntimeError("no PeerHaloContext is active")
+    return _HaloAggregate.apply(x_local.float().contiguous(), graph, hc)

@@ -37,6 +37,10 @@ def _gcn_message_pass(graph, x: torch.Tensor) -> torch.Tensor:
     elif x.size(0) == graph.num_dst_nodes:
         route = getattr(graph, "route", None)
         if route is not None and route.send_index is not None and dist.is_available() and dist.is_initialized():
+            from starry_unigraph.parallel.halo import get_halo_context, halo_aggregate
+
+            if x.is_cuda and get_halo_context() is not None:  # halo read from peers inside the aggregation
+                return halo_aggregate(graph, x)
             src_x = route.forward(x)
         else:
             extra = graph.num_src_nodes - graph.num_dst_nodes

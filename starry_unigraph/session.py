@@ -147,6 +147,7 @@ class SchedulerSession:
                 config=self.ctx.config)
             self.runtime = RuntimeBundle(state={"graph_mode": "dtdg"})
             init_flare_training(runtime=self.runtime, session_ctx=self.ctx, partition_data=part, device=device)
+            self._maybe_peer_halo(device)
             self.runtime.state.update({"flare_partition_path": str(path),
                                        "window_state": self.snapshot_core.describe_window_state(),
                                        "snapshot_state": self.snapshot_core.dump_state(),
@@ -167,6 +168,29 @@ class SchedulerSession:
         else:
             raise ValueError(f"Unknown graph_mode: {mode}")
         return self.runtime
+
+    def _maybe_peer_halo(self, device: str) -> None:
+        """Multi-GPU DTDG with ``comm.path: p2p``: halo rows are read from peer memory
+        inside the aggregation kernel (starry_unigraph.parallel.halo)."""
+        from starry_unigraph.parallel.halo import PeerHaloContext, set_halo_context
+
+        set_halo_context(None)
+        if not (self.ctx.dist.is_distributed and dist.is_initialized() and str(device).startswith("cuda")):
+            return
+        if str(self.ctx.config.get("comm", {}).get("path", "p2p")) != "p2p":
+            return
+        decay = self.ctx.config.get("dtdg", {}).get("chunk_decay")
+        if decay not in (None, "all", "null", 0):
+            # chunk decay truncates older window graphs per partition, so peers' row numbering
+            # differs from the full partition's: keep the collective route for those runs
+            return
+        path = self.prepared.directories.get("partitions", self.ctx.artifact_root / "partitions") / "node_parts.pt"
+        if not path.exists():
+            return
+        node_parts = torch.load(path, weights_only=True)
+        hc = PeerHaloContext(node_parts, int(self.ctx.config["model"]["hidden_dim"]), torch.device(device))
+        set_halo_context(hc)
+        self.runtime.state["halo"] = {"transport": "nvlink_p2p", "world": hc.world, "features": hc.F}
 
     def build_pipeline_engine(self, model: Any = None):
         from starry_unigraph.runtime.backend_adapters import (ChunkGraphBackend, CTDGGraphBackend,

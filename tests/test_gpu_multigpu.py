@@ -11,19 +11,20 @@ import torch
 pytestmark = pytest.mark.gpu
 ROOT = Path(__file__).resolve().parents[1]
 WORKER = ROOT / "tests" / "workers" / "ctdg_peer_worker.py"
+DTDG_WORKER = ROOT / "tests" / "workers" / "dtdg_peer_worker.py"
 
 need2 = pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2,
                            reason="needs 2 GPUs")
 
 
-def _run(out, nproc, *args):
+def _run(out, nproc, *args, worker=WORKER, port=29613):
     env = dict(os.environ)
     env.setdefault("NCCL_NVLS_ENABLE", "0")
     if nproc == 1:
-        cmd = [sys.executable, str(WORKER), "--out", str(out), *args]
+        cmd = [sys.executable, str(worker), "--out", str(out), *args]
     else:
         cmd = ["timeout", "-k", "30", "600", sys.executable, "-m", "torch.distributed.run", "--nnodes=1",
-               f"--nproc-per-node={nproc}", "--master-addr", "127.0.0.1", "--master-port", "29613", str(WORKER),
+               f"--nproc-per-node={nproc}", "--master-addr", "127.0.0.1", "--master-port", str(port), str(worker),
                "--out", str(out), *args]
     r = subprocess.run(cmd, cwd=ROOT, env=env, capture_output=True, text=True, timeout=900)
     assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-6000:]
@@ -59,3 +60,19 @@ def test_hash_partition_two_ranks_consistent(tmp_path):
     assert touched.any()
     assert not (r1["memory_ts"][owner == 0] >= 0).any()
     assert not (r0["memory_ts"][owner == 1] >= 0).any()
+
+
+@need2
+def test_dtdg_nvlink_halo_matches_nccl_route(tmp_path):
+    """MPNN-LSTM over 2 partitions: halo read from peer memory inside the
+    aggregation + fused all-reduce/Adam must track the NCCL route + all-reduce."""
+    _run(tmp_path, 2, "--path", "nccl", worker=DTDG_WORKER, port=29631)
+    _run(tmp_path, 2, "--path", "p2p", worker=DTDG_WORKER, port=29632)
+    for r in (0, 1):
+        a = torch.load(tmp_path / f"dtdg_p2p_r{r}.pt")
+        b = torch.load(tmp_path / f"dtdg_nccl_r{r}.pt")
+        assert a["halo"] is not None and b["halo"] is None
+        torch.testing.assert_close(torch.tensor(a["losses"]), torch.tensor(b["losses"]), rtol=2e-3, atol=1e-5)
+        torch.testing.assert_close(a["params"], b["params"], rtol=2e-3, atol=2e-5)
+    # replicas identical under the fused all-reduce
+    assert torch.equal(torch.load(tmp_path / "dtdg_p2p_r0.pt")["params"], torch.load(tmp_path / "dtdg_p2p_r1.pt")["params"])
