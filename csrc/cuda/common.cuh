@@ -242,6 +242,15 @@ __device__ __forceinline__ float warp_max(float v) {
 }
 
 __device__ __forceinline__ float sigmoidf_(float x) { return 1.f / (1.f + expf(-x)); }
+// Gate activations of the fused RNN-cell epilogues: the hardware exp2 and
+// reciprocal units (__expf, __frcp_rn) and tanh.approx.f32 (max relative error
+// about 2^-11, finer than the bf16 rounding of the GEMM operands feeding them).
+__device__ __forceinline__ float sigmoid_fast(float x) { return __frcp_rn(1.f + __expf(-x)); }
+__device__ __forceinline__ float tanh_fast(float x) {
+  float y;
+  asm("tanh.approx.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
 
 // Pack 8 floats to 8 bf16 (one 16-byte vector).
 __device__ __forceinline__ uint4 pack_bf16x8(const float* f) {

@@ -16,7 +16,9 @@ constexpr uint32_t kStreamOutDrop = 0x0D7D0u;
 // (PyTorch GRU gate convention). Produces h' = (1 - z) * n + z * h.
 // ---------------------------------------------------------------------------
 struct EpiGRU {
-  static constexpr bool kSplitCols = false;  // a tile's gate groups of one unit must meet in one thread
+  // a unit's four gate columns must meet in one thread: with gate groups of 16
+  // units, each half of a 128-column tile holds whole groups, so two warps split it
+  static constexpr bool kSplitCols = true;
   static constexpr int kScratchBytes = 0;
   int D = 0, DP = 0;  // DP = gate group width G: tile columns are [r | z | n_i | n_h] x G units
   const float* b_ih = nullptr;   // [3D]
@@ -36,8 +38,12 @@ struct EpiGRU {
   const float* ts_value = nullptr;
 
 #ifdef __CUDACC__
-  __device__ __forceinline__ void operator()(int row, bool valid, int n0, uint32_t taddr, int /*tile_cols*/) const {
-    const int u0 = (n0 / (4 * DP)) * DP;  // first hidden unit of this tile
+  // every gate group of 4*DP columns in the range this thread was given
+  __device__ __forceinline__ void operator()(int row, bool valid, int n0, uint32_t taddr, int tile_cols) const {
+    for (int g0 = 0; g0 < tile_cols; g0 += 4 * DP) group(row, valid, n0 + g0, taddr + g0);
+  }
+  __device__ __forceinline__ void group(int row, bool valid, int n0, uint32_t taddr) const {
+    const int u0 = (n0 / (4 * DP)) * DP;  // first hidden unit of this group
     const float* hp = nullptr;
     if (valid && hprev != nullptr) {
       const int64_t hr = hprev_index ? hprev_index[row] : row;
@@ -57,9 +63,9 @@ struct EpiGRU {
         const int c = u0 + c0 + i;
         if (c >= D) break;
         const float h = hp ? hp[c] : 0.f;
-        const float rg = sigmoidf_(r[i] + b_ih[c] + b_hh[c]);
-        const float zg = sigmoidf_(z[i] + b_ih[D + c] + b_hh[D + c]);
-        const float ng = tanhf(ni[i] + b_ih[2 * D + c] + rg * (nh[i] + b_hh[2 * D + c]));
+        const float rg = sigmoid_fast(r[i] + b_ih[c] + b_hh[c]);
+        const float zg = sigmoid_fast(z[i] + b_ih[D + c] + b_hh[D + c]);
+        const float ng = tanh_fast(ni[i] + b_ih[2 * D + c] + rg * (nh[i] + b_hh[2 * D + c]));
         const float hn = (1.f - zg) * ng + zg * h;
         if (save_prev) save_prev[(int64_t)row * D + c] = h;
         if (hout) hout[(int64_t)row * hout_ld + c] = hn;
@@ -173,7 +179,7 @@ namespace su {
 // over [x || h]). i, f, o = sigmoid, g = tanh, c' = f c + i g, h' = o tanh(c').
 // Saves the post-activation gates for the backward pass.
 struct EpiLSTM {
-  static constexpr bool kSplitCols = false;
+  static constexpr bool kSplitCols = true;  // gate groups of 16 units (see EpiGRU)
   static constexpr int kScratchBytes = 0;
   int H = 0, DP = 0;  // DP = gate group width G: tile columns are [i | f | g | o] x G units
   const float* b_i = nullptr;
@@ -186,7 +192,11 @@ struct EpiLSTM {
   float* gates = nullptr;         // [rows, 4H] (i, f, g, o) post-activation, optional
 
 #ifdef __CUDACC__
-  __device__ __forceinline__ void operator()(int row, bool valid, int n0, uint32_t taddr, int /*tc*/) const {
+  // every gate group of 4*DP columns in the range this thread was given
+  __device__ __forceinline__ void operator()(int row, bool valid, int n0, uint32_t taddr, int tile_cols) const {
+    for (int g0 = 0; g0 < tile_cols; g0 += 4 * DP) group(row, valid, n0 + g0, taddr + g0);
+  }
+  __device__ __forceinline__ void group(int row, bool valid, int n0, uint32_t taddr) const {
     const int u0 = (n0 / (4 * DP)) * DP;
     for (int c0 = 0; c0 < DP; c0 += 16) {
       float gi[16], gf[16], gg[16], go[16];
@@ -211,12 +221,12 @@ struct EpiLSTM {
 #pragma unroll
           for (int u = 0; u < 4; ++u) {
             const int j = 4 * q + u, c = cb + j;
-            iv[u] = sigmoidf_(gi[j] + b_i[c]);
-            fv[u] = sigmoidf_(gf[j] + b_f[c]);
-            gv[u] = tanhf(gg[j] + b_g[c]);
-            ov[u] = sigmoidf_(go[j] + b_o[c]);
+            iv[u] = sigmoid_fast(gi[j] + b_i[c]);
+            fv[u] = sigmoid_fast(gf[j] + b_f[c]);
+            gv[u] = tanh_fast(gg[j] + b_g[c]);
+            ov[u] = sigmoid_fast(go[j] + b_o[c]);
             cn[u] = fv[u] * cpv[u] + iv[u] * gv[u];
-            hn[u] = ov[u] * tanhf(cn[u]);
+            hn[u] = ov[u] * tanh_fast(cn[u]);
           }
           *reinterpret_cast<float4*>(c_out + rb + 4 * q) = make_float4(cn[0], cn[1], cn[2], cn[3]);
           *reinterpret_cast<float4*>(h_out + rb + 4 * q) = make_float4(hn[0], hn[1], hn[2], hn[3]);
@@ -233,14 +243,14 @@ struct EpiLSTM {
       for (int j = 0; j < 16; ++j) {
         const int c = u0 + c0 + j;
         if (c >= H) break;
-        const float i = sigmoidf_(gi[j] + b_i[c]);
-        const float f = sigmoidf_(gf[j] + b_f[c]);
-        const float g = tanhf(gg[j] + b_g[c]);
-        const float o = sigmoidf_(go[j] + b_o[c]);
+        const float i = sigmoid_fast(gi[j] + b_i[c]);
+        const float f = sigmoid_fast(gf[j] + b_f[c]);
+        const float g = tanh_fast(gg[j] + b_g[c]);
+        const float o = sigmoid_fast(go[j] + b_o[c]);
         const float cp = c_prev ? c_prev[(int64_t)row * H + c] : 0.f;
         const float cn = f * cp + i * g;
         c_out[(int64_t)row * H + c] = cn;
-        h_out[(int64_t)row * H + c] = o * tanhf(cn);
+        h_out[(int64_t)row * H + c] = o * tanh_fast(cn);
         if (gates) {
           float* gr = gates + (int64_t)row * 4 * H;
           gr[c] = i;
@@ -255,92 +265,4 @@ struct EpiLSTM {
 };
 
 
-// ---------------------------------------------------------------------------
-// time-encoder gradient epilogue: the accumulator holds dT = d(loss)/d cos(w t + b)
-// for a tile of rows; the epilogue reduces it straight into the encoder's
-// parameter gradients (no dT buffer):
-//   db[c] += sum_rows -sin(w[c] t + b[c]) dT[row, c],   dw[c] += same * t
-// Rows are reduced over each warp with shuffles, then one atomic per warp.
-// ---------------------------------------------------------------------------
-struct EpiTimeGrad {
-  static constexpr bool kSplitCols = true;
-  // per 128-thread epilogue group: two [16 columns][132] fp32 staging arrays
-  static constexpr int kScratchStride = 132;
-  static constexpr int kScratchBytes = 2 * 16 * kScratchStride * 4;
-  int T = 0;
-  const float* t = nullptr;  // per-row time input (nullptr: t = 0, only db gets contributions)
-  const float* w = nullptr;
-  const float* b = nullptr;
-  float* dw = nullptr;
-  float* db = nullptr;
-
-#ifdef __CUDACC__
-  __device__ __forceinline__ void operator()(int row, bool valid, int n0, uint32_t taddr, int tile_cols) const {
-    const float tr = (valid && t != nullptr) ? t[row] : 0.f;
-    const int lane = threadIdx.x & 31;
-    const int lim = min(T - n0, tile_cols);
-    for (int c0 = 0; c0 < lim; c0 += 16) {
-      float v[16];
-      tmem_ld16(taddr + c0, v);
-#pragma unroll
-      for (int i = 0; i < 16; ++i) {
-        const int c = n0 + c0 + i;
-        if (c0 + i >= lim) break;  // uniform across the warp
-        const float g = valid ? -sin_phase(w[c], tr, b[c]) * v[i] : 0.f;
-        float gb = g, gw = g * tr;
-#pragma unroll
-        for (int off = 16; off > 0; off >>= 1) {
-          gb += __shfl_xor_sync(0xffffffffu, gb, off);
-          gw += __shfl_xor_sync(0xffffffffu, gw, off);
-        }
-        if (lane == 0) {
-          atomicAdd(&db[c], gb);
-          if (t != nullptr) atomicAdd(&dw[c], gw);
-        }
-      }
-    }
-  }
-
-  // Same result with the 128 rows of a tile reduced through shared memory
-  // (16 columns at a time; 8 threads per column) instead of per-column warp
-  // shuffles. All 128 threads of the group (barrier `bar_id`) take part.
-  __device__ __forceinline__ void run(int row, bool valid, int n0, uint32_t taddr, int tile_cols, float* scr,
-                                      int bar_id) const {
-    const float tr = (valid && t != nullptr) ? t[row] : 0.f;
-    const int tid = threadIdx.x & 127;  // row within the tile
-    float* sb = scr;
-    float* sw = scr + 16 * kScratchStride;
-    const int lim = min(T - n0, tile_cols);
-    for (int c0 = 0; c0 < lim; c0 += 16) {
-      float v[16];
-      tmem_ld16(taddr + c0, v);
-#pragma unroll
-      for (int i = 0; i < 16; ++i) {
-        const int c = n0 + c0 + i;
-        const float g = (valid && c0 + i < lim) ? -sin_phase(w[c], tr, b[c]) * v[i] : 0.f;
-        sb[i * kScratchStride + tid] = g;
-        sw[i * kScratchStride + tid] = g * tr;
-      }
-      asm volatile("bar.sync %0, 128;" ::"r"(bar_id) : "memory");
-      const int i = tid >> 3, part = tid & 7;
-      float gb = 0.f, gw = 0.f;
-#pragma unroll
-      for (int r = 0; r < 16; ++r) {
-        gb += sb[i * kScratchStride + r * 8 + part];
-        gw += sw[i * kScratchStride + r * 8 + part];
-      }
-#pragma unroll
-      for (int off = 4; off > 0; off >>= 1) {
-        gb += __shfl_xor_sync(0xffffffffu, gb, off);
-        gw += __shfl_xor_sync(0xffffffffu, gw, off);
-      }
-      if (part == 0 && c0 + i < lim) {
-        atomicAdd(&db[n0 + c0 + i], gb);
-        if (t != nullptr) atomicAdd(&dw[n0 + c0 + i], gw);
-      }
-      asm volatile("bar.sync %0, 128;" ::"r"(bar_id) : "memory");
-    }
-  }
-#endif
-};
 }  // namespace su

@@ -237,11 +237,6 @@ void gemm(const SegSource& a, const WeightSource& b, const EpiOutLN& e, const Ge
   else launch_any<256, 1>(a, b, e, sh, st);
 }
 
-void gemm(const SegSource& a, const MNView<WeightSource>& b, const EpiTimeGrad& e, const GemmShape& sh,
-          cudaStream_t st) {
-  dispatch(a, b, e, sh, st);
-}
-
 void gemm(const SegSource& a, const WeightSource& b, const EpiLSTM& e, const GemmShape& sh, cudaStream_t st) {
   launch_any<128, 1>(a, b, e, sh, st);  // one tile = four gates x 32 hidden units (gate-grouped rows)
 }

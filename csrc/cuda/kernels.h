@@ -25,16 +25,15 @@ void gemm(const MNView<SegSource>& a, const MNView<SegSource>& b, const EpiWeigh
           cudaStream_t st);
 void gemm(const SegSource& a, const WeightSource& b, const EpiGRU& e, const GemmShape& sh, cudaStream_t st);
 void gemm(const SegSource& a, const WeightSource& b, const EpiOutLN& e, const GemmShape& sh, cudaStream_t st);
-void gemm(const SegSource& a, const MNView<WeightSource>& b, const EpiTimeGrad& e, const GemmShape& sh,
-          cudaStream_t st);
 // Same kernels, reporting into a caller-given device status word instead of the
 // lazily allocated per-device one (used by entry points that must not allocate).
 void gemm_with_status(const SegSource& a, const MNView<WeightSource>& b, const EpiLinear& e, const GemmShape& sh,
                       cudaStream_t st, int* status);
 void gemm_with_status(const MNView<SegSource>& a, const MNView<SegSource>& b, const EpiWeightGrad& e,
                       const GemmShape& sh, cudaStream_t st, int* status);
-void launch_time_grad_reduce(cudaStream_t st, const float* dT, int64_t rows, int T, const float* t, const float* w,
-                             const float* b, const int* gcount, int group, const int* nrows_dev, float* dw, float* db);
+void launch_time_grad_finish(cudaStream_t st, const float* wk, const float* wv, int ldw, int ct, const float* wq,
+                             int ldq, int cq, int Do, int T, const float* Mt, const float* M1, const float* gbq,
+                             const float* b, float* dw, float* db);
 
 // ---- TGN step kernels --------------------------------------------------------
 struct PrepArgs {

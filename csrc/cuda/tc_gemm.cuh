@@ -31,7 +31,7 @@ constexpr int kBM = 128;          // rows per tile (UMMA M)
 constexpr int kBK = 64;           // K elements per pipeline stage (4 UMMA k-steps of 16)
 constexpr int kStages = 2;
 constexpr int kGemmThreads = 160;
-constexpr int kMaxSeg = 4;
+constexpr int kMaxSeg = 6;
 constexpr int kMaxBlk = 4;
 
 // Byte offset of the 16-byte vector (row r, K-vector kv) inside a stage tile
@@ -70,6 +70,7 @@ enum SegKind : int {
   kSegOnes = 3,     // a single constant-1 column (bias trick for weight gradients)
   kSegSharded = 4,  // fp32 rows owned by peer GPUs: peers[owner[id]] + lrow[id] * ld
   kSegZero = 5,     // zero padding
+  kSegTimeSin = 6,  // -sin(w[c] * t[row] + b[c]), times t[row] when `tmul` (time-encoder gradient terms)
 };
 
 struct ASeg {
@@ -84,6 +85,7 @@ struct ASeg {
   const float* tdt = nullptr;        // time-encoding input per row
   const float* tw = nullptr;
   const float* tb = nullptr;
+  int tmul = 0;                      // kSegTimeSin: multiply by t
   const float* const* peers = nullptr;  // sharded: per-rank base pointers
   const int* owner = nullptr;           // sharded: owning rank per global id
   const int64_t* lrow = nullptr;        // sharded: row inside the owner's shard (nullptr: the global id)
@@ -143,6 +145,13 @@ __device__ __forceinline__ void seg_fill8(const ASeg& g, int row, int c, float (
       for (int i = 0; i < 8; ++i) f[i] = (c + i < g.width) ? cos_phase(g.tw[c + i], t, g.tb[c + i]) : 0.f;
       break;
     }
+    case kSegTimeSin: {
+      const float t = g.tdt ? g.tdt[row] : 0.f;
+      const float m = g.tmul ? -t : -1.f;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) f[i] = (c + i < g.width) ? m * sin_phase(g.tw[c + i], t, g.tb[c + i]) : 0.f;
+      break;
+    }
     case kSegOnes:
       if (c == 0) f[0] = 1.f;
       break;
@@ -167,6 +176,10 @@ __device__ __forceinline__ float seg_load1(const ASeg& g, int row, int c) {
     case kSegTime: {
       const float t = g.tdt ? g.tdt[row] : 0.f;
       return cos_phase(g.tw[c], t, g.tb[c]);
+    }
+    case kSegTimeSin: {
+      const float t = g.tdt ? g.tdt[row] : 0.f;
+      return (g.tmul ? -t : -1.f) * sin_phase(g.tw[c], t, g.tb[c]);
     }
     case kSegOnes:
       return c == 0 ? 1.f : 0.f;
@@ -260,7 +273,7 @@ struct WeightLayout {
   int nblk = 0, nseg = 0;
   int blk_rows[kMaxBlk] = {0, 0, 0, 0};  // valid rows of each output block
   int blk_pad[kMaxBlk] = {0, 0, 0, 0};   // padded rows of each output block
-  int seg_kpad[kMaxSeg] = {0, 0, 0, 0};  // padded K width of each input segment
+  int seg_kpad[kMaxSeg] = {0, 0, 0, 0, 0, 0};  // padded K width of each input segment
   WCell cell[kMaxBlk][kMaxSeg];
 
 #ifdef __CUDACC__

@@ -596,40 +596,54 @@ void launch_tgn_metrics(dim3 grid, dim3 block, cudaStream_t st, const float* __r
 
 namespace su {
 
-// dw[c] += sum_rows -sin(w[c] t + b[c]) * t * dT[row, c];  db[c] += sum_rows -sin(w[c] t + b[c]) * dT[row, c]
-// (gradient of the cosine time encoding). Threads own columns, blocks own row ranges.
-__global__ void time_grad_reduce_kernel(const float* __restrict__ dT, int64_t rows, int T, const float* __restrict__ t,
-                                        const float* __restrict__ w, const float* __restrict__ b,
-                                        const int* __restrict__ gcount, int group, const int* __restrict__ nrows_dev,
-                                        float* __restrict__ dw, float* __restrict__ db) {
-  const int c = threadIdx.x;
-  if (c >= T) return;
-  const int64_t r0 = static_cast<int64_t>(blockIdx.x) * 64;
-  const int64_t r1 = (rows < r0 + 64) ? rows : (r0 + 64);
-  const int64_t nd = nrows_dev ? static_cast<int64_t>(*nrows_dev) : rows;
-  const int64_t limit = nd < rows ? nd : rows;
-  const float wc = w[c], bc = b[c];
-  float gw = 0.f, gb = 0.f;
-  for (int64_t r = r0; r < r1; ++r) {
-    if (r >= limit) break;
-    if (gcount != nullptr && (r % group) >= gcount[r / group]) continue;
-    const float tt = t ? t[r] : 0.f;
-    const float g = -sin_phase(wc, tt, bc) * dT[r * T + c];
-    gb += g;
-    gw = fmaf(g, tt, gw);
+// Time-encoder gradient from the products accumulated by the W_kv weight-gradient
+// GEMM (M_t = dKV^T (-sin(w t + b) t), M_1 = dKV^T (-sin(w t + b))) and the b_q
+// gradient (row sums of dQ; roots encode t = 0):
+//   dw[c] += sum_o Wk[o, ct + c] M_t[o, c] + Wv[o, ct + c] M_t[Do + o, c]
+//   db[c] += (same with M_1) - sin(b[c]) * sum_o Wq[o, cq + c] gbq[o]
+__global__ void __launch_bounds__(1024) time_grad_finish_kernel(
+    const float* __restrict__ wk, const float* __restrict__ wv, int ldw, int ct, const float* __restrict__ wq,
+    int ldq, int cq, int Do, int T, const float* __restrict__ Mt, const float* __restrict__ M1,
+    const float* __restrict__ gbq, const float* __restrict__ b, float* __restrict__ dw, float* __restrict__ db) {
+  // block: 32 columns (lanes) x 32 warps over the output features o
+  __shared__ float red[3][32][33];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int c = blockIdx.x * 32 + lane;
+  float sw = 0.f, sb = 0.f, sq = 0.f;
+  if (c < T) {
+    for (int o = warp; o < Do; o += 32) {
+      const float a = wk[static_cast<int64_t>(o) * ldw + ct + c];
+      const float v = wv[static_cast<int64_t>(o) * ldw + ct + c];
+      sw = fmaf(a, Mt[static_cast<int64_t>(o) * T + c], sw);
+      sw = fmaf(v, Mt[static_cast<int64_t>(Do + o) * T + c], sw);
+      sb = fmaf(a, M1[static_cast<int64_t>(o) * T + c], sb);
+      sb = fmaf(v, M1[static_cast<int64_t>(Do + o) * T + c], sb);
+      sq = fmaf(wq[static_cast<int64_t>(o) * ldq + cq + c], gbq[o], sq);
+    }
   }
-  atomicAdd(&db[c], gb);
-  if (t) atomicAdd(&dw[c], gw);
+  red[0][warp][lane] = sw;
+  red[1][warp][lane] = sb;
+  red[2][warp][lane] = sq;
+  __syncthreads();
+  if (warp == 0 && c < T) {
+    float tw = 0.f, tb = 0.f, tq = 0.f;
+    for (int w = 0; w < 32; ++w) {
+      tw += red[0][w][lane];
+      tb += red[1][w][lane];
+      tq += red[2][w][lane];
+    }
+    dw[c] += tw;
+    db[c] += tb - sinf(b[c]) * tq;
+  }
 }
 
-void launch_time_grad_reduce(cudaStream_t st, const float* dT, int64_t rows, int T, const float* t, const float* w,
-                             const float* b, const int* gcount, int group, const int* nrows_dev, float* dw,
-                             float* db) {
-  if (rows == 0) return;
-  const int threads = (T + 31) / 32 * 32;
+void launch_time_grad_finish(cudaStream_t st, const float* wk, const float* wv, int ldw, int ct, const float* wq,
+                             int ldq, int cq, int Do, int T, const float* Mt, const float* M1, const float* gbq,
+                             const float* b, float* dw, float* db) {
+  if (T <= 0) return;
   count_launch();
-  time_grad_reduce_kernel<<<(rows + 63) / 64, threads, 0, st>>>(dT, rows, T, t, w, b, gcount, group, nrows_dev,
-                                                                    dw, db);
+  time_grad_finish_kernel<<<(T + 31) / 32, 1024, 0, st>>>(wk, wv, ldw, ct, wq, ldq, cq, Do, T, Mt, M1, gbq, b, dw,
+                                                          db);
 }
 
 }  // namespace su

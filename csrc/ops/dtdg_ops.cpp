@@ -44,7 +44,7 @@ std::vector<at::Tensor> lstm_fwd(const at::Tensor& x, const c10::optional<at::Te
   const int rows = static_cast<int>(x.size(0));
   const int in_dim = static_cast<int>(x.size(1));
   const int H = static_cast<int>(wi.size(0));
-  constexpr int G = 32;  // gate group: an N tile holds [i | f | g | o] for 32 hidden units
+  constexpr int G = 16;  // gate group: each 64-column half of an N tile holds [i | f | g | o] for 16 units
   auto h_out = at::empty({rows, H}, x.options());
   auto c_out = at::empty({rows, H}, x.options());
   at::Tensor gates = save_gates ? at::empty({rows, 4 * H}, x.options()) : at::Tensor();

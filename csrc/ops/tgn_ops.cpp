@@ -64,7 +64,9 @@ void tgn_sample(const at::Tensor& roots, const at::Tensor& n_roots, const at::Te
 
 // One GRU step over rows `index` of `x_src` (gathered, column block col0..col0+width)
 // with previous hidden rows (or zeros); see EpiGRU for outputs.
-static constexpr int kGateGroup = 32;  // hidden units per gate group in an N tile (4 gates x 32 = 128 columns)
+// hidden units per gate group: a 128-column tile holds two groups [r | z | n_i | n_h] x 16, one per
+// epilogue column half
+static constexpr int kGateGroup = 16;
 
 static void gru_step(const SegSource& a, int kx, int kh, const at::Tensor& w_ih, const at::Tensor& w_hh,
                      const at::Tensor& b_ih, const at::Tensor& b_hh, EpiGRU e, int rmax, const int* m_dev) {
@@ -420,8 +422,13 @@ void tgn_attn_proj_bwd(const at::Tensor& memory, const at::Tensor& roots, const 
     float* bg[4] = {g_bq.data_ptr<float>(), nullptr, nullptr, nullptr};
     proj_wgrad(dy, Do, x, pad8(D) + pad8(T) + 8, rmax, L, bg, 2);
   }
-  // ---------------- W_k, b_k, W_v, b_v (reduction over edges)
+  // ---------------- W_k, b_k, W_v, b_v (reduction over edges), plus the time-encoder terms
+  // The encoder gradient is  dw[c] = sum_r dT[r,c] (-sin(w_c t_r + b_c)) t_r  with  dT = dKV W_kv[:, time],
+  // i.e.  dw[c] = sum_o W_kv[o, time c] * M_t[o, c],  M_t = dKV^T (-sin(..) t)  (and M_1 without t for db):
+  // two extra column segments of this weight-gradient GEMM, then a T-wide finishing kernel.
   {
+    at::Tensor M_t = at::zeros({2 * Do, T}, dKV.options());
+    at::Tensor M_1 = at::zeros({2 * Do, T}, dKV.options());
     SegSource dy;
     dy.group = k;
     dy.gcount = nbr_cnt.data_ptr<int>();
@@ -430,14 +437,19 @@ void tgn_attn_proj_bwd(const at::Tensor& memory, const at::Tensor& roots, const 
     SegSource x;
     x.group = k;
     x.gcount = nbr_cnt.data_ptr<int>();
-    x.nseg = 4;
+    x.nseg = 6;
     x.seg[0] = seg_memory(memory, D, nbr.data_ptr<int64_t>(), pd, true);
     x.seg[1] = seg_f32(efeat, Ew, pad8(Ei), nbr_eid.data_ptr<int64_t>());
     x.seg[2] = seg_time(nbr_dt.data_ptr<float>(), te_w, te_b, pad8(T));
     x.seg[3] = seg_ones();
+    x.seg[4] = seg_time(nbr_dt.data_ptr<float>(), te_w, te_b, pad8(T));
+    x.seg[4].kind = kSegTimeSin;
+    x.seg[4].tmul = 1;
+    x.seg[5] = seg_time(nbr_dt.data_ptr<float>(), te_w, te_b, pad8(T));
+    x.seg[5].kind = kSegTimeSin;
     WeightLayout L;
     L.nblk = 2;
-    L.nseg = 4;
+    L.nseg = 6;
     L.blk_rows[0] = Do;
     L.blk_pad[0] = Do;
     L.blk_rows[1] = Do;
@@ -446,72 +458,24 @@ void tgn_attn_proj_bwd(const at::Tensor& memory, const at::Tensor& roots, const 
     L.seg_kpad[1] = pad8(Ei);
     L.seg_kpad[2] = pad8(T);
     L.seg_kpad[3] = 8;
+    L.seg_kpad[4] = pad8(T);
+    L.seg_kpad[5] = pad8(T);
     at::Tensor* gs[2] = {&g_wk, &g_wv};
     for (int i = 0; i < 2; ++i) {
       L.cell[i][0] = wcell(*gs[i], 0, 0, D);
       L.cell[i][1] = wcell(*gs[i], 0, D, Ei);
       L.cell[i][2] = wcell(*gs[i], 0, D + Ei, T);
+      L.cell[i][4] = wcell(M_t, i * Do, 0, T);
+      L.cell[i][5] = wcell(M_1, i * Do, 0, T);
     }
     float* bg[4] = {g_bk.data_ptr<float>(), g_bv.data_ptr<float>(), nullptr, nullptr};
-    proj_wgrad(dy, 2 * Do, x, pad8(D) + pad8(Ei) + pad8(T) + 8, rmax * k, L, bg, 3);
-  }
-  // ---------------- time encoder: d(time segment) = dKV [W_k; W_v][:, time] (edges), dQ W_q[:, time] (roots),
-  // then a column reduction with the derivative of cos(w t + b)
-  {
-    SegSource a;
-    a.group = k;
-    a.gcount = nbr_cnt.data_ptr<int>();
-    a.nseg = 1;
-    a.seg[0] = seg_f32(dKV, 2 * Do, pad8(2 * Do));
-    WeightLayout L;  // rows (GEMM K) = output features of [W_k; W_v], columns (GEMM N) = time dims
-    L.nblk = 2;
-    L.nseg = 1;
-    L.blk_rows[0] = Do;
-    L.blk_pad[0] = Do;
-    L.blk_rows[1] = Do;
-    L.blk_pad[1] = pad8(2 * Do) - Do;
-    L.seg_kpad[0] = pad8(T);
-    L.cell[0][0] = wcell(wk, 0, D + Ei, T);
-    L.cell[1][0] = wcell(wv, 0, D + Ei, T);
-    WeightMN b = weight_mn(L, pad8(2 * Do));
-    EpiTimeGrad e;  // reduces dT straight into the encoder gradients
-    e.T = T;
-    e.t = nbr_dt.data_ptr<float>();
-    e.w = te_w.data_ptr<float>();
-    e.b = te_b.data_ptr<float>();
-    e.dw = g_tw.data_ptr<float>();
-    e.db = g_tb.data_ptr<float>();
-    GemmShape sh;
-    sh.M = rmax * k;
-    sh.N = T;
-    sh.K = pad8(2 * Do);
-    gemm(a, b, e, sh, cur_stream());
-  }
-  {
-    SegSource a;
-    a.nrows_dev = n_roots.data_ptr<int>();
-    a.nseg = 1;
-    a.seg[0] = seg_f32(dQ, Do, pad8(Do));
-    WeightLayout L;
-    L.nblk = 1;
-    L.nseg = 1;
-    L.blk_rows[0] = Do;
-    L.blk_pad[0] = pad8(Do);
-    L.seg_kpad[0] = pad8(T);
-    L.cell[0][0] = wcell(wq, 0, D, T);
-    WeightMN b = weight_mn(L, pad8(Do));
-    EpiTimeGrad e;  // roots encode t = 0: only the bias gradient gets contributions
-    e.T = T;
-    e.w = te_w.data_ptr<float>();
-    e.b = te_b.data_ptr<float>();
-    e.dw = g_tw.data_ptr<float>();
-    e.db = g_tb.data_ptr<float>();
-    GemmShape sh;
-    sh.M = rmax;
-    sh.m_dev = n_roots.data_ptr<int>();
-    sh.N = T;
-    sh.K = pad8(Do);
-    gemm(a, b, e, sh, cur_stream());
+    proj_wgrad(dy, 2 * Do, x, pad8(D) + pad8(Ei) + pad8(T) + 8 + 2 * pad8(T), rmax * k, L, bg, 3);
+    // Q side: roots encode t = 0, so only db gets  -sin(b_c) sum_o W_q[o, time c] * (sum_rows dQ[r, o]);
+    // the row sum of dQ is this step's b_q gradient (computed above)
+    launch_time_grad_finish(cur_stream(), wk.data_ptr<float>(), wv.data_ptr<float>(), static_cast<int>(wk.stride(0)),
+                            D + Ei, wq.data_ptr<float>(), static_cast<int>(wq.stride(0)), D, Do, T,
+                            M_t.data_ptr<float>(), M_1.data_ptr<float>(), g_bq.data_ptr<float>(),
+                            te_b.data_ptr<float>(), g_tw.data_ptr<float>(), g_tb.data_ptr<float>());
   }
   SU_LAUNCH_CHECK();
 }
