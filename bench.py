@@ -31,6 +31,7 @@ from pathlib import Path
 ROOT = Path(__file__).resolve().parent
 METRIC = "TGN train events/sec & MPNN-LSTM snapshots/sec, 1/2/4/8 B200, max over ranks"
 MODEL_NAME = "TGN (1-layer temporal attention, 2 heads), CTDG online + async_sync"
+JODIE_NAME = "JODIE (tanh-RNN memory updater, time-projection embedding), CTDG online"
 
 
 def _args():
@@ -39,10 +40,12 @@ def _args():
     p.add_argument("--steps", type=int, default=200)
     p.add_argument("--warmup", type=int, default=10)
     p.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    p.add_argument("--events", type=int, default=7833140, help="stream length (config: 7,833,140)")
-    p.add_argument("--batch", type=int, default=600, help="events per rank per step")
-    p.add_argument("--workload", default="tgn", choices=["tgn", "mpnn_lstm"],
-                   help="tgn: TGN train events/sec (default); mpnn_lstm: MPNN-LSTM train snapshots/sec")
+    p.add_argument("--events", type=int, default=None,
+                   help="stream length (tgn config: 7,833,140; jodie config: 200,000,000)")
+    p.add_argument("--batch", type=int, default=None, help="events per rank per step (tgn: 600, jodie: 4000)")
+    p.add_argument("--workload", default="tgn", choices=["tgn", "jodie", "mpnn_lstm"],
+                   help="tgn: TGN train events/sec (default, config 3); jodie: JODIE train events/sec (config 4); "
+                        "mpnn_lstm: MPNN-LSTM train snapshots/sec (config 2)")
     p.add_argument("--snapshots", type=int, default=128, help="mpnn_lstm: snapshots generated (config: 128)")
     return p.parse_args()
 
@@ -152,17 +155,22 @@ def _mpnn_main(args):
             "train": {"epochs": 1, "snaps": args.snapshots, "lr": 1e-3},
             "runtime": {"device": "cuda"},
             "dtdg": {"window_from_size": True, "chunk_order": None, "chunk_decay": None, "resident": resident},
-            "dist": {"backend": "nccl", "timeout_s": 600},
+            "dist": {"backend": "nccl", "timeout_s": 1800},
         }
 
     session = SchedulerSession.from_config(cfg(True))
-    session.ctx.artifact_root = Path(os.environ.get("TMPDIR", "/tmp")) / f"su_mpnn_w{world}_r{rank}"
+    # one artifact set for all ranks (written by rank 0): every partition file holds its
+    # snapshots' features, so per-rank copies would multiply the disk footprint by N
+    session.ctx.artifact_root = Path(os.environ.get("TMPDIR", "/tmp")) / f"su_mpnn_w{world}"
     if world > 1:
         from starry_unigraph.distributed import initialize_distributed
 
         initialize_distributed(session.ctx.dist)
     t_prep = time.perf_counter()
-    session.prepare_data()
+    if rank == 0:
+        session.prepare_data()
+    if world > 1:
+        dist.barrier()
     session.build_runtime()
     prep_s = time.perf_counter() - t_prep
     core, rt = session.snapshot_core, session.runtime
@@ -225,6 +233,7 @@ def main():
         return _reference_arm(args)
     if args.workload == "mpnn_lstm":
         return _mpnn_main(args)
+    jodie = args.workload == "jodie"
     sys.path.insert(0, str(ROOT))
     import torch
     import torch.distributed as dist
@@ -236,10 +245,16 @@ def main():
     from starry_unigraph import SchedulerSession
     from starry_unigraph.ops import check_status
 
+    if args.events is None:
+        args.events = 200_000_000 if jodie else 7833140
+    if args.batch is None:
+        args.batch = 4000 if jodie else 600
+    fam, hidden, preset = ("jodie", 172, "jodie_large") if jodie else ("tgn", 100, "tgn_large")
     cfg = {
-        "model": {"name": "tgn", "family": "tgn", "task": "temporal_link_prediction", "hidden_dim": 100},
-        "data": {"root": "./data", "name": "tgn_large", "format": "synthetic",
-                 "synthetic": {"preset": "tgn_large", "num_events": args.events, "seed": 0}},
+        "model": {"name": fam, "family": fam, "task": "temporal_link_prediction", "hidden_dim": hidden,
+                  "memory": {"type": "rnn" if jodie else "gru"}},
+        "data": {"root": "./data", "name": preset, "format": "synthetic",
+                 "synthetic": {"preset": preset, "num_events": args.events, "seed": 0}},
         "train": {"epochs": 1, "batch_size": args.batch, "lr": 1e-4},
         "runtime": {"device": "cuda", "cuda_graphs": True},
         "ctdg": {"mailbox_slots": 1, "dim_time": 100, "num_head": 2, "dropout": 0.1, "att_dropout": 0.1,
@@ -324,7 +339,7 @@ def main():
     if rank == 0:
         bpe = 8 + 8 + 4 + 8  # src, dst, ts, eid per event
         line = {
-            "metric": "TGN train events/sec",
+            "metric": "JODIE train events/sec" if jodie else "TGN train events/sec",
             "value": value,
             "unit": "events/s",
             "n_gpus": world,
@@ -336,10 +351,13 @@ def main():
             "vs_baseline": None,
             "dtype": "bf16",
             "data": "synthetic (random-init weights)",
-            "config": {"model": MODEL_NAME, "global_batch": args.batch * world, "seq_len": None,
-                       "parallelism": f"dp{world}+memory-partition", "events": args.events, "nodes": 1140149,
-                       "fanout": 10, "mailbox_slots": 1, "dims": "memory=time=embed=100",
-                       "l2": "working set (memory 456 MB, mailbox 985 MB, edge features 500 MB) > 126 MB L2",
+            "config": {"model": JODIE_NAME if jodie else MODEL_NAME, "global_batch": args.batch * world,
+                       "seq_len": None, "parallelism": f"dp{world}+memory-partition", "events": args.events,
+                       "nodes": 11_000_000 if jodie else 1140149, "fanout": None if jodie else 10,
+                       "mailbox_slots": 1, "dims": "memory=172, edge features 32 (bf16 on the host)" if jodie
+                       else "memory=time=embed=100",
+                       "l2": ("working set (memory 7.6 GB, mailbox 30 GB, edge features 25 GB) > 126 MB L2" if jodie
+                              else "working set (memory 456 MB, mailbox 985 MB, edge features 500 MB) > 126 MB L2"),
                        "baseline_metric": METRIC},
             "clocks": clocks.summary(),
             "e2e": {"value": e2e, "unit": "events/s", "h2d_bytes_per_step": args.batch * bpe + 4,

@@ -21,8 +21,9 @@ struct EpiGRU {
   static constexpr bool kSplitCols = true;
   static constexpr int kScratchBytes = 0;
   int D = 0, DP = 0;  // DP = gate group width G: tile columns are [r | z | n_i | n_h] x G units
-  const float* b_ih = nullptr;   // [3D]
-  const float* b_hh = nullptr;   // [3D]
+  int ngates = 4;     // 4: GRU cell; 1: tanh RNN cell h' = tanh(W_ih x + b_ih + W_hh h + b_hh) (JODIE)
+  const float* b_ih = nullptr;   // [3D] (RNN: [D])
+  const float* b_hh = nullptr;   // [3D] (RNN: [D])
   const float* hprev = nullptr;  // previous hidden rows (nullptr -> zeros)
   const int64_t* hprev_index = nullptr;
   int hprev_ld = 0;
@@ -38,12 +39,12 @@ struct EpiGRU {
   const float* ts_value = nullptr;
 
 #ifdef __CUDACC__
-  // every gate group of 4*DP columns in the range this thread was given
+  // every gate group of ngates*DP columns in the range this thread was given
   __device__ __forceinline__ void operator()(int row, bool valid, int n0, uint32_t taddr, int tile_cols) const {
-    for (int g0 = 0; g0 < tile_cols; g0 += 4 * DP) group(row, valid, n0 + g0, taddr + g0);
+    for (int g0 = 0; g0 < tile_cols; g0 += ngates * DP) group(row, valid, n0 + g0, taddr + g0);
   }
   __device__ __forceinline__ void group(int row, bool valid, int n0, uint32_t taddr) const {
-    const int u0 = (n0 / (4 * DP)) * DP;  // first hidden unit of this group
+    const int u0 = (n0 / (ngates * DP)) * DP;  // first hidden unit of this group
     const float* hp = nullptr;
     if (valid && hprev != nullptr) {
       const int64_t hr = hprev_index ? hprev_index[row] : row;
@@ -51,6 +52,25 @@ struct EpiGRU {
     }
     int64_t srow = -1;
     if (valid && scatter != nullptr) srow = scatter_index[row];
+    if (ngates == 1) {
+      for (int c0 = 0; c0 < DP; c0 += 16) {
+        float pre[16];
+        tmem_ld16(taddr + c0, pre);
+        if (!valid) continue;
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          const int c = u0 + c0 + i;
+          if (c >= D) break;
+          const float h = hp ? hp[c] : 0.f;
+          const float hn = tanh_fast(pre[i] + b_ih[c] + b_hh[c]);
+          if (save_prev) save_prev[(int64_t)row * D + c] = h;
+          if (hout) hout[(int64_t)row * hout_ld + c] = hn;
+          if (srow >= 0) scatter[srow * scatter_ld + c] = hn;
+        }
+      }
+      if (valid && srow >= 0 && scatter_ts != nullptr && u0 == 0) scatter_ts[srow] = *ts_value;
+      return;
+    }
     for (int c0 = 0; c0 < DP; c0 += 16) {
       float r[16], z[16], ni[16], nh[16];
       tmem_ld16(taddr + c0, r);

@@ -646,4 +646,83 @@ void launch_time_grad_finish(cudaStream_t st, const float* wk, const float* wv, 
                                                           db);
 }
 
+// ---------------------------------------------------------------------------
+// JODIE time-projection embedding (warp per root row)
+//   prev_ts[r] = memory_ts of root r before this step's memory update
+//   z[r, c]    = h[r, c] * (1 + w[c] * dt_r + b[c]),  dt_r = root_ts - prev_ts[r] (0 if never updated)
+// h = the updated memory row: table row roots[r], or row r of `fresh` (multi-GPU step buffer).
+// ---------------------------------------------------------------------------
+__global__ void jodie_prev_ts_kernel(const int64_t* __restrict__ roots, const int* __restrict__ n_roots, int rmax,
+                                     const float* __restrict__ mem_ts, const float* const* __restrict__ ts_peers,
+                                     const int* __restrict__ owner, float* __restrict__ prev_ts) {
+  const int r = blockIdx.x * blockDim.x + threadIdx.x;
+  if (r >= rmax) return;
+  if (r >= *n_roots) {
+    prev_ts[r] = -1.f;
+    return;
+  }
+  const int64_t v = roots[r];
+  prev_ts[r] = ts_peers ? ts_peers[owner[v]][v] : mem_ts[v];
+}
+
+__global__ void jodie_project_kernel(const int64_t* __restrict__ roots, const int* __restrict__ n_roots, int rmax,
+                                     const float* __restrict__ mem, const float* __restrict__ fresh, int D,
+                                     const float* __restrict__ prev_ts, const int64_t* __restrict__ root_ts,
+                                     const float* __restrict__ w, const float* __restrict__ b,
+                                     float* __restrict__ out, float* __restrict__ dt_out) {
+  const int r = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (r >= rmax || r >= *n_roots) return;
+  const float pt = prev_ts[r];
+  const float dt = pt >= 0.f ? static_cast<float>(*root_ts) - pt : 0.f;
+  if (lane == 0) dt_out[r] = dt;
+  const float* h = fresh ? fresh + static_cast<int64_t>(r) * D : mem + roots[r] * D;
+  float* o = out + static_cast<int64_t>(r) * D;
+  for (int c = lane; c < D; c += 32) o[c] = h[c] * (1.f + fmaf(w[c], dt, b[c]));
+}
+
+// dw[c] += sum_r dz[r,c] h[r,c] dt_r ;  db[c] += sum_r dz[r,c] h[r,c]   (threads over columns, blocks over rows)
+__global__ void jodie_project_bwd_kernel(const int64_t* __restrict__ roots, const int* __restrict__ n_roots, int rmax,
+                                         const float* __restrict__ mem, const float* __restrict__ fresh, int D,
+                                         const float* __restrict__ dt, const float* __restrict__ dz,
+                                         float* __restrict__ dw, float* __restrict__ db) {
+  const int c = threadIdx.x;
+  if (c >= D) return;
+  const int r0 = blockIdx.x * 32;
+  const int n = min(*n_roots, rmax);
+  float gw = 0.f, gb = 0.f;
+  for (int r = r0; r < r0 + 32 && r < n; ++r) {
+    const float* h = fresh ? fresh + static_cast<int64_t>(r) * D : mem + roots[r] * D;
+    const float g = dz[static_cast<int64_t>(r) * D + c] * h[c];
+    gb += g;
+    gw = fmaf(g, dt[r], gw);
+  }
+  atomicAdd(&dw[c], gw);
+  atomicAdd(&db[c], gb);
+}
+
+void launch_jodie_prev_ts(cudaStream_t st, const int64_t* roots, const int* n_roots, int rmax, const float* mem_ts,
+                          const float* const* ts_peers, const int* owner, float* prev_ts) {
+  if (rmax <= 0) return;
+  count_launch();
+  jodie_prev_ts_kernel<<<(rmax + 255) / 256, 256, 0, st>>>(roots, n_roots, rmax, mem_ts, ts_peers, owner, prev_ts);
+}
+
+void launch_jodie_project(cudaStream_t st, const int64_t* roots, const int* n_roots, int rmax, const float* mem,
+                          const float* fresh, int D, const float* prev_ts, const int64_t* root_ts, const float* w,
+                          const float* b, float* out, float* dt_out) {
+  if (rmax <= 0) return;
+  count_launch();
+  jodie_project_kernel<<<(rmax * 32 + 255) / 256, 256, 0, st>>>(roots, n_roots, rmax, mem, fresh, D, prev_ts,
+                                                                 root_ts, w, b, out, dt_out);
+}
+
+void launch_jodie_project_bwd(cudaStream_t st, const int64_t* roots, const int* n_roots, int rmax, const float* mem,
+                              const float* fresh, int D, const float* dt, const float* dz, float* dw, float* db) {
+  if (rmax <= 0) return;
+  count_launch();
+  jodie_project_bwd_kernel<<<(rmax + 31) / 32, (D + 31) / 32 * 32, 0, st>>>(roots, n_roots, rmax, mem, fresh, D, dt,
+                                                                            dz, dw, db);
+}
+
 }  // namespace su

@@ -110,6 +110,18 @@ void spmm_peer_push(const at::Tensor& rowptr_t, const at::Tensor& col_t, const a
                     const at::Tensor& grad_dst, int64_t n_src, const at::Tensor& peers, const at::Tensor& src_owner,
                     const at::Tensor& src_row);
 
+void tgn_rnn_memory_update(const at::Tensor& roots, const at::Tensor& n_roots, const at::Tensor& mailbox,
+                           at::Tensor& memory, at::Tensor& memory_ts, const at::Tensor& ts_max,
+                           const at::Tensor& w_ih, const at::Tensor& w_hh, const at::Tensor& b_ih,
+                           const at::Tensor& b_hh, at::Tensor& mem_prev, at::Tensor& prev_ts,
+                           const c10::optional<at::Tensor>& peer);
+void jodie_project(const at::Tensor& roots, const at::Tensor& n_roots, const at::Tensor& memory,
+                   const at::Tensor& prev_ts, const at::Tensor& root_ts, const at::Tensor& w, const at::Tensor& b,
+                   at::Tensor& out, at::Tensor& dt, const c10::optional<at::Tensor>& peer);
+void jodie_project_bwd(const at::Tensor& roots, const at::Tensor& n_roots, const at::Tensor& memory,
+                       const at::Tensor& dt, const at::Tensor& dz, at::Tensor& dw, at::Tensor& db,
+                       const c10::optional<at::Tensor>& peer);
+
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "starry_unigraph sm_100a kernels (tcgen05 GEMMs, TGN step, DTDG ops, collectives)";
   m.def("status_read", &status_read, "read (and clear) the device status word", py::arg("clear") = true);
@@ -121,6 +133,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("tgn_sample", &tgn_sample);
   m.def("tgn_memory_update", &tgn_memory_update);
   m.def("tgn_mailbox_write", &tgn_mailbox_write);
+  m.def("tgn_rnn_memory_update", &tgn_rnn_memory_update);
+  m.def("jodie_project", &jodie_project);
+  m.def("jodie_project_bwd", &jodie_project_bwd);
   m.def("tgn_attn_proj", &tgn_attn_proj);
   m.def("tgn_attn_fwd", &tgn_attn_fwd);
   m.def("tgn_attn_bwd", &tgn_attn_bwd);

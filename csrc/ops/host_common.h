@@ -83,7 +83,7 @@ inline WCell wcell(const at::Tensor& w, int row0, int col0, int width) {
 // (peer pointers of symmetric allocations); rows of this step's roots are read
 // from the local `mem_new` buffer once the memory updater has produced them.
 // Passed from Python as a CPU int64 tensor of device addresses:
-//   [mem_peers, mail_peers, owner, stamp, node2root, step_ctr, mem_new]
+//   [mem_peers, mail_peers, owner, stamp, node2root, step_ctr, mem_new, ts_peers]
 struct PeerDesc {
   bool on = false;
   const float* const* mem_peers = nullptr;
@@ -93,12 +93,13 @@ struct PeerDesc {
   const int* node2root = nullptr;
   const int64_t* step_ctr = nullptr;
   float* mem_new = nullptr;
+  const float* const* ts_peers = nullptr;
 };
 
 inline PeerDesc peer_desc(const c10::optional<at::Tensor>& t) {
   PeerDesc d;
   if (!t.has_value() || !t->defined()) return d;
-  TORCH_CHECK(t->device().is_cpu() && t->scalar_type() == at::kLong && t->numel() == 7, "bad peer descriptor");
+  TORCH_CHECK(t->device().is_cpu() && t->scalar_type() == at::kLong && t->numel() >= 7, "bad peer descriptor");
   const int64_t* v = t->data_ptr<int64_t>();
   d.on = true;
   d.mem_peers = reinterpret_cast<const float* const*>(v[0]);
@@ -108,6 +109,7 @@ inline PeerDesc peer_desc(const c10::optional<at::Tensor>& t) {
   d.node2root = reinterpret_cast<const int*>(v[4]);
   d.step_ctr = reinterpret_cast<const int64_t*>(v[5]);
   d.mem_new = reinterpret_cast<float*>(v[6]);
+  if (t->numel() >= 8) d.ts_peers = reinterpret_cast<const float* const*>(v[7]);
   return d;
 }
 

@@ -167,6 +167,99 @@ void tgn_memory_update(const at::Tensor& roots, const at::Tensor& n_roots, const
   gru_step(a, pad8(D), pad8(D), cell_w_ih, cell_w_hh, cell_b_ih, cell_b_hh, e, rmax, m_dev);
 }
 
+// JODIE memory updater: tanh RNN cell over the (single) newest mailbox slot,
+//   h' = tanh(W_ih m + b_ih + W_hh h + b_hh),
+// with the same outputs as tgn_memory_update (memory rows, memory_ts, mem_prev),
+// after recording the roots' memory_ts before the update (prev_ts) for the
+// time projection.
+void tgn_rnn_memory_update(const at::Tensor& roots, const at::Tensor& n_roots, const at::Tensor& mailbox,
+                           at::Tensor& memory, at::Tensor& memory_ts, const at::Tensor& ts_max,
+                           const at::Tensor& w_ih, const at::Tensor& w_hh, const at::Tensor& b_ih,
+                           const at::Tensor& b_hh, at::Tensor& mem_prev, at::Tensor& prev_ts,
+                           const c10::optional<at::Tensor>& peer) {
+  const PeerDesc pd = peer_desc(peer);
+  const int rmax = static_cast<int>(roots.numel());
+  const int D = static_cast<int>(memory.size(1));
+  const int SW = static_cast<int>(w_ih.size(1));
+  const int* m_dev = n_roots.data_ptr<int>();
+  const int64_t* ridx = roots.data_ptr<int64_t>();
+  TORCH_CHECK(!pd.on || pd.ts_peers != nullptr, "peer descriptor without memory_ts tables");
+  launch_jodie_prev_ts(cur_stream(), ridx, m_dev, rmax, memory_ts.data_ptr<float>(), pd.on ? pd.ts_peers : nullptr,
+                       pd.owner, prev_ts.data_ptr<float>());
+  SegSource a;
+  a.nrows_dev = m_dev;
+  a.nseg = 2;
+  a.seg[0] = seg_f32(mailbox.view({mailbox.size(0), -1}), SW, pad8(SW), ridx, 0);
+  if (pd.on) {
+    a.seg[0].kind = kSegSharded;
+    a.seg[0].peers = pd.mail_peers;
+    a.seg[0].owner = pd.owner;
+  }
+  a.seg[1] = seg_memory(memory, D, ridx, pd, false);
+  WeightSource b;
+  b.gate_group = kGateGroup;
+  b.L.nblk = 1;
+  b.L.nseg = 2;
+  b.L.blk_rows[0] = D;
+  b.L.blk_pad[0] = D;
+  b.L.seg_kpad[0] = pad8(SW);
+  b.L.seg_kpad[1] = pad8(D);
+  b.L.cell[0][0] = wcell(w_ih, 0, 0, SW);
+  b.L.cell[0][1] = wcell(w_hh, 0, 0, D);
+  EpiGRU e;
+  e.D = D;
+  e.DP = kGateGroup;
+  e.ngates = 1;
+  e.b_ih = b_ih.data_ptr<float>();
+  e.b_hh = b_hh.data_ptr<float>();
+  e.hprev = memory.data_ptr<float>();
+  e.hprev_index = ridx;
+  e.hprev_ld = D;
+  e.save_prev = mem_prev.data_ptr<float>();
+  if (pd.on) {
+    e.hprev_peers = pd.mem_peers;
+    e.hprev_owner = pd.owner;
+    e.hout = pd.mem_new;
+    e.hout_ld = D;
+  } else {
+    e.scatter = memory.data_ptr<float>();
+    e.scatter_index = ridx;
+    e.scatter_ld = D;
+    e.scatter_ts = memory_ts.data_ptr<float>();
+    e.ts_value = ts_max.data_ptr<float>();
+  }
+  GemmShape sh;
+  sh.M = rmax;
+  sh.m_dev = m_dev;
+  sh.N = kGateGroup * ((D + kGateGroup - 1) / kGateGroup);
+  sh.K = pad8(SW) + pad8(D);
+  gemm(a, b, e, sh, cur_stream());
+  SU_LAUNCH_CHECK();
+}
+
+// z = memory(roots) * (1 + w dt + b)  (JODIE time projection), dt saved for the backward
+void jodie_project(const at::Tensor& roots, const at::Tensor& n_roots, const at::Tensor& memory,
+                   const at::Tensor& prev_ts, const at::Tensor& root_ts, const at::Tensor& w, const at::Tensor& b,
+                   at::Tensor& out, at::Tensor& dt, const c10::optional<at::Tensor>& peer) {
+  const PeerDesc pd = peer_desc(peer);
+  launch_jodie_project(cur_stream(), roots.data_ptr<int64_t>(), n_roots.data_ptr<int>(),
+                       static_cast<int>(roots.numel()), memory.data_ptr<float>(), pd.on ? pd.mem_new : nullptr,
+                       static_cast<int>(memory.size(1)), prev_ts.data_ptr<float>(), root_ts.data_ptr<int64_t>(),
+                       w.data_ptr<float>(), b.data_ptr<float>(), out.data_ptr<float>(), dt.data_ptr<float>());
+  SU_LAUNCH_CHECK();
+}
+
+void jodie_project_bwd(const at::Tensor& roots, const at::Tensor& n_roots, const at::Tensor& memory,
+                       const at::Tensor& dt, const at::Tensor& dz, at::Tensor& dw, at::Tensor& db,
+                       const c10::optional<at::Tensor>& peer) {
+  const PeerDesc pd = peer_desc(peer);
+  launch_jodie_project_bwd(cur_stream(), roots.data_ptr<int64_t>(), n_roots.data_ptr<int>(),
+                           static_cast<int>(roots.numel()), memory.data_ptr<float>(), pd.on ? pd.mem_new : nullptr,
+                           static_cast<int>(memory.size(1)), dt.data_ptr<float>(), dz.data_ptr<float>(),
+                           dw.data_ptr<float>(), db.data_ptr<float>());
+  SU_LAUNCH_CHECK();
+}
+
 void tgn_mailbox_write(const at::Tensor& roots, const at::Tensor& n_roots, const at::Tensor& win,
                        const at::Tensor& cnt, const at::Tensor& src_idx, const at::Tensor& dst_idx,
                        const at::Tensor& ev_eid, const at::Tensor& ev_ts, const at::Tensor& mem_prev,

@@ -55,13 +55,17 @@ def build_ctdg_runtime(session_ctx: SessionContext, dataset: TGTemporalDataset |
     family = str(cfg["model"]["family"])
     seed = int(cfg.get("train", {}).get("seed", 0))
     torch.manual_seed(seed)
+    embedding = str(c.get("embedding") or ("time_projection" if family == "jodie" else "attention"))
     model = build_ctdg_model(family, num_nodes=dataset.num_nodes, hidden_dim=hidden, edge_feat_dim=edim,
                              dim_time=int(c.get("dim_time", 100)), num_head=int(c.get("num_head", 2)),
-                             dropout=float(c.get("dropout", 0.1)), att_dropout=float(c.get("att_dropout", 0.1)))
+                             dropout=float(c.get("dropout", 0.1)), att_dropout=float(c.get("att_dropout", 0.1)),
+                             embedding=embedding)
     model = model.to(device)
     mem_type = str(cfg["model"].get("memory", {}).get("type", "gru"))
-    updater = build_memory_updater("gru" if device.startswith("cuda") else mem_type, hidden_dim=hidden,
-                                   mailbox_slot_dim=2 * hidden + edim, mailbox_slots=slots).to(device)
+    if embedding == "time_projection":
+        mem_type = "rnn"  # JODIE: tanh-RNN memory updater
+    updater = build_memory_updater(mem_type, hidden_dim=hidden, mailbox_slot_dim=2 * hidden + edim,
+                                   mailbox_slots=slots).to(device)
     for p in updater.parameters():
         p.requires_grad_(bool(c.get("memory_grad", False)))
     sampling = cfg["sampling"]
@@ -72,7 +76,8 @@ def build_ctdg_runtime(session_ctx: SessionContext, dataset: TGTemporalDataset |
     lr = float(cfg.get("train", {}).get("lr", 1e-3))
     route = CTDGFeatureRoute(route_type=str(cfg["graph"]["route"]), world_size=dctx.world_size)
     engine = None
-    if device.startswith("cuda"):
+    fused_ok = (embedding == "time_projection") == (mem_type == "rnn")  # TGN+GRU or JODIE+RNN
+    if device.startswith("cuda") and fused_ok:
         from starry_unigraph.ops.tgn import TGNCudaEngine
 
         grad_sync = None

@@ -159,6 +159,34 @@ class CTDGLinkPredictor(nn.Module):
         return CTDGModelOutput(pos_logits=pos, neg_logits=neg)
 
 
+class CTDGJodiePredictor(nn.Module):
+    """JODIE embedding + the link predictor (Kumar et al., KDD'19; a flagged
+    variant: the reference maps every CTDG family to the attention model,
+    backends/ctdg/runtime/models.py:332-342). A node's embedding is its memory
+    projected to the query time, z = memory * (1 + w_p * dt + b_p), with dt the
+    time since the node's previous memory update; no neighbour sampling."""
+
+    def __init__(self, num_nodes: int, hidden_dim: int, edge_feat_dim: int, dim_time: int = 100, num_head: int = 2,
+                 dropout: float = 0.1, att_dropout: float = 0.1) -> None:
+        super().__init__()
+        self.hidden_dim = hidden_dim
+        self.time_proj = nn.Linear(1, hidden_dim)
+        nn.init.normal_(self.time_proj.weight, 0.0, 1.0 / (hidden_dim ** 0.5))
+        nn.init.zeros_(self.time_proj.bias)
+        self.src_fc = nn.Linear(hidden_dim, hidden_dim)
+        self.dst_fc = nn.Linear(hidden_dim, hidden_dim)
+        self.out_fc = nn.Linear(hidden_dim, 1)
+
+    def embed(self, memory: torch.Tensor, dt: torch.Tensor) -> torch.Tensor:
+        return memory * (1.0 + self.time_proj(dt.float().reshape(-1, 1)))
+
+    def forward(self, src_conv: torch.Tensor, dst_conv: torch.Tensor, neg_conv: torch.Tensor) -> CTDGModelOutput:
+        h_src = self.src_fc(src_conv)
+        pos = self.out_fc(F.relu(h_src + self.dst_fc(dst_conv))).squeeze(-1)
+        neg = self.out_fc(F.relu(h_src + self.dst_fc(neg_conv))).squeeze(-1)
+        return CTDGModelOutput(pos_logits=pos, neg_logits=neg)
+
+
 @dataclass(frozen=True)
 class CTDGModelSpec:
     model_cls: type[nn.Module]
@@ -175,10 +203,13 @@ CTDG_MODEL_SPECS: dict[str, CTDGModelSpec] = {
 
 
 def build_ctdg_model(model_family: str, *, num_nodes: int, hidden_dim: int, edge_feat_dim: int, dim_time: int = 100,
-                     num_head: int = 2, dropout: float = 0.1, att_dropout: float = 0.1) -> nn.Module:
+                     num_head: int = 2, dropout: float = 0.1, att_dropout: float = 0.1,
+                     embedding: str = "attention") -> nn.Module:
     spec = CTDG_MODEL_SPECS.get(model_family.lower())
     if spec is None:
         raise KeyError(f"Unsupported CTDG model family: {model_family}")
+    if str(embedding) == "time_projection":
+        return CTDGJodiePredictor(num_nodes=num_nodes, hidden_dim=hidden_dim, edge_feat_dim=edge_feat_dim)
     return spec.model_cls(num_nodes=num_nodes, hidden_dim=hidden_dim, edge_feat_dim=edge_feat_dim, dim_time=dim_time,
                           num_head=num_head, dropout=dropout, att_dropout=att_dropout)
 

@@ -34,7 +34,10 @@ from .sampler import CTDGSampleOutput, NativeTemporalSampler
 class CTDGPreparedBatch:
     batch: CTDGDataBatch
     neg_dst: torch.Tensor
-    sample: CTDGSampleOutput
+    sample: CTDGSampleOutput | None
+    roots: torch.Tensor | None = None
+    root_ts: int = 0
+    prev_ts: torch.Tensor | None = None  # memory_ts of the roots before this step's update (JODIE)
 
 
 def _grad_allreduce(params: list[torch.nn.Parameter], world_size: int) -> None:
@@ -94,12 +97,22 @@ class CTDGOnlineRuntime:
             neg = pool[idx]
         return neg
 
+    @property
+    def _jodie(self) -> bool:
+        from .models import CTDGJodiePredictor
+
+        return isinstance(self._core, CTDGJodiePredictor)
+
     def _prepare(self, batch: CTDGDataBatch) -> CTDGPreparedBatch:
         neg = self._negative_sample(batch)
         roots = torch.unique(torch.cat([batch.src, batch.dst])).long()
-        ts = torch.full((roots.numel(),), int(batch.ts.max().item()), dtype=torch.long)
+        root_ts = int(batch.ts.max().item())
+        if self._jodie:  # time-projection embedding: no neighbour sampling
+            prev = self.memory.memory_ts[roots.to(self.memory.memory_ts.device)].clone()
+            return CTDGPreparedBatch(batch, neg, None, roots, root_ts, prev)
+        ts = torch.full((roots.numel(),), root_ts, dtype=torch.long)
         split = batch.split if batch.split != "predict" else "test"
-        return CTDGPreparedBatch(batch, neg, self.sampler.sample(split, roots, ts))
+        return CTDGPreparedBatch(batch, neg, self.sampler.sample(split, roots, ts), roots, root_ts)
 
     def _edge_feats(self) -> torch.Tensor:
         if self._edge_feat_dev is None:
@@ -120,6 +133,14 @@ class CTDGOnlineRuntime:
         return out * valid.unsqueeze(1)
 
     def _conv_all(self, prepared: CTDGPreparedBatch) -> tuple[torch.Tensor, torch.Tensor]:
+        if self._jodie:
+            roots = prepared.roots.to(self.device)
+            h = self.memory.gather(roots)
+            if not self.memory_grad:
+                h = h.detach()
+            prev = prepared.prev_ts.to(self.device)
+            dt = torch.where(prev >= 0, float(prepared.root_ts) - prev, torch.zeros_like(prev))
+            return roots, self._core.embed(h, dt)
         blk = prepared.sample.blocks[0]
         roots = blk.roots.to(self.device)
         mask = blk.mask().to(self.device)
@@ -226,7 +247,7 @@ class CTDGOnlineRuntime:
         submit_ms = (time.perf_counter() - t1) * 1000.0
         return {"loss": float(loss.item()), "predictions": torch.sigmoid(pos).detach().cpu().tolist(),
                 "targets": [1] * batch.size,
-                "meta": {"split": batch.split, "batch_size": batch.size, "sample": prepared.sample.describe(),
+                "meta": {"split": batch.split, "batch_size": batch.size, "sample": prepared.sample.describe() if prepared.sample is not None else None,
                          "metrics": self._metric_dict(pos, neg), "memory": self.memory.describe(),
                          "sync_wait_ms": wait_ms, "sync_submit_ms": submit_ms,
                          "step_ms": (time.perf_counter() - t0) * 1000.0}}

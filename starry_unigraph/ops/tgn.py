@@ -72,13 +72,21 @@ class TGNCudaEngine:
         self.memory = memory
         dev = memory.memory.device
         self.device = dev
-        conv = model.conv
         D = memory.hidden_dim
         E = memory.edge_feat_dim
-        self.s = TGNShapes(bmax=int(bmax), k=int(fanout), D=D, E=E, T=conv.dim_time, Do=conv.dim_out,
-                           H=int(num_head), K=memory.mailbox_slots)
-        if self.s.T <= 0:
-            raise ValueError("the fused TGN step requires dim_time > 0")
+        # "tgn": attention embedding over sampled neighbours + GRU memory updater;
+        # "jodie": time-projection embedding of the memory + tanh-RNN updater (no sampling)
+        self.kind = "jodie" if not hasattr(model, "conv") else "tgn"
+        if self.kind == "jodie":
+            if memory.mailbox_slots != 1:
+                raise ValueError("the fused JODIE step keeps one mailbox slot per node")
+            self.s = TGNShapes(bmax=int(bmax), k=1, D=D, E=E, T=1, Do=D, H=1, K=1)
+        else:
+            conv = model.conv
+            self.s = TGNShapes(bmax=int(bmax), k=int(fanout), D=D, E=E, T=conv.dim_time, Do=conv.dim_out,
+                               H=int(num_head), K=memory.mailbox_slots)
+            if self.s.T <= 0:
+                raise ValueError("the fused TGN step requires dim_time > 0")
         self.policy = 0 if policy == "recent" else 1
         self.dropout = float(dropout)
         self.att_dropout = float(att_dropout)
@@ -160,6 +168,9 @@ class TGNCudaEngine:
         self.dagg = torch.zeros(R, s.Do, **f32)
         self.dKV = torch.zeros(R * k, 2 * s.Do, **f32)
         self.dQ = torch.zeros(R, s.Do, **f32)
+        if self.kind == "jodie":
+            self.prev_ts = torch.zeros(R, **f32)
+            self.jdt = torch.zeros(R, **f32)
 
     # ------------------------------------------------------------------ inputs
     def load_batch(self, src: torch.Tensor, dst: torch.Tensor, ts: torch.Tensor, eid: torch.Tensor) -> None:
@@ -192,7 +203,54 @@ class TGNCudaEngine:
         c = m.conv
         return m, u, c
 
+    def _forward_jodie(self, split: str, train: bool) -> None:
+        """JODIE step: memory update (tanh RNN) -> mailbox -> time projection of the
+        updated memory -> link scores / BCE -> [projection and link gradients -> Adam]."""
+        C, s = self.C, self.s
+        m, u = self.model, self.updater
+        mem = self.memory
+        C.tgn_prep(self.ev_src, self.ev_dst, self.ev_ts, self.n_ev, self.neg_pool, self.stamp, self.node2root,
+                   self.step_ctr, self.seed, self.roots, self.n_roots, self.src_idx, self.dst_idx, self.neg,
+                   self.neg_idx, self.ts_max, self.root_ts, self.win_key, self.win, self.cnt)
+        cell = u.memory_cell
+        C.tgn_rnn_memory_update(self.roots, self.n_roots, mem.mailbox, mem.memory, mem.memory_ts, self.ts_max,
+                                cell.weight_ih, cell.weight_hh, cell.bias_ih, cell.bias_hh, self.mem_prev,
+                                self.prev_ts, self._pd)
+        if self.peer is None:
+            C.tgn_mailbox_write(self.roots, self.n_roots, self.win, self.cnt, self.src_idx, self.dst_idx,
+                                self.ev_eid, self.ev_ts, self.mem_prev, self.efeat, s.E, mem.mailbox, mem.mailbox_ts,
+                                mem.next_mail_pos)
+        tp = m.time_proj
+        C.jodie_project(self.roots, self.n_roots, mem.memory, self.prev_ts, self.root_ts, tp.weight, tp.bias,
+                        self.out, self.jdt, self._pd)
+        C.tgn_link_proj(self.out, self.n_roots, m.src_fc.weight, m.src_fc.bias, m.dst_fc.weight, m.dst_fc.bias,
+                        self.P)
+        self.loss.zero_()
+        if train:
+            self.flat.zero_grad()
+            self.dP.zero_()
+        gw = {n.split(".", 1)[1]: v for n, v in self.flat.grad_views.items()}
+        C.tgn_link_loss(self.P, self.src_idx, self.dst_idx, self.neg_idx, self.n_ev, m.dst_fc.bias, m.out_fc.weight,
+                        m.out_fc.bias, train, self.scores, self.loss, self.dP, gw["out_fc.weight"], gw["out_fc.bias"],
+                        gw["dst_fc.bias"])
+        C.tgn_metrics(self.scores, self.n_ev, self.metrics)
+        if train:
+            C.tgn_link_proj_bwd(self.dP, self.out, self.n_roots, m.src_fc.weight, m.dst_fc.weight,
+                                gw["src_fc.weight"], gw["src_fc.bias"], gw["dst_fc.weight"], gw["dst_fc.bias"],
+                                self.dout)
+            C.jodie_project_bwd(self.roots, self.n_roots, mem.memory, self.jdt, self.dout,
+                                gw["time_proj.weight"], gw["time_proj.bias"], self._pd)
+            if self.peer is None:
+                scale = 1.0
+                if self.grad_sync is not None:
+                    scale = self.grad_sync(self.flat.grad)
+                self.opt.step(grad_scale=scale)
+        if self.peer is not None:
+            self._peer_sync(train)
+
     def _forward(self, split: str, train: bool) -> None:
+        if self.kind == "jodie":
+            return self._forward_jodie(split, train)
         C, s = self.C, self.s
         m, u, c = self._params()
         mem = self.memory

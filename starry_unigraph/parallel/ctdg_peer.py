@@ -75,10 +75,10 @@ class PeerCTDGContext:
 
     def descriptor(self, stamp: torch.Tensor, node2root: torch.Tensor, step_ctr: torch.Tensor,
                    mem_new: torch.Tensor) -> torch.Tensor:
-        """CPU int64 [7] descriptor consumed by the memory-reading TGN ops."""
+        """CPU int64 [8] descriptor consumed by the memory-reading TGN / JODIE ops."""
         return torch.tensor([self.tables["memory"].data_ptr(), self.tables["mailbox"].data_ptr(),
                              self.owner.data_ptr(), stamp.data_ptr(), node2root.data_ptr(), step_ctr.data_ptr(),
-                             mem_new.data_ptr()], dtype=torch.int64)
+                             mem_new.data_ptr(), self.tables["memory_ts"].data_ptr()], dtype=torch.int64)
 
     def barrier(self, C) -> None:
         C.peer_barrier(self.tables["flags"], self.rank, self.world, self.epoch, self.budget)

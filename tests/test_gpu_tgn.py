@@ -154,3 +154,43 @@ def test_eval_and_predict_run(tmp_path):
     assert 0.0 <= v["metrics"]["ap"] <= 1.0
     p = s.predict("test")
     assert len(p.predictions) > 0
+
+
+def _jodie_session(device, tmp_path, **over):
+    from starry_unigraph import SchedulerSession
+
+    cfg = _cfg(device, **over)
+    cfg["model"].update({"name": "jodie", "family": "jodie"})
+    s = SchedulerSession.from_config(cfg)
+    s.ctx.artifact_root = tmp_path / ("jodie_" + device.replace(":", "_"))
+    s.prepare_data()
+    s.build_runtime()
+    return s
+
+
+def test_jodie_fused_step_matches_cpu_oracle(tmp_path):
+    """JODIE (tanh-RNN memory + time projection): losses, predictions, memory and
+    mailbox (lr = 0), then the gradients of the trainable parameters."""
+    g = _jodie_session("cuda", tmp_path, train={"lr": 0.0})
+    c = _jodie_session("cpu", tmp_path, train={"lr": 0.0})
+    rg, rc = g.ctdg_session.online_runtime, c.ctdg_session.online_runtime
+    assert rg.engine is not None and rg.engine.kind == "jodie"
+    eng = rg.engine
+    for i, batch in enumerate(list(rc.iter_batches("train", 100))[:8]):
+        res_g = rg.train_step(batch)
+        neg = eng.neg[: batch.size].cpu()
+        rc._negative_sample = lambda b, neg=neg: neg
+        res_c = rc.train_step(batch)
+        assert abs(res_g["loss"] - res_c["loss"]) <= 1e-2 * max(1.0, abs(res_c["loss"])), (i, res_g["loss"],
+                                                                                           res_c["loss"])
+        pg, pc = torch.tensor(res_g["predictions"]), torch.tensor(res_c["predictions"])
+        assert float((pg - pc).abs().max()) < 1e-2, i
+    from starry_unigraph.ops import check_status
+
+    check_status()
+    assert torch.allclose(rg.memory.memory.cpu(), rc.memory.memory, atol=2e-2, rtol=2e-2)
+    assert torch.allclose(rg.memory.mailbox.cpu(), rc.memory.mailbox, atol=2e-2, rtol=2e-2)
+    for (n, pg), pc in zip(rg.model.named_parameters(), rc.model.parameters()):
+        a, b = pg.grad.detach().cpu(), pc.grad.detach()
+        rel = float((a - b).norm() / (b.norm() + 1e-8))
+        assert rel < 5e-2, (n, rel)
