@@ -107,8 +107,8 @@ void launch_tgn_metrics(dim3 grid, dim3 block, cudaStream_t st, const float* __r
 void launch_jodie_prev_ts(cudaStream_t st, const int64_t* roots, const int* n_roots, int rmax, const float* mem_ts,
                           const float* const* ts_peers, const int* owner, float* prev_ts);
 void launch_jodie_project(cudaStream_t st, const int64_t* roots, const int* n_roots, int rmax, const float* mem,
-                          const float* fresh, int D, const float* prev_ts, const int64_t* root_ts, const float* w,
-                          const float* b, float* out, float* dt_out);
+                          const float* fresh, int D, const float* prev_ts, const int64_t* root_ts, float dt_scale,
+                          const float* w, const float* b, float* out, float* dt_out);
 void launch_jodie_project_bwd(cudaStream_t st, const int64_t* roots, const int* n_roots, int rmax, const float* mem,
                               const float* fresh, int D, const float* dt, const float* dz, float* dw, float* db);
 

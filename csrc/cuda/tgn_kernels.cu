@@ -649,7 +649,7 @@ void launch_time_grad_finish(cudaStream_t st, const float* wk, const float* wv, 
 // ---------------------------------------------------------------------------
 // JODIE time-projection embedding (warp per root row)
 //   prev_ts[r] = memory_ts of root r before this step's memory update
-//   z[r, c]    = h[r, c] * (1 + w[c] * dt_r + b[c]),  dt_r = root_ts - prev_ts[r] (0 if never updated)
+//   z[r, c]    = h[r, c] * (1 + w[c] * dt_r + b[c]),  dt_r = (root_ts - prev_ts[r]) * dt_scale (0 if never updated)
 // h = the updated memory row: table row roots[r], or row r of `fresh` (multi-GPU step buffer).
 // ---------------------------------------------------------------------------
 __global__ void jodie_prev_ts_kernel(const int64_t* __restrict__ roots, const int* __restrict__ n_roots, int rmax,
@@ -668,13 +668,13 @@ __global__ void jodie_prev_ts_kernel(const int64_t* __restrict__ roots, const in
 __global__ void jodie_project_kernel(const int64_t* __restrict__ roots, const int* __restrict__ n_roots, int rmax,
                                      const float* __restrict__ mem, const float* __restrict__ fresh, int D,
                                      const float* __restrict__ prev_ts, const int64_t* __restrict__ root_ts,
-                                     const float* __restrict__ w, const float* __restrict__ b,
+                                     float dt_scale, const float* __restrict__ w, const float* __restrict__ b,
                                      float* __restrict__ out, float* __restrict__ dt_out) {
   const int r = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
   if (r >= rmax || r >= *n_roots) return;
   const float pt = prev_ts[r];
-  const float dt = pt >= 0.f ? static_cast<float>(*root_ts) - pt : 0.f;
+  const float dt = pt >= 0.f ? (static_cast<float>(*root_ts) - pt) * dt_scale : 0.f;
   if (lane == 0) dt_out[r] = dt;
   const float* h = fresh ? fresh + static_cast<int64_t>(r) * D : mem + roots[r] * D;
   float* o = out + static_cast<int64_t>(r) * D;
@@ -709,12 +709,12 @@ void launch_jodie_prev_ts(cudaStream_t st, const int64_t* roots, const int* n_ro
 }
 
 void launch_jodie_project(cudaStream_t st, const int64_t* roots, const int* n_roots, int rmax, const float* mem,
-                          const float* fresh, int D, const float* prev_ts, const int64_t* root_ts, const float* w,
-                          const float* b, float* out, float* dt_out) {
+                          const float* fresh, int D, const float* prev_ts, const int64_t* root_ts, float dt_scale,
+                          const float* w, const float* b, float* out, float* dt_out) {
   if (rmax <= 0) return;
   count_launch();
   jodie_project_kernel<<<(rmax * 32 + 255) / 256, 256, 0, st>>>(roots, n_roots, rmax, mem, fresh, D, prev_ts,
-                                                                 root_ts, w, b, out, dt_out);
+                                                                 root_ts, dt_scale, w, b, out, dt_out);
 }
 
 void launch_jodie_project_bwd(cudaStream_t st, const int64_t* roots, const int* n_roots, int rmax, const float* mem,

@@ -116,8 +116,8 @@ void tgn_rnn_memory_update(const at::Tensor& roots, const at::Tensor& n_roots, c
                            const at::Tensor& b_hh, at::Tensor& mem_prev, at::Tensor& prev_ts,
                            const c10::optional<at::Tensor>& peer);
 void jodie_project(const at::Tensor& roots, const at::Tensor& n_roots, const at::Tensor& memory,
-                   const at::Tensor& prev_ts, const at::Tensor& root_ts, const at::Tensor& w, const at::Tensor& b,
-                   at::Tensor& out, at::Tensor& dt, const c10::optional<at::Tensor>& peer);
+                   const at::Tensor& prev_ts, const at::Tensor& root_ts, double dt_scale, const at::Tensor& w,
+                   const at::Tensor& b, at::Tensor& out, at::Tensor& dt, const c10::optional<at::Tensor>& peer);
 void jodie_project_bwd(const at::Tensor& roots, const at::Tensor& n_roots, const at::Tensor& memory,
                        const at::Tensor& dt, const at::Tensor& dz, at::Tensor& dw, at::Tensor& db,
                        const c10::optional<at::Tensor>& peer);

@@ -239,13 +239,14 @@ void tgn_rnn_memory_update(const at::Tensor& roots, const at::Tensor& n_roots, c
 
 // z = memory(roots) * (1 + w dt + b)  (JODIE time projection), dt saved for the backward
 void jodie_project(const at::Tensor& roots, const at::Tensor& n_roots, const at::Tensor& memory,
-                   const at::Tensor& prev_ts, const at::Tensor& root_ts, const at::Tensor& w, const at::Tensor& b,
-                   at::Tensor& out, at::Tensor& dt, const c10::optional<at::Tensor>& peer) {
+                   const at::Tensor& prev_ts, const at::Tensor& root_ts, double dt_scale, const at::Tensor& w,
+                   const at::Tensor& b, at::Tensor& out, at::Tensor& dt, const c10::optional<at::Tensor>& peer) {
   const PeerDesc pd = peer_desc(peer);
   launch_jodie_project(cur_stream(), roots.data_ptr<int64_t>(), n_roots.data_ptr<int>(),
                        static_cast<int>(roots.numel()), memory.data_ptr<float>(), pd.on ? pd.mem_new : nullptr,
                        static_cast<int>(memory.size(1)), prev_ts.data_ptr<float>(), root_ts.data_ptr<int64_t>(),
-                       w.data_ptr<float>(), b.data_ptr<float>(), out.data_ptr<float>(), dt.data_ptr<float>());
+                       static_cast<float>(dt_scale), w.data_ptr<float>(), b.data_ptr<float>(), out.data_ptr<float>(),
+                       dt.data_ptr<float>());
   SU_LAUNCH_CHECK();
 }
 

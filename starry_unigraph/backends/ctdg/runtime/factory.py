@@ -60,6 +60,9 @@ def build_ctdg_runtime(session_ctx: SessionContext, dataset: TGTemporalDataset |
                              dim_time=int(c.get("dim_time", 100)), num_head=int(c.get("num_head", 2)),
                              dropout=float(c.get("dropout", 0.1)), att_dropout=float(c.get("att_dropout", 0.1)),
                              embedding=embedding)
+    if hasattr(model, "dt_scale"):
+        span = float(dataset.ts.max() - dataset.ts.min()) if dataset.ts.numel() else 1.0
+        model.dt_scale = 1.0 / max(span, 1.0)
     model = model.to(device)
     mem_type = str(cfg["model"].get("memory", {}).get("type", "gru"))
     if embedding == "time_projection":

@@ -176,9 +176,12 @@ class CTDGJodiePredictor(nn.Module):
         self.src_fc = nn.Linear(hidden_dim, hidden_dim)
         self.dst_fc = nn.Linear(hidden_dim, hidden_dim)
         self.out_fc = nn.Linear(hidden_dim, 1)
+        # time deltas enter the projection in units of the stream's time span (JODIE normalises
+        # deltas; raw seconds would scale embeddings by ~1e5)
+        self.dt_scale = 1.0
 
     def embed(self, memory: torch.Tensor, dt: torch.Tensor) -> torch.Tensor:
-        return memory * (1.0 + self.time_proj(dt.float().reshape(-1, 1)))
+        return memory * (1.0 + self.time_proj((dt.float() * self.dt_scale).reshape(-1, 1)))
 
     def forward(self, src_conv: torch.Tensor, dst_conv: torch.Tensor, neg_conv: torch.Tensor) -> CTDGModelOutput:
         h_src = self.src_fc(src_conv)

@@ -221,8 +221,8 @@ class TGNCudaEngine:
                                 self.ev_eid, self.ev_ts, self.mem_prev, self.efeat, s.E, mem.mailbox, mem.mailbox_ts,
                                 mem.next_mail_pos)
         tp = m.time_proj
-        C.jodie_project(self.roots, self.n_roots, mem.memory, self.prev_ts, self.root_ts, tp.weight, tp.bias,
-                        self.out, self.jdt, self._pd)
+        C.jodie_project(self.roots, self.n_roots, mem.memory, self.prev_ts, self.root_ts, float(m.dt_scale),
+                        tp.weight, tp.bias, self.out, self.jdt, self._pd)
         C.tgn_link_proj(self.out, self.n_roots, m.src_fc.weight, m.src_fc.bias, m.dst_fc.weight, m.dst_fc.bias,
                         self.P)
         self.loss.zero_()

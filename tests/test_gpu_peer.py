@@ -105,3 +105,100 @@ def test_memory_writeback_and_mail_claims():
     assert torch.equal(mail[1][1][2 * D:], efeat[11])
     assert float(mail_ts[1][3]) == 7.0 and torch.equal(mail[1][3][2 * D:], efeat[21])
     assert float(mail_ts[0][2]) == 5.0 and torch.equal(mail[0][2][2 * D:], efeat[12])
+
+
+def test_sharded_memory_reads_match_local_table():
+    """The attention projections with node memory split over two emulated owner
+    tables (peer descriptor) equal the same projections on the full table, with
+    this step's roots read from the fresh-row buffer when stamped."""
+    C = _C()
+    torch.manual_seed(0)
+    N, D, E, T, Do, k, R = 64, 32, 8, 16, 32, 5, 24
+    dev = "cuda"
+    mem_full = torch.randn(N, D, device=dev)
+    owner = (torch.arange(N, device=dev) % 2).int()
+    tables = [torch.zeros(N, D, device=dev) for _ in range(2)]
+    for q in range(2):
+        tables[q][owner == q] = mem_full[owner == q]
+    roots = torch.randperm(N, device=dev)[:R].long()
+    n_roots = torch.tensor([R], dtype=torch.int32, device=dev)
+    nbr = torch.randint(0, N, (R * k,), device=dev)
+    nbr_eid = torch.randint(0, 50, (R * k,), device=dev)
+    nbr_dt = torch.rand(R * k, device=dev) * 1e4
+    nbr_cnt = torch.full((R,), k, dtype=torch.int32, device=dev)
+    efeat = torch.randn(50, E, device=dev)
+    te_w, te_b = torch.randn(T, device=dev), torch.randn(T, device=dev)
+    wq, bq = torch.randn(Do, D + T, device=dev), torch.randn(Do, device=dev)
+    wk, bk = torch.randn(Do, D + E + T, device=dev), torch.randn(Do, device=dev)
+    wv, bv = torch.randn(Do, D + E + T, device=dev), torch.randn(Do, device=dev)
+    Q0, KV0 = torch.zeros(R, Do, device=dev), torch.zeros(R * k, 2 * Do, device=dev)
+    C.tgn_attn_proj(mem_full, roots, n_roots, nbr, nbr_eid, nbr_dt, nbr_cnt, efeat, E, te_w, te_b, wq, bq, wk, bk,
+                    wv, bv, Q0, KV0, None)
+    # peer view: rows from the owners' tables; stamps never match the step tag -> no fresh rows
+    stamp = torch.zeros(N, dtype=torch.int32, device=dev)
+    node2root = torch.zeros(N, dtype=torch.int32, device=dev)
+    step = torch.full((1,), 7, dtype=torch.int64, device=dev)
+    mem_new = torch.zeros(R, D, device=dev)
+    desc = torch.tensor([_table(*tables).data_ptr(), 0, owner.data_ptr(), stamp.data_ptr(), node2root.data_ptr(),
+                         step.data_ptr(), mem_new.data_ptr(), 0], dtype=torch.int64)
+    keep = _table(*tables)  # keep the pointer table alive
+    desc[0] = keep.data_ptr()
+    Q1, KV1 = torch.zeros_like(Q0), torch.zeros_like(KV0)
+    C.tgn_attn_proj(torch.zeros(N, D, device=dev), roots, n_roots, nbr, nbr_eid, nbr_dt, nbr_cnt, efeat, E, te_w,
+                    te_b, wq, bq, wk, bk, wv, bv, Q1, KV1, desc)
+    torch.cuda.synchronize()
+    torch.testing.assert_close(Q1, Q0)
+    torch.testing.assert_close(KV1, KV0)
+    # stamped roots come from mem_new (tag = ((step - 1) & 0x3FFFFFFF) + 1 = 7)
+    stamp[roots] = 7
+    node2root[roots] = torch.arange(R, dtype=torch.int32, device=dev)
+    mem_new.copy_(mem_full[roots] * 2.0)
+    C.tgn_attn_proj(torch.zeros(N, D, device=dev), roots, n_roots, nbr, nbr_eid, nbr_dt, nbr_cnt, efeat, E, te_w,
+                    te_b, wq, bq, wk, bk, wv, bv, Q1, KV1, desc)
+    mem_ref = mem_full.clone()
+    mem_ref[roots] = mem_full[roots] * 2.0
+    C.tgn_attn_proj(mem_ref, roots, n_roots, nbr, nbr_eid, nbr_dt, nbr_cnt, efeat, E, te_w, te_b, wq, bq, wk, bk,
+                    wv, bv, Q0, KV0, None)
+    torch.cuda.synchronize()
+    torch.testing.assert_close(Q1, Q0)
+    torch.testing.assert_close(KV1, KV0)
+
+
+def test_halo_gather_and_push_kernels():
+    """Aggregation reading source rows from two emulated ranks' staging buffers,
+    and its transposed push, against dense references."""
+    C = _C()
+    torch.manual_seed(1)
+    F, n_dst, n_src = 64, 40, 70
+    src_owner = torch.randint(0, 2, (n_src,), dtype=torch.int32, device="cuda")
+    src_row = torch.zeros(n_src, dtype=torch.int32, device="cuda")
+    counts = [0, 0]
+    for i, o in enumerate(src_owner.tolist()):
+        src_row[i] = counts[o]
+        counts[o] += 1
+    stages = [torch.zeros(max(counts), F, device="cuda") for _ in range(2)]
+    x_src = torch.randn(n_src, F, device="cuda")
+    for i, (o, r) in enumerate(zip(src_owner.tolist(), src_row.tolist())):
+        stages[o][r] = x_src[i]
+    E = 400
+    src = torch.randint(0, n_src, (E,), device="cuda")
+    dst = torch.randint(0, n_dst, (E,), device="cuda")
+    val = torch.rand(E, device="cuda")
+    order = torch.argsort(dst, stable=True)
+    rowptr = torch.zeros(n_dst + 1, dtype=torch.int64, device="cuda")
+    rowptr[1:] = torch.cumsum(torch.bincount(dst, minlength=n_dst), 0)
+    out = C.spmm_peer_gather(rowptr, src[order].int().contiguous(), val[order].contiguous(), _table(*stages),
+                             src_owner, src_row, n_dst, F)
+    ref = torch.zeros(n_dst, F, device="cuda").index_add_(0, dst, x_src[src] * val[:, None])
+    torch.testing.assert_close(out, ref, rtol=1e-5, atol=1e-5)
+    # backward push: grad of source rows lands in the owners' buffers
+    g = torch.randn(n_dst, F, device="cuda")
+    order_t = torch.argsort(src, stable=True)
+    rowptr_t = torch.zeros(n_src + 1, dtype=torch.int64, device="cuda")
+    rowptr_t[1:] = torch.cumsum(torch.bincount(src, minlength=n_src), 0)
+    gbufs = [torch.zeros_like(s) for s in stages]
+    C.spmm_peer_push(rowptr_t, dst[order_t].int().contiguous(), val[order_t].contiguous(), g, n_src,
+                     _table(*gbufs), src_owner, src_row)
+    gref = torch.zeros(n_src, F, device="cuda").index_add_(0, src, g[dst] * val[:, None])
+    got = torch.stack([gbufs[o][r] for o, r in zip(src_owner.tolist(), src_row.tolist())])
+    torch.testing.assert_close(got, gref, rtol=1e-5, atol=1e-5)
