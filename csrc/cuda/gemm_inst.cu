@@ -109,19 +109,43 @@ void gemm_with_status(const MNView<SegSource>& a, const MNView<SegSource>& b, co
 // workspace that grows outside stream capture only; a call that would need to
 // grow it during capture runs the fused-producer kernel instead.
 // ---------------------------------------------------------------------------
-static uint8_t* g_ws[64] = {nullptr};
-static size_t g_ws_bytes[64] = {0};
+// One workspace per (device, stream): GEMMs issued concurrently on different
+// streams (weight gradients overlapping data gradients) must not share images.
+struct Workspace {
+  cudaStream_t stream = nullptr;
+  uint8_t* ptr = nullptr;
+  size_t bytes = 0;
+};
+constexpr int kMaxStreamsPerDevice = 8;
+static Workspace g_ws[64][kMaxStreamsPerDevice];
 
 static uint8_t* workspace(int device, size_t bytes, cudaStream_t st) {
-  if (bytes <= g_ws_bytes[device]) return g_ws[device];
+  Workspace* w = nullptr;
+  for (int i = 0; i < kMaxStreamsPerDevice; ++i) {
+    if (g_ws[device][i].ptr != nullptr && g_ws[device][i].stream == st) {
+      w = &g_ws[device][i];
+      break;
+    }
+  }
+  if (w == nullptr) {
+    for (int i = 0; i < kMaxStreamsPerDevice; ++i) {
+      if (g_ws[device][i].ptr == nullptr) {
+        w = &g_ws[device][i];
+        w->stream = st;
+        break;
+      }
+    }
+  }
+  if (w == nullptr) return nullptr;  // too many streams: the caller falls back to the fused-producer kernel
+  if (bytes <= w->bytes) return w->ptr;
   cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
   cudaStreamIsCapturing(st, &cs);
   if (cs != cudaStreamCaptureStatusNone) return nullptr;
-  if (g_ws[device] != nullptr) {
+  if (w->ptr != nullptr) {
     cudaDeviceSynchronize();  // earlier kernels may still read the old image
-    cudaFree(g_ws[device]);
-    g_ws[device] = nullptr;
-    g_ws_bytes[device] = 0;
+    cudaFree(w->ptr);
+    w->ptr = nullptr;
+    w->bytes = 0;
   }
   const size_t want = bytes + bytes / 2;
   void* p = nullptr;
@@ -129,9 +153,10 @@ static uint8_t* workspace(int device, size_t bytes, cudaStream_t st) {
     cudaGetLastError();
     return nullptr;
   }
-  g_ws[device] = static_cast<uint8_t*>(p);
-  g_ws_bytes[device] = want;
-  return g_ws[device];
+  w->ptr = static_cast<uint8_t*>(p);
+  w->bytes = want;
+  w->stream = st;
+  return w->ptr;
 }
 
 static bool packed_disabled() {

@@ -55,10 +55,12 @@ void tgn_attn_proj_bwd(const at::Tensor& memory, const at::Tensor& roots, const 
                        const at::Tensor& te_b, const at::Tensor& wq, const at::Tensor& wk, const at::Tensor& wv,
                        const at::Tensor& dQ, const at::Tensor& dKV, at::Tensor& g_wq, at::Tensor& g_bq,
                        at::Tensor& g_wk, at::Tensor& g_bk, at::Tensor& g_wv, at::Tensor& g_bv, at::Tensor& g_tw,
-                       at::Tensor& g_tb, const c10::optional<at::Tensor>& peer);
+                       at::Tensor& g_tb, at::Tensor& M_t, at::Tensor& M_1, const c10::optional<at::Tensor>& peer,
+                       int64_t part);
 void tgn_out_proj_bwd(const at::Tensor& dpre, const at::Tensor& agg, const at::Tensor& memory,
                       const at::Tensor& roots, const at::Tensor& n_roots, const at::Tensor& w_out, at::Tensor& g_wout,
-                      at::Tensor& g_bout, at::Tensor& dagg, const c10::optional<at::Tensor>& peer);
+                      at::Tensor& g_bout, at::Tensor& dagg, const c10::optional<at::Tensor>& peer,
+                      int64_t part);
 void tgn_link_proj(const at::Tensor& out, const at::Tensor& n_roots, const at::Tensor& w_src, const at::Tensor& b_src,
                    const at::Tensor& w_dst, const at::Tensor& b_dst, at::Tensor& P);
 void tgn_link_loss(const at::Tensor& P, const at::Tensor& src_idx, const at::Tensor& dst_idx,
@@ -68,7 +70,7 @@ void tgn_link_loss(const at::Tensor& P, const at::Tensor& src_idx, const at::Ten
 void tgn_metrics(const at::Tensor& scores, const at::Tensor& n_ev, at::Tensor& out);
 void tgn_link_proj_bwd(const at::Tensor& dP, const at::Tensor& out, const at::Tensor& n_roots,
                        const at::Tensor& w_src, const at::Tensor& w_dst, at::Tensor& g_wsrc, at::Tensor& g_bsrc,
-                       at::Tensor& g_wdst, at::Tensor& g_bdst, at::Tensor& dout);
+                       at::Tensor& g_wdst, at::Tensor& g_bdst, at::Tensor& dout, int64_t part);
 void adam_flat(at::Tensor& p, const at::Tensor& g, at::Tensor& m, at::Tensor& v, at::Tensor& step, at::Tensor& done,
                double lr, double b1, double b2, double eps, double wd, double grad_scale);
 

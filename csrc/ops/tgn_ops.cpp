@@ -481,8 +481,10 @@ void tgn_attn_proj_bwd(const at::Tensor& memory, const at::Tensor& roots, const 
                        const at::Tensor& te_b, const at::Tensor& wq, const at::Tensor& wk, const at::Tensor& wv,
                        const at::Tensor& dQ, const at::Tensor& dKV, at::Tensor& g_wq, at::Tensor& g_bq,
                        at::Tensor& g_wk, at::Tensor& g_bk, at::Tensor& g_wv, at::Tensor& g_bv, at::Tensor& g_tw,
-                       at::Tensor& g_tb,
-    const c10::optional<at::Tensor>& peer) {
+                       at::Tensor& g_tb, at::Tensor& M_t, at::Tensor& M_1,
+    const c10::optional<at::Tensor>& peer, int64_t part) {
+  // part 0: all; 1: W_q / b_q gradients; 2: W_k, W_v gradients and the encoder products M_t, M_1
+  // ([2*Do, T] buffers of the caller); 3: the encoder gradient from M_t, M_1 and g_bq
   const PeerDesc pd = peer_desc(peer);
   const int rmax = static_cast<int>(roots.numel());
   const int k = static_cast<int>(nbr.numel() / rmax);
@@ -492,7 +494,7 @@ void tgn_attn_proj_bwd(const at::Tensor& memory, const at::Tensor& roots, const 
   const int Ei = static_cast<int>(E);
   const int Ew = std::min<int>(Ei, static_cast<int>(efeat.size(1)));
   // ---------------- W_q, b_q
-  {
+  if (part == 0 || part == 1) {
     SegSource dy;
     dy.nrows_dev = n_roots.data_ptr<int>();
     dy.nseg = 1;
@@ -520,9 +522,10 @@ void tgn_attn_proj_bwd(const at::Tensor& memory, const at::Tensor& roots, const 
   // The encoder gradient is  dw[c] = sum_r dT[r,c] (-sin(w_c t_r + b_c)) t_r  with  dT = dKV W_kv[:, time],
   // i.e.  dw[c] = sum_o W_kv[o, time c] * M_t[o, c],  M_t = dKV^T (-sin(..) t)  (and M_1 without t for db):
   // two extra column segments of this weight-gradient GEMM, then a T-wide finishing kernel.
-  {
-    at::Tensor M_t = at::zeros({2 * Do, T}, dKV.options());
-    at::Tensor M_1 = at::zeros({2 * Do, T}, dKV.options());
+  TORCH_CHECK(M_t.numel() == 2 * Do * T && M_1.numel() == 2 * Do * T, "encoder product buffers must be [2*Do, T]");
+  if (part == 0 || part == 2) {
+    M_t.zero_();
+    M_1.zero_();
     SegSource dy;
     dy.group = k;
     dy.gcount = nbr_cnt.data_ptr<int>();
@@ -564,6 +567,8 @@ void tgn_attn_proj_bwd(const at::Tensor& memory, const at::Tensor& roots, const 
     }
     float* bg[4] = {g_bk.data_ptr<float>(), g_bv.data_ptr<float>(), nullptr, nullptr};
     proj_wgrad(dy, 2 * Do, x, pad8(D) + pad8(Ei) + pad8(T) + 8 + 2 * pad8(T), rmax * k, L, bg, 3);
+  }
+  if (part == 0 || part == 3) {
     // Q side: roots encode t = 0, so only db gets  -sin(b_c) sum_o W_q[o, time c] * (sum_rows dQ[r, o]);
     // the row sum of dQ is this step's b_q gradient (computed above)
     launch_time_grad_finish(cur_stream(), wk.data_ptr<float>(), wv.data_ptr<float>(), static_cast<int>(wk.stride(0)),
@@ -578,12 +583,13 @@ void tgn_attn_proj_bwd(const at::Tensor& memory, const at::Tensor& roots, const 
 void tgn_out_proj_bwd(const at::Tensor& dpre, const at::Tensor& agg, const at::Tensor& memory,
                       const at::Tensor& roots, const at::Tensor& n_roots, const at::Tensor& w_out, at::Tensor& g_wout,
                       at::Tensor& g_bout, at::Tensor& dagg,
-    const c10::optional<at::Tensor>& peer) {
+    const c10::optional<at::Tensor>& peer, int64_t part) {
+  // part 0: both; 1: weight gradients only; 2: data gradient only
   const PeerDesc pd = peer_desc(peer);
   const int rmax = static_cast<int>(roots.numel());
   const int Do = static_cast<int>(w_out.size(0));
   const int D = static_cast<int>(memory.size(1));
-  {
+  if (part != 2) {
     SegSource dy;
     dy.nrows_dev = n_roots.data_ptr<int>();
     dy.nseg = 1;
@@ -607,7 +613,7 @@ void tgn_out_proj_bwd(const at::Tensor& dpre, const at::Tensor& agg, const at::T
     float* bg[4] = {g_bout.data_ptr<float>(), nullptr, nullptr, nullptr};
     proj_wgrad(dy, Do, x, pad8(Do) + pad8(D) + 8, rmax, L, bg, 2);
   }
-  {
+  if (part != 1) {
     SegSource a;
     a.nrows_dev = n_roots.data_ptr<int>();
     a.nseg = 1;
@@ -695,11 +701,12 @@ void tgn_metrics(const at::Tensor& scores, const at::Tensor& n_ev, at::Tensor& o
 // and d(out) = dP [W_src; W_dst].
 void tgn_link_proj_bwd(const at::Tensor& dP, const at::Tensor& out, const at::Tensor& n_roots,
                        const at::Tensor& w_src, const at::Tensor& w_dst, at::Tensor& g_wsrc, at::Tensor& g_bsrc,
-                       at::Tensor& g_wdst, at::Tensor& g_bdst, at::Tensor& dout) {
+                       at::Tensor& g_wdst, at::Tensor& g_bdst, at::Tensor& dout, int64_t part) {
+  // part 0: both; 1: weight gradients only; 2: data gradient only (callers overlap the two on two streams)
   const int rmax = static_cast<int>(out.size(0));
   const int D = static_cast<int>(out.size(1));
   const int Dp = static_cast<int>(w_src.size(0));
-  {
+  if (part != 2) {
     SegSource dy;
     dy.nrows_dev = n_roots.data_ptr<int>();
     dy.nseg = 1;
@@ -723,7 +730,7 @@ void tgn_link_proj_bwd(const at::Tensor& dP, const at::Tensor& out, const at::Te
     float* bg[4] = {g_bsrc.data_ptr<float>(), g_bdst.data_ptr<float>(), nullptr, nullptr};
     proj_wgrad(dy, 2 * Dp, x, pad8(D) + 8, rmax, L, bg, 1);
   }
-  {
+  if (part != 1) {
     SegSource a;
     a.nrows_dev = n_roots.data_ptr<int>();
     a.nseg = 1;

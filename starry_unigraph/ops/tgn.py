@@ -114,6 +114,7 @@ class TGNCudaEngine:
         self._graphs: dict[tuple[str, bool], torch.cuda.CUDAGraph] = {}
         self._warm: dict[tuple[str, bool], int] = {}
         self._launches: dict[tuple[str, bool], int] = {}  # library kernel launches per step, counted eagerly
+        self._side = torch.cuda.Stream(self.device)  # weight-gradient GEMMs overlap the data-gradient chain
 
     # ------------------------------------------------------------------ buffers
     def _alloc(self) -> None:
@@ -168,6 +169,8 @@ class TGNCudaEngine:
         self.dagg = torch.zeros(R, s.Do, **f32)
         self.dKV = torch.zeros(R * k, 2 * s.Do, **f32)
         self.dQ = torch.zeros(R, s.Do, **f32)
+        self.Mt = torch.zeros(2 * s.Do, s.T, **f32)  # time-encoder products of the W_kv weight gradient
+        self.M1 = torch.zeros(2 * s.Do, s.T, **f32)
         if self.kind == "jodie":
             self.prev_ts = torch.zeros(R, **f32)
             self.jdt = torch.zeros(R, **f32)
@@ -237,7 +240,7 @@ class TGNCudaEngine:
         if train:
             C.tgn_link_proj_bwd(self.dP, self.out, self.n_roots, m.src_fc.weight, m.dst_fc.weight,
                                 gw["src_fc.weight"], gw["src_fc.bias"], gw["dst_fc.weight"], gw["dst_fc.bias"],
-                                self.dout)
+                                self.dout, 0)
             C.jodie_project_bwd(self.roots, self.n_roots, mem.memory, self.jdt, self.dout,
                                 gw["time_proj.weight"], gw["time_proj.bias"], self._pd)
             if self.peer is None:
@@ -318,24 +321,46 @@ class TGNCudaEngine:
         P.barrier(C)
 
     def _backward(self, gw: dict[str, torch.Tensor]) -> None:
+        """Data gradients on the main stream; every weight-gradient GEMM forks onto a
+        side stream as soon as its inputs exist, and the two join before Adam (the
+        fork/join is captured into the CUDA graph as dependencies)."""
         C, s = self.C, self.s
         m, u, c = self._params()
         mem = self.memory
+        main = torch.cuda.current_stream(self.device)
+        side = self._side
+
+        def fork():
+            side.wait_stream(main)
+            return torch.cuda.stream(side)
+
+        with fork():
+            C.tgn_link_proj_bwd(self.dP, self.out, self.n_roots, m.src_fc.weight, m.dst_fc.weight,
+                                gw["src_fc.weight"], gw["src_fc.bias"], gw["dst_fc.weight"], gw["dst_fc.bias"],
+                                self.dout, 1)
         C.tgn_link_proj_bwd(self.dP, self.out, self.n_roots, m.src_fc.weight, m.dst_fc.weight, gw["src_fc.weight"],
-                            gw["src_fc.bias"], gw["dst_fc.weight"], gw["dst_fc.bias"], self.dout)
+                            gw["src_fc.bias"], gw["dst_fc.weight"], gw["dst_fc.bias"], self.dout, 2)
         C.tgn_out_bwd(self.dout, self.xsave, self.mean, self.rstd, c.layer_norm.weight, self.n_roots, self.dropout,
                       self.seed, self.step_ctr, self.edge_total, self.dpre, gw["conv.layer_norm.weight"],
                       gw["conv.layer_norm.bias"])
+        with fork():
+            C.tgn_out_proj_bwd(self.dpre, self.agg, mem.memory, self.roots, self.n_roots, c.w_out.weight,
+                               gw["conv.w_out.weight"], gw["conv.w_out.bias"], self.dagg, self._pd, 1)
         C.tgn_out_proj_bwd(self.dpre, self.agg, mem.memory, self.roots, self.n_roots, c.w_out.weight,
-                           gw["conv.w_out.weight"], gw["conv.w_out.bias"], self.dagg, self._pd)
+                           gw["conv.w_out.weight"], gw["conv.w_out.bias"], self.dagg, self._pd, 2)
         C.tgn_attn_bwd(self.Q, self.KV, self.att_p, self.dagg, self.nbr_cnt, self.n_roots, s.H, self.att_dropout,
                        self.seed, self.step_ctr, self.dKV, self.dQ)
         te = c.time_enc.w
-        C.tgn_attn_proj_bwd(mem.memory, self.roots, self.n_roots, self.nbr, self.nbr_eid, self.nbr_dt, self.nbr_cnt,
-                            self.efeat, s.E, te.weight, te.bias, c.w_q.weight, c.w_k.weight, c.w_v.weight, self.dQ,
-                            self.dKV, gw["conv.w_q.weight"], gw["conv.w_q.bias"], gw["conv.w_k.weight"],
-                            gw["conv.w_k.bias"], gw["conv.w_v.weight"], gw["conv.w_v.bias"],
-                            gw["conv.time_enc.w.weight"], gw["conv.time_enc.w.bias"], self._pd)
+        args = (mem.memory, self.roots, self.n_roots, self.nbr, self.nbr_eid, self.nbr_dt, self.nbr_cnt, self.efeat,
+                s.E, te.weight, te.bias, c.w_q.weight, c.w_k.weight, c.w_v.weight, self.dQ, self.dKV,
+                gw["conv.w_q.weight"], gw["conv.w_q.bias"], gw["conv.w_k.weight"], gw["conv.w_k.bias"],
+                gw["conv.w_v.weight"], gw["conv.w_v.bias"], gw["conv.time_enc.w.weight"],
+                gw["conv.time_enc.w.bias"], self.Mt, self.M1, self._pd)
+        with fork():
+            C.tgn_attn_proj_bwd(*args, 1)
+        C.tgn_attn_proj_bwd(*args, 2)
+        main.wait_stream(side)
+        C.tgn_attn_proj_bwd(*args, 3)
         if self.peer is not None:
             return  # all-reduce + Adam run fused in _peer_sync
         scale = 1.0
