@@ -159,6 +159,16 @@ static uint8_t* workspace(int device, size_t bytes, cudaStream_t st) {
   return w->ptr;
 }
 
+// Optional stream-ordered allocator for the packed images (set by the torch
+// extension to the caching allocator, which also serves stream capture from the
+// graph's private pool). Without it the per-stream workspaces above are used.
+static WorkspaceAlloc g_ws_alloc = nullptr;
+static WorkspaceFree g_ws_free = nullptr;
+void set_workspace_allocator(WorkspaceAlloc a, WorkspaceFree f) {
+  g_ws_alloc = a;
+  g_ws_free = f;
+}
+
 static bool packed_disabled() {
   static int v = -1;
   if (v < 0) {
@@ -189,7 +199,7 @@ static bool launch_packed(const A& a, const B& b, const E& e, const GemmShape& s
   const size_t abytes = packed_bytes(sh.M, sh.K, kBM);
   const size_t bbytes = packed_bytes(sh.N, sh.K, B_ROWS);
   if (abytes == 0 || bbytes == 0) return true;
-  uint8_t* ws = workspace(device, abytes + bbytes, st);
+  uint8_t* ws = g_ws_alloc ? static_cast<uint8_t*>(g_ws_alloc(abytes + bbytes, st)) : workspace(device, abytes + bbytes, st);
   if (ws == nullptr) return false;
   auto kern = tc_gemm_packed_kernel<BN, NSUB, A::kMN, B::kMN, E>;
   static unsigned long long configured = 0ull;
@@ -227,6 +237,7 @@ static bool launch_packed(const A& a, const B& b, const E& e, const GemmShape& s
   cfg.numAttrs = 1;
   count_launch();
   cudaLaunchKernelEx(&cfg, kern, pa, pb, e, sh, status);
+  if (g_ws_alloc) g_ws_free(ws);  // stream-ordered: reused only by work queued after these kernels
   return true;
 }
 

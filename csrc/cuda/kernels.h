@@ -12,6 +12,10 @@ namespace su {
 
 // ---- device bookkeeping -----------------------------------------------------
 int* device_status_ptr(int device);  // per-device status word (bounded waits, bad indices)
+// Stream-ordered allocator for GEMM operand images (nullptr: internal workspaces).
+using WorkspaceAlloc = void* (*)(size_t bytes, cudaStream_t stream);
+using WorkspaceFree = void (*)(void* ptr);
+void set_workspace_allocator(WorkspaceAlloc alloc, WorkspaceFree free_fn);
 // Host-side count of kernel launches issued by this library (all devices).
 void count_launch();
 long long launch_count();

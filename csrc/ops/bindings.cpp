@@ -2,9 +2,20 @@
 #include <torch/extension.h>
 
 int64_t status_read(bool clear);
+#include <c10/cuda/CUDACachingAllocator.h>
+#include <cuda_runtime.h>
 namespace su {
 long long launch_count();
+using WorkspaceAlloc = void* (*)(size_t bytes, cudaStream_t stream);
+using WorkspaceFree = void (*)(void* ptr);
+void set_workspace_allocator(WorkspaceAlloc alloc, WorkspaceFree free_fn);
 }
+// GEMM operand images come from the caching allocator: stream-ordered reuse, and
+// the CUDA graph's private pool during capture
+static void* su_ws_alloc(size_t bytes, cudaStream_t st) {
+  return c10::cuda::CUDACachingAllocator::raw_alloc_with_stream(bytes, st);
+}
+static void su_ws_free(void* p) { c10::cuda::CUDACachingAllocator::raw_delete(p); }
 at::Tensor linear_fwd(const at::Tensor& x, const at::Tensor& w, const c10::optional<at::Tensor>& bias, int64_t act);
 at::Tensor linear_dgrad(const at::Tensor& dy, const at::Tensor& w);
 void linear_wgrad(const at::Tensor& dy, const at::Tensor& x, at::Tensor& dw, const c10::optional<at::Tensor>& db);
@@ -128,6 +139,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "starry_unigraph sm_100a kernels (tcgen05 GEMMs, TGN step, DTDG ops, collectives)";
   m.def("status_read", &status_read, "read (and clear) the device status word", py::arg("clear") = true);
   m.def("launch_count", &su::launch_count, "kernel launches issued by this library so far (host-side count)");
+  su::set_workspace_allocator(&su_ws_alloc, &su_ws_free);
   m.def("linear_fwd", &linear_fwd);
   m.def("linear_dgrad", &linear_dgrad);
   m.def("linear_wgrad", &linear_wgrad);

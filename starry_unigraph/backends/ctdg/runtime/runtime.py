@@ -303,6 +303,33 @@ class CTDGOnlineRuntime:
                 "meta": {"split": split, "batch_size": batch.size, "metrics": metrics,
                          "memory": self.memory.describe()}}
 
+    def run_batches_device(self, batches: list[CTDGDataBatch], split: str = "train", train: bool = True,
+                           on_step: Any = None) -> list[dict[str, Any]]:
+        """Stream given batches through the CUDA engine: per step the inputs are copied
+        host -> device (asynchronously from pinned memory) and the step's loss and
+        metrics device -> host into a pinned buffer, without a host synchronisation
+        between steps; one synchronisation at the end returns every step's result."""
+        eng = self.engine
+        n = len(batches)
+        res = torch.empty(n, 4, dtype=torch.float32, pin_memory=True)
+        if train:
+            self.model.train()
+        split = "test" if split == "predict" else split
+        for i, b in enumerate(batches):
+            if on_step is not None:
+                on_step(i)
+            eng.load_batch(b.src, b.dst, b.ts, b.event_ids)
+            eng.step(split, train)
+            res[i, 0:1].copy_(eng.loss, non_blocking=True)   # stream-ordered before the next step overwrites it
+            res[i, 1:4].copy_(eng.metrics, non_blocking=True)
+        torch.cuda.current_stream(self.device).synchronize()
+        out = []
+        for i, b in enumerate(batches):
+            loss, ap, auc, mrr = res[i].tolist()
+            out.append({"loss": loss, "meta": {"split": split, "batch_size": b.size,
+                                               "metrics": {"ap": ap, "auc": auc, "mrr": mrr} if b.size else {}}})
+        return out
+
     def run_split_device(self, split: str, batch_size: int, train: bool, max_steps: int | None = None,
                          collect_predictions: bool = False, on_step: Any = None) -> dict[str, Any]:
         """Epoch over a split without per-step host synchronisation (CUDA engine only):

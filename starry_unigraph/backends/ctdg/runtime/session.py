@@ -42,6 +42,15 @@ class CTDGSession:
     def iter_predict(self, ctx: SessionContext, split: str = "test"):
         yield from self.online_runtime.iter_batches(split, self._bs(ctx))
 
+    def train_batches(self, batches: list[Any]) -> list[dict[str, Any]]:
+        """Train on a list of batches (pinned host tensors): asynchronous per-step
+        host -> device inputs and device -> host loss/metrics, one synchronisation at
+        the end (CUDA engine); the per-step path elsewhere."""
+        rt = self.online_runtime
+        if rt.engine is not None:
+            return rt.run_batches_device(list(batches), "train", True)
+        return [self.train_step(b) for b in batches]
+
     def train_step(self, batch: Any) -> dict[str, Any]:
         return self.online_runtime.train_step(batch)
 

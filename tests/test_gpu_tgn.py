@@ -194,3 +194,18 @@ def test_jodie_fused_step_matches_cpu_oracle(tmp_path):
         a, b = pg.grad.detach().cpu(), pc.grad.detach()
         rel = float((a - b).norm() / (b.norm() + 1e-8))
         assert rel < 5e-2, (n, rel)
+
+
+def test_train_batches_matches_per_step_api(tmp_path):
+    """The pipelined public API (async per-step H2D/D2H, one final sync) returns the
+    same losses as stepping one batch at a time."""
+    # lr = 0: gradient atomics (split-K flushes, concurrent weight-gradient streams) sum in a run-dependent
+    # order, and Adam would turn those last-bit differences into diverging parameters
+    a = _session("cuda", tmp_path / "a", runtime={"cuda_graphs": True}, train={"lr": 0.0})
+    b = _session("cuda", tmp_path / "b", runtime={"cuda_graphs": True}, train={"lr": 0.0})
+    batches = list(a.ctdg_session.online_runtime.iter_batches("train", 100))[:10]
+    for x in batches:
+        x.src, x.dst, x.ts, x.event_ids = (t.pin_memory() for t in (x.src, x.dst, x.ts, x.event_ids))
+    la = [a.ctdg_session.train_step(x)["loss"] for x in batches]
+    lb = [r["loss"] for r in b.ctdg_session.train_batches(batches)]
+    torch.testing.assert_close(torch.tensor(lb), torch.tensor(la), rtol=1e-4, atol=1e-5)
