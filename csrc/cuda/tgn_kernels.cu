@@ -256,6 +256,41 @@ __device__ __forceinline__ float shfl_head(const float (&v)[4], int H, int h, in
   return h == 0 ? v0 : h == 1 ? v1 : h == 2 ? v2 : v3;
 }
 
+// Per-head dot products of this warp's root row (columns spread over lanes,
+// coalesced loads) with row `row` of a [*, ld] matrix at column offset `off`;
+// the result is reduced over the warp, so every lane gets all H sums.
+constexpr int kAttnMaxCols = 8;  // Do <= 256
+__device__ __forceinline__ void head_dots(const float (&xv)[kAttnMaxCols], const float* __restrict__ row, int Do,
+                                          int dh, int H, float (&out)[4]) {
+  const int lane = threadIdx.x & 31;
+  float p0 = 0.f, p1 = 0.f, p2 = 0.f, p3 = 0.f;
+#pragma unroll
+  for (int c = 0; c < kAttnMaxCols; ++c) {
+    const int d = lane + 32 * c;
+    if (d < Do) {
+      const float t = xv[c] * row[d];
+      const int h = d / dh;
+      if (h == 0) p0 += t;
+      else if (h == 1) p1 += t;
+      else if (h == 2) p2 += t;
+      else p3 += t;
+    }
+  }
+  out[0] = warp_sum(p0);
+  out[1] = H > 1 ? warp_sum(p1) : 0.f;
+  out[2] = H > 2 ? warp_sum(p2) : 0.f;
+  out[3] = H > 3 ? warp_sum(p3) : 0.f;
+}
+
+__device__ __forceinline__ void load_row_cols(const float* __restrict__ row, int Do, float (&xv)[kAttnMaxCols]) {
+  const int lane = threadIdx.x & 31;
+#pragma unroll
+  for (int c = 0; c < kAttnMaxCols; ++c) {
+    const int d = lane + 32 * c;
+    xv[c] = d < Do ? row[d] : 0.f;
+  }
+}
+
 __global__ void tgn_attn_fwd_kernel(const float* __restrict__ Q, const float* __restrict__ KV,
                                     const int* __restrict__ cnt, const int* __restrict__ n_roots, int rmax, int k,
                                     int Do, int H, float att_drop, uint64_t seed, const int64_t* __restrict__ step_ctr,
@@ -273,15 +308,27 @@ __global__ void tgn_attn_fwd_kernel(const float* __restrict__ Q, const float* __
   const uint64_t dseed = seed ^ (static_cast<uint64_t>(*step_ctr) * 0x9E3779B97F4A7C15ull);
   const float* q = Q + (int64_t)r * Do;
   const int64_t e = (int64_t)r * k + lane;
-  // scores (lane j = edge j), up to 4 heads
+  // raw scores q . K_j per head: edges one at a time with columns over lanes (coalesced),
+  // then lane j keeps edge j's sums
+  float qv[kAttnMaxCols];
+  load_row_cols(q, Do, qv);
+  float raw[4] = {0.f, 0.f, 0.f, 0.f};
+  for (int j = 0; j < nv; ++j) {
+    float hd[4];
+    head_dots(qv, KV + ((int64_t)r * k + j) * (2 * Do), Do, dh, H, hd);
+    if (lane == j) {
+      raw[0] = hd[0];
+      raw[1] = hd[1];
+      raw[2] = hd[2];
+      raw[3] = hd[3];
+    }
+  }
   float att[4] = {0.f, 0.f, 0.f, 0.f};
   const bool on = lane < nv;
   for (int h = 0; h < H && h < 4; ++h) {
     float s = -INFINITY;
     if (on) {
-      const float* kr = KV + e * (2 * Do) + h * dh;
-      float acc = 0.f;
-      for (int d = 0; d < dh; ++d) acc = fmaf(q[h * dh + d], kr[d], acc);
+      const float acc = raw[h];
       s = acc > 0.f ? acc : 0.2f * acc;  // LeakyReLU(0.2)
     }
     const float m = warp_max(s);
@@ -334,6 +381,24 @@ __global__ void tgn_attn_bwd_kernel(const float* __restrict__ Q, const float* __
   const float* g = dagg + (int64_t)r * Do;
   const int64_t e = (int64_t)r * k + lane;
   const bool on = lane < nv;
+  // per edge, columns over lanes: g . V_j (attention-weight gradient) and q . K_j (raw score)
+  float qv[kAttnMaxCols], gv[kAttnMaxCols];
+  load_row_cols(q, Do, qv);
+  load_row_cols(g, Do, gv);
+  float draw[4] = {0.f, 0.f, 0.f, 0.f}, sraw[4] = {0.f, 0.f, 0.f, 0.f};
+  for (int j = 0; j < nv; ++j) {
+    const float* kr = KV + ((int64_t)r * k + j) * (2 * Do);
+    float hv[4], hk[4];
+    head_dots(gv, kr + Do, Do, dh, H, hv);
+    head_dots(qv, kr, Do, dh, H, hk);
+    if (lane == j) {
+#pragma unroll
+      for (int h = 0; h < 4; ++h) {
+        draw[h] = hv[h];
+        sraw[h] = hk[h];
+      }
+    }
+  }
   float att[4] = {0.f, 0.f, 0.f, 0.f};
   float dsc[4] = {0.f, 0.f, 0.f, 0.f};
   for (int h = 0; h < H && h < 4; ++h) {
@@ -343,15 +408,8 @@ __global__ void tgn_attn_bwd_kernel(const float* __restrict__ Q, const float* __
       keep = 1.f;
       if (att_drop > 0.f)
         keep = dropout_keep(dseed, (uint64_t)(e * H + h), kStreamAttDrop, att_drop) ? 1.f / (1.f - att_drop) : 0.f;
-      const float* vr = KV + e * (2 * Do) + Do + h * dh;
-      const float* kr = KV + e * (2 * Do) + h * dh;
-      float acc = 0.f, sacc = 0.f;
-      for (int d = 0; d < dh; ++d) {
-        acc = fmaf(g[h * dh + d], vr[d], acc);
-        sacc = fmaf(q[h * dh + d], kr[d], sacc);
-      }
-      datt = acc;
-      s = sacc;
+      datt = draw[h];
+      s = sraw[h];
     }
     att[h] = p * keep;
     const float dp = datt * keep;               // through dropout

@@ -369,6 +369,7 @@ void tgn_attn_fwd(const at::Tensor& Q, const at::Tensor& KV, const at::Tensor& n
   const int k = static_cast<int>(KV.size(0) / rmax);
   TORCH_CHECK(k <= 32, "fused attention supports fanout <= 32");
   TORCH_CHECK(H <= 4 && Do % H == 0, "heads must divide the output dim (<= 4 heads)");
+  TORCH_CHECK(Do <= 256, "fused attention supports output dims up to 256");
   const int threads = 256;
   launch_tgn_attn_fwd(dim3((rmax * 32 + threads - 1) / threads), dim3(threads), cur_stream(), 
       Q.data_ptr<float>(), KV.data_ptr<float>(), nbr_cnt.data_ptr<int>(), n_roots.data_ptr<int>(), rmax, k, Do,
@@ -383,6 +384,7 @@ void tgn_attn_bwd(const at::Tensor& Q, const at::Tensor& KV, const at::Tensor& a
   const int rmax = static_cast<int>(Q.size(0));
   const int Do = static_cast<int>(Q.size(1));
   const int k = static_cast<int>(KV.size(0) / rmax);
+  TORCH_CHECK(k <= 32 && H <= 4 && Do % H == 0 && Do <= 256, "fused attention: fanout <= 32, <= 4 heads, dim <= 256");
   const int threads = 256;
   launch_tgn_attn_bwd(dim3((rmax * 32 + threads - 1) / threads), dim3(threads), cur_stream(), 
       Q.data_ptr<float>(), KV.data_ptr<float>(), att_p.data_ptr<float>(), dagg.data_ptr<float>(),
