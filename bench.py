@@ -47,6 +47,8 @@ def _args():
                    help="tgn: TGN train events/sec (default, config 3); jodie: JODIE train events/sec (config 4); "
                         "mpnn_lstm: MPNN-LSTM train snapshots/sec (config 2)")
     p.add_argument("--snapshots", type=int, default=128, help="mpnn_lstm: snapshots generated (config: 128)")
+    p.add_argument("--trace", action="store_true",
+                   help="tgn/jodie: after the timed region, print a per-op device-time table of one eager step")
     return p.parse_args()
 
 
@@ -324,6 +326,15 @@ def main():
     e2e_s = time.perf_counter() - t0
     barrier()
 
+    if args.trace and hasattr(eng, "trace_step"):
+        b = e2e_batches[-1] if e2e_batches else timed[-1]
+        eng.load_batch(b.src, b.dst, b.ts, b.event_ids)
+        rows = eng.trace_step("train", True)
+        if rank == 0:
+            print(f"# per-op device time, one eager step (rank 0): {sum(t for _, t in rows):.3f} ms summed",
+                  file=sys.stderr)
+            for name, t in rows:
+                print(f"#   {t * 1000:8.1f} us  {name}", file=sys.stderr)
     stats = torch.tensor([dev_ms, e2e_s, float(events), float(e2e_events)], dtype=torch.float64, device="cuda")
     if world > 1:
         mx = stats[:2].clone()

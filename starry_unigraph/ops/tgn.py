@@ -24,6 +24,32 @@ from starry_unigraph.ops import cuda_ext
 from starry_unigraph.ops.flat import FlatParams, FusedAdam
 
 
+class _TracingOps:
+    """Proxy of the extension module for one traced step: every op call gets an NVTX
+    range and a pair of CUDA events on the stream it runs on."""
+
+    def __init__(self, C: Any) -> None:
+        self._C = C
+        self.records: list[tuple[str, torch.cuda.Event, torch.cuda.Event]] = []
+
+    def __getattr__(self, name: str):
+        fn = getattr(self._C, name)
+        if not callable(fn) or name in ("launch_count", "status_read"):
+            return fn
+
+        def traced(*args, **kwargs):
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            torch.cuda.nvtx.range_push(name)
+            a.record()
+            out = fn(*args, **kwargs)
+            b.record()
+            torch.cuda.nvtx.range_pop()
+            self.records.append((name, a, b))
+            return out
+
+        return traced
+
+
 @dataclass
 class TGNShapes:
     bmax: int
@@ -408,6 +434,19 @@ class TGNCudaEngine:
 
     def _restore_state(self, state) -> None:
         return None
+
+    def trace_step(self, split: str, train: bool) -> list[tuple[str, float]]:
+        """Run one eager step (no graph replay) with every op bracketed by CUDA events
+        and NVTX ranges; returns (op, device ms) in issue order. Ops on the side stream
+        overlap the main-stream ones, so the list is a per-op profile, not a sum."""
+        tracer = _TracingOps(self.C)
+        real, self.C = self.C, tracer
+        try:
+            self._forward(split, train)
+        finally:
+            self.C = real
+        torch.cuda.synchronize(self.device)
+        return [(n, a.elapsed_time(b)) for n, a, b in tracer.records]
 
     def launches_per_step(self, train: bool = True) -> int:
         """Framework kernel launches in one step (torch memsets excluded): the count
