@@ -24,10 +24,15 @@ def _launch(out, family, extra_env=None, *args, wall=240):
     env = dict(os.environ)
     env.pop("CUDA_VISIBLE_DEVICES", None)
     env.update(extra_env or {})
-    cmd = ["timeout", "-k", "10", str(wall), sys.executable, "-m", "torch.distributed.run", "--nnodes=1",
-           "--nproc-per-node=2", "--master-addr", "127.0.0.1", "--master-port", str(_port()), str(WORKER),
-           "--family", family, "--out", str(out), *args]
-    return subprocess.run(cmd, cwd=ROOT, env=env, capture_output=True, text=True, timeout=wall + 30)
+    for attempt in range(3):  # a port picked free can be taken before the rendezvous binds it
+        cmd = ["timeout", "-k", "10", str(wall), sys.executable, "-m", "torch.distributed.run", "--nnodes=1",
+               "--nproc-per-node=2", "--master-addr", "127.0.0.1", "--master-port", str(_port()), str(WORKER),
+               "--family", family, "--out", str(out), *args]
+        res = subprocess.run(cmd, cwd=ROOT, env=env, capture_output=True, text=True, timeout=wall + 30)
+        text = res.stdout + res.stderr
+        if res.returncode == 0 or not any(m in text for m in ("Address already in use", "EADDRINUSE", "errno: 98")):
+            return res
+    return res
 
 
 def _outcome(out, r):
