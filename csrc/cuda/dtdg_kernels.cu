@@ -170,9 +170,9 @@ void launch_spmm_peer_push(cudaStream_t st, const int64_t* rowptr_t, const int* 
 
 // d(pre-activation) of the four gates and dc_prev from dh', dc' and the saved gates.
 __global__ void lstm_bwd_kernel(const float* __restrict__ gates, const float* __restrict__ c_prev,
-                                const float* __restrict__ c_new, const float* __restrict__ dh,
-                                const float* __restrict__ dc, int64_t rows, int H, float* __restrict__ dpre,
-                                float* __restrict__ dc_prev) {
+                                const float* __restrict__ c_new, const float* __restrict__ dh, int dh_ld,
+                                const float* __restrict__ dc, int dc_ld, int64_t rows, int H,
+                                float* __restrict__ dpre, float* __restrict__ dc_prev) {
   const int64_t idx = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
   if (idx >= rows * H) return;
   const int64_t r = idx / H;
@@ -181,8 +181,8 @@ __global__ void lstm_bwd_kernel(const float* __restrict__ gates, const float* __
   const float i = g[c], f = g[H + c], gg = g[2 * H + c], o = g[3 * H + c];
   const float cn = c_new[idx];
   const float tc = tanhf(cn);
-  const float dhv = dh ? dh[idx] : 0.f;
-  const float dct = (dc ? dc[idx] : 0.f) + dhv * o * (1.f - tc * tc);
+  const float dhv = dh ? dh[r * dh_ld + c] : 0.f;
+  const float dct = (dc ? dc[r * dc_ld + c] : 0.f) + dhv * o * (1.f - tc * tc);
   const float cp = c_prev ? c_prev[idx] : 0.f;
   float* d = dpre + r * 4 * H;
   d[c] = dct * gg * i * (1.f - i);
@@ -193,11 +193,12 @@ __global__ void lstm_bwd_kernel(const float* __restrict__ gates, const float* __
 }
 
 void launch_lstm_bwd(cudaStream_t st, const float* gates, const float* c_prev, const float* c_new, const float* dh,
-                     const float* dc, int64_t rows, int H, float* dpre, float* dc_prev) {
+                     int dh_ld, const float* dc, int dc_ld, int64_t rows, int H, float* dpre, float* dc_prev) {
   const int64_t n = rows * H;
   if (n == 0) return;
   count_launch();
-  lstm_bwd_kernel<<<(n + 255) / 256, 256, 0, st>>>(gates, c_prev, c_new, dh, dc, rows, H, dpre, dc_prev);
+  lstm_bwd_kernel<<<(n + 255) / 256, 256, 0, st>>>(gates, c_prev, c_new, dh, dh_ld, dc, dc_ld, rows, H, dpre,
+                                                   dc_prev);
 }
 
 }  // namespace su

@@ -127,7 +127,7 @@ void launch_spmm_peer_push(cudaStream_t st, const int64_t* rowptr_t, const int* 
                            const float* grad_dst, int64_t n_src, int F, float* const* peers, const int* src_owner,
                            const int* src_row);
 void launch_lstm_bwd(cudaStream_t st, const float* gates, const float* c_prev, const float* c_new, const float* dh,
-                     const float* dc, int64_t rows, int H, float* dpre, float* dc_prev);
+                     int dh_ld, const float* dc, int dc_ld, int64_t rows, int H, float* dpre, float* dc_prev);
 
 // ---- peer (NVLink) kernels -----------------------------------------------------
 void launch_peer_barrier(cudaStream_t st, uint64_t* const* flag_ptrs, int rank, int W, int64_t* epoch, int* status,

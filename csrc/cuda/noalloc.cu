@@ -158,7 +158,7 @@ extern "C" SU_EXPORT int su_lstm_cell_backward_noalloc(
   float* tmp = scratch + round_up64(static_cast<size_t>(rows) * DP4);
 
   // 1. gate pre-activation gradients (scratch) and d c_prev
-  launch_lstm_bwd(st, gates, c_prev, c_new, dh, dc, rows, H, dpre, dc_prev);
+  launch_lstm_bwd(st, gates, c_prev, c_new, dh, H, dc, H, rows, H, dpre, dc_prev);
 
   // 2. d[x || h] = dpre [W_i; W_f; W_g; W_o]
   {

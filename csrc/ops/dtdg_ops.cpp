@@ -99,15 +99,16 @@ std::vector<at::Tensor> lstm_bwd(const at::Tensor& x, const c10::optional<at::Te
   auto dc_prev = at::empty({rows, H}, x.options());
   auto dxh = at::empty({rows, in_dim + H}, x.options());
   if (rows == 0) return {dxh.narrow(1, 0, in_dim), dxh.narrow(1, in_dim, H), dc_prev};
-  const float* dh = (dh_opt.has_value() && dh_opt->defined()) ? dh_opt->contiguous().data_ptr<float>() : nullptr;
+  // row-strided upstream gradients are read in place (a column view of the next cell's [dx || dh])
   at::Tensor dh_c, dc_c;
-  if (dh_opt.has_value() && dh_opt->defined()) dh_c = dh_opt->contiguous();
-  if (dc_opt.has_value() && dc_opt->defined()) dc_c = dc_opt->contiguous();
+  if (dh_opt.has_value() && dh_opt->defined()) dh_c = dh_opt->stride(1) == 1 ? *dh_opt : dh_opt->contiguous();
+  if (dc_opt.has_value() && dc_opt->defined()) dc_c = dc_opt->stride(1) == 1 ? *dc_opt : dc_opt->contiguous();
   launch_lstm_bwd(cur_stream(), gates.data_ptr<float>(), has_c ? c->data_ptr<float>() : nullptr,
                   c_new.data_ptr<float>(), dh_c.defined() ? dh_c.data_ptr<float>() : nullptr,
-                  dc_c.defined() ? dc_c.data_ptr<float>() : nullptr, rows, H, dpre.data_ptr<float>(),
+                  dh_c.defined() ? static_cast<int>(dh_c.stride(0)) : H,
+                  dc_c.defined() ? dc_c.data_ptr<float>() : nullptr,
+                  dc_c.defined() ? static_cast<int>(dc_c.stride(0)) : H, rows, H, dpre.data_ptr<float>(),
                   dc_prev.data_ptr<float>());
-  (void)dh;
   const int DP4 = 4 * H;
   // d[x || h] = dpre [W_i; W_f; W_g; W_o]
   {

@@ -439,6 +439,7 @@ class TGNCudaEngine:
         """Run one eager step (no graph replay) with every op bracketed by CUDA events
         and NVTX ranges; returns (op, device ms) in issue order. Ops on the side stream
         overlap the main-stream ones, so the list is a per-op profile, not a sum."""
+        self._forward(split, train)  # untraced eager step first: caching-allocator and stream warm-up
         tracer = _TracingOps(self.C)
         real, self.C = self.C, tracer
         try:
