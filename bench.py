@@ -43,10 +43,13 @@ def _args():
     p.add_argument("--events", type=int, default=None,
                    help="stream length (tgn config: 7,833,140; jodie config: 200,000,000)")
     p.add_argument("--batch", type=int, default=None, help="events per rank per step (tgn: 600, jodie: 4000)")
-    p.add_argument("--workload", default="tgn", choices=["tgn", "jodie", "mpnn_lstm"],
+    p.add_argument("--workload", default="tgn", choices=["tgn", "jodie", "mpnn_lstm", "tgcn", "evolvegcn"],
                    help="tgn: TGN train events/sec (default, config 3); jodie: JODIE train events/sec (config 4); "
-                        "mpnn_lstm: MPNN-LSTM train snapshots/sec (config 2)")
-    p.add_argument("--snapshots", type=int, default=128, help="mpnn_lstm: snapshots generated (config: 128)")
+                        "mpnn_lstm: MPNN-LSTM train snapshots/sec (config 2); tgcn / evolvegcn: config 5")
+    p.add_argument("--snapshots", type=int, default=None, help="DTDG: snapshots generated (mpnn_lstm: 128, tgcn/evolvegcn: 32)")
+    p.add_argument("--nodes", type=int, default=None, help="DTDG: nodes (mpnn_lstm: 200,000; tgcn/evolvegcn: 2,000,000)")
+    p.add_argument("--edges", type=int, default=None,
+                   help="DTDG: edges per snapshot (mpnn_lstm: 2,000,000; tgcn/evolvegcn: 20,000,000)")
     p.add_argument("--trace", action="store_true",
                    help="tgn/jodie: after the timed region, print a per-op device-time table of one eager step")
     return p.parse_args()
@@ -131,6 +134,17 @@ def _reference_arm(args):
     return 0
 
 
+DTDG_WORKLOADS = {
+    # name: (family, task, hidden, window, preset, snapshots, nodes, edges, metric, config description)
+    "mpnn_lstm": ("mpnn_lstm", "snapshot_node_regression", 64, 8, "mpnn_lstm_large", 128, 200_000, 2_000_000,
+                  "MPNN-LSTM train snapshots/sec", "MPNN-LSTM (2 MPNN + 2 LSTM, hidden 64), flare_native, MSE"),
+    "tgcn": ("tgcn", "node_classification", 128, 4, "egcn_large", 32, 2_000_000, 20_000_000,
+             "T-GCN train snapshots/sec", "T-GCN (2 GCN layers, hidden 128, GRU-style gates), binary labels"),
+    "evolvegcn": ("evolvegcn", "node_classification", 128, 4, "egcn_large", 32, 2_000_000, 20_000_000,
+                  "EvolveGCN-O train snapshots/sec", "EvolveGCN-O (GCN weights evolved by a matrix GRU), binary labels"),
+}
+
+
 def _mpnn_main(args):
     """MPNN-LSTM: 200,000 nodes, 128 Chung-Lu snapshots of ~2M edges with 30% churn,
     64-dim features, window 8, two MPNN layers + two LSTMs of hidden 64, MSE. Nodes are partitioned over the
@@ -148,13 +162,19 @@ def _mpnn_main(args):
     from starry_unigraph.backends.dtdg.runtime.training import run_flare_train_step
     from starry_unigraph.ops import check_status
 
+    fam, task, hidden, window, preset, d_snaps, d_nodes, d_edges, metric_name, model_desc = DTDG_WORKLOADS[args.workload]
+    snaps = args.snapshots or d_snaps
+    nodes = args.nodes or d_nodes
+    edges = args.edges or d_edges
+    full = (snaps, nodes, edges) == (d_snaps, d_nodes, d_edges)
+
     def cfg(resident):
         return {
-            "model": {"name": "mpnn_lstm", "family": "mpnn_lstm", "task": "snapshot_node_regression",
-                      "hidden_dim": 64, "window": {"size": 8}},
-            "data": {"root": "./data", "name": "mpnn_large", "format": "synthetic",
-                     "synthetic": {"preset": "mpnn_lstm_large", "num_snapshots": args.snapshots}},
-            "train": {"epochs": 1, "snaps": args.snapshots, "lr": 1e-3},
+            "model": {"name": fam, "family": fam, "task": task, "hidden_dim": hidden, "window": {"size": window}},
+            "data": {"root": "./data", "name": f"{fam}_large", "format": "synthetic",
+                     "synthetic": {"preset": preset, "num_snapshots": snaps, "num_nodes": nodes,
+                                   "edges_per_snapshot": edges}},
+            "train": {"epochs": 1, "snaps": snaps, "lr": 1e-3},
             "runtime": {"device": "cuda"},
             "dtdg": {"window_from_size": True, "chunk_order": None, "chunk_decay": None, "resident": resident},
             "dist": {"backend": "nccl", "timeout_s": 1800},
@@ -163,7 +183,7 @@ def _mpnn_main(args):
     session = SchedulerSession.from_config(cfg(True))
     # one artifact set for all ranks (written by rank 0): every partition file holds its
     # snapshots' features, so per-rank copies would multiply the disk footprint by N
-    session.ctx.artifact_root = Path(os.environ.get("TMPDIR", "/tmp")) / f"su_mpnn_w{world}"
+    session.ctx.artifact_root = Path(os.environ.get("TMPDIR", "/tmp")) / f"su_{fam}_w{world}"
     if world > 1:
         from starry_unigraph.distributed import initialize_distributed
 
@@ -212,15 +232,14 @@ def _mpnn_main(args):
     value = args.steps / (dev_ms / 1000.0)
     if rank == 0:
         print(json.dumps({
-            "metric": "MPNN-LSTM train snapshots/sec", "value": value, "unit": "snapshots/s", "n_gpus": world,
+            "metric": metric_name, "value": value, "unit": "snapshots/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": dev_ms / args.steps,
             "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "fp32+bf16-tensor-core",
             "data": "synthetic (random-init weights)",
-            "config": {"model": "MPNN-LSTM (2 MPNN + 2 LSTM, hidden 64), flare_native", "global_batch": None,
-                       "seq_len": 8, "parallelism": f"graph-partition{world}", "nodes": 200000,
-                       "snapshots": args.snapshots, "edges_per_snapshot": 2000000, "window": 8,
-                       "l2": "per-snapshot working set (2M edges CSR ~24 MB + 200k x 64 fp32 features 51 MB) x 8 "
-                             "window graphs > 126 MB L2", "baseline_metric": METRIC},
+            "config": {"model": model_desc, "global_batch": None, "seq_len": window,
+                       "parallelism": f"graph-partition{world}", "nodes": nodes, "snapshots": snaps,
+                       "edges_per_snapshot": edges, "window": window, "full_config_shape": full,
+                       "l2": "window graphs' CSR + features exceed the 126 MB L2", "baseline_metric": METRIC},
             "clocks": clocks.summary(), "prep_s": prep_s}), flush=True)
     if world > 1:
         from starry_unigraph.distributed import finalize_distributed
@@ -233,7 +252,7 @@ def main():
     args = _args()
     if args.impl == "reference":
         return _reference_arm(args)
-    if args.workload == "mpnn_lstm":
+    if args.workload in DTDG_WORKLOADS:
         return _mpnn_main(args)
     jodie = args.workload == "jodie"
     sys.path.insert(0, str(ROOT))
