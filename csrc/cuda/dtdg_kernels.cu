@@ -58,11 +58,37 @@ struct PeerPush {
   }
 };
 
+template <int VEC>
+__device__ __forceinline__ void load_vec(const float* p, float (&t)[VEC]) {
+  if constexpr (VEC == 4) {
+    const float4 a = *reinterpret_cast<const float4*>(p);
+    t[0] = a.x; t[1] = a.y; t[2] = a.z; t[3] = a.w;
+  } else if constexpr (VEC == 2) {
+    const float2 a = *reinterpret_cast<const float2*>(p);
+    t[0] = a.x; t[1] = a.y;
+  } else {
+#pragma unroll
+    for (int v = 0; v < VEC; ++v) t[v] = p[v];
+  }
+}
+
 template <int VEC, class Rows, class Out>
-__global__ void spmm_chunked_kernel(const int64_t* __restrict__ rowptr, const int* __restrict__ col,
-                                    const float* __restrict__ val, const Rows rows, int64_t n_rows, int F,
-                                    const Out out) {
+__global__ void __launch_bounds__(256, 2) spmm_chunked_kernel(const int64_t* __restrict__ rowptr,
+                                                           const int* __restrict__ col,
+                                                           const float* __restrict__ val, const Rows rows,
+                                                           int64_t n_rows, int F, const Out out) {
+  // The warp walks its chunk as one flat stream of edges, kUnroll at a time
+  // (their source rows are gathered together, whatever rows the edges belong to),
+  // and closes a row segment whenever the stream crosses a row end. Columns and
+  // weights of the chunk are staged in shared memory once; the row ends come
+  // 32 at a time from one coalesced load of rowptr.
+  constexpr int kUnroll = VEC == 4 ? 8 : 16;
+  __shared__ int s_col[8][kSpmmChunk];
+  __shared__ float s_val[8][kSpmmChunk];
   const int lane = threadIdx.x & 31;
+  const int wib = threadIdx.x >> 5;
+  int* scol = s_col[wib];
+  float* sval = s_val[wib];
   const int64_t nnz = rowptr[n_rows];
   const int64_t nchunks = (nnz + kSpmmChunk - 1) / kSpmmChunk;
   const int64_t warps = (static_cast<int64_t>(gridDim.x) * blockDim.x) >> 5;
@@ -70,6 +96,12 @@ __global__ void spmm_chunked_kernel(const int64_t* __restrict__ rowptr, const in
        ch += warps) {
     const int64_t cb = ch * kSpmmChunk;
     const int64_t ce = (cb + kSpmmChunk < nnz) ? cb + kSpmmChunk : nnz;
+    const int n = static_cast<int>(ce - cb);
+    __syncwarp();
+    for (int k = lane; k < n; k += 32) {
+      scol[k] = col[cb + k];
+      sval[k] = val[cb + k];
+    }
     // row holding edge cb: last r with rowptr[r] <= cb
     int64_t lo = 0, hi = n_rows;
     while (hi - lo > 1) {
@@ -77,52 +109,58 @@ __global__ void spmm_chunked_kernel(const int64_t* __restrict__ rowptr, const in
       if (rowptr[mid] <= cb) lo = mid;
       else hi = mid;
     }
-    int64_t row = lo;
-    int64_t e = cb;
-    while (e < ce) {
-      const int64_t rs = rowptr[row], re = rowptr[row + 1];
-      const int64_t se = re < ce ? re : ce;
-      const bool whole = rs >= cb && re <= ce;
-      // every lane takes part in every shuffle; lanes beyond F only skip their loads
-      for (int fbase = 0; fbase < F; fbase += 32 * VEC) {
-        const int f0 = fbase + lane * VEC;
-        const bool active = f0 < F;
-        float acc[VEC];
+    __syncwarp();
+    for (int fbase = 0; fbase < F; fbase += 32 * VEC) {
+      const int f0 = fbase + lane * VEC;
+      const bool active = f0 < F;  // every lane takes part in the control flow
+      int64_t row = lo;
+      int64_t rs = rowptr[row];
+      // lane l holds the end of row `wrow + l`
+      int64_t wrow = row;
+      int64_t rend = (wrow + lane < n_rows) ? rowptr[wrow + lane + 1] : INT64_MAX;
+      int64_t re = __shfl_sync(0xffffffffu, rend, 0);
+      float acc[VEC];
 #pragma unroll
-        for (int v = 0; v < VEC; ++v) acc[v] = 0.f;
-        for (int64_t e0 = e; e0 < se; e0 += 32) {
-          const int64_t my = e0 + lane;
-          const int mc = my < se ? col[my] : 0;
-          const float mv = my < se ? val[my] : 0.f;
-          const int cnt = static_cast<int>((se - e0) < 32 ? (se - e0) : 32);
-          for (int j = 0; j < cnt; ++j) {
-            const int c = __shfl_sync(0xffffffffu, mc, j);
-            const float w = __shfl_sync(0xffffffffu, mv, j);
-            if (!active) continue;
-            const float* xr = rows.row(c) + f0;
-            if (VEC == 4) {
-              const float4 t = *reinterpret_cast<const float4*>(xr);
-              acc[0] = fmaf(w, t.x, acc[0]);
-              acc[1] = fmaf(w, t.y, acc[1]);
-              acc[2] = fmaf(w, t.z, acc[2]);
-              acc[3] = fmaf(w, t.w, acc[3]);
-            } else if (VEC == 2) {
-              const float2 t = *reinterpret_cast<const float2*>(xr);
-              acc[0] = fmaf(w, t.x, acc[0]);
-              acc[1] = fmaf(w, t.y, acc[1]);
-            } else {
+      for (int v = 0; v < VEC; ++v) acc[v] = 0.f;
+      bool have = false;
+      for (int e0 = 0; e0 < n; e0 += kUnroll) {
+        float t[kUnroll][VEC];
 #pragma unroll
-              for (int v = 0; v < VEC; ++v) acc[v] = fmaf(w, xr[v], acc[v]);
-            }
-          }
+        for (int u = 0; u < kUnroll; ++u) {
+          if (active && e0 + u < n) load_vec<VEC>(rows.row(scol[e0 + u]) + f0, t[u]);
         }
-        if (active) {
 #pragma unroll
-          for (int v = 0; v < VEC; ++v) out.put(row, f0 + v, acc[v], whole);
+        for (int u = 0; u < kUnroll; ++u) {
+          if (e0 + u >= n) continue;  // (no break: the loop must unroll to keep t[] in registers)
+          const int64_t e = cb + e0 + u;
+          while (e >= re) {  // the stream left row `row` (warp-uniform)
+            if (have && active) {
+              const bool whole = rs >= cb && re <= ce;
+#pragma unroll
+              for (int v = 0; v < VEC; ++v) out.put(row, f0 + v, acc[v], whole);
+            }
+#pragma unroll
+            for (int v = 0; v < VEC; ++v) acc[v] = 0.f;
+            have = false;
+            rs = re;
+            ++row;
+            if (row - wrow == 32) {
+              wrow = row;
+              rend = (wrow + lane < n_rows) ? rowptr[wrow + lane + 1] : INT64_MAX;
+            }
+            re = __shfl_sync(0xffffffffu, rend, static_cast<int>(row - wrow));
+          }
+          const float w = sval[e0 + u];
+#pragma unroll
+          for (int v = 0; v < VEC; ++v) acc[v] = fmaf(w, t[u][v], acc[v]);
+          have = true;
         }
       }
-      e = se;
-      ++row;
+      if (have && active) {
+        const bool whole = rs >= cb && re <= ce;
+#pragma unroll
+        for (int v = 0; v < VEC; ++v) out.put(row, f0 + v, acc[v], whole);
+      }
     }
   }
 }
@@ -192,6 +230,55 @@ __global__ void lstm_bwd_kernel(const float* __restrict__ gates, const float* __
   if (dc_prev) dc_prev[idx] = dct * f;
 }
 
+// Four consecutive units of one row per thread (H, dh_ld, dc_ld multiples of 4,
+// 16-byte aligned rows); the pre-activation gradients go out in bf16, the type in
+// which the following GEMMs consume them (the rounding is the one their operand
+// packing would apply to fp32 values).
+__global__ void lstm_bwd4_kernel(const float* __restrict__ gates, const float* __restrict__ c_prev,
+                                 const float* __restrict__ c_new, const float* __restrict__ dh, int dh_ld,
+                                 const float* __restrict__ dc, int dc_ld, int64_t rows, int H,
+                                 __nv_bfloat16* __restrict__ dpre, float* __restrict__ dc_prev) {
+  const int H4 = H >> 2;
+  const int64_t idx = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (idx >= rows * H4) return;
+  const int64_t r = idx / H4;
+  const int c = static_cast<int>(idx % H4) * 4;
+  const float* g = gates + r * 4 * H + c;
+  const float4 i4 = ldg4(g), f4 = ldg4(g + H), g4 = ldg4(g + 2 * H), o4 = ldg4(g + 3 * H);
+  const float4 cn4 = ldg4(c_new + r * H + c);
+  const float4 cp4 = c_prev ? ldg4(c_prev + r * H + c) : make_float4(0.f, 0.f, 0.f, 0.f);
+  const float4 dh4 = dh ? ldg4(dh + r * dh_ld + c) : make_float4(0.f, 0.f, 0.f, 0.f);
+  const float4 dc4 = dc ? ldg4(dc + r * dc_ld + c) : make_float4(0.f, 0.f, 0.f, 0.f);
+  const float iv[4] = {i4.x, i4.y, i4.z, i4.w}, fv[4] = {f4.x, f4.y, f4.z, f4.w};
+  const float gv[4] = {g4.x, g4.y, g4.z, g4.w}, ov[4] = {o4.x, o4.y, o4.z, o4.w};
+  const float cn[4] = {cn4.x, cn4.y, cn4.z, cn4.w}, cp[4] = {cp4.x, cp4.y, cp4.z, cp4.w};
+  const float dhv[4] = {dh4.x, dh4.y, dh4.z, dh4.w}, dcv[4] = {dc4.x, dc4.y, dc4.z, dc4.w};
+  float di[4], df[4], dg[4], dout[4], dcp[4];
+#pragma unroll
+  for (int u = 0; u < 4; ++u) {
+    const float tc = tanhf(cn[u]);
+    const float dct = dcv[u] + dhv[u] * ov[u] * (1.f - tc * tc);
+    di[u] = dct * gv[u] * iv[u] * (1.f - iv[u]);
+    df[u] = dct * cp[u] * fv[u] * (1.f - fv[u]);
+    dg[u] = dct * iv[u] * (1.f - gv[u] * gv[u]);
+    dout[u] = dhv[u] * tc * ov[u] * (1.f - ov[u]);
+    dcp[u] = dct * fv[u];
+  }
+  auto put = [](__nv_bfloat16* p, const float (&v)[4]) {
+    __nv_bfloat162 a = __floats2bfloat162_rn(v[0], v[1]), b = __floats2bfloat162_rn(v[2], v[3]);
+    uint2 w;
+    w.x = *reinterpret_cast<uint32_t*>(&a);
+    w.y = *reinterpret_cast<uint32_t*>(&b);
+    *reinterpret_cast<uint2*>(p) = w;
+  };
+  __nv_bfloat16* d = dpre + r * 4 * H + c;
+  put(d, di);
+  put(d + H, df);
+  put(d + 2 * H, dg);
+  put(d + 3 * H, dout);
+  if (dc_prev) *reinterpret_cast<float4*>(dc_prev + r * H + c) = make_float4(dcp[0], dcp[1], dcp[2], dcp[3]);
+}
+
 void launch_lstm_bwd(cudaStream_t st, const float* gates, const float* c_prev, const float* c_new, const float* dh,
                      int dh_ld, const float* dc, int dc_ld, int64_t rows, int H, float* dpre, float* dc_prev) {
   const int64_t n = rows * H;
@@ -199,6 +286,23 @@ void launch_lstm_bwd(cudaStream_t st, const float* gates, const float* c_prev, c
   count_launch();
   lstm_bwd_kernel<<<(n + 255) / 256, 256, 0, st>>>(gates, c_prev, c_new, dh, dh_ld, dc, dc_ld, rows, H, dpre,
                                                    dc_prev);
+}
+
+bool lstm_bwd_bf16_ok(const float* gates, const float* c_prev, const float* c_new, const float* dh, int dh_ld,
+                      const float* dc, int dc_ld, int H, const void* dpre, const float* dc_prev) {
+  auto al = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; };
+  return H % 4 == 0 && dh_ld % 4 == 0 && dc_ld % 4 == 0 && al(gates) && al(c_prev) && al(c_new) && al(dh) &&
+         al(dc) && al(dc_prev) && (reinterpret_cast<uintptr_t>(dpre) & 7) == 0;
+}
+
+void launch_lstm_bwd_bf16(cudaStream_t st, const float* gates, const float* c_prev, const float* c_new,
+                          const float* dh, int dh_ld, const float* dc, int dc_ld, int64_t rows, int H,
+                          __nv_bfloat16* dpre, float* dc_prev) {
+  const int64_t n = rows * (H / 4);
+  if (n == 0) return;
+  count_launch();
+  lstm_bwd4_kernel<<<(n + 255) / 256, 256, 0, st>>>(gates, c_prev, c_new, dh, dh_ld, dc, dc_ld, rows, H, dpre,
+                                                    dc_prev);
 }
 
 }  // namespace su

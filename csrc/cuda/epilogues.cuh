@@ -37,6 +37,9 @@ struct EpiGRU {
   int scatter_ld = 0;
   float* scatter_ts = nullptr;   // memory_ts[scatter_index[row]] = *ts_value
   const float* ts_value = nullptr;
+  // 1: D, hprev_ld, hout_ld and scatter_ld are multiples of 4 and every pointer
+  // (peer tables included) is 16-byte aligned: 16-byte loads and stores
+  int vec = 0;
 
 #ifdef __CUDACC__
   // every gate group of ngates*DP columns in the range this thread was given
@@ -54,6 +57,32 @@ struct EpiGRU {
     if (valid && scatter != nullptr) srow = scatter_index[row];
     if (ngates == 1) {
       for (int c0 = 0; c0 < DP; c0 += 16) {
+        const int cb = u0 + c0;
+        if (vec && cb + 16 <= D) {
+          uint32_t rp[16];
+          tmem_ld16_issue(taddr + c0, rp);
+          float4 h4[4], b4[4];
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            h4[q] = (hp && save_prev) ? *reinterpret_cast<const float4*>(hp + cb + 4 * q)
+                                      : make_float4(0.f, 0.f, 0.f, 0.f);
+            const float4 a = ldg4(b_ih + cb + 4 * q), b = ldg4(b_hh + cb + 4 * q);
+            b4[q] = make_float4(a.x + b.x, a.y + b.y, a.z + b.z, a.w + b.w);
+          }
+          tmem_wait_ld4(rp, rp, rp, rp);
+          if (!valid) continue;
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            const float4 o4 = make_float4(tanh_fast(__uint_as_float(rp[4 * q]) + b4[q].x),
+                                          tanh_fast(__uint_as_float(rp[4 * q + 1]) + b4[q].y),
+                                          tanh_fast(__uint_as_float(rp[4 * q + 2]) + b4[q].z),
+                                          tanh_fast(__uint_as_float(rp[4 * q + 3]) + b4[q].w));
+            if (save_prev) *reinterpret_cast<float4*>(save_prev + (int64_t)row * D + cb + 4 * q) = h4[q];
+            if (hout) *reinterpret_cast<float4*>(hout + (int64_t)row * hout_ld + cb + 4 * q) = o4;
+            if (srow >= 0) *reinterpret_cast<float4*>(scatter + srow * scatter_ld + cb + 4 * q) = o4;
+          }
+          continue;
+        }
         float pre[16];
         tmem_ld16(taddr + c0, pre);
         if (!valid) continue;
@@ -72,6 +101,57 @@ struct EpiGRU {
       return;
     }
     for (int c0 = 0; c0 < DP; c0 += 16) {
+      const int cb = u0 + c0;
+      if (vec && cb + 16 <= D) {
+        // whole group of 16 units (warp-uniform branch): the previous hidden rows of
+        // all 16 are in flight before the first TMEM load, and every load precedes
+        // every store (a row may be read from and written to the same table); the
+        // gates come in two halves of 8 units
+        float4 h4[4];
+#pragma unroll
+        for (int q = 0; q < 4; ++q)
+          h4[q] = hp ? *reinterpret_cast<const float4*>(hp + cb + 4 * q) : make_float4(0.f, 0.f, 0.f, 0.f);
+        float4 o4[4];
+#pragma unroll
+        for (int hh = 0; hh < 2; ++hh) {
+          uint32_t rr[8], rz[8], rni[8], rnh[8];
+          tmem_ld8_issue(taddr + c0 + 8 * hh, rr);
+          tmem_ld8_issue(taddr + DP + c0 + 8 * hh, rz);
+          tmem_ld8_issue(taddr + 2 * DP + c0 + 8 * hh, rni);
+          tmem_ld8_issue(taddr + 3 * DP + c0 + 8 * hh, rnh);
+          tmem_wait_ld4n<8>(rr, rz, rni, rnh);
+#pragma unroll
+          for (int qq = 0; qq < 2; ++qq) {
+            const int q = 2 * hh + qq;
+            const int cq = cb + 4 * q;
+            const float4 a = ldg4(b_ih + cq), b = ldg4(b_hh + cq);
+            const float4 c = ldg4(b_ih + D + cq), d = ldg4(b_hh + D + cq);
+            const float4 e = ldg4(b_ih + 2 * D + cq), f = ldg4(b_hh + 2 * D + cq);
+            const float br[4] = {a.x + b.x, a.y + b.y, a.z + b.z, a.w + b.w};
+            const float bz[4] = {c.x + d.x, c.y + d.y, c.z + d.z, c.w + d.w};
+            const float bni[4] = {e.x, e.y, e.z, e.w}, bnh[4] = {f.x, f.y, f.z, f.w};
+            const float hv[4] = {h4[q].x, h4[q].y, h4[q].z, h4[q].w};
+            float hn[4];
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+              const int i = 4 * qq + u;
+              const float rg = sigmoid_fast(__uint_as_float(rr[i]) + br[u]);
+              const float zg = sigmoid_fast(__uint_as_float(rz[i]) + bz[u]);
+              const float ng = tanh_fast(__uint_as_float(rni[i]) + bni[u] + rg * (__uint_as_float(rnh[i]) + bnh[u]));
+              hn[u] = (1.f - zg) * ng + zg * hv[u];
+            }
+            o4[q] = make_float4(hn[0], hn[1], hn[2], hn[3]);
+          }
+        }
+        if (!valid) continue;
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          if (save_prev) *reinterpret_cast<float4*>(save_prev + (int64_t)row * D + cb + 4 * q) = h4[q];
+          if (hout) *reinterpret_cast<float4*>(hout + (int64_t)row * hout_ld + cb + 4 * q) = o4[q];
+          if (srow >= 0) *reinterpret_cast<float4*>(scatter + srow * scatter_ld + cb + 4 * q) = o4[q];
+        }
+        continue;
+      }
       float r[16], z[16], ni[16], nh[16];
       tmem_ld16(taddr + c0, r);
       tmem_ld16(taddr + DP + c0, z);
@@ -210,55 +290,76 @@ struct EpiLSTM {
   float* h_out = nullptr;         // [rows, H]
   float* c_out = nullptr;         // [rows, H]
   float* gates = nullptr;         // [rows, 4H] (i, f, g, o) post-activation, optional
+  int vec = 0;  // 1: H % 4 == 0 and every pointer 16-byte aligned (16-byte loads and stores)
 
 #ifdef __CUDACC__
   // every gate group of 4*DP columns in the range this thread was given
   __device__ __forceinline__ void operator()(int row, bool valid, int n0, uint32_t taddr, int tile_cols) const {
+#pragma unroll 1
     for (int g0 = 0; g0 < tile_cols; g0 += 4 * DP) group(row, valid, n0 + g0, taddr + g0);
   }
   __device__ __forceinline__ void group(int row, bool valid, int n0, uint32_t taddr) const {
     const int u0 = (n0 / (4 * DP)) * DP;
+#pragma unroll 1
     for (int c0 = 0; c0 < DP; c0 += 16) {
+      const int cb = u0 + c0;
+      if (vec && cb + 16 <= H) {
+        // whole group of 16 units (warp-uniform branch): the previous cell state of
+        // all 16 is in flight before the first TMEM load; the gates come in two
+        // halves of 8 units (fewer live registers than one pass of 16)
+        const int64_t rb = (int64_t)row * H + cb;
+        float4 cp4[4];
+#pragma unroll
+        for (int q = 0; q < 4; ++q)
+          cp4[q] = (valid && c_prev) ? ldg4(c_prev + rb + 4 * q) : make_float4(0.f, 0.f, 0.f, 0.f);
+        float* gr = gates ? gates + (int64_t)row * 4 * H + cb : nullptr;
+#pragma unroll
+        for (int hh = 0; hh < 2; ++hh) {
+          uint32_t ri[8], rf[8], rg[8], ro[8];
+          tmem_ld8_issue(taddr + c0 + 8 * hh, ri);
+          tmem_ld8_issue(taddr + DP + c0 + 8 * hh, rf);
+          tmem_ld8_issue(taddr + 2 * DP + c0 + 8 * hh, rg);
+          tmem_ld8_issue(taddr + 3 * DP + c0 + 8 * hh, ro);
+          tmem_wait_ld4n<8>(ri, rf, rg, ro);
+          if (!valid) continue;
+#pragma unroll
+          for (int qq = 0; qq < 2; ++qq) {
+            const int q = 2 * hh + qq;  // 4-unit block inside the group
+            // biases: warp-uniform addresses, L1-resident after the first tile
+            const float4 bi4 = ldg4(b_i + cb + 4 * q), bf4 = ldg4(b_f + cb + 4 * q);
+            const float4 bg4 = ldg4(b_g + cb + 4 * q), bo4 = ldg4(b_o + cb + 4 * q);
+            const float cpv[4] = {cp4[q].x, cp4[q].y, cp4[q].z, cp4[q].w};
+            const float bi[4] = {bi4.x, bi4.y, bi4.z, bi4.w}, bf[4] = {bf4.x, bf4.y, bf4.z, bf4.w};
+            const float bg[4] = {bg4.x, bg4.y, bg4.z, bg4.w}, bo[4] = {bo4.x, bo4.y, bo4.z, bo4.w};
+            float iv[4], fv[4], gv[4], ov[4], cn[4], hn[4];
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+              const int j = 4 * qq + u;
+              iv[u] = sigmoid_fast(__uint_as_float(ri[j]) + bi[u]);
+              fv[u] = sigmoid_fast(__uint_as_float(rf[j]) + bf[u]);
+              gv[u] = tanh_fast(__uint_as_float(rg[j]) + bg[u]);
+              ov[u] = sigmoid_fast(__uint_as_float(ro[j]) + bo[u]);
+              cn[u] = fv[u] * cpv[u] + iv[u] * gv[u];
+              hn[u] = ov[u] * tanh_fast(cn[u]);
+            }
+            *reinterpret_cast<float4*>(c_out + rb + 4 * q) = make_float4(cn[0], cn[1], cn[2], cn[3]);
+            *reinterpret_cast<float4*>(h_out + rb + 4 * q) = make_float4(hn[0], hn[1], hn[2], hn[3]);
+            if (gr) {
+              *reinterpret_cast<float4*>(gr + 4 * q) = make_float4(iv[0], iv[1], iv[2], iv[3]);
+              *reinterpret_cast<float4*>(gr + H + 4 * q) = make_float4(fv[0], fv[1], fv[2], fv[3]);
+              *reinterpret_cast<float4*>(gr + 2 * H + 4 * q) = make_float4(gv[0], gv[1], gv[2], gv[3]);
+              *reinterpret_cast<float4*>(gr + 3 * H + 4 * q) = make_float4(ov[0], ov[1], ov[2], ov[3]);
+            }
+          }
+        }
+        continue;
+      }
       float gi[16], gf[16], gg[16], go[16];
       tmem_ld16(taddr + c0, gi);
       tmem_ld16(taddr + DP + c0, gf);
       tmem_ld16(taddr + 2 * DP + c0, gg);
       tmem_ld16(taddr + 3 * DP + c0, go);
       if (!valid) continue;
-      const int cb = u0 + c0;
-      if ((H & 3) == 0 && cb + 16 <= H) {
-        // whole group of 16 units: 16-byte loads and stores (rows are 16-byte aligned when H % 4 == 0)
-        const int64_t rb = (int64_t)row * H + cb;
-        float* gr = gates ? gates + (int64_t)row * 4 * H + cb : nullptr;
-#pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          float cpv[4] = {0.f, 0.f, 0.f, 0.f};
-          if (c_prev) {
-            const float4 t = *reinterpret_cast<const float4*>(c_prev + rb + 4 * q);
-            cpv[0] = t.x; cpv[1] = t.y; cpv[2] = t.z; cpv[3] = t.w;
-          }
-          float iv[4], fv[4], gv[4], ov[4], cn[4], hn[4];
-#pragma unroll
-          for (int u = 0; u < 4; ++u) {
-            const int j = 4 * q + u, c = cb + j;
-            iv[u] = sigmoid_fast(gi[j] + b_i[c]);
-            fv[u] = sigmoid_fast(gf[j] + b_f[c]);
-            gv[u] = tanh_fast(gg[j] + b_g[c]);
-            ov[u] = sigmoid_fast(go[j] + b_o[c]);
-            cn[u] = fv[u] * cpv[u] + iv[u] * gv[u];
-            hn[u] = ov[u] * tanh_fast(cn[u]);
-          }
-          *reinterpret_cast<float4*>(c_out + rb + 4 * q) = make_float4(cn[0], cn[1], cn[2], cn[3]);
-          *reinterpret_cast<float4*>(h_out + rb + 4 * q) = make_float4(hn[0], hn[1], hn[2], hn[3]);
-          if (gr) {
-            *reinterpret_cast<float4*>(gr + 4 * q) = make_float4(iv[0], iv[1], iv[2], iv[3]);
-            *reinterpret_cast<float4*>(gr + H + 4 * q) = make_float4(fv[0], fv[1], fv[2], fv[3]);
-            *reinterpret_cast<float4*>(gr + 2 * H + 4 * q) = make_float4(gv[0], gv[1], gv[2], gv[3]);
-            *reinterpret_cast<float4*>(gr + 3 * H + 4 * q) = make_float4(ov[0], ov[1], ov[2], ov[3]);
-          }
-        }
-        continue;
-      }
 #pragma unroll
       for (int j = 0; j < 16; ++j) {
         const int c = u0 + c0 + j;

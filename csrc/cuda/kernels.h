@@ -128,6 +128,12 @@ void launch_spmm_peer_push(cudaStream_t st, const int64_t* rowptr_t, const int* 
                            const int* src_row);
 void launch_lstm_bwd(cudaStream_t st, const float* gates, const float* c_prev, const float* c_new, const float* dh,
                      int dh_ld, const float* dc, int dc_ld, int64_t rows, int H, float* dpre, float* dc_prev);
+// vectorised form with bf16 pre-activation gradients; requires lstm_bwd_bf16_ok()
+bool lstm_bwd_bf16_ok(const float* gates, const float* c_prev, const float* c_new, const float* dh, int dh_ld,
+                      const float* dc, int dc_ld, int H, const void* dpre, const float* dc_prev);
+void launch_lstm_bwd_bf16(cudaStream_t st, const float* gates, const float* c_prev, const float* c_new,
+                          const float* dh, int dh_ld, const float* dc, int dc_ld, int64_t rows, int H,
+                          __nv_bfloat16* dpre, float* dc_prev);
 
 // ---- peer (NVLink) kernels -----------------------------------------------------
 void launch_peer_barrier(cudaStream_t st, uint64_t* const* flag_ptrs, int rank, int W, int64_t* epoch, int* status,

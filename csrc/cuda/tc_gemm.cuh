@@ -135,8 +135,18 @@ __device__ __forceinline__ void seg_fill8(const ASeg& g, int row, int c, float (
       int64_t r = g.index ? g.index[row] : row;
       if (r < 0) return;
       const __nv_bfloat16* p = static_cast<const __nv_bfloat16*>(g.ptr) + r * g.ld + g.col0;
+      if (g.vec && c + 8 <= g.width) {
+        const uint4 w = *reinterpret_cast<const uint4*>(p + c);
+        const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
 #pragma unroll
-      for (int i = 0; i < 8; ++i) f[i] = (c + i < g.width) ? __bfloat162float(p[c + i]) : 0.f;
+        for (int i = 0; i < 4; ++i) {
+          f[2 * i] = __uint_as_float(ws[i] << 16);
+          f[2 * i + 1] = __uint_as_float(ws[i] & 0xFFFF0000u);
+        }
+      } else {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) f[i] = (c + i < g.width) ? __bfloat162float(p[c + i]) : 0.f;
+      }
       break;
     }
     case kSegTime: {

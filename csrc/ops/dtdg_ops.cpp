@@ -73,6 +73,8 @@ std::vector<at::Tensor> lstm_fwd(const at::Tensor& x, const c10::optional<at::Te
   e.h_out = h_out.data_ptr<float>();
   e.c_out = c_out.data_ptr<float>();
   e.gates = save_gates ? gates.data_ptr<float>() : nullptr;
+  e.vec = (H % 4 == 0 && a16(e.b_i) && a16(e.b_f) && a16(e.b_g) && a16(e.b_o) && a16(e.c_prev) && a16(e.h_out) &&
+           a16(e.c_out) && a16(e.gates)) ? 1 : 0;
   GemmShape sh;
   sh.M = rows;
   sh.N = 4 * G * ((H + G - 1) / G);
@@ -95,7 +97,8 @@ std::vector<at::Tensor> lstm_bwd(const at::Tensor& x, const c10::optional<at::Te
   const int H = static_cast<int>(wi.size(0));
   const bool has_h = h.has_value() && h->defined();
   const bool has_c = c.has_value() && c->defined();
-  auto dpre = at::empty({rows, 4 * H}, x.options());
+  const float* dh_p = nullptr;
+  const float* dc_p = nullptr;
   auto dc_prev = at::empty({rows, H}, x.options());
   auto dxh = at::empty({rows, in_dim + H}, x.options());
   if (rows == 0) return {dxh.narrow(1, 0, in_dim), dxh.narrow(1, in_dim, H), dc_prev};
@@ -103,18 +106,33 @@ std::vector<at::Tensor> lstm_bwd(const at::Tensor& x, const c10::optional<at::Te
   at::Tensor dh_c, dc_c;
   if (dh_opt.has_value() && dh_opt->defined()) dh_c = dh_opt->stride(1) == 1 ? *dh_opt : dh_opt->contiguous();
   if (dc_opt.has_value() && dc_opt->defined()) dc_c = dc_opt->stride(1) == 1 ? *dc_opt : dc_opt->contiguous();
-  launch_lstm_bwd(cur_stream(), gates.data_ptr<float>(), has_c ? c->data_ptr<float>() : nullptr,
-                  c_new.data_ptr<float>(), dh_c.defined() ? dh_c.data_ptr<float>() : nullptr,
-                  dh_c.defined() ? static_cast<int>(dh_c.stride(0)) : H,
-                  dc_c.defined() ? dc_c.data_ptr<float>() : nullptr,
-                  dc_c.defined() ? static_cast<int>(dc_c.stride(0)) : H, rows, H, dpre.data_ptr<float>(),
-                  dc_prev.data_ptr<float>());
+  dh_p = dh_c.defined() ? dh_c.data_ptr<float>() : nullptr;
+  dc_p = dc_c.defined() ? dc_c.data_ptr<float>() : nullptr;
+  const int dh_ld = dh_c.defined() ? static_cast<int>(dh_c.stride(0)) : H;
+  const int dc_ld = dc_c.defined() ? static_cast<int>(dc_c.stride(0)) : H;
+  const float* cp_p = has_c ? c->data_ptr<float>() : nullptr;
   const int DP4 = 4 * H;
+  // pre-activation gradients in bf16 when the vectorised kernel applies (the GEMMs
+  // below read them as bf16 operands either way)
+  at::Tensor dpre = at::empty({rows, DP4}, x.options().dtype(at::kBFloat16));
+  ASeg dpre_seg;
+  if (lstm_bwd_bf16_ok(gates.data_ptr<float>(), cp_p, c_new.data_ptr<float>(), dh_p, dh_ld, dc_p, dc_ld, H,
+                       dpre.data_ptr(), dc_prev.data_ptr<float>())) {
+    launch_lstm_bwd_bf16(cur_stream(), gates.data_ptr<float>(), cp_p, c_new.data_ptr<float>(), dh_p, dh_ld, dc_p,
+                         dc_ld, rows, H, reinterpret_cast<__nv_bfloat16*>(dpre.data_ptr()),
+                         dc_prev.data_ptr<float>());
+    dpre_seg = seg_bf16(dpre, DP4, pad8(DP4));
+  } else {
+    dpre = at::empty({rows, DP4}, x.options());
+    launch_lstm_bwd(cur_stream(), gates.data_ptr<float>(), cp_p, c_new.data_ptr<float>(), dh_p, dh_ld, dc_p, dc_ld,
+                    rows, H, dpre.data_ptr<float>(), dc_prev.data_ptr<float>());
+    dpre_seg = seg_f32(dpre, DP4, pad8(DP4));
+  }
   // d[x || h] = dpre [W_i; W_f; W_g; W_o]
   {
     SegSource a;
     a.nseg = 1;
-    a.seg[0] = seg_f32(dpre, DP4, pad8(DP4));
+    a.seg[0] = dpre_seg;
     WeightLayout L = lstm_layout({wi, wf, wg, wo}, in_dim, H, H);
     L.blk_pad[3] = pad8(DP4) - 3 * H;
     WeightMN b = weight_mn(L, pad8(DP4));
@@ -144,7 +162,7 @@ std::vector<at::Tensor> lstm_bwd(const at::Tensor& x, const c10::optional<at::Te
   {
     SegSource dy;
     dy.nseg = 1;
-    dy.seg[0] = seg_f32(dpre, DP4, pad8(DP4));
+    dy.seg[0] = dpre_seg;
     SegSource xs;
     xs.nseg = 3;
     xs.seg[0] = seg_f32(x, in_dim, pad8(in_dim));

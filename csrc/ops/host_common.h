@@ -38,6 +38,19 @@ inline int wgrad_ksplit(int nchunks, int tiles) {
   return std::max(1, std::min(by_work, by_sms));
 }
 
+// 16-byte alignment of a device pointer (nullptr counts as aligned)
+inline bool a16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
+
+// vector flag of the GRU / tanh-RNN epilogue: row strides multiples of 4 floats and
+// every local pointer 16-byte aligned (peer tables are symmetric-memory
+// allocations, whose bases are page aligned)
+inline int gru_vec(const EpiGRU& e) {
+  const bool ld = (e.D % 4 == 0) && (e.hprev == nullptr || e.hprev_ld % 4 == 0) &&
+                  (e.hout == nullptr || e.hout_ld % 4 == 0) && (e.scatter == nullptr || e.scatter_ld % 4 == 0);
+  return (ld && a16(e.hprev) && a16(e.hout) && a16(e.save_prev) && a16(e.scatter) && a16(e.b_ih) &&
+          a16(e.b_hh) && e.DP % 16 == 0) ? 1 : 0;
+}
+
 // fp32 matrix segment (row-major, gathered through `index` if given)
 inline ASeg seg_f32(const at::Tensor& m, int width, int kpad, const int64_t* index = nullptr, int col0 = 0) {
   ASeg s;
@@ -49,6 +62,17 @@ inline ASeg seg_f32(const at::Tensor& m, int width, int kpad, const int64_t* ind
   s.kpad = kpad;
   s.index = index;
   s.vec = ((s.ld % 4) == 0 && (col0 % 4) == 0 && (reinterpret_cast<uintptr_t>(s.ptr) % 16) == 0) ? 1 : 0;
+  return s;
+}
+// bf16 matrix segment (row-major)
+inline ASeg seg_bf16(const at::Tensor& m, int width, int kpad) {
+  ASeg s;
+  s.kind = kSegBF16;
+  s.ptr = m.data_ptr();
+  s.ld = static_cast<int>(m.stride(0));
+  s.width = width;
+  s.kpad = kpad;
+  s.vec = ((s.ld % 8) == 0 && (reinterpret_cast<uintptr_t>(s.ptr) % 16) == 0) ? 1 : 0;
   return s;
 }
 inline ASeg seg_time(const float* dt, const at::Tensor& w, const at::Tensor& b, int kpad) {

@@ -100,6 +100,7 @@ static void gru_step(const SegSource& a, int kx, int kh, const at::Tensor& w_ih,
   sh.m_dev = m_dev;
   sh.N = 4 * kGateGroup * ((D + kGateGroup - 1) / kGateGroup);
   sh.K = kx + kh;
+  e.vec = gru_vec(e);
   gemm(a, b, e, sh, cur_stream());
 }
 
@@ -233,6 +234,7 @@ void tgn_rnn_memory_update(const at::Tensor& roots, const at::Tensor& n_roots, c
   sh.m_dev = m_dev;
   sh.N = kGateGroup * ((D + kGateGroup - 1) / kGateGroup);
   sh.K = pad8(SW) + pad8(D);
+  e.vec = gru_vec(e);
   gemm(a, b, e, sh, cur_stream());
   SU_LAUNCH_CHECK();
 }

@@ -39,6 +39,38 @@ def test_spmm_fwd_bwd(F):
     assert _rel(xc.grad.cpu(), x.grad) < 1e-5
 
 
+@pytest.mark.parametrize("F", [64, 128, 100])
+def test_spmm_csr_skewed_rows(F):
+    """Rows of every kind the edge-chunk walk meets: hubs spanning several chunks,
+    runs of empty rows longer than the 32-row look-ahead window, single-edge rows;
+    plain and accumulating output, against an fp64 index_add reference."""
+    import starry_unigraph._C as C
+
+    g = torch.Generator().manual_seed(7)
+    n_rows, n_src = 6000, 4000
+    deg = torch.randint(0, 4, (n_rows,), generator=g)
+    deg[100] = 5000           # hub: about twenty 256-edge chunks
+    deg[2000] = 700
+    deg[3000:3100] = 0        # 100 empty rows in a row
+    deg[4000:4300] = 1
+    rowptr = torch.zeros(n_rows + 1, dtype=torch.long)
+    rowptr[1:] = deg.cumsum(0)
+    nnz = int(rowptr[-1])
+    col = torch.randint(0, n_src, (nnz,), generator=g, dtype=torch.int32)
+    val = torch.rand(nnz, generator=g)
+    x = torch.randn(n_src, F, generator=g)
+    row_of = torch.repeat_interleave(torch.arange(n_rows), deg)
+    ref = torch.zeros(n_rows, F, dtype=torch.float64).index_add_(
+        0, row_of, val.double()[:, None] * x.double()[col.long()])
+    dev = lambda t: t.cuda()  # noqa: E731
+    out = C.spmm_csr(dev(rowptr), dev(col), dev(val), dev(x), n_rows, None, False)
+    assert _rel(out.cpu().double(), ref) < 1e-6
+    base = torch.randn(n_rows, F, generator=g)
+    acc = dev(base.clone())
+    C.spmm_csr(dev(rowptr), dev(col), dev(val), dev(x), n_rows, acc, True)
+    assert _rel(acc.cpu().double(), ref + base.double()) < 1e-6
+
+
 @pytest.mark.parametrize("H,IN", [(64, 64), (32, 40), (128, 128)])
 def test_lstm_cell_fused(H, IN):
     from starry_unigraph.runtime.modules.rnn_cells import _LSTMCell
