@@ -4,19 +4,24 @@
 //     pass runs the same kernel over the source-sorted (transposed) CSR. Rows
 //     inside one chunk are written directly; rows longer than a chunk (hubs)
 //     are combined with atomic adds.
-//   * LSTM cell backward (elementwise over the saved gates).
+//   * LSTM cell backward (elementwise over the saved gates, in the forward
+//     epilogue's grouped order: lstm_gate_index).
 #include "kernels.h"
 
 namespace su {
 
 // Work-balanced CSR SpMM. Power-law snapshots have hub rows with ~10^5 edges,
 // so a warp per row leaves one warp walking a hub while the rest of the GPU
-// idles. Instead every warp takes a fixed chunk of kChunk consecutive edges of
-// the CSR: it finds the row holding its first edge (binary search in rowptr),
-// accumulates row segment by row segment, and flushes each segment with a plain
-// store when the whole row lies inside the chunk, or an atomic add when the
-// row is shared with a neighbouring chunk (the output was zeroed first, or
-// holds the value to accumulate onto).
+// idles. Instead the edges are cut into one contiguous range per warp of a
+// persistent grid (equal edge counts): the warp finds the row holding its first
+// edge (a 33-ary search over rowptr, one probe per lane), then walks its range
+// as a flat stream, gathering the source rows of several edges at a time
+// whatever rows they belong to, and closes a row segment whenever the stream
+// crosses a row end. A segment is flushed with a plain store when the whole row
+// lies inside the range, with an atomic add when the row is shared with a
+// neighbouring warp's range (the output was zeroed first, or holds the value to
+// accumulate onto). Columns and weights are staged in shared memory in
+// sub-chunks of kSpmmChunk edges.
 constexpr int kSpmmChunk = 256;
 
 // where a source row lives: one local matrix, or any rank's copy of a symmetric
@@ -74,15 +79,11 @@ __device__ __forceinline__ void load_vec(const float* p, float (&t)[VEC]) {
 
 template <int VEC, class Rows, class Out>
 __global__ void __launch_bounds__(256, 2) spmm_chunked_kernel(const int64_t* __restrict__ rowptr,
-                                                           const int* __restrict__ col,
-                                                           const float* __restrict__ val, const Rows rows,
-                                                           int64_t n_rows, int F, const Out out) {
-  // The warp walks its chunk as one flat stream of edges, kUnroll at a time
-  // (their source rows are gathered together, whatever rows the edges belong to),
-  // and closes a row segment whenever the stream crosses a row end. Columns and
-  // weights of the chunk are staged in shared memory once; the row ends come
-  // 32 at a time from one coalesced load of rowptr.
-  constexpr int kUnroll = VEC == 4 ? 8 : 16;
+                                                              const int* __restrict__ col,
+                                                              const float* __restrict__ val, const Rows rows,
+                                                              int64_t n_rows, int F, const Out out) {
+  constexpr int kUnroll = VEC == 4 ? 8 : 16;  // source rows in flight per lane
+  constexpr int kPer = kSpmmChunk / 32;
   __shared__ int s_col[8][kSpmmChunk];
   __shared__ float s_val[8][kSpmmChunk];
   const int lane = threadIdx.x & 31;
@@ -90,39 +91,58 @@ __global__ void __launch_bounds__(256, 2) spmm_chunked_kernel(const int64_t* __r
   int* scol = s_col[wib];
   float* sval = s_val[wib];
   const int64_t nnz = rowptr[n_rows];
-  const int64_t nchunks = (nnz + kSpmmChunk - 1) / kSpmmChunk;
   const int64_t warps = (static_cast<int64_t>(gridDim.x) * blockDim.x) >> 5;
-  for (int64_t ch = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5; ch < nchunks;
-       ch += warps) {
-    const int64_t cb = ch * kSpmmChunk;
-    const int64_t ce = (cb + kSpmmChunk < nnz) ? cb + kSpmmChunk : nnz;
-    const int n = static_cast<int>(ce - cb);
-    __syncwarp();
-    for (int k = lane; k < n; k += 32) {
-      scol[k] = col[cb + k];
-      sval[k] = val[cb + k];
-    }
-    // row holding edge cb: last r with rowptr[r] <= cb
-    int64_t lo = 0, hi = n_rows;
-    while (hi - lo > 1) {
-      const int64_t mid = (lo + hi) >> 1;
-      if (rowptr[mid] <= cb) lo = mid;
-      else hi = mid;
-    }
-    __syncwarp();
-    for (int fbase = 0; fbase < F; fbase += 32 * VEC) {
-      const int f0 = fbase + lane * VEC;
-      const bool active = f0 < F;  // every lane takes part in the control flow
-      int64_t row = lo;
-      int64_t rs = rowptr[row];
-      // lane l holds the end of row `wrow + l`
-      int64_t wrow = row;
-      int64_t rend = (wrow + lane < n_rows) ? rowptr[wrow + lane + 1] : INT64_MAX;
-      int64_t re = __shfl_sync(0xffffffffu, rend, 0);
-      float acc[VEC];
+  const int64_t gw = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+  // this warp's edges [E0, E1): equal shares, rounded up to whole 32-edge rows of loads
+  const int64_t per = (((nnz + warps - 1) / warps) + 31) & ~int64_t(31);
+  const int64_t E0 = gw * per;
+  if (E0 >= nnz) return;  // warp-uniform
+  const int64_t E1 = (E0 + per < nnz) ? E0 + per : nnz;
+  // row holding edge E0: last r with rowptr[r] <= E0. 33-ary search, one probe per
+  // lane per round: about 4 dependent loads for 10^5..10^6 rows instead of the
+  // 17-20 of a binary search (invariant rowptr[lo] <= E0 < rowptr[hi])
+  int64_t lo = 0, hi = n_rows;
+  while (hi - lo > 1) {
+    const int64_t p = lo + (static_cast<int64_t>(lane + 1) * (hi - lo)) / 33;
+    const bool le = p <= lo ? true : (p >= hi ? false : rowptr[p] <= E0);
+    const unsigned m = __ballot_sync(0xffffffffu, le);
+    const int k = __popc(m);  // probes are nondecreasing in the lane, so `le` holds for lanes [0, k)
+    const int64_t plo = __shfl_sync(0xffffffffu, p, k > 0 ? k - 1 : 0);
+    const int64_t phi = __shfl_sync(0xffffffffu, p, k < 32 ? k : 31);
+    if (k > 0 && plo > lo) lo = plo;
+    if (k < 32 && phi < hi) hi = phi;
+  }
+  for (int fbase = 0; fbase < F; fbase += 32 * VEC) {
+    const int f0 = fbase + lane * VEC;
+    const bool active = f0 < F;  // every lane takes part in the control flow
+    int64_t row = lo;
+    int64_t rs = rowptr[row];
+    // lane l holds the end of row `wrow + l`
+    int64_t wrow = row;
+    int64_t rend = (wrow + lane < n_rows) ? rowptr[wrow + lane + 1] : INT64_MAX;
+    int64_t re = __shfl_sync(0xffffffffu, rend, 0);
+    float acc[VEC];
 #pragma unroll
-      for (int v = 0; v < VEC; ++v) acc[v] = 0.f;
-      bool have = false;
+    for (int v = 0; v < VEC; ++v) acc[v] = 0.f;
+    bool have = false;
+    for (int64_t sb = E0; sb < E1; sb += kSpmmChunk) {
+      const int n = static_cast<int>((E1 - sb) < kSpmmChunk ? (E1 - sb) : kSpmmChunk);
+      // stage the sub-chunk: all loads of a lane in flight together
+      int cv[kPer];
+      float vv[kPer];
+#pragma unroll
+      for (int i = 0; i < kPer; ++i) {
+        const int k = lane + 32 * i;
+        cv[i] = k < n ? col[sb + k] : 0;
+        vv[i] = k < n ? val[sb + k] : 0.f;
+      }
+      __syncwarp();
+#pragma unroll
+      for (int i = 0; i < kPer; ++i) {
+        scol[lane + 32 * i] = cv[i];
+        sval[lane + 32 * i] = vv[i];
+      }
+      __syncwarp();
       for (int e0 = 0; e0 < n; e0 += kUnroll) {
         float t[kUnroll][VEC];
 #pragma unroll
@@ -132,10 +152,10 @@ __global__ void __launch_bounds__(256, 2) spmm_chunked_kernel(const int64_t* __r
 #pragma unroll
         for (int u = 0; u < kUnroll; ++u) {
           if (e0 + u >= n) continue;  // (no break: the loop must unroll to keep t[] in registers)
-          const int64_t e = cb + e0 + u;
+          const int64_t e = sb + e0 + u;
           while (e >= re) {  // the stream left row `row` (warp-uniform)
             if (have && active) {
-              const bool whole = rs >= cb && re <= ce;
+              const bool whole = rs >= E0 && re <= E1;
 #pragma unroll
               for (int v = 0; v < VEC; ++v) out.put(row, f0 + v, acc[v], whole);
             }
@@ -156,11 +176,11 @@ __global__ void __launch_bounds__(256, 2) spmm_chunked_kernel(const int64_t* __r
           have = true;
         }
       }
-      if (have && active) {
-        const bool whole = rs >= cb && re <= ce;
+    }
+    if (have && active) {
+      const bool whole = rs >= E0 && re <= E1;
 #pragma unroll
-        for (int v = 0; v < VEC; ++v) out.put(row, f0 + v, acc[v], whole);
-      }
+      for (int v = 0; v < VEC; ++v) out.put(row, f0 + v, acc[v], whole);
     }
   }
 }
@@ -171,7 +191,7 @@ static void launch_chunked(cudaStream_t st, const int64_t* rowptr, const int* co
   int dev = 0;
   cudaGetDevice(&dev);
   const int threads = 256;
-  const int blocks = num_sms(dev) * 8;  // grid-stride over edge chunks (nnz is on the device)
+  const int blocks = num_sms(dev) * 2;  // persistent: two 256-thread blocks per SM (128 registers a thread)
   count_launch();
   if (F % 128 == 0) spmm_chunked_kernel<4><<<blocks, threads, 0, st>>>(rowptr, col, val, rows, n_rows, F, out);
   else if (F % 64 == 0) spmm_chunked_kernel<2><<<blocks, threads, 0, st>>>(rowptr, col, val, rows, n_rows, F, out);
@@ -215,8 +235,8 @@ __global__ void lstm_bwd_kernel(const float* __restrict__ gates, const float* __
   if (idx >= rows * H) return;
   const int64_t r = idx / H;
   const int c = static_cast<int>(idx % H);
-  const float* g = gates + r * 4 * H;
-  const float i = g[c], f = g[H + c], gg = g[2 * H + c], o = g[3 * H + c];
+  const float* g = gates + lstm_gate_index(r, H, 0, c);  // i, f, g, o 16 floats apart
+  const float i = g[0], f = g[16], gg = g[32], o = g[48];
   const float cn = c_new[idx];
   const float tc = tanhf(cn);
   const float dhv = dh ? dh[r * dh_ld + c] : 0.f;
@@ -243,8 +263,8 @@ __global__ void lstm_bwd4_kernel(const float* __restrict__ gates, const float* _
   if (idx >= rows * H4) return;
   const int64_t r = idx / H4;
   const int c = static_cast<int>(idx % H4) * 4;
-  const float* g = gates + r * 4 * H + c;
-  const float4 i4 = ldg4(g), f4 = ldg4(g + H), g4 = ldg4(g + 2 * H), o4 = ldg4(g + 3 * H);
+  const float* g = gates + lstm_gate_index(r, H, 0, c);
+  const float4 i4 = ldg4(g), f4 = ldg4(g + 16), g4 = ldg4(g + 32), o4 = ldg4(g + 48);
   const float4 cn4 = ldg4(c_new + r * H + c);
   const float4 cp4 = c_prev ? ldg4(c_prev + r * H + c) : make_float4(0.f, 0.f, 0.f, 0.f);
   const float4 dh4 = dh ? ldg4(dh + r * dh_ld + c) : make_float4(0.f, 0.f, 0.f, 0.f);

@@ -277,11 +277,24 @@ namespace su {
 // LSTM cell epilogue (reference runtime/modules/rnn_cells.py:92-116): the accumulator
 // holds four blocks of DP columns [x W_i^T + h ... | f | g | o] (one nn.Linear per gate
 // over [x || h]). i, f, o = sigmoid, g = tanh, c' = f c + i g, h' = o tanh(c').
-// Saves the post-activation gates for the backward pass.
+// Saves the post-activation gates for the backward pass in the tile's own order:
+// per row, per group of 16 units, [i(16) f(16) g(16) o(16)]
+//   gates[row * 64 * ceil(H/16) + (u / 16) * 64 + gate * 16 + u % 16],
+// so a row's group is 256 contiguous bytes.
+constexpr int kLstmGroup = 16;
+__host__ __device__ inline int64_t lstm_gate_index(int64_t row, int H, int gate, int u) {
+  const int groups = (H + kLstmGroup - 1) / kLstmGroup;
+  return row * 64 * groups + (u / kLstmGroup) * 64 + gate * kLstmGroup + u % kLstmGroup;
+}
+
 struct EpiLSTM {
   static constexpr bool kSplitCols = true;  // gate groups of 16 units (see EpiGRU)
-  static constexpr int kScratchBytes = 0;
-  int H = 0, DP = 0;  // DP = gate group width G: tile columns are [i | f | g | o] x G units
+  // staging rows for the coalesced stores of the packed kernel: per warp 32 rows x
+  // [i f g o c' h'] x 16 units, row stride padded to 100 floats (conflict-free
+  // 16-byte accesses); per 4-warp column half
+  static constexpr int kStageStride = 100;
+  static constexpr int kScratchBytes = 4 * 32 * kStageStride * 4;
+  int H = 0, DP = 0;  // DP = gate group width (16): tile columns are [i | f | g | o] x 16 units
   const float* b_i = nullptr;
   const float* b_f = nullptr;
   const float* b_g = nullptr;
@@ -289,17 +302,78 @@ struct EpiLSTM {
   const float* c_prev = nullptr;  // [rows, H] (nullptr -> zeros)
   float* h_out = nullptr;         // [rows, H]
   float* c_out = nullptr;         // [rows, H]
-  float* gates = nullptr;         // [rows, 4H] (i, f, g, o) post-activation, optional
+  float* gates = nullptr;         // grouped layout above, optional
   int vec = 0;  // 1: H % 4 == 0 and every pointer 16-byte aligned (16-byte loads and stores)
+  static constexpr bool kPrefetch = true;
 
 #ifdef __CUDACC__
-  // every gate group of 4*DP columns in the range this thread was given
+  // c_prev of the next tile's rows toward L2 (one 64-byte segment per group)
+  __device__ __forceinline__ void prefetch(int row, bool valid, int n0, int tile_cols) const {
+    if (!valid || c_prev == nullptr) return;
+    for (int g0 = 0; g0 < tile_cols; g0 += 4 * DP) {
+      const int u0 = ((n0 + g0) / (4 * DP)) * DP;
+      if (u0 < H) asm volatile("prefetch.global.L2 [%0];" ::"l"(c_prev + (int64_t)row * H + u0));
+    }
+  }
+  // fused-producer kernel: every gate group of 4*DP columns in the range, direct stores
   __device__ __forceinline__ void operator()(int row, bool valid, int n0, uint32_t taddr, int tile_cols) const {
 #pragma unroll 1
-    for (int g0 = 0; g0 < tile_cols; g0 += 4 * DP) group(row, valid, n0 + g0, taddr + g0);
+    for (int g0 = 0; g0 < tile_cols; g0 += 4 * DP) group(row, valid, n0 + g0, taddr + g0, nullptr);
   }
-  __device__ __forceinline__ void group(int row, bool valid, int n0, uint32_t taddr) const {
+  // packed kernel: whole groups are staged in this warp's rows of `scratch`
+  // and written out row-contiguously (4 full cache lines per gate store
+  // instruction instead of 32 partial ones)
+  __device__ __forceinline__ void run(int row, bool valid, int n0, uint32_t taddr, int tile_cols, float* scratch,
+                                      int /*barrier*/) const {
+    float* ws = scratch + ((threadIdx.x >> 5) & 3) * 32 * kStageStride;
+#pragma unroll 1
+    for (int g0 = 0; g0 < tile_cols; g0 += 4 * DP) group(row, valid, n0 + g0, taddr + g0, ws);
+  }
+
+  // 16 units: activations and state update for units [cb, cb + 16) of `row`
+  // (c_prev already loaded), handed to `put(q, i4, f4, g4, o4, c4, h4)` per 4-unit block
+  template <class Put>
+  __device__ __forceinline__ void compute16(uint32_t taddr, int c0, int cb, bool valid, const float4 (&cp4)[4],
+                                            Put&& put) const {
+#pragma unroll
+    for (int hh = 0; hh < 2; ++hh) {
+      uint32_t ri[8], rf[8], rg[8], ro[8];
+      tmem_ld8_issue(taddr + c0 + 8 * hh, ri);
+      tmem_ld8_issue(taddr + DP + c0 + 8 * hh, rf);
+      tmem_ld8_issue(taddr + 2 * DP + c0 + 8 * hh, rg);
+      tmem_ld8_issue(taddr + 3 * DP + c0 + 8 * hh, ro);
+      tmem_wait_ld4n<8>(ri, rf, rg, ro);
+      if (!valid) continue;
+#pragma unroll
+      for (int qq = 0; qq < 2; ++qq) {
+        const int q = 2 * hh + qq;  // 4-unit block inside the group
+        // biases: warp-uniform addresses, L1-resident after the first tile
+        const float4 bi4 = ldg4(b_i + cb + 4 * q), bf4 = ldg4(b_f + cb + 4 * q);
+        const float4 bg4 = ldg4(b_g + cb + 4 * q), bo4 = ldg4(b_o + cb + 4 * q);
+        const float cpv[4] = {cp4[q].x, cp4[q].y, cp4[q].z, cp4[q].w};
+        const float bi[4] = {bi4.x, bi4.y, bi4.z, bi4.w}, bf[4] = {bf4.x, bf4.y, bf4.z, bf4.w};
+        const float bg[4] = {bg4.x, bg4.y, bg4.z, bg4.w}, bo[4] = {bo4.x, bo4.y, bo4.z, bo4.w};
+        float iv[4], fv[4], gv[4], ov[4], cn[4], hn[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          const int j = 4 * qq + u;
+          iv[u] = sigmoid_fast(__uint_as_float(ri[j]) + bi[u]);
+          fv[u] = sigmoid_fast(__uint_as_float(rf[j]) + bf[u]);
+          gv[u] = tanh_fast(__uint_as_float(rg[j]) + bg[u]);
+          ov[u] = sigmoid_fast(__uint_as_float(ro[j]) + bo[u]);
+          cn[u] = fv[u] * cpv[u] + iv[u] * gv[u];
+          hn[u] = ov[u] * tanh_fast(cn[u]);
+        }
+        put(q, make_float4(iv[0], iv[1], iv[2], iv[3]), make_float4(fv[0], fv[1], fv[2], fv[3]),
+            make_float4(gv[0], gv[1], gv[2], gv[3]), make_float4(ov[0], ov[1], ov[2], ov[3]),
+            make_float4(cn[0], cn[1], cn[2], cn[3]), make_float4(hn[0], hn[1], hn[2], hn[3]));
+      }
+    }
+  }
+
+  __device__ __forceinline__ void group(int row, bool valid, int n0, uint32_t taddr, float* ws) const {
     const int u0 = (n0 / (4 * DP)) * DP;
+    const int lane = threadIdx.x & 31;
 #pragma unroll 1
     for (int c0 = 0; c0 < DP; c0 += 16) {
       const int cb = u0 + c0;
@@ -312,46 +386,58 @@ struct EpiLSTM {
 #pragma unroll
         for (int q = 0; q < 4; ++q)
           cp4[q] = (valid && c_prev) ? ldg4(c_prev + rb + 4 * q) : make_float4(0.f, 0.f, 0.f, 0.f);
-        float* gr = gates ? gates + (int64_t)row * 4 * H + cb : nullptr;
-#pragma unroll
-        for (int hh = 0; hh < 2; ++hh) {
-          uint32_t ri[8], rf[8], rg[8], ro[8];
-          tmem_ld8_issue(taddr + c0 + 8 * hh, ri);
-          tmem_ld8_issue(taddr + DP + c0 + 8 * hh, rf);
-          tmem_ld8_issue(taddr + 2 * DP + c0 + 8 * hh, rg);
-          tmem_ld8_issue(taddr + 3 * DP + c0 + 8 * hh, ro);
-          tmem_wait_ld4n<8>(ri, rf, rg, ro);
-          if (!valid) continue;
-#pragma unroll
-          for (int qq = 0; qq < 2; ++qq) {
-            const int q = 2 * hh + qq;  // 4-unit block inside the group
-            // biases: warp-uniform addresses, L1-resident after the first tile
-            const float4 bi4 = ldg4(b_i + cb + 4 * q), bf4 = ldg4(b_f + cb + 4 * q);
-            const float4 bg4 = ldg4(b_g + cb + 4 * q), bo4 = ldg4(b_o + cb + 4 * q);
-            const float cpv[4] = {cp4[q].x, cp4[q].y, cp4[q].z, cp4[q].w};
-            const float bi[4] = {bi4.x, bi4.y, bi4.z, bi4.w}, bf[4] = {bf4.x, bf4.y, bf4.z, bf4.w};
-            const float bg[4] = {bg4.x, bg4.y, bg4.z, bg4.w}, bo[4] = {bo4.x, bo4.y, bo4.z, bo4.w};
-            float iv[4], fv[4], gv[4], ov[4], cn[4], hn[4];
-#pragma unroll
-            for (int u = 0; u < 4; ++u) {
-              const int j = 4 * qq + u;
-              iv[u] = sigmoid_fast(__uint_as_float(ri[j]) + bi[u]);
-              fv[u] = sigmoid_fast(__uint_as_float(rf[j]) + bf[u]);
-              gv[u] = tanh_fast(__uint_as_float(rg[j]) + bg[u]);
-              ov[u] = sigmoid_fast(__uint_as_float(ro[j]) + bo[u]);
-              cn[u] = fv[u] * cpv[u] + iv[u] * gv[u];
-              hn[u] = ov[u] * tanh_fast(cn[u]);
-            }
-            *reinterpret_cast<float4*>(c_out + rb + 4 * q) = make_float4(cn[0], cn[1], cn[2], cn[3]);
-            *reinterpret_cast<float4*>(h_out + rb + 4 * q) = make_float4(hn[0], hn[1], hn[2], hn[3]);
-            if (gr) {
-              *reinterpret_cast<float4*>(gr + 4 * q) = make_float4(iv[0], iv[1], iv[2], iv[3]);
-              *reinterpret_cast<float4*>(gr + H + 4 * q) = make_float4(fv[0], fv[1], fv[2], fv[3]);
-              *reinterpret_cast<float4*>(gr + 2 * H + 4 * q) = make_float4(gv[0], gv[1], gv[2], gv[3]);
-              *reinterpret_cast<float4*>(gr + 3 * H + 4 * q) = make_float4(ov[0], ov[1], ov[2], ov[3]);
-            }
+        if (ws == nullptr) {
+          float* gr = gates ? gates + lstm_gate_index(row, H, 0, cb) : nullptr;
+          compute16(taddr, c0, cb, valid, cp4,
+                    [&](int q, float4 i4, float4 f4, float4 g4, float4 o4, float4 c4, float4 h4) {
+                      *reinterpret_cast<float4*>(c_out + rb + 4 * q) = c4;
+                      *reinterpret_cast<float4*>(h_out + rb + 4 * q) = h4;
+                      if (gr) {
+                        *reinterpret_cast<float4*>(gr + 4 * q) = i4;
+                        *reinterpret_cast<float4*>(gr + 16 + 4 * q) = f4;
+                        *reinterpret_cast<float4*>(gr + 32 + 4 * q) = g4;
+                        *reinterpret_cast<float4*>(gr + 48 + 4 * q) = o4;
+                      }
+                    });
+          continue;
+        }
+        float* mine = ws + lane * kStageStride;
+        compute16(taddr, c0, cb, valid, cp4,
+                  [&](int q, float4 i4, float4 f4, float4 g4, float4 o4, float4 c4, float4 h4) {
+                    *reinterpret_cast<float4*>(mine + 4 * q) = i4;
+                    *reinterpret_cast<float4*>(mine + 16 + 4 * q) = f4;
+                    *reinterpret_cast<float4*>(mine + 32 + 4 * q) = g4;
+                    *reinterpret_cast<float4*>(mine + 48 + 4 * q) = o4;
+                    *reinterpret_cast<float4*>(mine + 64 + 4 * q) = c4;
+                    *reinterpret_cast<float4*>(mine + 80 + 4 * q) = h4;
+                  });
+        __syncwarp();
+        // rows row0 .. row0 + nvalid - 1 of this warp are inside the matrix
+        const int64_t row0 = row - lane;
+        const int nvalid = __popc(__ballot_sync(0xffffffffu, valid));
+        if (gates) {
+          // 32 rows x 16 float4: two rows (2 x 256 contiguous bytes) per instruction
+          float* gbase = gates + lstm_gate_index(row0, H, 0, cb);
+          const int64_t gstride = 64 * ((H + kLstmGroup - 1) / kLstmGroup);
+#pragma unroll 4
+          for (int k = 0; k < 16; ++k) {
+            const int idx = k * 32 + lane, r = idx >> 4, j = idx & 15;
+            if (r < nvalid)
+              *reinterpret_cast<float4*>(gbase + r * gstride + 4 * j) =
+                  *reinterpret_cast<const float4*>(ws + r * kStageStride + 4 * j);
           }
         }
+        // c' and h': 32 rows x 4 float4 each, eight rows (64 bytes each) per instruction
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          const int idx = k * 32 + lane, r = idx >> 2, j = idx & 3;
+          if (r < nvalid) {
+            const int64_t o = (row0 + r) * H + cb + 4 * j;
+            *reinterpret_cast<float4*>(c_out + o) = *reinterpret_cast<const float4*>(ws + r * kStageStride + 64 + 4 * j);
+            *reinterpret_cast<float4*>(h_out + o) = *reinterpret_cast<const float4*>(ws + r * kStageStride + 80 + 4 * j);
+          }
+        }
+        __syncwarp();
         continue;
       }
       float gi[16], gf[16], gg[16], go[16];
@@ -373,11 +459,10 @@ struct EpiLSTM {
         c_out[(int64_t)row * H + c] = cn;
         h_out[(int64_t)row * H + c] = o * tanh_fast(cn);
         if (gates) {
-          float* gr = gates + (int64_t)row * 4 * H;
-          gr[c] = i;
-          gr[H + c] = f;
-          gr[2 * H + c] = g;
-          gr[3 * H + c] = o;
+          gates[lstm_gate_index(row, H, 0, c)] = i;
+          gates[lstm_gate_index(row, H, 1, c)] = f;
+          gates[lstm_gate_index(row, H, 2, c)] = g;
+          gates[lstm_gate_index(row, H, 3, c)] = o;
         }
       }
     }

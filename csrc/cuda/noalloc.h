@@ -45,7 +45,8 @@ extern "C" {
 //   h_prev   [rows, hidden] or NULL    previous hidden state (NULL: zeros)
 //   c_prev   [rows, hidden] or NULL    previous cell state (NULL: zeros)
 //   c_new    [rows, hidden]            forward cell output
-//   gates    [rows, 4*hidden]          post-activation gates (i, f, g, o) saved by the forward
+//   gates    [rows, 64*ceil(hidden/16)] post-activation gates (i, f, g, o) as saved by the
+//                                      forward: per row, per group of 16 units, i f g o x 16
 //   dh, dc   [rows, hidden] or NULL    upstream gradients of h' and c'
 //   w_*      [hidden, in_dim + hidden] gate weights, row-major ([W_x | W_h])
 //   gw_*     [hidden, in_dim + hidden] weight gradients (accumulated)

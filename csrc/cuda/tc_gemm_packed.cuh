@@ -19,6 +19,8 @@
 // (bounded) for its copies in flight, frees TMEM and returns.
 #pragma once
 
+#include <type_traits>
+
 #include "tc_gemm.cuh"
 
 namespace su {
@@ -59,6 +61,14 @@ __device__ __forceinline__ void call_epilogue(const Epi& e, int row, bool valid,
     e(row, valid, n0, taddr, cols);
   }
 }
+
+// Epilogues that read per-row inputs from global memory (the LSTM's c_prev) may
+// declare kPrefetch and a prefetch(row, valid, n0, cols) that pulls the rows of
+// the CTA's NEXT tile toward L2 while the current tile is waited on and processed.
+template <class Epi, class = void>
+struct has_prefetch : std::false_type {};
+template <class Epi>
+struct has_prefetch<Epi, std::void_t<decltype(Epi::kPrefetch)>> : std::integral_constant<bool, Epi::kPrefetch> {};
 #endif
 
 // bytes of a packed operand with `mn` rows (MN extent) and K extent `k`
@@ -229,6 +239,16 @@ __global__ void __launch_bounds__(kPackedThreads, 1)
       const int ks = tile % ksplit;
       if (ks * cps >= nchunks) continue;  // empty split: nothing was accumulated
       const int slot = tl % NACC;
+      constexpr int kCols = Epi::kSplitCols ? B_ROWS / 2 : B_ROWS;
+      const int c0 = Epi::kSplitCols ? half * kCols : 0;
+      if constexpr (has_prefetch<Epi>::value) {
+        const int nx = tile + gridDim.x;
+        if (nx < total) {
+          const int mnx = nx / ksplit;
+          const int rowx = (mnx / tiles_n) * kBM + q * 32 + lane;
+          epi.prefetch(rowx, rowx < M, (mnx % tiles_n) * B_ROWS + c0, kCols);
+        }
+      }
       if (!mbar_wait_bounded(&acc_full[slot], (tl / NACC) & 1) || *abort_flag) {
         record_status(status, kTimeoutAccum);
         *abort_flag = 1;
@@ -236,8 +256,6 @@ __global__ void __launch_bounds__(kPackedThreads, 1)
       }
       tc_fence_after();
       const int row = mt * kBM + q * 32 + lane;
-      constexpr int kCols = Epi::kSplitCols ? B_ROWS / 2 : B_ROWS;
-      const int c0 = Epi::kSplitCols ? half * kCols : 0;
       const uint32_t taddr = tmem_base + (static_cast<uint32_t>(q * 32) << 16) +
                              static_cast<uint32_t>(slot * B_ROWS + c0);
       call_epilogue(epi, row, row < M, nt * B_ROWS + c0, taddr, kCols, epi_scratch, half);

@@ -35,7 +35,8 @@ static WeightLayout lstm_layout(const std::vector<at::Tensor>& ws, int in_dim, i
   return L;
 }
 
-// (h', c', gates) = LSTMCell(x, (h, c)); gates [rows, 4H] post-activation (i, f, g, o)
+// (h', c', gates) = LSTMCell(x, (h, c)); gates: post-activation (i, f, g, o) in groups of
+// 16 units per row (lstm_gate_index)
 std::vector<at::Tensor> lstm_fwd(const at::Tensor& x, const c10::optional<at::Tensor>& h,
                                  const c10::optional<at::Tensor>& c, const at::Tensor& wi, const at::Tensor& bi,
                                  const at::Tensor& wf, const at::Tensor& bf, const at::Tensor& wg,
@@ -47,7 +48,8 @@ std::vector<at::Tensor> lstm_fwd(const at::Tensor& x, const c10::optional<at::Te
   constexpr int G = 16;  // gate group: each 64-column half of an N tile holds [i | f | g | o] for 16 units
   auto h_out = at::empty({rows, H}, x.options());
   auto c_out = at::empty({rows, H}, x.options());
-  at::Tensor gates = save_gates ? at::empty({rows, 4 * H}, x.options()) : at::Tensor();
+  // gates in the epilogue's grouped order (see lstm_gate_index): [rows, 64 * ceil(H / 16)]
+  at::Tensor gates = save_gates ? at::empty({rows, 64 * ((H + G - 1) / G)}, x.options()) : at::Tensor();
   if (rows == 0) return {h_out, c_out, gates};
   const bool has_h = h.has_value() && h->defined();
   SegSource a;

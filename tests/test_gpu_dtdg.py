@@ -71,7 +71,7 @@ def test_spmm_csr_skewed_rows(F):
     assert _rel(acc.cpu().double(), ref + base.double()) < 1e-6
 
 
-@pytest.mark.parametrize("H,IN", [(64, 64), (32, 40), (128, 128)])
+@pytest.mark.parametrize("H,IN", [(64, 64), (32, 40), (128, 128), (20, 12)])
 def test_lstm_cell_fused(H, IN):
     from starry_unigraph.runtime.modules.rnn_cells import _LSTMCell
 
