@@ -6,6 +6,8 @@
 //     are combined with atomic adds.
 //   * LSTM cell backward (elementwise over the saved gates, in the forward
 //     epilogue's grouped order: lstm_gate_index).
+#include <algorithm>
+
 #include "kernels.h"
 
 namespace su {
@@ -38,6 +40,17 @@ struct PeerRows {
   int F;
   __device__ __forceinline__ const float* row(int c) const {
     return peers[owner[c]] + static_cast<int64_t>(lrow[c]) * F;
+  }
+};
+// this rank's rows (columns below n_split, the layer input) and the halo rows
+// pulled from the owners (columns from n_split on, in pull order)
+struct TwoTables {
+  const float* x;
+  const float* halo;
+  int n_split;
+  int F;
+  __device__ __forceinline__ const float* row(int c) const {
+    return c < n_split ? x + static_cast<int64_t>(c) * F : halo + static_cast<int64_t>(c - n_split) * F;
   }
 };
 // where a finished row segment goes: this rank's output (plain store for rows
@@ -214,6 +227,43 @@ void launch_spmm_peer_gather(cudaStream_t st, const int64_t* rowptr, const int* 
   if (n_rows == 0) return;
   cudaMemsetAsync(out, 0, static_cast<size_t>(n_rows) * F * sizeof(float), st);
   launch_chunked(st, rowptr, col, val, PeerRows{peers, src_owner, src_row, F}, n_rows, F, LocalOut{out, F, 0});
+}
+
+// Halo rows pulled over NVLink once each: out[i] = row lrow[c] of owner[c]'s
+// staging buffer for c = halo_src[i]. Sixteen-byte vectors, F / 4 lanes per row.
+__global__ void halo_pull_kernel(const float* const* __restrict__ peers, const int* __restrict__ owner,
+                                 const int* __restrict__ lrow, const int* __restrict__ halo_src, int64_t n_halo,
+                                 int F4, float4* __restrict__ out) {
+  const int64_t total = n_halo * F4;
+  const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < total; i += stride) {
+    const int64_t h = i / F4;
+    const int v = static_cast<int>(i - h * F4);
+    const int c = halo_src[h];
+    const float4* src = reinterpret_cast<const float4*>(peers[owner[c]] + static_cast<int64_t>(lrow[c]) * F4 * 4);
+    out[i] = src[v];
+  }
+}
+
+void launch_halo_pull(cudaStream_t st, const float* const* peers, const int* owner, const int* lrow,
+                      const int* halo_src, int64_t n_halo, int F, float* out) {
+  if (n_halo == 0) return;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const int64_t total = n_halo * (F / 4);
+  const int blocks = static_cast<int>(std::min<int64_t>((total + 255) / 256, static_cast<int64_t>(num_sms(dev)) * 8));
+  count_launch();
+  halo_pull_kernel<<<blocks, 256, 0, st>>>(peers, owner, lrow, halo_src, n_halo, F / 4,
+                                           reinterpret_cast<float4*>(out));
+}
+
+// Aggregation over [this rank's rows | pulled halo rows] (columns remapped once
+// per graph: local sources -> their row in x, halo sources -> n_split + pull slot).
+void launch_spmm_two_tables(cudaStream_t st, const int64_t* rowptr, const int* col, const float* val, const float* x,
+                            const float* halo, int n_split, int64_t n_rows, int F, float* out) {
+  if (n_rows == 0) return;
+  cudaMemsetAsync(out, 0, static_cast<size_t>(n_rows) * F * sizeof(float), st);
+  launch_chunked(st, rowptr, col, val, TwoTables{x, halo, n_split, F}, n_rows, F, LocalOut{out, F, 0});
 }
 
 // Its backward over the transposed CSR (rows = source rows): each source row's

@@ -119,6 +119,10 @@ void tgn_peer_mail_write(const at::Tensor& roots, const at::Tensor& n_roots, con
 at::Tensor spmm_peer_gather(const at::Tensor& rowptr, const at::Tensor& col, const at::Tensor& val,
                             const at::Tensor& peers, const at::Tensor& src_owner, const at::Tensor& src_row,
                             int64_t n_rows, int64_t F);
+at::Tensor halo_pull(const at::Tensor& peers, const at::Tensor& src_owner, const at::Tensor& src_row,
+                     const at::Tensor& halo_src, int64_t F);
+at::Tensor spmm_two_tables(const at::Tensor& rowptr, const at::Tensor& col, const at::Tensor& val,
+                           const at::Tensor& x, const at::Tensor& halo, int64_t n_rows);
 void spmm_peer_push(const at::Tensor& rowptr_t, const at::Tensor& col_t, const at::Tensor& val_t,
                     const at::Tensor& grad_dst, int64_t n_src, const at::Tensor& peers, const at::Tensor& src_owner,
                     const at::Tensor& src_row);
@@ -170,6 +174,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("spmm_csr", &spmm_csr);
   m.def("spmm_peer_gather", &spmm_peer_gather);
   m.def("spmm_peer_push", &spmm_peer_push);
+  m.def("halo_pull", &halo_pull);
+  m.def("spmm_two_tables", &spmm_two_tables);
   m.def("lstm_fwd", &lstm_fwd);
   m.def("lstm_bwd", &lstm_bwd);
 }

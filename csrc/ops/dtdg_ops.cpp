@@ -216,6 +216,33 @@ at::Tensor spmm_peer_gather(const at::Tensor& rowptr, const at::Tensor& col, con
   return out;
 }
 
+at::Tensor halo_pull(const at::Tensor& peers, const at::Tensor& src_owner, const at::Tensor& src_row,
+                     const at::Tensor& halo_src, int64_t F) {
+  SU_CHECK_I32(src_owner); SU_CHECK_I32(src_row); SU_CHECK_I32(halo_src);
+  TORCH_CHECK(peers.is_cuda() && peers.scalar_type() == at::kLong, "peer table must be cuda int64");
+  TORCH_CHECK(F % 4 == 0, "halo rows are pulled in 16-byte vectors: F must be a multiple of 4");
+  at::Tensor out = at::empty({halo_src.numel(), F}, src_owner.options().dtype(at::kFloat));
+  launch_halo_pull(cur_stream(), reinterpret_cast<const float* const*>(peers.data_ptr<int64_t>()),
+                   src_owner.data_ptr<int>(), src_row.data_ptr<int>(), halo_src.data_ptr<int>(), halo_src.numel(),
+                   static_cast<int>(F), out.data_ptr<float>());
+  SU_LAUNCH_CHECK();
+  return out;
+}
+
+at::Tensor spmm_two_tables(const at::Tensor& rowptr, const at::Tensor& col, const at::Tensor& val,
+                           const at::Tensor& x, const at::Tensor& halo, int64_t n_rows) {
+  SU_CHECK_I64(rowptr); SU_CHECK_I32(col); SU_CHECK_F32(val); SU_CHECK_F32(x); SU_CHECK_CONTIG(x);
+  SU_CHECK_F32(halo); SU_CHECK_CONTIG(halo);
+  const int F = static_cast<int>(x.size(1));
+  TORCH_CHECK(halo.numel() == 0 || halo.size(1) == F, "halo rows must have the width of x");
+  at::Tensor out = at::empty({n_rows, F}, x.options());
+  launch_spmm_two_tables(cur_stream(), rowptr.data_ptr<int64_t>(), col.data_ptr<int>(), val.data_ptr<float>(),
+                         x.data_ptr<float>(), halo.numel() ? halo.data_ptr<float>() : nullptr,
+                         static_cast<int>(x.size(0)), n_rows, F, out.data_ptr<float>());
+  SU_LAUNCH_CHECK();
+  return out;
+}
+
 void spmm_peer_push(const at::Tensor& rowptr_t, const at::Tensor& col_t, const at::Tensor& val_t,
                     const at::Tensor& grad_dst, int64_t n_src, const at::Tensor& peers, const at::Tensor& src_owner,
                     const at::Tensor& src_row) {

@@ -191,6 +191,17 @@ def test_halo_gather_and_push_kernels():
                              src_owner, src_row, n_dst, F)
     ref = torch.zeros(n_dst, F, device="cuda").index_add_(0, dst, x_src[src] * val[:, None])
     torch.testing.assert_close(out, ref, rtol=1e-5, atol=1e-5)
+    # pull-once form: rank 0's view, the rows owned by rank 1 are pulled into a
+    # local halo table and the aggregation reads [rank 0's rows | halo rows]
+    remote = src_owner != 0
+    halo_src = torch.nonzero(remote).view(-1).int()
+    halo = C.halo_pull(_table(*stages), src_owner, src_row, halo_src, F)
+    torch.testing.assert_close(halo, x_src[halo_src.long()])
+    slot = torch.cumsum(remote.int(), 0) - 1
+    remap = torch.where(remote, counts[0] + slot, src_row.long())
+    col2 = remap[src[order]].int().contiguous()
+    out2 = C.spmm_two_tables(rowptr, col2, val[order].contiguous(), stages[0][: counts[0]].contiguous(), halo, n_dst)
+    torch.testing.assert_close(out2, ref, rtol=1e-5, atol=1e-5)
     # backward push: grad of source rows lands in the owners' buffers
     g = torch.randn(n_dst, F, device="cuda")
     order_t = torch.argsort(src, stable=True)
