@@ -162,6 +162,63 @@ __global__ void __launch_bounds__(256, 2) spmm_chunked_kernel(const int64_t* __r
         for (int u = 0; u < kUnroll; ++u) {
           if (active && e0 + u < n) load_vec<VEC>(rows.row(scol[e0 + u]) + f0, t[u]);
         }
+        const int cnt = (n - e0) < kUnroll ? (n - e0) : kUnroll;
+        const int64_t s0 = sb + e0;  // first edge of the batch
+        // the current row must hold edge s0 (after a slow-path batch it may end just before)
+        while (s0 >= re) {
+          if (have && active) {
+            const bool whole = rs >= E0 && re <= E1;
+#pragma unroll
+            for (int v = 0; v < VEC; ++v) out.put(row, f0 + v, acc[v], whole);
+          }
+#pragma unroll
+          for (int v = 0; v < VEC; ++v) acc[v] = 0.f;
+          have = false;
+          rs = re;
+          ++row;
+          if (row - wrow == 32) {
+            wrow = row;
+            rend = (wrow + lane < n_rows) ? rowptr[wrow + lane + 1] : INT64_MAX;
+          }
+          re = __shfl_sync(0xffffffffu, rend, static_cast<int>(row - wrow));
+        }
+        // Fast path: the 32-row window holds every row that ends inside the batch
+        // and the row of the edge after it. The positions where rows end come
+        // as one bit mask, so an edge costs its FMAs and a bit test.
+        if (__shfl_sync(0xffffffffu, rend, 31) <= s0 + cnt && wrow != row) {
+          wrow = row;
+          rend = (wrow + lane < n_rows) ? rowptr[wrow + lane + 1] : INT64_MAX;
+        }
+        if (__shfl_sync(0xffffffffu, rend, 31) > s0 + cnt) {
+          const int64_t pe = rend - 1 - s0;  // this lane's row ends at batch edge pe
+          unsigned ends = (pe >= 0 && pe < cnt) ? (1u << static_cast<int>(pe)) : 0u;
+#pragma unroll
+          for (int o = 16; o > 0; o >>= 1) ends |= __shfl_xor_sync(0xffffffffu, ends, o);
+#pragma unroll
+          for (int u = 0; u < kUnroll; ++u) {
+            if (u >= cnt) continue;
+            const float w = sval[e0 + u];
+#pragma unroll
+            for (int v = 0; v < VEC; ++v) acc[v] = fmaf(w, t[u][v], acc[v]);
+            have = true;
+            if ((ends >> u) & 1u) {  // row `row` ends at this edge (warp-uniform)
+              if (active) {
+                const bool whole = rs >= E0;  // its end s0 + u + 1 is inside the range
+#pragma unroll
+                for (int v = 0; v < VEC; ++v) out.put(row, f0 + v, acc[v], whole);
+              }
+#pragma unroll
+              for (int v = 0; v < VEC; ++v) acc[v] = 0.f;
+              have = false;
+              // next: the row holding edge s0 + u + 1 (empty rows in between end at s0 + u + 1)
+              const int l = __ffs(__ballot_sync(0xffffffffu, rend > s0 + u + 1)) - 1;
+              row = wrow + l;
+              rs = s0 + u + 1;
+              re = __shfl_sync(0xffffffffu, rend, l);
+            }
+          }
+          continue;
+        }
 #pragma unroll
         for (int u = 0; u < kUnroll; ++u) {
           if (e0 + u >= n) continue;  // (no break: the loop must unroll to keep t[] in registers)
