@@ -91,7 +91,7 @@ __device__ __forceinline__ void load_vec(const float* p, float (&t)[VEC]) {
 }
 
 template <int VEC, class Rows, class Out>
-__global__ void __launch_bounds__(256, 2) spmm_chunked_kernel(const int64_t* __restrict__ rowptr,
+__global__ void __launch_bounds__(256, 3) spmm_chunked_kernel(const int64_t* __restrict__ rowptr,
                                                               const int* __restrict__ col,
                                                               const float* __restrict__ val, const Rows rows,
                                                               int64_t n_rows, int F, const Out out) {
@@ -127,7 +127,9 @@ __global__ void __launch_bounds__(256, 2) spmm_chunked_kernel(const int64_t* __r
   }
   for (int fbase = 0; fbase < F; fbase += 32 * VEC) {
     const int f0 = fbase + lane * VEC;
-    const bool active = f0 < F;  // every lane takes part in the control flow
+    // every lane takes part in the control flow; with VEC >= 2 the dispatch
+    // guarantees F % (32 * VEC) == 0, so every lane has features in every pass
+    const bool active = VEC >= 2 || f0 < F;
     int64_t row = lo;
     int64_t rs = rowptr[row];
     // lane l holds the end of row `wrow + l`
@@ -158,9 +160,16 @@ __global__ void __launch_bounds__(256, 2) spmm_chunked_kernel(const int64_t* __r
       __syncwarp();
       for (int e0 = 0; e0 < n; e0 += kUnroll) {
         float t[kUnroll][VEC];
+        if (e0 + kUnroll <= n) {
 #pragma unroll
-        for (int u = 0; u < kUnroll; ++u) {
-          if (active && e0 + u < n) load_vec<VEC>(rows.row(scol[e0 + u]) + f0, t[u]);
+          for (int u = 0; u < kUnroll; ++u) {
+            if (active) load_vec<VEC>(rows.row(scol[e0 + u]) + f0, t[u]);
+          }
+        } else {
+#pragma unroll
+          for (int u = 0; u < kUnroll; ++u) {
+            if (active && e0 + u < n) load_vec<VEC>(rows.row(scol[e0 + u]) + f0, t[u]);
+          }
         }
         const int cnt = (n - e0) < kUnroll ? (n - e0) : kUnroll;
         const int64_t s0 = sb + e0;  // first edge of the batch
@@ -194,6 +203,16 @@ __global__ void __launch_bounds__(256, 2) spmm_chunked_kernel(const int64_t* __r
           unsigned ends = (pe >= 0 && pe < cnt) ? (1u << static_cast<int>(pe)) : 0u;
 #pragma unroll
           for (int o = 16; o > 0; o >>= 1) ends |= __shfl_xor_sync(0xffffffffu, ends, o);
+          if (ends == 0u && cnt == kUnroll) {  // the whole batch continues row `row`
+#pragma unroll
+            for (int u = 0; u < kUnroll; ++u) {
+              const float w = sval[e0 + u];
+#pragma unroll
+              for (int v = 0; v < VEC; ++v) acc[v] = fmaf(w, t[u][v], acc[v]);
+            }
+            have = true;
+            continue;
+          }
 #pragma unroll
           for (int u = 0; u < kUnroll; ++u) {
             if (u >= cnt) continue;
@@ -261,7 +280,7 @@ static void launch_chunked(cudaStream_t st, const int64_t* rowptr, const int* co
   int dev = 0;
   cudaGetDevice(&dev);
   const int threads = 256;
-  const int blocks = num_sms(dev) * 2;  // persistent: two 256-thread blocks per SM (128 registers a thread)
+  const int blocks = num_sms(dev) * 3;  // persistent: three 256-thread blocks per SM (80 registers a thread)
   count_launch();
   if (F % 128 == 0) spmm_chunked_kernel<4><<<blocks, threads, 0, st>>>(rowptr, col, val, rows, n_rows, F, out);
   else if (F % 64 == 0) spmm_chunked_kernel<2><<<blocks, threads, 0, st>>>(rowptr, col, val, rows, n_rows, F, out);
