@@ -37,6 +37,7 @@ def spmm() -> dict:
     C = cuda_ext()
     dev = "cuda"
     n, m, F = 200_000, 2_000_000, 64
+    torch.manual_seed(1)
     g = torch.Generator().manual_seed(1)
     deg = torch.distributions.Pareto(torch.tensor(1.0), torch.tensor(1.5)).sample((n,)).clamp(max=50_000)
     deg = (deg / deg.sum() * m).round().long()

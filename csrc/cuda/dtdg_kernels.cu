@@ -425,6 +425,96 @@ __global__ void lstm_bwd4_kernel(const float* __restrict__ gates, const float* _
   if (dc_prev) *reinterpret_cast<float4*>(dc_prev + r * H + c) = make_float4(dcp[0], dcp[1], dcp[2], dcp[3]);
 }
 
+// The same gate gradients written straight into the two packed bf16 images the
+// following GEMMs read (no row-major copy, no packing pass): the K-major image
+// of dpre [rows, 4H] for d[x || h] = dpre W, and the MN-major image of dpre^T
+// for dW = dpre^T [x || h] (K = rows). Layout of both: block(tile, chunk) of
+// 128 x 64 bf16 = 16 KB, then 8-row group * 1024 + 8-column group * 128 + row * 16.
+// A thread takes 8 units of one row (one 16-byte vector per gate and image);
+// rows past `rows` write zeros (tile padding of the K-major image, the K
+// padding of the MN-major one, which the weight-gradient GEMM sums over).
+// Requires H % 32 == 0 (whole 64-wide chunks of 4H and whole 128-row MN tiles).
+__global__ void lstm_bwd_pack_kernel(const float* __restrict__ gates, const float* __restrict__ c_prev,
+                                     const float* __restrict__ c_new, const float* __restrict__ dh, int dh_ld,
+                                     const float* __restrict__ dc, int dc_ld, int64_t rows, int H,
+                                     uint8_t* __restrict__ img_k, uint8_t* __restrict__ img_mn,
+                                     float* __restrict__ dc_prev, int64_t rows_k, int64_t rows_mn) {
+  const int H8 = H >> 3;
+  const int64_t idx = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  const int64_t r = idx / H8;
+  if (r >= rows_k) return;
+  const int u0 = static_cast<int>(idx - r * H8) * 8;
+  float d[4][8];
+  if (r < rows) {
+    const float* g = gates + lstm_gate_index(r, H, 0, u0);  // i, f, g, o 16 floats apart
+    const float zero[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    float iv[8], fv[8], gv[8], ov[8], cn[8], cp[8], dhv[8], dcv[8];
+    auto ld8 = [](const float* p, float (&v)[8]) {
+      const float4 a = ldg4(p), b = ldg4(p + 4);
+      v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w; v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+    };
+    ld8(g, iv);
+    ld8(g + 16, fv);
+    ld8(g + 32, gv);
+    ld8(g + 48, ov);
+    ld8(c_new + r * H + u0, cn);
+    if (c_prev) ld8(c_prev + r * H + u0, cp);
+    else for (int u = 0; u < 8; ++u) cp[u] = zero[u];
+    if (dh) ld8(dh + r * dh_ld + u0, dhv);
+    else for (int u = 0; u < 8; ++u) dhv[u] = zero[u];
+    if (dc) ld8(dc + r * dc_ld + u0, dcv);
+    else for (int u = 0; u < 8; ++u) dcv[u] = zero[u];
+    float dcp[8];
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      const float tc = tanhf(cn[u]);
+      const float dct = dcv[u] + dhv[u] * ov[u] * (1.f - tc * tc);
+      d[0][u] = dct * gv[u] * iv[u] * (1.f - iv[u]);
+      d[1][u] = dct * cp[u] * fv[u] * (1.f - fv[u]);
+      d[2][u] = dct * iv[u] * (1.f - gv[u] * gv[u]);
+      d[3][u] = dhv[u] * tc * ov[u] * (1.f - ov[u]);
+      dcp[u] = dct * fv[u];
+    }
+    if (dc_prev) {
+      float4* o = reinterpret_cast<float4*>(dc_prev + r * H + u0);
+      o[0] = make_float4(dcp[0], dcp[1], dcp[2], dcp[3]);
+      o[1] = make_float4(dcp[4], dcp[5], dcp[6], dcp[7]);
+    }
+  } else {
+#pragma unroll
+    for (int q = 0; q < 4; ++q)
+#pragma unroll
+      for (int u = 0; u < 8; ++u) d[q][u] = 0.f;
+  }
+  const int64_t nch_k = (4 * H) >> 6;
+  const int64_t nch_mn = rows_mn >> 6;
+  const int r8 = static_cast<int>(r & 7);
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    const uint4 v = pack_bf16x8(d[q]);
+    const int k = q * H + u0;  // column of dpre = MN index of dpre^T
+    const int64_t off_k = ((r >> 7) * nch_k + (k >> 6)) * 16384 + ((r & 127) >> 3) * 1024 + ((k & 63) >> 3) * 128 + r8 * 16;
+    *reinterpret_cast<uint4*>(img_k + off_k) = v;
+    if (r < rows_mn) {
+      const int64_t off_m = (static_cast<int64_t>(k >> 7) * nch_mn + (r >> 6)) * 16384 + ((k & 127) >> 3) * 1024 +
+                            ((r & 63) >> 3) * 128 + r8 * 16;
+      *reinterpret_cast<uint4*>(img_mn + off_m) = v;
+    }
+  }
+}
+
+void launch_lstm_bwd_pack(cudaStream_t st, const float* gates, const float* c_prev, const float* c_new,
+                          const float* dh, int dh_ld, const float* dc, int dc_ld, int64_t rows, int H, uint8_t* img_k,
+                          uint8_t* img_mn, float* dc_prev) {
+  const int64_t rows_k = (rows + 127) / 128 * 128;
+  const int64_t rows_mn = (rows + 63) / 64 * 64;
+  const int64_t n = rows_k * (H / 8);
+  if (n == 0) return;
+  count_launch();
+  lstm_bwd_pack_kernel<<<(n + 255) / 256, 256, 0, st>>>(gates, c_prev, c_new, dh, dh_ld, dc, dc_ld, rows, H, img_k,
+                                                        img_mn, dc_prev, rows_k, rows_mn);
+}
+
 void launch_lstm_bwd(cudaStream_t st, const float* gates, const float* c_prev, const float* c_new, const float* dh,
                      int dh_ld, const float* dc, int dc_ld, int64_t rows, int H, float* dpre, float* dc_prev) {
   const int64_t n = rows * H;

@@ -194,11 +194,12 @@ template <int BN, int NSUB, class A, class B, class E>
 static bool launch_packed(const A& a, const B& b, const E& e, const GemmShape& sh, cudaStream_t st) {
   constexpr int B_ROWS = BN * NSUB;
   constexpr int smem = packed_smem_bytes<BN, NSUB, E>();
+  constexpr bool kPrepackedA = is_prepacked<A>::value;
   int device = 0;
   cudaGetDevice(&device);
-  const size_t abytes = packed_bytes(sh.M, sh.K, kBM);
+  const size_t abytes = kPrepackedA ? 0 : packed_bytes(sh.M, sh.K, kBM);
   const size_t bbytes = packed_bytes(sh.N, sh.K, B_ROWS);
-  if (abytes == 0 || bbytes == 0) return true;
+  if (packed_bytes(sh.M, sh.K, kBM) == 0 || bbytes == 0) return true;
   uint8_t* ws = g_ws_alloc ? static_cast<uint8_t*>(g_ws_alloc(abytes + bbytes, st)) : workspace(device, abytes + bbytes, st);
   if (ws == nullptr) return false;
   auto kern = tc_gemm_packed_kernel<BN, NSUB, A::kMN, B::kMN, E>;
@@ -215,15 +216,24 @@ static bool launch_packed(const A& a, const B& b, const E& e, const GemmShape& s
   const int64_t va = static_cast<int64_t>(tiles_a) * nchunks * kBM * 8;
   const int64_t vb = static_cast<int64_t>(tiles_b) * nchunks * B_ROWS * 8;
   const int cap = num_sms(device) * 16;
-  const int blocks_a = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>((va + 255) / 256, cap)));
-  const int blocks_b = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>((vb + 255) / 256, cap / 2)));
-  count_launch();
-  pack2_kernel<kBM, A, B_ROWS, B><<<blocks_a + blocks_b, 256, 0, st>>>(a, b, ws, ws + abytes, tiles_a, tiles_b, nchunks,
-                                                                      sh.M, sh.m_dev, sh.N, blocks_a);
-  const int total = tiles_a * tiles_b * std::max(1, sh.ksplit);
-  const int grid = std::min(total, num_sms(device));
   const uint8_t* pa = ws;
   const uint8_t* pb = ws + abytes;
+  if constexpr (kPrepackedA) {
+    (void)va;
+    const int blocks_b = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>((vb + 255) / 256, cap)));
+    count_launch();
+    pack_kernel<B_ROWS, B><<<blocks_b, 256, 0, st>>>(b, ws, tiles_b, nchunks, sh.N, nullptr, sh.N);
+    pa = a.image;
+    pb = ws;
+  } else {
+    const int blocks_a = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>((va + 255) / 256, cap)));
+    const int blocks_b = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>((vb + 255) / 256, cap / 2)));
+    count_launch();
+    pack2_kernel<kBM, A, B_ROWS, B><<<blocks_a + blocks_b, 256, 0, st>>>(a, b, ws, ws + abytes, tiles_a, tiles_b,
+                                                                        nchunks, sh.M, sh.m_dev, sh.N, blocks_a);
+  }
+  const int total = tiles_a * tiles_b * std::max(1, sh.ksplit);
+  const int grid = std::min(total, num_sms(device));
   int* status = device_status_ptr(device);
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(grid);
@@ -265,6 +275,25 @@ void gemm(const MNView<SegSource>& a, const MNView<SegSource>& b, const EpiWeigh
           cudaStream_t st) {
   dispatch(a, b, e, sh, st);
 }
+// Pre-packed A (no fused-producer fallback exists for it): false when the packed
+// path is disabled or its workspace cannot be allocated, nothing launched then.
+template <class A, class B, class E>
+static bool dispatch_prepacked(const A& a, const B& b, const E& e, const GemmShape& sh, cudaStream_t st) {
+  if (packed_disabled()) return false;
+  if (sh.N <= 128) return launch_packed<128, 1>(a, b, e, sh, st);
+  if (sh.N <= 256) return launch_packed<256, 1>(a, b, e, sh, st);
+  return launch_packed<256, 2>(a, b, e, sh, st);
+}
+bool gemm_prepacked(const Prepacked<false>& a, const MNView<WeightSource>& b, const EpiLinear& e, const GemmShape& sh,
+                    cudaStream_t st) {
+  return dispatch_prepacked(a, b, e, sh, st);
+}
+bool gemm_prepacked(const Prepacked<true>& a, const MNView<SegSource>& b, const EpiWeightGrad& e, const GemmShape& sh,
+                    cudaStream_t st) {
+  return dispatch_prepacked(a, b, e, sh, st);
+}
+bool packed_gemm_enabled() { return !packed_disabled(); }
+
 void gemm(const SegSource& a, const WeightSource& b, const EpiGRU& e, const GemmShape& sh, cudaStream_t st) {
   launch_any<128, 1>(a, b, e, sh, st);  // one tile = four gates x 32 hidden units (gate-grouped rows)
 }

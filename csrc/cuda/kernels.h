@@ -118,6 +118,13 @@ void launch_jodie_project_bwd(cudaStream_t st, const int64_t* roots, const int* 
 
 // ---- DTDG ---------------------------------------------------------------------
 void gemm(const SegSource& a, const WeightSource& b, const EpiLSTM& e, const GemmShape& sh, cudaStream_t st);
+// GEMMs whose A image a kernel of the caller wrote (packed path only): false, with
+// nothing launched, when that path is disabled or its workspace is unavailable
+bool gemm_prepacked(const Prepacked<false>& a, const MNView<WeightSource>& b, const EpiLinear& e, const GemmShape& sh,
+                    cudaStream_t st);
+bool gemm_prepacked(const Prepacked<true>& a, const MNView<SegSource>& b, const EpiWeightGrad& e, const GemmShape& sh,
+                    cudaStream_t st);
+bool packed_gemm_enabled();
 void launch_spmm_csr(cudaStream_t st, const int64_t* rowptr, const int* col, const float* val, const float* x,
                      int64_t n_rows, int F, float* out, int accumulate);
 void launch_spmm_peer_gather(cudaStream_t st, const int64_t* rowptr, const int* col, const float* val,
@@ -134,6 +141,12 @@ void launch_spmm_peer_push(cudaStream_t st, const int64_t* rowptr_t, const int* 
                            const int* src_row);
 void launch_lstm_bwd(cudaStream_t st, const float* gates, const float* c_prev, const float* c_new, const float* dh,
                      int dh_ld, const float* dc, int dc_ld, int64_t rows, int H, float* dpre, float* dc_prev);
+// gate gradients written as the K-major image of dpre (the input-gradient GEMM's A)
+// and the MN-major image of dpre^T (the weight-gradient GEMM's A); H % 32 == 0,
+// every pointer 16-byte aligned, dh_ld and dc_ld multiples of 4
+void launch_lstm_bwd_pack(cudaStream_t st, const float* gates, const float* c_prev, const float* c_new,
+                          const float* dh, int dh_ld, const float* dc, int dc_ld, int64_t rows, int H, uint8_t* img_k,
+                          uint8_t* img_mn, float* dc_prev);
 // vectorised form with bf16 pre-activation gradients; requires lstm_bwd_bf16_ok()
 bool lstm_bwd_bf16_ok(const float* gates, const float* c_prev, const float* c_new, const float* dh, int dh_ld,
                       const float* dc, int dc_ld, int H, const void* dpre, const float* dc_prev);

@@ -23,6 +23,8 @@
 // drains its in-flight tensor-core work and frees TMEM before returning.
 #pragma once
 
+#include <type_traits>
+
 #include "common.cuh"
 
 namespace su {
@@ -264,6 +266,19 @@ struct MNView {
   }
 #endif
 };
+
+// An A operand whose packed image was written by an earlier kernel of the caller
+// in the layout of pack_range (tc_gemm_packed.cuh) (K-major when !MN, MN-major when MN), zero
+// padded to whole tiles and chunks. The GEMM then packs B only.
+template <bool MN>
+struct Prepacked {
+  static constexpr bool kMN = MN;
+  const uint8_t* image = nullptr;
+};
+template <class T>
+struct is_prepacked : std::false_type {};
+template <bool MN>
+struct is_prepacked<Prepacked<MN>> : std::true_type {};
 
 // ---------------------------------------------------------------------------
 // Weight sources: rows = concatenated output blocks, K = concatenated input

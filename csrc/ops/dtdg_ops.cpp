@@ -114,6 +114,70 @@ std::vector<at::Tensor> lstm_bwd(const at::Tensor& x, const c10::optional<at::Te
   const int dc_ld = dc_c.defined() ? static_cast<int>(dc_c.stride(0)) : H;
   const float* cp_p = has_c ? c->data_ptr<float>() : nullptr;
   const int DP4 = 4 * H;
+  // xs = [x || h || 1]: the B operand of the weight-gradient GEMM (the ones column gives the bias gradient)
+  SegSource xs;
+  xs.nseg = 3;
+  xs.seg[0] = seg_f32(x, in_dim, pad8(in_dim));
+  if (has_h) xs.seg[1] = seg_f32(*h, H, pad8(H));
+  else {
+    xs.seg[1].kind = kSegZero;
+    xs.seg[1].kpad = pad8(H);
+  }
+  xs.seg[2] = seg_ones();
+  auto wgrad_epi = [&]() {
+    EpiWeightGrad e;
+    e.L = lstm_layout({gwi, gwf, gwg, gwo}, in_dim, H, H);
+    e.L.nseg = 3;
+    e.L.seg_kpad[2] = 8;
+    float* bgs[4] = {gbi.data_ptr<float>(), gbf.data_ptr<float>(), gbg.data_ptr<float>(), gbo.data_ptr<float>()};
+    for (int i = 0; i < 4; ++i) e.bias_grad[i] = bgs[i];
+    e.bias_seg = 2;
+    e.ncols = pad8(in_dim) + pad8(H) + 8;
+    return e;
+  };
+  auto wgrad_shape = [&](int ncols) {
+    GemmShape sh;
+    sh.M = DP4;
+    sh.N = ncols;
+    sh.K = rows;
+    const int nchunks = (rows + kBK - 1) / kBK;
+    const int tiles = ((DP4 + kBM - 1) / kBM) * ((sh.N + 255) / 256);
+    sh.ksplit = wgrad_ksplit(nchunks, tiles);
+    return sh;
+  };
+  // Packed path: the backward kernel writes dpre straight into the two bf16 tile
+  // images the GEMMs read (no row-major dpre, no packing pass over it)
+  if (H % 32 == 0 && in_dim % 8 == 0 && packed_gemm_enabled() &&
+      lstm_bwd_bf16_ok(gates.data_ptr<float>(), cp_p, c_new.data_ptr<float>(), dh_p, dh_ld, dc_p, dc_ld, H, nullptr,
+                       dc_prev.data_ptr<float>())) {
+    const int64_t tiles_k = (rows + kBM - 1) / kBM, chunks_mn = (rows + kBK - 1) / kBK;
+    at::Tensor img_k = at::empty({tiles_k * (DP4 / kBK) * kBM * kBK * 2}, x.options().dtype(at::kByte));
+    at::Tensor img_mn = at::empty({(DP4 / kBM) * chunks_mn * kBM * kBK * 2}, x.options().dtype(at::kByte));
+    launch_lstm_bwd_pack(cur_stream(), gates.data_ptr<float>(), cp_p, c_new.data_ptr<float>(), dh_p, dh_ld, dc_p,
+                         dc_ld, rows, H, img_k.data_ptr<uint8_t>(), img_mn.data_ptr<uint8_t>(),
+                         dc_prev.data_ptr<float>());
+    Prepacked<false> ak;
+    ak.image = img_k.data_ptr<uint8_t>();
+    WeightLayout L = lstm_layout({wi, wf, wg, wo}, in_dim, H, H);
+    L.blk_pad[3] = DP4 - 3 * H;
+    EpiLinear e;
+    e.out = dxh.data_ptr<float>();
+    e.ldo = in_dim + H;
+    e.ncols = in_dim + H;
+    GemmShape sh;
+    sh.M = rows;
+    sh.N = in_dim + pad8(H);
+    sh.K = DP4;
+    TORCH_CHECK(gemm_prepacked(ak, weight_mn(L, DP4), e, sh, cur_stream()),
+                "lstm_bwd: packed GEMM workspace unavailable");
+    Prepacked<true> am;
+    am.image = img_mn.data_ptr<uint8_t>();
+    EpiWeightGrad ew = wgrad_epi();
+    TORCH_CHECK(gemm_prepacked(am, seg_mn(xs, rows), ew, wgrad_shape(ew.ncols), cur_stream()),
+                "lstm_bwd: packed GEMM workspace unavailable");
+    SU_LAUNCH_CHECK();
+    return {dxh.narrow(1, 0, in_dim), dxh.narrow(1, in_dim, H), dc_prev};
+  }
   // pre-activation gradients in bf16 when the vectorised kernel applies (the GEMMs
   // below read them as bf16 operands either way)
   at::Tensor dpre = at::empty({rows, DP4}, x.options().dtype(at::kBFloat16));
@@ -165,33 +229,8 @@ std::vector<at::Tensor> lstm_bwd(const at::Tensor& x, const c10::optional<at::Te
     SegSource dy;
     dy.nseg = 1;
     dy.seg[0] = dpre_seg;
-    SegSource xs;
-    xs.nseg = 3;
-    xs.seg[0] = seg_f32(x, in_dim, pad8(in_dim));
-    if (has_h) xs.seg[1] = seg_f32(*h, H, pad8(H));
-    else {
-      xs.seg[1].kind = kSegZero;
-      xs.seg[1].kpad = pad8(H);
-    }
-    xs.seg[2] = seg_ones();
-    SegMN ta = seg_mn(dy, rows);
-    SegMN tb = seg_mn(xs, rows);
-    EpiWeightGrad e;
-    e.L = lstm_layout({gwi, gwf, gwg, gwo}, in_dim, H, H);
-    e.L.nseg = 3;
-    e.L.seg_kpad[2] = 8;
-    float* bgs[4] = {gbi.data_ptr<float>(), gbf.data_ptr<float>(), gbg.data_ptr<float>(), gbo.data_ptr<float>()};
-    for (int i = 0; i < 4; ++i) e.bias_grad[i] = bgs[i];
-    e.bias_seg = 2;
-    e.ncols = pad8(in_dim) + pad8(H) + 8;
-    GemmShape sh;
-    sh.M = DP4;
-    sh.N = e.ncols;
-    sh.K = rows;
-    const int nchunks = (rows + kBK - 1) / kBK;
-    const int tiles = ((DP4 + kBM - 1) / kBM) * ((sh.N + 255) / 256);
-    sh.ksplit = wgrad_ksplit(nchunks, tiles);
-    gemm(ta, tb, e, sh, cur_stream());
+    EpiWeightGrad e = wgrad_epi();
+    gemm(seg_mn(dy, rows), seg_mn(xs, rows), e, wgrad_shape(e.ncols), cur_stream());
   }
   SU_LAUNCH_CHECK();
   return {dxh.narrow(1, 0, in_dim), dxh.narrow(1, in_dim, H), dc_prev};
