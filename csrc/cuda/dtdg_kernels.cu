@@ -541,4 +541,70 @@ void launch_lstm_bwd_bf16(cudaStream_t st, const float* gates, const float* c_pr
                                                     dc_prev);
 }
 
+// ---------------------------------------------------------------------------
+// Reset-gated GRU cell backward (the elementwise parts; the GEMMs run on the
+// tcgen05 kernel). Forward: z, r = sigmoid(...), c = tanh(W_c [x_c | r h] + b_c),
+// h' = z h + (1 - z) c.
+// ---------------------------------------------------------------------------
+// dz_pre = dh' (h - c) z (1 - z) -> dzr[:, 0:H];  dc_pre = dh' (1 - z) (1 - c^2);  dh_acc = dh' z
+__global__ void rgru_bwd1_kernel(const float* __restrict__ dhn, int dhn_ld, const float* __restrict__ h, int h_ld,
+                                 const float* __restrict__ z, const float* __restrict__ c, int64_t rows, int H,
+                                 float* __restrict__ dzr, float* __restrict__ dc_pre, float* __restrict__ dh_acc) {
+  const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (i >= rows * H) return;
+  const int64_t r = i / H;
+  const int u = static_cast<int>(i - r * H);
+  const float g = dhn[r * dhn_ld + u];
+  const float hv = h ? h[r * h_ld + u] : 0.f;
+  const float zv = z[i], cv = c[i];
+  dzr[r * 2 * H + u] = g * (hv - cv) * zv * (1.f - zv);
+  dc_pre[i] = g * (1.f - zv) * (1.f - cv * cv);
+  if (dh_acc) dh_acc[i] = g * zv;
+}
+
+// dr_pre = drh h r (1 - r) -> dzr[:, H:2H];  dh_acc += drh r
+__global__ void rgru_bwd2_kernel(const float* __restrict__ drh, int drh_ld, const float* __restrict__ h, int h_ld,
+                                 const float* __restrict__ rg, int64_t rows, int H, float* __restrict__ dzr,
+                                 float* __restrict__ dh_acc) {
+  const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (i >= rows * H) return;
+  const int64_t r = i / H;
+  const int u = static_cast<int>(i - r * H);
+  const float d = drh[r * drh_ld + u];
+  const float rv = rg[i];
+  const float hv = h ? h[r * h_ld + u] : 0.f;
+  dzr[r * 2 * H + H + u] = d * hv * rv * (1.f - rv);
+  if (dh_acc) dh_acc[i] += d * rv;
+}
+
+// out = a + b (b row-strided): the direct and the GEMM parts of dh
+__global__ void add_rows_kernel(const float* __restrict__ a, const float* __restrict__ b, int b_ld, int64_t rows, int H,
+                                float* __restrict__ out) {
+  const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (i >= rows * H) return;
+  const int64_t r = i / H;
+  out[i] = a[i] + b[r * b_ld + (i - r * H)];
+}
+
+void launch_rgru_bwd1(cudaStream_t st, const float* dhn, int dhn_ld, const float* h, int h_ld, const float* z,
+                      const float* c, int64_t rows, int H, float* dzr, float* dc_pre, float* dh_acc) {
+  const int64_t n = rows * H;
+  if (n == 0) return;
+  count_launch();
+  rgru_bwd1_kernel<<<(n + 255) / 256, 256, 0, st>>>(dhn, dhn_ld, h, h_ld, z, c, rows, H, dzr, dc_pre, dh_acc);
+}
+void launch_rgru_bwd2(cudaStream_t st, const float* drh, int drh_ld, const float* h, int h_ld, const float* r,
+                      int64_t rows, int H, float* dzr, float* dh_acc) {
+  const int64_t n = rows * H;
+  if (n == 0) return;
+  count_launch();
+  rgru_bwd2_kernel<<<(n + 255) / 256, 256, 0, st>>>(drh, drh_ld, h, h_ld, r, rows, H, dzr, dh_acc);
+}
+void launch_add_rows(cudaStream_t st, const float* a, const float* b, int b_ld, int64_t rows, int H, float* out) {
+  const int64_t n = rows * H;
+  if (n == 0) return;
+  count_launch();
+  add_rows_kernel<<<(n + 255) / 256, 256, 0, st>>>(a, b, b_ld, rows, H, out);
+}
+
 }  // namespace su

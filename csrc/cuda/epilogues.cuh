@@ -471,4 +471,96 @@ struct EpiLSTM {
 };
 
 
+
+// ---------------------------------------------------------------------------
+// Reset-gated GRU cell, the recurrence of T-GCN (reference
+// backends/dtdg/runtime/models.py:166-178) and of EvolveGCN's MatGRU
+// (runtime/modules/rnn_cells.py:38-53):
+//   z = sigmoid(W_z [x_z | h] + b_z), r = sigmoid(W_r [x_r | h] + b_r),
+//   c = tanh(W_c [x_c | r * h] + b_c), h' = z * h + (1 - z) * c.
+// Two GEMMs: the first produces z and r (columns interleaved in groups of 16
+// units, [z | r] x 16, so one thread sees both gates of a unit) and writes z, r
+// and r * h; the second produces c and writes c and h'.
+// ---------------------------------------------------------------------------
+constexpr int kRGruGroup = 16;
+
+struct EpiRGruZR {
+  static constexpr bool kSplitCols = true;
+  static constexpr int kScratchBytes = 0;
+  int H = 0;
+  const float* bz = nullptr;
+  const float* br = nullptr;
+  const float* h = nullptr;  // [rows, h_ld] previous state (nullptr -> zeros)
+  int h_ld = 0;
+  float* z_out = nullptr;    // [rows, H]
+  float* r_out = nullptr;    // [rows, H]
+  float* rh_out = nullptr;   // [rows, H]: r * h, the second GEMM's input
+
+#ifdef __CUDACC__
+  __device__ __forceinline__ void operator()(int row, bool valid, int n0, uint32_t taddr, int tile_cols) const {
+#pragma unroll 1
+    for (int g0 = 0; g0 < tile_cols; g0 += 2 * kRGruGroup) {
+      const int u0 = ((n0 + g0) / (2 * kRGruGroup)) * kRGruGroup;
+      float zv[16], rv[16];
+      tmem_ld16(taddr + g0, zv);
+      tmem_ld16(taddr + g0 + kRGruGroup, rv);
+      if (!valid || u0 >= H) continue;
+      float hv[16];
+#pragma unroll
+      for (int j = 0; j < 16; ++j) hv[j] = (h != nullptr && u0 + j < H) ? h[(int64_t)row * h_ld + u0 + j] : 0.f;
+#pragma unroll
+      for (int j = 0; j < 16; ++j) {
+        const int c = u0 + j;
+        if (c >= H) break;
+        const float z = sigmoidf_(zv[j] + bz[c]);
+        const float r = sigmoidf_(rv[j] + br[c]);
+        const int64_t o = (int64_t)row * H + c;
+        z_out[o] = z;
+        r_out[o] = r;
+        rh_out[o] = r * hv[j];
+      }
+    }
+  }
+#endif
+};
+
+struct EpiRGruOut {
+  static constexpr bool kSplitCols = true;
+  static constexpr int kScratchBytes = 0;
+  int H = 0;
+  const float* bc = nullptr;
+  const float* z = nullptr;  // [rows, H] from the first GEMM
+  const float* h = nullptr;  // [rows, h_ld] (nullptr -> zeros)
+  int h_ld = 0;
+  float* c_out = nullptr;    // [rows, H]
+  float* h_out = nullptr;    // [rows, H]
+
+#ifdef __CUDACC__
+  __device__ __forceinline__ void operator()(int row, bool valid, int n0, uint32_t taddr, int tile_cols) const {
+    const int lim = min(H - n0, tile_cols);
+    for (int c0 = 0; c0 < lim; c0 += 16) {
+      float v[16];
+      tmem_ld16(taddr + c0, v);
+      if (!valid) continue;
+      float zv[16], hv[16];
+#pragma unroll
+      for (int j = 0; j < 16; ++j) {
+        const int c = n0 + c0 + j;
+        zv[j] = c < H ? z[(int64_t)row * H + c] : 0.f;
+        hv[j] = (h != nullptr && c < H) ? h[(int64_t)row * h_ld + c] : 0.f;
+      }
+#pragma unroll
+      for (int j = 0; j < 16; ++j) {
+        const int c = n0 + c0 + j;
+        if (c >= H) break;
+        const float cv = tanhf(v[j] + bc[c]);
+        const int64_t o = (int64_t)row * H + c;
+        c_out[o] = cv;
+        h_out[o] = zv[j] * hv[j] + (1.f - zv[j]) * cv;
+      }
+    }
+  }
+#endif
+};
+
 }  // namespace su

@@ -302,6 +302,13 @@ void gemm(const SegSource& a, const WeightSource& b, const EpiOutLN& e, const Ge
   else launch_any<256, 1>(a, b, e, sh, st);
 }
 
+void gemm(const SegSource& a, const WeightSource& b, const EpiRGruZR& e, const GemmShape& sh, cudaStream_t st) {
+  launch_any<128, 1>(a, b, e, sh, st);  // one tile = [z | r] x 16 units, four times
+}
+void gemm(const SegSource& a, const WeightSource& b, const EpiRGruOut& e, const GemmShape& sh, cudaStream_t st) {
+  if (sh.N <= 128) launch_any<128, 1>(a, b, e, sh, st);
+  else launch_any<256, 1>(a, b, e, sh, st);
+}
 void gemm(const SegSource& a, const WeightSource& b, const EpiLSTM& e, const GemmShape& sh, cudaStream_t st) {
   launch_any<128, 1>(a, b, e, sh, st);  // one tile = four gates x 32 hidden units (gate-grouped rows)
 }

@@ -125,6 +125,14 @@ bool gemm_prepacked(const Prepacked<false>& a, const MNView<WeightSource>& b, co
 bool gemm_prepacked(const Prepacked<true>& a, const MNView<SegSource>& b, const EpiWeightGrad& e, const GemmShape& sh,
                     cudaStream_t st);
 bool packed_gemm_enabled();
+void gemm(const SegSource& a, const WeightSource& b, const EpiRGruZR& e, const GemmShape& sh, cudaStream_t st);
+void gemm(const SegSource& a, const WeightSource& b, const EpiRGruOut& e, const GemmShape& sh, cudaStream_t st);
+// reset-gated GRU cell backward, elementwise parts (dtdg_kernels.cu)
+void launch_rgru_bwd1(cudaStream_t st, const float* dhn, int dhn_ld, const float* h, int h_ld, const float* z,
+                      const float* c, int64_t rows, int H, float* dzr, float* dc_pre, float* dh_acc);
+void launch_rgru_bwd2(cudaStream_t st, const float* drh, int drh_ld, const float* h, int h_ld, const float* r,
+                      int64_t rows, int H, float* dzr, float* dh_acc);
+void launch_add_rows(cudaStream_t st, const float* a, const float* b, int b_ld, int64_t rows, int H, float* out);
 void launch_spmm_csr(cudaStream_t st, const int64_t* rowptr, const int* col, const float* val, const float* x,
                      int64_t n_rows, int F, float* out, int accumulate);
 void launch_spmm_peer_gather(cudaStream_t st, const int64_t* rowptr, const int* col, const float* val,

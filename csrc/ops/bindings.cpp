@@ -123,6 +123,16 @@ at::Tensor halo_pull(const at::Tensor& peers, const at::Tensor& src_owner, const
                      const at::Tensor& halo_src, int64_t F);
 at::Tensor spmm_two_tables(const at::Tensor& rowptr, const at::Tensor& col, const at::Tensor& val,
                            const at::Tensor& x, const at::Tensor& halo, int64_t n_rows);
+std::vector<at::Tensor> rgru_fwd(const at::Tensor& xz, const at::Tensor& xr, const at::Tensor& xc,
+                                 const c10::optional<at::Tensor>& h, const at::Tensor& wz, const at::Tensor& bz,
+                                 const at::Tensor& wr, const at::Tensor& br, const at::Tensor& wc,
+                                 const at::Tensor& bc);
+std::vector<at::Tensor> rgru_bwd(const at::Tensor& xz, const at::Tensor& xr, const at::Tensor& xc,
+                                 const c10::optional<at::Tensor>& h, const at::Tensor& z, const at::Tensor& r,
+                                 const at::Tensor& c, const at::Tensor& rh, const at::Tensor& dhn,
+                                 const at::Tensor& wz, const at::Tensor& wr, const at::Tensor& wc, at::Tensor& gwz,
+                                 at::Tensor& gbz, at::Tensor& gwr, at::Tensor& gbr, at::Tensor& gwc,
+                                 at::Tensor& gbc);
 void spmm_peer_push(const at::Tensor& rowptr_t, const at::Tensor& col_t, const at::Tensor& val_t,
                     const at::Tensor& grad_dst, int64_t n_src, const at::Tensor& peers, const at::Tensor& src_owner,
                     const at::Tensor& src_row);
@@ -175,6 +185,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("spmm_peer_gather", &spmm_peer_gather);
   m.def("spmm_peer_push", &spmm_peer_push);
   m.def("halo_pull", &halo_pull);
+  m.def("rgru_fwd", &rgru_fwd);
+  m.def("rgru_bwd", &rgru_bwd);
   m.def("spmm_two_tables", &spmm_two_tables);
   m.def("lstm_fwd", &lstm_fwd);
   m.def("lstm_bwd", &lstm_bwd);

@@ -293,3 +293,255 @@ void spmm_peer_push(const at::Tensor& rowptr_t, const at::Tensor& col_t, const a
                         src_row.data_ptr<int>());
   SU_LAUNCH_CHECK();
 }
+
+// ---------------------------------------------------------------------------
+// Reset-gated GRU cell (T-GCN, EvolveGCN MatGRU); see EpiRGruZR.
+//   w_z, w_r, w_c: [H, Fx + H] over [x | h] (w_c over [x_c | r * h]).
+// Forward returns (h', z, r, c, rh); the last four are saved for the backward.
+// ---------------------------------------------------------------------------
+static int rgru_check(const at::Tensor& xz, const at::Tensor& xr, const at::Tensor& xc, const at::Tensor& wz) {
+  SU_CHECK_F32(xz); SU_CHECK_F32(xr); SU_CHECK_F32(xc); SU_CHECK_F32(wz);
+  TORCH_CHECK(xz.stride(1) == 1 && xr.stride(1) == 1 && xc.stride(1) == 1, "gate inputs need unit column stride");
+  const int H = static_cast<int>(wz.size(0));
+  TORCH_CHECK(H % 8 == 0, "reset-gated GRU cell: hidden size must be a multiple of 8");
+  return H;
+}
+
+std::vector<at::Tensor> rgru_fwd(const at::Tensor& xz, const at::Tensor& xr, const at::Tensor& xc,
+                                 const c10::optional<at::Tensor>& h, const at::Tensor& wz, const at::Tensor& bz,
+                                 const at::Tensor& wr, const at::Tensor& br, const at::Tensor& wc,
+                                 const at::Tensor& bc) {
+  const int H = rgru_check(xz, xr, xc, wz);
+  const int rows = static_cast<int>(xz.size(0));
+  const int Fx = static_cast<int>(xz.size(1));
+  const int pF = pad8(Fx);
+  const bool has_h = h.has_value() && h->defined();
+  if (has_h) { SU_CHECK_F32(*h); TORCH_CHECK(h->stride(1) == 1, "h needs unit column stride"); }
+  auto opt = xz.options();
+  at::Tensor z = at::empty({rows, H}, opt), r = at::empty({rows, H}, opt), rh = at::empty({rows, H}, opt);
+  at::Tensor c = at::empty({rows, H}, opt), hn = at::empty({rows, H}, opt);
+  if (rows == 0) return {hn, z, r, c, rh};
+  // z, r = sigmoid([x_z | x_r | h] [[W_zx, 0, W_zh], [0, W_rx, W_rh]]^T + b)
+  {
+    SegSource a;
+    a.nseg = 3;
+    a.seg[0] = seg_f32(xz, Fx, pF);
+    a.seg[1] = seg_f32(xr, Fx, pF);
+    if (has_h) a.seg[2] = seg_f32(*h, H, H);
+    else { a.seg[2].kind = kSegZero; a.seg[2].kpad = H; }
+    WeightSource b;
+    b.gate_group = kRGruGroup;
+    b.L.nblk = 2;
+    b.L.nseg = 3;
+    b.L.seg_kpad[0] = pF;
+    b.L.seg_kpad[1] = pF;
+    b.L.seg_kpad[2] = H;
+    for (int i = 0; i < 2; ++i) {
+      b.L.blk_rows[i] = H;
+      b.L.blk_pad[i] = H;
+    }
+    b.L.cell[0][0] = wcell(wz, 0, 0, Fx);
+    b.L.cell[0][2] = wcell(wz, 0, Fx, H);
+    b.L.cell[1][1] = wcell(wr, 0, 0, Fx);
+    b.L.cell[1][2] = wcell(wr, 0, Fx, H);
+    EpiRGruZR e;
+    e.H = H;
+    e.bz = bz.data_ptr<float>();
+    e.br = br.data_ptr<float>();
+    e.h = has_h ? h->data_ptr<float>() : nullptr;
+    e.h_ld = has_h ? static_cast<int>(h->stride(0)) : H;
+    e.z_out = z.data_ptr<float>();
+    e.r_out = r.data_ptr<float>();
+    e.rh_out = rh.data_ptr<float>();
+    GemmShape sh;
+    sh.M = rows;
+    sh.N = 2 * kRGruGroup * ((H + kRGruGroup - 1) / kRGruGroup);
+    sh.K = 2 * pF + H;
+    gemm(a, b, e, sh, cur_stream());
+  }
+  // c = tanh([x_c | r h] W_c^T + b_c), h' = z h + (1 - z) c
+  {
+    SegSource a;
+    a.nseg = 2;
+    a.seg[0] = seg_f32(xc, Fx, pF);
+    a.seg[1] = seg_f32(rh, H, H);
+    WeightSource b;
+    b.L.nblk = 1;
+    b.L.nseg = 2;
+    b.L.seg_kpad[0] = pF;
+    b.L.seg_kpad[1] = H;
+    b.L.blk_rows[0] = H;
+    b.L.blk_pad[0] = H;
+    b.L.cell[0][0] = wcell(wc, 0, 0, Fx);
+    b.L.cell[0][1] = wcell(wc, 0, Fx, H);
+    EpiRGruOut e;
+    e.H = H;
+    e.bc = bc.data_ptr<float>();
+    e.z = z.data_ptr<float>();
+    e.h = has_h ? h->data_ptr<float>() : nullptr;
+    e.h_ld = has_h ? static_cast<int>(h->stride(0)) : H;
+    e.c_out = c.data_ptr<float>();
+    e.h_out = hn.data_ptr<float>();
+    GemmShape sh;
+    sh.M = rows;
+    sh.N = H;
+    sh.K = pF + H;
+    gemm(a, b, e, sh, cur_stream());
+  }
+  SU_LAUNCH_CHECK();
+  return {hn, z, r, c, rh};
+}
+
+// Backward of rgru_fwd: returns (dx_z, dx_r, dx_c, dh) and accumulates the weight
+// and bias gradients (gw_*, gb_*).
+std::vector<at::Tensor> rgru_bwd(const at::Tensor& xz, const at::Tensor& xr, const at::Tensor& xc,
+                                 const c10::optional<at::Tensor>& h, const at::Tensor& z, const at::Tensor& r,
+                                 const at::Tensor& c, const at::Tensor& rh, const at::Tensor& dhn,
+                                 const at::Tensor& wz, const at::Tensor& wr, const at::Tensor& wc, at::Tensor& gwz,
+                                 at::Tensor& gbz, at::Tensor& gwr, at::Tensor& gbr, at::Tensor& gwc,
+                                 at::Tensor& gbc) {
+  const int H = rgru_check(xz, xr, xc, wz);
+  const int rows = static_cast<int>(xz.size(0));
+  const int Fx = static_cast<int>(xz.size(1));
+  const int pF = pad8(Fx);
+  const bool has_h = h.has_value() && h->defined();
+  SU_CHECK_F32(dhn);
+  TORCH_CHECK(dhn.stride(1) == 1, "dh' needs unit column stride");
+  auto opt = xz.options();
+  at::Tensor dzr = at::empty({rows, 2 * H}, opt);  // [dz_pre | dr_pre]
+  at::Tensor dcp = at::empty({rows, H}, opt);
+  at::Tensor dh_acc = has_h ? at::empty({rows, H}, opt) : at::Tensor();
+  at::Tensor t2 = at::empty({rows, pF + H}, opt);        // d[x_c | r h]
+  at::Tensor t1 = at::empty({rows, 2 * pF + H}, opt);    // d[x_z | x_r | h] through the z, r GEMM
+  at::Tensor dh = has_h ? at::empty({rows, H}, opt) : at::Tensor();
+  auto ret = [&]() {
+    return std::vector<at::Tensor>{t1.narrow(1, 0, Fx), t1.narrow(1, pF, Fx), t2.narrow(1, 0, Fx), dh};
+  };
+  if (rows == 0) return ret();
+  const float* hp = has_h ? h->data_ptr<float>() : nullptr;
+  const int h_ld = has_h ? static_cast<int>(h->stride(0)) : H;
+  launch_rgru_bwd1(cur_stream(), dhn.data_ptr<float>(), static_cast<int>(dhn.stride(0)), hp, h_ld, z.data_ptr<float>(),
+                   c.data_ptr<float>(), rows, H, dzr.data_ptr<float>(), dcp.data_ptr<float>(),
+                   has_h ? dh_acc.data_ptr<float>() : nullptr);
+  auto ksplit_for = [&](int M, int N) {
+    const int nchunks = (rows + kBK - 1) / kBK;
+    const int tiles = ((M + kBM - 1) / kBM) * ((N + 255) / 256);
+    return wgrad_ksplit(nchunks, tiles);
+  };
+  // --- candidate GEMM: d[x_c | r h] = dc_pre W_c; dW_c += dc_pre^T [x_c | r h | 1]
+  WeightLayout Lc;
+  Lc.nblk = 1;
+  Lc.nseg = 2;
+  Lc.seg_kpad[0] = pF;
+  Lc.seg_kpad[1] = H;
+  Lc.blk_rows[0] = H;
+  Lc.blk_pad[0] = H;
+  Lc.cell[0][0] = wcell(wc, 0, 0, Fx);
+  Lc.cell[0][1] = wcell(wc, 0, Fx, H);
+  {
+    SegSource a;
+    a.nseg = 1;
+    a.seg[0] = seg_f32(dcp, H, H);
+    EpiLinear e;
+    e.out = t2.data_ptr<float>();
+    e.ldo = pF + H;
+    e.ncols = pF + H;
+    GemmShape sh;
+    sh.M = rows;
+    sh.N = pF + H;
+    sh.K = H;
+    gemm(a, weight_mn(Lc, H), e, sh, cur_stream());
+  }
+  {
+    SegSource dy;
+    dy.nseg = 1;
+    dy.seg[0] = seg_f32(dcp, H, H);
+    SegSource xs;
+    xs.nseg = 3;
+    xs.seg[0] = seg_f32(xc, Fx, pF);
+    xs.seg[1] = seg_f32(rh, H, H);
+    xs.seg[2] = seg_ones();
+    EpiWeightGrad e;
+    e.L = Lc;
+    e.L.nseg = 3;
+    e.L.seg_kpad[2] = 8;
+    e.L.cell[0][0] = wcell(gwc, 0, 0, Fx);
+    e.L.cell[0][1] = wcell(gwc, 0, Fx, H);
+    e.bias_grad[0] = gbc.data_ptr<float>();
+    e.bias_seg = 2;
+    e.ncols = pF + H + 8;
+    GemmShape sh;
+    sh.M = H;
+    sh.N = e.ncols;
+    sh.K = rows;
+    sh.ksplit = ksplit_for(sh.M, sh.N);
+    gemm(seg_mn(dy, rows), seg_mn(xs, rows), e, sh, cur_stream());
+  }
+  // dr_pre = d(r h) h r (1 - r); dh += d(r h) r
+  launch_rgru_bwd2(cur_stream(), t2.data_ptr<float>() + pF, pF + H, hp, h_ld, r.data_ptr<float>(), rows, H,
+                   dzr.data_ptr<float>(), has_h ? dh_acc.data_ptr<float>() : nullptr);
+  // --- gate GEMM: d[x_z | x_r | h] = [dz_pre | dr_pre] [[W_zx, 0, W_zh], [0, W_rx, W_rh]]
+  WeightLayout Lg;
+  Lg.nblk = 2;
+  Lg.nseg = 3;
+  Lg.seg_kpad[0] = pF;
+  Lg.seg_kpad[1] = pF;
+  Lg.seg_kpad[2] = H;
+  for (int i = 0; i < 2; ++i) {
+    Lg.blk_rows[i] = H;
+    Lg.blk_pad[i] = H;
+  }
+  Lg.cell[0][0] = wcell(wz, 0, 0, Fx);
+  Lg.cell[0][2] = wcell(wz, 0, Fx, H);
+  Lg.cell[1][1] = wcell(wr, 0, 0, Fx);
+  Lg.cell[1][2] = wcell(wr, 0, Fx, H);
+  {
+    SegSource a;
+    a.nseg = 1;
+    a.seg[0] = seg_f32(dzr, 2 * H, 2 * H);
+    EpiLinear e;
+    e.out = t1.data_ptr<float>();
+    e.ldo = 2 * pF + H;
+    e.ncols = 2 * pF + H;
+    GemmShape sh;
+    sh.M = rows;
+    sh.N = 2 * pF + H;
+    sh.K = 2 * H;
+    gemm(a, weight_mn(Lg, 2 * H), e, sh, cur_stream());
+  }
+  {
+    SegSource dy;
+    dy.nseg = 1;
+    dy.seg[0] = seg_f32(dzr, 2 * H, 2 * H);
+    SegSource xs;
+    xs.nseg = 4;
+    xs.seg[0] = seg_f32(xz, Fx, pF);
+    xs.seg[1] = seg_f32(xr, Fx, pF);
+    if (has_h) xs.seg[2] = seg_f32(*h, H, H);
+    else { xs.seg[2].kind = kSegZero; xs.seg[2].kpad = H; }
+    xs.seg[3] = seg_ones();
+    EpiWeightGrad e;
+    e.L = Lg;
+    e.L.nseg = 4;
+    e.L.seg_kpad[3] = 8;
+    e.L.cell[0][0] = wcell(gwz, 0, 0, Fx);
+    e.L.cell[0][2] = wcell(gwz, 0, Fx, H);
+    e.L.cell[1][1] = wcell(gwr, 0, 0, Fx);
+    e.L.cell[1][2] = wcell(gwr, 0, Fx, H);
+    e.bias_grad[0] = gbz.data_ptr<float>();
+    e.bias_grad[1] = gbr.data_ptr<float>();
+    e.bias_seg = 3;
+    e.ncols = 2 * pF + H + 8;
+    GemmShape sh;
+    sh.M = 2 * H;
+    sh.N = e.ncols;
+    sh.K = rows;
+    sh.ksplit = ksplit_for(sh.M, sh.N);
+    gemm(seg_mn(dy, rows), seg_mn(xs, rows), e, sh, cur_stream());
+  }
+  if (has_h)
+    launch_add_rows(cur_stream(), dh_acc.data_ptr<float>(), t1.data_ptr<float>() + 2 * pF, 2 * pF + H, rows, H,
+                    dh.data_ptr<float>());
+  SU_LAUNCH_CHECK();
+  return ret();
+}

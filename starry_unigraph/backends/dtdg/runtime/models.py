@@ -16,7 +16,7 @@ from typing import Any
 import torch
 import torch.nn as nn
 
-from starry_unigraph.ops.dtdg import linear
+from starry_unigraph.ops.dtdg import linear, rgru_cell
 from starry_unigraph.runtime.modules import GCNStack, MatGRUCell, _LSTMCell
 from starry_unigraph.runtime.modules.gcn_layers import _gcn_message_pass, _graph_input
 
@@ -77,10 +77,8 @@ class FlareTGCN(nn.Module):
             if h is None:
                 h = torch.zeros(urc.size(0), self.hidden_size, dtype=urc.dtype, device=urc.device)
             u, r, c = urc.chunk(3, dim=-1)
-            u = linear(torch.cat([u, h], -1), self.u_t.weight, self.u_t.bias, 2)
-            r = linear(torch.cat([r, h], -1), self.r_t.weight, self.r_t.bias, 2)
-            c = linear(torch.cat([c, r * h], -1), self.c_t.weight, self.c_t.bias, 3)
-            h = u * h + (1 - u) * c
+            h = rgru_cell(u, r, c, h, self.u_t.weight, self.u_t.bias, self.r_t.weight, self.r_t.bias,
+                          self.c_t.weight, self.c_t.bias)
             if hasattr(graph, "flare_store_state"):
                 graph.flare_store_state(h)
             outputs.append(linear(h, self.out.weight, self.out.bias))

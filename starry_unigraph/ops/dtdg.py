@@ -96,6 +96,41 @@ class _LSTMCell(torch.autograd.Function):
                 gw[0], gb[0], gw[1], gb[1], gw[2], gb[2], gw[3], gb[3])
 
 
+class _RGRUCell(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, xz, xr, xc, h, wz, bz, wr, br, wc, bc):
+        hn, z, r, c, rh = cuda_ext().rgru_fwd(xz, xr, xc, h, wz, bz, wr, br, wc, bc)
+        ctx.save_for_backward(xz, xr, xc, h, z, r, c, rh, wz, wr, wc)
+        return hn
+
+    @staticmethod
+    def backward(ctx, dhn):
+        xz, xr, xc, h, z, r, c, rh, wz, wr, wc = ctx.saved_tensors
+        gw = [torch.zeros_like(w) for w in (wz, wr, wc)]
+        gb = [torch.zeros(w.size(0), device=w.device) for w in (wz, wr, wc)]
+        dxz, dxr, dxc, dh = cuda_ext().rgru_bwd(xz, xr, xc, h, z, r, c, rh, dhn.contiguous(), wz, wr, wc,
+                                                gw[0], gb[0], gw[1], gb[1], gw[2], gb[2])
+        return dxz, dxr, dxc, dh, gw[0], gb[0], gw[1], gb[1], gw[2], gb[2]
+
+
+def rgru_cell(xz: torch.Tensor, xr: torch.Tensor, xc: torch.Tensor, h: torch.Tensor, wz, bz, wr, br, wc,
+              bc) -> torch.Tensor:
+    """Reset-gated GRU cell (T-GCN gates, EvolveGCN MatGRU):
+    z = sigmoid(W_z [x_z | h] + b_z), r = sigmoid(W_r [x_r | h] + b_r),
+    c = tanh(W_c [x_c | r h] + b_c), h' = z h + (1 - z) c.
+    On CUDA two tcgen05 GEMMs with the gate math in their epilogues and a fused
+    backward; elsewhere the same math with torch ops."""
+    H = wz.size(0)
+    if xz.is_cuda and xz.dtype == torch.float32 and H % 8 == 0:
+        def unit(t):
+            return t if t.stride(-1) == 1 else t.contiguous()
+        return _RGRUCell.apply(unit(xz), unit(xr), unit(xc), unit(h), wz, bz, wr, br, wc, bc)
+    z = torch.sigmoid(F.linear(torch.cat([xz, h], -1), wz, bz))
+    r = torch.sigmoid(F.linear(torch.cat([xr, h], -1), wr, br))
+    c = torch.tanh(F.linear(torch.cat([xc, r * h], -1), wc, bc))
+    return z * h + (1 - z) * c
+
+
 def lstm_cell(x: torch.Tensor, h, c, cell) -> tuple[torch.Tensor, torch.Tensor]:
     """cell: module with i_t, f_t, g_t, o_t nn.Linear(in + hidden, hidden)."""
     return _LSTMCell.apply(x.float(), h, c, cell.i_t.weight, cell.i_t.bias, cell.f_t.weight, cell.f_t.bias,

@@ -11,7 +11,7 @@ from __future__ import annotations
 import torch
 import torch.nn as nn
 
-from starry_unigraph.ops.dtdg import linear, lstm_cell
+from starry_unigraph.ops.dtdg import linear, lstm_cell, rgru_cell
 
 
 class MatGRUCell(nn.Module):
@@ -23,6 +23,9 @@ class MatGRUCell(nn.Module):
 
     def forward(self, prev_w: torch.Tensor, inputs: torch.Tensor) -> torch.Tensor:
         inputs = inputs.reshape(1, -1).repeat(prev_w.size(0), 1)
+        if inputs.is_cuda:
+            return rgru_cell(inputs, inputs, inputs, prev_w.float(), self.update.weight, self.update.bias,
+                             self.reset.weight, self.reset.bias, self.htilda.weight, self.htilda.bias)
         xc = torch.cat([inputs, prev_w], dim=1)
         z = linear(xc, self.update.weight, self.update.bias, 2)
         r = linear(xc, self.reset.weight, self.reset.bias, 2)

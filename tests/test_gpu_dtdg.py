@@ -71,6 +71,38 @@ def test_spmm_csr_skewed_rows(F):
     assert _rel(acc.cpu().double(), ref + base.double()) < 1e-6
 
 
+@pytest.mark.parametrize("H,FX,strided", [(64, 64, True), (128, 128, True), (32, 20, False)])
+def test_rgru_cell_fused(H, FX, strided):
+    """Reset-gated GRU cell (T-GCN gates / MatGRU) on the tcgen05 path against
+    the fp32 torch math: outputs and every gradient."""
+    from starry_unigraph.ops.dtdg import rgru_cell
+
+    torch.manual_seed(0)
+    rows = 700
+    if strided:  # gate inputs as column chunks of one [rows, 3 FX] tensor (T-GCN's urc)
+        urc = torch.randn(rows, 3 * FX)
+    else:
+        urc = torch.randn(rows, FX)
+    h0 = torch.randn(rows, H)
+    ws = [torch.randn(H, FX + H) * 0.2 for _ in range(3)]
+    bs = [torch.randn(H) * 0.1 for _ in range(3)]
+
+    def run(dev):
+        u = urc.detach().to(dev).clone().requires_grad_()
+        h = h0.detach().to(dev).clone().requires_grad_()
+        w = [t.detach().to(dev).clone().requires_grad_() for t in ws]
+        b = [t.detach().to(dev).clone().requires_grad_() for t in bs]
+        xz, xr, xc = u.chunk(3, -1) if strided else (u, u, u)
+        out = rgru_cell(xz, xr, xc, h, w[0], b[0], w[1], b[1], w[2], b[2])
+        (out * torch.linspace(-1, 1, H, device=dev)).sum().backward()
+        return [out] + [t.grad for t in (u, h, *w, *b)]
+
+    ref = run("cpu")
+    got = run("cuda")
+    for a, r in zip(got, ref):
+        assert _rel(a.detach().cpu(), r.detach()) < 1.5e-2
+
+
 @pytest.mark.parametrize("H,IN", [(64, 64), (32, 40), (128, 128), (20, 12)])
 def test_lstm_cell_fused(H, IN):
     from starry_unigraph.runtime.modules.rnn_cells import _LSTMCell
