@@ -168,9 +168,17 @@ void launch_peer_barrier(cudaStream_t st, uint64_t* const* flag_ptrs, int rank, 
 void launch_peer_allreduce_adam(cudaStream_t st, int blocks, const float* const* grads, int W, float* p, float* m,
                                 float* v, int64_t n, int64_t* step, unsigned int* done, float lr, float b1, float b2,
                                 float eps, float wd, float scale);
+// historical-cache filter of the write-back (cache == nullptr: push every row)
+struct HistCache {
+  const int64_t* slot_of = nullptr;  // global node id -> cache row (-1: owned here, no filter)
+  float* cache = nullptr;            // [shared nodes, D] last pushed rows
+  float* cache_ts = nullptr;         // [shared nodes] ts of the last push (< 0: never pushed)
+  float thresh = 0.5f;               // push when 1 - cos(new, cached) > thresh
+  int rank = 0;
+};
 void launch_tgn_peer_writeback(cudaStream_t st, const int64_t* roots, const int* n_roots, int rmax,
                                const float* mem_new, int D, const int* owner, float* const* mem_tables,
-                               float* const* ts_tables, const float* ts_max);
+                               float* const* ts_tables, const float* ts_max, const HistCache& hc);
 void launch_tgn_peer_mail_claim(cudaStream_t st, const int64_t* roots, const int* n_roots, int rmax, const int* win,
                                 const int64_t* ev_eid, const float* ev_ts, const int* owner,
                                 unsigned long long* const* claim_tables);

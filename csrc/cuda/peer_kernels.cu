@@ -130,18 +130,59 @@ void launch_peer_allreduce_adam(cudaStream_t st, int blocks, const float* const*
 }
 
 // ---------------------------------------------------------------------------
-// CTDG memory write-back (block per root, D columns)
+// CTDG memory write-back (block of 64 threads per root, D columns)
+//
+// Optional historical-cache filter (reference backends/ctdg/runtime/cache.py:
+// MemShare-style): a root owned by another rank keeps a cached copy of the last
+// row this rank pushed; the new row is pushed only when it was never pushed or
+// its cosine distance to the cached row exceeds `thresh` (= 1 - alpha). A pushed
+// row refreshes the cache.
 // ---------------------------------------------------------------------------
 __global__ void tgn_peer_writeback_kernel(const int64_t* __restrict__ roots, const int* __restrict__ n_roots, int rmax,
                                           const float* __restrict__ mem_new, int D, const int* __restrict__ owner,
                                           float* const* __restrict__ mem_tables, float* const* __restrict__ ts_tables,
-                                          const float* __restrict__ ts_max) {
+                                          const float* __restrict__ ts_max, HistCache hc) {
   const int r = blockIdx.x;
   if (r >= rmax || r >= *n_roots) return;
   const int64_t v = roots[r];
   const int o = owner[v];
-  float* dst = mem_tables[o] + v * D;
   const float* src = mem_new + static_cast<int64_t>(r) * D;
+  if (hc.cache != nullptr && o != hc.rank) {
+    const int64_t slot = hc.slot_of[v];
+    if (slot >= 0) {
+      float* cr = hc.cache + slot * D;
+      float dot = 0.f, na = 0.f, nb = 0.f;
+      for (int c = threadIdx.x; c < D; c += blockDim.x) {
+        const float a = src[c], b = cr[c];
+        dot += a * b;
+        na += a * a;
+        nb += b * b;
+      }
+      __shared__ float red[3][2];
+#pragma unroll
+      for (int off = 16; off > 0; off >>= 1) {
+        dot += __shfl_xor_sync(0xffffffffu, dot, off);
+        na += __shfl_xor_sync(0xffffffffu, na, off);
+        nb += __shfl_xor_sync(0xffffffffu, nb, off);
+      }
+      const int w = threadIdx.x >> 5;
+      if ((threadIdx.x & 31) == 0) {
+        red[0][w] = dot;
+        red[1][w] = na;
+        red[2][w] = nb;
+      }
+      __syncthreads();
+      dot = red[0][0] + red[0][1];
+      na = red[1][0] + red[1][1];
+      nb = red[2][0] + red[2][1];
+      const bool never = hc.cache_ts[slot] < 0.f;
+      const float cosv = dot / fmaxf(sqrtf(na) * sqrtf(nb), 1e-8f);
+      if (!never && 1.f - cosv <= hc.thresh) return;  // block-uniform: skip the push
+      for (int c = threadIdx.x; c < D; c += blockDim.x) cr[c] = src[c];
+      if (threadIdx.x == 0) hc.cache_ts[slot] = *ts_max;
+    }
+  }
+  float* dst = mem_tables[o] + v * D;
   if ((D & 3) == 0) {
     for (int c = threadIdx.x; c < D / 4; c += blockDim.x)
       reinterpret_cast<float4*>(dst)[c] = reinterpret_cast<const float4*>(src)[c];
@@ -156,11 +197,11 @@ __global__ void tgn_peer_writeback_kernel(const int64_t* __restrict__ roots, con
 
 void launch_tgn_peer_writeback(cudaStream_t st, const int64_t* roots, const int* n_roots, int rmax,
                                const float* mem_new, int D, const int* owner, float* const* mem_tables,
-                               float* const* ts_tables, const float* ts_max) {
+                               float* const* ts_tables, const float* ts_max, const HistCache& hc) {
   if (rmax <= 0) return;
   count_launch();
   tgn_peer_writeback_kernel<<<rmax, 64, 0, st>>>(roots, n_roots, rmax, mem_new, D, owner, mem_tables, ts_tables,
-                                                 ts_max);
+                                                 ts_max, hc);
 }
 
 // ---------------------------------------------------------------------------

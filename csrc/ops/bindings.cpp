@@ -106,7 +106,8 @@ void peer_allreduce_adam(const at::Tensor& grad_ptrs, int64_t world, at::Tensor&
                          double scale);
 void tgn_peer_writeback(const at::Tensor& roots, const at::Tensor& n_roots, const at::Tensor& mem_new,
                         const at::Tensor& owner, const at::Tensor& mem_ptrs, const at::Tensor& ts_ptrs,
-                        const at::Tensor& ts_max);
+                        const at::Tensor& ts_max, const c10::optional<std::vector<at::Tensor>>& cache,
+                        double thresh, int64_t rank);
 void tgn_peer_mail_claim(const at::Tensor& roots, const at::Tensor& n_roots, const at::Tensor& win,
                          const at::Tensor& ev_eid, const at::Tensor& ev_ts, const at::Tensor& owner,
                          const at::Tensor& claim_ptrs);
@@ -178,7 +179,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("adam_flat", &adam_flat);
   m.def("peer_barrier", &peer_barrier);
   m.def("peer_allreduce_adam", &peer_allreduce_adam);
-  m.def("tgn_peer_writeback", &tgn_peer_writeback);
+  m.def("tgn_peer_writeback", &tgn_peer_writeback, py::arg("roots"), py::arg("n_roots"), py::arg("mem_new"),
+        py::arg("owner"), py::arg("mem_ptrs"), py::arg("ts_ptrs"), py::arg("ts_max"), py::arg("cache") = py::none(),
+        py::arg("thresh") = 0.5, py::arg("rank") = 0);
   m.def("tgn_peer_mail_claim", &tgn_peer_mail_claim);
   m.def("tgn_peer_mail_write", &tgn_peer_mail_write);
   m.def("spmm_csr", &spmm_csr);

@@ -36,14 +36,31 @@ void peer_allreduce_adam(const at::Tensor& grad_ptrs, int64_t world, at::Tensor&
   SU_LAUNCH_CHECK();
 }
 
+// cache: optional (slot_of int64 [num_nodes], cache f32 [shared, D], cache_ts f32 [shared]) with
+// threshold `thresh` = 1 - alpha and this rank's id: the historical-cache filter of the push
 void tgn_peer_writeback(const at::Tensor& roots, const at::Tensor& n_roots, const at::Tensor& mem_new,
                         const at::Tensor& owner, const at::Tensor& mem_ptrs, const at::Tensor& ts_ptrs,
-                        const at::Tensor& ts_max) {
+                        const at::Tensor& ts_max, const c10::optional<std::vector<at::Tensor>>& cache,
+                        double thresh, int64_t rank) {
   SU_CHECK_I64(roots); SU_CHECK_I32(owner); SU_CHECK_F32(mem_new);
+  HistCache hc;
+  if (cache.has_value() && !cache->empty()) {
+    TORCH_CHECK(cache->size() == 3, "historical cache: (slot_of, cache, cache_ts)");
+    const at::Tensor& slot_of = (*cache)[0];
+    const at::Tensor& rows = (*cache)[1];
+    const at::Tensor& ts = (*cache)[2];
+    SU_CHECK_I64(slot_of); SU_CHECK_F32(rows); SU_CHECK_F32(ts); SU_CHECK_CONTIG(rows);
+    TORCH_CHECK(rows.size(1) == mem_new.size(1), "historical cache rows must have the memory width");
+    hc.slot_of = slot_of.data_ptr<int64_t>();
+    hc.cache = rows.data_ptr<float>();
+    hc.cache_ts = ts.data_ptr<float>();
+    hc.thresh = static_cast<float>(thresh);
+    hc.rank = static_cast<int>(rank);
+  }
   launch_tgn_peer_writeback(cur_stream(), roots.data_ptr<int64_t>(), n_roots.data_ptr<int>(),
                             static_cast<int>(roots.numel()), mem_new.data_ptr<float>(),
                             static_cast<int>(mem_new.size(1)), owner.data_ptr<int>(), table<float* const*>(mem_ptrs),
-                            table<float* const*>(ts_ptrs), ts_max.data_ptr<float>());
+                            table<float* const*>(ts_ptrs), ts_max.data_ptr<float>(), hc);
   SU_LAUNCH_CHECK();
 }
 

@@ -95,6 +95,8 @@ def build_ctdg_runtime(session_ctx: SessionContext, dataset: TGTemporalDataset |
                                    mailbox_slots=slots, grad_numel=sum(p.numel() for p in model.parameters()),
                                    owner=owner, device=torch.device(device))
             peer.attach(memory)
+            if bool(c.get("historical_filter", True)):
+                peer.enable_historical_filter(float(c.get("historical_alpha", 0.5)))
         elif dctx.is_distributed:
             import torch.distributed as dist
 

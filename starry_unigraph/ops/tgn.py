@@ -343,7 +343,7 @@ class TGNCudaEngine:
                                   o.done, float(o.param_groups[0]["lr"]), float(o.betas[0]), float(o.betas[1]),
                                   float(o.eps), float(o.weight_decay), 1.0 / P.world)
         C.tgn_peer_writeback(self.roots, self.n_roots, self.mem_new, P.owner, P.tables["memory"],
-                             P.tables["memory_ts"], self.ts_max)
+                             P.tables["memory_ts"], self.ts_max, P.hist_cache, P.hist_thresh, P.rank)
         C.tgn_peer_mail_claim(self.roots, self.n_roots, self.win, self.ev_eid, self.ev_ts, P.owner, P.tables["claim"])
         P.barrier(C)
         C.tgn_peer_mail_write(self.roots, self.n_roots, self.win, self.src_idx, self.dst_idx, self.ev_eid, self.ev_ts,

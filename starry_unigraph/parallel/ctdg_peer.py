@@ -65,6 +65,24 @@ class PeerCTDGContext:
         torch.cuda.synchronize(self.device)
         a.barrier_host()
 
+    def enable_historical_filter(self, alpha: float) -> None:
+        """Historical-cache filter of the memory push (reference
+        backends/ctdg/runtime/cache.py): for every node this rank does not own, the
+        last row it pushed is kept here, and a new row is pushed to the owner only
+        when its cosine distance to that row exceeds 1 - alpha (or it was never
+        pushed). The check runs inside the write-back kernel."""
+        N, D = self.arena["memory"].shape
+        shared = self.owner != self.rank
+        slot_of = torch.full((N,), -1, dtype=torch.int64, device=self.device)
+        n_shared = int(shared.sum())
+        slot_of[shared] = torch.arange(n_shared, dtype=torch.int64, device=self.device)
+        self.hist_cache = [slot_of, torch.zeros(n_shared, D, device=self.device),
+                           torch.full((n_shared,), -1.0, device=self.device)]
+        self.hist_thresh = 1.0 - float(alpha)
+
+    hist_cache: list[torch.Tensor] | None = None
+    hist_thresh: float = 0.5
+
     def attach(self, memory_bank) -> None:
         """Re-seat a CTDGMemoryBank's tables on the symmetric storage."""
         a = self.arena

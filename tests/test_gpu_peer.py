@@ -107,6 +107,41 @@ def test_memory_writeback_and_mail_claims():
     assert float(mail_ts[0][2]) == 5.0 and torch.equal(mail[0][2][2 * D:], efeat[12])
 
 
+def test_writeback_historical_filter():
+    """Rank 0 pushes rows of nodes owned by rank 1 through the historical cache:
+    a first push always lands, a row within the cosine threshold of the cached one
+    is dropped, a row beyond it lands and refreshes the cache; rank 0's own nodes
+    are never filtered."""
+    C = _C()
+    N, D = 6, 16
+    owner = (torch.arange(N, device="cuda") % 2).int()
+    mem = [torch.zeros(N, D, device="cuda") for _ in range(2)]
+    mts = [torch.full((N,), -1.0, device="cuda") for _ in range(2)]
+    shared = owner != 0
+    slot_of = torch.full((N,), -1, dtype=torch.int64, device="cuda")
+    slot_of[shared] = torch.arange(int(shared.sum()), device="cuda")
+    cache = [slot_of, torch.zeros(int(shared.sum()), D, device="cuda"),
+             torch.full((int(shared.sum()),), -1.0, device="cuda")]
+    base = torch.randn(D, device="cuda")
+
+    def push(rows, ts):
+        r = torch.tensor([1, 0], dtype=torch.int64, device="cuda")  # node 1 (rank 1's), node 0 (own)
+        C.tgn_peer_writeback(r, torch.tensor([2], dtype=torch.int32, device="cuda"), torch.stack(rows), owner,
+                             _table(*mem), _table(*mts), torch.tensor([ts], device="cuda"), cache, 0.5, 0)
+        torch.cuda.synchronize()
+
+    push([base, base], 1.0)                                   # never pushed: lands
+    assert torch.equal(mem[1][1], base) and float(mts[1][1]) == 1.0
+    near = base + 0.01 * torch.randn(D, device="cuda")        # cos distance ~ 1e-4 < 0.5: dropped
+    push([near, near], 2.0)
+    assert torch.equal(mem[1][1], base) and float(mts[1][1]) == 1.0
+    assert torch.equal(mem[0][0], near) and float(mts[0][0]) == 2.0  # own node: always written
+    far = -base                                               # cos distance 2 > 0.5: lands, cache refreshed
+    push([far, far], 3.0)
+    assert torch.equal(mem[1][1], far) and float(mts[1][1]) == 3.0
+    assert torch.equal(cache[1][int(slot_of[1])], far) and float(cache[2][int(slot_of[1])]) == 3.0
+
+
 def test_sharded_memory_reads_match_local_table():
     """The attention projections with node memory split over two emulated owner
     tables (peer descriptor) equal the same projections on the full table, with
