@@ -42,12 +42,39 @@ def gcn_aggregate(block, x_src: torch.Tensor) -> torch.Tensor:
     return out.index_add(0, block.edge_dst.long(), x_src[block.edge_src.long()] * norm.unsqueeze(1))
 
 
+def _grad_sink(t: torch.Tensor | None) -> torch.Tensor | None:
+    """The parameter's own .grad when the weight-gradient kernels may add into it
+    in place: a leaf parameter whose gradient already exists (the flat gradient
+    buffer's views). The backward then returns None for it, so autograd runs no
+    zero-fill and no accumulation kernel. Otherwise None (a fresh buffer is
+    returned as usual)."""
+    if t is not None and t.is_leaf and t.requires_grad and t.grad is not None and t.grad.is_contiguous() \
+            and t.grad.dtype == torch.float32:
+        return t.grad
+    return None
+
+
+def _wgrad_buffers(ws, bs):
+    """Per weight, then per bias: (buffer the kernel accumulates into, value the
+    backward returns for it)."""
+    out = []
+    for t in list(ws) + list(bs):
+        sink = _grad_sink(t)
+        if sink is not None:
+            out.append((sink, None))
+        else:
+            z = torch.zeros_like(t, dtype=torch.float32)
+            out.append((z, z))
+    return out
+
+
 class _Linear(torch.autograd.Function):
     @staticmethod
     def forward(ctx, x, w, b, act):
         y = cuda_ext().linear_fwd(x.contiguous(), w.contiguous(), b, int(act))
         ctx.act = int(act)
         ctx.has_b = b is not None
+        ctx.w_ref, ctx.b_ref = w, b  # parameters: their .grad may take the gradient in place
         ctx.save_for_backward(x, w, y if act else None)
         return y
 
@@ -63,10 +90,14 @@ class _Linear(torch.autograd.Function):
         elif ctx.act == 3:
             gy = gy * (1 - y * y)
         gx = C.linear_dgrad(gy, w.contiguous()) if ctx.needs_input_grad[0] else None
-        gw = torch.zeros_like(w)
-        gb = torch.zeros(w.size(0), device=w.device) if ctx.has_b else None
+        sw = _grad_sink(ctx.w_ref)
+        gw = sw if sw is not None else torch.zeros_like(w)
+        gb, sb = None, None
+        if ctx.has_b:
+            sb = _grad_sink(ctx.b_ref)
+            gb = sb if sb is not None else torch.zeros(w.size(0), device=w.device)
         C.linear_wgrad(gy, x.contiguous(), gw, gb)
-        return gx, gw, gb, None
+        return gx, (None if sw is not None else gw), (None if sb is not None else gb), None
 
 
 def linear(x: torch.Tensor, w: torch.Tensor, b: torch.Tensor | None = None, act: int = 0) -> torch.Tensor:
@@ -81,19 +112,21 @@ class _LSTMCell(torch.autograd.Function):
     def forward(ctx, x, h, c, wi, bi, wf, bf, wg, bg, wo, bo):
         hn, cn, gates = cuda_ext().lstm_fwd(x.contiguous(), h, c, wi, bi, wf, bf, wg, bg, wo, bo, True)
         ctx.save_for_backward(x, h, c, cn, gates, wi, wf, wg, wo)
+        ctx.params = (wi, bi, wf, bf, wg, bg, wo, bo)
         ctx.has_h, ctx.has_c = h is not None, c is not None
         return hn, cn
 
     @staticmethod
     def backward(ctx, dh, dc):
         x, h, c, cn, gates, wi, wf, wg, wo = ctx.saved_tensors
-        gw = [torch.zeros_like(w) for w in (wi, wf, wg, wo)]
-        gb = [torch.zeros(w.size(0), device=w.device) for w in (wi, wf, wg, wo)]
+        bufs = _wgrad_buffers(ctx.params[0::2], ctx.params[1::2])  # w_i, w_f, w_g, w_o, b_i, b_f, b_g, b_o
+        gw, gb = [b[0] for b in bufs[:4]], [b[0] for b in bufs[4:]]
         dx, dhp, dcp = cuda_ext().lstm_bwd(x.contiguous(), h if ctx.has_h else None, c if ctx.has_c else None, cn,
                                            gates, dh, dc, wi, wf, wg, wo, gw[0], gb[0], gw[1], gb[1], gw[2], gb[2],
                                            gw[3], gb[3])
+        rw, rb = [b[1] for b in bufs[:4]], [b[1] for b in bufs[4:]]
         return (dx, dhp if ctx.has_h else None, dcp if ctx.has_c else None,
-                gw[0], gb[0], gw[1], gb[1], gw[2], gb[2], gw[3], gb[3])
+                rw[0], rb[0], rw[1], rb[1], rw[2], rb[2], rw[3], rb[3])
 
 
 class _RGRUCell(torch.autograd.Function):
@@ -101,16 +134,18 @@ class _RGRUCell(torch.autograd.Function):
     def forward(ctx, xz, xr, xc, h, wz, bz, wr, br, wc, bc):
         hn, z, r, c, rh = cuda_ext().rgru_fwd(xz, xr, xc, h, wz, bz, wr, br, wc, bc)
         ctx.save_for_backward(xz, xr, xc, h, z, r, c, rh, wz, wr, wc)
+        ctx.params = (wz, bz, wr, br, wc, bc)
         return hn
 
     @staticmethod
     def backward(ctx, dhn):
         xz, xr, xc, h, z, r, c, rh, wz, wr, wc = ctx.saved_tensors
-        gw = [torch.zeros_like(w) for w in (wz, wr, wc)]
-        gb = [torch.zeros(w.size(0), device=w.device) for w in (wz, wr, wc)]
+        bufs = _wgrad_buffers(ctx.params[0::2], ctx.params[1::2])  # w_z, w_r, w_c, b_z, b_r, b_c
+        gw, gb = [b[0] for b in bufs[:3]], [b[0] for b in bufs[3:]]
         dxz, dxr, dxc, dh = cuda_ext().rgru_bwd(xz, xr, xc, h, z, r, c, rh, dhn.contiguous(), wz, wr, wc,
                                                 gw[0], gb[0], gw[1], gb[1], gw[2], gb[2])
-        return dxz, dxr, dxc, dh, gw[0], gb[0], gw[1], gb[1], gw[2], gb[2]
+        rw, rb = [b[1] for b in bufs[:3]], [b[1] for b in bufs[3:]]
+        return dxz, dxr, dxc, dh, rw[0], rb[0], rw[1], rb[1], rw[2], rb[2]
 
 
 def rgru_cell(xz: torch.Tensor, xr: torch.Tensor, xc: torch.Tensor, h: torch.Tensor, wz, bz, wr, br, wc,
