@@ -478,17 +478,37 @@ struct EpiWeightGrad {
       tmem_ld16(taddr + c0, v);
       if (!valid) continue;
 #pragma unroll
-      for (int i = 0; i < 16; ++i) {
-        const int n = n0 + c0 + i;
-        int s, c;
-        if (!L.find_seg(n, s, c)) continue;
-        if (s == bias_seg) {
-          if (c == 0 && bias_grad[b] != nullptr) atomicAdd(bias_grad[b] + r, v[i]);
-          continue;
+      for (int j = 0; j < 4; ++j) {
+        // four columns of one cell: one 16-byte vector reduction instead of four atomics
+        // (segments start at multiples of 8, so an aligned quad never straddles one)
+        {
+          const int n = n0 + c0 + 4 * j;
+          int s, c;
+          if (L.find_seg(n, s, c) && s != bias_seg) {
+            const WCell& e = L.cell[b][s];
+            if (e.vec && e.ptr != nullptr && (c & 3) == 0 && c + 4 <= e.width) {
+              float* dst = const_cast<float*>(e.ptr) + (int64_t)(e.row0 + r) * e.ld + e.col0 + c;
+              asm volatile("red.global.add.v4.f32 [%0], {%1,%2,%3,%4};" ::"l"(dst), "f"(v[4 * j]),
+                           "f"(v[4 * j + 1]), "f"(v[4 * j + 2]), "f"(v[4 * j + 3])
+                           : "memory");
+              continue;
+            }
+          }
         }
-        const WCell& e = L.cell[b][s];
-        if (e.ptr != nullptr && c < e.width)
-          atomicAdd(const_cast<float*>(e.ptr) + (int64_t)(e.row0 + r) * e.ld + e.col0 + c, v[i]);
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          const int i = 4 * j + u;
+          const int n = n0 + c0 + i;
+          int s, c;
+          if (!L.find_seg(n, s, c)) continue;
+          if (s == bias_seg) {
+            if (c == 0 && bias_grad[b] != nullptr) atomicAdd(bias_grad[b] + r, v[i]);
+            continue;
+          }
+          const WCell& e = L.cell[b][s];
+          if (e.ptr != nullptr && c < e.width)
+            atomicAdd(const_cast<float*>(e.ptr) + (int64_t)(e.row0 + r) * e.ld + e.col0 + c, v[i]);
+        }
       }
     }
   }
