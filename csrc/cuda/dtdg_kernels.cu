@@ -56,6 +56,20 @@ struct TwoTables {
 // where a finished row segment goes: this rank's output (plain store for rows
 // inside the chunk, atomic add for rows shared with another chunk), or pushed
 // into the owner rank's buffer with a remote atomic add
+// add v[0..VEC) to p[0..VEC) (16- or 8-byte aligned for VEC 4 / 2) with one vector reduction
+template <int VEC>
+__device__ __forceinline__ void red_add_vec(float* p, const float (&v)[VEC]) {
+  if constexpr (VEC == 4) {
+    asm volatile("red.global.add.v4.f32 [%0], {%1,%2,%3,%4};" ::"l"(p), "f"(v[0]), "f"(v[1]), "f"(v[2]), "f"(v[3])
+                 : "memory");
+  } else if constexpr (VEC == 2) {
+    asm volatile("red.global.add.v2.f32 [%0], {%1,%2};" ::"l"(p), "f"(v[0]), "f"(v[1]) : "memory");
+  } else {
+#pragma unroll
+    for (int i = 0; i < VEC; ++i) atomicAdd(p + i, v[i]);
+  }
+}
+
 struct LocalOut {
   float* out;
   int F;
@@ -65,6 +79,27 @@ struct LocalOut {
     if (whole) *o = accumulate ? *o + v : v;
     else atomicAdd(o, v);
   }
+  // VEC consecutive features at f (f a multiple of VEC; rows VEC-aligned since F % VEC == 0)
+  template <int VEC>
+  __device__ __forceinline__ void put_vec(int64_t row, int f, const float (&v)[VEC], bool whole) const {
+    float* o = out + row * F + f;
+    if (!whole) {
+      red_add_vec<VEC>(o, v);
+      return;
+    }
+    float w[VEC];
+#pragma unroll
+    for (int i = 0; i < VEC; ++i) w[i] = v[i];
+    if (accumulate) {
+#pragma unroll
+      for (int i = 0; i < VEC; ++i) w[i] += o[i];
+    }
+    if constexpr (VEC == 4) *reinterpret_cast<float4*>(o) = make_float4(w[0], w[1], w[2], w[3]);
+    else if constexpr (VEC == 2) *reinterpret_cast<float2*>(o) = make_float2(w[0], w[1]);
+    else
+#pragma unroll
+      for (int i = 0; i < VEC; ++i) o[i] = w[i];
+  }
 };
 struct PeerPush {
   float* const* peers;
@@ -73,6 +108,10 @@ struct PeerPush {
   int F;
   __device__ __forceinline__ void put(int64_t row, int f, float v, bool /*whole*/) const {
     atomicAdd(peers[owner[row]] + static_cast<int64_t>(lrow[row]) * F + f, v);
+  }
+  template <int VEC>
+  __device__ __forceinline__ void put_vec(int64_t row, int f, const float (&v)[VEC], bool /*whole*/) const {
+    red_add_vec<VEC>(peers[owner[row]] + static_cast<int64_t>(lrow[row]) * F + f, v);
   }
 };
 
@@ -177,8 +216,7 @@ __global__ void __launch_bounds__(256, 3) spmm_chunked_kernel(const int64_t* __r
         while (s0 >= re) {
           if (have && active) {
             const bool whole = rs >= E0 && re <= E1;
-#pragma unroll
-            for (int v = 0; v < VEC; ++v) out.put(row, f0 + v, acc[v], whole);
+            out.template put_vec<VEC>(row, f0, acc, whole);
           }
 #pragma unroll
           for (int v = 0; v < VEC; ++v) acc[v] = 0.f;
@@ -223,8 +261,7 @@ __global__ void __launch_bounds__(256, 3) spmm_chunked_kernel(const int64_t* __r
             if ((ends >> u) & 1u) {  // row `row` ends at this edge (warp-uniform)
               if (active) {
                 const bool whole = rs >= E0;  // its end s0 + u + 1 is inside the range
-#pragma unroll
-                for (int v = 0; v < VEC; ++v) out.put(row, f0 + v, acc[v], whole);
+                out.template put_vec<VEC>(row, f0, acc, whole);
               }
 #pragma unroll
               for (int v = 0; v < VEC; ++v) acc[v] = 0.f;
@@ -245,8 +282,7 @@ __global__ void __launch_bounds__(256, 3) spmm_chunked_kernel(const int64_t* __r
           while (e >= re) {  // the stream left row `row` (warp-uniform)
             if (have && active) {
               const bool whole = rs >= E0 && re <= E1;
-#pragma unroll
-              for (int v = 0; v < VEC; ++v) out.put(row, f0 + v, acc[v], whole);
+              out.template put_vec<VEC>(row, f0, acc, whole);
             }
 #pragma unroll
             for (int v = 0; v < VEC; ++v) acc[v] = 0.f;
@@ -268,8 +304,7 @@ __global__ void __launch_bounds__(256, 3) spmm_chunked_kernel(const int64_t* __r
     }
     if (have && active) {
       const bool whole = rs >= E0 && re <= E1;
-#pragma unroll
-      for (int v = 0; v < VEC; ++v) out.put(row, f0 + v, acc[v], whole);
+      out.template put_vec<VEC>(row, f0, acc, whole);
     }
   }
 }

@@ -437,20 +437,12 @@ __global__ void tgn_attn_bwd_kernel(const float* __restrict__ Q, const float* __
 
 
 // LayerNorm + ReLU + dropout backward (warp per row).
-__global__ void tgn_out_bwd_kernel(const float* __restrict__ dout, const float* __restrict__ xsave,
-                                   const float* __restrict__ mean, const float* __restrict__ rstd,
-                                   const float* __restrict__ gamma, const int* __restrict__ n_roots, int rmax, int Do,
-                                   float drop, uint64_t seed, const int64_t* __restrict__ step_ctr,
-                                   const int* __restrict__ edge_total, float* __restrict__ dpre,
-                                   float* __restrict__ dgamma, float* __restrict__ dbeta) {
-  const int r = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
-  const int lane = threadIdx.x & 31;
-  if (r >= rmax) return;
+__device__ __forceinline__ void tgn_out_bwd_row(const float* __restrict__ dout, const float* __restrict__ xsave,
+                                                const float* __restrict__ mean, const float* __restrict__ rstd,
+                                                const float* __restrict__ gamma, int r, int lane, int Do, float drop,
+                                                uint64_t seed, const int64_t* __restrict__ step_ctr,
+                                                float* __restrict__ dpre, float* s_red) {
   float* dp = dpre + (int64_t)r * Do;
-  if (r >= *n_roots || *edge_total == 0) {
-    for (int c = lane; c < Do; c += 32) dp[c] = 0.f;
-    return;
-  }
   const uint64_t dseed = seed ^ (static_cast<uint64_t>(*step_ctr) * 0x9E3779B97F4A7C15ull);
   const float mu = mean[r], rs = rstd[r];
   const float* x = xsave + (int64_t)r * Do;
@@ -461,8 +453,8 @@ __global__ void tgn_out_bwd_kernel(const float* __restrict__ dout, const float* 
     const float dxh = dy[c] * gamma[c];
     sa += dxh;
     sb += dxh * xh;
-    atomicAdd(&dgamma[c], dy[c] * xh);
-    atomicAdd(&dbeta[c], dy[c]);
+    atomicAdd(&s_red[c], dy[c] * xh);
+    atomicAdd(&s_red[Do + c], dy[c]);
   }
   sa = warp_sum(sa) / Do;
   sb = warp_sum(sb) / Do;
@@ -477,20 +469,44 @@ __global__ void tgn_out_bwd_kernel(const float* __restrict__ dout, const float* 
   }
 }
 
+__global__ void tgn_out_bwd_kernel(const float* __restrict__ dout, const float* __restrict__ xsave,
+                                   const float* __restrict__ mean, const float* __restrict__ rstd,
+                                   const float* __restrict__ gamma, const int* __restrict__ n_roots, int rmax, int Do,
+                                   float drop, uint64_t seed, const int64_t* __restrict__ step_ctr,
+                                   const int* __restrict__ edge_total, float* __restrict__ dpre,
+                                   float* __restrict__ dgamma, float* __restrict__ dbeta) {
+  // dgamma / dbeta: summed over the block's rows in shared memory, then one global
+  // atomic per column and block (every row adds to the same Do addresses)
+  extern __shared__ float s_red[];  // [2 * Do]
+  for (int c = threadIdx.x; c < 2 * Do; c += blockDim.x) s_red[c] = 0.f;
+  __syncthreads();
+  const int r = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  bool act = r < rmax;
+  if (act && (r >= *n_roots || *edge_total == 0)) {
+    float* dp = dpre + (int64_t)r * Do;
+    for (int c = lane; c < Do; c += 32) dp[c] = 0.f;
+    act = false;
+  }
+  if (act) tgn_out_bwd_row(dout, xsave, mean, rstd, gamma, r, lane, Do, drop, seed, step_ctr, dpre, s_red);
+  __syncthreads();
+  for (int c = threadIdx.x; c < Do; c += blockDim.x) {
+    if (s_red[c] != 0.f) atomicAdd(&dgamma[c], s_red[c]);
+    if (s_red[Do + c] != 0.f) atomicAdd(&dbeta[c], s_red[Do + c]);
+  }
+}
+
 // ---------------------------------------------------------------------------
 // link predictor scoring + BCE loss + gradients (warp per event)
 // P: [rmax, 2D] per-root projections (src_fc | dst_fc incl. bias)
 // ---------------------------------------------------------------------------
-__global__ void tgn_link_kernel(const float* __restrict__ P, const int* __restrict__ src_idx,
-                                const int* __restrict__ dst_idx, const int* __restrict__ neg_idx,
-                                const int* __restrict__ n_ev, int bmax, int D, const float* __restrict__ b_dst,
-                                const float* __restrict__ w_out, const float* __restrict__ b_out, int need_grad,
-                                float* __restrict__ scores, float* __restrict__ loss, float* __restrict__ dP,
-                                float* __restrict__ g_w_out, float* __restrict__ g_b_out, float* __restrict__ g_b_dst) {
-  const int i = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
-  const int lane = threadIdx.x & 31;
-  const int n = *n_ev;
-  if (i >= bmax || i >= n) return;
+__device__ __forceinline__ void tgn_link_event(const float* __restrict__ P, const int* __restrict__ src_idx,
+                                               const int* __restrict__ dst_idx, const int* __restrict__ neg_idx,
+                                               int n, int i, int lane, int bmax, int D,
+                                               const float* __restrict__ b_dst, const float* __restrict__ w_out,
+                                               const float* __restrict__ b_out, int need_grad,
+                                               float* __restrict__ scores, float* __restrict__ loss,
+                                               float* __restrict__ dP, float* s_red) {
   const int si = src_idx[i], di = dst_idx[i], ni = neg_idx[i];
   const float* ps = P + (int64_t)si * 2 * D;
   const float* pd = P + (int64_t)di * 2 * D + D;
@@ -521,15 +537,44 @@ __global__ void tgn_link_kernel(const float* __restrict__ P, const int* __restri
   for (int d = lane; d < D; d += 32) {
     const float a = ps[d] + pd[d];
     const float bneg = ps[d] + (pn ? pn[d] : b_dst[d]);
-    atomicAdd(&g_w_out[d], dpos * fmaxf(a, 0.f) + dneg * fmaxf(bneg, 0.f));
+    atomicAdd(&s_red[d], dpos * fmaxf(a, 0.f) + dneg * fmaxf(bneg, 0.f));
     const float da = a > 0.f ? dpos * w_out[d] : 0.f;
     const float db = bneg > 0.f ? dneg * w_out[d] : 0.f;
     atomicAdd(&dps[d], da + db);
     atomicAdd(&dpd[d], da);
     if (dpn) atomicAdd(&dpn[d], db);
-    else atomicAdd(&g_b_dst[d], db);
+    else atomicAdd(&s_red[D + d], db);
   }
-  if (lane == 0) atomicAdd(g_b_out, dpos + dneg);
+  if (lane == 0) atomicAdd(&s_red[2 * D], dpos + dneg);
+}
+
+__global__ void tgn_link_kernel(const float* __restrict__ P, const int* __restrict__ src_idx,
+                                const int* __restrict__ dst_idx, const int* __restrict__ neg_idx,
+                                const int* __restrict__ n_ev, int bmax, int D, const float* __restrict__ b_dst,
+                                const float* __restrict__ w_out, const float* __restrict__ b_out, int need_grad,
+                                float* __restrict__ scores, float* __restrict__ loss, float* __restrict__ dP,
+                                float* __restrict__ g_w_out, float* __restrict__ g_b_out, float* __restrict__ g_b_dst) {
+  // g_w_out, g_b_dst, g_b_out: summed over the block's events in shared memory, then
+  // one global atomic per entry and block (every event adds to the same addresses)
+  extern __shared__ float s_red[];  // [2 * D + 1] when need_grad
+  if (need_grad) {
+    for (int c = threadIdx.x; c < 2 * D + 1; c += blockDim.x) s_red[c] = 0.f;
+    __syncthreads();
+  }
+  const int i = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  const int n = *n_ev;
+  if (i < bmax && i < n) tgn_link_event(P, src_idx, dst_idx, neg_idx, n, i, lane, bmax, D, b_dst, w_out, b_out,
+                                        need_grad, scores, loss, dP, s_red);
+  if (!need_grad) return;  // kernel-uniform
+  __syncthreads();
+  for (int c = threadIdx.x; c < 2 * D + 1; c += blockDim.x) {
+    const float v = s_red[c];
+    if (v == 0.f) continue;
+    if (c < D) atomicAdd(&g_w_out[c], v);
+    else if (c < 2 * D) atomicAdd(&g_b_dst[c - D], v);
+    else atomicAdd(g_b_out, v);
+  }
 }
 
 // AP (sklearn semantics), ROC-AUC (ties count 1/2) and the pairwise "mrr" of the reference.
@@ -627,7 +672,7 @@ void launch_tgn_out_bwd(dim3 grid, dim3 block, cudaStream_t st, const float* __r
                                    const int* __restrict__ edge_total, float* __restrict__ dpre,
                                    float* __restrict__ dgamma, float* __restrict__ dbeta) {
   count_launch();
-  tgn_out_bwd_kernel<<<grid, block, 0, st>>>(dout, xsave, mean, rstd, gamma, n_roots, rmax, Do, drop, seed, step_ctr, edge_total, dpre, dgamma, dbeta);
+  tgn_out_bwd_kernel<<<grid, block, 2 * Do * sizeof(float), st>>>(dout, xsave, mean, rstd, gamma, n_roots, rmax, Do, drop, seed, step_ctr, edge_total, dpre, dgamma, dbeta);
 }
 
 void launch_tgn_link(dim3 grid, dim3 block, cudaStream_t st, const float* __restrict__ P, const int* __restrict__ src_idx,
@@ -637,7 +682,7 @@ void launch_tgn_link(dim3 grid, dim3 block, cudaStream_t st, const float* __rest
                                 float* __restrict__ scores, float* __restrict__ loss, float* __restrict__ dP,
                                 float* __restrict__ g_w_out, float* __restrict__ g_b_out, float* __restrict__ g_b_dst) {
   count_launch();
-  tgn_link_kernel<<<grid, block, 0, st>>>(P, src_idx, dst_idx, neg_idx, n_ev, bmax, D, b_dst, w_out, b_out, need_grad, scores, loss, dP, g_w_out, g_b_out, g_b_dst);
+  tgn_link_kernel<<<grid, block, need_grad ? (2 * D + 1) * sizeof(float) : 0, st>>>(P, src_idx, dst_idx, neg_idx, n_ev, bmax, D, b_dst, w_out, b_out, need_grad, scores, loss, dP, g_w_out, g_b_out, g_b_dst);
 }
 
 void launch_tgn_metrics(dim3 grid, dim3 block, cudaStream_t st, const float* __restrict__ scores,
