@@ -556,24 +556,23 @@ __global__ void tgn_link_kernel(const float* __restrict__ P, const int* __restri
                                 float* __restrict__ g_w_out, float* __restrict__ g_b_out, float* __restrict__ g_b_dst) {
   // g_w_out, g_b_dst, g_b_out: summed over the block's events in shared memory, then
   // one global atomic per entry and block (every event adds to the same addresses)
-  extern __shared__ float s_red[];  // [2 * D + 1] when need_grad
-  if (need_grad) {
-    for (int c = threadIdx.x; c < 2 * D + 1; c += blockDim.x) s_red[c] = 0.f;
-    __syncthreads();
-  }
+  // and the loss: [g_w_out (D) | g_b_dst (D) | g_b_out | loss]
+  extern __shared__ float s_red[];  // [2 * D + 2]
+  for (int c = threadIdx.x; c < 2 * D + 2; c += blockDim.x) s_red[c] = 0.f;
+  __syncthreads();
   const int i = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
   const int n = *n_ev;
   if (i < bmax && i < n) tgn_link_event(P, src_idx, dst_idx, neg_idx, n, i, lane, bmax, D, b_dst, w_out, b_out,
-                                        need_grad, scores, loss, dP, s_red);
-  if (!need_grad) return;  // kernel-uniform
+                                        need_grad, scores, s_red + 2 * D + 1, dP, s_red);
   __syncthreads();
-  for (int c = threadIdx.x; c < 2 * D + 1; c += blockDim.x) {
+  for (int c = threadIdx.x; c < 2 * D + 2; c += blockDim.x) {
     const float v = s_red[c];
     if (v == 0.f) continue;
     if (c < D) atomicAdd(&g_w_out[c], v);
     else if (c < 2 * D) atomicAdd(&g_b_dst[c - D], v);
-    else atomicAdd(g_b_out, v);
+    else if (c == 2 * D) atomicAdd(g_b_out, v);
+    else atomicAdd(loss, v);
   }
 }
 
@@ -682,7 +681,7 @@ void launch_tgn_link(dim3 grid, dim3 block, cudaStream_t st, const float* __rest
                                 float* __restrict__ scores, float* __restrict__ loss, float* __restrict__ dP,
                                 float* __restrict__ g_w_out, float* __restrict__ g_b_out, float* __restrict__ g_b_dst) {
   count_launch();
-  tgn_link_kernel<<<grid, block, need_grad ? (2 * D + 1) * sizeof(float) : 0, st>>>(P, src_idx, dst_idx, neg_idx, n_ev, bmax, D, b_dst, w_out, b_out, need_grad, scores, loss, dP, g_w_out, g_b_out, g_b_dst);
+  tgn_link_kernel<<<grid, block, (2 * D + 2) * sizeof(float), st>>>(P, src_idx, dst_idx, neg_idx, n_ev, bmax, D, b_dst, w_out, b_out, need_grad, scores, loss, dP, g_w_out, g_b_out, g_b_dst);
 }
 
 void launch_tgn_metrics(dim3 grid, dim3 block, cudaStream_t st, const float* __restrict__ scores,
