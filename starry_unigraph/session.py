@@ -374,10 +374,16 @@ class SchedulerSession:
             extra = None
             if exact_resume:
                 mb = self.ctdg_session.online_runtime.memory
+                rng = {"torch": torch.get_rng_state()}
+                if torch.cuda.is_available():
+                    rng["cuda"] = torch.cuda.get_rng_state_all()
+                engine = getattr(self.ctdg_session.online_runtime, "engine", None)
+                if engine is not None and hasattr(engine, "step_ctr"):
+                    rng["engine_step"] = engine.step_ctr.detach().cpu()  # dropout streams are keyed on it
                 extra = {"memory_bank": {n: getattr(mb, n).cpu() for n in
                                          ("memory", "memory_ts", "mailbox", "mailbox_ts", "next_mail_pos")},
-                         "optimizer": self.runtime.optimizer.state_dict(), "epoch": self.current_epoch,
-                         "global_step": self.global_step}
+                         "optimizer": self.runtime.optimizer.state_dict(), "rng": rng,
+                         "epoch": self.current_epoch, "global_step": self.global_step}
             self.ctdg_session.save_checkpoint(path, extra)
             return path
         model = self.runtime.model.module if hasattr(self.runtime.model, "module") else self.runtime.model
@@ -395,6 +401,18 @@ class SchedulerSession:
             ckpt = self.ctdg_session.load_checkpoint(path)
             self.current_epoch = int(ckpt.get("epoch", self.current_epoch))
             self.global_step = int(ckpt.get("global_step", self.global_step))
+            # exact-resume keys (absent from reference checkpoints): optimizer moments, RNG streams
+            if isinstance(ckpt.get("optimizer"), dict) and self.runtime.optimizer is not None:
+                self.runtime.optimizer.load_state_dict(ckpt["optimizer"])
+            rng = ckpt.get("rng")
+            if isinstance(rng, dict):
+                if "torch" in rng:
+                    torch.set_rng_state(rng["torch"])
+                if "cuda" in rng and torch.cuda.is_available():
+                    torch.cuda.set_rng_state_all(rng["cuda"])
+                engine = getattr(self.ctdg_session.online_runtime, "engine", None)
+                if "engine_step" in rng and engine is not None and hasattr(engine, "step_ctr"):
+                    engine.step_ctr.copy_(rng["engine_step"])
             return ckpt
         payload = load_checkpoint(path)
         state = payload.get("model_state")

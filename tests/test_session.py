@@ -87,9 +87,20 @@ def test_ctdg_checkpoint_roundtrip(tmp_path):
     s2.prepared = None
     s2.ctx.artifact_root = s.ctx.artifact_root
     s2.build_runtime()
+    torch.manual_seed(12345)  # a different RNG position than at save time
     s2.load_checkpoint(path)
     for a, b in zip(s.runtime.model.state_dict().values(), s2.runtime.model.state_dict().values()):
         assert torch.equal(a, b)
+    # exact resume: memory bank, optimizer moments, RNG stream and counters come back
+    for n in ("memory", "memory_ts", "mailbox", "mailbox_ts"):
+        assert torch.equal(getattr(s.ctdg_session.online_runtime.memory, n).cpu(),
+                           getattr(s2.ctdg_session.online_runtime.memory, n).cpu())
+    st1, st2 = s.runtime.optimizer.state_dict()["state"], s2.runtime.optimizer.state_dict()["state"]
+    assert st1.keys() == st2.keys() and len(st1) > 0
+    for k in st1:
+        assert torch.equal(st1[k]["exp_avg"], st2[k]["exp_avg"])
+    assert torch.equal(torch.get_rng_state(), ck["rng"]["torch"])
+    assert s2.global_step == s.global_step and s2.current_epoch == s.current_epoch
 
 
 def test_dtdg_checkpoint_roundtrip(tmp_path):
