@@ -232,8 +232,10 @@ class CTDGMemoryBank:
         ids = node_ids.to(self._storage_device).long()
         remote = self.owner[ids] != ctx.rank
         ids = ids[remote]
-        payload = torch.cat([mail_slots.detach().float()[remote].reshape(ids.numel(), -1),
-                             mail_ts.detach().float()[remote].reshape(ids.numel(), -1)], dim=1)
+        def rows(t: torch.Tensor) -> torch.Tensor:  # [n, ...] -> [n, width], also for n == 0
+            return t.flatten(1) if t.dim() > 1 else t.unsqueeze(1)
+
+        payload = torch.cat([rows(mail_slots.detach().float()[remote]), rows(mail_ts.detach().float()[remote])], dim=1)
         self._exchange(ctx, ids, payload, "mail")
 
     def wait_pending_syncs(self) -> None:
@@ -279,7 +281,7 @@ class CTDGMemoryBank:
         dist.all_to_all_single(req, ids, rc, sc)
         K, SW, D = self.mailbox_slots, self.slot_width, self.hidden_dim
         rq = req.to(self._storage_device)
-        rows = torch.cat([self.memory[rq], self.memory_ts[rq].unsqueeze(1), self.mailbox[rq].reshape(rq.numel(), -1),
+        rows = torch.cat([self.memory[rq], self.memory_ts[rq].unsqueeze(1), self.mailbox[rq].flatten(1),
                           self.mailbox_ts[rq], self.next_mail_pos[rq].float().unsqueeze(1)], dim=1).to(dev)
         width = rows.size(1) if rows.dim() == 2 and rows.numel() else D + 1 + K * SW + K + 1
         ans = torch.empty(sum(sc), width, dtype=torch.float32, device=dev)

@@ -1,6 +1,6 @@
-"""Two-rank runs on CPU (gloo) through the public session API: DTDG halo
-exchange and data-parallel gradients, CTDG memory partitioning, and failure
-detection on the host (a rank that exits between steps)."""
+"""Multi-rank runs on CPU (gloo) through the public session API: DTDG halo
+exchange and data-parallel gradients, CTDG memory partitioning (two and four
+ranks), and failure detection on the host (a rank that exits between steps)."""
 import json
 import os
 import socket
@@ -20,13 +20,13 @@ def _port() -> int:
         return s.getsockname()[1]
 
 
-def _launch(out, family, extra_env=None, *args, wall=240):
+def _launch(out, family, extra_env=None, *args, wall=240, nproc=2):
     env = dict(os.environ)
     env.pop("CUDA_VISIBLE_DEVICES", None)
     env.update(extra_env or {})
     for attempt in range(3):  # a port picked free can be taken before the rendezvous binds it
         cmd = ["timeout", "-k", "10", str(wall), sys.executable, "-m", "torch.distributed.run", "--nnodes=1",
-               "--nproc-per-node=2", "--master-addr", "127.0.0.1", "--master-port", str(_port()), str(WORKER),
+               f"--nproc-per-node={nproc}", "--master-addr", "127.0.0.1", "--master-port", str(_port()), str(WORKER),
                "--family", family, "--out", str(out), *args]
         res = subprocess.run(cmd, cwd=ROOT, env=env, capture_output=True, text=True, timeout=wall + 30)
         text = res.stdout + res.stderr
@@ -59,6 +59,24 @@ def test_ctdg_two_ranks_memory_partition(tmp_path):
     p0, p1 = torch.load(tmp_path / "r0.pt"), torch.load(tmp_path / "r1.pt")
     for a, b in zip(p0["params"], p1["params"]):
         assert torch.allclose(a, b, atol=1e-6)
+
+
+def test_four_ranks_dtdg_and_ctdg(tmp_path):
+    """W = 4: every rank finishes the same number of steps with identical
+    replicas (one all-reduced gradient per step), for the DTDG halo pipeline and
+    the CTDG memory partition."""
+    for family in ("mpnn_lstm", "tgn"):
+        out = tmp_path / family
+        out.mkdir()
+        res = _launch(out, family, nproc=4, wall=400)
+        assert res.returncode == 0, res.stdout[-2000:] + res.stderr[-4000:]
+        outs = [_outcome(out, r) for r in range(4)]
+        assert all(o["error"] is None for o in outs)
+        assert len({o["steps"] for o in outs}) == 1 and outs[0]["steps"] > 0
+        ps = [torch.load(out / f"r{r}.pt") for r in range(4)]
+        for r in range(1, 4):
+            for a, b in zip(ps[0]["params"], ps[r]["params"]):
+                assert torch.allclose(a, b, atol=1e-6)
 
 
 def test_rank_exit_between_steps_is_detected(tmp_path):
