@@ -159,7 +159,9 @@ def _loss_and_predictions(runtime: RuntimeBundle, blob_or_batch, training: bool,
     if pred.size(-1) != labels.size(-1):
         labels = labels[..., : pred.size(-1)]
     scale = float(runtime.state.get("part_loss_scale", 1.0))
-    if runtime.state.get("task") == "node_classification":
+    if labels.numel() == 0:  # no labelled row of this partition in the snapshot: zero loss, zero gradients
+        loss = pred.sum() * 0.0
+    elif runtime.state.get("task") == "node_classification":
         if pred.size(-1) == 1:
             loss = F.binary_cross_entropy_with_logits(pred, labels.float()) * scale
         else:
