@@ -1,0 +1,77 @@
+"""Host-side logic of the NVLink halo path, checked on CPU: the pull plan of a
+partitioned snapshot block (which source rows are pulled from other ranks, and
+the aggregation columns remapped to [local rows | pulled rows]) must give the
+same aggregation as indexing every source row by its global id; and the
+in-place weight-gradient routing of the DTDG autograd ops."""
+import torch
+
+from starry_unigraph.data.partition import NID, SnapshotBlock
+from starry_unigraph.parallel.halo import PeerHaloContext
+
+
+def _plan_ctx(node_parts: torch.Tensor, rank: int) -> PeerHaloContext:
+    # the plan needs only the ownership maps, not the symmetric buffers
+    hc = PeerHaloContext.__new__(PeerHaloContext)
+    hc.device = torch.device("cpu")
+    hc.rank, hc.world = rank, int(node_parts.max()) + 1
+    local_index = torch.empty_like(node_parts)
+    for q in range(hc.world):
+        ids = torch.nonzero(node_parts == q).view(-1)
+        local_index[ids] = torch.arange(ids.numel())
+    hc.owner = node_parts.int()
+    hc.local_index = local_index.int()
+    return hc
+
+
+def test_pull_plan_matches_global_indexing():
+    g = torch.Generator().manual_seed(3)
+    n, F, world = 300, 6, 3
+    parts = torch.randint(0, world, (n,), generator=g)
+    x_global = torch.randn(n, F, generator=g)
+    for rank in range(world):
+        hc = _plan_ctx(parts, rank)
+        mine = torch.nonzero(parts == rank).view(-1)
+        # block: destination rows = this rank's nodes; sources = its nodes plus some
+        # other ranks' nodes, in an arbitrary order (the plan must not rely on one)
+        others = torch.nonzero(parts != rank).view(-1)
+        halo = others[torch.randperm(others.numel(), generator=g)[:40]]
+        src_nodes = torch.cat([halo[:20], mine, halo[20:]])
+        m = 500
+        edge_src = torch.randint(0, src_nodes.numel(), (m,), generator=g)
+        edge_dst = torch.randint(0, mine.numel(), (m,), generator=g)
+        block = SnapshotBlock(num_src_nodes=int(src_nodes.numel()), num_dst_nodes=int(mine.numel()),
+                              edge_src=edge_src, edge_dst=edge_dst, srcdata={NID: src_nodes},
+                              edata={"gcn_norm": torch.rand(m, generator=g)})
+        x_local = x_global[mine]
+        halo_src, col = hc.pull_plan(block, int(mine.numel()))
+        owner, row = hc.src_maps(block)
+        assert (owner[halo_src.long()] != rank).all()
+        assert int((owner != rank).sum()) == halo_src.numel()
+        # what the pull kernel gathers: row `row[c]` of owner[c]'s layer input
+        pulled = torch.stack([x_global[parts == owner[c]][row[c]] for c in halo_src.tolist()]) \
+            if halo_src.numel() else torch.zeros(0, F)
+        table = torch.cat([x_local, pulled])
+        csr = block.csr()
+        dst_of_edge = torch.repeat_interleave(torch.arange(block.num_dst_nodes), csr["rowptr"].diff())
+        got = torch.zeros(block.num_dst_nodes, F).index_add_(0, dst_of_edge,
+                                                             table[col.long()] * csr["val"][:, None])
+        ref = torch.zeros(block.num_dst_nodes, F).index_add_(
+            0, dst_of_edge, x_global[src_nodes[csr["col"].long()]] * csr["val"][:, None])
+        torch.testing.assert_close(got, ref)
+        # cached on the block for the next call
+        assert hc.pull_plan(block, int(mine.numel()))[1] is col
+
+
+def test_weight_gradients_go_to_existing_grad_in_place():
+    from starry_unigraph.ops.dtdg import _grad_sink, _wgrad_buffers
+
+    w = torch.nn.Parameter(torch.randn(4, 3))
+    b = torch.nn.Parameter(torch.randn(4))
+    fresh = _wgrad_buffers([w], [b])
+    assert all(buf is ret for buf, ret in fresh)           # no .grad yet: fresh buffers are returned
+    w.grad = torch.zeros_like(w)
+    b.grad = torch.zeros_like(b)
+    sink = _wgrad_buffers([w], [b])
+    assert sink[0][0] is w.grad and sink[1][0] is b.grad    # kernels add into .grad ...
+    assert sink[0][1] is None and sink[1][1] is None        # ... and autograd gets None
+    assert _grad_sink(w.detach() * 2) is None               # computed weights get a returned gradient
