@@ -134,6 +134,18 @@ class _HaloAggregate(autograd.Function):
         return gx, None, None
 
 
+def halo_width(model, default: int) -> int:
+    """Feature width of the aggregations that exchange halo rows: the inputs of a
+    GCN stack's second and later layers (its hidden width; the first layer
+    aggregates the block's stored source features and exchanges nothing). T-GCN's
+    stack is 3 x hidden wide, MPNN-LSTM's hidden."""
+    from starry_unigraph.runtime.modules.gcn_layers import GCNStack
+
+    widths = [int(m.layers[0].weight.shape[0]) for m in model.modules()
+              if isinstance(m, GCNStack) and len(m.layers) > 1]
+    return max(widths) if widths else int(default)
+
+
 _CONTEXT: dict[str, PeerHaloContext | None] = {"ctx": None}
 
 

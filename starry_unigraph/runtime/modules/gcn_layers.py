@@ -39,7 +39,8 @@ def _gcn_message_pass(graph, x: torch.Tensor) -> torch.Tensor:
         if route is not None and route.send_index is not None and dist.is_available() and dist.is_initialized():
             from starry_unigraph.parallel.halo import get_halo_context, halo_aggregate
 
-            if x.is_cuda and get_halo_context() is not None:  # halo read from peers inside the aggregation
+            hc = get_halo_context()
+            if x.is_cuda and hc is not None and x.size(-1) == hc.F:  # halo rows pulled from the peers
                 return halo_aggregate(graph, x)
             src_x = route.forward(x)
         else:

@@ -172,7 +172,7 @@ class SchedulerSession:
     def _maybe_peer_halo(self, device: str) -> None:
         """Multi-GPU DTDG with ``comm.path: p2p``: halo rows are read from peer memory
         inside the aggregation kernel (starry_unigraph.parallel.halo)."""
-        from starry_unigraph.parallel.halo import PeerHaloContext, set_halo_context
+        from starry_unigraph.parallel.halo import PeerHaloContext, halo_width, set_halo_context
 
         set_halo_context(None)
         if not (self.ctx.dist.is_distributed and dist.is_initialized() and str(device).startswith("cuda")):
@@ -188,7 +188,8 @@ class SchedulerSession:
         if not path.exists():
             return
         node_parts = torch.load(path, weights_only=True)
-        hc = PeerHaloContext(node_parts, int(self.ctx.config["model"]["hidden_dim"]), torch.device(device))
+        width = halo_width(self.runtime.model, int(self.ctx.config["model"]["hidden_dim"]))
+        hc = PeerHaloContext(node_parts, width, torch.device(device))
         set_halo_context(hc)
         self.runtime.state["halo"] = {"transport": "nvlink_p2p", "world": hc.world, "features": hc.F}
 

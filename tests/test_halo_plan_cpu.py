@@ -75,3 +75,13 @@ def test_weight_gradients_go_to_existing_grad_in_place():
     assert sink[0][0] is w.grad and sink[1][0] is b.grad    # kernels add into .grad ...
     assert sink[0][1] is None and sink[1][1] is None        # ... and autograd gets None
     assert _grad_sink(w.detach() * 2) is None               # computed weights get a returned gradient
+
+
+def test_halo_width_of_the_flare_models():
+    from starry_unigraph.backends.dtdg.runtime.models import build_flare_model
+    from starry_unigraph.parallel.halo import halo_width
+
+    assert halo_width(build_flare_model("tgcn", 128, 128, 2), 128) == 384      # GCN stack of 3 x hidden
+    assert halo_width(build_flare_model("mpnn_lstm", 64, 64, 1), 64) == 64
+    assert halo_width(build_flare_model("evolvegcn", 128, 128, 2), 128) == 128  # no stack: the default
+
