@@ -84,6 +84,20 @@ def test_many_ranks_dtdg_and_ctdg(tmp_path, world):
                 assert torch.allclose(a, b, atol=1e-6)
 
 
+@pytest.mark.parametrize("family", ["tgcn", "evolvegcn"])
+def test_two_ranks_tgcn_evolvegcn(tmp_path, family):
+    """The other Flare models over two partitions (T-GCN exchanges halo rows of
+    its 3 x hidden wide GCN layer; EvolveGCN evolves replicated weights)."""
+    res = _launch(tmp_path, family)
+    assert res.returncode == 0, res.stdout[-2000:] + res.stderr[-4000:]
+    o0, o1 = _outcome(tmp_path, 0), _outcome(tmp_path, 1)
+    assert o0["error"] is None and o1["error"] is None and o0["steps"] == o1["steps"] > 0
+    assert math.isfinite(o0["loss"])
+    p0, p1 = torch.load(tmp_path / "r0.pt"), torch.load(tmp_path / "r1.pt")
+    for a, b in zip(p0["params"], p1["params"]):
+        assert torch.allclose(a, b, atol=1e-6)
+
+
 def test_rank_exit_between_steps_is_detected(tmp_path):
     """Rank 1 exits before step 2; rank 0 must stop with an error (heartbeat or
     collective timeout) instead of waiting forever."""
