@@ -84,10 +84,11 @@ def test_many_ranks_dtdg_and_ctdg(tmp_path, world):
                 assert torch.allclose(a, b, atol=1e-6)
 
 
-@pytest.mark.parametrize("family", ["tgcn", "evolvegcn"])
-def test_two_ranks_tgcn_evolvegcn(tmp_path, family):
-    """The other Flare models over two partitions (T-GCN exchanges halo rows of
-    its 3 x hidden wide GCN layer; EvolveGCN evolves replicated weights)."""
+@pytest.mark.parametrize("family", ["tgcn", "evolvegcn", "jodie"])
+def test_two_ranks_other_models(tmp_path, family):
+    """The other models over two ranks: T-GCN (exchanges halo rows of its
+    3 x hidden wide GCN layer), EvolveGCN (evolves replicated weights), JODIE
+    (memory partitioned by owner, time-projection embedding)."""
     res = _launch(tmp_path, family)
     assert res.returncode == 0, res.stdout[-2000:] + res.stderr[-4000:]
     o0, o1 = _outcome(tmp_path, 0), _outcome(tmp_path, 1)
