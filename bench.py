@@ -221,8 +221,10 @@ def _mpnn_main(args):
     launches0 = cuda_ext().launch_count()  # host-side count of this library's kernel launches
     with ClockSampler(local_rank) as clocks:
         start.record()
+        h0 = time.perf_counter()
         for b in timed:
             run_flare_train_step(rt, b, {"meta": {}}, need_host=False)
+        host_issue_s = time.perf_counter() - h0  # host time to issue the steps (no sync inside)
         end.record()
         torch.cuda.synchronize()
     launches = cuda_ext().launch_count() - launches0
@@ -256,6 +258,7 @@ def _mpnn_main(args):
                        "edges_per_snapshot": edges, "window": window, "full_config_shape": full,
                        "l2": "window graphs' CSR + features exceed the 126 MB L2", "baseline_metric": METRIC},
             "clocks": clocks.summary(), "gpu_launches": launches,
+            "host_issue_ms_per_step": host_issue_s * 1000.0 / args.steps,
             "e2e": {"value": args.steps / e2e_s, "unit": "snapshots/s", "h2d_bytes_per_step": 0,
                     "d2h_bytes_per_step": 4, "note": "snapshots resident on the device (dtdg.resident); "
                     "the loss is read back every step"},

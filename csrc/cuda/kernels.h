@@ -184,9 +184,29 @@ void launch_tgn_peer_mail_claim(cudaStream_t st, const int64_t* roots, const int
                                 unsigned long long* const* claim_tables);
 void launch_tgn_peer_mail_write(cudaStream_t st, const int64_t* roots, const int* n_roots, int rmax, const int* win,
                                 const int* src_idx, const int* dst_idx, const int64_t* ev_eid, const float* ev_ts,
-                                const float* mem_prev, int D, const float* efeat, int efeat_ld, int e_raw, int E,
-                                const int* owner, const unsigned long long* const* claim_tables,
+                                const float* mem_prev, int D, const void* efeat, int efeat_bf16, int efeat_ld,
+                                int e_raw, int E, const int* owner, const unsigned long long* const* claim_tables,
                                 float* const* mail_tables, float* const* mail_ts_tables);
+// split end-of-step barrier: signal now, wait (fused with the next step's claims) later
+void launch_peer_signal(cudaStream_t st, uint64_t* const* flag_ptrs, int rank, int W, int64_t* epoch);
+void launch_peer_wait(cudaStream_t st, const uint64_t* my_flags, int rank, int W, const int64_t* epoch, int* status,
+                      long long budget);
+void launch_tgn_peer_wait_claim(cudaStream_t st, const uint64_t* my_flags, int rank, int W, const int64_t* epoch,
+                                int* status, long long budget, const int64_t* roots, const int* n_roots, int rmax,
+                                const int* win, const int64_t* ev_eid, const float* ev_ts, const int* owner,
+                                unsigned long long* const* claim_tables);
+// memory write-back + mailbox write of the claim winners (mail_tables == nullptr: memory only)
+void launch_tgn_peer_push(cudaStream_t st, int blocks, const int64_t* roots, const int* n_roots, int rmax,
+                          const float* mem_new, const float* ts_max, float* const* mem_tables,
+                          float* const* ts_tables, const HistCache& hc, const int* win, const int* src_idx,
+                          const int* dst_idx, const int64_t* ev_eid, const float* ev_ts, const float* mem_prev, int D,
+                          const void* efeat, int efeat_bf16, int efeat_ld, int e_raw, int E, const int* owner,
+                          const unsigned long long* const* claim_tables, float* const* mail_tables,
+                          float* const* mail_ts_tables);
+// reduce-scatter + Adam on this rank's shard + all-gather of the new parameters
+void launch_peer_rs_adam_ag(cudaStream_t st, int blocks, const float* const* grads, float* const* params, int W,
+                            int rank, float* m, float* v, int64_t n, int64_t* step, unsigned int* done, float lr,
+                            float b1, float b2, float eps, float wd, float scale);
 
 // ---- optimiser ---------------------------------------------------------------
 void launch_adam_flat(cudaStream_t st, int blocks, float* p, const float* g, float* m, float* v, int64_t n,

@@ -7,17 +7,30 @@
 //                      (st.release.sys) and waits until all peers' slots in its
 //                      own array reach the epoch (ld.acquire.sys). The wait is
 //                      bounded: on expiry it records kPeerTimeout and returns.
+//  peer_signal / the wait inside tgn_peer_wait_claim: the same barrier split in
+//                      two halves, so that work placed between them (the next
+//                      step's sampling) overlaps the peers' arrival.
 //  peer_allreduce_adam: gradient all-reduce fused with the Adam update. Every
 //                      rank reads the W gradient buffers, sums them in rank
 //                      order (bit-identical sums on all ranks), scales and
 //                      applies Adam to its own parameter copy.
-//  tgn_peer_writeback: new memory rows of this step's roots stored into the
-//                      owner rank's memory table; memory_ts = max over writers.
-//  tgn_peer_mail_claim/write: one mailbox slot per node (mailbox_slots = 1):
-//                      each rank proposes its final mail for each root with the
-//                      key (ts, event id); the key is claimed with a 64-bit
-//                      atomicMax on the owner; after a barrier the winner
-//                      writes the slot into the owner's mailbox.
+//  peer_rs_adam_ag   : the traffic-optimal form: rank r sums only its 1/W shard
+//                      of the gradient over the W buffers (reduce-scatter),
+//                      applies Adam to that shard and stores the new parameter
+//                      shard into every rank's parameter buffer (all-gather):
+//                      2 (W-1)/W of the buffer crosses NVLink per rank instead
+//                      of (W-1) x. Each element is computed by one rank only,
+//                      so the replicas stay bit-identical.
+//  tgn_peer_wait_claim: (after the end-of-step wait) each rank proposes its
+//                      final mail for each root with the key (ts, event id),
+//                      claimed with a 64-bit atomicMax on the owner. Claims are
+//                      posted before the step's barrier, so the winners can
+//                      write right after it without a second barrier.
+//  tgn_peer_push     : per root, the new memory row stored into the owner
+//                      rank's memory table (memory_ts = max over writers; rows
+//                      of one node written by several ranks are identical, they
+//                      come from the same state) and, for the claim winner, the
+//                      mailbox slot.
 //
 // The multi-rank orchestration lives in starry_unigraph/parallel (reference
 // semantics: backends/ctdg/runtime/memory.py:328-553 pushes memory and mail to
@@ -68,6 +81,53 @@ void launch_peer_barrier(cudaStream_t st, uint64_t* const* flag_ptrs, int rank, 
                          long long budget) {
   count_launch();
   peer_barrier_kernel<<<1, 32, 0, st>>>(flag_ptrs, rank, W, epoch, status, budget);
+}
+
+// Split barrier: signal (store the next epoch into this rank's slot of every
+// peer's flag array, no wait) ...
+__global__ void peer_signal_kernel(uint64_t* const* __restrict__ flag_ptrs, int rank, int W,
+                                   int64_t* __restrict__ epoch) {
+  const int p = threadIdx.x;
+  const uint64_t e = static_cast<uint64_t>(*epoch) + 1ull;
+  __threadfence_system();  // this rank's earlier stores to peer memory are visible before the flag
+  if (p < W && p != rank) st_release_sys_u64(flag_ptrs[p] + rank, e);
+  __syncthreads();
+  if (p == 0) *epoch = static_cast<int64_t>(e);
+}
+
+void launch_peer_signal(cudaStream_t st, uint64_t* const* flag_ptrs, int rank, int W, int64_t* epoch) {
+  count_launch();
+  peer_signal_kernel<<<1, 32, 0, st>>>(flag_ptrs, rank, W, epoch);
+}
+
+// ... and, later, wait (bounded) until every peer's slot in this rank's own
+// flag array has reached this rank's current epoch. Called by one warp (lanes
+// = peers); the caller synchronises the block afterwards.
+__device__ __forceinline__ void peer_wait_warp(const uint64_t* __restrict__ my_flags, int rank, int W,
+                                               const int64_t* __restrict__ epoch, int* status, long long budget) {
+  const int p = threadIdx.x & 31;
+  const uint64_t e = static_cast<uint64_t>(*epoch);
+  if (p < W && p != rank) {
+    const long long t0 = clock64();
+    while (ld_acquire_sys_u64(my_flags + p) < e) {
+      if (clock64() - t0 > budget) {
+        record_status(status, kPeerTimeout);
+        break;
+      }
+      __nanosleep(64);
+    }
+  }
+}
+
+__global__ void peer_wait_kernel(const uint64_t* __restrict__ my_flags, int rank, int W,
+                                 const int64_t* __restrict__ epoch, int* status, long long budget) {
+  peer_wait_warp(my_flags, rank, W, epoch, status, budget);
+}
+
+void launch_peer_wait(cudaStream_t st, const uint64_t* my_flags, int rank, int W, const int64_t* epoch, int* status,
+                      long long budget) {
+  count_launch();
+  peer_wait_kernel<<<1, 32, 0, st>>>(my_flags, rank, W, epoch, status, budget);
 }
 
 // ---------------------------------------------------------------------------
@@ -130,6 +190,75 @@ void launch_peer_allreduce_adam(cudaStream_t st, int blocks, const float* const*
 }
 
 // ---------------------------------------------------------------------------
+// reduce-scatter + Adam + all-gather over peer memory
+//
+// Rank r owns float4 elements [r * shard4, (r + 1) * shard4): it sums them over
+// the W gradient buffers in rank order, applies Adam (its moments are kept
+// for its own shard only) and stores the new values into the parameter buffer
+// of every rank, its own included.
+// ---------------------------------------------------------------------------
+__global__ void peer_rs_adam_ag_kernel(const float* const* __restrict__ grads, float* const* __restrict__ params,
+                                       int W, int rank, float* __restrict__ m, float* __restrict__ v, int64_t n4,
+                                       int64_t shard4, int64_t* __restrict__ step, unsigned int* __restrict__ done,
+                                       float lr, float b1, float b2, float eps, float wd, float scale) {
+  const float t = static_cast<float>(*step + 1);
+  const float bc1 = 1.f - powf(b1, t);
+  const float bc2_sqrt = sqrtf(1.f - powf(b2, t));
+  const float step_size = lr / bc1;
+  const int64_t lo = static_cast<int64_t>(rank) * shard4;
+  const int64_t hi = min(n4, lo + shard4);
+  const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+  const float4* mine = reinterpret_cast<const float4*>(params[rank]);
+  for (int64_t i = lo + static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < hi; i += stride) {
+    float4 g = reinterpret_cast<const float4*>(grads[0])[i];
+    for (int q = 1; q < W; ++q) {
+      const float4 h = reinterpret_cast<const float4*>(grads[q])[i];
+      g.x += h.x;
+      g.y += h.y;
+      g.z += h.z;
+      g.w += h.w;
+    }
+    float4 pp = mine[i];
+    float4 mm = reinterpret_cast<float4*>(m)[i];
+    float4 vv = reinterpret_cast<float4*>(v)[i];
+    float* pa = &pp.x;
+    float* ma = &mm.x;
+    float* va = &vv.x;
+    const float* ga = &g.x;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float gr = ga[j] * scale + wd * pa[j];
+      ma[j] = b1 * ma[j] + (1.f - b1) * gr;
+      va[j] = b2 * va[j] + (1.f - b2) * gr * gr;
+      pa[j] -= step_size * ma[j] / (sqrtf(va[j]) / bc2_sqrt + eps);
+    }
+    reinterpret_cast<float4*>(m)[i] = mm;
+    reinterpret_cast<float4*>(v)[i] = vv;
+    for (int q = 0; q < W; ++q) reinterpret_cast<float4*>(params[q])[i] = pp;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence();
+    const unsigned int prev = atomicAdd(done, 1u);
+    if (prev == gridDim.x - 1) {
+      *step += 1;
+      *done = 0u;
+      __threadfence();
+    }
+  }
+}
+
+void launch_peer_rs_adam_ag(cudaStream_t st, int blocks, const float* const* grads, float* const* params, int W,
+                            int rank, float* m, float* v, int64_t n, int64_t* step, unsigned int* done, float lr,
+                            float b1, float b2, float eps, float wd, float scale) {
+  const int64_t n4 = n / 4;  // n is a multiple of 4 (flat buffers are padded)
+  const int64_t shard4 = (n4 + W - 1) / W;
+  count_launch();
+  peer_rs_adam_ag_kernel<<<blocks, 256, 0, st>>>(grads, params, W, rank, m, v, n4, shard4, step, done, lr, b1, b2,
+                                                  eps, wd, scale);
+}
+
+// ---------------------------------------------------------------------------
 // CTDG memory write-back (block of 64 threads per root, D columns)
 //
 // Optional historical-cache filter (reference backends/ctdg/runtime/cache.py:
@@ -138,12 +267,14 @@ void launch_peer_allreduce_adam(cudaStream_t st, int blocks, const float* const*
 // its cosine distance to the cached row exceeds `thresh` (= 1 - alpha). A pushed
 // row refreshes the cache.
 // ---------------------------------------------------------------------------
-__global__ void tgn_peer_writeback_kernel(const int64_t* __restrict__ roots, const int* __restrict__ n_roots, int rmax,
-                                          const float* __restrict__ mem_new, int D, const int* __restrict__ owner,
-                                          float* const* __restrict__ mem_tables, float* const* __restrict__ ts_tables,
-                                          const float* __restrict__ ts_max, HistCache hc) {
-  const int r = blockIdx.x;
-  if (r >= rmax || r >= *n_roots) return;
+// Stores root r's new memory row into the owner's table (unless the historical
+// filter drops it). Block-uniform control flow; blockDim.x is a multiple of 32
+// and at most 256.
+__device__ __forceinline__ void writeback_root(int r, const int64_t* __restrict__ roots,
+                                               const float* __restrict__ mem_new, int D,
+                                               const int* __restrict__ owner, float* const* __restrict__ mem_tables,
+                                               float* const* __restrict__ ts_tables, const float* __restrict__ ts_max,
+                                               const HistCache& hc) {
   const int64_t v = roots[r];
   const int o = owner[v];
   const float* src = mem_new + static_cast<int64_t>(r) * D;
@@ -158,7 +289,7 @@ __global__ void tgn_peer_writeback_kernel(const int64_t* __restrict__ roots, con
         na += a * a;
         nb += b * b;
       }
-      __shared__ float red[3][2];
+      __shared__ float red[3][8];
 #pragma unroll
       for (int off = 16; off > 0; off >>= 1) {
         dot += __shfl_xor_sync(0xffffffffu, dot, off);
@@ -172,9 +303,13 @@ __global__ void tgn_peer_writeback_kernel(const int64_t* __restrict__ roots, con
         red[2][w] = nb;
       }
       __syncthreads();
-      dot = red[0][0] + red[0][1];
-      na = red[1][0] + red[1][1];
-      nb = red[2][0] + red[2][1];
+      dot = na = nb = 0.f;
+      for (int i = 0; i < static_cast<int>(blockDim.x >> 5); ++i) {
+        dot += red[0][i];
+        na += red[1][i];
+        nb += red[2][i];
+      }
+      __syncthreads();  // red is reused by the next root of this block
       const bool never = hc.cache_ts[slot] < 0.f;
       const float cosv = dot / fmaxf(sqrtf(na) * sqrtf(nb), 1e-8f);
       if (!never && 1.f - cosv <= hc.thresh) return;  // block-uniform: skip the push
@@ -193,6 +328,15 @@ __global__ void tgn_peer_writeback_kernel(const int64_t* __restrict__ roots, con
     // timestamps are >= 0, so their bit patterns order like signed ints
     atomicMax(reinterpret_cast<int*>(ts_tables[o] + v), __float_as_int(*ts_max));
   }
+}
+
+__global__ void tgn_peer_writeback_kernel(const int64_t* __restrict__ roots, const int* __restrict__ n_roots, int rmax,
+                                          const float* __restrict__ mem_new, int D, const int* __restrict__ owner,
+                                          float* const* __restrict__ mem_tables, float* const* __restrict__ ts_tables,
+                                          const float* __restrict__ ts_max, HistCache hc) {
+  const int r = blockIdx.x;
+  if (r >= rmax || r >= *n_roots) return;
+  writeback_root(r, roots, mem_new, D, owner, mem_tables, ts_tables, ts_max, hc);
 }
 
 void launch_tgn_peer_writeback(cudaStream_t st, const int64_t* roots, const int* n_roots, int rmax,
@@ -225,12 +369,10 @@ __device__ __forceinline__ unsigned long long mail_key(float ts, int64_t eid) {
          static_cast<unsigned long long>(static_cast<uint32_t>(eid));
 }
 
-__global__ void tgn_peer_mail_claim_kernel(const int64_t* __restrict__ roots, const int* __restrict__ n_roots,
-                                           int rmax, const int* __restrict__ win, const int64_t* __restrict__ ev_eid,
+__device__ __forceinline__ void claim_root(int r, int rmax, const int64_t* __restrict__ roots,
+                                           const int* __restrict__ win, const int64_t* __restrict__ ev_eid,
                                            const float* __restrict__ ev_ts, const int* __restrict__ owner,
                                            unsigned long long* const* __restrict__ claim_tables) {
-  const int r = blockIdx.x * blockDim.x + threadIdx.x;
-  if (r >= rmax || r >= *n_roots) return;
   int pass = 0;
   const int i = final_mail_event(win, rmax, r, pass);
   if (i < 0) return;
@@ -238,17 +380,42 @@ __global__ void tgn_peer_mail_claim_kernel(const int64_t* __restrict__ roots, co
   atomicMax(claim_tables[owner[v]] + v, mail_key(ev_ts[i], ev_eid[i]));
 }
 
-__global__ void tgn_peer_mail_write_kernel(const int64_t* __restrict__ roots, const int* __restrict__ n_roots,
-                                           int rmax, const int* __restrict__ win, const int* __restrict__ src_idx,
-                                           const int* __restrict__ dst_idx, const int64_t* __restrict__ ev_eid,
-                                           const float* __restrict__ ev_ts, const float* __restrict__ mem_prev, int D,
-                                           const float* __restrict__ efeat, int efeat_ld, int e_raw, int E,
-                                           const int* __restrict__ owner,
-                                           const unsigned long long* const* __restrict__ claim_tables,
-                                           float* const* __restrict__ mail_tables,
-                                           float* const* __restrict__ mail_ts_tables) {
-  const int r = blockIdx.x;
+__global__ void tgn_peer_mail_claim_kernel(const int64_t* __restrict__ roots, const int* __restrict__ n_roots,
+                                           int rmax, const int* __restrict__ win, const int64_t* __restrict__ ev_eid,
+                                           const float* __restrict__ ev_ts, const int* __restrict__ owner,
+                                           unsigned long long* const* __restrict__ claim_tables) {
+  const int r = blockIdx.x * blockDim.x + threadIdx.x;
   if (r >= rmax || r >= *n_roots) return;
+  claim_root(r, rmax, roots, win, ev_eid, ev_ts, owner, claim_tables);
+}
+
+// The second half of the split end-of-step barrier fused with this step's
+// claims: every block first waits (bounded) until all peers signalled the end
+// of the previous step, i.e. finished their write-backs and mail writes into
+// the tables and their reads of this rank's gradient buffer.
+__global__ void tgn_peer_wait_claim_kernel(const uint64_t* __restrict__ my_flags, int rank, int W,
+                                           const int64_t* __restrict__ epoch, int* status, long long budget,
+                                           const int64_t* __restrict__ roots, const int* __restrict__ n_roots,
+                                           int rmax, const int* __restrict__ win, const int64_t* __restrict__ ev_eid,
+                                           const float* __restrict__ ev_ts, const int* __restrict__ owner,
+                                           unsigned long long* const* __restrict__ claim_tables) {
+  if (threadIdx.x < 32) peer_wait_warp(my_flags, rank, W, epoch, status, budget);
+  __syncthreads();
+  const int r = blockIdx.x * blockDim.x + threadIdx.x;
+  if (r >= rmax || r >= *n_roots) return;
+  claim_root(r, rmax, roots, win, ev_eid, ev_ts, owner, claim_tables);
+}
+
+// Root r's final mail written into the owner's slot when this rank's claim won.
+__device__ __forceinline__ void mail_write_root(int r, int rmax, const int64_t* __restrict__ roots,
+                                                const int* __restrict__ win, const int* __restrict__ src_idx,
+                                                const int* __restrict__ dst_idx, const int64_t* __restrict__ ev_eid,
+                                                const float* __restrict__ ev_ts, const float* __restrict__ mem_prev,
+                                                int D, const void* __restrict__ efeat, int efeat_bf16, int efeat_ld,
+                                                int e_raw, int E, const int* __restrict__ owner,
+                                                const unsigned long long* const* __restrict__ claim_tables,
+                                                float* const* __restrict__ mail_tables,
+                                                float* const* __restrict__ mail_ts_tables) {
   int pass = 0;
   const int i = final_mail_event(win, rmax, r, pass);
   if (i < 0) return;
@@ -267,11 +434,53 @@ __global__ void tgn_peer_mail_write_kernel(const int64_t* __restrict__ roots, co
     else if (c < 2 * D) x = mem_prev[static_cast<int64_t>(other) * D + (c - D)];
     else {
       const int ce = c - 2 * D;
-      x = (ce < e_raw) ? efeat[e * efeat_ld + ce] : 0.f;
+      x = 0.f;
+      if (ce < e_raw) {
+        x = efeat_bf16 ? __bfloat162float(static_cast<const __nv_bfloat16*>(efeat)[e * efeat_ld + ce])
+                       : static_cast<const float*>(efeat)[e * efeat_ld + ce];
+      }
     }
     slot[c] = x;
   }
   if (threadIdx.x == 0) mail_ts_tables[o][v] = ev_ts[i];
+}
+
+__global__ void tgn_peer_mail_write_kernel(const int64_t* __restrict__ roots, const int* __restrict__ n_roots,
+                                           int rmax, const int* __restrict__ win, const int* __restrict__ src_idx,
+                                           const int* __restrict__ dst_idx, const int64_t* __restrict__ ev_eid,
+                                           const float* __restrict__ ev_ts, const float* __restrict__ mem_prev, int D,
+                                           const void* __restrict__ efeat, int efeat_bf16, int efeat_ld, int e_raw,
+                                           int E, const int* __restrict__ owner,
+                                           const unsigned long long* const* __restrict__ claim_tables,
+                                           float* const* __restrict__ mail_tables,
+                                           float* const* __restrict__ mail_ts_tables) {
+  const int r = blockIdx.x;
+  if (r >= rmax || r >= *n_roots) return;
+  mail_write_root(r, rmax, roots, win, src_idx, dst_idx, ev_eid, ev_ts, mem_prev, D, efeat, efeat_bf16, efeat_ld,
+                  e_raw, E, owner, claim_tables, mail_tables, mail_ts_tables);
+}
+
+// End-of-step push of one root per block: memory write-back (historical
+// filter included) and, for the claim winner, the mailbox slot. Blocks loop
+// over roots so that the grid need not cover rmax.
+__global__ void tgn_peer_push_kernel(const int64_t* __restrict__ roots, const int* __restrict__ n_roots, int rmax,
+                                     const float* __restrict__ mem_new, const float* __restrict__ ts_max,
+                                     float* const* __restrict__ mem_tables, float* const* __restrict__ ts_tables,
+                                     HistCache hc, const int* __restrict__ win, const int* __restrict__ src_idx,
+                                     const int* __restrict__ dst_idx, const int64_t* __restrict__ ev_eid,
+                                     const float* __restrict__ ev_ts, const float* __restrict__ mem_prev, int D,
+                                     const void* __restrict__ efeat, int efeat_bf16, int efeat_ld, int e_raw, int E,
+                                     const int* __restrict__ owner,
+                                     const unsigned long long* const* __restrict__ claim_tables,
+                                     float* const* __restrict__ mail_tables,
+                                     float* const* __restrict__ mail_ts_tables) {
+  const int n = min(rmax, *n_roots);
+  for (int r = blockIdx.x; r < n; r += gridDim.x) {
+    writeback_root(r, roots, mem_new, D, owner, mem_tables, ts_tables, ts_max, hc);
+    if (mail_tables != nullptr)
+      mail_write_root(r, rmax, roots, win, src_idx, dst_idx, ev_eid, ev_ts, mem_prev, D, efeat, efeat_bf16,
+                      efeat_ld, e_raw, E, owner, claim_tables, mail_tables, mail_ts_tables);
+  }
 }
 
 void launch_tgn_peer_mail_claim(cudaStream_t st, const int64_t* roots, const int* n_roots, int rmax, const int* win,
@@ -285,14 +494,38 @@ void launch_tgn_peer_mail_claim(cudaStream_t st, const int64_t* roots, const int
 
 void launch_tgn_peer_mail_write(cudaStream_t st, const int64_t* roots, const int* n_roots, int rmax, const int* win,
                                 const int* src_idx, const int* dst_idx, const int64_t* ev_eid, const float* ev_ts,
-                                const float* mem_prev, int D, const float* efeat, int efeat_ld, int e_raw, int E,
-                                const int* owner, const unsigned long long* const* claim_tables,
+                                const float* mem_prev, int D, const void* efeat, int efeat_bf16, int efeat_ld,
+                                int e_raw, int E, const int* owner, const unsigned long long* const* claim_tables,
                                 float* const* mail_tables, float* const* mail_ts_tables) {
   if (rmax <= 0) return;
   count_launch();
   tgn_peer_mail_write_kernel<<<rmax, 128, 0, st>>>(roots, n_roots, rmax, win, src_idx, dst_idx, ev_eid, ev_ts,
-                                                   mem_prev, D, efeat, efeat_ld, e_raw, E, owner, claim_tables,
-                                                   mail_tables, mail_ts_tables);
+                                                   mem_prev, D, efeat, efeat_bf16, efeat_ld, e_raw, E, owner,
+                                                   claim_tables, mail_tables, mail_ts_tables);
+}
+
+void launch_tgn_peer_wait_claim(cudaStream_t st, const uint64_t* my_flags, int rank, int W, const int64_t* epoch,
+                                int* status, long long budget, const int64_t* roots, const int* n_roots, int rmax,
+                                const int* win, const int64_t* ev_eid, const float* ev_ts, const int* owner,
+                                unsigned long long* const* claim_tables) {
+  count_launch();
+  const int blocks = rmax > 0 ? (rmax + 127) / 128 : 1;
+  tgn_peer_wait_claim_kernel<<<blocks, 128, 0, st>>>(my_flags, rank, W, epoch, status, budget, roots, n_roots, rmax,
+                                                      win, ev_eid, ev_ts, owner, claim_tables);
+}
+
+void launch_tgn_peer_push(cudaStream_t st, int blocks, const int64_t* roots, const int* n_roots, int rmax,
+                          const float* mem_new, const float* ts_max, float* const* mem_tables,
+                          float* const* ts_tables, const HistCache& hc, const int* win, const int* src_idx,
+                          const int* dst_idx, const int64_t* ev_eid, const float* ev_ts, const float* mem_prev, int D,
+                          const void* efeat, int efeat_bf16, int efeat_ld, int e_raw, int E, const int* owner,
+                          const unsigned long long* const* claim_tables, float* const* mail_tables,
+                          float* const* mail_ts_tables) {
+  if (rmax <= 0) return;
+  count_launch();
+  tgn_peer_push_kernel<<<blocks, 128, 0, st>>>(roots, n_roots, rmax, mem_new, ts_max, mem_tables, ts_tables, hc, win,
+                                               src_idx, dst_idx, ev_eid, ev_ts, mem_prev, D, efeat, efeat_bf16,
+                                               efeat_ld, e_raw, E, owner, claim_tables, mail_tables, mail_ts_tables);
 }
 
 }  // namespace su

@@ -356,6 +356,103 @@ __global__ void tgn_attn_fwd_kernel(const float* __restrict__ Q, const float* __
   }
 }
 
+// Attention forward for k * H <= 32 and k <= 16 (the configured fanouts): one
+// warp per root. Every lane issues all its K-row loads at once (columns lane +
+// 32 c of the k rows), accumulates per-(edge, head) partial dot products in
+// registers and one transposed butterfly (31 shuffles) leaves the full score of
+// (edge j, head h) in lane j * H + h. The softmax runs across the lanes of one
+// head; the aggregation reads the V rows with the weights fetched by shuffle.
+// Same outputs and dropout stream as tgn_attn_fwd_kernel.
+template <int KMAX, int H>
+__global__ void __launch_bounds__(256) tgn_attn_fwd_wide_kernel(
+    const float* __restrict__ Q, const float* __restrict__ KV, const int* __restrict__ cnt,
+    const int* __restrict__ n_roots, int rmax, int k, int Do, float att_drop, uint64_t seed,
+    const int64_t* __restrict__ step_ctr, float* __restrict__ att_p, float* __restrict__ agg) {
+  static_assert(KMAX * H <= 32, "one score per lane");
+  const int r = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (r >= rmax) return;
+  const int dh = Do / H;
+  float* ag = agg + (int64_t)r * Do;
+  const int nv = (r < *n_roots) ? min(cnt[r], k) : 0;
+  if (nv == 0) {
+    for (int d = lane; d < Do; d += 32) ag[d] = 0.f;
+    return;
+  }
+  const float* q = Q + (int64_t)r * Do;
+  const float* kv = KV + (int64_t)r * k * (2 * Do);
+  float qv[kAttnMaxCols];
+  load_row_cols(q, Do, qv);
+  // part[j * H + h]: this lane's share of score (j, h)
+  float part[32];
+#pragma unroll
+  for (int i = 0; i < 32; ++i) part[i] = 0.f;
+#pragma unroll
+  for (int j = 0; j < KMAX; ++j) {
+    if (j < nv) {
+      const float* row = kv + (int64_t)j * (2 * Do);
+#pragma unroll
+      for (int c = 0; c < kAttnMaxCols; ++c) {
+        const int d = lane + 32 * c;
+        if (d < Do) {
+          const float t = qv[c] * __ldg(row + d);
+          const int h = d / dh;
+#pragma unroll
+          for (int hh = 0; hh < H; ++hh)
+            if (h == hh) part[j * H + hh] += t;
+        }
+      }
+    }
+  }
+  // transposed butterfly: after it, lane l holds the warp total of part[l]
+#pragma unroll
+  for (int off = 16; off >= 1; off >>= 1) {
+    const bool up = (lane & off) != 0;
+#pragma unroll
+    for (int i = 0; i < off; ++i) {
+      const float send = up ? part[i] : part[i + off];
+      const float keep = up ? part[i + off] : part[i];
+      part[i] = keep + __shfl_xor_sync(0xffffffffu, send, off);
+    }
+  }
+  const int j = lane / H;
+  const int h = lane % H;
+  const bool on = j < nv;
+  float sc = -INFINITY;
+  if (on) sc = part[0] > 0.f ? part[0] : 0.2f * part[0];  // LeakyReLU(0.2)
+  float m = sc;
+  for (int o = H; o < 32; o <<= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+  const float ex = on ? expf(sc - m) : 0.f;
+  float sum = ex;
+  for (int o = H; o < 32; o <<= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+  const float p = on ? ex / sum : 0.f;
+  const int64_t e = (int64_t)r * k + j;
+  float a = p;
+  if (on) {
+    att_p[e * H + h] = p;
+    if (att_drop > 0.f) {
+      const uint64_t dseed = seed ^ (static_cast<uint64_t>(*step_ctr) * 0x9E3779B97F4A7C15ull);
+      a = dropout_keep(dseed, (uint64_t)(e * H + h), kStreamAttDrop, att_drop) ? p / (1.f - att_drop) : 0.f;
+    }
+  }
+  // aggregate: lanes over feature columns, weights of (edge jj, head of column d) by shuffle
+#pragma unroll
+  for (int c = 0; c < kAttnMaxCols; ++c) {
+    const int d = lane + 32 * c;
+    if (32 * c >= Do) break;  // warp-uniform
+    const int hd = d < Do ? d / dh : 0;
+    float acc = 0.f;
+#pragma unroll
+    for (int jj = 0; jj < KMAX; ++jj) {
+      if (jj < nv) {
+        const float w = __shfl_sync(0xffffffffu, a, jj * H + hd);
+        if (d < Do) acc = fmaf(w, __ldg(kv + (int64_t)jj * (2 * Do) + Do + d), acc);
+      }
+    }
+    if (d < Do) ag[d] = acc;
+  }
+}
+
 // Backward of the attention: dagg -> dKV (rows of invalid edges stay zero), dQ.
 __global__ void tgn_attn_bwd_kernel(const float* __restrict__ Q, const float* __restrict__ KV,
                                     const float* __restrict__ att_p, const float* __restrict__ dagg,
@@ -652,6 +749,18 @@ void launch_tgn_attn_fwd(dim3 grid, dim3 block, cudaStream_t st, const float* __
                                     int Do, int H, float att_drop, uint64_t seed, const int64_t* __restrict__ step_ctr,
                                     float* __restrict__ att_p, float* __restrict__ agg) {
   count_launch();
+  if (Do % H == 0 && Do <= 32 * kAttnMaxCols) {
+#define SU_ATTN_WIDE(KM, HH)                                                                                  \
+  tgn_attn_fwd_wide_kernel<KM, HH><<<grid, block, 0, st>>>(Q, KV, cnt, n_roots, rmax, k, Do, att_drop, seed, \
+                                                           step_ctr, att_p, agg);                            \
+  return;
+    if (H == 1 && k <= 8) { SU_ATTN_WIDE(8, 1) }
+    if (H == 1 && k <= 16) { SU_ATTN_WIDE(16, 1) }
+    if (H == 2 && k <= 8) { SU_ATTN_WIDE(8, 2) }
+    if (H == 2 && k <= 16) { SU_ATTN_WIDE(16, 2) }
+    if (H == 4 && k <= 8) { SU_ATTN_WIDE(8, 4) }
+#undef SU_ATTN_WIDE
+  }
   tgn_attn_fwd_kernel<<<grid, block, 0, st>>>(Q, KV, cnt, n_roots, rmax, k, Do, H, att_drop, seed, step_ctr, att_p, agg);
 }
 

@@ -117,6 +117,23 @@ void tgn_peer_mail_write(const at::Tensor& roots, const at::Tensor& n_roots, con
                          const at::Tensor& owner, const at::Tensor& claim_ptrs, const at::Tensor& mail_ptrs,
                          const at::Tensor& mail_ts_ptrs);
 
+void peer_signal(const at::Tensor& flag_ptrs, int64_t rank, int64_t world, at::Tensor& epoch);
+void peer_wait(const at::Tensor& my_flags, int64_t rank, int64_t world, const at::Tensor& epoch, int64_t budget);
+void tgn_peer_wait_claim(const at::Tensor& my_flags, int64_t rank, int64_t world, const at::Tensor& epoch,
+                         int64_t budget, const at::Tensor& roots, const at::Tensor& n_roots, const at::Tensor& win,
+                         const at::Tensor& ev_eid, const at::Tensor& ev_ts, const at::Tensor& owner,
+                         const at::Tensor& claim_ptrs);
+void tgn_peer_push(const at::Tensor& roots, const at::Tensor& n_roots, const at::Tensor& mem_new,
+                   const at::Tensor& ts_max, const at::Tensor& owner, const at::Tensor& mem_ptrs,
+                   const at::Tensor& ts_ptrs, const c10::optional<std::vector<at::Tensor>>& cache, double thresh,
+                   int64_t rank, const at::Tensor& win, const at::Tensor& src_idx, const at::Tensor& dst_idx,
+                   const at::Tensor& ev_eid, const at::Tensor& ev_ts, const at::Tensor& mem_prev,
+                   const at::Tensor& efeat, int64_t E, const at::Tensor& claim_ptrs,
+                   const c10::optional<at::Tensor>& mail_ptrs, const c10::optional<at::Tensor>& mail_ts_ptrs);
+void peer_rs_adam_ag(const at::Tensor& grad_ptrs, const at::Tensor& param_ptrs, int64_t world, int64_t rank,
+                     const at::Tensor& p_local, at::Tensor& m, at::Tensor& v, at::Tensor& step, at::Tensor& done,
+                     double lr, double b1, double b2, double eps, double wd, double scale);
+
 at::Tensor spmm_peer_gather(const at::Tensor& rowptr, const at::Tensor& col, const at::Tensor& val,
                             const at::Tensor& peers, const at::Tensor& src_owner, const at::Tensor& src_row,
                             int64_t n_rows, int64_t F);
@@ -184,6 +201,15 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("thresh") = 0.5, py::arg("rank") = 0);
   m.def("tgn_peer_mail_claim", &tgn_peer_mail_claim);
   m.def("tgn_peer_mail_write", &tgn_peer_mail_write);
+  m.def("peer_signal", &peer_signal);
+  m.def("peer_wait", &peer_wait);
+  m.def("tgn_peer_wait_claim", &tgn_peer_wait_claim);
+  m.def("tgn_peer_push", &tgn_peer_push, py::arg("roots"), py::arg("n_roots"), py::arg("mem_new"), py::arg("ts_max"),
+        py::arg("owner"), py::arg("mem_ptrs"), py::arg("ts_ptrs"), py::arg("cache"), py::arg("thresh"),
+        py::arg("rank"), py::arg("win"), py::arg("src_idx"), py::arg("dst_idx"), py::arg("ev_eid"), py::arg("ev_ts"),
+        py::arg("mem_prev"), py::arg("efeat"), py::arg("E"), py::arg("claim_ptrs"), py::arg("mail_ptrs") = py::none(),
+        py::arg("mail_ts_ptrs") = py::none());
+  m.def("peer_rs_adam_ag", &peer_rs_adam_ag);
   m.def("spmm_csr", &spmm_csr);
   m.def("spmm_peer_gather", &spmm_peer_gather);
   m.def("spmm_peer_push", &spmm_peer_push);

@@ -27,13 +27,15 @@ inline const T* opt_ptr(const c10::optional<at::Tensor>& t) {
 
 inline int pad8(int x) { return (x + 7) / 8 * 8; }
 
-// Split-K factor of a weight-gradient GEMM (K = the data rows): every split
-// accumulates at least 12 k-chunks (768 rows) in TMEM before its one atomic
-// flush (the flush atomics, not the copies, bound these small-output GEMMs),
-// and the splits x output tiles fill the SMs at most once.
+// Split-K factor of a weight-gradient GEMM (K = the data rows): with many
+// k-chunks every split accumulates at least 12 of them (768 rows) in TMEM
+// before its one atomic flush (the flush atomics, not the copies, bound these
+// small-output GEMMs); with few (K = one row per root, ~20 chunks) a single CTA
+// walking them all is latency-bound (~20 us measured for 19 chunks), so splits
+// of 4 chunks run side by side. The splits x output tiles fill the SMs at most once.
 inline int wgrad_ksplit(int nchunks, int tiles) {
   const int sms = num_sms(at::cuda::current_device());
-  const int by_work = std::max(1, nchunks / 12);
+  const int by_work = std::max(1, nchunks / (nchunks >= 96 ? 12 : 4));
   const int by_sms = std::max(1, sms / std::max(1, tiles));
   return std::max(1, std::min(by_work, by_sms));
 }

@@ -1,8 +1,13 @@
 """CTDG event-stream dataset and batch containers (reference backends/ctdg/runtime/data.py:23-239).
 
 ``iter_batches`` walks the split in global windows of ``batch_size * world_size``
-events when edge ownership is configured and keeps the events owned by this
-rank (possibly none: empty batches still take part in every collective).
+events when the stream is partitioned over ranks. With ``assignment ==
+"owner"`` (the reference's rule, data.py:172-180) a rank keeps the events whose
+source it owns, so per-rank batch sizes follow the skew of the stream (possibly
+none: empty batches still take part in every step). With ``"balanced"`` rank r
+takes events r, r + W, r + 2W, ... of the window: exactly ``batch_size`` events
+per rank. That needs ranks to read and write memory rows of nodes they do not
+own, which the NVLink path (remote fetch + push to owners) provides.
 ``sampler_graph(split)`` returns the events visible to the split: train events
 for train, [0, val_end) for val, [0, test_end) for test.
 """
@@ -66,13 +71,18 @@ class TGTemporalDataset:
         self.edge_parts: torch.Tensor | None = None
         self.partition_rank = 0
         self.partition_world_size = 1
+        self.assignment = "owner"
         self._dst_pool: torch.Tensor | None = None
 
-    def configure_partition(self, *, node_parts, edge_parts, rank: int, world_size: int) -> None:
+    def configure_partition(self, *, node_parts, edge_parts, rank: int, world_size: int,
+                            assignment: str = "owner") -> None:
+        if assignment not in ("owner", "balanced"):
+            raise ValueError(f"unknown event assignment {assignment!r} (owner | balanced)")
         self.node_parts = node_parts
         self.edge_parts = edge_parts
         self.partition_rank = rank
         self.partition_world_size = world_size
+        self.assignment = assignment
 
     def split_event_ids(self, split: str) -> torch.Tensor:
         if split not in self._split_cache:
@@ -111,7 +121,10 @@ class TGTemporalDataset:
         for bi, start in enumerate(range(start_window * gbs, int(indices.numel()), gbs), start=start_window):
             ev = indices[start:start + gbs]
             if distributed:
-                ev = ev[self.edge_parts[ev] == self.partition_rank]
+                if self.assignment == "balanced":
+                    ev = ev[self.partition_rank::self.partition_world_size]
+                else:
+                    ev = ev[self.edge_parts[ev] == self.partition_rank]
             s, d, t = self.src[ev], self.dst[ev], self.ts[ev]
             yield CTDGDataBatch(index=bi, split=split, event_ids=ev, src=s, dst=d, ts=t, edge_feat=self.edge_feat[ev],
                                 src_node_feat=self.lookup_node_features(s, t) if self.node_feat_dim else None,

@@ -46,8 +46,16 @@ def build_ctdg_runtime(session_ctx: SessionContext, dataset: TGTemporalDataset |
     if dctx.world_size > 1 and node_parts is None:
         node_parts = torch.arange(dataset.num_nodes, dtype=torch.long) % dctx.world_size
         edge_parts = node_parts[dataset.src]
+    # events per rank: "owner" = the events whose source this rank owns (reference rule;
+    # per-rank batch sizes follow the stream's skew), "balanced" = an equal share of each
+    # global window (needs every rank to read and push any node's rows); "auto" picks
+    # balanced on the NVLink path with remote reads, owner elsewhere
+    assignment = str(c.get("event_partition", "auto"))
+    if assignment == "auto":
+        nvlink = device.startswith("cuda") and str(cfg.get("comm", {}).get("path", "p2p")) == "p2p"
+        assignment = "balanced" if (nvlink and bool(c.get("remote_fetch", True))) else "owner"
     dataset.configure_partition(node_parts=node_parts, edge_parts=edge_parts, rank=dctx.rank,
-                                world_size=dctx.world_size)
+                                world_size=dctx.world_size, assignment=assignment)
     memory = CTDGMemoryBank(num_nodes=dataset.num_nodes, hidden_dim=hidden, device=device, mailbox_slots=slots,
                             edge_feat_dim=edim, rank=dctx.rank, world_size=dctx.world_size,
                             async_sync=bool(c.get("async_sync", True)), node_parts=node_parts,
@@ -107,7 +115,7 @@ def build_ctdg_runtime(session_ctx: SessionContext, dataset: TGTemporalDataset |
                 return 1.0 / world
 
         bmax = int(cfg["train"]["batch_size"])
-        if dctx.world_size > 1 and edge_parts is not None:
+        if dctx.world_size > 1 and edge_parts is not None and assignment == "owner":
             bmax = int(session_ctx.provider_state.get("max_local_batch", bmax * 2))
         engine = TGNCudaEngine(model=model, updater=updater, memory=memory, edge_feat=dataset.edge_feat,
                                neg_pool=dataset.dst_pool(), csr_provider=sampler.csr, bmax=bmax, fanout=fanout[0],

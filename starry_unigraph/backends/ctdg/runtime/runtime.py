@@ -322,7 +322,7 @@ class CTDGOnlineRuntime:
             eng.step(split, train)
             res[i, 0:1].copy_(eng.loss, non_blocking=True)   # stream-ordered before the next step overwrites it
             res[i, 1:4].copy_(eng.metrics, non_blocking=True)
-        torch.cuda.current_stream(self.device).synchronize()
+        eng.drain()
         out = []
         for i, b in enumerate(batches):
             loss, ap, auc, mrr = res[i].tolist()
@@ -347,6 +347,7 @@ class CTDGOnlineRuntime:
             sizes.append(batch.size)
             if collect_predictions:
                 preds.append(eng.pos_probs(batch.size).clone())
+        eng.drain()  # multi-GPU: every peer's last pushes have landed before the caller reads anything
         if not losses:
             return {"losses": [], "metrics": [], "sizes": [], "predictions": []}
         L = torch.cat(losses).tolist()

@@ -1,12 +1,14 @@
 """Checkpoint IO (reference checkpoint/io.py:9-20: pickle of a payload dict).
 
-Payloads are written with ``torch.save`` (a pickle container that also stores
-tensors efficiently) and read back with ``weights_only=False`` so both
-state-dict payloads and the reference's live-object payloads load.
+Payloads are written with ``pickle.dump``, the reference's format, so the
+reference's ``load_checkpoint`` (``pickle.load``) reads them; tensors pickle
+through torch's own reduction. Files written by ``torch.save`` (earlier
+builds of this framework, the CTDG checkpoint) also load.
 """
 from __future__ import annotations
 
 import pickle
+import zipfile
 from pathlib import Path
 from typing import Any
 
@@ -17,15 +19,15 @@ def save_checkpoint(path: str | Path, payload: dict[str, Any]) -> Path:
     path = Path(path)
     path.parent.mkdir(parents=True, exist_ok=True)
     tmp = path.with_suffix(path.suffix + ".tmp")
-    torch.save(payload, tmp)
+    with tmp.open("wb") as handle:
+        pickle.dump(payload, handle, protocol=pickle.HIGHEST_PROTOCOL)
     tmp.replace(path)
     return path
 
 
 def load_checkpoint(path: str | Path) -> dict[str, Any]:
     path = Path(path)
-    try:
+    if zipfile.is_zipfile(path):  # torch.save container
         return torch.load(path, map_location="cpu", weights_only=False)
-    except Exception:
-        with path.open("rb") as handle:
-            return pickle.load(handle)
+    with path.open("rb") as handle:
+        return pickle.load(handle)

@@ -61,6 +61,21 @@ class FlatParams:
             self.grad_views[name] = gview
             off += n
 
+    def rebind_data(self, buffer: torch.Tensor) -> None:
+        """Move the parameters onto `buffer` (e.g. a symmetric allocation that
+        peer GPUs write updated shards into); values are copied over."""
+        assert buffer.numel() >= self.data.numel() and buffer.dtype == torch.float32
+        new = buffer.view(-1)[: self.data.numel()]
+        new.copy_(self.data)
+        self.data = new
+        off = 0
+        for name, p in zip(self.names, self.params):
+            n = p.numel()
+            view = self.data[off:off + n].view_as(p)
+            p.data = view
+            self.views[name] = view
+            off += n
+
     def zero_grad(self) -> None:
         self.grad.zero_()
 

@@ -129,8 +129,10 @@ class TGNCudaEngine:
         self.flat = FlatParams([model], dev)
         self.peer = peer
         if peer is not None:
-            # gradients in the symmetric buffer: the fused all-reduce reads them from every rank
+            # gradients and parameters in symmetric buffers: each rank reduces its shard of
+            # every rank's gradient and stores the updated shard into every rank's parameters
             self.flat.rebind_grad(peer.arena["grad"])
+            self.flat.rebind_data(peer.arena["param"])
         self.opt = FusedAdam(self.flat, lr=lr)
         self._alloc()
         self._pd = None
@@ -241,6 +243,8 @@ class TGNCudaEngine:
         C.tgn_prep(self.ev_src, self.ev_dst, self.ev_ts, self.n_ev, self.neg_pool, self.stamp, self.node2root,
                    self.step_ctr, self.seed, self.roots, self.n_roots, self.src_idx, self.dst_idx, self.neg,
                    self.neg_idx, self.ts_max, self.root_ts, self.win_key, self.win, self.cnt)
+        if self.peer is not None:
+            self.peer.wait_claim(C, self.roots, self.n_roots, self.win, self.ev_eid, self.ev_ts)
         cell = u.memory_cell
         C.tgn_rnn_memory_update(self.roots, self.n_roots, mem.mailbox, mem.memory, mem.memory_ts, self.ts_max,
                                 cell.weight_ih, cell.weight_hh, cell.bias_ih, cell.bias_hh, self.mem_prev,
@@ -291,6 +295,8 @@ class TGNCudaEngine:
                    self.neg_idx, self.ts_max, self.root_ts, self.win_key, self.win, self.cnt)
         C.tgn_sample(self.roots, self.n_roots, self.root_ts, csr.rowptr, csr.nbr, csr.eid, csr.ts, s.k, self.policy,
                      self.seed, self.step_ctr, self.nbr, self.nbr_eid, self.nbr_dt, self.nbr_cnt, self.edge_total)
+        if self.peer is not None:  # previous step's pushes complete on every rank; post this step's claims
+            self.peer.wait_claim(C, self.roots, self.n_roots, self.win, self.ev_eid, self.ev_ts)
         g = u.mail_aggregator
         cell = u.memory_cell
         C.tgn_memory_update(self.roots, self.n_roots, mem.mailbox, s.K, mem.memory, mem.memory_ts, self.ts_max,
@@ -332,24 +338,27 @@ class TGNCudaEngine:
             self._peer_sync(train)
 
     def _peer_sync(self, train: bool) -> None:
-        """Multi-GPU end of step over NVLink: gradient all-reduce fused with Adam,
-        memory write-back and mailbox claim/write into the owner ranks' tables,
-        separated by device-side barriers (see starry_unigraph.parallel.ctdg_peer)."""
+        """Multi-GPU end of step over NVLink (see starry_unigraph.parallel.ctdg_peer):
+        barrier A, then the memory write-back and the claim winners' mailbox slots on
+        the side stream while the main stream runs the reduce-scatter + Adam +
+        all-gather of the parameters, then the end-of-step signal, whose wait is
+        fused into the next step's claims."""
         C, s, P = self.C, self.s, self.peer
         P.barrier(C)
+        main = torch.cuda.current_stream(self.device)
+        self._side.wait_stream(main)
+        with torch.cuda.stream(self._side):
+            C.tgn_peer_push(self.roots, self.n_roots, self.mem_new, self.ts_max, P.owner, P.tables["memory"],
+                            P.tables["memory_ts"], P.hist_cache, P.hist_thresh, P.rank, self.win, self.src_idx,
+                            self.dst_idx, self.ev_eid, self.ev_ts, self.mem_prev, self.efeat, s.E,
+                            P.tables["claim"], P.tables["mailbox"], P.tables["mailbox_ts"])
         if train:
             o = self.opt
-            C.peer_allreduce_adam(P.tables["grad"], P.world, self.flat.data, o.exp_avg, o.exp_avg_sq, o.step_ctr,
-                                  o.done, float(o.param_groups[0]["lr"]), float(o.betas[0]), float(o.betas[1]),
-                                  float(o.eps), float(o.weight_decay), 1.0 / P.world)
-        C.tgn_peer_writeback(self.roots, self.n_roots, self.mem_new, P.owner, P.tables["memory"],
-                             P.tables["memory_ts"], self.ts_max, P.hist_cache, P.hist_thresh, P.rank)
-        C.tgn_peer_mail_claim(self.roots, self.n_roots, self.win, self.ev_eid, self.ev_ts, P.owner, P.tables["claim"])
-        P.barrier(C)
-        C.tgn_peer_mail_write(self.roots, self.n_roots, self.win, self.src_idx, self.dst_idx, self.ev_eid, self.ev_ts,
-                              self.mem_prev, self.efeat, s.E, P.owner, P.tables["claim"], P.tables["mailbox"],
-                              P.tables["mailbox_ts"])
-        P.barrier(C)
+            C.peer_rs_adam_ag(P.tables["grad"], P.tables["param"], P.world, P.rank, self.flat.data, o.exp_avg,
+                              o.exp_avg_sq, o.step_ctr, o.done, float(o.param_groups[0]["lr"]), float(o.betas[0]),
+                              float(o.betas[1]), float(o.eps), float(o.weight_decay), 1.0 / P.world)
+        main.wait_stream(self._side)
+        P.signal_end(C)
 
     def _backward(self, gw: dict[str, torch.Tensor]) -> None:
         """Data gradients on the main stream; every weight-gradient GEMM forks onto a
@@ -459,11 +468,20 @@ class TGNCudaEngine:
         bwd = 11             # link-proj (2), LN, out-proj (2), attention, W_q/W_kv/time-encoder (4), Adam
         n = fwd + (bwd if train else 0)
         if self.peer is not None:
-            # - local mailbox; + 3 barriers, write-back, claim, mail write (Adam becomes the fused all-reduce + Adam)
-            n += -1 + 6
+            # - local mailbox; + wait/claim, barrier, push, end signal (Adam becomes reduce-scatter + Adam + all-gather)
+            n += -1 + 4
         return n
 
+    def drain(self) -> None:
+        """Multi-GPU: wait for every peer's end of the last step (its pushes into
+        this rank's tables and its reads of this rank's buffers) and synchronise.
+        Call before reading node tables on the host and before teardown."""
+        if self.peer is not None:
+            self.peer.drain(self.C)
+        torch.cuda.synchronize(self.device)
+
     def reset_graphs(self) -> None:
+        self.drain()
         self._graphs.clear()
         self._warm.clear()
 

@@ -2,20 +2,26 @@
 timestamps live in symmetric allocations; each node's rows are authoritative
 on its owner rank (``node_parts``, default ``id % world``).
 
-Per step (reference semantics: remote memory/mail pushed to owners and applied
-before the next step, backends/ctdg/runtime/memory.py:328-553, runtime.py:243-246):
+Per step t (reference semantics: remote memory/mail pushed to owners and
+applied before the next step reads them, backends/ctdg/runtime/memory.py:
+328-553, runtime.py:243-246):
 
-  1. compute (all ranks, no communication call): the memory updater reads the
-     roots' mailbox and memory rows straight from their owners' tables inside
-     the GEMM producers and writes the new rows to a local buffer; attention
-     reads neighbour rows from the owners (this step's roots from the local
-     buffer); backward likewise.
-  2. barrier A (tables and gradients are no longer read for this step)
-  3. gradient all-reduce fused with Adam (train), memory write-back to owners
-     (memory_ts = max over writers), mailbox claims: 64-bit atomicMax of
-     (ts, event id) on the owner
-  4. barrier B, then the claim winners write the mailbox slots
-  5. barrier C (the next step reads consistent tables)
+  1. prep + neighbour sampling (local; overlaps the peers still finishing
+     step t-1)
+  2. wait C(t-1): every peer finished step t-1's pushes into the tables and its
+     reads of this rank's gradient buffer; fused with this step's mailbox
+     claims (64-bit atomicMax of (ts, event id) on the owner)
+  3. compute, no communication call: the memory updater reads the roots'
+     mailbox and memory rows straight from their owners' tables inside the GEMM
+     producers and writes the new rows to a local buffer; attention reads
+     neighbour rows from the owners (this step's roots from the local buffer);
+     backward likewise
+  4. barrier A (every rank's gradients are complete and nobody reads the
+     tables for step t any more)
+  5. on a side stream: memory write-back (memory_ts = max over writers) and the
+     claim winners' mailbox slots; on the main stream: reduce-scatter of the
+     gradient, Adam on this rank's shard, all-gather of the new parameters
+  6. signal C(t), no wait (the wait is step t+1's item 2)
 
 Every wait is a bounded device spin that records a status code and returns.
 """
@@ -45,7 +51,9 @@ class PeerCTDGContext:
             "mailbox_ts": ((N, 1), torch.float32),
             "claim": ((N,), torch.int64),
             "grad": (((int(grad_numel) + 3) // 4 * 4,), torch.float32),
-            "flags": ((32,), torch.int64),
+            "param": (((int(grad_numel) + 3) // 4 * 4,), torch.float32),
+            "flags": ((32,), torch.int64),    # barrier A
+            "flags_c": ((32,), torch.int64),  # end-of-step signal / next-step wait
         }
         self.arena = SymmetricArena(specs, self.device, group)
         self.rank, self.world = self.arena.rank, self.arena.world_size
@@ -56,12 +64,15 @@ class PeerCTDGContext:
         a["mailbox_ts"].zero_()
         a["claim"].zero_()
         a["grad"].zero_()
+        a["param"].zero_()
         a["flags"].zero_()
+        a["flags_c"].zero_()
         self.owner = owner.to(self.device, torch.int32).contiguous()
         self.epoch = torch.zeros(1, dtype=torch.int64, device=self.device)
+        self.epoch_c = torch.zeros(1, dtype=torch.int64, device=self.device)
         self.budget = int(barrier_budget)
         self.tables = {n: a.peer_table(n) for n in ("memory", "memory_ts", "mailbox", "mailbox_ts", "claim", "grad",
-                                                    "flags")}
+                                                    "param", "flags", "flags_c")}
         torch.cuda.synchronize(self.device)
         a.barrier_host()
 
@@ -100,3 +111,20 @@ class PeerCTDGContext:
 
     def barrier(self, C) -> None:
         C.peer_barrier(self.tables["flags"], self.rank, self.world, self.epoch, self.budget)
+
+    def signal_end(self, C) -> None:
+        """First half of the end-of-step barrier (no wait)."""
+        C.peer_signal(self.tables["flags_c"], self.rank, self.world, self.epoch_c)
+
+    def drain(self, C) -> None:
+        """Wait until every peer finished its last step's pushes (and reads of this
+        rank's buffers). Needed before the tables are read on the host and before
+        teardown: with the split end-of-step barrier a fast rank may otherwise free
+        memory that a slow peer still writes into."""
+        C.peer_wait(self.arena["flags_c"], self.rank, self.world, self.epoch_c, self.budget)
+
+    def wait_claim(self, C, roots, n_roots, win, ev_eid, ev_ts) -> None:
+        """Second half of the previous step's end-of-step barrier, fused with this
+        step's mailbox claims."""
+        C.tgn_peer_wait_claim(self.arena["flags_c"], self.rank, self.world, self.epoch_c, self.budget, roots, n_roots,
+                              win, ev_eid, ev_ts, self.owner, self.tables["claim"])

@@ -366,27 +366,99 @@ class SchedulerSession:
         return float(stats[0]), int(stats[1]), float(stats[2])
 
     # ------------------------------------------------------------------ checkpoints
-    def save_checkpoint(self, path: str | Path, *, exact_resume: bool = False) -> Path:
+    @staticmethod
+    def rank_state_path(path: str | Path, rank: int) -> Path:
+        """File of one rank's exact-resume state next to checkpoint `path`."""
         path = Path(path)
-        if self.ctx.dist.is_distributed and dist.is_initialized() and dist.get_rank() != 0:
+        return path.with_name(f"{path.name}.rank{rank}")
+
+    def _ctdg_rank_state(self) -> dict[str, Any]:
+        """This rank's share of the CTDG training state: the memory-bank rows it
+        holds (rows that were ever written: on the NVLink path these are the
+        nodes it owns, on the collective path also its view of remote rows), its
+        optimizer moments (sharded by rank on the NVLink path), the random
+        streams, the fused step's counter and the historical-cache rows."""
+        rt = self.ctdg_session.online_runtime
+        mb = rt.memory
+        rt.memory.wait_pending_syncs()  # pushes submitted after the last step land in the tables first
+        touched = (mb.memory_ts >= 0) | (mb.mailbox_ts != 0).any(dim=1) | (mb.next_mail_pos != 0)
+        idx = torch.nonzero(touched).view(-1)
+        bank = {"index": idx.cpu()}
+        for n in ("memory", "memory_ts", "mailbox", "mailbox_ts", "next_mail_pos"):
+            bank[n] = getattr(mb, n)[idx].cpu()
+        rng: dict[str, Any] = {"torch": torch.get_rng_state(), "negatives": rt._gen.get_state()}
+        if torch.cuda.is_available():
+            rng["cuda"] = torch.cuda.get_rng_state_all()
+        engine = rt.engine
+        state: dict[str, Any] = {"rank": self.ctx.dist.rank, "world_size": self.ctx.dist.world_size,
+                                 "memory_bank": bank, "optimizer": self.runtime.optimizer.state_dict(), "rng": rng}
+        if engine is not None:
+            state["engine_step"] = engine.step_ctr.detach().cpu()  # dropout / negative streams are keyed on it
+            peer = engine.peer
+            if peer is not None and peer.hist_cache is not None:
+                state["hist_cache"] = [t.detach().cpu() for t in peer.hist_cache]
+        return state
+
+    def _load_ctdg_rank_state(self, state: dict[str, Any]) -> None:
+        rt = self.ctdg_session.online_runtime
+        if int(state["world_size"]) != self.ctx.dist.world_size:
+            raise RuntimeError(f"exact-resume state was written by {state['world_size']} ranks, "
+                               f"this run has {self.ctx.dist.world_size}")
+        mb = rt.memory
+        bank = state["memory_bank"]
+        with torch.no_grad():
+            mb.memory.zero_()
+            mb.memory_ts.fill_(-1.0)
+            mb.mailbox.zero_()
+            mb.mailbox_ts.zero_()
+            mb.next_mail_pos.zero_()
+            idx = bank["index"].to(mb.memory.device)
+            for n in ("memory", "memory_ts", "mailbox", "mailbox_ts", "next_mail_pos"):
+                getattr(mb, n)[idx] = bank[n].to(mb.memory.device)
+        self.runtime.optimizer.load_state_dict(state["optimizer"])
+        rng = state["rng"]
+        torch.set_rng_state(rng["torch"])
+        rt._gen.set_state(rng["negatives"])
+        if "cuda" in rng and torch.cuda.is_available():
+            torch.cuda.set_rng_state_all(rng["cuda"])
+        engine = rt.engine
+        if engine is not None:
+            if "engine_step" in state:
+                engine.step_ctr.copy_(state["engine_step"])
+            peer = engine.peer
+            if peer is not None:
+                peer.arena["claim"].zero_()  # claim keys of the abandoned run would outrank resumed mails
+                if peer.hist_cache is not None and "hist_cache" in state:
+                    for dst, src in zip(peer.hist_cache, state["hist_cache"]):
+                        dst.copy_(src)
+
+    def save_checkpoint(self, path: str | Path, *, exact_resume: bool = False) -> Path:
+        """Reference keys in `path` (rank 0 writes it: all ranks hold identical
+        parameters). With ``exact_resume`` (CTDG) every rank also writes
+        ``<path>.rank<r>`` with its own memory-bank rows, optimizer moments and
+        random streams; all ranks must call this then."""
+        path = Path(path)
+        distributed = self.ctx.dist.is_distributed and dist.is_initialized()
+        rank = dist.get_rank() if distributed else 0
+        if self.ctdg_session is not None:
+            engine = getattr(self.ctdg_session.online_runtime, "engine", None)
+            if engine is not None:
+                engine.drain()  # multi-GPU: the peers' last pushes have landed in this rank's tables
+            if exact_resume:
+                path.parent.mkdir(parents=True, exist_ok=True)
+                save_checkpoint(self.rank_state_path(path, rank), self._ctdg_rank_state())
+            if rank == 0:
+                path.parent.mkdir(parents=True, exist_ok=True)
+                extra = {"epoch": self.current_epoch, "global_step": self.global_step}
+                if exact_resume:
+                    extra["exact_resume"] = {"world_size": self.ctx.dist.world_size}
+                self.ctdg_session.save_checkpoint(path, extra)
+            if distributed:
+                dist.barrier()
+            return path
+        if distributed and rank != 0:
             return path  # one writer (all ranks hold identical parameters)
         path.parent.mkdir(parents=True, exist_ok=True)
-        if self.ctdg_session is not None:
-            extra = None
-            if exact_resume:
-                mb = self.ctdg_session.online_runtime.memory
-                rng = {"torch": torch.get_rng_state()}
-                if torch.cuda.is_available():
-                    rng["cuda"] = torch.cuda.get_rng_state_all()
-                engine = getattr(self.ctdg_session.online_runtime, "engine", None)
-                if engine is not None and hasattr(engine, "step_ctr"):
-                    rng["engine_step"] = engine.step_ctr.detach().cpu()  # dropout streams are keyed on it
-                extra = {"memory_bank": {n: getattr(mb, n).cpu() for n in
-                                         ("memory", "memory_ts", "mailbox", "mailbox_ts", "next_mail_pos")},
-                         "optimizer": self.runtime.optimizer.state_dict(), "rng": rng,
-                         "epoch": self.current_epoch, "global_step": self.global_step}
-            self.ctdg_session.save_checkpoint(path, extra)
-            return path
         model = self.runtime.model.module if hasattr(self.runtime.model, "module") else self.runtime.model
         opt = self.runtime.optimizer
         payload = {"model_state": {k: v.detach().cpu() for k, v in model.state_dict().items()},
@@ -398,22 +470,23 @@ class SchedulerSession:
     def load_checkpoint(self, path: str | Path) -> dict[str, Any]:
         if self.ctdg_session is None and self.snapshot_core is None:
             self.build_runtime()
+        distributed = self.ctx.dist.is_distributed and dist.is_initialized()
         if self.ctdg_session is not None:
+            engine = getattr(self.ctdg_session.online_runtime, "engine", None)
+            if engine is not None:
+                engine.drain()
             ckpt = self.ctdg_session.load_checkpoint(path)
             self.current_epoch = int(ckpt.get("epoch", self.current_epoch))
             self.global_step = int(ckpt.get("global_step", self.global_step))
-            # exact-resume keys (absent from reference checkpoints): optimizer moments, RNG streams
-            if isinstance(ckpt.get("optimizer"), dict) and self.runtime.optimizer is not None:
-                self.runtime.optimizer.load_state_dict(ckpt["optimizer"])
-            rng = ckpt.get("rng")
-            if isinstance(rng, dict):
-                if "torch" in rng:
-                    torch.set_rng_state(rng["torch"])
-                if "cuda" in rng and torch.cuda.is_available():
-                    torch.cuda.set_rng_state_all(rng["cuda"])
-                engine = getattr(self.ctdg_session.online_runtime, "engine", None)
-                if "engine_step" in rng and engine is not None and hasattr(engine, "step_ctr"):
-                    engine.step_ctr.copy_(rng["engine_step"])
+            if isinstance(ckpt.get("exact_resume"), dict):
+                rank_file = self.rank_state_path(path, self.ctx.dist.rank)
+                if not rank_file.exists():
+                    raise FileNotFoundError(f"exact-resume checkpoint without this rank's state: {rank_file}")
+                self._load_ctdg_rank_state(load_checkpoint(rank_file))
+            if engine is not None:
+                torch.cuda.synchronize(engine.device)
+            if distributed:
+                dist.barrier()  # no rank steps (and reads peers' tables) before all have loaded
             return ckpt
         payload = load_checkpoint(path)
         state = payload.get("model_state")
@@ -426,11 +499,19 @@ class SchedulerSession:
                 for k, v in model.state_dict().items():
                     v.copy_(state[k])
         opt_state = payload.get("optimizer_state")
-        if opt_state is not None and self.runtime.optimizer is not None and isinstance(opt_state, dict):
-            try:
+        if opt_state is not None and self.runtime.optimizer is not None:
+            if isinstance(opt_state, dict):  # written by this framework: a mismatch is an error
                 self.runtime.optimizer.load_state_dict(opt_state)
-            except Exception:
-                pass
+            else:
+                # the reference pickles its live torch optimizer, whose state layout need not
+                # match this framework's flat optimizer: keep fresh moments and say so
+                try:
+                    self.runtime.optimizer.load_state_dict(opt_state.state_dict())
+                except Exception as exc:  # noqa: BLE001
+                    import warnings
+
+                    warnings.warn(f"optimizer state of the checkpoint not restored ({exc}); "
+                                  "training resumes with fresh Adam moments")
         self.runtime.scheduler = payload.get("scheduler_state")
         self.current_epoch = int(payload.get("epoch", 0))
         self.global_step = int(payload.get("global_step", 0))

@@ -63,6 +63,22 @@ def test_ctdg_two_ranks_memory_partition(tmp_path):
         assert torch.allclose(a, b, atol=1e-6)
 
 
+def test_ctdg_exact_resume_two_ranks(tmp_path):
+    """Each rank saves its own memory-bank rows, optimizer moments and random
+    streams; a fresh session that loads them continues exactly like the
+    uninterrupted run (losses, parameters, memory and mailbox on every rank)."""
+    res = _launch(tmp_path, "tgn", None, "--resume")
+    assert res.returncode == 0, res.stdout[-2000:] + res.stderr[-4000:]
+    for r in range(2):
+        d = torch.load(tmp_path / f"resume_r{r}.pt")
+        assert d["rank_file"]
+        torch.testing.assert_close(torch.tensor(d["resumed"]), torch.tensor(d["full"]), rtol=0, atol=1e-6)
+        for a, b in zip(d["params_full"], d["params_resumed"]):
+            torch.testing.assert_close(a, b, rtol=0, atol=1e-6)
+        torch.testing.assert_close(d["memory_resumed"], d["memory_full"], rtol=0, atol=1e-6)
+        torch.testing.assert_close(d["mailbox_resumed"], d["mailbox_full"], rtol=0, atol=1e-6)
+
+
 @pytest.mark.parametrize("world", [4, 8])
 def test_many_ranks_dtdg_and_ctdg(tmp_path, world):
     """W = 4 and 8: every rank finishes the same number of steps with a finite

@@ -46,11 +46,14 @@ def test_owner0_run_matches_single_gpu(tmp_path):
 
 
 @need2
-def test_hash_partition_two_ranks_consistent(tmp_path):
-    _run(tmp_path, 2, "--batch", "100", "--steps", "12", "--mode", "hash")
+@pytest.mark.parametrize("assign", ["balanced", "owner"])
+def test_hash_partition_two_ranks_consistent(tmp_path, assign):
+    _run(tmp_path, 2, "--batch", "100", "--steps", "12", "--mode", "hash", "--assign", assign)
     r0 = torch.load(tmp_path / "w2_r0.pt")
     r1 = torch.load(tmp_path / "w2_r1.pt")
     assert r0["peer"] and r1["peer"]
+    if assign == "balanced":
+        assert r0["sizes"] == r1["sizes"] == [100] * 12
     # the fused all-reduce sums in rank order on every rank: parameters stay bit-identical
     assert torch.equal(r0["params"], r1["params"])
     assert all(torch.isfinite(torch.tensor(r0["losses"] + r1["losses"])))

@@ -248,3 +248,103 @@ def test_halo_gather_and_push_kernels():
     gref = torch.zeros(n_src, F, device="cuda").index_add_(0, src, g[dst] * val[:, None])
     got = torch.stack([gbufs[o][r] for o, r in zip(src_owner.tolist(), src_row.tolist())])
     torch.testing.assert_close(got, gref, rtol=1e-5, atol=1e-5)
+
+
+def test_rs_adam_ag_matches_torch_on_every_replica():
+    """Reduce-scatter + Adam + all-gather, three ranks emulated by three launches:
+    every replica ends with the torch Adam result of the mean gradient, each rank
+    having updated only its own shard."""
+    C = _C()
+    W, n = 3, 4096 + 12
+    torch.manual_seed(0)
+    g = [torch.randn(n, device="cuda") for _ in range(W)]
+    p0 = torch.randn(n, device="cuda")
+    params = [p0.clone() for _ in range(W)]
+    mv = [(torch.zeros(n, device="cuda"), torch.zeros(n, device="cuda")) for _ in range(W)]
+    steps = [torch.zeros(1, dtype=torch.int64, device="cuda") for _ in range(W)]
+    dones = [torch.zeros(1, dtype=torch.int32, device="cuda") for _ in range(W)]
+    gt, pt = _table(*g), _table(*params)
+    ref = p0.clone().requires_grad_(True)
+    opt = torch.optim.Adam([ref], lr=1e-2)
+    for it in range(3):
+        for r in range(W):
+            C.peer_rs_adam_ag(gt, pt, W, r, params[r], mv[r][0], mv[r][1], steps[r], dones[r], 1e-2, 0.9, 0.999,
+                              1e-8, 0.0, 1.0 / W)
+        ref.grad = sum(g) / W
+        opt.step()
+        for x in g:
+            x.mul_(0.5)
+    torch.cuda.synchronize()
+    assert all(int(s) == 3 for s in steps)
+    for r in range(W):
+        torch.testing.assert_close(params[r], ref.detach(), rtol=1e-5, atol=1e-6)
+    assert torch.equal(params[0], params[1]) and torch.equal(params[1], params[2])
+
+
+def test_wait_claim_and_push():
+    """The end-of-step protocol on two emulated ranks: the fused wait + claim
+    (peers' flags already at the epoch, so the wait passes), then one push per
+    rank (memory write-back + the claim winners' mailbox slots); the end-of-step
+    signal stores the next epoch into the peer's flag array."""
+    C = _C()
+    N, D, E = 10, 8, 4
+    SW = 2 * D + E
+    owner = (torch.arange(N, device="cuda") % 2).int()
+    mem = [torch.zeros(N, D, device="cuda") for _ in range(2)]
+    mts = [torch.full((N,), -1.0, device="cuda") for _ in range(2)]
+    mail = [torch.zeros(N, SW, device="cuda") for _ in range(2)]
+    mail_ts = [torch.zeros(N, device="cuda") for _ in range(2)]
+    claim = [torch.zeros(N, dtype=torch.int64, device="cuda") for _ in range(2)]
+    flags = [torch.zeros(32, dtype=torch.int64, device="cuda") for _ in range(2)]
+    epochs = [torch.ones(1, dtype=torch.int64, device="cuda") for _ in range(2)]
+    flags[0][1] = 1
+    flags[1][0] = 1
+    efeat = torch.randn(50, E, device="cuda")
+
+    def rank_data(roots, ts_max, ev, fill):
+        R = len(roots)
+        return dict(r=torch.tensor(roots, dtype=torch.int64, device="cuda"),
+                    nr=torch.tensor([R], dtype=torch.int32, device="cuda"),
+                    mem_new=torch.full((R, D), fill, device="cuda"), ts_max=torch.tensor([ts_max], device="cuda"),
+                    win=torch.cat([torch.arange(R), torch.full((R,), -1)]).int().cuda(),
+                    src_idx=torch.arange(R, dtype=torch.int32, device="cuda"),
+                    dst_idx=((torch.arange(R) + 1) % R).int().cuda(),
+                    eid=torch.tensor([e for e, _ in ev], dtype=torch.int64, device="cuda"),
+                    ets=torch.tensor([t for _, t in ev], dtype=torch.float32, device="cuda"),
+                    mem_prev=torch.full((R, D), fill, device="cuda"))
+
+    data = [rank_data([0, 1, 2], 5.0, [(10, 4.0), (11, 5.0), (12, 5.0)], 1.0),
+            rank_data([1, 3], 7.0, [(20, 3.0), (21, 7.0)], 2.0)]
+    for q, x in enumerate(data):
+        C.tgn_peer_wait_claim(flags[q], q, 2, epochs[q], 50_000_000, x["r"], x["nr"], x["win"], x["eid"], x["ets"],
+                              owner, _table(*claim))
+    for q, x in enumerate(data):
+        C.tgn_peer_push(x["r"], x["nr"], x["mem_new"], x["ts_max"], owner, _table(*mem), _table(*mts), None, 0.5, q,
+                        x["win"], x["src_idx"], x["dst_idx"], x["eid"], x["ets"], x["mem_prev"], efeat, E,
+                        _table(*claim), _table(*mail), _table(*mail_ts))
+    C.peer_signal(_table(*flags), 0, 2, epochs[0])
+    torch.cuda.synchronize()
+    from starry_unigraph.ops import check_status
+
+    check_status()
+    assert int(flags[1][0]) == 2 and int(epochs[0]) == 2
+    assert torch.equal(mem[0][0], torch.ones(D, device="cuda")) and torch.equal(mem[0][2], torch.ones(D, device="cuda"))
+    assert float(mts[1][1]) == 7.0 and float(mts[1][3]) == 7.0 and float(mts[0][0]) == 5.0
+    assert float(mem[1][3][0]) == 2.0
+    # node 1: rank 0 proposes (ts 5, eid 11), rank 1 (ts 3, eid 20) -> rank 0's mail wins
+    assert float(mail_ts[1][1]) == 5.0 and float(mail[1][1][0]) == 1.0
+    assert torch.equal(mail[1][1][2 * D:], efeat[11])
+    assert float(mail_ts[1][3]) == 7.0 and torch.equal(mail[1][3][2 * D:], efeat[21])
+    assert float(mail_ts[0][2]) == 5.0 and torch.equal(mail[0][2][2 * D:], efeat[12])
+    # bf16 edge features give the same slot values as their fp32 copies
+    mail_b = [torch.zeros_like(m) for m in mail]
+    mts_b = [torch.zeros_like(m) for m in mail_ts]
+    mem_b = [torch.zeros_like(m) for m in mem]
+    ets_b = [torch.full_like(m, -1.0) for m in mts]
+    ef_b = efeat.bfloat16()
+    for q, x in enumerate(data):
+        C.tgn_peer_push(x["r"], x["nr"], x["mem_new"], x["ts_max"], owner, _table(*mem_b), _table(*ets_b), None, 0.5,
+                        q, x["win"], x["src_idx"], x["dst_idx"], x["eid"], x["ets"], x["mem_prev"], ef_b, E,
+                        _table(*claim), _table(*mail_b), _table(*mts_b))
+    torch.cuda.synchronize()
+    assert torch.equal(mail_b[1][3][2 * D:], ef_b[21].float())

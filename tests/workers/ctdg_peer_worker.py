@@ -5,7 +5,9 @@ and saves the node tables, parameters and losses of this rank.
     python tests/workers/ctdg_peer_worker.py --out DIR --batch B --steps S --mode {hash,owner0} [--lr LR]
 
 mode owner0: every node and every event belongs to rank 0 (other ranks see
-empty batches), so rank 0 must reproduce a single-GPU run with batch W*B.
+empty batches, events assigned by owner), so rank 0 must reproduce a single-GPU
+run with batch W*B. mode hash: nodes hash-partitioned, events assigned by
+--assign (balanced: B events per rank; owner: the events of owned sources).
 """
 import argparse
 import json
@@ -25,6 +27,7 @@ def main():
     p.add_argument("--mode", default="hash", choices=["hash", "owner0"])
     p.add_argument("--lr", type=float, default=1e-3)
     p.add_argument("--graphs", type=int, default=1)
+    p.add_argument("--assign", default="balanced", choices=["balanced", "owner"])
     a = p.parse_args()
     import torch
 
@@ -40,7 +43,8 @@ def main():
                                   "num_dst": 120}},
            "train": {"epochs": 1, "batch_size": a.batch, "lr": a.lr},
            "runtime": {"device": "cuda", "cuda_graphs": bool(a.graphs)},
-           "ctdg": {"mailbox_slots": 1, "dim_time": 16, "num_head": 2, "dropout": 0.0, "att_dropout": 0.0},
+           "ctdg": {"mailbox_slots": 1, "dim_time": 16, "num_head": 2, "dropout": 0.0, "att_dropout": 0.0,
+                    "event_partition": "owner" if a.mode == "owner0" else a.assign},
            "sampling": {"neighbor_limit": [5], "strategy": "recent", "history": 1},
            "graph": {"partition": "round_robin"},
            "dist": {"backend": "nccl", "timeout_s": 120}}
@@ -60,19 +64,20 @@ def main():
         s.prepared.provider_meta["max_local_batch"] = a.batch * world
     s.build_runtime()
     rt = s.ctdg_session.online_runtime
-    losses = []
+    losses, sizes = [], []
     for i, b in enumerate(rt.iter_batches("train", a.batch)):
         if i >= a.steps:
             break
         out = s.ctdg_session.train_step(b)
         losses.append(float(out["loss"]))
+        sizes.append(b.size)
     torch.cuda.synchronize()
     check_status()
     mb = rt.memory
     eng = rt.engine
     torch.save({"memory": mb.memory.cpu(), "memory_ts": mb.memory_ts.cpu(), "mailbox": mb.mailbox.cpu(),
                 "mailbox_ts": mb.mailbox_ts.cpu(), "params": eng.flat.data.cpu(), "losses": losses,
-                "owner": mb.owner.cpu(), "peer": eng.peer is not None},
+                "owner": mb.owner.cpu(), "peer": eng.peer is not None, "sizes": sizes},
                Path(a.out) / f"w{world}_r{rank}.pt")
     if world > 1:
         eng.reset_graphs()

@@ -21,6 +21,8 @@ def main():
     p.add_argument("--out", required=True)
     p.add_argument("--timeout", type=float, default=60.0)
     p.add_argument("--heartbeat", type=float, default=0.0)
+    p.add_argument("--resume", action="store_true",
+                   help="CTDG: train K1 + K2 steps, and K1 steps -> exact-resume checkpoint -> new session -> K2 steps")
     a = p.parse_args()
     import torch
 
@@ -40,6 +42,10 @@ def main():
     s = SchedulerSession.from_config(cfg)
     s.ctx.artifact_root = Path(a.out) / f"art_r{rank}"
     initialize_distributed(s.ctx.dist)
+    if a.resume:
+        _resume_check(a, cfg, s, rank)
+        finalize_distributed(s.ctx.dist)
+        os._exit(0)
     t0 = time.time()
     outcome = {"rank": rank, "error": None}
     try:
@@ -60,6 +66,47 @@ def main():
     if outcome["error"] is None:
         finalize_distributed(s.ctx.dist)
     os._exit(0 if outcome["error"] is None else 3)
+
+
+def _resume_check(a, cfg, s, rank):
+    """Uninterrupted run against save / fresh session / load / continue."""
+    import torch
+
+    from starry_unigraph import SchedulerSession
+
+    k1, k2 = 3, 4
+    s.prepare_data()
+    s.build_runtime()
+    batches = list(s.ctdg_session.online_runtime.iter_batches("train", 8))[: k1 + k2]
+    full = [float(s.ctdg_session.train_step(b)["loss"]) for b in batches]
+    mem_full = s.ctdg_session.online_runtime.memory
+
+    def fresh():
+        t = SchedulerSession.from_config(cfg)
+        t.ctx.artifact_root = s.ctx.artifact_root
+        t.build_runtime()
+        return t
+
+    first = fresh()
+    for b in batches[:k1]:
+        first.ctdg_session.train_step(b)
+    ckpt = Path(a.out) / "ckpt" / "resume.pt"
+    first.save_checkpoint(ckpt, exact_resume=True)
+    second = fresh()
+    second.load_checkpoint(ckpt)
+    rest = [float(second.ctdg_session.train_step(b)["loss"]) for b in batches[k1:]]
+    m2 = second.ctdg_session.online_runtime.memory
+    model_a = s.runtime.model.module if hasattr(s.runtime.model, "module") else s.runtime.model
+    model_b = second.runtime.model.module if hasattr(second.runtime.model, "module") else second.runtime.model
+    mem_full.wait_pending_syncs()
+    m2.wait_pending_syncs()
+    torch.save({"full": full[k1:], "resumed": rest,
+                "params_full": [p.detach().clone() for p in model_a.parameters()],
+                "params_resumed": [p.detach().clone() for p in model_b.parameters()],
+                "memory_full": mem_full.memory.clone(), "memory_resumed": m2.memory.clone(),
+                "mailbox_full": mem_full.mailbox.clone(), "mailbox_resumed": m2.mailbox.clone(),
+                "rank_file": SchedulerSession.rank_state_path(ckpt, rank).exists()},
+               Path(a.out) / f"resume_r{rank}.pt")
 
 
 if __name__ == "__main__":
