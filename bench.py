@@ -1,4 +1,5 @@
-"""Benchmark: TGN train events/sec on N GPUs of one node.
+"""Benchmark: TGN train events/sec on N GPUs of one node, with the
+MPNN-LSTM snapshots/sec of config 2 nested in the same JSON line (``mpnn_lstm``).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
     torchrun --nnodes=1 --nproc-per-node N --master-addr 127.0.0.1 --master-port P bench.py --gpus N ...
@@ -52,6 +53,11 @@ def _args():
                    help="DTDG: edges per snapshot (mpnn_lstm: 2,000,000; tgcn/evolvegcn: 20,000,000)")
     p.add_argument("--trace", action="store_true",
                    help="tgn/jodie: after the timed region, print a per-op device-time table of one eager step")
+    p.add_argument("--no-mpnn", action="store_true",
+                   help="default workload: skip the nested MPNN-LSTM (config 2) measurement")
+    p.add_argument("--mpnn-steps", type=int, default=40,
+                   help="default workload: timed MPNN-LSTM windows (at most the train split's windows)")
+    p.add_argument("--no-graphs", action="store_true", help="DTDG: eager steps instead of CUDA-graph replays")
     return p.parse_args()
 
 
@@ -145,42 +151,42 @@ DTDG_WORKLOADS = {
 }
 
 
-def _mpnn_main(args):
-    """MPNN-LSTM: 200,000 nodes, 128 Chung-Lu snapshots of ~2M edges with 30% churn,
-    64-dim features, window 8, two MPNN layers + two LSTMs of hidden 64, MSE. Nodes are partitioned over the
-    ranks (strong scaling: the same graph on every N). One step = one training window ending at the next
-    snapshot, so snapshots/sec = steps/sec."""
-    sys.path.insert(0, str(ROOT))
+def _dtdg_run(args, workload: str, steps: int, warmup: int) -> dict:
+    """DTDG snapshot throughput on the workload's BASELINE.json shape. mpnn_lstm (config 2): 200,000 nodes,
+    128 Chung-Lu snapshots of ~2M edges with 30% churn, 64-dim features, window 8, two MPNN layers + two LSTMs
+    of hidden 64, MSE. Nodes are partitioned over the ranks (strong scaling: the same graph on every N). One
+    step = one training window ending at the next snapshot, so snapshots/sec = steps/sec.
+
+    Steps run as CUDA graphs of the whole window step (forward, backward, Adam): the timed windows are
+    captured in an untimed pass after the warm-up, then the timed pass replays them (full work every replay,
+    parameters change every step); the end-to-end pass replays them once more through the public per-step
+    call with the loss read back each step. The process group must already be initialised for N > 1."""
     import torch
     import torch.distributed as dist
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
-    torch.cuda.set_device(local_rank)
     from starry_unigraph import SchedulerSession
     from starry_unigraph.backends.dtdg.runtime.training import run_flare_train_step
-    from starry_unigraph.ops import check_status
+    from starry_unigraph.ops import check_status, cuda_ext
 
-    fam, task, hidden, window, preset, d_snaps, d_nodes, d_edges, metric_name, model_desc = DTDG_WORKLOADS[args.workload]
+    fam, task, hidden, window, preset, d_snaps, d_nodes, d_edges, metric_name, model_desc = DTDG_WORKLOADS[workload]
     snaps = args.snapshots or d_snaps
     nodes = args.nodes or d_nodes
     edges = args.edges or d_edges
     full = (snaps, nodes, edges) == (d_snaps, d_nodes, d_edges)
-
-    def cfg(resident):
-        return {
-            "model": {"name": fam, "family": fam, "task": task, "hidden_dim": hidden, "window": {"size": window}},
-            "data": {"root": "./data", "name": f"{fam}_large", "format": "synthetic",
-                     "synthetic": {"preset": preset, "num_snapshots": snaps, "num_nodes": nodes,
-                                   "edges_per_snapshot": edges}},
-            "train": {"epochs": 1, "snaps": snaps, "lr": 1e-3},
-            "runtime": {"device": "cuda"},
-            "dtdg": {"window_from_size": True, "chunk_order": None, "chunk_decay": None, "resident": resident},
-            "dist": {"backend": "nccl", "timeout_s": 1800},
-        }
-
-    session = SchedulerSession.from_config(cfg(True))
+    cfg = {
+        "model": {"name": fam, "family": fam, "task": task, "hidden_dim": hidden, "window": {"size": window}},
+        "data": {"root": "./data", "name": f"{fam}_large", "format": "synthetic",
+                 "synthetic": {"preset": preset, "num_snapshots": snaps, "num_nodes": nodes,
+                               "edges_per_snapshot": edges}},
+        "train": {"epochs": 1, "snaps": snaps, "lr": 1e-3},
+        "runtime": {"device": "cuda", "cuda_graphs": not args.no_graphs},
+        "dtdg": {"window_from_size": True, "chunk_order": None, "chunk_decay": None, "resident": True},
+        "dist": {"backend": "nccl", "timeout_s": 1800},
+    }
+    session = SchedulerSession.from_config(cfg)
     # one artifact set for all ranks (written by rank 0): every partition file holds its
     # snapshots' features, so per-rank copies would multiply the disk footprint by N
     session.ctx.artifact_root = Path(os.environ.get("TMPDIR", "/tmp")) / f"su_{fam}_w{world}"
@@ -196,28 +202,26 @@ def _mpnn_main(args):
     session.build_runtime()
     prep_s = time.perf_counter() - t_prep
     core, rt = session.snapshot_core, session.runtime
-    need = args.warmup + 2 * args.steps
-    blob_list = list(core.iter_train(max_steps=need))
-    if len(blob_list) < need:  # the train split holds ~70% of the snapshots
-        args.steps = (len(blob_list) - args.warmup) // 2
-        if args.steps <= 0:
-            raise SystemExit(f"train split has only {len(blob_list)} windows")
-    blobs = iter(blob_list)
+    graphs = rt.state.get("step_graphs")
+    avail = len(list(core.iter_train()))
+    steps = max(1, min(steps, avail - warmup))
+    blob_list = list(core.iter_train(max_steps=warmup + steps))
+    warm, timed = blob_list[:warmup], blob_list[warmup:warmup + steps]
 
     def barrier():
         if world > 1:
             dist.barrier()
 
-    for _ in range(args.warmup):
-        run_flare_train_step(rt, next(blobs), {"meta": {}}, need_host=False)
+    for b in warm:
+        run_flare_train_step(rt, b, {"meta": {}}, need_host=False)
+    if graphs is not None:
+        for b in timed:  # capture pass (untimed): one graph per timed window
+            run_flare_train_step(rt, b, {"meta": {}}, need_host=False)
     torch.cuda.synchronize()
     check_status()
-    timed = [next(blobs) for _ in range(args.steps)]
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     barrier()
     torch.cuda.synchronize()
-    from starry_unigraph.ops import cuda_ext
-
     launches0 = cuda_ext().launch_count()  # host-side count of this library's kernel launches
     with ClockSampler(local_rank) as clocks:
         start.record()
@@ -228,17 +232,20 @@ def _mpnn_main(args):
         end.record()
         torch.cuda.synchronize()
     launches = cuda_ext().launch_count() - launches0
+    if graphs is not None:
+        # replays issue no host-side launches; the count comes from the captured (eager) steps
+        launches = int(graphs.launches_per_step * steps)
     barrier()
     dev_ms = start.elapsed_time(end)
     check_status()
-    # end to end through the per-step train call with the loss read back to the host
-    # every step (the partitioned snapshots are resident on the device: no per-step H2D)
-    e2e_blobs = [next(blobs) for _ in range(args.steps)]
+    # end to end through the per-step train call with the loss read back to the host every step
+    # (the partitioned snapshots are resident on the device: no per-step H2D)
     barrier()
     torch.cuda.synchronize()
     t0 = time.perf_counter()
-    for b in e2e_blobs:
-        float(run_flare_train_step(rt, b, {"meta": {}}, need_host=False)["loss"])  # 4-byte D2H per step
+    last_loss = None
+    for b in timed:
+        last_loss = float(run_flare_train_step(rt, b, {"meta": {}}, need_host=False)["loss"])  # 4-byte D2H
     torch.cuda.synchronize()
     e2e_s = time.perf_counter() - t0
     barrier()
@@ -246,38 +253,67 @@ def _mpnn_main(args):
     if world > 1:
         dist.all_reduce(stats, op=dist.ReduceOp.MAX)
     dev_ms, e2e_s = float(stats[0]), float(stats[1])
-    value = args.steps / (dev_ms / 1000.0)
-    if rank == 0:
-        print(json.dumps({
-            "metric": metric_name, "value": value, "unit": "snapshots/s", "n_gpus": world,
-            "steps": args.steps, "warmup": args.warmup, "ms_per_step": dev_ms / args.steps,
-            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "fp32+bf16-tensor-core",
-            "data": "synthetic (random-init weights)",
-            "config": {"model": model_desc, "global_batch": None, "seq_len": window,
-                       "parallelism": f"graph-partition{world}", "nodes": nodes, "snapshots": snaps,
-                       "edges_per_snapshot": edges, "window": window, "full_config_shape": full,
-                       "l2": "window graphs' CSR + features exceed the 126 MB L2", "baseline_metric": METRIC},
-            "clocks": clocks.summary(), "gpu_launches": launches,
-            "host_issue_ms_per_step": host_issue_s * 1000.0 / args.steps,
-            "e2e": {"value": args.steps / e2e_s, "unit": "snapshots/s", "h2d_bytes_per_step": 0,
-                    "d2h_bytes_per_step": 4, "note": "snapshots resident on the device (dtdg.resident); "
-                    "the loss is read back every step"},
-            "prep_s": prep_s}), flush=True)
+    out = {
+        "metric": metric_name, "value": steps / (dev_ms / 1000.0), "unit": "snapshots/s", "n_gpus": world,
+        "steps": steps, "warmup": warmup, "ms_per_step": dev_ms / steps, "higher_is_better": True,
+        "scaling": "strong", "dtype": "fp32 storage, bf16 tensor-core operands, fp32 accumulate",
+        "data": "synthetic (random-init weights)",
+        "config": {"model": model_desc, "global_batch": None, "seq_len": window,
+                   "parallelism": f"graph-partition{world}", "nodes": nodes, "snapshots": snaps,
+                   "edges_per_snapshot": edges, "window": window, "full_config_shape": full,
+                   "cuda_graphs": graphs is not None,
+                   "capture_pass": ("each timed window captured once in an untimed pass before timing"
+                                    if graphs is not None else None),
+                   "l2": "window graphs' CSR + features exceed the 126 MB L2"},
+        "clocks": clocks.summary(), "gpu_launches": launches,
+        "host_issue_ms_per_step": host_issue_s * 1000.0 / steps,
+        "e2e": {"value": steps / e2e_s, "unit": "snapshots/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 4,
+                "note": "snapshots resident on the device (dtdg.resident); the loss is read back every step"},
+        "prep_s": prep_s, "last_loss": last_loss,
+    }
     if world > 1:
-        from starry_unigraph.distributed import finalize_distributed
+        out["consistency"] = _replicas_equal(rt.optimizer.flat.data if hasattr(rt.optimizer, "flat") else
+                                             torch.cat([p.detach().view(-1) for p in rt.model.parameters()]))
+    if graphs is not None:
+        graphs.reset()
+    return out
 
-        finalize_distributed(session.ctx.dist)
+
+def _replicas_equal(flat) -> dict:
+    """Cross-rank check: every rank's parameter buffer is bit-identical (float64 sum and max abs
+    difference against rank 0's copy)."""
+    import torch
+    import torch.distributed as dist
+
+    ref = flat.detach().clone()
+    dist.broadcast(ref, src=0)
+    diff = torch.tensor([float((flat.detach() - ref).abs().max())], dtype=torch.float64, device=flat.device)
+    dist.all_reduce(diff, op=dist.ReduceOp.MAX)
+    return {"params_max_abs_diff_vs_rank0": float(diff), "params_equal": float(diff) == 0.0}
+
+
+def _mpnn_main(args):
+    import torch
+
+    sys.path.insert(0, str(ROOT))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    torch.cuda.set_device(int(os.environ.get("LOCAL_RANK", "0")))
+    out = _dtdg_run(args, args.workload, args.steps, args.warmup)
+    out["vs_baseline"] = None
+    out["config"]["baseline_metric"] = METRIC
+    if int(os.environ.get("RANK", "0")) == 0:
+        print(json.dumps(out), flush=True)
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
+        dist.destroy_process_group()
     return 0
 
 
-def main():
-    args = _args()
-    if args.impl == "reference":
-        return _reference_arm(args)
-    if args.workload in DTDG_WORKLOADS:
-        return _mpnn_main(args)
+def _ctdg_run(args) -> dict:
+    """TGN (config 3) or JODIE (config 4) events/sec; the process group must be initialised for N > 1."""
     jodie = args.workload == "jodie"
-    sys.path.insert(0, str(ROOT))
     import torch
     import torch.distributed as dist
 
@@ -304,14 +340,14 @@ def main():
                  "async_sync": True},
         "sampling": {"neighbor_limit": [10], "strategy": "recent", "history": 1},
         "graph": {"partition": "round_robin"},
-        "dist": {"backend": "nccl", "timeout_s": 300},
+        "dist": {"backend": "nccl", "timeout_s": 1800},
     }
     session = SchedulerSession.from_config(cfg)
     session.ctx.artifact_root = Path(os.environ.get("TMPDIR", "/tmp")) / f"su_bench_w{world}_r{rank}"
     if world > 1:
         from starry_unigraph.distributed import initialize_distributed
 
-        initialize_distributed(session.ctx.dist)
+        initialize_distributed(session.ctx.dist)  # the process group exists: records it in the context
     t_prep = time.perf_counter()
     session.prepare_data()
     session.build_runtime()
@@ -387,44 +423,79 @@ def main():
     value = events_all / (dev_ms / 1000.0)
     e2e = e2e_events_all / e2e_s
     per_step_launches = eng.launches_per_step(train=True) if hasattr(eng, "launches_per_step") else None
+    bpe = 8 + 8 + 4 + 8  # src, dst, ts, eid per event
+    line = {
+        "metric": "JODIE train events/sec" if jodie else "TGN train events/sec",
+        "value": value,
+        "unit": "events/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": dev_ms / args.steps,
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "bf16",
+        "data": "synthetic (random-init weights)",
+        "config": {"model": JODIE_NAME if jodie else MODEL_NAME, "global_batch": args.batch * world,
+                   "seq_len": None, "parallelism": f"dp{world}+memory-partition", "events": args.events,
+                   "nodes": 11_000_000 if jodie else 1140149, "fanout": None if jodie else 10,
+                   "mailbox_slots": 1, "dims": "memory=172, edge features 32 (bf16 on the host)" if jodie
+                   else "memory=time=embed=100",
+                   "event_assignment": rt.dataset.assignment if world > 1 else None,
+                   "l2": ("working set (memory 7.6 GB, mailbox 30 GB, edge features 25 GB) > 126 MB L2" if jodie
+                          else "working set (memory 456 MB, mailbox 985 MB, edge features 500 MB) > 126 MB L2"),
+                   "baseline_metric": METRIC},
+        "clocks": clocks.summary(),
+        "e2e": {"value": e2e, "unit": "events/s", "h2d_bytes_per_step": args.batch * bpe,
+                "d2h_bytes_per_step": 16,
+                "api": "SchedulerSession.ctdg_session.train_batches (pinned inputs copied per step, per-step "
+                       "loss + AP/AUC/MRR read back per step into pinned memory)"},
+        "gpu_launches": (per_step_launches * args.steps) if per_step_launches else None,
+        "prep_s": prep_s,
+        "last_loss": last["loss"] if last else None,
+    }
+    eng.drain()
+    if world > 1:
+        cons = _replicas_equal(eng.flat.data)
+        mem = rt.memory
+        stray = ((mem.memory_ts >= 0) & (mem.owner != rank)).sum().to(torch.float64).view(1)
+        dist.all_reduce(stray)
+        cons["rows_written_on_non_owners"] = int(stray)
+        cons["peer_path"] = eng.peer is not None
+        line["consistency"] = cons
+    eng.reset_graphs()
+    return line
+
+
+def main():
+    args = _args()
+    if args.impl == "reference":
+        return _reference_arm(args)
+    if args.workload in DTDG_WORKLOADS:
+        return _mpnn_main(args)
+    sys.path.insert(0, str(ROOT))
+    import torch
+    import torch.distributed as dist
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    torch.cuda.set_device(int(os.environ.get("LOCAL_RANK", "0")))
+    if world > 1:
+        import datetime
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=1800),
+                                device_id=torch.device("cuda", int(os.environ.get("LOCAL_RANK", "0"))))
+    line = _ctdg_run(args)
+    if args.workload == "tgn" and not args.no_mpnn:
+        # BASELINE.json's headline pairs TGN events/sec with MPNN-LSTM snapshots/sec (config 2): measured in
+        # the same run, reported nested, with its own device timing, clocks and end-to-end rate
+        line["mpnn_lstm"] = _dtdg_run(args, "mpnn_lstm", args.mpnn_steps, max(3, args.warmup))
     if rank == 0:
-        bpe = 8 + 8 + 4 + 8  # src, dst, ts, eid per event
-        line = {
-            "metric": "JODIE train events/sec" if jodie else "TGN train events/sec",
-            "value": value,
-            "unit": "events/s",
-            "n_gpus": world,
-            "steps": args.steps,
-            "warmup": args.warmup,
-            "ms_per_step": dev_ms / args.steps,
-            "higher_is_better": True,
-            "scaling": "weak",
-            "vs_baseline": None,
-            "dtype": "bf16",
-            "data": "synthetic (random-init weights)",
-            "config": {"model": JODIE_NAME if jodie else MODEL_NAME, "global_batch": args.batch * world,
-                       "seq_len": None, "parallelism": f"dp{world}+memory-partition", "events": args.events,
-                       "nodes": 11_000_000 if jodie else 1140149, "fanout": None if jodie else 10,
-                       "mailbox_slots": 1, "dims": "memory=172, edge features 32 (bf16 on the host)" if jodie
-                       else "memory=time=embed=100",
-                       "l2": ("working set (memory 7.6 GB, mailbox 30 GB, edge features 25 GB) > 126 MB L2" if jodie
-                              else "working set (memory 456 MB, mailbox 985 MB, edge features 500 MB) > 126 MB L2"),
-                       "baseline_metric": METRIC},
-            "clocks": clocks.summary(),
-            "e2e": {"value": e2e, "unit": "events/s", "h2d_bytes_per_step": args.batch * bpe,
-                    "d2h_bytes_per_step": 16,
-                    "api": "SchedulerSession.ctdg_session.train_batches (pinned inputs copied per step, per-step "
-                           "loss + AP/AUC/MRR read back per step into pinned memory)"},
-            "gpu_launches": (per_step_launches * args.steps) if per_step_launches else None,
-            "prep_s": prep_s,
-            "last_loss": last["loss"] if last else None,
-        }
         print(json.dumps(line), flush=True)
     if world > 1:
-        eng.reset_graphs()
-        from starry_unigraph.distributed import finalize_distributed
-
-        finalize_distributed(session.ctx.dist)
+        dist.barrier()
+        dist.destroy_process_group()
     return 0
 
 

@@ -119,6 +119,13 @@ def init_flare_training(runtime: RuntimeBundle, session_ctx: SessionContext, par
                                     "part_loss_scale": scale, "task": task}
     runtime.state["part_loss_scale"] = scale
     runtime.state["task"] = task
+    dev = torch.device(device)
+    comm = str(cfg.get("comm", {}).get("path", "nccl"))
+    world = dist.get_world_size() if dist.is_available() and dist.is_initialized() else 1
+    graphs_ok = dev.type == "cuda" and bool(cfg.get("runtime", {}).get("cuda_graphs", True)) and \
+        (world == 1 or comm == "p2p")
+    runtime.state["cuda_graphs"] = graphs_ok
+    runtime.state["step_graphs"] = StepGraphs(dev) if graphs_ok else None
 
 
 def _get_labels(graph: Any) -> torch.Tensor | None:
@@ -172,8 +179,100 @@ def _loss_and_predictions(runtime: RuntimeBundle, blob_or_batch, training: bool,
     return loss, pred_values, targets
 
 
+class StepGraphs:
+    """Whole DTDG training steps (forward, backward, optimizer) as CUDA graphs,
+    one per training window.
+
+    An eager step issues a few hundred kernels from Python (~50 us of host time
+    each), which bounds the step once its GPU work is split over several ranks.
+    A window's step is captured the first time it is seen after two eager
+    warm-up steps and replayed afterwards (every epoch visits the same windows).
+    All graphs share one memory pool: only transient activations live there;
+    parameters, gradients, optimizer moments and halo buffers are allocated
+    before capture, and each replay's loss / predictions are copied out of the
+    pool before the next one can overwrite them. Host-side per-snapshot caches
+    (CSR orders, halo pull plans) are built eagerly before a capture.
+
+    Used on CUDA for ``pad``-mode windows (the state is not carried between
+    windows) on one GPU or with the NVLink collectives (``comm.path: p2p``)."""
+
+    WARMUP = 2
+
+    def __init__(self, device: torch.device) -> None:
+        self.device = torch.device(device)
+        self.graphs: dict[tuple, tuple] = {}
+        self.pool = torch.cuda.graph_pool_handle()
+        self.eager = 0
+        self.captures = 0
+        self.launches_per_step = 0  # this library's kernel launches in one captured step
+
+    @staticmethod
+    def supported(runtime: RuntimeBundle, blob: Any) -> bool:
+        if not isinstance(blob, STGraphBlob) or not bool(runtime.state.get("cuda_graphs", False)):
+            return False
+        state = blob.state
+        return getattr(state, "_mode", "pad") == "pad"
+
+    @staticmethod
+    def key(blob: Any) -> tuple:
+        return tuple((int(getattr(g, "flare_snapshot_id", -1)), int(g.num_src_nodes), int(g.num_dst_nodes),
+                      int(g.num_edges())) for g in blob)
+
+    @staticmethod
+    def _prepare(blob: Any) -> None:
+        from starry_unigraph.parallel.halo import get_halo_context
+
+        hc = get_halo_context()
+        for g in blob:
+            g.csr()
+            if hc is not None and getattr(g, "route", None) is not None and g.num_src_nodes > g.num_dst_nodes:
+                hc.pull_plan(g, g.num_dst_nodes)
+
+    def _step(self, runtime: RuntimeBundle, blob: Any):
+        loss, preds, targets = _loss_and_predictions(runtime, blob, training=True, need_host=False)
+        runtime.optimizer.zero_grad(set_to_none=True)
+        loss.backward()
+        runtime.optimizer.step()
+        return loss.detach(), preds, targets
+
+    def run(self, runtime: RuntimeBundle, blob: Any):
+        key = self.key(blob)
+        entry = self.graphs.get(key)
+        if entry is None:
+            if self.eager < self.WARMUP:
+                self.eager += 1
+                return self._step(runtime, blob)
+            self._prepare(blob)
+            torch.cuda.synchronize(self.device)
+            from starry_unigraph.ops import cuda_ext
+
+            n0 = cuda_ext().launch_count()
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph, pool=self.pool):
+                out = self._step(runtime, blob)
+            self.launches_per_step = int(cuda_ext().launch_count() - n0)
+            entry = (graph, out, blob)  # the blob keeps the captured tensors alive
+            self.graphs[key] = entry
+            self.captures += 1
+        graph, (loss, preds, targets), _ = entry
+        graph.replay()
+        return loss.clone(), preds.clone(), (None if targets is None else targets.clone())
+
+    def reset(self) -> None:
+        self.graphs.clear()
+
+
 def run_flare_train_step(runtime: RuntimeBundle, batch: Any, kernel_output: dict[str, Any],
                          need_host: bool = True) -> dict[str, Any]:
+    graphs = runtime.state.get("step_graphs")
+    if graphs is not None and StepGraphs.supported(runtime, batch):
+        loss, preds, targets = graphs.run(runtime, batch)
+        if need_host:
+            preds = preds.view(-1).cpu().tolist()
+            targets = None if targets is None else targets.view(-1).cpu().tolist()
+        return {"loss": float(loss.item()) if need_host else loss, "predictions": preds, "targets": targets,
+                "meta": kernel_output.get("meta", {}) | {"model": runtime.state["flare_model"],
+                                                          "sequence_state": "updated", "cuda_graph": True}}
     loss, preds, targets = _loss_and_predictions(runtime, batch, training=True, need_host=need_host)
     if loss is None:
         raise RuntimeError("Training labels are required for flare_native train_step")

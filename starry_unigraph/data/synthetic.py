@@ -105,14 +105,44 @@ class SnapshotSpec:
     seed: int = 0
 
 
+class _InverseCDF:
+    """Draws indices i in [0, n) with probability p_i by inverse transform, with
+    a bucket table in place of a binary search per sample: bucket j of M equal
+    slices of [0, 1) stores the first index whose cumulative mass exceeds j / M,
+    and a sample walks forward from its bucket's index (a few steps at most when
+    M exceeds the number of indices with non-negligible mass per slice). Gives
+    the same indices as ``searchsorted(cdf, u, side="right")``."""
+
+    def __init__(self, w: np.ndarray, buckets: int = 1 << 22):
+        cdf = np.cumsum(w, dtype=np.float64)
+        cdf /= cdf[-1]
+        self.cdf = cdf
+        self.m = int(buckets)
+        self.table = np.searchsorted(cdf, np.arange(self.m, dtype=np.float64) / self.m, side="right")
+
+    def __call__(self, u: np.ndarray) -> np.ndarray:
+        idx = self.table[np.minimum((u * self.m).astype(np.int64), self.m - 1)]
+        n = self.cdf.size
+        todo = np.arange(u.size)
+        while todo.size:
+            i = idx[todo]
+            adv = (i < n - 1) & (self.cdf[np.minimum(i, n - 1)] <= u[todo])
+            todo = todo[adv]
+            idx[todo] += 1
+        return np.minimum(idx, n - 1)
+
+
+_CDF_CACHE: dict[tuple, _InverseCDF] = {}
+
+
 def _chung_lu_edges(n: int, m: int, gamma: float, rng: np.random.Generator, perm: np.ndarray) -> np.ndarray:
     # expected degrees w_i ~ i^(-1/(gamma-1)); endpoints drawn proportionally to w
-    w = np.power(np.arange(1, n + 1, dtype=np.float64), -1.0 / (gamma - 1.0))
-    cdf = np.cumsum(w)
-    cdf /= cdf[-1]
-    u = rng.random((2, m))
-    e = np.minimum(np.searchsorted(cdf, u, side="right"), n - 1)
-    return perm[e]
+    key = (int(n), float(gamma))
+    if key not in _CDF_CACHE:
+        _CDF_CACHE.clear()
+        _CDF_CACHE[key] = _InverseCDF(np.power(np.arange(1, n + 1, dtype=np.float64), -1.0 / (gamma - 1.0)))
+    u = rng.random(2 * m)
+    return perm[_CDF_CACHE[key](u).reshape(2, m)]
 
 
 def _rmat_edges(n: int, m: int, abc: tuple[float, float, float], rng: np.random.Generator) -> np.ndarray:

@@ -155,3 +155,41 @@ def test_flare_model_cuda_matches_cpu(tmp_path, family):
         s.build_runtime()
         losses[dev] = s.run_epoch("train")["loss"]
     assert abs(losses["cpu"] - losses["cuda"]) <= 2e-2 * abs(losses["cpu"]) + 1e-4, losses
+
+
+@pytest.mark.parametrize("family", ["mpnn_lstm", "tgcn"])
+def test_graph_replayed_steps_match_eager(tmp_path, family):
+    """Training windows run as captured CUDA graphs (forward, backward, Adam) give
+    the losses and parameters of eager steps, including windows replayed a second
+    time (second epoch over the same windows)."""
+    from starry_unigraph import SchedulerSession
+    from starry_unigraph.backends.dtdg.runtime.training import run_flare_train_step
+
+    results = {}
+    for graphs in (False, True):
+        cfg = {"model": {"name": family, "family": family, "task": "snapshot_node_regression", "hidden_dim": 32,
+                         "window": {"size": 3}},
+               "data": {"root": "./data", "name": "gdt", "format": "synthetic",
+                        "synthetic": {"num_nodes": 3000, "num_snapshots": 10, "edges_per_snapshot": 30000,
+                                      "churn": 0.3, "feat_dim": 16}},
+               "train": {"epochs": 1, "batch_size": 1, "lr": 1e-3},
+               "runtime": {"device": "cuda", "cuda_graphs": graphs},
+               "graph": {"storage": "snapshots"},
+               "dtdg": {"chunk_order": None, "chunk_decay": None, "window_from_size": True}}
+        s = SchedulerSession.from_config(cfg)
+        s.ctx.artifact_root = tmp_path / f"g{int(graphs)}"
+        s.prepare_data()
+        s.build_runtime()
+        blobs = list(s.snapshot_core.iter_train())
+        assert len(blobs) >= 4
+        losses = [float(run_flare_train_step(s.runtime, b, {"meta": {}}, need_host=False)["loss"])
+                  for b in blobs + blobs]  # every window twice: captures, then replays
+        torch.cuda.synchronize()
+        sg = s.runtime.state.get("step_graphs")
+        if graphs:
+            assert sg is not None and sg.captures == len(blobs)  # the two eager warm-up windows on the 2nd pass
+        results[graphs] = (losses, [p.detach().cpu().clone() for p in s.runtime.model.parameters()])
+    (le, pe), (lg, pg) = results[False], results[True]
+    torch.testing.assert_close(torch.tensor(lg), torch.tensor(le), rtol=1e-3, atol=1e-5)
+    for a, b in zip(pg, pe):
+        torch.testing.assert_close(a, b, rtol=1e-3, atol=1e-5)
