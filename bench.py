@@ -58,6 +58,11 @@ def _args():
     p.add_argument("--mpnn-steps", type=int, default=40,
                    help="default workload: timed MPNN-LSTM windows (at most the train split's windows)")
     p.add_argument("--no-graphs", action="store_true", help="DTDG: eager steps instead of CUDA-graph replays")
+    p.add_argument("--dtdg-precision", default="bf16", choices=["tf32", "bf16"],
+                   help="DTDG tensor-core operand precision (config 2 names fp32/bf16, config 5 bf16)")
+    p.add_argument("--precision", default="tf32", choices=["tf32", "bf16"],
+                   help="tensor-core operand precision of the headline (runtime.precision)")
+    p.add_argument("--no-bf16", action="store_true", help="tgn/jodie: skip the nested bf16 measurement")
     return p.parse_args()
 
 
@@ -182,7 +187,7 @@ def _dtdg_run(args, workload: str, steps: int, warmup: int) -> dict:
                  "synthetic": {"preset": preset, "num_snapshots": snaps, "num_nodes": nodes,
                                "edges_per_snapshot": edges}},
         "train": {"epochs": 1, "snaps": snaps, "lr": 1e-3},
-        "runtime": {"device": "cuda", "cuda_graphs": not args.no_graphs},
+        "runtime": {"device": "cuda", "cuda_graphs": not args.no_graphs, "precision": args.dtdg_precision},
         "dtdg": {"window_from_size": True, "chunk_order": None, "chunk_decay": None, "resident": True},
         "dist": {"backend": "nccl", "timeout_s": 1800},
     }
@@ -256,7 +261,9 @@ def _dtdg_run(args, workload: str, steps: int, warmup: int) -> dict:
     out = {
         "metric": metric_name, "value": steps / (dev_ms / 1000.0), "unit": "snapshots/s", "n_gpus": world,
         "steps": steps, "warmup": warmup, "ms_per_step": dev_ms / steps, "higher_is_better": True,
-        "scaling": "strong", "dtype": "fp32 storage, bf16 tensor-core operands, fp32 accumulate",
+        "scaling": "strong", "dtype": "tf32" if rt.state.get("precision_tf32") else "bf16",
+        "dtype_detail": ("tf32" if rt.state.get("precision_tf32") else "bf16") +
+        " tensor-core operands, fp32 storage and accumulation (SpMM, LSTM gates and Adam in fp32)",
         "data": "synthetic (random-init weights)",
         "config": {"model": model_desc, "global_batch": None, "seq_len": window,
                    "parallelism": f"graph-partition{world}", "nodes": nodes, "snapshots": snaps,
@@ -311,8 +318,9 @@ def _mpnn_main(args):
     return 0
 
 
-def _ctdg_run(args) -> dict:
-    """TGN (config 3) or JODIE (config 4) events/sec; the process group must be initialised for N > 1."""
+def _ctdg_run(args, precision: str = "tf32") -> dict:
+    """TGN (config 3) or JODIE (config 4) events/sec with the given tensor-core operand precision
+    (runtime.precision); the process group must be initialised for N > 1."""
     jodie = args.workload == "jodie"
     import torch
     import torch.distributed as dist
@@ -335,7 +343,7 @@ def _ctdg_run(args) -> dict:
         "data": {"root": "./data", "name": preset, "format": "synthetic",
                  "synthetic": {"preset": preset, "num_events": args.events, "seed": 0}},
         "train": {"epochs": 1, "batch_size": args.batch, "lr": 1e-4},
-        "runtime": {"device": "cuda", "cuda_graphs": True},
+        "runtime": {"device": "cuda", "cuda_graphs": True, "precision": precision},
         "ctdg": {"mailbox_slots": 1, "dim_time": 100, "num_head": 2, "dropout": 0.1, "att_dropout": 0.1,
                  "async_sync": True},
         "sampling": {"neighbor_limit": [10], "strategy": "recent", "history": 1},
@@ -343,7 +351,7 @@ def _ctdg_run(args) -> dict:
         "dist": {"backend": "nccl", "timeout_s": 1800},
     }
     session = SchedulerSession.from_config(cfg)
-    session.ctx.artifact_root = Path(os.environ.get("TMPDIR", "/tmp")) / f"su_bench_w{world}_r{rank}"
+    session.ctx.artifact_root = Path(os.environ.get("TMPDIR", "/tmp")) / f"su_bench_{precision}_w{world}_r{rank}"
     if world > 1:
         from starry_unigraph.distributed import initialize_distributed
 
@@ -435,7 +443,9 @@ def _ctdg_run(args) -> dict:
         "higher_is_better": True,
         "scaling": "weak",
         "vs_baseline": None,
-        "dtype": "bf16",
+        "dtype": "tf32" if precision == "tf32" else "bf16",
+        "dtype_detail": (f"{precision} tensor-core operands (kind::{'tf32' if precision == 'tf32' else 'f16'}), "
+                         "fp32 storage and accumulation"),
         "data": "synthetic (random-init weights)",
         "config": {"model": JODIE_NAME if jodie else MODEL_NAME, "global_batch": args.batch * world,
                    "seq_len": None, "parallelism": f"dp{world}+memory-partition", "events": args.events,
@@ -486,7 +496,12 @@ def main():
 
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=1800),
                                 device_id=torch.device("cuda", int(os.environ.get("LOCAL_RANK", "0"))))
-    line = _ctdg_run(args)
+    line = _ctdg_run(args, args.precision)
+    if args.precision == "tf32" and not args.no_bf16:
+        # the same step with bf16 tensor-core operands, reported separately (device-timed)
+        fast = _ctdg_run(args, "bf16")
+        line["bf16"] = {k: fast[k] for k in ("metric", "value", "unit", "ms_per_step", "dtype", "dtype_detail",
+                                              "clocks")} | {"e2e": fast["e2e"]["value"]}
     if args.workload == "tgn" and not args.no_mpnn:
         # BASELINE.json's headline pairs TGN events/sec with MPNN-LSTM snapshots/sec (config 2): measured in
         # the same run, reported nested, with its own device timing, clocks and end-to-end rate

@@ -48,6 +48,18 @@ constexpr uint32_t umma_idesc_bf16_f32(int M, int N) {
          | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
 }
 
+// Instruction descriptor for kind::tf32 (fp32 operands read as TF32, FP32
+// accumulate), both operands K-major, shape M x N.
+#ifdef __CUDACC__
+__host__ __device__
+#endif
+constexpr uint32_t umma_idesc_tf32_f32(int M, int N) {
+  return (1u << 4)            // D format: F32
+         | (2u << 7)          // A format: TF32
+         | (2u << 10)         // B format: TF32
+         | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
+}
+
 #ifdef __CUDACC__
 
 __device__ __forceinline__ void record_status(int* status, int code) {
@@ -157,6 +169,15 @@ __device__ __forceinline__ void umma_bf16(uint32_t d_tmem, uint64_t a_desc, uint
   asm volatile(
       "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
       "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+__device__ __forceinline__ void umma_tf32(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                          uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
       "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
       : "memory");
 }
@@ -285,6 +306,17 @@ __device__ __forceinline__ float tanh_fast(float x) {
   float y;
   asm("tanh.approx.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
+}
+
+// Round 4 floats to TF32 (round to nearest, ties away from zero: cvt.rna) and
+// return them as one 16-byte vector of 32-bit containers.
+__device__ __forceinline__ uint4 pack_tf32x4(const float* f) {
+  uint4 u;
+  asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(u.x) : "f"(f[0]));
+  asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(u.y) : "f"(f[1]));
+  asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(u.z) : "f"(f[2]));
+  asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(u.w) : "f"(f[3]));
+  return u;
 }
 
 // Pack 8 floats to 8 bf16 (one 16-byte vector).

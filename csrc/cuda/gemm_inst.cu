@@ -190,19 +190,21 @@ static void launch_pack(const Src& src, uint8_t* out, int mn, const int* mn_dev,
   pack_kernel<ROWS, Src><<<blocks, 256, 0, st>>>(src, out, tiles, nchunks, mn, mn_dev, mn);
 }
 
-template <int BN, int NSUB, class A, class B, class E>
+template <int BN, int NSUB, bool TF32, class A, class B, class E>
 static bool launch_packed(const A& a, const B& b, const E& e, const GemmShape& sh, cudaStream_t st) {
   constexpr int B_ROWS = BN * NSUB;
   constexpr int smem = packed_smem_bytes<BN, NSUB, E>();
   constexpr bool kPrepackedA = is_prepacked<A>::value;
+  static_assert(!(TF32 && kPrepackedA), "pre-packed operand images are bf16");
   int device = 0;
   cudaGetDevice(&device);
-  const size_t abytes = kPrepackedA ? 0 : packed_bytes(sh.M, sh.K, kBM);
-  const size_t bbytes = packed_bytes(sh.N, sh.K, B_ROWS);
-  if (packed_bytes(sh.M, sh.K, kBM) == 0 || bbytes == 0) return true;
+  const size_t abytes = kPrepackedA ? 0 : packed_bytes(sh.M, sh.K, kBM, TF32);
+  const size_t bbytes = packed_bytes(sh.N, sh.K, B_ROWS, TF32);
+  if (packed_bytes(sh.M, sh.K, kBM, TF32) == 0 || bbytes == 0) return true;
   uint8_t* ws = g_ws_alloc ? static_cast<uint8_t*>(g_ws_alloc(abytes + bbytes, st)) : workspace(device, abytes + bbytes, st);
   if (ws == nullptr) return false;
-  auto kern = tc_gemm_packed_kernel<BN, NSUB, A::kMN, B::kMN, E>;
+  // tf32: both operands K-major (transposed sources are transposed by the pack kernel)
+  auto kern = tc_gemm_packed_kernel<BN, NSUB, TF32 ? false : A::kMN, TF32 ? false : B::kMN, E, TF32>;
   static unsigned long long configured = 0ull;
   if (!(configured & (1ull << device))) {
     cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
@@ -210,11 +212,11 @@ static bool launch_packed(const A& a, const B& b, const E& e, const GemmShape& s
   }
   // one launch packs both operands; the GEMM is launched with programmatic
   // stream serialisation so its prologue (barriers, TMEM) overlaps the packing
-  const int nchunks = (sh.K + kBK - 1) / kBK;
+  const int nchunks = (sh.K + chunk_k(TF32) - 1) / chunk_k(TF32);
   const int tiles_a = (sh.M + kBM - 1) / kBM;
   const int tiles_b = (sh.N + B_ROWS - 1) / B_ROWS;
-  const int64_t va = static_cast<int64_t>(tiles_a) * nchunks * kBM * 8;
-  const int64_t vb = static_cast<int64_t>(tiles_b) * nchunks * B_ROWS * 8;
+  const int64_t va = pack_items<kBM, TF32, A::kMN>(tiles_a, nchunks);
+  const int64_t vb = pack_items<B_ROWS, TF32, B::kMN>(tiles_b, nchunks);
   const int cap = num_sms(device) * 16;
   const uint8_t* pa = ws;
   const uint8_t* pb = ws + abytes;
@@ -222,15 +224,15 @@ static bool launch_packed(const A& a, const B& b, const E& e, const GemmShape& s
     (void)va;
     const int blocks_b = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>((vb + 255) / 256, cap)));
     count_launch();
-    pack_kernel<B_ROWS, B><<<blocks_b, 256, 0, st>>>(b, ws, tiles_b, nchunks, sh.N, nullptr, sh.N);
+    pack_kernel<B_ROWS, B, TF32><<<blocks_b, 256, 0, st>>>(b, ws, tiles_b, nchunks, sh.N, nullptr, sh.N);
     pa = a.image;
     pb = ws;
   } else {
     const int blocks_a = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>((va + 255) / 256, cap)));
     const int blocks_b = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>((vb + 255) / 256, cap / 2)));
     count_launch();
-    pack2_kernel<kBM, A, B_ROWS, B><<<blocks_a + blocks_b, 256, 0, st>>>(a, b, ws, ws + abytes, tiles_a, tiles_b,
-                                                                        nchunks, sh.M, sh.m_dev, sh.N, blocks_a);
+    pack2_kernel<kBM, A, B_ROWS, B, TF32><<<blocks_a + blocks_b, 256, 0, st>>>(
+        a, b, ws, ws + abytes, tiles_a, tiles_b, nchunks, sh.M, sh.m_dev, sh.N, blocks_a);
   }
   const int total = tiles_a * tiles_b * std::max(1, sh.ksplit);
   const int grid = std::min(total, num_sms(device));
@@ -251,9 +253,36 @@ static bool launch_packed(const A& a, const B& b, const E& e, const GemmShape& s
   return true;
 }
 
+// Precision of the GEMMs whose shape does not say (GemmShape::tf32 = 0), for
+// the whole process (autograd runs backward kernels from its own threads): set
+// by set_gemm_precision (the TGN / JODIE engines and the DTDG trainer select
+// runtime.precision before they issue a step).
+static std::atomic<int> g_tf32{0};
+
+// Host-detected failure reported through the device status word (read by the
+// host after the step): the low byte of a zero word set to `code` (< 256).
+static void record_host_error(int code) {
+  int device = 0;
+  cudaGetDevice(&device);
+  int* st = device_status_ptr(device);
+  if (st != nullptr) cudaMemsetAsync(st, code, 1, nullptr);
+}
+void set_gemm_precision(bool tf32) { g_tf32.store(tf32 ? 1 : 0); }
+bool gemm_precision_tf32() { return g_tf32.load() != 0; }
+
 template <int BN, int NSUB, class A, class B, class E>
 static void launch_any(const A& a, const B& b, const E& e, const GemmShape& sh, cudaStream_t st) {
-  if (!packed_disabled() && launch_packed<BN, NSUB>(a, b, e, sh, st)) return;
+  if (sh.tf32 || g_tf32.load(std::memory_order_relaxed)) {
+    GemmShape s2 = sh;
+    s2.tf32 = 1;
+    // tf32 operands exist in the packed form only (the fused-producer kernel stages bf16 tiles)
+    if (!launch_packed<BN, NSUB, true>(a, b, e, s2, st)) {
+      fprintf(stderr, "starry_unigraph: tf32 GEMM needs an operand workspace (allocation failed)\n");
+      record_host_error(kTooLarge);
+    }
+    return;
+  }
+  if (!packed_disabled() && launch_packed<BN, NSUB, false>(a, b, e, sh, st)) return;
   launch_cfg<BN, NSUB>(a, b, e, sh, st);
 }
 
@@ -279,10 +308,10 @@ void gemm(const MNView<SegSource>& a, const MNView<SegSource>& b, const EpiWeigh
 // path is disabled or its workspace cannot be allocated, nothing launched then.
 template <class A, class B, class E>
 static bool dispatch_prepacked(const A& a, const B& b, const E& e, const GemmShape& sh, cudaStream_t st) {
-  if (packed_disabled()) return false;
-  if (sh.N <= 128) return launch_packed<128, 1>(a, b, e, sh, st);
-  if (sh.N <= 256) return launch_packed<256, 1>(a, b, e, sh, st);
-  return launch_packed<256, 2>(a, b, e, sh, st);
+  if (packed_disabled()) return false;  // bf16 images only (written by the caller's kernels)
+  if (sh.N <= 128) return launch_packed<128, 1, false>(a, b, e, sh, st);
+  if (sh.N <= 256) return launch_packed<256, 1, false>(a, b, e, sh, st);
+  return launch_packed<256, 2, false>(a, b, e, sh, st);
 }
 bool gemm_prepacked(const Prepacked<false>& a, const MNView<WeightSource>& b, const EpiLinear& e, const GemmShape& sh,
                     cudaStream_t st) {

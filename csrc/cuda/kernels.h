@@ -20,6 +20,10 @@ void set_workspace_allocator(WorkspaceAlloc alloc, WorkspaceFree free_fn);
 void count_launch();
 long long launch_count();
 int num_sms(int device);
+// Operand precision of the tcgen05 GEMMs issued from this thread (a GemmShape
+// may also ask for tf32 itself): bf16 (default) or tf32.
+void set_gemm_precision(bool tf32);
+bool gemm_precision_tf32();
 
 // ---- tcgen05 GEMM entry points (one overload per producer/epilogue combo) ---
 void gemm(const SegSource& a, const WeightSource& b, const EpiLinear& e, const GemmShape& sh, cudaStream_t st);

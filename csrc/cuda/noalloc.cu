@@ -128,7 +128,19 @@ extern "C" SU_EXPORT int su_noalloc_status(int* out4) {
   int* status = nullptr;
   if (out4 == nullptr) return SU_NOALLOC_ERR_ARGUMENT;
   if (device_symbols(&scratch, &status) != SU_NOALLOC_OK) return SU_NOALLOC_ERR_CUDA;
+  // every stream of the device, non-blocking ones included, finishes first: the copy
+  // below runs on the legacy default stream, which is not ordered with those
+  if (cudaDeviceSynchronize() != cudaSuccess) return SU_NOALLOC_ERR_CUDA;
   if (cudaMemcpyFromSymbol(out4, g_status, sizeof(int) * 4) != cudaSuccess) return SU_NOALLOC_ERR_CUDA;
+  return SU_NOALLOC_OK;
+}
+
+extern "C" SU_EXPORT int su_noalloc_status_reset(void) {
+  float* scratch = nullptr;
+  int* status = nullptr;
+  if (device_symbols(&scratch, &status) != SU_NOALLOC_OK) return SU_NOALLOC_ERR_CUDA;
+  if (cudaDeviceSynchronize() != cudaSuccess) return SU_NOALLOC_ERR_CUDA;
+  if (cudaMemset(status, 0, sizeof(int) * 4) != cudaSuccess) return SU_NOALLOC_ERR_CUDA;
   return SU_NOALLOC_OK;
 }
 

@@ -71,8 +71,15 @@ size_t su_noalloc_scratch_capacity(void);
 // Copies the status words of the calls made through this entry point (4 ints;
 // word 0 is 0 while every bounded wait of the GEMM kernels finished, else the
 // first failure's code: 1-4 a wait that gave up, 7 a size above a kernel bound)
-// to `out4`, waiting for the device. Returns SU_NOALLOC_OK or SU_NOALLOC_ERR_CUDA.
+// to `out4`. It first waits for every stream of the current device
+// (cudaDeviceSynchronize), so calls issued on non-blocking streams are included.
+// The status is sticky: it keeps the first failure of any call since the library
+// was loaded or since the last su_noalloc_status_reset(). Returns SU_NOALLOC_OK
+// or SU_NOALLOC_ERR_CUDA.
 int su_noalloc_status(int* out4);
+
+// Clears the status words of the current device (waits for the device first).
+int su_noalloc_status_reset(void);
 
 // Human-readable text of a return code.
 const char* su_noalloc_strerror(int code);

@@ -521,6 +521,7 @@ struct GemmShape {
   int N = 0;                  // columns of D (rows of B)
   int K = 0;                  // reduction extent
   int ksplit = 1;             // split-K factor (epilogue must accumulate atomically)
+  int tf32 = 0;               // 1: fp32 operands read as TF32 (kind::tf32), else bf16 operands (kind::f16)
 };
 
 constexpr int tmem_cols_for(int n) {

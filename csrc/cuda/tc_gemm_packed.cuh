@@ -71,11 +71,15 @@ template <class Epi>
 struct has_prefetch<Epi, std::void_t<decltype(Epi::kPrefetch)>> : std::integral_constant<bool, Epi::kPrefetch> {};
 #endif
 
+// K elements per 128-byte chunk row of a packed image: 64 bf16 or 32 tf32
+constexpr int chunk_k(bool tf32) { return tf32 ? kBK / 2 : kBK; }
+
 // bytes of a packed operand with `mn` rows (MN extent) and K extent `k`
-inline size_t packed_bytes(int mn, int k, int rows_per_tile) {
+inline size_t packed_bytes(int mn, int k, int rows_per_tile, bool tf32 = false) {
   const size_t tiles = (static_cast<size_t>(mn) + rows_per_tile - 1) / rows_per_tile;
-  const size_t chunks = (static_cast<size_t>(k) + kBK - 1) / kBK;
-  return tiles * chunks * static_cast<size_t>(rows_per_tile) * kBK * 2;
+  const size_t ck = static_cast<size_t>(chunk_k(tf32));
+  const size_t chunks = (static_cast<size_t>(k) + ck - 1) / ck;
+  return tiles * chunks * static_cast<size_t>(rows_per_tile) * 128;
 }
 
 #ifdef __CUDACC__
@@ -120,12 +124,85 @@ __device__ __forceinline__ void pack_range(const Src& src, uint8_t* __restrict__
   }
 }
 
+// TF32 images, always K-major: a chunk row holds 32 K values as eight 16-byte
+// vectors of four. Row sources: one item = 8 consecutive K of one row (two
+// vectors). Transposed (MN-view) sources: one item = 8 consecutive MN x 4
+// consecutive K, transposed in registers into eight vectors (the tf32 MMA
+// reads both operands K-major).
+template <int ROWS, class Src>
+__device__ __forceinline__ void pack_range_tf32(const Src& src, uint8_t* __restrict__ out, int tiles, int nchunks,
+                                                int lim, int64_t first, int64_t stride) {
+  constexpr int CK = chunk_k(true);
+  if constexpr (!Src::kMN) {
+    const int64_t total = static_cast<int64_t>(tiles) * nchunks * (ROWS / 8) * 32;
+    for (int64_t idx = first; idx < total; idx += stride) {
+      const int r8 = static_cast<int>(idx & 7);
+      const int kv2 = static_cast<int>((idx >> 3) & 3);
+      int64_t rest = idx >> 5;
+      const int g = static_cast<int>(rest % (ROWS / 8));
+      rest /= (ROWS / 8);
+      const int kc = static_cast<int>(rest % nchunks);
+      const int t = static_cast<int>(rest / nchunks);
+      if (t * ROWS >= lim) continue;
+      float f[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) f[i] = 0.f;
+      const int row = t * ROWS + g * 8 + r8;
+      if (row < lim) src.load8f(row, kc * (CK / 8) + kv2, lim, f);
+      uint8_t* base = out + (static_cast<int64_t>(t) * nchunks + kc) * (ROWS * 128) + g * 1024 + r8 * 16;
+      *reinterpret_cast<uint4*>(base + (2 * kv2) * 128) = pack_tf32x4(f);
+      *reinterpret_cast<uint4*>(base + (2 * kv2 + 1) * 128) = pack_tf32x4(f + 4);
+    }
+  } else {
+    const int64_t total = static_cast<int64_t>(tiles) * nchunks * (ROWS / 8) * 8;
+    for (int64_t idx = first; idx < total; idx += stride) {
+      const int kq = static_cast<int>(idx & 7);
+      int64_t rest = idx >> 3;
+      const int g = static_cast<int>(rest % (ROWS / 8));
+      rest /= (ROWS / 8);
+      const int kc = static_cast<int>(rest % nchunks);
+      const int t = static_cast<int>(rest / nchunks);
+      if (t * ROWS >= lim) continue;
+      float f[4][8];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) f[j][i] = 0.f;
+      }
+      const int mng = t * (ROWS / 8) + g;
+      if (mng * 8 < lim) {
+#pragma unroll
+        for (int j = 0; j < 4; ++j) src.load8f(mng, kc * CK + kq * 4 + j, lim, f[j]);
+      }
+      uint8_t* base = out + (static_cast<int64_t>(t) * nchunks + kc) * (ROWS * 128) + g * 1024 + kq * 128;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const float v[4] = {f[0][i], f[1][i], f[2][i], f[3][i]};
+        *reinterpret_cast<uint4*>(base + i * 16) = pack_tf32x4(v);
+      }
+    }
+  }
+}
+
+// Work items of pack_range / pack_range_tf32 for an operand of `tiles` x `nchunks` blocks
+template <int ROWS, bool TF32, bool MN>
+constexpr int64_t pack_items(int tiles, int nchunks) {
+  return static_cast<int64_t>(tiles) * nchunks * (ROWS / 8) * (TF32 ? (MN ? 8 : 32) : 64);
+}
+
+template <int ROWS, bool TF32, class Src>
+__device__ __forceinline__ void pack_any(const Src& src, uint8_t* __restrict__ out, int tiles, int nchunks, int lim,
+                                         int64_t first, int64_t stride) {
+  if constexpr (TF32) pack_range_tf32<ROWS>(src, out, tiles, nchunks, lim, first, stride);
+  else pack_range<ROWS>(src, out, tiles, nchunks, lim, first, stride);
+}
+
 // One thread = one 16-byte vector (8 bf16) of the packed image.
 // Vector index -> (tile t, chunk kc, 8-row group g, k-vector kv, r8):
 //   K-major : row = t*ROWS + g*8 + r8, columns [kc*64 + kv*8, +8)
 //   MN-major: MN group t*ROWS/8 + g (8 consecutive MN indices), k = kc*64 + kv*8 + r8
 // both land at block(t, kc) + g*1024 + kv*128 + r8*16.
-template <int ROWS, class Src>
+template <int ROWS, class Src, bool TF32 = false>
 __global__ void __launch_bounds__(256) pack_kernel(const __grid_constant__ Src src, uint8_t* __restrict__ out,
                                                    int tiles, int nchunks, int limit, const int* limit_dev,
                                                    int nrows) {
@@ -133,14 +210,13 @@ __global__ void __launch_bounds__(256) pack_kernel(const __grid_constant__ Src s
   int lim = limit;
   if (limit_dev != nullptr) lim = min(lim, *limit_dev);
   (void)nrows;
-  pack_range<ROWS>(src, out, tiles, nchunks, lim,
-                   static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x,
-                   static_cast<int64_t>(gridDim.x) * blockDim.x);
+  pack_any<ROWS, TF32>(src, out, tiles, nchunks, lim, static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x,
+                       static_cast<int64_t>(gridDim.x) * blockDim.x);
   pdl_launch_dependents();
 }
 
 // Both operands of one GEMM in one launch: blocks [0, blocks_a) pack A, the rest pack B.
-template <int ROWS_A, class SrcA, int ROWS_B, class SrcB>
+template <int ROWS_A, class SrcA, int ROWS_B, class SrcB, bool TF32 = false>
 __global__ void __launch_bounds__(256) pack2_kernel(const __grid_constant__ SrcA a, const __grid_constant__ SrcB b,
                                                     uint8_t* __restrict__ out_a, uint8_t* __restrict__ out_b,
                                                     int tiles_a, int tiles_b, int nchunks, int lim_a,
@@ -149,21 +225,23 @@ __global__ void __launch_bounds__(256) pack2_kernel(const __grid_constant__ SrcA
   if (static_cast<int>(blockIdx.x) < blocks_a) {
     int lim = lim_a;
     if (lim_a_dev != nullptr) lim = min(lim, *lim_a_dev);
-    pack_range<ROWS_A>(a, out_a, tiles_a, nchunks, lim, static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x,
-                       static_cast<int64_t>(blocks_a) * blockDim.x);
+    pack_any<ROWS_A, TF32>(a, out_a, tiles_a, nchunks, lim,
+                           static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x,
+                           static_cast<int64_t>(blocks_a) * blockDim.x);
   } else {
     const int bb = static_cast<int>(blockIdx.x) - blocks_a;
     const int nb = static_cast<int>(gridDim.x) - blocks_a;
-    pack_range<ROWS_B>(b, out_b, tiles_b, nchunks, lim_b, static_cast<int64_t>(bb) * blockDim.x + threadIdx.x,
-                       static_cast<int64_t>(nb) * blockDim.x);
+    pack_any<ROWS_B, TF32>(b, out_b, tiles_b, nchunks, lim_b, static_cast<int64_t>(bb) * blockDim.x + threadIdx.x,
+                           static_cast<int64_t>(nb) * blockDim.x);
   }
   pdl_launch_dependents();
 }
 
-template <int BN, int NSUB, bool AMN, bool BMN, class Epi>
+template <int BN, int NSUB, bool AMN, bool BMN, class Epi, bool TF32 = false>
 __global__ void __launch_bounds__(kPackedThreads, 1)
     tc_gemm_packed_kernel(const uint8_t* __restrict__ pa, const uint8_t* __restrict__ pb,
                           const __grid_constant__ Epi epi, const GemmShape shape, int* status) {
+  static_assert(!TF32 || (!AMN && !BMN), "tf32 operands are packed K-major");
   static_assert(BN % 16 == 0 && BN >= 16 && BN <= 256, "UMMA N for M=128 must be a multiple of 16 in [16, 256]");
   static_assert(NSUB >= 1 && BN * NSUB <= 512, "accumulator exceeds TMEM");
   constexpr int A_BYTES = kBM * kBK * 2;
@@ -175,8 +253,10 @@ __global__ void __launch_bounds__(kPackedThreads, 1)
   // two accumulators when they fit in TMEM: the epilogue of tile i overlaps the MMA of tile i+1
   constexpr int NACC = (2 * B_ROWS <= 512) ? 2 : 1;
   constexpr uint32_t TMEM_COLS = tmem_cols_for(NACC * B_ROWS);
-  constexpr uint32_t IDESC =
-      umma_idesc_bf16_f32(kBM, BN) | (AMN ? (1u << 15) : 0u) | (BMN ? (1u << 16) : 0u);
+  constexpr uint32_t IDESC = TF32 ? umma_idesc_tf32_f32(kBM, BN)
+                                  : (umma_idesc_bf16_f32(kBM, BN) | (AMN ? (1u << 15) : 0u) | (BMN ? (1u << 16) : 0u));
+  constexpr int CK = chunk_k(TF32);        // K elements per chunk (128 bytes per row either way)
+  constexpr int KSTEP = TF32 ? 8 : 16;     // K per MMA instruction (32 bytes per row either way)
 
   extern __shared__ uint8_t smem_dyn[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_dyn) + 1023) & ~uintptr_t(1023));
@@ -221,7 +301,7 @@ __global__ void __launch_bounds__(kPackedThreads, 1)
   if (shape.m_dev != nullptr) M = min(M, *shape.m_dev);
   const int tiles_m = (M + kBM - 1) / kBM;
   const int tiles_n = (shape.N + B_ROWS - 1) / B_ROWS;
-  const int nchunks = (shape.K + kBK - 1) / kBK;
+  const int nchunks = (shape.K + CK - 1) / CK;
   const int ksplit = max(1, shape.ksplit);
   const int cps = (nchunks + ksplit - 1) / ksplit;
   const int total = tiles_m * tiles_n * ksplit;
@@ -331,14 +411,15 @@ __global__ void __launch_bounds__(kPackedThreads, 1)
           tc_fence_after();
           const uint32_t a_base = smem_u32(smemA + s * A_BYTES);
           const uint32_t b_base = smem_u32(smemB + s * B_BYTES);
-          const int ksteps = min(kBK / 16, (shape.K - kc * kBK + 15) / 16);
+          const int ksteps = min(CK / KSTEP, (shape.K - kc * CK + KSTEP - 1) / KSTEP);
           for (int kk = 0; kk < ksteps; ++kk) {
             const uint64_t adesc = umma_desc_kmajor_noswizzle(a_base + kk * 256, 128, 1024);
 #pragma unroll
             for (int sub = 0; sub < NSUB; ++sub) {
               const uint64_t bdesc =
                   umma_desc_kmajor_noswizzle(b_base + sub * (BN / 8) * 1024 + kk * 256, 128, 1024);
-              umma_bf16(acc + sub * BN, adesc, bdesc, IDESC, (kc > kc0 || kk > 0) ? 1u : 0u);
+              if constexpr (TF32) umma_tf32(acc + sub * BN, adesc, bdesc, IDESC, (kc > kc0 || kk > 0) ? 1u : 0u);
+              else umma_bf16(acc + sub * BN, adesc, bdesc, IDESC, (kc > kc0 || kk > 0) ? 1u : 0u);
             }
             issued = true;
           }

@@ -6,6 +6,8 @@ int64_t status_read(bool clear);
 #include <cuda_runtime.h>
 namespace su {
 long long launch_count();
+void set_gemm_precision(bool tf32);
+bool gemm_precision_tf32();
 using WorkspaceAlloc = void* (*)(size_t bytes, cudaStream_t stream);
 using WorkspaceFree = void (*)(void* ptr);
 void set_workspace_allocator(WorkspaceAlloc alloc, WorkspaceFree free_fn);
@@ -171,6 +173,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "starry_unigraph sm_100a kernels (tcgen05 GEMMs, TGN step, DTDG ops, collectives)";
   m.def("status_read", &status_read, "read (and clear) the device status word", py::arg("clear") = true);
   m.def("launch_count", &su::launch_count, "kernel launches issued by this library so far (host-side count)");
+  m.def("set_gemm_precision", &su::set_gemm_precision, "tensor-core operand precision of the GEMMs: tf32 or bf16",
+        py::arg("tf32"));
+  m.def("gemm_precision_tf32", &su::gemm_precision_tf32);
   su::set_workspace_allocator(&su_ws_alloc, &su_ws_free);
   m.def("linear_fwd", &linear_fwd);
   m.def("linear_dgrad", &linear_dgrad);

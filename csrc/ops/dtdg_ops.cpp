@@ -147,7 +147,8 @@ std::vector<at::Tensor> lstm_bwd(const at::Tensor& x, const c10::optional<at::Te
   };
   // Packed path: the backward kernel writes dpre straight into the two bf16 tile
   // images the GEMMs read (no row-major dpre, no packing pass over it)
-  if (H % 32 == 0 && in_dim % 8 == 0 && packed_gemm_enabled() &&
+  // (bf16 images: the tf32 precision takes the fp32 path below)
+  if (H % 32 == 0 && in_dim % 8 == 0 && packed_gemm_enabled() && !gemm_precision_tf32() &&
       lstm_bwd_bf16_ok(gates.data_ptr<float>(), cp_p, c_new.data_ptr<float>(), dh_p, dh_ld, dc_p, dc_ld, H, nullptr,
                        dc_prev.data_ptr<float>())) {
     const int64_t tiles_k = (rows + kBM - 1) / kBM, chunks_mn = (rows + kBK - 1) / kBK;
@@ -182,7 +183,7 @@ std::vector<at::Tensor> lstm_bwd(const at::Tensor& x, const c10::optional<at::Te
   // below read them as bf16 operands either way)
   at::Tensor dpre = at::empty({rows, DP4}, x.options().dtype(at::kBFloat16));
   ASeg dpre_seg;
-  if (lstm_bwd_bf16_ok(gates.data_ptr<float>(), cp_p, c_new.data_ptr<float>(), dh_p, dh_ld, dc_p, dc_ld, H,
+  if (!gemm_precision_tf32() && lstm_bwd_bf16_ok(gates.data_ptr<float>(), cp_p, c_new.data_ptr<float>(), dh_p, dh_ld, dc_p, dc_ld, H,
                        dpre.data_ptr(), dc_prev.data_ptr<float>())) {
     launch_lstm_bwd_bf16(cur_stream(), gates.data_ptr<float>(), cp_p, c_new.data_ptr<float>(), dh_p, dh_ld, dc_p,
                          dc_ld, rows, H, reinterpret_cast<__nv_bfloat16*>(dpre.data_ptr()),

@@ -122,7 +122,8 @@ def build_ctdg_runtime(session_ctx: SessionContext, dataset: TGTemporalDataset |
                                policy=str(sampling["strategy"]), lr=lr, dropout=float(c.get("dropout", 0.1)),
                                att_dropout=float(c.get("att_dropout", 0.1)), num_head=int(c.get("num_head", 2)),
                                seed=seed, use_graphs=bool(cfg["runtime"].get("cuda_graphs", True)),
-                               grad_sync=grad_sync, peer=peer)
+                               grad_sync=grad_sync, peer=peer,
+                               precision=str(cfg["runtime"].get("precision", "tf32")))
         optimizer = engine.opt
     else:
         optimizer = torch.optim.Adam(list(model.parameters()) + [p for p in updater.parameters() if p.requires_grad],

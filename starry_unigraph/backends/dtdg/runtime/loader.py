@@ -83,13 +83,13 @@ class STGraphLoader:
             for i in range(len(self)):
                 states = RNNStateManager(ends_list=[None], mode="pad", disable_routes=disable_routes)
                 states.add(self.fetch_graph(i, perm=perm))
-                yield STGraphBlob(states)
+                yield states.snapshot()
         else:
             states = RNNStateManager(ends_list=ends_list, mode="pad" if disable_states else "mix",
                                      disable_routes=disable_routes)
             for i in range(len(self)):
                 states.add(self.fetch_graph(i, perm=perm))
-                yield STGraphBlob(states)
+                yield states.snapshot()  # frozen: the window stays valid after the loader slides on
 
     def __iter__(self):
         yield from self.__call__()
@@ -106,7 +106,6 @@ class STGraphLoader:
         if self.size == 1 or disable_routes:
             block.route = None
         block.flare_snapshot_id = index
-        block.flare_rnn_state_idx = 1
         block.flare_is_full_snapshot = ends is None
         return block
 

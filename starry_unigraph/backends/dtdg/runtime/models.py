@@ -1,17 +1,24 @@
-"""Flare DTDG models (reference backends/dtdg/runtime/models.py:31-295).
+"""Flare DTDG models (reference equations and parameter names:
+backends/dtdg/runtime/models.py:102-248; the names are kept so checkpoints load
+across the two frameworks).
 
-* ``FlareEvolveGCN`` (EvolveGCN): W_t = MatGRU(W_{t-1}, pool_proj(mean(x))),
-  out = Linear((A x) W_t).
-* ``FlareTGCN`` (T-GCN; also serves ``gcn``): urc = GCNStack(F -> 3h), GRU-style
-  gates u, r, c, h' = u h + (1 - u) c, out = Linear(h).
-* ``FlareMPNNLSTM`` (MPNN-LSTM): GCNStack(F -> h, 2 layers) then two stacked
-  LSTM cells, state (h1, c1, h2, c2) carried through the window's state manager.
+* ``FlareEvolveGCN`` (EvolveGCN): the GCN weight evolves by a matrix GRU driven by
+  a pooled graph context, W_t = MatGRU(W_{t-1}, pool_proj(mean(x))); the output
+  head reads (A x) W_t.
+* ``FlareTGCN`` (T-GCN, also ``gcn``): a two-layer GCN produces [u | r | c] of width
+  3h; a reset-gated GRU cell updates h; the head reads h.
+* ``FlareMPNNLSTM`` (MPNN-LSTM): a two-layer GCN of width h feeds two stacked LSTM
+  cells whose four state tensors (h1, c1, h2, c2) travel with the window.
+
+A model takes a window (``STGraphBlob``) or one graph. Over a window it walks
+the window's steps; each step hands the carried state to its slot
+(``step.fetch``: padded / mixed to the graph's rows) and back (``step.store``).
 Every dense layer runs on the tcgen05 GEMM on CUDA (``starry_unigraph.ops.dtdg``).
 """
 from __future__ import annotations
 
 from dataclasses import dataclass
-from typing import Any
+from typing import Any, Callable
 
 import torch
 import torch.nn as nn
@@ -20,19 +27,12 @@ from starry_unigraph.ops.dtdg import linear, rgru_cell
 from starry_unigraph.runtime.modules import GCNStack, MatGRUCell, _LSTMCell
 from starry_unigraph.runtime.modules.gcn_layers import _gcn_message_pass, _graph_input
 
-from .state import STGraphBlob
+from .state import STGraphBlob, graph_steps
 
 
-def _graph_sequence(blob_or_graph) -> list[Any]:
-    return list(blob_or_graph) if isinstance(blob_or_graph, STGraphBlob) else [blob_or_graph]
-
-
-def _graph_labels(graph) -> torch.Tensor | None:
-    if "y" in graph.dstdata:
-        return graph.dstdata["y"]
-    if "y" in graph.srcdata:
-        return graph.srcdata["y"][: graph.num_dst_nodes]
-    return None
+def _collect(blob_or_graph: Any, outputs: list[torch.Tensor]):
+    """Per-step outputs for a window, the last output for a single graph."""
+    return outputs if isinstance(blob_or_graph, STGraphBlob) else outputs[-1]
 
 
 class FlareEvolveGCN(nn.Module):
@@ -44,19 +44,19 @@ class FlareEvolveGCN(nn.Module):
         self.pool_proj = nn.Linear(input_size, input_size)
         self.out = nn.Linear(hidden_size, output_size)
 
-    def _pool_graph_context(self, graph) -> torch.Tensor:
-        x = _graph_input(graph).float()[: graph.num_dst_nodes]
-        return linear(x.mean(dim=0, keepdim=True), self.pool_proj.weight, self.pool_proj.bias)
+    def _context(self, graph: Any) -> torch.Tensor:
+        rows = _graph_input(graph).float()[: graph.num_dst_nodes]
+        return linear(rows.mean(dim=0, keepdim=True), self.pool_proj.weight, self.pool_proj.bias)
 
-    def forward(self, blob_or_graph, state: torch.Tensor | None = None):
-        weights = self.initial_weight if state is None else state
-        outputs = []
-        for graph in _graph_sequence(blob_or_graph):
-            weights = self.mat_gru(weights, self._pool_graph_context(graph))
-            agg = _gcn_message_pass(graph, _graph_input(graph).float())
-            h = linear(agg, weights.t().contiguous())
-            outputs.append(linear(h, self.out.weight, self.out.bias))
-        return (outputs if isinstance(blob_or_graph, STGraphBlob) else outputs[-1]), weights
+    def forward(self, blob_or_graph: Any, state: torch.Tensor | None = None):
+        w = state if state is not None else self.initial_weight
+        preds = []
+        for step in graph_steps(blob_or_graph):
+            g = step.graph
+            w = self.mat_gru(w, self._context(g))
+            hidden = linear(_gcn_message_pass(g, _graph_input(g).float()), w.t().contiguous())
+            preds.append(linear(hidden, self.out.weight, self.out.bias))
+        return _collect(blob_or_graph, preds), w
 
 
 class FlareTGCN(nn.Module):
@@ -69,20 +69,24 @@ class FlareTGCN(nn.Module):
         self.c_t = nn.Linear(hidden_size * 2, hidden_size)
         self.out = nn.Linear(hidden_size, output_size)
 
-    def forward(self, blob_or_graph, state: torch.Tensor | None = None):
-        outputs = []
+    def _cell(self, urc: torch.Tensor, h: torch.Tensor) -> torch.Tensor:
+        xu, xr, xc = urc.chunk(3, dim=-1)
+        return rgru_cell(xu, xr, xc, h, self.u_t.weight, self.u_t.bias, self.r_t.weight, self.r_t.bias,
+                         self.c_t.weight, self.c_t.bias)
+
+    def forward(self, blob_or_graph: Any, state: torch.Tensor | None = None):
+        steps = graph_steps(blob_or_graph)
+        gates = self.gcn.layerwise(blob_or_graph)
         h = state
-        for graph, urc in zip(_graph_sequence(blob_or_graph), self.gcn.layerwise(blob_or_graph)):
-            h = graph.flare_fetch_state(h) if hasattr(graph, "flare_fetch_state") and h is not None else h
+        preds = []
+        for step, urc in zip(steps, gates):
+            h = step.fetch(h)
             if h is None:
-                h = torch.zeros(urc.size(0), self.hidden_size, dtype=urc.dtype, device=urc.device)
-            u, r, c = urc.chunk(3, dim=-1)
-            h = rgru_cell(u, r, c, h, self.u_t.weight, self.u_t.bias, self.r_t.weight, self.r_t.bias,
-                          self.c_t.weight, self.c_t.bias)
-            if hasattr(graph, "flare_store_state"):
-                graph.flare_store_state(h)
-            outputs.append(linear(h, self.out.weight, self.out.bias))
-        return (outputs if isinstance(blob_or_graph, STGraphBlob) else outputs[-1]), h
+                h = urc.new_zeros(urc.size(0), self.hidden_size)
+            h = self._cell(urc, h)
+            step.store(h)
+            preds.append(linear(h, self.out.weight, self.out.bias))
+        return _collect(blob_or_graph, preds), h
 
 
 class FlareMPNNLSTM(nn.Module):
@@ -93,19 +97,25 @@ class FlareMPNNLSTM(nn.Module):
         self.rnn = nn.ModuleList([_LSTMCell(hidden_size, hidden_size), _LSTMCell(hidden_size, hidden_size)])
         self.out = nn.Linear(hidden_size, output_size)
 
-    def forward(self, blob_or_graph, state=None):
-        outputs = []
-        h = state
-        for graph, x in zip(_graph_sequence(blob_or_graph), self.gcn.layerwise(blob_or_graph)):
-            h = graph.flare_fetch_state(h)
-            s1 = None if h is None else h[0:2]
-            s2 = None if h is None else h[2:4]
-            x, _ = s1 = self.rnn[0](x, s1)
-            x, _ = s2 = self.rnn[1](x, s2)
-            h = tuple(s1) + tuple(s2)
-            graph.flare_store_state(h)
-            outputs.append(linear(x, self.out.weight, self.out.bias))
-        return (outputs if isinstance(blob_or_graph, STGraphBlob) else outputs[-1]), h
+    def _stack(self, x: torch.Tensor, carried: Any):
+        """Both LSTM layers on one snapshot; `carried` is (h1, c1, h2, c2) or None."""
+        states = []
+        for layer, cell in enumerate(self.rnn):
+            prev = None if carried is None else tuple(carried[2 * layer: 2 * layer + 2])
+            x, c = cell(x, prev)
+            states.extend((x, c))
+        return x, tuple(states)
+
+    def forward(self, blob_or_graph: Any, state: Any = None):
+        steps = graph_steps(blob_or_graph)
+        feats = self.gcn.layerwise(blob_or_graph)
+        carried = state
+        preds = []
+        for step, x in zip(steps, feats):
+            top, carried = self._stack(x, step.fetch(carried))
+            step.store(carried)
+            preds.append(linear(top, self.out.weight, self.out.bias))
+        return _collect(blob_or_graph, preds), carried
 
 
 @dataclass(frozen=True)
@@ -113,26 +123,26 @@ class FlareModelSpec:
     model_cls: type[nn.Module]
 
 
-MODEL_SPECS: dict[str, FlareModelSpec] = {
-    "evolvegcn": FlareModelSpec(FlareEvolveGCN),
-    "tgcn": FlareModelSpec(FlareTGCN),
-    "mpnn_lstm": FlareModelSpec(FlareMPNNLSTM),
-    "gcn": FlareModelSpec(FlareTGCN),
-}
+# registry names of the reference (``gcn`` runs T-GCN)
+MODEL_SPECS: dict[str, FlareModelSpec] = {name: FlareModelSpec(cls) for name, cls in (
+    ("evolvegcn", FlareEvolveGCN), ("tgcn", FlareTGCN), ("mpnn_lstm", FlareMPNNLSTM), ("gcn", FlareTGCN))}
 
 
 def build_flare_model(model_name: str, input_size: int, hidden_size: int, output_size: int) -> nn.Module:
-    key = model_name.lower()
-    if key not in MODEL_SPECS:
-        raise KeyError(f"Unsupported flare model: {model_name}")
-    return MODEL_SPECS[key].model_cls(input_size=input_size, hidden_size=hidden_size, output_size=output_size)
+    spec = MODEL_SPECS.get(model_name.lower())
+    if spec is None:
+        raise KeyError(f"Unsupported flare model: {model_name} (known: {sorted(MODEL_SPECS)})")
+    return spec.model_cls(input_size=input_size, hidden_size=hidden_size, output_size=output_size)
 
 
-def extract_graph_labels(blob_or_graph) -> torch.Tensor | None:
-    graphs = _graph_sequence(blob_or_graph)
-    if not graphs:
+def extract_graph_labels(blob_or_graph: Any) -> torch.Tensor | None:
+    steps = graph_steps(blob_or_graph)
+    if not steps:
         return None
-    y = _graph_labels(graphs[-1])
+    g = steps[-1].graph
+    y = g.dstdata.get("y")
+    if y is None and "y" in g.srcdata:
+        y = g.srcdata["y"][: g.num_dst_nodes]
     if y is None:
         return None
     return y.view(-1, 1) if y.dim() == 1 else y

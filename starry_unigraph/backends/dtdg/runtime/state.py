@@ -1,19 +1,28 @@
-"""RNN state management over a sliding window of snapshots
-(reference backends/dtdg/runtime/state.py:22-346).
+"""Sliding training windows of snapshot graphs and the RNN state carried between
+them (reference behaviour: backends/dtdg/runtime/state.py:22-346).
 
-``RNNStateManager`` keeps the window's graphs and patches each with
-``flare_fetch_state`` / ``flare_store_state``:
-  * ``pad``: state rows are zero-padded / truncated to the graph's node count
-    (and forgotten between steps),
-  * ``mix``: missing rows are filled from the detached state stored for that
-    window slot in the previous step.
-Older window slots may be truncated to the first ``end`` nodes of the
-chunk-permuted order (temporal decay); truncated graphs drop their halo.
+A window has ``len(ends_list)`` slots, the newest snapshot in the last slot.
+Slot ``s`` may truncate its graph to the first ``ends_list[s]`` nodes of the
+chunk-permuted order (temporal decay; ``None`` keeps the whole graph, and a
+truncated graph drops its halo). Every slot also owns a state cell:
+
+* ``pad``: a slot's incoming state is zero-padded or cut to the graph's rows and
+  nothing is remembered between windows;
+* ``mix``: rows missing from the incoming state are taken from the detached
+  state this slot produced in the previous window.
+
+Design: the slot states live in ``RNNStateManager`` (owned by the loader that
+slides the window); graphs are never modified. ``add`` returns nothing, and
+``snapshot()`` freezes the current window into an ``STGraphBlob`` whose steps
+carry explicit ``fetch`` / ``store`` closures bound to their slot, so a blob kept
+for later (a pre-built list of windows, a captured CUDA graph) still describes
+its own window after the loader has moved on.
 """
 from __future__ import annotations
 
-import types
-from typing import Any
+from collections import deque
+from dataclasses import dataclass, field
+from typing import Any, Callable
 
 import torch
 import torch.nn.functional as F
@@ -22,166 +31,206 @@ from torch import Tensor
 from starry_unigraph.data.partition import SnapshotBlock
 
 
+# ---------------------------------------------------------------------------
+# state transforms (tensor, tuple / list or dict of tensors)
+# ---------------------------------------------------------------------------
+def _map_state(fn: Callable[..., Any], state: Any, other: Any = None) -> Any:
+    if isinstance(state, dict):
+        return {k: _map_state(fn, v, None if other is None else other[k]) for k, v in state.items()}
+    if isinstance(state, (tuple, list)):
+        parts = [_map_state(fn, s, None if other is None else other[i]) for i, s in enumerate(state)]
+        return tuple(parts) if isinstance(state, tuple) else parts
+    if not isinstance(state, Tensor):
+        return state
+    return fn(state) if other is None else fn(state, other)
+
+
+def _fit_rows(t: Tensor, rows: int) -> Tensor:
+    """First `rows` rows of `t`, zero rows appended when it is shorter."""
+    if t.size(0) >= rows:
+        return t[:rows]
+    return F.pad(t, [0, 0] * (t.dim() - 1) + [0, rows - t.size(0)])
+
+
+def _complete_rows(cur: Tensor, old: Tensor, rows: int) -> Tensor:
+    """`cur` extended to `rows` rows with the rows of `old` that follow it."""
+    if cur.size(0) >= rows:
+        return cur[:rows]
+    tail = _fit_rows(old[cur.size(0):], rows - cur.size(0))
+    return torch.cat([cur, tail], dim=0)
+
+
+@dataclass
+class WindowStep:
+    """One snapshot of a frozen window: its (possibly truncated) graph and the
+    state hooks of the slot it occupies."""
+
+    graph: Any
+    slot: int
+    snapshot_id: int
+    full: bool
+    fetch: Callable[[Any], Any]
+    store: Callable[[Any], None]
+
+
+def _identity(state: Any) -> Any:
+    return state
+
+
+def _discard(state: Any) -> None:
+    return None
+
+
+def graph_steps(blob_or_graph: Any) -> list[WindowStep]:
+    """The steps of a window, or one stateless step for a bare graph."""
+    if isinstance(blob_or_graph, STGraphBlob):
+        return list(blob_or_graph.steps)
+    g = blob_or_graph
+    return [WindowStep(g, -1, int(getattr(g, "flare_snapshot_id", -1)), True, _identity, _discard)]
+
+
 class RNNStateManager:
+    """Window slots (truncation + carried state) of one training pass."""
+
     def __init__(self, ends_list: list[int | None], mode: str = "pad", disable_routes: bool = False) -> None:
-        ends_list = [e for e in ends_list if e is None or e > 0]
-        self._ends_list = ends_list
-        self._state_list: list[Any] = [None] * len(ends_list)
-        self._graph_list: list[Any] = []
-        self._mode = mode
-        self._disable_routes = disable_routes
-        self._snapshot_count = 0
+        if mode not in ("pad", "mix"):
+            raise ValueError(f"Unknown mode: {mode}")
+        self.ends: list[int | None] = [e for e in ends_list if e is None or e > 0] or [None]
+        self.mode = mode
+        self.disable_routes = bool(disable_routes)
+        self.cells: list[Any] = [None] * len(self.ends)   # carried state per slot (mix mode)
+        self._graphs: deque = deque(maxlen=len(self.ends))
+        self._views: dict[tuple[int, int | None], Any] = {}  # (id(graph), end) -> truncated view
+        self._next_id = 0
+
+    @property
+    def _mode(self) -> str:  # name the step-graph capture checks
+        return self.mode
+
+    @property
+    def capacity(self) -> int:
+        return len(self.ends)
+
+    def add(self, graph: Any) -> None:
+        """Slide the window by one snapshot (the oldest leaves when the window is full)."""
+        if getattr(graph, "flare_snapshot_id", None) is None:
+            graph.flare_snapshot_id = self._next_id
+        self._next_id += 1
+        if len(self._graphs) == self._graphs.maxlen:
+            gone = self._graphs[0]
+            for key in [k for k in self._views if k[0] == id(gone)]:
+                del self._views[key]
+        self._graphs.append(graph)
+
+    def slot_of(self, position: int) -> int:
+        """Slot of the window's `position`-th graph (0 = oldest present)."""
+        return self.capacity - len(self._graphs) + position
+
+    def _view(self, graph: Any, end: int | None) -> Any:
+        if end is None and not self.disable_routes:
+            return graph
+        key = (id(graph), end)
+        if key not in self._views:
+            self._views[key] = truncate_block(graph, end)
+        return self._views[key]
+
+    def fetch(self, slot: int, state: Any, rows: int) -> Any:
+        old = self.cells[slot]
+        if state is None and old is None:
+            return None
+        if self.mode == "pad" or old is None:
+            return _map_state(lambda t: _fit_rows(t, rows), state)
+        return _map_state(lambda cur, prev: _complete_rows(cur, prev, rows), state, old)
+
+    def store(self, slot: int, state: Any) -> None:
+        self.cells[slot] = _map_state(lambda t: t.detach(), state) if self.mode == "mix" else None
+
+    def snapshot(self) -> "STGraphBlob":
+        steps = []
+        for pos, graph in enumerate(self._graphs):
+            slot = self.slot_of(pos)
+            end = self.ends[slot]
+            view = self._view(graph, end)
+            rows = int(view.num_dst_nodes)
+            steps.append(WindowStep(
+                graph=view, slot=slot, snapshot_id=int(graph.flare_snapshot_id), full=end is None,
+                fetch=lambda state, s=slot, n=rows: self.fetch(s, state, n),
+                store=lambda state, s=slot: self.store(s, state)))
+        return STGraphBlob(self, steps)
+
+    # helpers kept under the reference's names for callers of the old static API
+    @staticmethod
+    def state_detach(state: Any) -> Any:
+        return _map_state(lambda t: t.detach(), state)
+
+    @staticmethod
+    def state_padding(state: Any, end: int) -> Any:
+        return _map_state(lambda t: _fit_rows(t, end), state)
+
+    @staticmethod
+    def state_mixing(state: Any, old_state: Any, end: int) -> Any:
+        return _map_state(lambda cur, prev: _complete_rows(cur, prev, end), state, old_state)
 
     def __len__(self) -> int:
-        return len(self._graph_list)
+        return len(self._graphs)
 
     def __getitem__(self, i: int) -> Any:
-        return self._graph_list[i]
-
-    @classmethod
-    def patch_dummy_methods(cls, g: Any) -> Any:
-        g.flare_snapshot_id = getattr(g, "flare_snapshot_id", -1)
-        g.flare_rnn_state_idx = -1
-        g.flare_is_full_snapshot = True
-        g.flare_fetch_state = types.MethodType(lambda self, x, end=None: x, g)
-        g.flare_store_state = types.MethodType(lambda self, x: None, g)
-        return g
-
-    def add(self, g: Any) -> None:
-        while len(self._graph_list) >= len(self._state_list):
-            self._graph_list.pop(0)
-        self._graph_list = [self._patch(h) for h in self._graph_list]
-        self._graph_list.append(self._patch(g))
-
-    def _patch(self, g: Any) -> Any:
-        snap = getattr(g, "flare_snapshot_id", None)
-        if snap is None:
-            snap = self._snapshot_count
-            self._snapshot_count += 1
-        idx = getattr(g, "flare_rnn_state_idx", len(self._ends_list)) - 1
-        end = self._ends_list[idx]
-        if self._disable_routes or end is not None:
-            base = getattr(g, "_untruncated", g)
-            g = self._truncate_graph(base, end)
-            g._untruncated = base
-        g.flare_rnn_state_idx = idx
-        g.flare_fetch_state = types.MethodType(self._fetch, g)
-        g.flare_store_state = types.MethodType(self._store, g)
-        g.flare_snapshot_id = snap
-        g.flare_is_full_snapshot = end is None
-        return g
-
-    def _fetch(self, this: Any, state: Any, end: int | None = None) -> Any:
-        old = self._state_list[this.flare_rnn_state_idx]
-        if end is None:
-            end = this.num_dst_nodes
-        if old is None or self._mode == "pad":
-            return self.state_padding(state, end)
-        if self._mode == "mix":
-            return self.state_mixing(state, old, end)
-        raise ValueError(f"Unknown mode: {self._mode}")
-
-    def _store(self, this: Any, state: Any) -> None:
-        if self._mode == "pad":
-            self._state_list[this.flare_rnn_state_idx] = None
-        elif self._mode == "mix":
-            self._state_list[this.flare_rnn_state_idx] = self.state_detach(state)
-        else:
-            raise ValueError(f"Unknown mode: {self._mode}")
-
-    @classmethod
-    def apply_state(cls, fn, state: Any, old_state: Any = None) -> Any:
-        if isinstance(state, (tuple, list)):
-            olds = old_state if old_state is not None else [None] * len(state)
-            res = [fn(s, t) if old_state is not None else fn(s) for s, t in zip(state, olds)]
-            return tuple(res) if isinstance(state, tuple) else res
-        if isinstance(state, dict):
-            return {k: (fn(v, old_state[k]) if old_state is not None else fn(v)) for k, v in state.items()}
-        return fn(state) if old_state is None else fn(state, old_state)
-
-    @classmethod
-    def state_detach(cls, state: Any) -> Any:
-        return cls.apply_state(lambda s: s.detach() if isinstance(s, Tensor) else s, state)
-
-    @classmethod
-    def state_padding(cls, state: Any, end: int) -> Any:
-        def pad(s):
-            if not isinstance(s, Tensor):
-                return s
-            n = s.size(0)
-            if n > end:
-                return s[:end]
-            if n < end:
-                return F.pad(s, [0] * (s.dim() * 2 - 1) + [end - n])
-            return s
-
-        return cls.apply_state(pad, state)
-
-    @classmethod
-    def state_mixing(cls, state: Any, old_state: Any, end: int) -> Any:
-        def mix(cur, old):
-            if not isinstance(cur, Tensor):
-                return cur
-            if cur.size(0) >= end:
-                return cur[:end]
-            need = end - cur.size(0)
-            tail = old[cur.size(0):end] if old.size(0) >= end else \
-                F.pad(old[cur.size(0):], [0] * (old.dim() * 2 - 1) + [end - old.size(0)])
-            return torch.cat([cur, tail[:need]], dim=0)
-
-        return cls.apply_state(mix, state, old_state)
-
-    @classmethod
-    def _truncate_graph(cls, g: SnapshotBlock, end: int | None) -> SnapshotBlock:
-        n_dst = g.num_dst_nodes
-        end = n_dst if end is None else min(end, n_dst)
-        keep = (g.edge_src < end) & (g.edge_dst < end)
-        out = SnapshotBlock(num_src_nodes=end, num_dst_nodes=end, edge_src=g.edge_src[keep], edge_dst=g.edge_dst[keep])
-        for k, v in g.srcdata.items():
-            out.dstdata[k] = v[:end]
-        for k, v in g.dstdata.items():
-            out.dstdata[k] = v[:end]
-        for k, v in g.edata.items():
-            out.edata[k] = v[keep]
-        out.route = None
-        out.is_block = False
-        out.graph_meta = dict(g.graph_meta)
-        return out
+        return self.snapshot().steps[i].graph
 
 
+def truncate_block(g: SnapshotBlock, end: int | None) -> SnapshotBlock:
+    """The block restricted to its first `end` destination nodes (and the edges
+    among them), without halo rows or route."""
+    keep_n = g.num_dst_nodes if end is None else min(int(end), g.num_dst_nodes)
+    edge_mask = (g.edge_src < keep_n) & (g.edge_dst < keep_n)
+    out = SnapshotBlock(num_src_nodes=keep_n, num_dst_nodes=keep_n, edge_src=g.edge_src[edge_mask],
+                        edge_dst=g.edge_dst[edge_mask])
+    for table in (g.srcdata, g.dstdata):
+        for name, value in table.items():
+            out.dstdata[name] = value[:keep_n]
+    out.edata.update({name: value[edge_mask] for name, value in g.edata.items()})
+    out.route = None
+    out.is_block = False
+    out.graph_meta = dict(g.graph_meta)
+    out.flare_snapshot_id = getattr(g, "flare_snapshot_id", -1)
+    return out
+
+
+@dataclass
 class STWindowState:
-    def __init__(self, full_snapshot_limit: int = 1) -> None:
-        self.full_snapshot_limit = full_snapshot_limit
+    full_snapshot_limit: int = 1
 
     def describe(self) -> dict[str, Any]:
         return {"full_snapshot_limit": self.full_snapshot_limit}
 
 
+@dataclass
 class STGraphBlob:
-    def __init__(self, state: RNNStateManager) -> None:
-        self.state = state
+    """A frozen window: its steps (graphs + slot hooks) in time order."""
+
+    state: RNNStateManager
+    steps: list[WindowStep] = field(default_factory=list)
 
     def __len__(self) -> int:
-        return len(self.state)
+        return len(self.steps)
 
     def __getitem__(self, idx: int) -> Any:
-        return self.state[idx]
+        return self.steps[idx].graph
 
     def __iter__(self):
-        for i in range(len(self)):
-            yield self.state[i]
+        return (s.graph for s in self.steps)
 
     @property
     def current_graph(self) -> Any:
-        return self.state[-1]
+        return self.steps[-1].graph
 
     @property
     def flare_is_full_snapshot(self) -> bool:
-        return bool(getattr(self.current_graph, "flare_is_full_snapshot", True))
+        return self.steps[-1].full if self.steps else True
 
     @property
     def snapshot_index(self) -> int:
-        return int(getattr(self.current_graph, "flare_snapshot_id", 0))
+        return self.steps[-1].snapshot_id if self.steps else 0
 
     def describe(self) -> dict[str, Any]:
         return {"len": len(self), "snapshot_index": self.snapshot_index, "is_full_snapshot": self.flare_is_full_snapshot}

@@ -19,7 +19,7 @@ from starry_unigraph.types import RuntimeBundle, SessionContext
 
 from .models import build_flare_model
 from .session_loader import DTDGBatch
-from .state import RNNStateManager, STGraphBlob
+from .state import STGraphBlob
 
 
 def _infer_dims(partition_data: Any) -> tuple[int, int]:
@@ -125,6 +125,10 @@ def init_flare_training(runtime: RuntimeBundle, session_ctx: SessionContext, par
     graphs_ok = dev.type == "cuda" and bool(cfg.get("runtime", {}).get("cuda_graphs", True)) and \
         (world == 1 or comm == "p2p")
     runtime.state["cuda_graphs"] = graphs_ok
+    precision = str(cfg.get("runtime", {}).get("precision", "tf32"))
+    if precision not in ("tf32", "bf16"):
+        raise ValueError(f"runtime.precision must be tf32 or bf16, got {precision!r}")
+    runtime.state["precision_tf32"] = (precision == "tf32") if dev.type == "cuda" else None
     runtime.state["step_graphs"] = StepGraphs(dev) if graphs_ok else None
 
 
@@ -139,9 +143,20 @@ def _get_labels(graph: Any) -> torch.Tensor | None:
 
 
 def _forward_single_graph(runtime: RuntimeBundle, graph: Any, state: Any):
-    graph = RNNStateManager.patch_dummy_methods(graph)
+    """One snapshot outside a window (evaluation): the state passes through unchanged."""
     model = runtime.model.module if hasattr(runtime.model, "module") else runtime.model
     return model(graph, state)
+
+
+def _precision(runtime: RuntimeBundle):
+    """Context selecting the run's tensor-core operand precision (no-op on CPU)."""
+    from contextlib import nullcontext
+
+    if runtime.state.get("precision_tf32") is None:
+        return nullcontext()
+    from starry_unigraph.ops import gemm_precision
+
+    return gemm_precision(bool(runtime.state["precision_tf32"]))
 
 
 def _loss_and_predictions(runtime: RuntimeBundle, blob_or_batch, training: bool, need_host: bool = True):
@@ -210,13 +225,12 @@ class StepGraphs:
     def supported(runtime: RuntimeBundle, blob: Any) -> bool:
         if not isinstance(blob, STGraphBlob) or not bool(runtime.state.get("cuda_graphs", False)):
             return False
-        state = blob.state
-        return getattr(state, "_mode", "pad") == "pad"
+        return getattr(blob.state, "mode", "pad") == "pad"
 
     @staticmethod
     def key(blob: Any) -> tuple:
-        return tuple((int(getattr(g, "flare_snapshot_id", -1)), int(g.num_src_nodes), int(g.num_dst_nodes),
-                      int(g.num_edges())) for g in blob)
+        return tuple((st.snapshot_id, st.slot, int(st.graph.num_src_nodes), int(st.graph.num_dst_nodes),
+                      int(st.graph.num_edges())) for st in blob.steps)
 
     @staticmethod
     def _prepare(blob: Any) -> None:
@@ -229,10 +243,11 @@ class StepGraphs:
                 hc.pull_plan(g, g.num_dst_nodes)
 
     def _step(self, runtime: RuntimeBundle, blob: Any):
-        loss, preds, targets = _loss_and_predictions(runtime, blob, training=True, need_host=False)
-        runtime.optimizer.zero_grad(set_to_none=True)
-        loss.backward()
-        runtime.optimizer.step()
+        with _precision(runtime):
+            loss, preds, targets = _loss_and_predictions(runtime, blob, training=True, need_host=False)
+            runtime.optimizer.zero_grad(set_to_none=True)
+            loss.backward()
+            runtime.optimizer.step()
         return loss.detach(), preds, targets
 
     def run(self, runtime: RuntimeBundle, blob: Any):
@@ -273,12 +288,13 @@ def run_flare_train_step(runtime: RuntimeBundle, batch: Any, kernel_output: dict
         return {"loss": float(loss.item()) if need_host else loss, "predictions": preds, "targets": targets,
                 "meta": kernel_output.get("meta", {}) | {"model": runtime.state["flare_model"],
                                                           "sequence_state": "updated", "cuda_graph": True}}
-    loss, preds, targets = _loss_and_predictions(runtime, batch, training=True, need_host=need_host)
-    if loss is None:
-        raise RuntimeError("Training labels are required for flare_native train_step")
-    runtime.optimizer.zero_grad(set_to_none=True)
-    loss.backward()
-    runtime.optimizer.step()
+    with _precision(runtime):
+        loss, preds, targets = _loss_and_predictions(runtime, batch, training=True, need_host=need_host)
+        if loss is None:
+            raise RuntimeError("Training labels are required for flare_native train_step")
+        runtime.optimizer.zero_grad(set_to_none=True)
+        loss.backward()
+        runtime.optimizer.step()
     return {"loss": float(loss.detach().item()) if need_host else loss.detach(), "predictions": preds,
             "targets": targets,
             "meta": kernel_output.get("meta", {}) | {"model": runtime.state["flare_model"],
@@ -286,7 +302,7 @@ def run_flare_train_step(runtime: RuntimeBundle, batch: Any, kernel_output: dict
 
 
 def run_flare_eval_step(runtime: RuntimeBundle, batch: Any, kernel_output: dict[str, Any]) -> dict[str, Any]:
-    with torch.no_grad():
+    with torch.no_grad(), _precision(runtime):
         if getattr(batch, "chain", "") == "snapshot_warmup":
             _, new_state = _forward_single_graph(runtime, batch.graph, runtime.state.get("eval_rnn_state"))
             runtime.state["eval_rnn_state"] = new_state
@@ -304,7 +320,7 @@ def run_flare_eval_step(runtime: RuntimeBundle, batch: Any, kernel_output: dict[
 
 
 def run_flare_predict_step(runtime: RuntimeBundle, batch: Any, kernel_output: dict[str, Any]) -> dict[str, Any]:
-    with torch.no_grad():
+    with torch.no_grad(), _precision(runtime):
         if getattr(batch, "chain", "") == "snapshot_warmup":
             _, new_state = _forward_single_graph(runtime, batch.graph, runtime.state.get("eval_rnn_state"))
             runtime.state["eval_rnn_state"] = new_state

@@ -9,6 +9,7 @@ partitioner) or None when it was not built.
 from __future__ import annotations
 
 import importlib
+from contextlib import contextmanager
 from functools import lru_cache
 
 import torch
@@ -58,3 +59,18 @@ def check_status(clear: bool = True) -> None:
                  4: "TMEM drain wait timed out", 5: "index out of range", 6: "peer flag wait timed out",
                  7: "size above compiled bound"}
         raise RuntimeError(f"device status {code}: {names.get(code, 'unknown')}")
+
+
+@contextmanager
+def gemm_precision(tf32: bool):
+    """Run the enclosed GEMM launches with tf32 (True) or bf16 (False) tensor-core
+    operands and restore the previous setting afterwards. The setting is
+    process-wide (autograd issues backward kernels from its own threads), so a
+    step that selects its precision this way leaves other callers unaffected."""
+    C = cuda_ext()
+    prev = bool(C.gemm_precision_tf32())
+    C.set_gemm_precision(bool(tf32))
+    try:
+        yield
+    finally:
+        C.set_gemm_precision(prev)

@@ -34,7 +34,7 @@ class _TracingOps:
 
     def __getattr__(self, name: str):
         fn = getattr(self._C, name)
-        if not callable(fn) or name in ("launch_count", "status_read"):
+        if not callable(fn) or name in ("launch_count", "status_read", "set_gemm_precision", "gemm_precision_tf32"):
             return fn
 
         def traced(*args, **kwargs):
@@ -91,8 +91,13 @@ class TGNCudaEngine:
         use_graphs: bool = True,
         grad_sync: Callable[[torch.Tensor], float] | None = None,
         peer: Any = None,
+        precision: str = "tf32",
     ) -> None:
         self.C = cuda_ext()
+        if precision not in ("tf32", "bf16"):
+            raise ValueError(f"runtime.precision must be tf32 or bf16, got {precision!r}")
+        # tensor-core operand precision of every GEMM of the step (fp32 storage and accumulation)
+        self.tf32 = precision == "tf32"
         self.model = model
         self.updater = updater
         self.memory = memory
@@ -282,8 +287,17 @@ class TGNCudaEngine:
             self._peer_sync(train)
 
     def _forward(self, split: str, train: bool) -> None:
-        if self.kind == "jodie":
-            return self._forward_jodie(split, train)
+        # host-side precision switch: picks the kernels issued (and captured) below, then restored
+        prev = bool(self.C.gemm_precision_tf32())
+        self.C.set_gemm_precision(self.tf32)
+        try:
+            if self.kind == "jodie":
+                return self._forward_jodie(split, train)
+            return self._forward_tgn(split, train)
+        finally:
+            self.C.set_gemm_precision(prev)
+
+    def _forward_tgn(self, split: str, train: bool) -> None:
         C, s = self.C, self.s
         m, u, c = self._params()
         mem = self.memory

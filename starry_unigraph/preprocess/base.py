@@ -1,20 +1,54 @@
-"""Artifact-emitting preprocessor base (reference preprocess/base.py:13-89).
+"""Preprocessors that turn a raw dataset into the artifact tree a runtime loads
+(reference interface: preprocess/base.py:13-89).
 
-Layout under ``<artifact_root>``: ``meta/artifacts.json`` (provider meta) plus
-mode-specific directories; JSON payloads are pretty-printed with sorted keys,
-tensor payloads use ``torch.save``.
+Artifact tree under ``<artifact_root>``: ``meta/artifacts.json`` (the provider
+meta, read back by ``load_prepared_from_disk``) and one directory per artifact
+family (``partitions``, ``routes``, ``sampling``, ``snapshots``, plus ``flare``
+and ``clusters`` written by some modes). Every file is written to a temporary
+name and renamed into place, so an interrupted preprocessing run never leaves a
+truncated artifact that a later run would load.
 """
 from __future__ import annotations
 
 import json
+import os
 from abc import ABC, abstractmethod
 from dataclasses import dataclass
 from pathlib import Path
-from typing import Any
+from typing import Any, Callable
 
 import torch
 
 from starry_unigraph.types import PreparedArtifacts, SessionContext
+
+KNOWN_ARTIFACT_DIRS = ("meta", "partitions", "routes", "sampling", "snapshots", "flare", "clusters")
+META_FILE = ("meta", "artifacts.json")
+
+
+def _dump_json(payload: Any, handle) -> None:
+    handle.write(json.dumps(payload, indent=2, sort_keys=True, default=str).encode("utf-8"))
+
+
+def _dump_torch(payload: Any, handle) -> None:
+    torch.save(payload, handle)
+
+
+# serializer name -> writer(payload, binary file handle)
+SERIALIZERS: dict[str, Callable[[Any, Any], None]] = {"json": _dump_json, "torch": _dump_torch}
+
+
+def write_artifact(path: Path, payload: Any, serializer: str = "json") -> Path:
+    """Write one artifact atomically (temporary file in the same directory, then rename)."""
+    writer = SERIALIZERS.get(serializer)
+    if writer is None:
+        raise ValueError(f"Unsupported artifact serializer: {serializer} (known: {sorted(SERIALIZERS)})")
+    path = Path(path)
+    path.parent.mkdir(parents=True, exist_ok=True)
+    staging = path.with_name(f".{path.name}.{os.getpid()}.partial")
+    with staging.open("wb") as handle:
+        writer(payload, handle)
+    os.replace(staging, path)
+    return path
 
 
 @dataclass
@@ -24,7 +58,7 @@ class ArtifactLayout:
 
     @property
     def meta_path(self) -> Path:
-        return self.directories["meta"] / "artifacts.json"
+        return self.directories[META_FILE[0]] / META_FILE[1]
 
 
 @dataclass
@@ -41,6 +75,9 @@ class ArtifactPayload:
 
 
 class GraphPreprocessor(ABC):
+    """Three stages run in order by ``run``: read the raw data, partition it, and
+    build the runtime artifacts (the last stage usually ends in ``emit_artifacts``)."""
+
     artifact_dirs: tuple[str, ...] = ("meta", "partitions", "routes", "sampling", "snapshots")
 
     @abstractmethod
@@ -52,53 +89,37 @@ class GraphPreprocessor(ABC):
     @abstractmethod
     def build_runtime_artifacts(self, session_ctx: SessionContext) -> PreparedArtifacts: ...
 
+    def run(self, session_ctx: SessionContext) -> PreparedArtifacts:
+        stages = (self.prepare_raw, self.build_partitions)
+        for stage in stages:
+            stage(session_ctx)
+        return self.build_runtime_artifacts(session_ctx)
+
     def ensure_artifact_layout(self, session_ctx: SessionContext) -> ArtifactLayout:
-        dirs = {name: session_ctx.artifact_root / name for name in self.artifact_dirs}
-        for p in dirs.values():
-            p.mkdir(parents=True, exist_ok=True)
-        return ArtifactLayout(root=session_ctx.artifact_root, directories=dirs)
+        root = Path(session_ctx.artifact_root)
+        layout = ArtifactLayout(root=root, directories={d: root / d for d in self.artifact_dirs})
+        for directory in layout.directories.values():
+            directory.mkdir(parents=True, exist_ok=True)
+        return layout
 
     def emit_artifacts(self, session_ctx: SessionContext, payload: ArtifactPayload) -> PreparedArtifacts:
+        """Write every output, then the provider meta last: a tree whose meta exists is complete."""
         layout = self.ensure_artifact_layout(session_ctx)
-        self._write_json(layout.meta_path, payload.provider_meta)
-        for out in payload.outputs:
-            self._write_output(layout.root / out.relative_path, out.payload, out.serializer)
+        for output in payload.outputs:
+            write_artifact(layout.root / output.relative_path, output.payload, output.serializer)
+        write_artifact(layout.meta_path, payload.provider_meta, "json")
         return PreparedArtifacts(meta_path=layout.meta_path, directories=layout.directories,
                                  provider_meta=payload.provider_meta)
 
-    def run(self, session_ctx: SessionContext) -> PreparedArtifacts:
-        self.prepare_raw(session_ctx)
-        self.build_partitions(session_ctx)
-        return self.build_runtime_artifacts(session_ctx)
-
-    @staticmethod
-    def _write_json(path: Path, payload: dict[str, Any]) -> None:
-        path.parent.mkdir(parents=True, exist_ok=True)
-        with path.open("w", encoding="utf-8") as handle:
-            json.dump(payload, handle, indent=2, sort_keys=True, default=str)
-
-    @classmethod
-    def _write_output(cls, path: Path, payload: Any, serializer: str) -> None:
-        path.parent.mkdir(parents=True, exist_ok=True)
-        if serializer == "json":
-            cls._write_json(path, payload)
-        elif serializer == "torch":
-            torch.save(payload, path)
-        else:
-            raise ValueError(f"Unsupported artifact serializer: {serializer}")
-
 
 def read_artifact_meta(meta_path: Path) -> dict[str, Any]:
-    with Path(meta_path).open("r", encoding="utf-8") as handle:
-        return json.load(handle)
-
-
-KNOWN_ARTIFACT_DIRS = ("meta", "partitions", "routes", "sampling", "snapshots", "flare", "clusters")
+    return json.loads(Path(meta_path).read_text(encoding="utf-8"))
 
 
 def load_prepared_from_disk(artifact_root: Path) -> PreparedArtifacts:
-    meta_path = Path(artifact_root) / "meta" / "artifacts.json"
-    if not meta_path.exists():
+    root = Path(artifact_root)
+    meta_path = root.joinpath(*META_FILE)
+    if not meta_path.is_file():
         raise RuntimeError("Data not prepared. Call prepare_data() first.")
-    dirs = {n: Path(artifact_root) / n for n in KNOWN_ARTIFACT_DIRS if (Path(artifact_root) / n).exists()}
-    return PreparedArtifacts(meta_path=meta_path, directories=dirs, provider_meta=read_artifact_meta(meta_path))
+    present = {name: root / name for name in KNOWN_ARTIFACT_DIRS if (root / name).is_dir()}
+    return PreparedArtifacts(meta_path=meta_path, directories=present, provider_meta=read_artifact_meta(meta_path))

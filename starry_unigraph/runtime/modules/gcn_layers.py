@@ -31,24 +31,35 @@ def _gcn_norm(graph) -> torch.Tensor:
     return graph.edge_norm().unsqueeze(-1)
 
 
-def _gcn_message_pass(graph, x: torch.Tensor) -> torch.Tensor:
-    if x.size(0) == graph.num_src_nodes:
-        src_x = x
-    elif x.size(0) == graph.num_dst_nodes:
-        route = getattr(graph, "route", None)
-        if route is not None and route.send_index is not None and dist.is_available() and dist.is_initialized():
-            from starry_unigraph.parallel.halo import get_halo_context, halo_aggregate
+def _gcn_message_pass(graph, x: torch.Tensor, exchange: bool | None = None) -> torch.Tensor:
+    """Normalised neighbour sum of `graph` over source rows built from `x`.
 
-            hc = get_halo_context()
-            if x.is_cuda and hc is not None and x.size(-1) == hc.F:  # halo rows pulled from the peers
-                return halo_aggregate(graph, x)
-            src_x = route.forward(x)
-        else:
-            extra = graph.num_src_nodes - graph.num_dst_nodes
-            src_x = torch.cat([x, x.new_zeros(extra, x.size(-1))], dim=0) if extra > 0 else x
-    else:
+    `x` is either the block's stored source features (local + halo rows, nothing
+    to exchange) or a layer output over the block's destination rows, whose halo
+    rows are fetched from their owners (``exchange``). When not given,
+    ``exchange`` is inferred from the row count; callers that know which case
+    they are in pass it, since a block without halo rows has equal counts and
+    every rank must still take part in the exchange."""
+    if exchange is None:
+        exchange = x.size(0) != graph.num_src_nodes
+    if not exchange:
+        if x.size(0) != graph.num_src_nodes:
+            raise ValueError(f"Unexpected feature rows for block graph: got {x.size(0)}, expected "
+                             f"{graph.num_src_nodes} source rows")
+        return gcn_aggregate(graph, x)
+    if x.size(0) != graph.num_dst_nodes:
         raise ValueError(f"Unexpected feature rows for block graph: got {x.size(0)}, expected "
-                         f"{graph.num_dst_nodes} or {graph.num_src_nodes}")
+                         f"{graph.num_dst_nodes} destination rows")
+    route = getattr(graph, "route", None)
+    if route is not None and route.send_index is not None and dist.is_available() and dist.is_initialized():
+        from starry_unigraph.parallel.halo import get_halo_context, halo_aggregate
+
+        hc = get_halo_context()
+        if x.is_cuda and hc is not None and x.size(-1) == hc.F:  # halo rows pulled from the peers
+            return halo_aggregate(graph, x)
+        return gcn_aggregate(graph, route.forward(x))
+    extra = graph.num_src_nodes - graph.num_dst_nodes  # no route: halo rows read as zeros
+    src_x = torch.cat([x, x.new_zeros(extra, x.size(-1))], dim=0) if extra > 0 else x
     return gcn_aggregate(graph, src_x)
 
 
@@ -64,7 +75,9 @@ class GCNStack(nn.Module):
     def forward_graph(self, graph, x: torch.Tensor | None = None) -> torch.Tensor:
         h = _graph_input(graph) if x is None else x
         for i, layer in enumerate(self.layers):
-            h = _gcn_message_pass(graph, h.float())
+            # the first layer reads the block's stored source rows (halo rows included when the block
+            # has any); every later layer's input covers the destination rows only and exchanges halo rows
+            h = _gcn_message_pass(graph, h.float(), exchange=True if (i > 0 or x is not None) else None)
             h = linear(h, layer.weight, None, 1 if i < len(self.layers) - 1 else 0)
         return h
 

@@ -191,5 +191,7 @@ def test_graph_replayed_steps_match_eager(tmp_path, family):
         results[graphs] = (losses, [p.detach().cpu().clone() for p in s.runtime.model.parameters()])
     (le, pe), (lg, pg) = results[False], results[True]
     torch.testing.assert_close(torch.tensor(lg), torch.tensor(le), rtol=1e-3, atol=1e-5)
+    # weight-gradient atomics sum in a run-dependent order; Adam turns last-bit differences of
+    # near-zero gradients into differences of up to lr in single elements
     for a, b in zip(pg, pe):
-        torch.testing.assert_close(a, b, rtol=1e-3, atol=1e-5)
+        torch.testing.assert_close(a, b, rtol=1e-2, atol=2e-4)

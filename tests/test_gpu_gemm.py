@@ -1,5 +1,6 @@
-"""tcgen05 GEMM numerics against a plain fp32 PyTorch reference (bf16 operands,
-fp32 accumulate: relative tolerance ~1e-2)."""
+"""tcgen05 GEMM numerics against a plain fp32 PyTorch reference: bf16 operands
+(kind::f16, relative tolerance ~1e-2) and tf32 operands (kind::tf32, relative
+tolerance ~2e-3), fp32 accumulation either way."""
 import pytest
 import torch
 
@@ -83,3 +84,53 @@ def test_adam_matches_torch():
         ref.step()
     for a, b in zip(m1.parameters(), m2.parameters()):
         assert torch.allclose(a, b, atol=1e-5, rtol=1e-4)
+
+
+@pytest.fixture
+def tf32():
+    C = _C()
+    C.set_gemm_precision(True)
+    yield C
+    C.set_gemm_precision(False)
+
+
+def _fp32_ref(fn):
+    prev = torch.backends.cuda.matmul.allow_tf32
+    torch.backends.cuda.matmul.allow_tf32 = False
+    try:
+        return fn()
+    finally:
+        torch.backends.cuda.matmul.allow_tf32 = prev
+
+
+@pytest.mark.parametrize("M,K,N", [(1, 8, 16), (128, 64, 128), (300, 100, 100), (1000, 216, 200), (257, 33, 300),
+                                   (4096, 128, 512)])
+def test_linear_fwd_tf32(tf32, M, K, N):
+    C = tf32
+    torch.manual_seed(0)
+    x = torch.randn(M, K, device="cuda")
+    w = torch.randn(N, K, device="cuda") / K ** 0.5
+    b = torch.randn(N, device="cuda")
+    y = C.linear_fwd(x, w, b, 0)
+    ref = _fp32_ref(lambda: x @ w.t() + b)
+    torch.cuda.synchronize()
+    assert C.status_read(True) == 0
+    assert _rel(y, ref) < 2e-3, _rel(y, ref)
+
+
+@pytest.mark.parametrize("M,K,N", [(64, 16, 32), (1000, 100, 200), (3000, 216, 100)])
+def test_linear_dgrad_wgrad_tf32(tf32, M, K, N):
+    """The transposed operands (W^T of the data gradient, dY^T and X^T of the weight
+    gradient) are transposed by the pack kernel into K-major tf32 images."""
+    C = tf32
+    torch.manual_seed(1)
+    dy = torch.randn(M, N, device="cuda")
+    w = torch.randn(N, K, device="cuda") / N ** 0.5
+    x = torch.randn(M, K, device="cuda")
+    dx = C.linear_dgrad(dy, w)
+    assert _rel(dx, _fp32_ref(lambda: dy @ w)) < 2e-3
+    dw = torch.zeros(N, K, device="cuda")
+    db = torch.zeros(N, device="cuda")
+    C.linear_wgrad(dy, x, dw, db)
+    assert _rel(dw, _fp32_ref(lambda: dy.t() @ x)) < 2e-3
+    assert _rel(db, dy.sum(0)) < 1e-3  # the bias gradient comes from a ones column of the tf32 GEMM

@@ -61,11 +61,21 @@ def test_sampler_kernel_matches_torch(tmp_path):
     assert int(tot) == int(ref.count.sum())
 
 
+# tolerances of the fused step against the fp32 CPU oracle per operand precision
+# (gradient errors of both are dominated by the time encoding of large time deltas: fp32 w * dt
+# has an ulp of ~0.25 rad at dt ~ 1e6, so cos / sin there differ between any two implementations)
+TOL = {"bf16": {"loss": 1e-2, "pred": 1e-2, "table": 2e-2, "grad": 5e-2},
+       "tf32": {"loss": 3e-3, "pred": 3e-3, "table": 5e-3, "grad": 5e-2}}
+
+
+@pytest.mark.parametrize("precision", ["tf32", "bf16"])
 @pytest.mark.parametrize("slots", [1, 2])
-def test_fused_forward_and_memory_match_cpu_oracle(tmp_path, slots):
+def test_fused_forward_and_memory_match_cpu_oracle(tmp_path, slots, precision):
     """lr = 0: parameters stay fixed, so per-step losses, the memory table and the
     mailbox isolate the forward pass and the memory/mailbox semantics."""
-    g = _session("cuda", tmp_path, ctdg={"mailbox_slots": slots}, train={"lr": 0.0})
+    tol = TOL[precision]
+    g = _session("cuda", tmp_path, ctdg={"mailbox_slots": slots}, train={"lr": 0.0},
+                 runtime={"precision": precision})
     c = _session("cpu", tmp_path, ctdg={"mailbox_slots": slots}, train={"lr": 0.0})
     rg, rc = g.ctdg_session.online_runtime, c.ctdg_session.online_runtime
     for a, b in zip(rg.model.state_dict().values(), rc.model.state_dict().values()):
@@ -77,22 +87,23 @@ def test_fused_forward_and_memory_match_cpu_oracle(tmp_path, slots):
         rc._negative_sample = lambda b, neg=neg: neg
         res_c = rc.train_step(batch)
         lg, lc = res_g["loss"], res_c["loss"]
-        assert abs(lg - lc) <= 1e-2 * max(1.0, abs(lc)), (i, lg, lc)
+        assert abs(lg - lc) <= tol["loss"] * max(1.0, abs(lc)), (i, lg, lc)
         pg, pc = torch.tensor(res_g["predictions"]), torch.tensor(res_c["predictions"])
-        assert float((pg - pc).abs().max()) < 1e-2, (i, float((pg - pc).abs().max()))
+        assert float((pg - pc).abs().max()) < tol["pred"], (i, float((pg - pc).abs().max()))
     from starry_unigraph.ops import check_status
 
     check_status()
     mg, mc = rg.memory, rc.memory
-    assert torch.allclose(mg.memory.cpu(), mc.memory, atol=2e-2, rtol=2e-2)
-    assert torch.allclose(mg.mailbox.cpu(), mc.mailbox, atol=2e-2, rtol=2e-2)
+    assert torch.allclose(mg.memory.cpu(), mc.memory, atol=tol["table"], rtol=tol["table"])
+    assert torch.allclose(mg.mailbox.cpu(), mc.mailbox, atol=tol["table"], rtol=tol["table"])
     assert torch.equal(mg.next_mail_pos.cpu(), mc.next_mail_pos)
 
 
-def test_fused_gradients_match_autograd(tmp_path):
+@pytest.mark.parametrize("precision", ["tf32", "bf16"])
+def test_fused_gradients_match_autograd(tmp_path, precision):
     """Gradients of every trainable parameter after the same steps (lr = 0 keeps
     both models identical; gradients of the last step are compared)."""
-    g = _session("cuda", tmp_path, train={"lr": 0.0})
+    g = _session("cuda", tmp_path, train={"lr": 0.0}, runtime={"precision": precision})
     c = _session("cpu", tmp_path, train={"lr": 0.0})
     rg, rc = g.ctdg_session.online_runtime, c.ctdg_session.online_runtime
     eng = rg.engine
@@ -142,7 +153,7 @@ def test_fused_gradients_match_autograd(tmp_path):
         else:
             errs[n] = float((a - b).norm() / (b.norm() + 1e-8))
     tol = {"conv.time_enc.w.weight": 2e-2, "conv.w_k.bias": 0.2}
-    bad = {n: e for n, e in errs.items() if e > tol.get(n, 5e-2)}
+    bad = {n: e for n, e in errs.items() if e > tol.get(n, TOL[precision]["grad"])}
     assert not bad, errs
 
 
@@ -168,10 +179,12 @@ def _jodie_session(device, tmp_path, **over):
     return s
 
 
-def test_jodie_fused_step_matches_cpu_oracle(tmp_path):
+@pytest.mark.parametrize("precision", ["tf32", "bf16"])
+def test_jodie_fused_step_matches_cpu_oracle(tmp_path, precision):
     """JODIE (tanh-RNN memory + time projection): losses, predictions, memory and
     mailbox (lr = 0), then the gradients of the trainable parameters."""
-    g = _jodie_session("cuda", tmp_path, train={"lr": 0.0})
+    tol = TOL[precision]
+    g = _jodie_session("cuda", tmp_path, train={"lr": 0.0}, runtime={"precision": precision})
     c = _jodie_session("cpu", tmp_path, train={"lr": 0.0})
     rg, rc = g.ctdg_session.online_runtime, c.ctdg_session.online_runtime
     assert rg.engine is not None and rg.engine.kind == "jodie"
@@ -181,19 +194,19 @@ def test_jodie_fused_step_matches_cpu_oracle(tmp_path):
         neg = eng.neg[: batch.size].cpu()
         rc._negative_sample = lambda b, neg=neg: neg
         res_c = rc.train_step(batch)
-        assert abs(res_g["loss"] - res_c["loss"]) <= 1e-2 * max(1.0, abs(res_c["loss"])), (i, res_g["loss"],
-                                                                                           res_c["loss"])
+        assert abs(res_g["loss"] - res_c["loss"]) <= tol["loss"] * max(1.0, abs(res_c["loss"])), \
+            (i, res_g["loss"], res_c["loss"])
         pg, pc = torch.tensor(res_g["predictions"]), torch.tensor(res_c["predictions"])
-        assert float((pg - pc).abs().max()) < 1e-2, i
+        assert float((pg - pc).abs().max()) < tol["pred"], i
     from starry_unigraph.ops import check_status
 
     check_status()
-    assert torch.allclose(rg.memory.memory.cpu(), rc.memory.memory, atol=2e-2, rtol=2e-2)
-    assert torch.allclose(rg.memory.mailbox.cpu(), rc.memory.mailbox, atol=2e-2, rtol=2e-2)
+    assert torch.allclose(rg.memory.memory.cpu(), rc.memory.memory, atol=tol["table"], rtol=tol["table"])
+    assert torch.allclose(rg.memory.mailbox.cpu(), rc.memory.mailbox, atol=tol["table"], rtol=tol["table"])
     for (n, pg), pc in zip(rg.model.named_parameters(), rc.model.parameters()):
         a, b = pg.grad.detach().cpu(), pc.grad.detach()
         rel = float((a - b).norm() / (b.norm() + 1e-8))
-        assert rel < 5e-2, (n, rel)
+        assert rel < tol["grad"], (n, rel)
 
 
 def test_train_batches_matches_per_step_api(tmp_path):

@@ -23,6 +23,7 @@ def _lib():
     lib.su_noalloc_scratch_capacity.restype = ctypes.c_size_t
     lib.su_noalloc_status.restype = ctypes.c_int
     lib.su_noalloc_status.argtypes = [ctypes.POINTER(ctypes.c_int)]
+    lib.su_noalloc_status_reset.restype = ctypes.c_int
     lib.su_noalloc_strerror.restype = ctypes.c_char_p
     lib.su_noalloc_strerror.argtypes = [ctypes.c_int]
     return C, lib
@@ -53,20 +54,25 @@ def _call_noalloc(lib, x, h, c, cn, gates, dh, dc, w, gw, gb, rows, in_dim, H):
     return rc, dxh, dcp
 
 
-@pytest.mark.parametrize("in_dim", [20, 64])
-def test_noalloc_matches_lstm_bwd_on_two_calls(in_dim):
+@pytest.mark.parametrize("in_dim,H", [(20, 32), (64, 32), (24, 20)])
+def test_noalloc_matches_lstm_bwd_on_two_calls(in_dim, H):
+    """hidden = 20 exercises the padded hidden width (24) and the clipped output columns."""
+    from starry_unigraph.ops import gemm_precision
+
     C, lib = _lib()
-    rows, H = 1000, 32
+    rows = 1000
+    assert lib.su_noalloc_status_reset() == 0
     gw_ref = [torch.zeros(H, in_dim + H, device="cuda") for _ in range(4)]
     gb_ref = [torch.zeros(H, device="cuda") for _ in range(4)]
     gw_na = [torch.zeros(H, in_dim + H, device="cuda") for _ in range(4)]
     gb_na = [torch.zeros(H, device="cuda") for _ in range(4)]
     for seed in (1, 2):
         x, h, c, w, b, dh, dc = _case(rows, in_dim, H, seed)
-        _, cn, gates = C.lstm_fwd(x, h, c, w[0], b[0], w[1], b[1], w[2], b[2], w[3], b[3], True)
-        dx_ref, dhp_ref, dcp_ref = C.lstm_bwd(x, h, c, cn, gates, dh, dc, w[0], w[1], w[2], w[3],
-                                              gw_ref[0], gb_ref[0], gw_ref[1], gb_ref[1], gw_ref[2], gb_ref[2],
-                                              gw_ref[3], gb_ref[3])
+        with gemm_precision(False):  # the entry point runs bf16 operands; compare with the op in bf16
+            _, cn, gates = C.lstm_fwd(x, h, c, w[0], b[0], w[1], b[1], w[2], b[2], w[3], b[3], True)
+            dx_ref, dhp_ref, dcp_ref = C.lstm_bwd(x, h, c, cn, gates, dh, dc, w[0], w[1], w[2], w[3],
+                                                  gw_ref[0], gb_ref[0], gw_ref[1], gb_ref[1], gw_ref[2],
+                                                  gb_ref[2], gw_ref[3], gb_ref[3])
         rc, dxh, dcp = _call_noalloc(lib, x, h, c, cn, gates, dh, dc, w, gw_na, gb_na, rows, in_dim, H)
         torch.cuda.synchronize()
         assert rc == 0, lib.su_noalloc_strerror(rc)
