@@ -30,13 +30,36 @@ class HotCache:
         return hit, self.rows[slot]
 
     def insert(self, node_ids: Tensor, rows: Tensor) -> None:
-        ids = node_ids.to(self.ids.device).long()
-        for i in range(ids.numel()):
-            present = torch.nonzero(self.ids == ids[i])
-            slot = int(present[0]) if present.numel() else int(torch.argmin(self.freq))
-            self.ids[slot] = ids[i]
-            self.rows[slot] = rows[i].to(self.rows)
-            self.freq[slot] = self.freq[slot] + 1 if present.numel() else 1
+        """Insert or refresh rows in one pass: ids already cached are updated in
+        place (frequency + 1), new ids take the least-frequently used slots (at
+        most `capacity` of them, the last occurrence of a repeated id wins)."""
+        ids = node_ids.to(self.ids.device).long().view(-1)
+        rows = rows.to(self.rows)
+        if ids.numel() == 0:
+            return
+        # last occurrence of every id in the batch
+        uniq, inverse = torch.unique(ids, return_inverse=True)
+        last = torch.full((uniq.numel(),), -1, dtype=torch.long, device=ids.device)
+        last.scatter_reduce_(0, inverse, torch.arange(ids.numel(), device=ids.device), reduce="amax")
+        ids, rows = uniq, rows[last]
+        # ids already resident: sorted search over the occupied slot ids
+        occupied = torch.nonzero(self.ids >= 0).view(-1)
+        present = torch.zeros(ids.numel(), dtype=torch.bool, device=ids.device)
+        if occupied.numel():
+            key, order = torch.sort(self.ids[occupied])
+            pos = torch.searchsorted(key, ids).clamp(max=key.numel() - 1)
+            present = key[pos] == ids
+            slots = occupied[order[pos[present]]]
+            self.rows[slots] = rows[present]
+            self.freq[slots] += 1
+        fresh_ids, fresh_rows = ids[~present], rows[~present]
+        take = min(fresh_ids.numel(), self.capacity)
+        if take:
+            # least-frequently used slots first (free slots have frequency 0)
+            victims = torch.topk(self.freq, take, largest=False).indices
+            self.ids[victims] = fresh_ids[:take]
+            self.rows[victims] = fresh_rows[:take]
+            self.freq[victims] = 1
 
     def clear(self) -> None:
         self.ids.fill_(-1)

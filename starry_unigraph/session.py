@@ -148,6 +148,10 @@ class SchedulerSession:
             self.runtime = RuntimeBundle(state={"graph_mode": "dtdg"})
             init_flare_training(runtime=self.runtime, session_ctx=self.ctx, partition_data=part, device=device)
             self._maybe_peer_halo(device)
+            from starry_unigraph.runtime.route.comm_plan import plan_from_routes
+
+            if getattr(part, "routes", None) is not None:
+                self.runtime.state["halo_volume"] = plan_from_routes(part.routes)
             self.runtime.state.update({"flare_partition_path": str(path),
                                        "window_state": self.snapshot_core.describe_window_state(),
                                        "snapshot_state": self.snapshot_core.dump_state(),
@@ -204,16 +208,35 @@ class SchedulerSession:
             self.build_runtime()
         mode = self.prepared.provider_meta.get("graph_mode")
         if mode == "ctdg":
+            from starry_unigraph.runtime.state import CTDGStateManager
+
             backend = CTDGGraphBackend(self.ctdg_session)
+            state_manager = CTDGStateManager(self.ctdg_session.online_runtime.memory)
         elif mode == "dtdg":
+            from starry_unigraph.runtime.state import DTDGStateManager
+
             backend = FlareGraphBackend(self.snapshot_core)
+            state_manager = DTDGStateManager()
         else:
             backend = ChunkGraphBackend(self.snapshot_core)
-        self.pipeline_engine = PipelineEngine(backend=backend, state_manager=DummyStateManager(),
+            state_manager = DummyStateManager()
+        self.pipeline_engine = PipelineEngine(backend=backend, state_manager=state_manager,
                                               model=model or self.runtime.model or self.model_spec,
                                               task_adapter=self.task_adapter, device=self._device(),
                                               optimizer=self.runtime.optimizer)
         return self.pipeline_engine
+
+    def build_runner(self):
+        """Runner of the session's mode (``runtime.runner``): build_sequence ->
+        prepare_data -> sync_data -> compute -> post_compute per unit of work,
+        driven by ``starry_unigraph.runtime.runner.run_units``."""
+        from starry_unigraph.runtime.runner import CTDGRunner, DTDGRunner
+
+        if self.ctdg_session is None and self.snapshot_core is None:
+            self.build_runtime()
+        if self.ctdg_session is not None:
+            return CTDGRunner(self.ctdg_session.online_runtime, int(self.ctx.config["train"]["batch_size"]))
+        return DTDGRunner(self.snapshot_core, self.runtime)
 
     # ------------------------------------------------------------------ step hooks
     def _between_steps(self, step: int) -> None:

@@ -1,0 +1,145 @@
+"""Unified-runtime pieces on CPU: the hot cache (vectorised insert), the CTDG /
+DTDG state managers, the runners driven through the session, the spatial /
+state communication plans and the route volume summary the DTDG session
+records."""
+import torch
+
+from starry_unigraph import SchedulerSession
+from starry_unigraph.runtime.cache import DecayCache, HotCache
+from starry_unigraph.runtime.comm.spatial_plan import SpatialPlan
+from starry_unigraph.runtime.comm.state_plan import StatePlan
+from starry_unigraph.runtime.runner import run_units
+
+
+def test_hot_cache_insert_and_lookup():
+    torch.manual_seed(0)
+    cache = HotCache(capacity=8, dim=4)
+    ids = torch.tensor([5, 3, 5, 9])      # repeated id: the last row wins
+    rows = torch.arange(16, dtype=torch.float32).view(4, 4)
+    cache.insert(ids, rows)
+    hit, got = cache.lookup(torch.tensor([5, 3, 9, 7]))
+    assert hit.tolist() == [True, True, True, False]
+    assert torch.equal(got[0], rows[2]) and torch.equal(got[1], rows[1]) and torch.equal(got[2], rows[3])
+    # refresh a resident id: updated in place, frequency grows, no new slot taken
+    occupied = int((cache.ids >= 0).sum())
+    cache.insert(torch.tensor([3]), torch.full((1, 4), -1.0))
+    assert int((cache.ids >= 0).sum()) == occupied
+    assert torch.equal(cache.lookup(torch.tensor([3]))[1][0], torch.full((4,), -1.0))
+    # overflow: the least-frequently used slots are replaced, resident hot ids stay
+    cache.insert(torch.arange(100, 106), torch.ones(6, 4))
+    assert int((cache.ids >= 0).sum()) == 8
+    assert bool(cache.lookup(torch.tensor([3]))[0][0])  # frequency 3 after two lookups and a refresh
+
+
+def test_hot_cache_invariants_over_batches():
+    """Over batches that overflow the cache: every id of the newest batch is
+    resident with its newest row, every resident id holds the last row written
+    for it, and the cache never holds more than its capacity."""
+    cache = HotCache(capacity=16, dim=2)
+    last_row = {}
+    g = torch.Generator().manual_seed(3)
+    for _ in range(6):
+        ids = torch.randperm(40, generator=g)[:6]
+        rows = torch.randn(6, 2, generator=g)
+        cache.insert(ids, rows)
+        last_row.update({int(v): rows[i] for i, v in enumerate(ids.tolist())})
+        assert int((cache.ids >= 0).sum()) <= 16
+        hit, got = cache.lookup(ids)
+        assert bool(hit.all())
+        assert torch.equal(got, rows)
+    for v in cache.ids.tolist():
+        if v >= 0:
+            assert torch.equal(cache.lookup(torch.tensor([v]))[1][0], last_row[v])
+
+
+def test_decay_cache_expires_old_versions():
+    d = DecayCache(max_versions=2)
+    for v in range(4):
+        d.put(v, torch.tensor([v]), torch.zeros(1, 2))
+    d.expire(3)
+    assert sorted(d.entries) == [2, 3] and d.get(1) is None
+
+
+def _ctdg_session(tmp_path):
+    cfg = {"model": {"name": "tgn", "family": "tgn", "task": "temporal_link_prediction", "hidden_dim": 16},
+           "data": {"root": str(tmp_path / "data"), "name": "ur_tgn", "format": "mock"},
+           "train": {"epochs": 1, "batch_size": 16}, "runtime": {"device": "cpu"},
+           "ctdg": {"dim_time": 8, "mailbox_slots": 1}}
+    s = SchedulerSession.from_config(cfg)
+    s.ctx.artifact_root = tmp_path / "art_tgn"
+    s.prepare_data()
+    s.build_runtime()
+    return s
+
+
+def _dtdg_session(tmp_path):
+    cfg = {"model": {"name": "mpnn_lstm", "family": "mpnn_lstm", "task": "snapshot_node_regression",
+                     "hidden_dim": 16},
+           "data": {"root": str(tmp_path / "data"), "name": "ur_mpnn", "format": "mock"},
+           "train": {"epochs": 1, "batch_size": 1, "snaps": 8}, "runtime": {"device": "cpu"},
+           "graph": {"storage": "snapshots"}}
+    s = SchedulerSession.from_config(cfg)
+    s.ctx.artifact_root = tmp_path / "art_mpnn"
+    s.prepare_data()
+    s.build_runtime()
+    return s
+
+
+def test_ctdg_state_manager_and_runner(tmp_path):
+    from starry_unigraph.runtime.state import CTDGStateManager
+
+    s = _ctdg_session(tmp_path)
+    results = run_units(s.build_runner(), "train", True)
+    assert results and all("loss" in r for r in results)
+    mb = s.ctdg_session.online_runtime.memory
+    mgr = CTDGStateManager(mb, hot_capacity=32)
+    ids = torch.arange(6)
+    st = mgr.prepare(ids)
+    assert torch.equal(st["memory"], mb.memory[ids]) and st["mailbox"].shape[0] == 6
+    mgr.update({"memory_ids": ids[:2], "memory_rows": torch.ones(2, mb.hidden_dim),
+                "memory_ts": torch.full((2,), 1e9)}, None)
+    assert torch.equal(mb.memory[:2], torch.ones(2, mb.hidden_dim))
+    mgr.patch(ids[2:4], torch.full((2, mb.hidden_dim), 3.0))
+    mgr.step()
+    assert mgr.describe()["version"] == 1 and mgr.describe()["hot"]["occupied"] == 2
+    eng = s.build_pipeline_engine()
+    assert type(eng.state_manager).__name__ == "CTDGStateManager"
+
+
+def test_dtdg_runner_state_manager_and_plans(tmp_path):
+    from starry_unigraph.runtime.state import DTDGStateManager
+
+    s = _dtdg_session(tmp_path)
+    runner = s.build_runner()
+    results = run_units(runner, "train", True)
+    assert results and len(runner.history) == len(results)
+    mgr = DTDGStateManager()
+    mgr.update({"state": (torch.ones(5, 3), torch.ones(5, 3))}, None)
+    st = mgr.prepare(torch.arange(7))["state"]
+    assert st[0].shape == (7, 3) and float(st[0][5:].abs().sum()) == 0.0
+    blob = next(iter(s.snapshot_core.iter_train()))
+    plan = StatePlan.from_window(blob)
+    assert plan.describe()["writes"] == blob.current_graph.num_dst_nodes
+    # single partition: no halo route, nothing to send
+    assert SpatialPlan.from_route(getattr(blob.current_graph, "route", None)).volume() == 0
+
+
+def test_spatial_plan_from_route():
+    from starry_unigraph.backends.dtdg.runtime.route import Route
+
+    r = Route(send_sizes=[0, 2, 1], recv_sizes=[3, 0, 2], send_index=torch.tensor([4, 7, 1]))
+    plan = SpatialPlan.from_route(r)
+    assert plan.volume() == 3 and plan.received() == 5
+    assert plan.send_ids[1].tolist() == [4, 7] and plan.send_ids[2].tolist() == [1]
+    assert plan.recv_ids[0].tolist() == [0, 1, 2] and plan.recv_ids[2].tolist() == [3, 4]
+
+
+def test_route_volume_summary():
+    from starry_unigraph.runtime.route.comm_plan import plan_from_routes
+
+    class _Routes:
+        send_sizes = [[1, 2], [0, 0], [4, 1]]
+        recv_sizes = [[0, 3], [1, 0], [2, 2]]
+
+    v = plan_from_routes(_Routes())
+    assert v["send_rows"] == [3, 0, 5] and v["max_recv"] == 4 and v["total_send"] == 8
