@@ -42,10 +42,14 @@ class ChunkBuilder:
 
         return apply_partition(torch.stack([src, dst]), num_nodes, self.num_clusters, self.seed)
 
-    def build(self, src, dst, ts, num_nodes: int, eid=None) -> list[ChunkAtomic]:
+    def build(self, src, dst, ts, num_nodes: int, eid=None, slice_ids=None, clusters=None) -> list[ChunkAtomic]:
+        """Chunks of the stream; `slice_ids` (per event) and `clusters` (per node)
+        may be given precomputed, else they come from slice_ids() / clusters()."""
         eid = torch.arange(src.numel()) if eid is None else eid
-        sl = self.slice_ids(src, dst, ts)
-        cl = self.clusters(src, dst, num_nodes)
+        sl = self.slice_ids(src, dst, ts) if slice_ids is None else slice_ids
+        cl = self.clusters(src, dst, num_nodes) if clusters is None else clusters
+        if clusters is not None:
+            self.num_clusters = max(self.num_clusters, int(cl.max()) + 1 if cl.numel() else 1)
         out: list[ChunkAtomic] = []
         for t in range(int(sl.max()) + 1 if sl.numel() else 0):
             in_t = sl == t

@@ -29,15 +29,22 @@ class ChunkPreprocessor(GraphPreprocessor):
         ctx.provider_state["chunk_dataset"] = ds
 
     def build_partitions(self, ctx: SessionContext) -> None:
+        from starry_unigraph.backends.chunk.prepare.adaptive import ChunkGenerator, schedule
+
         ds = ctx.provider_state["chunk_dataset"]
         c = ctx.config.get("chunk", {})
-        builder = ChunkBuilder(num_clusters=int(c.get("node_clusters", 8)), time_slices=int(c.get("time_slices", 16)),
-                               adaptive=bool(c.get("adaptive", False)))
-        chunks = builder.build(ds.src, ds.dst, ds.ts, ds.num_nodes, ds.event_ids)
+        gen = ChunkGenerator(num_clusters=int(c.get("node_clusters", 8)), time_slices=int(c.get("time_slices", 16)),
+                             adaptive=bool(c.get("adaptive", False)),
+                             info_loss_threshold=float(c.get("info_loss_threshold", 0.3)))
+        out = gen.generate(ds.src, ds.dst, ds.ts, ds.num_nodes, eid=ds.event_ids)
+        chunks = out["chunks"]
         W = int(ctx.config["dist"]["world_size"])
         parts = [[ch for ch in chunks if ch.chunk_id[1] % W == p] for p in range(W)]
         ctx.provider_state["chunk_parts"] = parts
-        ctx.provider_state["chunk_builder"] = builder.describe()
+        ctx.provider_state["chunk_routes"] = out["routes"]
+        ctx.provider_state["chunk_order"] = schedule(out["routes"])
+        ctx.provider_state["chunk_builder"] = out["builder"] | {"num_clusters": out["num_clusters"],
+                                                                "cross_ratio": out["cross_ratio"]}
 
     def build_runtime_artifacts(self, ctx: SessionContext) -> PreparedArtifacts:
         parts = ctx.provider_state["chunk_parts"]
@@ -47,8 +54,11 @@ class ChunkPreprocessor(GraphPreprocessor):
                                 "num_nodes": ds.num_nodes, "num_edges": ds.num_edges,
                                 "builder": ctx.provider_state["chunk_builder"], "pipeline": "chunked"}
         slices = sorted({ch.chunk_id[0] for p in parts for ch in p})
+        routes = ctx.provider_state["chunk_routes"]
         outputs = [ArtifactOutput("partitions/manifest.json", {"num_parts": W, "partition_algo": "cluster_round_robin"}),
-                   ArtifactOutput("routes/manifest.json", {"route_type": ctx.config["graph"]["route"]}),
+                   ArtifactOutput("routes/manifest.json", {"route_type": ctx.config["graph"]["route"],
+                                                           "dependence_routes": [r.describe() for r in routes],
+                                                           "order": [list(cid) for cid in ctx.provider_state["chunk_order"]]}),
                    ArtifactOutput("snapshots/manifest.json", {"time_slices": slices, "num_chunks": sum(map(len, parts))})]
         for p, chunks in enumerate(parts):
             outputs.append(ArtifactOutput(f"clusters/part_{p:03d}/cluster_manifest.json",

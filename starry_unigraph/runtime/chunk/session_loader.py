@@ -27,7 +27,11 @@ class ChunkRuntimeLoader:
         self.world_size = world_size
         self.cursor = 0
         self._ctdg = None
-        ordered = sorted(chunks.chunks, key=lambda c: (c.chunk_id[0], c.chunk_id[1]))
+        # run order: the preprocessor's dependency-respecting schedule when recorded
+        # (every chunk after the chunks of its cluster in earlier slices), else by (slice, cluster)
+        rank_of = {tuple(cid): i for i, cid in enumerate(manifest.get("order", []))}
+        ordered = sorted(chunks.chunks, key=lambda c: (rank_of.get(tuple(c.chunk_id), len(rank_of)),
+                                                       c.chunk_id[0], c.chunk_id[1]))
         ratio = normalize_split_ratio(config.get("data", {}).get("split_ratio"))
         n = len(ordered)
         self._splits = {s: ordered[slice(*split_bounds(n, s, ratio))] for s in ("train", "val", "test")}
@@ -40,6 +44,9 @@ class ChunkRuntimeLoader:
         part = Path(prepared_dir) / "clusters" / f"part_{min(rank, world_size - 1):03d}"
         chunks = ChunkData.load(part / "chunks.pt")
         manifest = json.loads((part / "cluster_manifest.json").read_text())
+        routes_path = Path(prepared_dir) / "routes" / "manifest.json"
+        if routes_path.exists():
+            manifest["order"] = json.loads(routes_path.read_text()).get("order", [])
         return cls(chunks, manifest, config, device, rank, world_size)
 
     def attach_ctdg(self, online_runtime: Any) -> None:

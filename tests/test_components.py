@@ -80,3 +80,66 @@ def test_native_sampler_wrapper():
     smp = BTSNativeSampler(tnb, num_nodes=4, num_edges=5, num_layers=1, fanout=[2], policy="recent")
     ret = smp.sample_from_nodes(torch.tensor([3, 1]), torch.tensor([10, 10]))
     assert len(ret) == 1
+
+
+def _stream(n_nodes=60, n_events=800, seed=0):
+    g = torch.Generator().manual_seed(seed)
+    src = torch.randint(0, n_nodes, (n_events,), generator=g)
+    dst = torch.randint(0, n_nodes, (n_events,), generator=g)
+    ts = torch.sort(torch.rand(n_events, generator=g) * 1000).values
+    return src, dst, ts, n_nodes
+
+
+def test_chunk_dependence_routes_and_schedule():
+    """Temporal routes: same cluster, earlier slices, newest first, decay^k
+    weights; spatial routes: clusters joined by an event of the same slice;
+    the schedule runs every chunk after its temporal dependencies."""
+    from starry_unigraph.backends.chunk.prepare import ChunkGenerator, schedule
+
+    src, dst, ts, n = _stream()
+    gen = ChunkGenerator(num_clusters=3, time_slices=4, adaptive=False, decay_base=0.5)
+    out = gen.generate(src, dst, ts, n)
+    cluster, routes = out["clusters"], out["routes"]
+    ids = {r.chunk_id for r in routes}
+    slice_of = torch.arange(src.numel()) // ((src.numel() + 3) // 4)
+    for r in routes:
+        t, c = r.chunk_id
+        expect_t = sorted((s for s, cc in ids if cc == c and s < t), reverse=True)
+        assert r.temporal_deps == [(s, c) for s in expect_t]
+        assert torch.allclose(r.decay_weights, 0.5 ** torch.arange(1, len(expect_t) + 1, dtype=torch.float32))
+        m = slice_of == t
+        a, b = cluster[src[m]], cluster[dst[m]]
+        linked = set(b[a == c].tolist()) | set(a[b == c].tolist())
+        assert set(d[1] for d in r.gnn_deps) == {x for x in linked if x != c and (t, x) in ids}
+    order = schedule(routes)
+    pos = {cid: i for i, cid in enumerate(order)}
+    assert len(order) == len(routes)
+    assert all(pos[d] < pos[r.chunk_id] for r in routes for d in r.temporal_deps)
+
+
+def test_adaptive_cluster_count_grows_with_cross_traffic():
+    from starry_unigraph.backends.chunk.prepare import ChunkGenerator
+
+    src, dst, ts, n = _stream(n_nodes=200, n_events=3000, seed=1)  # random graph: most events cross clusters
+    fixed = ChunkGenerator(num_clusters=2, adaptive=False)
+    grown = ChunkGenerator(num_clusters=2, adaptive=True, info_loss_threshold=0.2)
+    _, n_fixed, r_fixed = fixed.generate_graph_clusters(src, dst, n)
+    _, n_grown, _ = grown.generate_graph_clusters(src, dst, n)
+    assert n_fixed == 2 and r_fixed > 0.2
+    import math
+
+    assert n_grown == math.ceil(2 * r_fixed / 0.2)
+
+
+def test_chunk_artifacts_carry_routes_and_order(tmp_path):
+    import json
+
+    s = _chunk_session(tmp_path)
+    s.prepare_data()
+    routes = json.loads((s.ctx.artifact_root / "routes" / "manifest.json").read_text())
+    assert routes["dependence_routes"] and routes["order"]
+    s.build_runtime()
+    order = [tuple(c) for c in routes["order"]]
+    mine = [c.chunk_id for c in s.snapshot_core._splits["train"]]
+    ranks = [order.index(tuple(c)) for c in mine]
+    assert ranks == sorted(ranks)
