@@ -127,21 +127,57 @@ class ClockSampler:
 
 
 def _reference_arm(args):
-    """Run the unmodified reference from baseline/_ref through its own API."""
+    """Run the unmodified reference from baseline/_ref through its own public API
+    (bench_reference.py in a subprocess whose import path holds only the reference),
+    on the same synthetic stream; print its JSON line, or an ``unavailable`` line."""
+    import subprocess
+    import tempfile
+
+    rank = int(os.environ.get("RANK", "0"))
+
+    def unavailable(reason: str) -> int:
+        if rank == 0:
+            print(json.dumps({"impl": "reference", "unavailable": reason}), flush=True)
+        return 0
+
     ref = ROOT / "baseline" / "_ref"
-    reason = None
     if not (ref / "starry_unigraph").exists():
-        reason = "reference not installed under baseline/_ref"
-    else:
-        try:
-            import dgl  # noqa: F401
-        except Exception:
-            reason = ("reference requires DGL (its package import chain imports dgl), which is not "
-                      "installed and cannot be installed offline on this image")
-    if reason is None:
-        reason = "reference CTDG benchmark driver not wired"
-    if int(os.environ.get("RANK", "0")) == 0:
-        print(json.dumps({"impl": "reference", "unavailable": reason}), flush=True)
+        return unavailable("reference not installed under baseline/_ref")
+    env = dict(os.environ)
+    env["PYTHONPATH"] = str(ref)
+    scratch = Path(tempfile.mkdtemp(prefix=f"su_ref_r{rank}_"))
+    probe = subprocess.run([sys.executable, "-c", "import dgl, starry_unigraph.session"], cwd=scratch, env=env,
+                           capture_output=True, text=True)
+    if probe.returncode != 0:
+        last = (probe.stderr.strip().splitlines() or ["import failed"])[-1]
+        return unavailable("reference requires DGL (its package import chain imports dgl), which is not installed "
+                           f"and has no offline wheel on this image ({last})")
+    if args.workload != "tgn":
+        return unavailable(f"reference arm is wired for the headline TGN workload, not {args.workload}")
+    # the workload in the reference's CSV format (data/raw_temporal.py): edges.csv + edge_features.pt
+    sys.path.insert(0, str(ROOT))
+    import pandas as pd
+    import torch
+
+    from starry_unigraph.data.synthetic import ctdg_preset
+
+    stream = ctdg_preset("tgn_large", num_events=args.events or 7833140, seed=0)
+    ds = scratch / "data" / "tgn_large"
+    ds.mkdir(parents=True, exist_ok=True)
+    pd.DataFrame({"src": stream["src"].numpy(), "dst": stream["dst"].numpy(),
+                  "time": stream["ts"].numpy()}).to_csv(ds / "edges.csv", index=False)
+    torch.save(stream["edge_feat"].float(), ds / "edge_features.pt")
+    driver = ROOT / "bench_reference.py"
+    cmd = [sys.executable, "-c", f"import runpy; runpy.run_path({str(driver)!r}, run_name='__main__')",
+           "--data", str(scratch / "data"), "--name", "tgn_large", "--steps", str(args.steps),
+           "--warmup", str(args.warmup), "--batch", str(args.batch or 600)]
+    run = subprocess.run(cmd, cwd=scratch, env=env, capture_output=True, text=True)
+    lines = [ln for ln in run.stdout.splitlines() if ln.startswith("{")]
+    if run.returncode != 0 or (rank == 0 and not lines):
+        last = (run.stderr.strip().splitlines() or ["no output"])[-1]
+        return unavailable(f"reference run failed: {last}")
+    if rank == 0:
+        print(lines[-1], flush=True)
     return 0
 
 
@@ -208,15 +244,16 @@ def _dtdg_run(args, workload: str, steps: int, warmup: int) -> dict:
     prep_s = time.perf_counter() - t_prep
     core, rt = session.snapshot_core, session.runtime
     graphs = rt.state.get("step_graphs")
-    avail = len(list(core.iter_train()))
-    steps = max(1, min(steps, avail - warmup))
-    blob_list = list(core.iter_train(max_steps=warmup + steps))
+    blob_list = list(core.iter_train())  # frozen windows of the train split
+    steps = max(1, min(steps, len(blob_list) - warmup))
     warm, timed = blob_list[:warmup], blob_list[warmup:warmup + steps]
 
     def barrier():
         if world > 1:
             dist.barrier()
 
+    barrier()  # ranks enter the first step (and its device-side halo barriers) together
+    torch.cuda.synchronize()
     for b in warm:
         run_flare_train_step(rt, b, {"meta": {}}, need_host=False)
     if graphs is not None:
@@ -377,7 +414,9 @@ def _ctdg_run(args, precision: str = "tf32") -> dict:
         if world > 1:
             dist.barrier()
 
-    # warm-up (includes CUDA-graph capture)
+    # warm-up (includes CUDA-graph capture); ranks enter the first step together
+    barrier()
+    torch.cuda.synchronize()
     for b in batches[: args.warmup]:
         rt._engine_step(b, "train", True, want_outputs=False)
     torch.cuda.synchronize()

@@ -290,6 +290,10 @@ class SchedulerSession:
                 "elapsed_s": max_elapsed, "local_elapsed_s": elapsed, "outputs": outputs}
 
     def run_epoch(self, split: str = "train") -> dict[str, Any]:
+        if self.ctx.dist.is_distributed and dist.is_initialized():
+            # ranks start the epoch's first step together: its device-side peer barriers then
+            # wait only for the GPU work of the step, not for host-side work of a lagging rank
+            dist.barrier()
         if self.ctdg_session is not None:
             rt = self.ctdg_session.online_runtime
             train = split == "train"
