@@ -105,13 +105,13 @@ struct PeerPush {
   float* const* peers;
   const int* owner;
   const int* lrow;
-  int F;
+  int ld;  // row stride of the owners' gradient buffers (>= the layer width)
   __device__ __forceinline__ void put(int64_t row, int f, float v, bool /*whole*/) const {
-    atomicAdd(peers[owner[row]] + static_cast<int64_t>(lrow[row]) * F + f, v);
+    atomicAdd(peers[owner[row]] + static_cast<int64_t>(lrow[row]) * ld + f, v);
   }
   template <int VEC>
   __device__ __forceinline__ void put_vec(int64_t row, int f, const float (&v)[VEC], bool /*whole*/) const {
-    red_add_vec<VEC>(peers[owner[row]] + static_cast<int64_t>(lrow[row]) * F + f, v);
+    red_add_vec<VEC>(peers[owner[row]] + static_cast<int64_t>(lrow[row]) * ld + f, v);
   }
 };
 
@@ -342,29 +342,31 @@ void launch_spmm_peer_gather(cudaStream_t st, const int64_t* rowptr, const int* 
 
 // Halo rows pulled over NVLink once each: out[i] = row lrow[c] of owner[c]'s
 // staging buffer for c = halo_src[i]. Sixteen-byte vectors, F / 4 lanes per row.
+// Peers' staging rows have a stride of LD4 float4s (the staging width); the
+// pulled rows are F4 float4s wide (the layer width, at most the staging width).
 __global__ void halo_pull_kernel(const float* const* __restrict__ peers, const int* __restrict__ owner,
                                  const int* __restrict__ lrow, const int* __restrict__ halo_src, int64_t n_halo,
-                                 int F4, float4* __restrict__ out) {
+                                 int F4, int LD4, float4* __restrict__ out) {
   const int64_t total = n_halo * F4;
   const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
   for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < total; i += stride) {
     const int64_t h = i / F4;
     const int v = static_cast<int>(i - h * F4);
     const int c = halo_src[h];
-    const float4* src = reinterpret_cast<const float4*>(peers[owner[c]] + static_cast<int64_t>(lrow[c]) * F4 * 4);
+    const float4* src = reinterpret_cast<const float4*>(peers[owner[c]] + static_cast<int64_t>(lrow[c]) * LD4 * 4);
     out[i] = src[v];
   }
 }
 
 void launch_halo_pull(cudaStream_t st, const float* const* peers, const int* owner, const int* lrow,
-                      const int* halo_src, int64_t n_halo, int F, float* out) {
+                      const int* halo_src, int64_t n_halo, int F, int ld, float* out) {
   if (n_halo == 0) return;
   int dev = 0;
   cudaGetDevice(&dev);
   const int64_t total = n_halo * (F / 4);
   const int blocks = static_cast<int>(std::min<int64_t>((total + 255) / 256, static_cast<int64_t>(num_sms(dev)) * 8));
   count_launch();
-  halo_pull_kernel<<<blocks, 256, 0, st>>>(peers, owner, lrow, halo_src, n_halo, F / 4,
+  halo_pull_kernel<<<blocks, 256, 0, st>>>(peers, owner, lrow, halo_src, n_halo, F / 4, ld / 4,
                                            reinterpret_cast<float4*>(out));
 }
 
@@ -380,11 +382,11 @@ void launch_spmm_two_tables(cudaStream_t st, const int64_t* rowptr, const int* c
 // Its backward over the transposed CSR (rows = source rows): each source row's
 // gradient is pushed into the owner's gradient buffer with remote atomic adds.
 void launch_spmm_peer_push(cudaStream_t st, const int64_t* rowptr_t, const int* col_t, const float* val_t,
-                           const float* grad_dst, int64_t n_src, int F, float* const* peers, const int* src_owner,
-                           const int* src_row) {
+                           const float* grad_dst, int64_t n_src, int F, int ld, float* const* peers,
+                           const int* src_owner, const int* src_row) {
   if (n_src == 0) return;
   launch_chunked(st, rowptr_t, col_t, val_t, LocalRows{grad_dst, F}, n_src, F,
-                 PeerPush{peers, src_owner, src_row, F});
+                 PeerPush{peers, src_owner, src_row, ld});
 }
 
 // d(pre-activation) of the four gates and dc_prev from dh', dc' and the saved gates.

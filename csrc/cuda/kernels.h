@@ -145,12 +145,12 @@ void launch_spmm_peer_gather(cudaStream_t st, const int64_t* rowptr, const int* 
 // DTDG halo, pull-once form: unique halo rows copied from the owners' staging
 // buffers (P2P loads), then the aggregation over [local rows | halo rows]
 void launch_halo_pull(cudaStream_t st, const float* const* peers, const int* owner, const int* lrow,
-                      const int* halo_src, int64_t n_halo, int F, float* out);
+                      const int* halo_src, int64_t n_halo, int F, int ld, float* out);
 void launch_spmm_two_tables(cudaStream_t st, const int64_t* rowptr, const int* col, const float* val, const float* x,
                             const float* halo, int n_split, int64_t n_rows, int F, float* out);
 void launch_spmm_peer_push(cudaStream_t st, const int64_t* rowptr_t, const int* col_t, const float* val_t,
-                           const float* grad_dst, int64_t n_src, int F, float* const* peers, const int* src_owner,
-                           const int* src_row);
+                           const float* grad_dst, int64_t n_src, int F, int ld, float* const* peers,
+                           const int* src_owner, const int* src_row);
 void launch_lstm_bwd(cudaStream_t st, const float* gates, const float* c_prev, const float* c_new, const float* dh,
                      int dh_ld, const float* dc, int dc_ld, int64_t rows, int H, float* dpre, float* dc_prev);
 // gate gradients written as the K-major image of dpre (the input-gradient GEMM's A)

@@ -140,7 +140,7 @@ at::Tensor spmm_peer_gather(const at::Tensor& rowptr, const at::Tensor& col, con
                             const at::Tensor& peers, const at::Tensor& src_owner, const at::Tensor& src_row,
                             int64_t n_rows, int64_t F);
 at::Tensor halo_pull(const at::Tensor& peers, const at::Tensor& src_owner, const at::Tensor& src_row,
-                     const at::Tensor& halo_src, int64_t F);
+                     const at::Tensor& halo_src, int64_t F, int64_t ld);
 at::Tensor spmm_two_tables(const at::Tensor& rowptr, const at::Tensor& col, const at::Tensor& val,
                            const at::Tensor& x, const at::Tensor& halo, int64_t n_rows);
 std::vector<at::Tensor> rgru_fwd(const at::Tensor& xz, const at::Tensor& xr, const at::Tensor& xc,
@@ -155,7 +155,7 @@ std::vector<at::Tensor> rgru_bwd(const at::Tensor& xz, const at::Tensor& xr, con
                                  at::Tensor& gbc);
 void spmm_peer_push(const at::Tensor& rowptr_t, const at::Tensor& col_t, const at::Tensor& val_t,
                     const at::Tensor& grad_dst, int64_t n_src, const at::Tensor& peers, const at::Tensor& src_owner,
-                    const at::Tensor& src_row);
+                    const at::Tensor& src_row, int64_t ld);
 
 void tgn_rnn_memory_update(const at::Tensor& roots, const at::Tensor& n_roots, const at::Tensor& mailbox,
                            at::Tensor& memory, at::Tensor& memory_ts, const at::Tensor& ts_max,
@@ -217,8 +217,11 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("peer_rs_adam_ag", &peer_rs_adam_ag);
   m.def("spmm_csr", &spmm_csr);
   m.def("spmm_peer_gather", &spmm_peer_gather);
-  m.def("spmm_peer_push", &spmm_peer_push);
-  m.def("halo_pull", &halo_pull);
+  m.def("spmm_peer_push", &spmm_peer_push, py::arg("rowptr_t"), py::arg("col_t"), py::arg("val_t"),
+        py::arg("grad_dst"), py::arg("n_src"), py::arg("peers"), py::arg("src_owner"), py::arg("src_row"),
+        py::arg("ld") = -1);
+  m.def("halo_pull", &halo_pull, py::arg("peers"), py::arg("src_owner"), py::arg("src_row"), py::arg("halo_src"),
+        py::arg("F"), py::arg("ld") = -1);
   m.def("rgru_fwd", &rgru_fwd);
   m.def("rgru_bwd", &rgru_bwd);
   m.def("spmm_two_tables", &spmm_two_tables);

@@ -256,15 +256,18 @@ at::Tensor spmm_peer_gather(const at::Tensor& rowptr, const at::Tensor& col, con
   return out;
 }
 
+// `ld`: row stride of the peers' staging buffers (-1: F)
 at::Tensor halo_pull(const at::Tensor& peers, const at::Tensor& src_owner, const at::Tensor& src_row,
-                     const at::Tensor& halo_src, int64_t F) {
+                     const at::Tensor& halo_src, int64_t F, int64_t ld) {
   SU_CHECK_I32(src_owner); SU_CHECK_I32(src_row); SU_CHECK_I32(halo_src);
   TORCH_CHECK(peers.is_cuda() && peers.scalar_type() == at::kLong, "peer table must be cuda int64");
-  TORCH_CHECK(F % 4 == 0, "halo rows are pulled in 16-byte vectors: F must be a multiple of 4");
+  if (ld < 0) ld = F;
+  TORCH_CHECK(F % 4 == 0 && ld % 4 == 0 && ld >= F,
+              "halo rows are pulled in 16-byte vectors: F and the row stride must be multiples of 4, stride >= F");
   at::Tensor out = at::empty({halo_src.numel(), F}, src_owner.options().dtype(at::kFloat));
   launch_halo_pull(cur_stream(), reinterpret_cast<const float* const*>(peers.data_ptr<int64_t>()),
                    src_owner.data_ptr<int>(), src_row.data_ptr<int>(), halo_src.data_ptr<int>(), halo_src.numel(),
-                   static_cast<int>(F), out.data_ptr<float>());
+                   static_cast<int>(F), static_cast<int>(ld), out.data_ptr<float>());
   SU_LAUNCH_CHECK();
   return out;
 }
@@ -283,13 +286,17 @@ at::Tensor spmm_two_tables(const at::Tensor& rowptr, const at::Tensor& col, cons
   return out;
 }
 
+// `ld`: row stride of the owners' gradient buffers (-1: the gradient width)
 void spmm_peer_push(const at::Tensor& rowptr_t, const at::Tensor& col_t, const at::Tensor& val_t,
                     const at::Tensor& grad_dst, int64_t n_src, const at::Tensor& peers, const at::Tensor& src_owner,
-                    const at::Tensor& src_row) {
+                    const at::Tensor& src_row, int64_t ld) {
   SU_CHECK_F32(grad_dst); SU_CHECK_CONTIG(grad_dst);
   TORCH_CHECK(peers.is_cuda() && peers.scalar_type() == at::kLong, "peer table must be cuda int64");
+  const int F = static_cast<int>(grad_dst.size(1));
+  if (ld < 0) ld = F;
+  TORCH_CHECK(ld >= F, "gradient buffer rows narrower than the gradient");
   launch_spmm_peer_push(cur_stream(), rowptr_t.data_ptr<int64_t>(), col_t.data_ptr<int>(), val_t.data_ptr<float>(),
-                        grad_dst.data_ptr<float>(), n_src, static_cast<int>(grad_dst.size(1)),
+                        grad_dst.data_ptr<float>(), n_src, F, static_cast<int>(ld),
                         reinterpret_cast<float* const*>(peers.data_ptr<int64_t>()), src_owner.data_ptr<int>(),
                         src_row.data_ptr<int>());
   SU_LAUNCH_CHECK();

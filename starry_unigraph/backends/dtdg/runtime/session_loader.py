@@ -160,10 +160,26 @@ class FlareRuntimeLoader:
     def load_snapshot(self, index: int, split: str) -> DTDGBatch:
         return _block_to_batch(self.load_block(index), split, self.window_state.window_size, self.route_plan)
 
+    def _publish_row_order(self, perm: torch.Tensor | None) -> None:
+        """NVLink halo: tell the peers where this rank's rows are (collective; every
+        rank calls it at the same point of the epoch)."""
+        from starry_unigraph.parallel.halo import get_halo_context
+
+        hc = get_halo_context()
+        if hc is None:
+            return
+        ids = None
+        if perm is not None:
+            dst_ids = self.partition_data.dst_ids[0].item().to(perm.device)
+            ids = dst_ids[perm.long()]
+        hc.set_row_order(ids)
+
     def iter_train(self, split: str = "train", max_steps: int | None = None) -> Iterable[STGraphBlob]:
         start, end = self._bounds["train"]
         loader = self.graph_loader[start:end]
         order = _parse_chunk_order(self.train_chunk_order, loader.chunk_count, self._gen)
+        perm, _ = loader._get_perm_ends(order, self.train_chunk_decay, self.train_num_full_snaps)
+        self._publish_row_order(perm)
         window = self.window_state.window_size if self.window_from_size else None
         for i, blob in enumerate(loader(chunk_order=order, chunk_decay=self.train_chunk_decay,
                                         num_full_snaps=self.train_num_full_snaps, window=window)):
@@ -174,6 +190,7 @@ class FlareRuntimeLoader:
             yield blob
 
     def _replay(self, split: str, tag: str) -> Iterable[DTDGBatch]:
+        self._publish_row_order(None)  # evaluation reads snapshots in the stored row order
         _, train_end = self._bounds["train"]
         s, e = self._bounds[split]
         for index in range(e):

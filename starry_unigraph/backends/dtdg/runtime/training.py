@@ -225,7 +225,9 @@ class StepGraphs:
     def supported(runtime: RuntimeBundle, blob: Any) -> bool:
         if not isinstance(blob, STGraphBlob) or not bool(runtime.state.get("cuda_graphs", False)):
             return False
-        return getattr(blob.state, "mode", "pad") == "pad"
+        # windows with decayed (truncated) slots come from a chunk order drawn anew every epoch:
+        # their graphs would never replay, so they run eagerly
+        return getattr(blob.state, "mode", "pad") == "pad" and all(st.full for st in blob.steps)
 
     @staticmethod
     def key(blob: Any) -> tuple:

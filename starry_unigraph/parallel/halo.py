@@ -17,7 +17,14 @@ row); after a barrier each rank takes its rows out.
 Staging and gradient buffers alternate between two copies, so a rank may start
 writing call k+1 while a slower peer still reads call k: a buffer is reused
 two calls later, after a barrier that every peer passes only once it finished
-reading it.
+reading it. Buffers are as wide as the widest exchanging layer; a narrower layer
+uses the first columns of each row (the kernels take the row stride), so any
+width up to that one (a multiple of 4) takes this path.
+
+Row order: a partition's rows follow ascending node id unless the training
+loader permutes them (chunk order with temporal decay); ``set_row_order``
+publishes every rank's current order (one all-gather) so peers address the
+owner's rows where they are.
 """
 from __future__ import annotations
 
@@ -55,6 +62,10 @@ class PeerHaloContext:
             local_index[ids] = torch.arange(ids.numel())
         self.owner = node_parts.to(self.device, torch.int32)
         self.local_index = local_index.to(self.device, torch.int32)
+        self._default_index = self.local_index
+        self._node_parts = node_parts
+        self.order_version = 0  # bumped whenever a rank's row order changes (invalidates pull plans)
+        self._group = group
         self.epoch = torch.zeros(1, dtype=torch.int64, device=self.device)
         self.budget = int(barrier_budget)
         self.fwd_calls = 0
@@ -66,6 +77,40 @@ class PeerHaloContext:
     def barrier(self) -> None:
         self._C.peer_barrier(self.tables["flags"], self.rank, self.world, self.epoch, self.budget)
 
+    def supports(self, width: int) -> bool:
+        """Layer widths this context exchanges over NVLink."""
+        return width == self.F or (width <= self.F and width % 4 == 0)
+
+    def set_row_order(self, local_ids: torch.Tensor | None) -> None:
+        """Collective: this rank's local rows are the global nodes `local_ids` in
+        this order (None: ascending node id, the partition's stored order). Every
+        rank calls it with its own order; afterwards `local_index[gid]` is the
+        row of gid in its owner's current order."""
+        counts = torch.bincount(self._node_parts, minlength=self.world)
+        rows = int(counts.max())
+        mine = torch.full((rows,), -1, dtype=torch.int64, device=self.device)
+        if local_ids is not None:
+            ids = local_ids.to(self.device, torch.int64).view(-1)
+            if ids.numel() != int(counts[self.rank]):
+                raise ValueError(f"row order of {ids.numel()} nodes for a partition of {int(counts[self.rank])}")
+            mine[: ids.numel()] = ids
+        flag = torch.tensor([0 if local_ids is None else 1], dtype=torch.int64, device=self.device)
+        flags = [torch.zeros_like(flag) for _ in range(self.world)]
+        dist.all_gather(flags, flag, group=self._group)
+        if not any(int(f) for f in flags):
+            if self.local_index is not self._default_index:
+                self.local_index = self._default_index
+                self.order_version += 1
+            return
+        orders = [torch.empty_like(mine) for _ in range(self.world)]
+        dist.all_gather(orders, mine, group=self._group)
+        index = self._default_index.clone()
+        for order in orders:
+            valid = order >= 0
+            index[order[valid]] = torch.arange(int(valid.sum()), dtype=torch.int32, device=self.device)
+        self.local_index = index
+        self.order_version += 1
+
     def src_maps(self, graph) -> tuple[torch.Tensor, torch.Tensor]:
         gid = graph.srcdata[NID].to(self.device).long()
         return self.owner[gid].contiguous(), self.local_index[gid].contiguous()
@@ -75,7 +120,7 @@ class PeerHaloContext:
         once per call, in this order) and the aggregation columns remapped to
         [row of a local source in the layer input | n_local + pull slot].
         Cached on the block."""
-        key = ("_halo_pull", self.rank, self.world, int(n_local))
+        key = ("_halo_pull", self.rank, self.world, int(n_local), self.order_version)
         meta = graph.graph_meta
         if meta.get("_halo_pull_key") != key:
             owner, row = self.src_maps(graph)
@@ -96,21 +141,18 @@ class _HaloAggregate(autograd.Function):
         buf = f"x{hc.fwd_calls % 2}"
         hc.fwd_calls += 1
         n_local, F = x_local.shape
-        if F > hc.F:
-            raise ValueError(f"halo staging holds {hc.F} features, got {F}")
+        if not hc.supports(F):
+            raise ValueError(f"halo staging rows hold {hc.F} features; layer width {F} is not exchanged here")
         stage = hc.arena[buf]
-        if F == hc.F:
-            stage[:n_local].copy_(x_local)
-        else:  # narrower layer: rows of F values at the buffer's stride would break the kernel's row math
-            raise ValueError("halo staging buffers are sized for one feature width")
+        stage[:n_local, :F].copy_(x_local)  # rows at the staging stride hc.F
         hc.barrier()
         csr = graph.csr()
         owner, row = hc.src_maps(graph)
         if F % 4 == 0:
             halo_src, col = hc.pull_plan(graph, n_local)
-            halo = C.halo_pull(hc.tables[buf], owner, row, halo_src, F)
+            halo = C.halo_pull(hc.tables[buf], owner, row, halo_src, F, hc.F)
             out = C.spmm_two_tables(csr["rowptr"], col, csr["val"], x_local, halo, graph.num_dst_nodes)
-        else:
+        else:  # F == hc.F (supports): per-edge peer reads at the staging stride
             out = C.spmm_peer_gather(csr["rowptr"], csr["col"], csr["val"], hc.tables[buf], owner, row,
                                      graph.num_dst_nodes, F)
         ctx.hc, ctx.graph, ctx.n_local = hc, graph, n_local
@@ -125,12 +167,13 @@ class _HaloAggregate(autograd.Function):
         buf = f"g{hc.bwd_calls % 2}"
         hc.bwd_calls += 1
         csr = ctx.graph.csr()
+        F = grad.size(1)
         C.spmm_peer_push(csr["rowptr_t"], csr["col_t"], csr["val_t"], grad.contiguous(), ctx.graph.num_src_nodes,
-                         hc.tables[buf], owner, row)
+                         hc.tables[buf], owner, row, hc.F)
         hc.barrier()
         g = hc.arena[buf]
-        gx = g[: ctx.n_local].clone()
-        g[: ctx.n_local].zero_()  # ready for its next use, two calls later
+        gx = g[: ctx.n_local, :F].clone()
+        g[: ctx.n_local, :F].zero_()  # ready for its next use, two calls later
         return gx, None, None
 
 

@@ -55,7 +55,7 @@ def _gcn_message_pass(graph, x: torch.Tensor, exchange: bool | None = None) -> t
         from starry_unigraph.parallel.halo import get_halo_context, halo_aggregate
 
         hc = get_halo_context()
-        if x.is_cuda and hc is not None and x.size(-1) == hc.F:  # halo rows pulled from the peers
+        if x.is_cuda and hc is not None and hc.supports(int(x.size(-1))):  # halo rows pulled from the peers
             return halo_aggregate(graph, x)
         return gcn_aggregate(graph, route.forward(x))
     extra = graph.num_src_nodes - graph.num_dst_nodes  # no route: halo rows read as zeros

@@ -183,11 +183,6 @@ class SchedulerSession:
             return
         if str(self.ctx.config.get("comm", {}).get("path", "p2p")) != "p2p":
             return
-        decay = self.ctx.config.get("dtdg", {}).get("chunk_decay")
-        if decay not in (None, "all", "null", 0):
-            # chunk decay truncates older window graphs per partition, so peers' row numbering
-            # differs from the full partition's: keep the collective route for those runs
-            return
         path = self.prepared.directories.get("partitions", self.ctx.artifact_root / "partitions") / "node_parts.pt"
         if not path.exists():
             return

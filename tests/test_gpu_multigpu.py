@@ -66,16 +66,22 @@ def test_hash_partition_two_ranks_consistent(tmp_path, assign):
 
 
 @need2
-def test_dtdg_nvlink_halo_matches_nccl_route(tmp_path):
+@pytest.mark.parametrize("decay", [False, True])
+def test_dtdg_nvlink_halo_matches_nccl_route(tmp_path, decay):
     """MPNN-LSTM over 2 partitions: halo read from peer memory inside the
-    aggregation + fused all-reduce/Adam must track the NCCL route + all-reduce."""
-    _run(tmp_path, 2, "--path", "nccl", worker=DTDG_WORKER, port=29631)
-    _run(tmp_path, 2, "--path", "p2p", worker=DTDG_WORKER, port=29632)
+    aggregation + fused all-reduce/Adam must track the NCCL route + all-reduce;
+    with decay, under a random chunk order (rows permuted per rank, published to
+    the peers) and truncated older window slots."""
+    extra = ["--decay"] if decay else []
+    tag = "_decay" if decay else ""
+    _run(tmp_path, 2, "--path", "nccl", *extra, worker=DTDG_WORKER, port=29631 + 4 * decay)
+    _run(tmp_path, 2, "--path", "p2p", *extra, worker=DTDG_WORKER, port=29632 + 4 * decay)
     for r in (0, 1):
-        a = torch.load(tmp_path / f"dtdg_p2p_r{r}.pt")
-        b = torch.load(tmp_path / f"dtdg_nccl_r{r}.pt")
+        a = torch.load(tmp_path / f"dtdg_p2p{tag}_r{r}.pt")
+        b = torch.load(tmp_path / f"dtdg_nccl{tag}_r{r}.pt")
         assert a["halo"] is not None and b["halo"] is None
         torch.testing.assert_close(torch.tensor(a["losses"]), torch.tensor(b["losses"]), rtol=2e-3, atol=1e-5)
         torch.testing.assert_close(a["params"], b["params"], rtol=2e-3, atol=2e-5)
     # replicas identical under the fused all-reduce
-    assert torch.equal(torch.load(tmp_path / "dtdg_p2p_r0.pt")["params"], torch.load(tmp_path / "dtdg_p2p_r1.pt")["params"])
+    assert torch.equal(torch.load(tmp_path / f"dtdg_p2p{tag}_r0.pt")["params"],
+                       torch.load(tmp_path / f"dtdg_p2p{tag}_r1.pt")["params"])

@@ -3,34 +3,59 @@ partitioned snapshot block (which source rows are pulled from other ranks, and
 the aggregation columns remapped to [local rows | pulled rows]) must give the
 same aggregation as indexing every source row by its global id; and the
 in-place weight-gradient routing of the DTDG autograd ops."""
+import os
+
+import pytest
 import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
 
 from starry_unigraph.data.partition import NID, SnapshotBlock
 from starry_unigraph.parallel.halo import PeerHaloContext
 
 
-def _plan_ctx(node_parts: torch.Tensor, rank: int) -> PeerHaloContext:
+def _plan_ctx(node_parts: torch.Tensor, rank: int, world: int | None = None) -> PeerHaloContext:
     # the plan needs only the ownership maps, not the symmetric buffers
     hc = PeerHaloContext.__new__(PeerHaloContext)
     hc.device = torch.device("cpu")
-    hc.rank, hc.world = rank, int(node_parts.max()) + 1
+    hc.rank, hc.world = rank, world or int(node_parts.max()) + 1
     local_index = torch.empty_like(node_parts)
     for q in range(hc.world):
         ids = torch.nonzero(node_parts == q).view(-1)
         local_index[ids] = torch.arange(ids.numel())
     hc.owner = node_parts.int()
     hc.local_index = local_index.int()
+    hc._default_index = hc.local_index
+    hc._node_parts = node_parts.long()
+    hc._group = None
+    hc.order_version = 0
     return hc
 
 
-def test_pull_plan_matches_global_indexing():
+def _orders(parts: torch.Tensor, world: int, permuted: bool, g: torch.Generator) -> list[torch.Tensor]:
+    """Each rank's current row order (global ids of its local rows)."""
+    out = []
+    for q in range(world):
+        ids = torch.nonzero(parts == q).view(-1)
+        out.append(ids[torch.randperm(ids.numel(), generator=g)] if permuted else ids)
+    return out
+
+
+@pytest.mark.parametrize("permuted", [False, True])
+def test_pull_plan_matches_global_indexing(permuted):
     g = torch.Generator().manual_seed(3)
     n, F, world = 300, 6, 3
     parts = torch.randint(0, world, (n,), generator=g)
     x_global = torch.randn(n, F, generator=g)
+    orders = _orders(parts, world, permuted, g)
     for rank in range(world):
         hc = _plan_ctx(parts, rank)
-        mine = torch.nonzero(parts == rank).view(-1)
+        if permuted:  # what set_row_order computes from the gathered orders
+            index = hc.local_index.clone()
+            for order in orders:
+                index[order] = torch.arange(order.numel(), dtype=torch.int32)
+            hc.local_index = index
+        mine = orders[rank]
         # block: destination rows = this rank's nodes; sources = its nodes plus some
         # other ranks' nodes, in an arbitrary order (the plan must not rely on one)
         others = torch.nonzero(parts != rank).view(-1)
@@ -48,7 +73,7 @@ def test_pull_plan_matches_global_indexing():
         assert (owner[halo_src.long()] != rank).all()
         assert int((owner != rank).sum()) == halo_src.numel()
         # what the pull kernel gathers: row `row[c]` of owner[c]'s layer input
-        pulled = torch.stack([x_global[parts == owner[c]][row[c]] for c in halo_src.tolist()]) \
+        pulled = torch.stack([x_global[orders[int(owner[c])]][row[c]] for c in halo_src.tolist()]) \
             if halo_src.numel() else torch.zeros(0, F)
         table = torch.cat([x_local, pulled])
         csr = block.csr()
@@ -58,8 +83,35 @@ def test_pull_plan_matches_global_indexing():
         ref = torch.zeros(block.num_dst_nodes, F).index_add_(
             0, dst_of_edge, x_global[src_nodes[csr["col"].long()]] * csr["val"][:, None])
         torch.testing.assert_close(got, ref)
-        # cached on the block for the next call
+        # cached on the block for the next call, rebuilt when a row order changes
         assert hc.pull_plan(block, int(mine.numel()))[1] is col
+        hc.order_version += 1
+        assert hc.pull_plan(block, int(mine.numel()))[1] is not col
+
+
+def _row_order_worker(rank: int, world: int, port: int, out: str):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        g = torch.Generator().manual_seed(11)
+        parts = torch.randint(0, world, (200,), generator=g)
+        orders = _orders(parts, world, True, g)
+        hc = _plan_ctx(parts, rank, world)
+        default = hc.local_index.clone()
+        hc.set_row_order(orders[rank] if rank == 0 else None)  # rank 1 keeps its stored order
+        expect = default.clone()
+        expect[orders[0]] = torch.arange(orders[0].numel(), dtype=torch.int32)
+        ok = torch.equal(hc.local_index, expect) and hc.order_version == 1
+        hc.set_row_order(None)  # everyone back to ascending ids
+        ok = ok and torch.equal(hc.local_index, default) and hc.order_version == 2
+        torch.save(ok, f"{out}/r{rank}.pt")
+    finally:
+        dist.destroy_process_group()
+
+
+def test_set_row_order_publishes_every_ranks_order(tmp_path):
+    mp.spawn(_row_order_worker, args=(2, 29611, str(tmp_path)), nprocs=2, join=True)
+    assert all(torch.load(tmp_path / f"r{r}.pt") for r in range(2))
 
 
 def test_weight_gradients_go_to_existing_grad_in_place():

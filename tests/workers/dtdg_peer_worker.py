@@ -3,7 +3,7 @@ sequence, partitioned over the ranks, with the halo exchange and gradient
 all-reduce over NVLink (comm.path p2p) or NCCL (comm.path nccl). Saves this
 rank's losses and parameters.
 
-    torchrun --nproc-per-node 2 tests/workers/dtdg_peer_worker.py --out DIR --path {p2p,nccl}
+    torchrun --nproc-per-node 2 tests/workers/dtdg_peer_worker.py --out DIR --path {p2p,nccl} [--decay]
 """
 import argparse
 import json
@@ -20,6 +20,7 @@ def main():
     p.add_argument("--out", required=True)
     p.add_argument("--path", default="p2p", choices=["p2p", "nccl"])
     p.add_argument("--steps", type=int, default=6)
+    p.add_argument("--decay", action="store_true", help="random chunk order + chunk_decay half (permuted rows)")
     a = p.parse_args()
     import torch
 
@@ -38,11 +39,13 @@ def main():
                                   "edges_per_snapshot": 40000, "feat_dim": 16}},
            "train": {"epochs": 1, "snaps": 12, "lr": 1e-3},
            "runtime": {"device": "cuda"},
-           "dtdg": {"window_from_size": True, "chunk_order": None, "chunk_decay": None},
+           "dtdg": {"window_from_size": True, "chunk_order": "rand" if a.decay else None,
+                    "chunk_decay": "half" if a.decay else None},
            "comm": {"path": a.path},
            "dist": {"backend": "nccl", "timeout_s": 120}}
     s = SchedulerSession.from_config(cfg)
-    s.ctx.artifact_root = Path(a.out) / f"art_{a.path}_w{world}_r{rank}"
+    tag = f"{a.path}{'_decay' if a.decay else ''}"
+    s.ctx.artifact_root = Path(a.out) / f"art_{tag}_w{world}_r{rank}"
     initialize_distributed(s.ctx.dist)
     s.prepare_data()
     s.build_runtime()
@@ -54,7 +57,7 @@ def main():
     check_status()
     flat = s.runtime.optimizer.flat.data.cpu()
     torch.save({"losses": losses, "params": flat, "halo": s.runtime.state.get("halo")},
-               Path(a.out) / f"dtdg_{a.path}_r{rank}.pt")
+               Path(a.out) / f"dtdg_{tag}_r{rank}.pt")
     from starry_unigraph.parallel.halo import set_halo_context
 
     set_halo_context(None)
