@@ -6,9 +6,12 @@
 Rank 0 prints one JSON line per path and size:
 
 * ``allreduce_adam``: the data-parallel gradient all-reduce fused with Adam
-  (``PeerAllReduceAdam``: device barrier, every rank sums all W gradient buffers
-  in rank order over NVLink and applies Adam in the same kernel, barrier)
-  against ``dist.all_reduce`` (NCCL) followed by the fused Adam kernel.
+  (``PeerAllReduceAdam``: device barrier, one kernel in which rank r sums shard r
+  of all W gradient buffers in rank order over NVLink, applies Adam to it and
+  stores the new shard into every rank's parameters, barrier) against
+  ``dist.all_reduce`` (NCCL) followed by the fused Adam kernel.
+  ``all_read_us`` times the earlier form in which every rank reads all W
+  gradient buffers whole and updates all parameters itself.
 * ``halo_gather``: the DTDG halo exchange of ``halo_aggregate`` (staging copy,
   device barrier, each halo row pulled once from its owner over NVLink, SpMM
   over [own | halo] rows) against the reference's scheme: gather the boundary
@@ -79,12 +82,14 @@ def bench_allreduce_adam(n: int, iters: int, warmup: int, C) -> dict:
     world, rank = dist.get_world_size(), dist.get_rank()
     dev = torch.device("cuda", torch.cuda.current_device())
     n = (n + 3) // 4 * 4
-    arena = SymmetricArena({"grad": ((n,), torch.float32), "flags": ((32,), torch.int64)}, dev)
+    arena = SymmetricArena({"grad": ((n,), torch.float32), "param": ((n,), torch.float32),
+                            "flags": ((32,), torch.int64)}, dev)
     g = arena["grad"]
     g.normal_(generator=torch.Generator(device=dev).manual_seed(rank))
     arena["flags"].zero_()
-    tg, tf = arena.peer_table("grad"), arena.peer_table("flags")
-    p = torch.randn(n, device=dev)
+    p = arena["param"]
+    p.normal_(generator=torch.Generator(device=dev).manual_seed(99))  # same on every rank
+    tg, tp, tf = arena.peer_table("grad"), arena.peer_table("param"), arena.peer_table("flags")
     m, v = torch.zeros_like(p), torch.zeros_like(p)
     step = torch.zeros(1, dtype=torch.int64, device=dev)
     done = torch.zeros(1, dtype=torch.int32, device=dev)
@@ -94,22 +99,38 @@ def bench_allreduce_adam(n: int, iters: int, warmup: int, C) -> dict:
 
     def fused():
         C.peer_barrier(tf, rank, world, epoch, DEFAULT_BARRIER_BUDGET)
-        C.peer_allreduce_adam(tg, world, p, m, v, step, done, 1e-6, 0.9, 0.999, 1e-8, 0.0, 1.0 / world)
+        C.peer_rs_adam_ag(tg, tp, world, rank, p, m, v, step, done, 1e-6, 0.9, 0.999, 1e-8, 0.0, 1.0 / world)
+        C.peer_barrier(tf, rank, world, epoch, DEFAULT_BARRIER_BUDGET)
+
+    p2 = torch.randn(n, device=dev)
+
+    def all_read():
+        C.peer_barrier(tf, rank, world, epoch, DEFAULT_BARRIER_BUDGET)
+        C.peer_allreduce_adam(tg, world, p2, m, v, step, done, 1e-6, 0.9, 0.999, 1e-8, 0.0, 1.0 / world)
         C.peer_barrier(tf, rank, world, epoch, DEFAULT_BARRIER_BUDGET)
 
     g2 = torch.randn(n, device=dev)
 
     def nccl():
         dist.all_reduce(g2)
-        C.adam_flat(p, g2, m, v, step, done, 1e-6, 0.9, 0.999, 1e-8, 0.0, 1.0 / world)
+        C.adam_flat(p2, g2, m, v, step, done, 1e-6, 0.9, 0.999, 1e-8, 0.0, 1.0 / world)
 
     fused_ms = _time(fused, iters, warmup)
+    all_read_ms = _time(all_read, iters, warmup)
     nccl_ms = _time(nccl, iters, warmup)
-    # every rank pulls the W-1 remote gradient buffers; locally it reads its own
-    # gradient and p, m, v and writes p, m, v
-    nvl = (world - 1) * n * 4.0
-    hbm = 7 * n * 4.0
-    return _report("allreduce_adam", {"numel": n}, fused_ms, nccl_ms, nvl, hbm, world)
+    # replicas must hold the same parameters after the fused steps
+    ref = p.clone()
+    dist.broadcast(ref, src=0)
+    same = bool(torch.equal(ref, p))
+    # per rank: pull shard r of the W-1 remote gradient buffers, push the new shard into
+    # the W-1 remote parameter buffers (each direction (W-1)/W * n * 4 bytes); locally
+    # read its own gradient shard, p, m, v and write p, m, v of the shard
+    nvl = (world - 1) * (n // world) * 4.0
+    hbm = 7 * (n // world) * 4.0
+    r = _report("allreduce_adam", {"numel": n}, fused_ms, nccl_ms, nvl, hbm, world)
+    r["all_read_us"] = round(all_read_ms * 1e3, 2)
+    r["replicas_equal"] = same
+    return r
 
 
 def bench_halo_gather(n: int, m: int, F: int, iters: int, warmup: int, C) -> dict:

@@ -91,6 +91,10 @@ class FlareOptimizer:
             self.opt.step()
 
     def state_dict(self) -> dict:
+        """Full optimizer state. On the NVLink path the moments are sharded by rank
+        and this is a collective: every rank must call it."""
+        if self._allreduce is not None:
+            return self._allreduce.gather_state()
         return self.opt.state_dict()
 
     def load_state_dict(self, state: dict) -> None:

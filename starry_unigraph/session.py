@@ -478,13 +478,15 @@ class SchedulerSession:
             if distributed:
                 dist.barrier()
             return path
+        opt = self.runtime.optimizer
+        # every rank: on the NVLink path the optimizer moments are sharded and gathered here
+        opt_state = opt.state_dict() if opt is not None else None
         if distributed and rank != 0:
             return path  # one writer (all ranks hold identical parameters)
         path.parent.mkdir(parents=True, exist_ok=True)
         model = self.runtime.model.module if hasattr(self.runtime.model, "module") else self.runtime.model
-        opt = self.runtime.optimizer
         payload = {"model_state": {k: v.detach().cpu() for k, v in model.state_dict().items()},
-                   "optimizer_state": opt.state_dict() if opt is not None else None,
+                   "optimizer_state": opt_state,
                    "scheduler_state": self.runtime.scheduler, "config": self.ctx.config,
                    "epoch": self.current_epoch, "global_step": self.global_step}
         return save_checkpoint(path, payload)
