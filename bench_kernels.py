@@ -2,6 +2,7 @@
 
     python bench_kernels.py spmm     # CSR aggregation, 200k rows x 2M edges, F = 64
     python bench_kernels.py lstm     # fused LSTM cell forward and backward, 200k rows, hidden 64
+    python bench_kernels.py linear   # GCN linear forward / input gradient, 200k rows, 64 -> 64 and 128 -> 256
 
 Each case prints one JSON line of device times (CUDA events on the current
 stream, 5 warm-up calls, mean of 20, synchronised on both sides). The inputs
@@ -83,7 +84,30 @@ def lstm() -> dict:
     return {"case": "lstm", "rows": rows, "in": IN, "hidden": H, "fwd_us": round(t_fwd, 1), "bwd_us": round(t_bwd, 1)}
 
 
+def linear() -> dict:
+    """Packed tcgen05 linear with the per-row store epilogue against the TMA-store
+    epilogue (threshold switched per run); the memory roofline is the fp32 input
+    read once plus the fp32 output written once at the measured copy bandwidth."""
+    C = cuda_ext()
+    rows = 200_000
+    out = {"case": "linear", "rows": rows}
+    old = C.tma_store_min_rows()
+    try:
+        for K, N in ((64, 64), (128, 256)):
+            x = torch.randn(rows, K, device="cuda")
+            w = torch.randn(N, K, device="cuda") / K ** 0.5
+            gy = torch.randn(rows, N, device="cuda")
+            for name, thr in (("direct", -1), ("tma", 0)):
+                C.set_tma_store_min_rows(thr)
+                out[f"fwd_{K}x{N}_{name}_us"] = round(_time(lambda: C.linear_fwd(x, w, None, 0)), 1)
+                out[f"dgrad_{K}x{N}_{name}_us"] = round(_time(lambda: C.linear_dgrad(gy, w)), 1)
+            out[f"fwd_{K}x{N}_bytes"] = rows * (K + N) * 4
+    finally:
+        C.set_tma_store_min_rows(old)
+    return out
+
+
 if __name__ == "__main__":
-    cases = {"spmm": spmm, "lstm": lstm}
+    cases = {"spmm": spmm, "lstm": lstm, "linear": linear}
     for name in (sys.argv[1:] or list(cases)):
         print(json.dumps(cases[name]()), flush=True)

@@ -108,6 +108,27 @@ __device__ __forceinline__ void bulk_g2s(void* smem_dst, const void* gmem_src, u
       "l"(gmem_src), "r"(bytes), "r"(smem_u32(bar))
       : "memory");
 }
+// Tiled TMA store of one 2D box from shared memory to global memory (bulk
+// async-group completion, no multicast). `tmap` is the generic address of a
+// CUtensorMap in parameter / constant / global memory; (x, y) the box origin
+// in elements (x: innermost; x * element size a multiple of 16 bytes, both >= 0).
+__device__ __forceinline__ void tma_store_2d(const void* tmap, const void* smem_src, int x, int y) {
+  asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];" ::"l"(tmap),
+               "r"(smem_u32(smem_src)), "r"(x), "r"(y)
+               : "memory");
+}
+__device__ __forceinline__ void bulk_commit_group() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+// Wait until at most N of this thread's bulk groups are still reading shared memory.
+template <int N>
+__device__ __forceinline__ void bulk_wait_group_read() {
+  asm volatile("cp.async.bulk.wait_group.read %0;" ::"n"(N) : "memory");
+}
+// Wait until at most N of this thread's bulk groups are still in flight (writes done).
+template <int N>
+__device__ __forceinline__ void bulk_wait_group() {
+  asm volatile("cp.async.bulk.wait_group %0;" ::"n"(N) : "memory");
+}
+
 // Returns false when the budget ran out (caller records a status and unwinds).
 __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity) {
   if (mbar_try_wait(bar, parity)) return true;
@@ -233,6 +254,14 @@ __device__ __forceinline__ void tmem_wait_ld4(uint32_t (&a)[16], uint32_t (&b)[1
   for (int i = 0; i < 16; ++i) asm volatile("" : "+r"(a[i]), "+r"(b[i]), "+r"(c[i]), "+r"(d[i]));
 }
 
+// One wait for every load issued into `r` (any length).
+template <int N>
+__device__ __forceinline__ void tmem_wait_ld_all(uint32_t (&r)[N]) {
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+  for (int i = 0; i < N; ++i) asm volatile("" : "+r"(r[i]));
+}
+
 // read-only 16-byte global load through the non-coherent path (data that no
 // thread of the running kernel writes)
 __device__ __forceinline__ float4 ldg4(const float* p) { return __ldg(reinterpret_cast<const float4*>(p)); }
@@ -301,12 +330,14 @@ __device__ __forceinline__ float sigmoidf_(float x) { return 1.f / (1.f + expf(-
 // Gate activations of the fused RNN-cell epilogues: the hardware exp2 and
 // reciprocal units (__expf, __frcp_rn) and tanh.approx.f32 (max relative error
 // about 2^-11, finer than the bf16 rounding of the GEMM operands feeding them).
-__device__ __forceinline__ float sigmoid_fast(float x) { return __frcp_rn(1.f + __expf(-x)); }
 __device__ __forceinline__ float tanh_fast(float x) {
   float y;
   asm("tanh.approx.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
 }
+// sigmoid(x) = (1 + tanh(x / 2)) / 2: one tanh.approx (a single special-function
+// instruction) and two FMAs, with tanh_fast's absolute error halved.
+__device__ __forceinline__ float sigmoid_fast(float x) { return fmaf(0.5f, tanh_fast(0.5f * x), 0.5f); }
 
 // Round 4 floats to TF32 (round to nearest, ties away from zero: cvt.rna) and
 // return them as one 16-byte vector of 32-bit containers.

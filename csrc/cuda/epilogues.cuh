@@ -305,6 +305,14 @@ struct EpiLSTM {
   float* gates = nullptr;         // grouped layout above, optional
   int vec = 0;  // 1: H % 4 == 0 and every pointer 16-byte aligned (16-byte loads and stores)
   static constexpr bool kPrefetch = true;
+  // TMA stores (packed kernel, whole 16-unit groups): per warp and group the 32
+  // rows' [i f | g o] gates go out as two 32 x 32 fp32 boxes (128-byte swizzle)
+  // and c', h' as 16 x 32 boxes (64-byte swizzle) from a 12 KB shared-memory region
+  int tma = 0;
+  alignas(64) CUtensorMap map_g;  // gates [rows, 64 * H / 16], box 32 x 32
+  alignas(64) CUtensorMap map_c;  // c_out [rows, H], box 16 x 32
+  alignas(64) CUtensorMap map_h;  // h_out [rows, H], box 16 x 32
+  static constexpr int kTmaRegion = 12 * 1024;
 
 #ifdef __CUDACC__
   // c_prev of the next tile's rows toward L2 (one 64-byte segment per group)
@@ -325,9 +333,58 @@ struct EpiLSTM {
   // instruction instead of 32 partial ones)
   __device__ __forceinline__ void run(int row, bool valid, int n0, uint32_t taddr, int tile_cols, float* scratch,
                                       int /*barrier*/) const {
+    if (tma) {
+      uint8_t* reg = reinterpret_cast<uint8_t*>(scratch) + ((threadIdx.x >> 5) & 3) * kTmaRegion;
+#pragma unroll 1
+      for (int g0 = 0; g0 < tile_cols; g0 += 4 * DP) group_tma(row, valid, n0 + g0, taddr + g0, reg);
+      return;
+    }
     float* ws = scratch + ((threadIdx.x >> 5) & 3) * 32 * kStageStride;
 #pragma unroll 1
     for (int g0 = 0; g0 < tile_cols; g0 += 4 * DP) group(row, valid, n0 + g0, taddr + g0, ws);
+  }
+  __device__ __forceinline__ void finish() const {
+    if (tma && (threadIdx.x & 31) == 0) bulk_wait_group<0>();
+    __syncwarp();
+  }
+
+  // One 16-unit group (DP == 16, H % 16 == 0) through TMA stores. The region is
+  // 1024-byte aligned: [gates i f | gates g o | c' | h'] at 0, 4 KB, 8 KB, 10 KB.
+  // Rows past the matrix are clipped by the tensor maps.
+  __device__ __forceinline__ void group_tma(int row, bool valid, int n0, uint32_t taddr, uint8_t* reg) const {
+    const int lane = threadIdx.x & 31;
+    const int cb = (n0 / (4 * DP)) * DP;  // first unit of the group
+    if (cb >= H) return;                  // warp-uniform
+    const int64_t rb = (int64_t)row * H + cb;
+    float4 cp4[4];
+#pragma unroll
+    for (int q = 0; q < 4; ++q)
+      cp4[q] = (valid && c_prev) ? ldg4(c_prev + rb + 4 * q) : make_float4(0.f, 0.f, 0.f, 0.f);
+    // the previous group's boxes must have been read out by the TMA engine
+    if (lane == 0) bulk_wait_group_read<0>();
+    __syncwarp();
+    const int s128 = lane & 7;         // 128-byte swizzle: chunk j of a 128-byte row at j ^ (row % 8)
+    const int s64 = (lane >> 1) & 3;   // 64-byte swizzle: chunk j of a 64-byte row at j ^ ((row / 2) % 4)
+    compute16(taddr, 0, cb, valid, cp4, [&](int q, float4 i4, float4 f4, float4 g4, float4 o4, float4 c4, float4 h4) {
+      *reinterpret_cast<float4*>(reg + lane * 128 + ((q ^ s128) << 4)) = i4;
+      *reinterpret_cast<float4*>(reg + lane * 128 + (((4 + q) ^ s128) << 4)) = f4;
+      *reinterpret_cast<float4*>(reg + 4096 + lane * 128 + ((q ^ s128) << 4)) = g4;
+      *reinterpret_cast<float4*>(reg + 4096 + lane * 128 + (((4 + q) ^ s128) << 4)) = o4;
+      *reinterpret_cast<float4*>(reg + 8192 + lane * 64 + ((q ^ s64) << 4)) = c4;
+      *reinterpret_cast<float4*>(reg + 10240 + lane * 64 + ((q ^ s64) << 4)) = h4;
+    });
+    fence_proxy_async_smem();
+    __syncwarp();
+    if (lane == 0) {
+      const int gx = (cb / kLstmGroup) * 64;  // the group's first column in the gates matrix
+      if (gates) {
+        tma_store_2d(&map_g, reg, gx, row);
+        tma_store_2d(&map_g, reg + 4096, gx + 32, row);
+      }
+      tma_store_2d(&map_c, reg + 8192, cb, row);
+      tma_store_2d(&map_h, reg + 10240, cb, row);
+      bulk_commit_group();
+    }
   }
 
   // 16 units: activations and state update for units [cb, cb + 16) of `row`

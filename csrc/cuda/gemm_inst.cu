@@ -190,8 +190,91 @@ static void launch_pack(const Src& src, uint8_t* out, int mn, const int* mn_dev,
   pack_kernel<ROWS, Src><<<blocks, 256, 0, st>>>(src, out, tiles, nchunks, mn, mn_dev, mn);
 }
 
+// ---------------------------------------------------------------------------
+// TMA-store epilogue selection (EpiLinear with plain fp32 stores, large M)
+// ---------------------------------------------------------------------------
+static int tma_rows_from_env() {
+  const char* e = getenv("SU_TMA_STORE_MIN_ROWS");
+  return e != nullptr ? atoi(e) : 2048;
+}
+static std::atomic<int> g_tma_store_min_rows{tma_rows_from_env()};
+void set_tma_store_min_rows(int rows) { g_tma_store_min_rows.store(rows); }
+int tma_store_min_rows() { return g_tma_store_min_rows.load(); }
+
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+static EncodeTiledFn encode_tiled_fn() {
+  static EncodeTiledFn fn = [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q = cudaDriverEntryPointSymbolNotFound;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess) {
+      cudaGetLastError();
+      p = nullptr;
+    }
+    return reinterpret_cast<EncodeTiledFn>(p);
+  }();
+  return fn;
+}
+
+// Tensor map of an fp32 [rows, cols] matrix with row stride `ld` elements for
+// boxes of `box_cols` x 32 rows: 32 columns with the 128-byte swizzle, 16 with
+// the 64-byte one. False when it cannot be encoded.
+static bool encode_store_map(CUtensorMap* map, const float* base, int rows, int cols, int ld, int box_cols = 32) {
+  EncodeTiledFn fn = encode_tiled_fn();
+  if (fn == nullptr || rows <= 0 || cols <= 0 || (box_cols != 32 && box_cols != 16)) return false;
+  if ((reinterpret_cast<uintptr_t>(base) & 15) != 0 || (ld & 3) != 0) return false;
+  const cuuint64_t dims[2] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows)};
+  const cuuint64_t strides[1] = {static_cast<cuuint64_t>(ld) * sizeof(float)};
+  const cuuint32_t box[2] = {static_cast<cuuint32_t>(box_cols), 32};
+  const cuuint32_t elem[2] = {1, 1};
+  return fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(base), dims, strides, box, elem,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, box_cols == 32 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B,
+            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+template <int BN, int NSUB, bool TF32, class A, class B, class E>
+static bool launch_packed_impl(const A& a, const B& b, const E& e, const GemmShape& sh, cudaStream_t st);
+
 template <int BN, int NSUB, bool TF32, class A, class B, class E>
 static bool launch_packed(const A& a, const B& b, const E& e, const GemmShape& sh, cudaStream_t st) {
+  if constexpr (std::is_same<E, EpiLinear>::value && NSUB == 1) {
+    const int min_rows = g_tma_store_min_rows.load(std::memory_order_relaxed);
+    if (min_rows >= 0 && sh.M >= min_rows && sh.m_dev == nullptr && sh.ksplit <= 1 && e.out != nullptr &&
+        e.out_bf16 == nullptr && e.accumulate == 0 && e.scatter == nullptr && e.ncols > 0 &&
+        (e.bias == nullptr || (reinterpret_cast<uintptr_t>(e.bias) & 15) == 0) &&
+        (e.bias2 == nullptr || ((reinterpret_cast<uintptr_t>(e.bias2) & 15) == 0 && (e.bias_split & 3) == 0))) {
+      EpiLinearTma t;
+      if (encode_store_map(&t.tmap, e.out, sh.M, e.ncols, e.ldo)) {
+        t.ncols = e.ncols;
+        t.bias = e.bias;
+        t.bias2 = e.bias2;
+        t.bias_split = e.bias_split;
+        t.act = e.act;
+        t.scale = e.scale;
+        return launch_packed_impl<BN, NSUB, TF32>(a, b, t, sh, st);
+      }
+    }
+  }
+  if constexpr (std::is_same<E, EpiLSTM>::value && NSUB == 1) {
+    const int min_rows = g_tma_store_min_rows.load(std::memory_order_relaxed);
+    if (min_rows >= 0 && sh.M >= min_rows && sh.m_dev == nullptr && e.vec && e.DP == kLstmGroup &&
+        e.H % kLstmGroup == 0 && e.h_out != nullptr && e.c_out != nullptr) {
+      EpiLSTM t = e;
+      t.tma = 1;
+      const int gcols = 64 * (e.H / kLstmGroup);
+      if ((e.gates == nullptr || encode_store_map(&t.map_g, e.gates, sh.M, gcols, gcols, 32)) &&
+          encode_store_map(&t.map_c, e.c_out, sh.M, e.H, e.H, 16) &&
+          encode_store_map(&t.map_h, e.h_out, sh.M, e.H, e.H, 16))
+        return launch_packed_impl<BN, NSUB, TF32>(a, b, t, sh, st);
+    }
+  }
+  return launch_packed_impl<BN, NSUB, TF32>(a, b, e, sh, st);
+}
+
+template <int BN, int NSUB, bool TF32, class A, class B, class E>
+static bool launch_packed_impl(const A& a, const B& b, const E& e, const GemmShape& sh, cudaStream_t st) {
   constexpr int B_ROWS = BN * NSUB;
   constexpr int smem = packed_smem_bytes<BN, NSUB, E>();
   constexpr bool kPrepackedA = is_prepacked<A>::value;

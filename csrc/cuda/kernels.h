@@ -24,6 +24,10 @@ int num_sms(int device);
 // may also ask for tf32 itself): bf16 (default) or tf32.
 void set_gemm_precision(bool tf32);
 bool gemm_precision_tf32();
+// Packed GEMMs with plain fp32 outputs and at least this many rows store their
+// tiles with TMA (negative: never).
+void set_tma_store_min_rows(int rows);
+int tma_store_min_rows();
 
 // ---- tcgen05 GEMM entry points (one overload per producer/epilogue combo) ---
 void gemm(const SegSource& a, const WeightSource& b, const EpiLinear& e, const GemmShape& sh, cudaStream_t st);
@@ -83,8 +87,8 @@ void launch_tgn_mailbox(dim3 grid, dim3 block, cudaStream_t st, const int64_t* _
                                    const int* __restrict__ win, const int* __restrict__ cnt,
                                    const int* __restrict__ src_idx, const int* __restrict__ dst_idx,
                                    const int64_t* __restrict__ ev_eid, const float* __restrict__ ev_ts,
-                                   const float* __restrict__ mem_prev, int D, const float* __restrict__ efeat,
-                                   int efeat_ld, int e_raw, int E, float* __restrict__ mailbox,
+                                   const float* __restrict__ mem_prev, int D, const void* __restrict__ efeat,
+                                   int efeat_bf16, int efeat_ld, int e_raw, int E, float* __restrict__ mailbox,
                                    float* __restrict__ mailbox_ts, int64_t* __restrict__ next_pos, int K);
 void launch_tgn_attn_fwd(dim3 grid, dim3 block, cudaStream_t st, const float* __restrict__ Q, const float* __restrict__ KV,
                                     const int* __restrict__ cnt, const int* __restrict__ n_roots, int rmax, int k,

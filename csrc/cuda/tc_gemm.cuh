@@ -388,6 +388,20 @@ __device__ __forceinline__ float apply_act(float v, int act) {
   }
 }
 
+template <int ACT>
+__device__ __forceinline__ float act_ct(float v) {
+  if constexpr (ACT == kActRelu) return fmaxf(v, 0.f);
+  else if constexpr (ACT == kActSigmoid) return sigmoidf_(v);
+  else if constexpr (ACT == kActTanh) return tanhf(v);
+  else return v;
+}
+
+// Bias of 4 consecutive columns [col, col + 4) of a linear epilogue with an
+// optional second bias from column `split` on (split % 4 == 0, both 16-byte aligned).
+__device__ __forceinline__ float4 bias4(const float* b, const float* b2, int split, int col) {
+  const float* p = col < split ? (b ? b + col : nullptr) : (b2 ? b2 + (col - split) : nullptr);
+  return p ? __ldg(reinterpret_cast<const float4*>(p)) : make_float4(0.f, 0.f, 0.f, 0.f);
+}
 #endif  // __CUDACC__
 
 // out[row, col] (=|+=) act(scale * acc + bias[col]); optional row scatter.
@@ -407,6 +421,56 @@ struct EpiLinear {
   const int64_t* scatter = nullptr;  // row -> output row
 
 #ifdef __CUDACC__
+  // Per batch of up to 64 columns: every TMEM load and the columns' bias (the same
+  // for every row: broadcast loads) are in flight together before one wait.
+  // Plain fp32 stores of whole 16-column groups run a loop specialised on the
+  // activation (a warp-uniform switch outside it); a runtime activation switch or
+  // a bias load inside the per-element loop costs several times the stores
+  // themselves. Everything else (scatter rows, accumulation, bf16 copies, ragged
+  // column groups) takes the generic per-element path.
+  __device__ __forceinline__ bool vec_bias_ok() const {
+    return (bias == nullptr || (reinterpret_cast<uintptr_t>(bias) & 15) == 0) &&
+           (bias2 == nullptr || ((reinterpret_cast<uintptr_t>(bias2) & 15) == 0 && (bias_split & 3) == 0));
+  }
+  template <int ACT>
+  __device__ __forceinline__ void store16(float* o, const uint32_t* r, const float4* b) const {
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      reinterpret_cast<float4*>(o)[j] =
+          make_float4(act_ct<ACT>(fmaf(scale, __uint_as_float(r[4 * j]), b[j].x)),
+                      act_ct<ACT>(fmaf(scale, __uint_as_float(r[4 * j + 1]), b[j].y)),
+                      act_ct<ACT>(fmaf(scale, __uint_as_float(r[4 * j + 2]), b[j].z)),
+                      act_ct<ACT>(fmaf(scale, __uint_as_float(r[4 * j + 3]), b[j].w)));
+    }
+  }
+  template <int ACT>
+  __device__ __forceinline__ void store_groups(float* o, int groups, const uint32_t (&r)[64],
+                                               const float4 (&b)[16]) const {
+#pragma unroll
+    for (int k = 0; k < 4; ++k)
+      if (k < groups) store16<ACT>(o + 16 * k, r + 16 * k, b + 4 * k);
+  }
+  struct Vals16 {
+    float v[16];
+  };
+  // Generic per-element stores of up to 16 columns from col0 (scatter rows,
+  // accumulation, bf16 copies, ragged groups). Out of line: inlined once per
+  // column group, its runtime activation switch made the epilogue's code large
+  // enough to slow every tile.
+  __device__ __noinline__ void store_generic(int64_t orow, int col0, int n, Vals16 x) const {
+    for (int i = 0; i < n; ++i) {
+      const int col = col0 + i;
+      const float bv = col < bias_split ? (bias ? bias[col] : 0.f) : (bias2 ? bias2[col - bias_split] : 0.f);
+      const float y = apply_act(scale * x.v[i] + bv, act);
+      if (out != nullptr) {
+        float* o = out + orow * ldo + col;
+        if (accumulate == 2) atomicAdd(o, y);
+        else if (accumulate == 1) *o += y;
+        else *o = y;
+      }
+      if (out_bf16) out_bf16[orow * ldo + col] = __float2bfloat16(y);
+    }
+  }
   __device__ __forceinline__ void operator()(int row, bool valid, int n0, uint32_t taddr, int tile_cols) const {
     int64_t orow = row;
     if (valid && scatter != nullptr) {
@@ -414,45 +478,140 @@ struct EpiLinear {
       if (orow < 0) valid = false;
     }
     const int lim = min(ncols - n0, tile_cols);
-    // plain stores of whole 16-column groups go out as four 16-byte vectors
     const bool vec_ok = out != nullptr && accumulate == 0 && out_bf16 == nullptr && (ldo & 3) == 0 &&
-                        (reinterpret_cast<uintptr_t>(out) & 15) == 0;
-    for (int c0 = 0; c0 < lim; c0 += 16) {
-      float v[16];
-      tmem_ld16(taddr + c0, v);  // warp-uniform
-      if (!valid) continue;
-      const int cb = n0 + c0;
-      if (vec_ok && cb + 16 <= ncols && (cb & 3) == 0) {
-        float4* o = reinterpret_cast<float4*>(out + orow * ldo + cb);
+                        (reinterpret_cast<uintptr_t>(out) & 15) == 0 && (n0 & 3) == 0 && vec_bias_ok();
+    for (int b0 = 0; b0 < lim; b0 += 64) {
+      const int cols = min(64, lim - b0);
+      const int groups = vec_ok ? cols / 16 : 0;  // whole 16-column groups on the vector path
+      uint32_t r[64];
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          float x[4];
-#pragma unroll
-          for (int u = 0; u < 4; ++u) {
-            const int col = cb + 4 * j + u;
-            const float bv = col < bias_split ? (bias ? bias[col] : 0.f) : (bias2 ? bias2[col - bias_split] : 0.f);
-            x[u] = apply_act(scale * v[4 * j + u] + bv, act);
-          }
-          o[j] = make_float4(x[0], x[1], x[2], x[3]);
+      for (int k = 0; k < 4; ++k) {
+        if (16 * k < cols) {  // warp-uniform
+          uint32_t (&rk)[16] = *reinterpret_cast<uint32_t (*)[16]>(r + 16 * k);
+          tmem_ld16_issue(taddr + b0 + 16 * k, rk);
         }
-        continue;
+      }
+      float4 b[16];
+#pragma unroll
+      for (int q = 0; q < 16; ++q)
+        b[q] = (q < 4 * groups && valid) ? bias4(bias, bias2, bias_split, n0 + b0 + 4 * q) : make_float4(0.f, 0.f, 0.f, 0.f);
+      tmem_wait_ld_all(r);
+      if (!valid) continue;
+      if (groups > 0) {
+        float* o = out + orow * ldo + n0 + b0;
+        switch (act) {
+          case kActRelu: store_groups<kActRelu>(o, groups, r, b); break;
+          case kActSigmoid: store_groups<kActSigmoid>(o, groups, r, b); break;
+          case kActTanh: store_groups<kActTanh>(o, groups, r, b); break;
+          default: store_groups<kActNone>(o, groups, r, b); break;
+        }
       }
 #pragma unroll
-      for (int i = 0; i < 16; ++i) {
-        const int col = n0 + c0 + i;
-        if (col >= ncols) break;
-        const float bv = col < bias_split ? (bias ? bias[col] : 0.f) : (bias2 ? bias2[col - bias_split] : 0.f);
-        float x = scale * v[i] + bv;
-        x = apply_act(x, act);
-        float* o = out ? out + orow * ldo + col : nullptr;
-        if (o) {
-          if (accumulate == 2) atomicAdd(o, x);
-          else if (accumulate == 1) *o += x;
-          else *o = x;
-        }
-        if (out_bf16) out_bf16[orow * ldo + col] = __float2bfloat16(x);
+      for (int k = 0; k < 4; ++k) {
+        if (16 * k >= cols || k < groups) continue;  // warp-uniform
+        Vals16 x;
+#pragma unroll
+        for (int i = 0; i < 16; ++i) x.v[i] = __uint_as_float(r[16 * k + i]);
+        store_generic(orow, n0 + b0 + 16 * k, min(16, cols - 16 * k), x);
       }
     }
+  }
+#endif
+};
+
+// Plain fp32 stores of EpiLinear (no scatter, no accumulation) for large row
+// counts: each epilogue warp moves its 32 rows x 32 columns from TMEM into a
+// 128-byte-swizzled shared-memory box (conflict-free 16-byte stores) and one
+// lane writes the box out with a tiled TMA store. A warp's plain per-row stores
+// touch 32 cache lines per instruction; the TMA store writes whole lines. Two
+// boxes per warp alternate, so the TMEM loads of chunk k+1 overlap the store of
+// chunk k. Rows past M and columns past ncols are clipped by the tensor map.
+struct EpiLinearTma {
+  static constexpr bool kSplitCols = true;
+  static constexpr int kBoxBytes = 32 * 32 * 4;  // 32 rows x 128 bytes
+  // per 4-warp column half: 4 warps x 2 boxes, then one 1 KB line of per-warp box counters
+  static constexpr int kScratchBytes = 4 * 2 * kBoxBytes + 1024;
+  alignas(64) CUtensorMap tmap;  // [M rows, ncols] fp32, row stride ldo, box 32 x 32, 128-byte swizzle
+  int ncols = 0;
+  const float* bias = nullptr;
+  const float* bias2 = nullptr;
+  int bias_split = 1 << 30;
+  int act = kActNone;
+  float scale = 1.f;
+
+#ifdef __CUDACC__
+  template <int ACT>
+  __device__ __forceinline__ void stage(uint8_t* box, int lane, const uint32_t (&r)[32], const float4 (&b)[8]) const {
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      // 128-byte swizzle: 16-byte chunk j of row `lane` sits at chunk j ^ (lane % 8)
+      *reinterpret_cast<float4*>(box + lane * 128 + ((j ^ (lane & 7)) << 4)) =
+          make_float4(act_ct<ACT>(fmaf(scale, __uint_as_float(r[4 * j]), b[j].x)),
+                      act_ct<ACT>(fmaf(scale, __uint_as_float(r[4 * j + 1]), b[j].y)),
+                      act_ct<ACT>(fmaf(scale, __uint_as_float(r[4 * j + 2]), b[j].z)),
+                      act_ct<ACT>(fmaf(scale, __uint_as_float(r[4 * j + 3]), b[j].w)));
+    }
+  }
+  __device__ __forceinline__ void run(int row, bool /*valid*/, int n0, uint32_t taddr, int tile_cols, float* scratch,
+                                      int /*barrier*/) const {
+    const int lane = threadIdx.x & 31;
+    const int wq = (threadIdx.x >> 5) & 3;
+    uint8_t* base = reinterpret_cast<uint8_t*>(scratch);
+    uint8_t* boxes = base + wq * 2 * kBoxBytes;  // 1024-byte aligned (the swizzle pattern's period)
+    volatile int* counter = reinterpret_cast<volatile int*>(base + 4 * 2 * kBoxBytes) + wq;
+    const int row0 = row - lane;  // first row of this warp's 32
+    const int lim = min(ncols - n0, tile_cols);
+    int k = *counter;  // boxes written so far by this warp (any start value works: only its parity is used)
+    for (int c0 = 0; c0 < lim; c0 += 32, ++k) {
+      uint8_t* box = boxes + (k & 1) * kBoxBytes;
+      uint32_t r[32];
+      {
+        uint32_t (&r0)[16] = *reinterpret_cast<uint32_t (*)[16]>(r);
+        uint32_t (&r1)[16] = *reinterpret_cast<uint32_t (*)[16]>(r + 16);
+        tmem_ld16_issue(taddr + c0, r0);
+        tmem_ld16_issue(taddr + c0 + 16, r1);
+      }
+      float4 b[8];
+#pragma unroll
+      for (int q = 0; q < 8; ++q) {
+        const int col = n0 + c0 + 4 * q;
+        if (col + 4 <= ncols) {
+          b[q] = bias4(bias, bias2, bias_split, col);
+        } else {  // ragged last quad: columns past ncols are clipped by the store
+          float t[4];
+#pragma unroll
+          for (int u = 0; u < 4; ++u) {
+            const int cu = col + u;
+            t[u] = cu >= ncols ? 0.f : cu < bias_split ? (bias ? bias[cu] : 0.f) : (bias2 ? bias2[cu - bias_split] : 0.f);
+          }
+          b[q] = make_float4(t[0], t[1], t[2], t[3]);
+        }
+      }
+      tmem_wait_ld_all(r);
+      // the store issued from this box two chunks ago must have finished reading it
+      if (lane == 0) bulk_wait_group_read<1>();
+      __syncwarp();
+      switch (act) {
+        case kActRelu: stage<kActRelu>(box, lane, r, b); break;
+        case kActSigmoid: stage<kActSigmoid>(box, lane, r, b); break;
+        case kActTanh: stage<kActTanh>(box, lane, r, b); break;
+        default: stage<kActNone>(box, lane, r, b); break;
+      }
+      fence_proxy_async_smem();  // generic-proxy writes visible to the TMA engine
+      __syncwarp();
+      if (lane == 0) {
+        tma_store_2d(&tmap, box, n0 + c0, row0);
+        bulk_commit_group();
+      }
+    }
+    __syncwarp();
+    if (lane == 0) *counter = k;
+    __syncwarp();
+  }
+  // after the last tile: this warp's stores complete before the CTA (and its shared memory) goes away
+  __device__ __forceinline__ void finish() const {
+    if ((threadIdx.x & 31) == 0) bulk_wait_group<0>();
+    __syncwarp();
   }
 #endif
 };

@@ -20,6 +20,7 @@
 #pragma once
 
 #include <type_traits>
+#include <utility>
 
 #include "tc_gemm.cuh"
 
@@ -69,6 +70,13 @@ template <class Epi, class = void>
 struct has_prefetch : std::false_type {};
 template <class Epi>
 struct has_prefetch<Epi, std::void_t<decltype(Epi::kPrefetch)>> : std::integral_constant<bool, Epi::kPrefetch> {};
+
+// Epilogues that issue asynchronous stores (TMA) declare finish(), run by every
+// epilogue thread after its last tile, before the CTA's shared memory is released.
+template <class Epi, class = void>
+struct has_finish : std::false_type {};
+template <class Epi>
+struct has_finish<Epi, std::void_t<decltype(std::declval<const Epi&>().finish())>> : std::true_type {};
 #endif
 
 // K elements per 128-byte chunk row of a packed image: 64 bf16 or 32 tf32
@@ -342,6 +350,9 @@ __global__ void __launch_bounds__(kPackedThreads, 1)
       tc_fence_before();
       mbar_arrive(&acc_empty[slot]);
       ++tl;
+    }
+    if constexpr (has_finish<Epi>::value) {
+      if (active) epi.finish();
     }
   } else if (warp == kProducerWarp) {
     // --------------------------- copy producer ----------------------------

@@ -207,8 +207,8 @@ __global__ void tgn_mailbox_kernel(const int64_t* __restrict__ roots, const int*
                                    const int* __restrict__ win, const int* __restrict__ cnt,
                                    const int* __restrict__ src_idx, const int* __restrict__ dst_idx,
                                    const int64_t* __restrict__ ev_eid, const float* __restrict__ ev_ts,
-                                   const float* __restrict__ mem_prev, int D, const float* __restrict__ efeat,
-                                   int efeat_ld, int e_raw, int E, float* __restrict__ mailbox,
+                                   const float* __restrict__ mem_prev, int D, const void* __restrict__ efeat,
+                                   int efeat_bf16, int efeat_ld, int e_raw, int E, float* __restrict__ mailbox,
                                    float* __restrict__ mailbox_ts, int64_t* __restrict__ next_pos, int K) {
   const int r = blockIdx.x;
   if (r >= *n_roots || r >= rmax) return;
@@ -230,7 +230,10 @@ __global__ void tgn_mailbox_kernel(const int64_t* __restrict__ roots, const int*
       else if (c < 2 * D) x = mem_prev[(int64_t)other * D + (c - D)];
       else {
         const int ce = c - 2 * D;
-        x = (ce < e_raw) ? efeat[e * efeat_ld + ce] : 0.f;
+        x = 0.f;
+        if (ce < e_raw)
+          x = efeat_bf16 ? __bfloat162float(static_cast<const __nv_bfloat16*>(efeat)[e * efeat_ld + ce])
+                         : static_cast<const float*>(efeat)[e * efeat_ld + ce];
       }
       slot[c] = x;
     }
@@ -737,11 +740,11 @@ void launch_tgn_mailbox(dim3 grid, dim3 block, cudaStream_t st, const int64_t* _
                                    const int* __restrict__ win, const int* __restrict__ cnt,
                                    const int* __restrict__ src_idx, const int* __restrict__ dst_idx,
                                    const int64_t* __restrict__ ev_eid, const float* __restrict__ ev_ts,
-                                   const float* __restrict__ mem_prev, int D, const float* __restrict__ efeat,
-                                   int efeat_ld, int e_raw, int E, float* __restrict__ mailbox,
+                                   const float* __restrict__ mem_prev, int D, const void* __restrict__ efeat,
+                                   int efeat_bf16, int efeat_ld, int e_raw, int E, float* __restrict__ mailbox,
                                    float* __restrict__ mailbox_ts, int64_t* __restrict__ next_pos, int K) {
   count_launch();
-  tgn_mailbox_kernel<<<grid, block, 0, st>>>(roots, n_roots, rmax, win, cnt, src_idx, dst_idx, ev_eid, ev_ts, mem_prev, D, efeat, efeat_ld, e_raw, E, mailbox, mailbox_ts, next_pos, K);
+  tgn_mailbox_kernel<<<grid, block, 0, st>>>(roots, n_roots, rmax, win, cnt, src_idx, dst_idx, ev_eid, ev_ts, mem_prev, D, efeat, efeat_bf16, efeat_ld, e_raw, E, mailbox, mailbox_ts, next_pos, K);
 }
 
 void launch_tgn_attn_fwd(dim3 grid, dim3 block, cudaStream_t st, const float* __restrict__ Q, const float* __restrict__ KV,

@@ -8,6 +8,8 @@ namespace su {
 long long launch_count();
 void set_gemm_precision(bool tf32);
 bool gemm_precision_tf32();
+void set_tma_store_min_rows(int rows);
+int tma_store_min_rows();
 using WorkspaceAlloc = void* (*)(size_t bytes, cudaStream_t stream);
 using WorkspaceFree = void (*)(void* ptr);
 void set_workspace_allocator(WorkspaceAlloc alloc, WorkspaceFree free_fn);
@@ -176,6 +178,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("set_gemm_precision", &su::set_gemm_precision, "tensor-core operand precision of the GEMMs: tf32 or bf16",
         py::arg("tf32"));
   m.def("gemm_precision_tf32", &su::gemm_precision_tf32);
+  m.def("set_tma_store_min_rows", &su::set_tma_store_min_rows,
+        "packed GEMMs with plain fp32 outputs of at least this many rows store tiles with TMA (negative: never)");
+  m.def("tma_store_min_rows", &su::tma_store_min_rows);
   su::set_workspace_allocator(&su_ws_alloc, &su_ws_free);
   m.def("linear_fwd", &linear_fwd);
   m.def("linear_dgrad", &linear_dgrad);

@@ -67,15 +67,22 @@ inline ASeg seg_f32(const at::Tensor& m, int width, int kpad, const int64_t* ind
   return s;
 }
 // bf16 matrix segment (row-major)
-inline ASeg seg_bf16(const at::Tensor& m, int width, int kpad) {
+inline ASeg seg_bf16(const at::Tensor& m, int width, int kpad, const int64_t* index = nullptr) {
   ASeg s;
   s.kind = kSegBF16;
   s.ptr = m.data_ptr();
   s.ld = static_cast<int>(m.stride(0));
   s.width = width;
   s.kpad = kpad;
+  s.index = index;
   s.vec = ((s.ld % 8) == 0 && (reinterpret_cast<uintptr_t>(s.ptr) % 16) == 0) ? 1 : 0;
   return s;
+}
+// edge-feature rows (fp32 or bf16 storage), gathered through `index`
+inline ASeg seg_feat(const at::Tensor& m, int width, int kpad, const int64_t* index) {
+  TORCH_CHECK(m.scalar_type() == at::kFloat || m.scalar_type() == at::kBFloat16,
+              "edge features must be float32 or bfloat16");
+  return m.scalar_type() == at::kBFloat16 ? seg_bf16(m, width, kpad, index) : seg_f32(m, width, kpad, index);
 }
 inline ASeg seg_time(const float* dt, const at::Tensor& w, const at::Tensor& b, int kpad) {
   ASeg s;

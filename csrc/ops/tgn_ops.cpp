@@ -274,7 +274,8 @@ void tgn_mailbox_write(const at::Tensor& roots, const at::Tensor& n_roots, const
   launch_tgn_mailbox(dim3(rmax), dim3(128), cur_stream(), 
       roots.data_ptr<int64_t>(), n_roots.data_ptr<int>(), rmax, win.data_ptr<int>(), cnt.data_ptr<int>(),
       src_idx.data_ptr<int>(), dst_idx.data_ptr<int>(), ev_eid.data_ptr<int64_t>(), ev_ts.data_ptr<float>(),
-      mem_prev.data_ptr<float>(), D, efeat.data_ptr<float>(), static_cast<int>(efeat.stride(0)),
+      mem_prev.data_ptr<float>(), D, efeat.data_ptr(), efeat.scalar_type() == at::kBFloat16 ? 1 : 0,
+      static_cast<int>(efeat.stride(0)),
       static_cast<int>(efeat.size(1)), static_cast<int>(E), mailbox.data_ptr<float>(), mailbox_ts.data_ptr<float>(),
       next_pos.data_ptr<int64_t>(), K);
   SU_LAUNCH_CHECK();
@@ -330,7 +331,7 @@ void tgn_attn_proj(const at::Tensor& memory, const at::Tensor& roots, const at::
     a.gcount = nbr_cnt.data_ptr<int>();
     a.nseg = 3;
     a.seg[0] = seg_memory(memory, D, nbr.data_ptr<int64_t>(), pd, true);
-    a.seg[1] = seg_f32(efeat, Ew, pad8(static_cast<int>(E)), nbr_eid.data_ptr<int64_t>());
+    a.seg[1] = seg_feat(efeat, Ew, pad8(static_cast<int>(E)), nbr_eid.data_ptr<int64_t>());
     a.seg[2] = seg_time(nbr_dt.data_ptr<float>(), te_w, te_b, pad8(T));
     WeightSource b;
     b.L.nblk = 2;
@@ -540,7 +541,7 @@ void tgn_attn_proj_bwd(const at::Tensor& memory, const at::Tensor& roots, const 
     x.gcount = nbr_cnt.data_ptr<int>();
     x.nseg = 6;
     x.seg[0] = seg_memory(memory, D, nbr.data_ptr<int64_t>(), pd, true);
-    x.seg[1] = seg_f32(efeat, Ew, pad8(Ei), nbr_eid.data_ptr<int64_t>());
+    x.seg[1] = seg_feat(efeat, Ew, pad8(Ei), nbr_eid.data_ptr<int64_t>());
     x.seg[2] = seg_time(nbr_dt.data_ptr<float>(), te_w, te_b, pad8(T));
     x.seg[3] = seg_ones();
     x.seg[4] = seg_time(nbr_dt.data_ptr<float>(), te_w, te_b, pad8(T));

@@ -125,6 +125,9 @@ def _synthetic_events(dataset_name: str, config: dict[str, Any]) -> RawTemporalE
     seed = int(spec.pop("seed", 0))
     params = dict(CTDG_PRESETS[preset]) if preset else {}
     params.update(spec)
+    if isinstance(params.get("edge_dtype"), str):  # YAML spelling: bf16 / bfloat16 / fp32 / float32
+        names = {"bf16": torch.bfloat16, "bfloat16": torch.bfloat16, "fp32": torch.float32, "float32": torch.float32}
+        params["edge_dtype"] = names[params["edge_dtype"].lower()]
     stream = zipf_event_stream(**params, seed=seed)
     n = int(stream["src"].numel())
     return RawTemporalEvents(

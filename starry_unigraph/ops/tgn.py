@@ -125,7 +125,11 @@ class TGNCudaEngine:
         self.use_graphs = bool(use_graphs)
         self.csr_provider = csr_provider
         self.grad_sync = grad_sync
-        ef = edge_feat.to(dev, dtype=torch.float32)
+        # bf16 edge features stay bf16 on the device (the operand producers, the
+        # mailbox kernels and the peer mail write read them as bf16); others are fp32
+        ef = edge_feat.to(dev)
+        if ef.dtype not in (torch.float32, torch.bfloat16):
+            ef = ef.float()
         if ef.dim() == 1:
             ef = ef.view(-1, 1)
         self.efeat = ef.contiguous()

@@ -134,3 +134,65 @@ def test_linear_dgrad_wgrad_tf32(tf32, M, K, N):
     C.linear_wgrad(dy, x, dw, db)
     assert _rel(dw, _fp32_ref(lambda: dy.t() @ x)) < 2e-3
     assert _rel(db, dy.sum(0)) < 1e-3  # the bias gradient comes from a ones column of the tf32 GEMM
+
+
+@pytest.fixture
+def tma_rows():
+    """Restores the TMA-store row threshold after a test that changes it."""
+    C = _C()
+    old = C.tma_store_min_rows()
+    yield C
+    C.set_tma_store_min_rows(old)
+
+
+@pytest.mark.parametrize("M,K,N,act", [(2048, 64, 64, 0), (5000, 64, 100, 1), (20011, 128, 256, 0),
+                                       (333, 96, 48, 3), (4099, 216, 130, 2)])
+def test_linear_tma_store_matches_direct_stores(tma_rows, M, K, N, act):
+    """The TMA-store epilogue (swizzled shared-memory boxes, tiled bulk stores)
+    writes exactly what the per-row store epilogue writes, clipped to M x N."""
+    C = tma_rows
+    torch.manual_seed(1)
+    x = torch.randn(M, K, device="cuda")
+    w = torch.randn(N, K, device="cuda") / K ** 0.5
+    b = torch.randn(N, device="cuda")
+    C.set_tma_store_min_rows(0)
+    y_tma = C.linear_fwd(x, w, b, act)
+    gx_tma = C.linear_dgrad(y_tma, w)
+    C.set_tma_store_min_rows(-1)
+    y_dir = C.linear_fwd(x, w, b, act)
+    gx_dir = C.linear_dgrad(y_dir, w)
+    torch.cuda.synchronize()
+    assert C.status_read(True) == 0
+    assert torch.equal(y_tma, y_dir)
+    assert torch.equal(gx_tma, gx_dir)
+    z = x @ w.t() + b
+    ref = {0: z, 1: torch.relu(z), 2: torch.sigmoid(z), 3: torch.tanh(z)}[act]
+    assert _rel(y_tma, ref) < 1.5e-2
+
+
+
+@pytest.mark.parametrize("rows,IN,H,with_c", [(2500, 64, 64, True), (20011, 32, 48, False), (4096, 100, 32, True)])
+def test_lstm_tma_store_matches_staged_stores(tma_rows, rows, IN, H, with_c):
+    """The LSTM cell epilogue's TMA-store path (swizzled shared-memory boxes of
+    the gates, c' and h') writes exactly what its staged-store path writes."""
+    C = tma_rows
+    torch.manual_seed(2)
+    x = torch.randn(rows, IN, device="cuda")
+    h = torch.randn(rows, H, device="cuda")
+    c = torch.randn(rows, H, device="cuda") if with_c else None
+    w = [torch.randn(H, IN + H, device="cuda") * 0.1 for _ in range(4)]
+    b = [torch.randn(H, device="cuda") * 0.1 for _ in range(4)]
+    args = (x, h, c, w[0], b[0], w[1], b[1], w[2], b[2], w[3], b[3], True)
+    C.set_tma_store_min_rows(0)
+    h1, c1, g1 = C.lstm_fwd(*args)
+    C.set_tma_store_min_rows(-1)
+    h2, c2, g2 = C.lstm_fwd(*args)
+    torch.cuda.synchronize()
+    assert C.status_read(True) == 0
+    assert torch.equal(h1, h2) and torch.equal(c1, c2) and torch.equal(g1, g2)
+    # and against the fp32 math of one nn.Linear per gate over [x || h]
+    xh = torch.cat([x, h], 1)
+    i, f, g, o = (xh @ w[k].t() + b[k] for k in range(4))
+    cn = torch.sigmoid(f) * (c if with_c else 0) + torch.sigmoid(i) * torch.tanh(g)
+    hn = torch.sigmoid(o) * torch.tanh(cn)
+    assert _rel(c1, cn) < 2e-2 and _rel(h1, hn) < 2e-2

@@ -179,13 +179,18 @@ def _jodie_session(device, tmp_path, **over):
     return s
 
 
-@pytest.mark.parametrize("precision", ["tf32", "bf16"])
-def test_jodie_fused_step_matches_cpu_oracle(tmp_path, precision):
+@pytest.mark.parametrize("precision,edge_dtype", [("tf32", "fp32"), ("bf16", "fp32"), ("bf16", "bf16")])
+def test_jodie_fused_step_matches_cpu_oracle(tmp_path, precision, edge_dtype):
     """JODIE (tanh-RNN memory + time projection): losses, predictions, memory and
-    mailbox (lr = 0), then the gradients of the trainable parameters."""
+    mailbox (lr = 0), then the gradients of the trainable parameters. With bf16
+    edge features (the JODIE config's storage) the device keeps them in bf16 and
+    the CPU path widens the same values."""
     tol = TOL[precision]
-    g = _jodie_session("cuda", tmp_path, train={"lr": 0.0}, runtime={"precision": precision})
-    c = _jodie_session("cpu", tmp_path, train={"lr": 0.0})
+    data = {"synthetic": dict(_cfg("cpu")["data"]["synthetic"], edge_dtype=edge_dtype)}
+    g = _jodie_session("cuda", tmp_path, train={"lr": 0.0}, runtime={"precision": precision}, data=data)
+    c = _jodie_session("cpu", tmp_path, train={"lr": 0.0}, data=data)
+    if edge_dtype == "bf16":
+        assert g.ctdg_session.online_runtime.engine.efeat.dtype == torch.bfloat16
     rg, rc = g.ctdg_session.online_runtime, c.ctdg_session.online_runtime
     assert rg.engine is not None and rg.engine.kind == "jodie"
     eng = rg.engine
