@@ -291,6 +291,14 @@ def _dtdg_run(args, workload: str, steps: int, warmup: int) -> dict:
     torch.cuda.synchronize()
     e2e_s = time.perf_counter() - t0
     barrier()
+    # this rank's own device time and work (edges of every window graph it aggregated, its rows)
+    own_edges = sum(int(st.graph.edge_src.numel()) for b in timed for st in b.steps)
+    own_rows = int(timed[0].steps[-1].graph.num_dst_nodes) if timed and timed[0].steps else 0
+    mine = torch.tensor([dev_ms, float(own_edges), float(own_rows)], dtype=torch.float64, device="cuda")
+    per_rank = [mine]
+    if world > 1:
+        per_rank = [torch.empty_like(mine) for _ in range(world)]
+        dist.all_gather(per_rank, mine)
     stats = torch.tensor([dev_ms, e2e_s], dtype=torch.float64, device="cuda")
     if world > 1:
         dist.all_reduce(stats, op=dist.ReduceOp.MAX)
@@ -314,6 +322,9 @@ def _dtdg_run(args, workload: str, steps: int, warmup: int) -> dict:
         "e2e": {"value": steps / e2e_s, "unit": "snapshots/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 4,
                 "note": "snapshots resident on the device (dtdg.resident); the loss is read back every step"},
         "prep_s": prep_s, "last_loss": last_loss,
+        # per rank: device ms per step, aggregated edges per step (all window graphs), owned rows
+        "per_rank": [{"ms_per_step": round(float(t[0]) / steps, 3), "edges_per_step": int(float(t[1]) / steps),
+                      "rows": int(t[2])} for t in per_rank],
     }
     if world > 1:
         out["consistency"] = _replicas_equal(rt.optimizer.flat.data if hasattr(rt.optimizer, "flat") else
