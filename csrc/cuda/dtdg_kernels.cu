@@ -49,8 +49,9 @@ struct TwoTables {
   const float* halo;
   int n_split;
   int F;
+  int ld;  // row stride of x (>= F: rows of a wider staging buffer)
   __device__ __forceinline__ const float* row(int c) const {
-    return c < n_split ? x + static_cast<int64_t>(c) * F : halo + static_cast<int64_t>(c - n_split) * F;
+    return c < n_split ? x + static_cast<int64_t>(c) * ld : halo + static_cast<int64_t>(c - n_split) * F;
   }
 };
 // where a finished row segment goes: this rank's output (plain store for rows
@@ -373,10 +374,10 @@ void launch_halo_pull(cudaStream_t st, const float* const* peers, const int* own
 // Aggregation over [this rank's rows | pulled halo rows] (columns remapped once
 // per graph: local sources -> their row in x, halo sources -> n_split + pull slot).
 void launch_spmm_two_tables(cudaStream_t st, const int64_t* rowptr, const int* col, const float* val, const float* x,
-                            const float* halo, int n_split, int64_t n_rows, int F, float* out) {
+                            int x_ld, const float* halo, int n_split, int64_t n_rows, int F, float* out) {
   if (n_rows == 0) return;
   cudaMemsetAsync(out, 0, static_cast<size_t>(n_rows) * F * sizeof(float), st);
-  launch_chunked(st, rowptr, col, val, TwoTables{x, halo, n_split, F}, n_rows, F, LocalOut{out, F, 0});
+  launch_chunked(st, rowptr, col, val, TwoTables{x, halo, n_split, F, x_ld}, n_rows, F, LocalOut{out, F, 0});
 }
 
 // Its backward over the transposed CSR (rows = source rows): each source row's

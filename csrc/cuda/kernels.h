@@ -151,7 +151,7 @@ void launch_spmm_peer_gather(cudaStream_t st, const int64_t* rowptr, const int* 
 void launch_halo_pull(cudaStream_t st, const float* const* peers, const int* owner, const int* lrow,
                       const int* halo_src, int64_t n_halo, int F, int ld, float* out);
 void launch_spmm_two_tables(cudaStream_t st, const int64_t* rowptr, const int* col, const float* val, const float* x,
-                            const float* halo, int n_split, int64_t n_rows, int F, float* out);
+                            int x_ld, const float* halo, int n_split, int64_t n_rows, int F, float* out);
 void launch_spmm_peer_push(cudaStream_t st, const int64_t* rowptr_t, const int* col_t, const float* val_t,
                            const float* grad_dst, int64_t n_src, int F, int ld, float* const* peers,
                            const int* src_owner, const int* src_row);

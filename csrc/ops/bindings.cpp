@@ -21,6 +21,8 @@ static void* su_ws_alloc(size_t bytes, cudaStream_t st) {
 }
 static void su_ws_free(void* p) { c10::cuda::CUDACachingAllocator::raw_delete(p); }
 at::Tensor linear_fwd(const at::Tensor& x, const at::Tensor& w, const c10::optional<at::Tensor>& bias, int64_t act);
+void linear_fwd_into(const at::Tensor& x, const at::Tensor& w, const c10::optional<at::Tensor>& bias, int64_t act,
+                     at::Tensor& out);
 at::Tensor linear_dgrad(const at::Tensor& dy, const at::Tensor& w);
 void linear_wgrad(const at::Tensor& dy, const at::Tensor& x, at::Tensor& dw, const c10::optional<at::Tensor>& db);
 
@@ -183,6 +185,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("tma_store_min_rows", &su::tma_store_min_rows);
   su::set_workspace_allocator(&su_ws_alloc, &su_ws_free);
   m.def("linear_fwd", &linear_fwd);
+  m.def("linear_fwd_into", &linear_fwd_into);
   m.def("linear_dgrad", &linear_dgrad);
   m.def("linear_wgrad", &linear_wgrad);
   m.def("tgn_prep", &tgn_prep);

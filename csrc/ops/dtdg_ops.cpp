@@ -274,13 +274,16 @@ at::Tensor halo_pull(const at::Tensor& peers, const at::Tensor& src_owner, const
 
 at::Tensor spmm_two_tables(const at::Tensor& rowptr, const at::Tensor& col, const at::Tensor& val,
                            const at::Tensor& x, const at::Tensor& halo, int64_t n_rows) {
-  SU_CHECK_I64(rowptr); SU_CHECK_I32(col); SU_CHECK_F32(val); SU_CHECK_F32(x); SU_CHECK_CONTIG(x);
+  SU_CHECK_I64(rowptr); SU_CHECK_I32(col); SU_CHECK_F32(val); SU_CHECK_F32(x);
+  TORCH_CHECK(x.dim() == 2 && x.stride(1) == 1, "x must be a row-major matrix (any row stride)");
   SU_CHECK_F32(halo); SU_CHECK_CONTIG(halo);
   const int F = static_cast<int>(x.size(1));
   TORCH_CHECK(halo.numel() == 0 || halo.size(1) == F, "halo rows must have the width of x");
+  TORCH_CHECK(F % 4 != 0 || (x.stride(0) % 4 == 0 && (reinterpret_cast<uintptr_t>(x.data_ptr()) & 15) == 0),
+              "row-strided x needs 16-byte aligned rows");
   at::Tensor out = at::empty({n_rows, F}, x.options());
   launch_spmm_two_tables(cur_stream(), rowptr.data_ptr<int64_t>(), col.data_ptr<int>(), val.data_ptr<float>(),
-                         x.data_ptr<float>(), halo.numel() ? halo.data_ptr<float>() : nullptr,
+                         x.data_ptr<float>(), static_cast<int>(x.stride(0)), halo.numel() ? halo.data_ptr<float>() : nullptr,
                          static_cast<int>(x.size(0)), n_rows, F, out.data_ptr<float>());
   SU_LAUNCH_CHECK();
   return out;

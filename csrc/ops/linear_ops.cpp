@@ -32,13 +32,10 @@ static WeightLayout single_weight_layout(const at::Tensor& w) {
   return L;
 }
 
-at::Tensor linear_fwd(const at::Tensor& x, const at::Tensor& w, const c10::optional<at::Tensor>& bias, int64_t act) {
-  SU_CHECK_CUDA(x); SU_CHECK_F32(x); SU_CHECK_F32(w); SU_CHECK_CONTIG(w);
-  TORCH_CHECK(x.dim() == 2 && x.stride(1) == 1, "x must be a row-major matrix");
+static void linear_fwd_impl(const at::Tensor& x, const at::Tensor& w, const c10::optional<at::Tensor>& bias,
+                            int64_t act, at::Tensor& y) {
   const int M = static_cast<int>(x.size(0)), K = static_cast<int>(x.size(1)), N = static_cast<int>(w.size(0));
-  TORCH_CHECK(w.size(1) == K, "shape mismatch");
-  auto y = at::empty({M, N}, x.options());
-  if (M == 0) return y;
+  if (M == 0) return;
   SegSource a;
   a.nseg = 1;
   a.seg[0] = seg_f32(x, K, pad8(K));
@@ -46,7 +43,7 @@ at::Tensor linear_fwd(const at::Tensor& x, const at::Tensor& w, const c10::optio
   b.L = single_weight_layout(w);
   EpiLinear e;
   e.out = y.data_ptr<float>();
-  e.ldo = N;
+  e.ldo = static_cast<int>(y.stride(0));
   e.ncols = N;
   e.bias = opt_ptr<float>(bias);
   e.act = static_cast<int>(act);
@@ -56,7 +53,28 @@ at::Tensor linear_fwd(const at::Tensor& x, const at::Tensor& w, const c10::optio
   sh.K = pad8(K);
   gemm(a, b, e, sh, cur_stream());
   SU_LAUNCH_CHECK();
+}
+
+at::Tensor linear_fwd(const at::Tensor& x, const at::Tensor& w, const c10::optional<at::Tensor>& bias, int64_t act) {
+  SU_CHECK_CUDA(x); SU_CHECK_F32(x); SU_CHECK_F32(w); SU_CHECK_CONTIG(w);
+  TORCH_CHECK(x.dim() == 2 && x.stride(1) == 1, "x must be a row-major matrix");
+  TORCH_CHECK(w.size(1) == x.size(1), "shape mismatch");
+  auto y = at::empty({x.size(0), w.size(0)}, x.options());
+  linear_fwd_impl(x, w, bias, act, y);
   return y;
+}
+
+// The same into `out` ([M, N], unit column stride, any row stride): e.g. the rows of a
+// symmetric staging buffer that peer GPUs read.
+void linear_fwd_into(const at::Tensor& x, const at::Tensor& w, const c10::optional<at::Tensor>& bias, int64_t act,
+                     at::Tensor& out) {
+  SU_CHECK_CUDA(x); SU_CHECK_F32(x); SU_CHECK_F32(w); SU_CHECK_CONTIG(w); SU_CHECK_F32(out);
+  TORCH_CHECK(x.dim() == 2 && x.stride(1) == 1, "x must be a row-major matrix");
+  TORCH_CHECK(w.size(1) == x.size(1), "shape mismatch");
+  TORCH_CHECK(out.dim() == 2 && out.size(0) == x.size(0) && out.size(1) == w.size(0) && out.stride(1) == 1 &&
+                  out.stride(0) >= out.size(1),
+              "out must be an [M, N] row-major view");
+  linear_fwd_impl(x, w, bias, act, out);
 }
 
 at::Tensor linear_dgrad(const at::Tensor& dy, const at::Tensor& w) {

@@ -178,14 +178,14 @@ class _HaloAggregate(autograd.Function):
 
 
 def halo_width(model, default: int) -> int:
-    """Feature width of the aggregations that exchange halo rows: the inputs of a
-    GCN stack's second and later layers (its hidden width; the first layer
-    aggregates the block's stored source features and exchanges nothing). T-GCN's
-    stack is 3 x hidden wide, MPNN-LSTM's hidden."""
+    """Feature width of the rows that exchange halo rows: the outputs of a GCN
+    stack's second and later layers, which run their linear map before the
+    exchange (the first layer aggregates the block's stored source features and
+    exchanges nothing). T-GCN's stack is 3 x hidden wide, MPNN-LSTM's hidden."""
     from starry_unigraph.runtime.modules.gcn_layers import GCNStack
 
-    widths = [int(m.layers[0].weight.shape[0]) for m in model.modules()
-              if isinstance(m, GCNStack) and len(m.layers) > 1]
+    widths = [int(layer.weight.shape[0]) for m in model.modules() if isinstance(m, GCNStack)
+              for layer in list(m.layers)[1:]]
     return max(widths) if widths else int(default)
 
 

@@ -1,10 +1,14 @@
 """Multi-layer GCN over partitioned snapshot blocks
 (reference runtime/modules/gcn_layers.py:20-165).
 
-Per layer: normalised neighbour aggregation then ``Linear(bias=False)``, ReLU
+Per layer: normalised neighbour aggregation and ``Linear(bias=False)``, ReLU
 between layers. For a block, the first layer aggregates the stored source
-features (local rows + halo rows); later layers obtain halo rows through the
-block's ``Route`` (peer exchange) when running distributed, or zero-pad them.
+features (local rows + halo rows), then applies its linear map. Later layers
+exchange halo rows (the block's ``Route`` over NCCL, or peer memory over
+NVLink, when running distributed; zero rows otherwise) and run their linear
+map first: A (H W^T) = (A H) W^T without a bias, so the exchanged rows are the
+layer's output width and, on the NVLink path, the GEMM's epilogue writes them
+straight into the staging buffer the peers read (``parallel/halo_linear.py``).
 """
 from __future__ import annotations
 
@@ -63,6 +67,23 @@ def _gcn_message_pass(graph, x: torch.Tensor, exchange: bool | None = None) -> t
     return gcn_aggregate(graph, src_x)
 
 
+def _linear_then_exchange(graph, x: torch.Tensor, weight: torch.Tensor) -> torch.Tensor:
+    """Normalised neighbour sum of `graph` over the rows of x W^T, whose halo rows
+    come from their owners. On the NVLink path (an active halo context that takes
+    the width) one fused layer; otherwise the linear map, then the message pass."""
+    route = getattr(graph, "route", None)
+    if (x.is_cuda and route is not None and route.send_index is not None and dist.is_available()
+            and dist.is_initialized()):
+        from starry_unigraph.parallel.halo import get_halo_context
+
+        hc = get_halo_context()
+        if hc is not None and int(weight.size(0)) % 4 == 0 and hc.supports(int(weight.size(0))):
+            from starry_unigraph.parallel.halo_linear import halo_linear_aggregate
+
+            return halo_linear_aggregate(graph, x, weight, hc)
+    return _gcn_message_pass(graph, linear(x, weight, None, 0), exchange=True)
+
+
 class GCNStack(nn.Module):
     def __init__(self, input_size: int, hidden_size: int, num_layers: int = 2) -> None:
         super().__init__()
@@ -74,11 +95,18 @@ class GCNStack(nn.Module):
 
     def forward_graph(self, graph, x: torch.Tensor | None = None) -> torch.Tensor:
         h = _graph_input(graph) if x is None else x
+        last = len(self.layers) - 1
         for i, layer in enumerate(self.layers):
-            # the first layer reads the block's stored source rows (halo rows included when the block
-            # has any); every later layer's input covers the destination rows only and exchanges halo rows
-            h = _gcn_message_pass(graph, h.float(), exchange=True if (i > 0 or x is not None) else None)
-            h = linear(h, layer.weight, None, 1 if i < len(self.layers) - 1 else 0)
+            act = 1 if i < last else 0
+            if i > 0 or x is not None:
+                # input over the destination rows only: linear map first, then the exchange
+                h = _linear_then_exchange(graph, h.float(), layer.weight)
+                if act:
+                    h = torch.relu(h)
+            else:
+                # the block's stored source rows (halo rows included when the block has any)
+                h = _gcn_message_pass(graph, h.float(), exchange=None)
+                h = linear(h, layer.weight, None, act)
         return h
 
     def layerwise(self, blob_or_graph) -> list[torch.Tensor]:

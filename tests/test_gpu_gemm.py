@@ -196,3 +196,20 @@ def test_lstm_tma_store_matches_staged_stores(tma_rows, rows, IN, H, with_c):
     cn = torch.sigmoid(f) * (c if with_c else 0) + torch.sigmoid(i) * torch.tanh(g)
     hn = torch.sigmoid(o) * torch.tanh(cn)
     assert _rel(c1, cn) < 2e-2 and _rel(h1, hn) < 2e-2
+
+
+@pytest.mark.parametrize("M,K,N,ld", [(3000, 64, 64, 96), (500, 32, 64, 64), (5000, 128, 48, 128)])
+def test_linear_fwd_into_row_strided_view(tma_rows, M, K, N, ld):
+    """linear_fwd_into writes X W^T into the first N columns of a wider buffer's
+    rows (a staging buffer with row stride ld) and leaves the other columns."""
+    C = tma_rows
+    x = torch.randn(M, K, device="cuda")
+    w = torch.randn(N, K, device="cuda") / K ** 0.5
+    for thr in (0, -1):  # TMA-store and direct-store epilogues
+        C.set_tma_store_min_rows(thr)
+        buf = torch.full((M + 7, ld), 3.0, device="cuda")
+        C.linear_fwd_into(x, w, None, 0, buf[:M, :N])
+        torch.cuda.synchronize()
+        assert C.status_read(True) == 0
+        assert _rel(buf[:M, :N], x @ w.t()) < 1.5e-2
+        assert torch.all(buf[:M, N:] == 3.0) and torch.all(buf[M:] == 3.0)

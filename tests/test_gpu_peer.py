@@ -237,6 +237,11 @@ def test_halo_gather_and_push_kernels():
     col2 = remap[src[order]].int().contiguous()
     out2 = C.spmm_two_tables(rowptr, col2, val[order].contiguous(), stages[0][: counts[0]].contiguous(), halo, n_dst)
     torch.testing.assert_close(out2, ref, rtol=1e-5, atol=1e-5)
+    # local rows read in place from a wider staging buffer (row stride 2F + 4)
+    wide = torch.zeros(counts[0], 2 * F + 4, device="cuda")
+    wide[:, :F] = stages[0][: counts[0]]
+    out3 = C.spmm_two_tables(rowptr, col2, val[order].contiguous(), wide[:, :F], halo, n_dst)
+    torch.testing.assert_close(out3, ref, rtol=1e-5, atol=1e-5)
     # backward push: grad of source rows lands in the owners' buffers
     g = torch.randn(n_dst, F, device="cuda")
     order_t = torch.argsort(src, stable=True)
