@@ -197,6 +197,27 @@ void launch_peer_allreduce_adam(cudaStream_t st, int blocks, const float* const*
 // for its own shard only) and stores the new values into the parameter buffer
 // of every rank, its own included.
 // ---------------------------------------------------------------------------
+// Per thread kRsUnroll float4 of the shard, strided by the grid: all W gradient
+// loads of the group (local and over NVLink) are issued before any arithmetic,
+// so each thread keeps kRsUnroll * W 16-byte loads in flight instead of W.
+constexpr int kRsUnroll = 4;
+
+__device__ __forceinline__ float4 adam4(float4 g, float4& pp, float4& mm, float4& vv, float b1, float b2,
+                                        float eps, float wd, float scale, float step_size, float bc2_sqrt) {
+  float* pa = &pp.x;
+  float* ma = &mm.x;
+  float* va = &vv.x;
+  const float* ga = &g.x;
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const float gr = ga[j] * scale + wd * pa[j];
+    ma[j] = b1 * ma[j] + (1.f - b1) * gr;
+    va[j] = b2 * va[j] + (1.f - b2) * gr * gr;
+    pa[j] -= step_size * ma[j] / (sqrtf(va[j]) / bc2_sqrt + eps);
+  }
+  return pp;
+}
+
 __global__ void peer_rs_adam_ag_kernel(const float* const* __restrict__ grads, float* const* __restrict__ params,
                                        int W, int rank, float* __restrict__ m, float* __restrict__ v, int64_t n4,
                                        int64_t shard4, int64_t* __restrict__ step, unsigned int* __restrict__ done,
@@ -209,32 +230,42 @@ __global__ void peer_rs_adam_ag_kernel(const float* const* __restrict__ grads, f
   const int64_t hi = min(n4, lo + shard4);
   const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
   const float4* mine = reinterpret_cast<const float4*>(params[rank]);
-  for (int64_t i = lo + static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < hi; i += stride) {
-    float4 g = reinterpret_cast<const float4*>(grads[0])[i];
-    for (int q = 1; q < W; ++q) {
-      const float4 h = reinterpret_cast<const float4*>(grads[q])[i];
-      g.x += h.x;
-      g.y += h.y;
-      g.z += h.z;
-      g.w += h.w;
-    }
-    float4 pp = mine[i];
-    float4 mm = reinterpret_cast<float4*>(m)[i];
-    float4 vv = reinterpret_cast<float4*>(v)[i];
-    float* pa = &pp.x;
-    float* ma = &mm.x;
-    float* va = &vv.x;
-    const float* ga = &g.x;
+  for (int64_t base = lo + static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; base < hi;
+       base += stride * kRsUnroll) {
+    float4 g[kRsUnroll];
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      const float gr = ga[j] * scale + wd * pa[j];
-      ma[j] = b1 * ma[j] + (1.f - b1) * gr;
-      va[j] = b2 * va[j] + (1.f - b2) * gr * gr;
-      pa[j] -= step_size * ma[j] / (sqrtf(va[j]) / bc2_sqrt + eps);
+    for (int u = 0; u < kRsUnroll; ++u) {
+      const int64_t i = base + u * stride;
+      g[u] = i < hi ? reinterpret_cast<const float4*>(grads[0])[i] : make_float4(0.f, 0.f, 0.f, 0.f);
     }
-    reinterpret_cast<float4*>(m)[i] = mm;
-    reinterpret_cast<float4*>(v)[i] = vv;
-    for (int q = 0; q < W; ++q) reinterpret_cast<float4*>(params[q])[i] = pp;
+    for (int q = 1; q < W; ++q) {
+      const float4* gq = reinterpret_cast<const float4*>(grads[q]);
+      float4 h[kRsUnroll];
+#pragma unroll
+      for (int u = 0; u < kRsUnroll; ++u) {
+        const int64_t i = base + u * stride;
+        h[u] = i < hi ? gq[i] : make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+#pragma unroll
+      for (int u = 0; u < kRsUnroll; ++u) {  // rank order: every replica sums identically
+        g[u].x += h[u].x;
+        g[u].y += h[u].y;
+        g[u].z += h[u].z;
+        g[u].w += h[u].w;
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < kRsUnroll; ++u) {
+      const int64_t i = base + u * stride;
+      if (i >= hi) break;
+      float4 pp = mine[i];
+      float4 mm = reinterpret_cast<float4*>(m)[i];
+      float4 vv = reinterpret_cast<float4*>(v)[i];
+      adam4(g[u], pp, mm, vv, b1, b2, eps, wd, scale, step_size, bc2_sqrt);
+      reinterpret_cast<float4*>(m)[i] = mm;
+      reinterpret_cast<float4*>(v)[i] = vv;
+      for (int q = 0; q < W; ++q) reinterpret_cast<float4*>(params[q])[i] = pp;
+    }
   }
   __syncthreads();
   if (threadIdx.x == 0) {

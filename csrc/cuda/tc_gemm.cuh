@@ -98,6 +98,10 @@ struct ASeg {
   const int64_t* step_ctr = nullptr;    // the step tag is ((*step_ctr - 1) & 0x3FFFFFFF) + 1
   const float* fresh = nullptr;
   int fresh_ld = 0;
+  // kSegF32 without index, optional: values kept only where mask[row, col] > 0
+  // (the ReLU derivative from the forward output, applied as the operand is packed)
+  const float* mask = nullptr;
+  int mask_ld = 0;
 };
 
 #ifdef __CUDACC__
@@ -127,9 +131,23 @@ __device__ __forceinline__ void seg_fill8(const ASeg& g, int row, int c, float (
         const float4 b = *reinterpret_cast<const float4*>(p + c + 4);
         f[0] = a.x; f[1] = a.y; f[2] = a.z; f[3] = a.w;
         f[4] = b.x; f[5] = b.y; f[6] = b.z; f[7] = b.w;
+        if (g.mask != nullptr) {
+          const float* m = g.mask + static_cast<int64_t>(row) * g.mask_ld + g.col0 + c;
+          const float4 ma = *reinterpret_cast<const float4*>(m);
+          const float4 mb = *reinterpret_cast<const float4*>(m + 4);
+          const float mv[8] = {ma.x, ma.y, ma.z, ma.w, mb.x, mb.y, mb.z, mb.w};
+#pragma unroll
+          for (int i = 0; i < 8; ++i) f[i] = mv[i] > 0.f ? f[i] : 0.f;
+        }
       } else {
 #pragma unroll
         for (int i = 0; i < 8; ++i) f[i] = (c + i < g.width) ? p[c + i] : 0.f;
+        if (g.mask != nullptr) {
+          const float* m = g.mask + static_cast<int64_t>(row) * g.mask_ld + g.col0 + c;
+#pragma unroll
+          for (int i = 0; i < 8; ++i)
+            if (c + i < g.width && !(m[i] > 0.f)) f[i] = 0.f;
+        }
       }
       break;
     }
@@ -178,7 +196,9 @@ __device__ __forceinline__ float seg_load1(const ASeg& g, int row, int c) {
     case kSegF32:
     case kSegSharded: {
       const float* p = seg_row_f32(g, row);
-      return p ? p[c] : 0.f;
+      if (p == nullptr) return 0.f;
+      if (g.mask != nullptr && !(g.mask[static_cast<int64_t>(row) * g.mask_ld + g.col0 + c] > 0.f)) return 0.f;
+      return p[c];
     }
     case kSegBF16: {
       int64_t r = g.index ? g.index[row] : row;

@@ -23,8 +23,9 @@ static void su_ws_free(void* p) { c10::cuda::CUDACachingAllocator::raw_delete(p)
 at::Tensor linear_fwd(const at::Tensor& x, const at::Tensor& w, const c10::optional<at::Tensor>& bias, int64_t act);
 void linear_fwd_into(const at::Tensor& x, const at::Tensor& w, const c10::optional<at::Tensor>& bias, int64_t act,
                      at::Tensor& out);
-at::Tensor linear_dgrad(const at::Tensor& dy, const at::Tensor& w);
-void linear_wgrad(const at::Tensor& dy, const at::Tensor& x, at::Tensor& dw, const c10::optional<at::Tensor>& db);
+at::Tensor linear_dgrad(const at::Tensor& dy, const at::Tensor& w, const c10::optional<at::Tensor>& mask);
+void linear_wgrad(const at::Tensor& dy, const at::Tensor& x, at::Tensor& dw, const c10::optional<at::Tensor>& db,
+                  const c10::optional<at::Tensor>& mask);
 
 void tgn_prep(const at::Tensor& src, const at::Tensor& dst, const at::Tensor& ts, const at::Tensor& n_ev,
               const at::Tensor& neg_pool, at::Tensor& stamp, at::Tensor& node2root, at::Tensor& step_ctr, int64_t seed,
@@ -186,8 +187,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   su::set_workspace_allocator(&su_ws_alloc, &su_ws_free);
   m.def("linear_fwd", &linear_fwd);
   m.def("linear_fwd_into", &linear_fwd_into);
-  m.def("linear_dgrad", &linear_dgrad);
-  m.def("linear_wgrad", &linear_wgrad);
+  m.def("linear_dgrad", &linear_dgrad, py::arg("dy"), py::arg("w"), py::arg("mask") = py::none());
+  m.def("linear_wgrad", &linear_wgrad, py::arg("dy"), py::arg("x"), py::arg("dw"), py::arg("db"),
+        py::arg("mask") = py::none());
   m.def("tgn_prep", &tgn_prep);
   m.def("tgn_sample", &tgn_sample);
   m.def("tgn_memory_update", &tgn_memory_update);

@@ -3,6 +3,8 @@
 //   linear_fwd     : Y = act(X W^T + b)
 //   linear_dgrad   : dX = dY W              (B operand = W^T evaluated on the fly)
 //   linear_wgrad   : dW += dY^T X, db += sum_rows dY   (split-K, atomic epilogue;
+//   (both take dY with any row stride, and an optional mask: dY is read as
+//   dY * (mask > 0), the ReLU derivative from the forward output)
 //                    the bias gradient comes from a constant-1 column appended
 //                    to X inside the producer)
 #include "host_common.h"
@@ -55,6 +57,23 @@ static void linear_fwd_impl(const at::Tensor& x, const at::Tensor& w, const c10:
   SU_LAUNCH_CHECK();
 }
 
+// dY as an operand segment: unit column stride, any row stride, optionally masked
+// by the forward output (ReLU derivative, mask[r, c] > 0) while it is packed
+static ASeg grad_seg(const at::Tensor& dy, int N, const c10::optional<at::Tensor>& mask) {
+  TORCH_CHECK(dy.dim() == 2 && dy.stride(1) == 1, "dy must be a row-major matrix (any row stride)");
+  ASeg s = seg_f32(dy, N, pad8(N));
+  if (mask.has_value() && mask->defined()) {
+    SU_CHECK_F32(*mask);
+    TORCH_CHECK(mask->dim() == 2 && mask->size(0) == dy.size(0) && mask->size(1) == dy.size(1) &&
+                    mask->stride(1) == 1,
+                "mask must be a row-major matrix of dy's shape");
+    s.mask = mask->data_ptr<float>();
+    s.mask_ld = static_cast<int>(mask->stride(0));
+    if ((s.mask_ld % 4) != 0 || (reinterpret_cast<uintptr_t>(s.mask) % 16) != 0) s.vec = 0;
+  }
+  return s;
+}
+
 at::Tensor linear_fwd(const at::Tensor& x, const at::Tensor& w, const c10::optional<at::Tensor>& bias, int64_t act) {
   SU_CHECK_CUDA(x); SU_CHECK_F32(x); SU_CHECK_F32(w); SU_CHECK_CONTIG(w);
   TORCH_CHECK(x.dim() == 2 && x.stride(1) == 1, "x must be a row-major matrix");
@@ -77,14 +96,14 @@ void linear_fwd_into(const at::Tensor& x, const at::Tensor& w, const c10::option
   linear_fwd_impl(x, w, bias, act, out);
 }
 
-at::Tensor linear_dgrad(const at::Tensor& dy, const at::Tensor& w) {
-  SU_CHECK_CUDA(dy); SU_CHECK_F32(dy); SU_CHECK_CONTIG(dy); SU_CHECK_F32(w); SU_CHECK_CONTIG(w);
+at::Tensor linear_dgrad(const at::Tensor& dy, const at::Tensor& w, const c10::optional<at::Tensor>& mask) {
+  SU_CHECK_CUDA(dy); SU_CHECK_F32(dy); SU_CHECK_F32(w); SU_CHECK_CONTIG(w);
   const int M = static_cast<int>(dy.size(0)), N = static_cast<int>(w.size(0)), K = static_cast<int>(w.size(1));
   auto dx = at::empty({M, K}, dy.options());
   if (M == 0) return dx;
   SegSource a;
   a.nseg = 1;
-  a.seg[0] = seg_f32(dy, N, pad8(N));
+  a.seg[0] = grad_seg(dy, N, mask);
   WeightLayout L = single_weight_layout(w);
   L.blk_pad[0] = pad8(N);
   WeightMN b = weight_mn(L, pad8(N));
@@ -101,13 +120,14 @@ at::Tensor linear_dgrad(const at::Tensor& dy, const at::Tensor& w) {
   return dx;
 }
 
-void linear_wgrad(const at::Tensor& dy, const at::Tensor& x, at::Tensor& dw, const c10::optional<at::Tensor>& db) {
-  SU_CHECK_CUDA(dy); SU_CHECK_F32(dy); SU_CHECK_CONTIG(dy); SU_CHECK_F32(x); SU_CHECK_F32(dw); SU_CHECK_CONTIG(dw);
+void linear_wgrad(const at::Tensor& dy, const at::Tensor& x, at::Tensor& dw, const c10::optional<at::Tensor>& db,
+                  const c10::optional<at::Tensor>& mask) {
+  SU_CHECK_CUDA(dy); SU_CHECK_F32(dy); SU_CHECK_F32(x); SU_CHECK_F32(dw); SU_CHECK_CONTIG(dw);
   const int M = static_cast<int>(dy.size(0)), N = static_cast<int>(dy.size(1)), K = static_cast<int>(x.size(1));
   if (M == 0) return;
   SegSource dys;  // A[n, m] = dY[m, n] (MN-major view)
   dys.nseg = 1;
-  dys.seg[0] = seg_f32(dy, N, pad8(N));
+  dys.seg[0] = grad_seg(dy, N, mask);
   SegSource xs;  // B[k, m] = X[m, k] (+ ones column for the bias gradient)
   xs.nseg = 2;
   xs.seg[0] = seg_f32(x, K, pad8(K));

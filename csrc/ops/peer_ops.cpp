@@ -189,8 +189,9 @@ void peer_rs_adam_ag(const at::Tensor& grad_ptrs, const at::Tensor& param_ptrs, 
   TORCH_CHECK(world >= 1 && grad_ptrs.numel() == world && param_ptrs.numel() == world, "pointer tables of W ranks");
   const int64_t n = p_local.numel();
   const int64_t shard4 = (n / 4 + world - 1) / world;
-  const int blocks = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(num_sms(p_local.get_device()) * 2,
-                                                                               (shard4 + 255) / 256)));
+  // 256 threads x 4 float4 per block pass; up to four blocks per SM keep the NVLink loads in flight
+  const int blocks = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(num_sms(p_local.get_device()) * 4,
+                                                                               (shard4 + 1023) / 1024)));
   launch_peer_rs_adam_ag(cur_stream(), blocks, table<const float* const*>(grad_ptrs), table<float* const*>(param_ptrs),
                          static_cast<int>(world), static_cast<int>(rank), m.data_ptr<float>(), v.data_ptr<float>(), n,
                          step.data_ptr<int64_t>(), reinterpret_cast<unsigned int*>(done.data_ptr<int>()),

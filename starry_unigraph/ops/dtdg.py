@@ -82,21 +82,23 @@ class _Linear(torch.autograd.Function):
     def backward(ctx, gy):
         x, w, y = ctx.saved_tensors
         C = cuda_ext()
-        gy = gy.contiguous()
+        if gy.stride(-1) != 1:  # the GEMM producers read any row stride
+            gy = gy.contiguous()
+        mask = None
         if ctx.act == 1:
-            gy = gy * (y > 0)
+            mask = y  # ReLU derivative applied while the GEMMs pack dY
         elif ctx.act == 2:
             gy = gy * y * (1 - y)
         elif ctx.act == 3:
             gy = gy * (1 - y * y)
-        gx = C.linear_dgrad(gy, w.contiguous()) if ctx.needs_input_grad[0] else None
+        gx = C.linear_dgrad(gy, w.contiguous(), mask) if ctx.needs_input_grad[0] else None
         sw = _grad_sink(ctx.w_ref)
         gw = sw if sw is not None else torch.zeros_like(w)
         gb, sb = None, None
         if ctx.has_b:
             sb = _grad_sink(ctx.b_ref)
             gb = sb if sb is not None else torch.zeros(w.size(0), device=w.device)
-        C.linear_wgrad(gy, x.contiguous(), gw, gb)
+        C.linear_wgrad(gy, x.contiguous(), gw, gb, mask)
         return gx, (None if sw is not None else gw), (None if sb is not None else gb), None
 
 
@@ -114,6 +116,9 @@ class _LSTMCell(torch.autograd.Function):
         ctx.save_for_backward(x, h, c, cn, gates, wi, wf, wg, wo)
         ctx.params = (wi, bi, wf, bf, wg, bg, wo, bo)
         ctx.has_h, ctx.has_c = h is not None, c is not None
+        # an output nobody used (the last cell state of a window) arrives as None, not
+        # as a zero-filled tensor: the backward kernel reads a missing dh / dc as zero
+        ctx.set_materialize_grads(False)
         return hn, cn
 
     @staticmethod

@@ -65,7 +65,7 @@ class _HaloLinearAggregate(autograd.Function):
         if ctx.needs_input_grad[1]:
             sink = _grad_sink(ctx.w_ref)
             target = sink if sink is not None else torch.zeros_like(w)
-            C.linear_wgrad(gz, x.contiguous(), target, None)
+            C.linear_wgrad(gz, x.contiguous(), target, None, None)
             gw = None if sink is not None else target
         return gx, gw, None, None
 

@@ -213,3 +213,25 @@ def test_linear_fwd_into_row_strided_view(tma_rows, M, K, N, ld):
         assert C.status_read(True) == 0
         assert _rel(buf[:M, :N], x @ w.t()) < 1.5e-2
         assert torch.all(buf[:M, N:] == 3.0) and torch.all(buf[M:] == 3.0)
+
+
+@pytest.mark.parametrize("M,K,N", [(3000, 64, 64), (777, 40, 100)])
+def test_linear_grads_with_relu_mask_and_row_stride(M, K, N):
+    """dY read through a row-strided view and masked by the forward output while
+    it is packed: the data and weight gradients equal those of dY * (y > 0)."""
+    C = _C()
+    torch.manual_seed(3)
+    x = torch.randn(M, K, device="cuda")
+    w = torch.randn(N, K, device="cuda") / K ** 0.5
+    y = torch.relu(x @ w.t())
+    wide = torch.randn(M, N + 12, device="cuda")
+    dy = wide[:, 4:4 + N]  # row stride N + 12
+    ref = dy * (y > 0)
+    dx = C.linear_dgrad(dy, w, y)
+    dw, db = torch.zeros(N, K, device="cuda"), torch.zeros(N, device="cuda")
+    C.linear_wgrad(dy, x, dw, db, y)
+    torch.cuda.synchronize()
+    assert C.status_read(True) == 0
+    assert _rel(dx, ref @ w) < 1.5e-2
+    assert _rel(dw, ref.t() @ x) < 1.5e-2
+    assert _rel(db, ref.sum(0)) < 1.5e-2
