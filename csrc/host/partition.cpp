@@ -1,7 +1,12 @@
 // Graph partitioner used when pymetis is not installed: a streaming Linear
 // Deterministic Greedy pass (Stanton & Kliot, KDD'12) over the symmetrised graph
 // in BFS order, followed by balanced label-propagation refinement sweeps.
-// Objective: few cut edges under a capacity of (1 + eps) * N / k nodes per part.
+// Objective: few cut edges under a capacity of (1 + eps) / k of the total vertex
+// weight per part, a vertex weighing 1 + edge_weight * degree. With edge_weight
+// 0 that is node balance. On power-law graphs node balance alone puts the dense
+// core into one part, whose aggregation work (edges) then sets every step, while
+// the dense per-row work (GEMMs, recurrent cells) wants rows balanced: the
+// weight prices one edge endpoint at `edge_weight` rows.
 #include <omp.h>
 
 #include <algorithm>
@@ -14,7 +19,7 @@
 namespace sun {
 
 torch::Tensor partition_graph(torch::Tensor src, torch::Tensor dst, int64_t num_nodes, int64_t num_parts,
-                              double imbalance, int64_t refine_iters, int64_t seed) {
+                              double imbalance, int64_t refine_iters, int64_t seed, double edge_weight) {
   TORCH_CHECK(num_parts >= 1, "num_parts must be >= 1");
   auto out = torch::zeros({num_nodes}, torch::kInt64);
   if (num_parts == 1 || num_nodes == 0) return out;
@@ -64,8 +69,13 @@ torch::Tensor partition_graph(torch::Tensor src, torch::Tensor dst, int64_t num_
     }
   }
   const int64_t k = num_parts;
-  const double cap = std::max(1.0, (1.0 + std::max(0.0, imbalance - 1.0)) * static_cast<double>(num_nodes) / k);
-  std::vector<int64_t> part(num_nodes, -1), load(k, 0);
+  const double lam = std::max(0.0, edge_weight);
+  auto wt = [&](int64_t v) { return 1.0 + lam * static_cast<double>(ptr[v + 1] - ptr[v]); };
+  double total = 0.0;
+  for (int64_t v = 0; v < num_nodes; ++v) total += wt(v);
+  const double cap = std::max(1.0, (1.0 + std::max(0.0, imbalance - 1.0)) * total / k);
+  std::vector<int64_t> part(num_nodes, -1);
+  std::vector<double> load(k, 0.0);
   std::vector<int64_t> cnt(k, 0);
   for (int64_t v : order) {
     std::fill(cnt.begin(), cnt.end(), 0);
@@ -73,10 +83,11 @@ torch::Tensor partition_graph(torch::Tensor src, torch::Tensor dst, int64_t num_
       const int64_t p = part[adj[e]];
       if (p >= 0) cnt[p]++;
     }
+    const double w = wt(v);
     int64_t best = -1;
     double best_score = -1.0;
     for (int64_t p = 0; p < k; ++p) {
-      if (load[p] >= cap) continue;
+      if (load[p] + w > cap && load[p] > 0.0) continue;
       const double sc = (cnt[p] + 1e-9) * (1.0 - load[p] / cap);
       if (sc > best_score || (sc == best_score && best >= 0 && load[p] < load[best])) {
         best_score = sc;
@@ -85,7 +96,7 @@ torch::Tensor partition_graph(torch::Tensor src, torch::Tensor dst, int64_t num_
     }
     if (best < 0) best = std::min_element(load.begin(), load.end()) - load.begin();
     part[v] = best;
-    load[best]++;
+    load[best] += w;
   }
   // balanced label-propagation refinement
   for (int64_t it = 0; it < refine_iters; ++it) {
@@ -94,13 +105,14 @@ torch::Tensor partition_graph(torch::Tensor src, torch::Tensor dst, int64_t num_
       std::fill(cnt.begin(), cnt.end(), 0);
       for (int64_t e = ptr[v]; e < ptr[v + 1]; ++e) cnt[part[adj[e]]]++;
       const int64_t cur = part[v];
+      const double w = wt(v);
       int64_t best = cur;
       for (int64_t p = 0; p < k; ++p)
-        if (p != cur && cnt[p] > cnt[best] && load[p] + 1 <= cap) best = p;
+        if (p != cur && cnt[p] > cnt[best] && load[p] + w <= cap) best = p;
       if (best != cur) {
         part[v] = best;
-        load[cur]--;
-        load[best]++;
+        load[cur] -= w;
+        load[best] += w;
         ++moved;
       }
     }
