@@ -25,7 +25,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("get_norm_temporal", &get_norm_temporal);
   m.def("partition_graph", &partition_graph, py::arg("src"), py::arg("dst"), py::arg("num_nodes"),
         py::arg("num_parts"), py::arg("imbalance") = 1.03, py::arg("refine_iters") = 3, py::arg("seed") = 0,
-        py::arg("edge_weight") = 0.0);
+        py::arg("edge_share") = 0.0);
 
   py::class_<TemporalGraphBlock>(m, "TemporalGraphBlock")
       .def(py::init<>())

@@ -141,7 +141,7 @@ SplitResult adaptive_split(torch::Tensor src, torch::Tensor dst, torch::Tensor t
                            double drop_rate, int64_t window_size);
 
 torch::Tensor partition_graph(torch::Tensor src, torch::Tensor dst, int64_t num_nodes, int64_t num_parts,
-                              double imbalance, int64_t refine_iters, int64_t seed, double edge_weight);
+                              double imbalance, int64_t refine_iters, int64_t seed, double edge_share);
 
 torch::Tensor heads_unique(torch::Tensor array, torch::Tensor heads, int threads);
 std::vector<torch::Tensor> divide_nodes_to_part(torch::Tensor nodes, const std::vector<NodeId>& part_ptr,

@@ -2,11 +2,13 @@
 // Deterministic Greedy pass (Stanton & Kliot, KDD'12) over the symmetrised graph
 // in BFS order, followed by balanced label-propagation refinement sweeps.
 // Objective: few cut edges under a capacity of (1 + eps) / k of the total vertex
-// weight per part, a vertex weighing 1 + edge_weight * degree. With edge_weight
-// 0 that is node balance. On power-law graphs node balance alone puts the dense
-// core into one part, whose aggregation work (edges) then sets every step, while
-// the dense per-row work (GEMMs, recurrent cells) wants rows balanced: the
-// weight prices one edge endpoint at `edge_weight` rows.
+// weight per part. A vertex weighs (1 - s) / N + s * degree / D (N vertices, D
+// edge endpoints): `edge_share` s is the fraction of the per-step work that
+// scales with edges rather than rows, independent of how many snapshots the
+// lifetime graph merges; s = 0 is node balance. On power-law graphs node balance
+// alone puts the dense core into one part, whose aggregation work then sets
+// every step, while the dense per-row work (GEMMs, recurrent cells) wants rows
+// balanced.
 #include <omp.h>
 
 #include <algorithm>
@@ -19,7 +21,7 @@
 namespace sun {
 
 torch::Tensor partition_graph(torch::Tensor src, torch::Tensor dst, int64_t num_nodes, int64_t num_parts,
-                              double imbalance, int64_t refine_iters, int64_t seed, double edge_weight) {
+                              double imbalance, int64_t refine_iters, int64_t seed, double edge_share) {
   TORCH_CHECK(num_parts >= 1, "num_parts must be >= 1");
   auto out = torch::zeros({num_nodes}, torch::kInt64);
   if (num_parts == 1 || num_nodes == 0) return out;
@@ -69,11 +71,11 @@ torch::Tensor partition_graph(torch::Tensor src, torch::Tensor dst, int64_t num_
     }
   }
   const int64_t k = num_parts;
-  const double lam = std::max(0.0, edge_weight);
-  auto wt = [&](int64_t v) { return 1.0 + lam * static_cast<double>(ptr[v + 1] - ptr[v]); };
-  double total = 0.0;
-  for (int64_t v = 0; v < num_nodes; ++v) total += wt(v);
-  const double cap = std::max(1.0, (1.0 + std::max(0.0, imbalance - 1.0)) * total / k);
+  const double share = std::min(1.0, std::max(0.0, edge_share));
+  const double endpoints = static_cast<double>(std::max<int64_t>(1, ptr[num_nodes]));
+  const double w_node = (1.0 - share) / static_cast<double>(num_nodes), w_end = share / endpoints;
+  auto wt = [&](int64_t v) { return w_node + w_end * static_cast<double>(ptr[v + 1] - ptr[v]); };
+  const double cap = (1.0 + std::max(0.0, imbalance - 1.0)) / static_cast<double>(k);  // total weight is 1
   std::vector<int64_t> part(num_nodes, -1);
   std::vector<double> load(k, 0.0);
   std::vector<int64_t> cnt(k, 0);

@@ -2,8 +2,8 @@
 (reference backends/dtdg/dtdg_prepare.py:45-537).
 
 * ``apply_partition``: METIS through pymetis when installed; otherwise the
-  native streaming partitioner of ``starry_unigraph._native`` (balancing the
-  vertex weight 1 + ``preprocess.partition_edge_weight`` x degree; linear
+  native streaming partitioner of ``starry_unigraph._native`` (balancing a
+  vertex weight with ``preprocess.partition_edge_share`` of it on edges; linear
   deterministic greedy with a balance cap over the symmetrised lifetime graph,
   followed by label-propagation refinement); random assignment only when
   neither is available (the reference's fallback).
@@ -45,9 +45,10 @@ def _merge_snapshot_edges(snapshots: list[dict[str, Any]]) -> torch.Tensor:
 
 
 def apply_partition(edge_index: torch.Tensor, num_nodes: int, num_parts: int, seed: int = 0,
-                    edge_weight: float = 0.0) -> torch.Tensor:
-    """Part of every node. Native partitioner: parts balance the vertex weight
-    1 + edge_weight * degree (0: node counts)."""
+                    edge_share: float = 0.0) -> torch.Tensor:
+    """Part of every node. Native partitioner: parts balance a vertex weight in
+    which `edge_share` of the total goes to edge endpoints and the rest to nodes
+    (0: node counts)."""
     num_nodes, num_parts = max(0, int(num_nodes)), max(1, int(num_parts))
     if num_nodes == 0:
         return torch.zeros(0, dtype=torch.long)
@@ -72,7 +73,7 @@ def apply_partition(edge_index: torch.Tensor, num_nodes: int, num_parts: int, se
     nat = native_ext()
     if nat is not None:
         return nat.partition_graph(src.contiguous(), dst.contiguous(), num_nodes, num_parts, 1.03, 3, seed,
-                                   float(edge_weight)).long()
+                                   float(edge_share)).long()
     print("[Partition] pymetis and the native partitioner unavailable; random partition")
     g = torch.Generator().manual_seed(seed)
     return torch.randint(0, num_parts, (num_nodes,), generator=g)
@@ -87,8 +88,8 @@ def build_dtdg_partitions(graph_data: Any, num_parts: int, algo: str, config: di
     elif algo_l in ("round_robin", "hash"):
         node_parts = torch.arange(num_nodes) % max(1, num_parts)
     else:
-        ew = float(config.get("preprocess", {}).get("partition_edge_weight", 0.0))
-        node_parts = apply_partition(merged, num_nodes, max(1, num_parts), edge_weight=ew)
+        share = float(config.get("preprocess", {}).get("partition_edge_share", 0.0))
+        node_parts = apply_partition(merged, num_nodes, max(1, num_parts), edge_share=share)
     parts = [{"partition_id": p, "node_ids": torch.nonzero(node_parts == p).view(-1),
               "num_nodes": int((node_parts == p).sum())} for p in range(max(1, num_parts))]
     return {"algo": algo, "num_parts": max(1, num_parts), "node_parts": node_parts, "parts": parts,

@@ -102,9 +102,10 @@ def test_partitioner_balanced_and_better_than_random():
 
 
 def test_partitioner_weighted_balance_on_power_law_graph():
-    """Vertex weight 1 + edge_weight * degree: on a power-law graph node balance
-    alone leaves one part with most edge endpoints; the weighted balance keeps
-    every part's weight within the imbalance bound (a single vertex may exceed it)."""
+    """Vertex weight (1 - s) / N + s * degree / D: on a power-law graph node
+    balance alone leaves one part with most edge endpoints; the weighted balance
+    keeps every part's weight within the imbalance bound (a single vertex may
+    exceed it)."""
     g = torch.Generator().manual_seed(1)
     n, m, k = 20000, 200000, 4
     w = torch.arange(1, n + 1, dtype=torch.float64) ** (-1 / 1.1)
@@ -113,15 +114,16 @@ def test_partitioner_weighted_balance_on_power_law_graph():
     keep = src != dst
     src, dst = src[keep], dst[keep]
     deg = (torch.bincount(src, minlength=n) + torch.bincount(dst, minlength=n)).double()
-    lam = 0.05
-    for ew, bound in ((0.0, None), (lam, 1.03)):
-        p = N.partition_graph(src, dst, n, k, 1.03, 3, 0, ew)
-        weight = torch.zeros(k, dtype=torch.float64).index_add_(0, p, 1.0 + lam * deg)
+    share = 0.3
+    vw = (1 - share) / n + share * deg / deg.sum()
+    for s, bound in ((0.0, None), (share, 1.03)):
+        p = N.partition_graph(src, dst, n, k, 1.03, 3, 0, s)
+        weight = torch.zeros(k, dtype=torch.float64).index_add_(0, p, vw)
         ratio = float(weight.max() / weight.mean())
         if bound is None:
             node_only = ratio
         else:
-            assert ratio <= bound + float((1.0 + lam * deg).max() / weight.mean()), ratio
+            assert ratio <= bound + float(vw.max() / weight.mean()), ratio
             assert ratio < node_only
 
 
