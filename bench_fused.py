@@ -206,7 +206,7 @@ def bench_halo_gather(n: int, m: int, F: int, iters: int, warmup: int, C) -> dic
         dist.all_to_all_single(recv, sendbuf, output_split_sizes=sizes_r, input_split_sizes=sizes_s)
         ext[:n_local].copy_(x_local)
         ext[n_local:].copy_(recv)
-        return C.spmm_csr(csr["rowptr"], csr["col"], csr["val"], ext, n_local, None, False)
+        return C.spmm_csr(csr["rowptr"], csr["col"], csr["val"], ext, n_local, None, False, csr.get("plan"))
 
     a, b, c = fused(), nccl(), per_edge()
     torch.cuda.synchronize()

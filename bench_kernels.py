@@ -1,6 +1,6 @@
 """Single-GPU timings of the DTDG hot kernels in isolation.
 
-    python bench_kernels.py spmm     # CSR aggregation, 200k rows x 2M edges, F = 64
+    python bench_kernels.py spmm     # CSR aggregation, 200k rows x 2M edges, F = 64 (edge-stream and item kernels)
     python bench_kernels.py lstm     # fused LSTM cell forward and backward, 200k rows, hidden 64
     python bench_kernels.py linear   # GCN linear forward / input gradient, 200k rows, 64 -> 64 and 128 -> 256
 
@@ -51,6 +51,10 @@ def spmm() -> dict:
     rp, cl, vl = rowptr.to(dev), col.to(dev), val.to(dev)
     out = torch.empty(n, F, device=dev)
     t = _time(lambda: C.spmm_csr(rp, cl, vl, x, n, out, False))
+    from starry_unigraph.data.partition import spmm_plan
+
+    plan = spmm_plan(rp)
+    t_items = _time(lambda: C.spmm_csr(rp, cl, vl, x, n, out, False, plan))
     A = torch.sparse_csr_tensor(rp, cl.long(), vl, size=(n, n))
     t_cusparse = _time(lambda: A @ x)
     rp2 = torch.arange(0, n + 1, device=dev, dtype=torch.long) * (m // n)
@@ -60,6 +64,7 @@ def spmm() -> dict:
     cl3 = torch.arange(m, device=dev, dtype=torch.int32) % n
     t_seq = _time(lambda: C.spmm_csr(rp2, cl3, vl2, x, n, out, False))
     return {"case": "spmm", "rows": n, "nnz": nnz, "F": F, "max_row": int(deg.max()), "spmm_us": round(t, 1),
+            "items_us": round(t_items, 1),
             "cusparse_us": round(t_cusparse, 1), "uniform_rows_us": round(t_uniform, 1),
             "sequential_cols_us": round(t_seq, 1)}
 

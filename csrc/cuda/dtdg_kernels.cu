@@ -310,6 +310,90 @@ __global__ void __launch_bounds__(256, 3) spmm_chunked_kernel(const int64_t* __r
   }
 }
 
+// Item-based SpMM for F = 64 (the MPNN-LSTM width). The host plan cuts every
+// row into items of at most kSpmmItemEdges edges (rows with no edges get one
+// empty item, which stores the zero row) and gives each warp of a fixed grid a
+// contiguous run of items of about equal edge count. A warp works on one item
+// at a time, two edges per step: lanes 0-15 take the even edges, lanes 16-31 the
+// odd ones, each lane one float4 of the 64 features, four edges in flight per
+// half; the halves are summed by one shuffle and lanes 0-15 store the row.
+// Items of rows split over several items add atomically into rows that a small
+// kernel zeroed first. Against the edge-stream kernel above this halves the
+// instructions per edge (a float4 per lane and no per-edge row-end test).
+constexpr int kSpmmItemWarpsPerSm = 64;  // 8 blocks of 256 threads per SM
+
+template <class Out>
+struct zero_empty : std::true_type {};
+template <>
+struct zero_empty<PeerPush> : std::false_type {};  // nothing to push for a row without edges
+
+template <class Rows, class Out>
+__global__ void __launch_bounds__(256) spmm_items64_kernel(const int* __restrict__ items, int n_items,
+                                                           const int* __restrict__ warp_off, int warps,
+                                                           const int* __restrict__ col,
+                                                           const float* __restrict__ val, const Rows rows,
+                                                           const Out out) {
+  const int lane = threadIdx.x & 31, half = lane >> 4, l16 = lane & 15;
+  const int gw = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  if (gw >= warps) return;  // warp-uniform
+  const int i0 = warp_off[gw], i1 = warp_off[gw + 1];
+  for (int it = i0; it < i1; ++it) {
+    const int renc = items[it], e0 = items[n_items + it], e1 = items[2 * n_items + it];
+    const bool whole = renc >= 0;
+    const int r = whole ? renc : -renc - 1;
+    if (e0 == e1 && !zero_empty<Out>::value) continue;
+    float a[4] = {0.f, 0.f, 0.f, 0.f};
+    int e = e0 + half;
+    for (; e + 6 < e1; e += 8) {  // edges e, e + 2, e + 4, e + 6 of this half
+      int c[4];
+      float v[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        c[u] = col[e + 2 * u];
+        v[u] = val[e + 2 * u];
+      }
+      float t[4][4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) load_vec<4>(rows.row(c[u]) + 4 * l16, t[u]);
+#pragma unroll
+      for (int u = 0; u < 4; ++u)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) a[j] = fmaf(v[u], t[u][j], a[j]);
+    }
+    for (; e < e1; e += 2) {
+      float t[4];
+      load_vec<4>(rows.row(col[e]) + 4 * l16, t);
+      const float v = val[e];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) a[j] = fmaf(v, t[j], a[j]);
+    }
+#pragma unroll
+    for (int j = 0; j < 4; ++j) a[j] += __shfl_xor_sync(0xffffffffu, a[j], 16);
+    if (half == 0) out.template put_vec<4>(r, 4 * l16, a, whole);
+  }
+}
+
+__global__ void zero_rows64_kernel(const int* __restrict__ rows_list, int n, float* __restrict__ out, int ld) {
+  const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (i >= static_cast<int64_t>(n) * 16) return;
+  const int r = rows_list[i >> 4];
+  reinterpret_cast<float4*>(out + static_cast<int64_t>(r) * ld)[i & 15] = make_float4(0.f, 0.f, 0.f, 0.f);
+}
+
+template <class Rows, class Out>
+static void launch_items(cudaStream_t st, const SpmmPlan& plan, const int* col, const float* val, const Rows& rows,
+                         const Out& out) {
+  if (plan.n_items == 0) return;
+  count_launch();
+  spmm_items64_kernel<<<(plan.warps + 7) / 8, 256, 0, st>>>(plan.items, plan.n_items, plan.warp_off, plan.warps, col,
+                                                            val, rows, out);
+}
+
+// the plan applies: 64 features, a plain (non-accumulating) output
+static bool plan_ok(const SpmmPlan* plan, int F) { return plan != nullptr && plan->items != nullptr && F == 64; }
+
+int spmm_plan_warps(int device) { return num_sms(device) * kSpmmItemWarpsPerSm; }
+
 template <class Rows, class Out>
 static void launch_chunked(cudaStream_t st, const int64_t* rowptr, const int* col, const float* val, const Rows& rows,
                            int64_t n_rows, int F, const Out& out) {
@@ -324,8 +408,16 @@ static void launch_chunked(cudaStream_t st, const int64_t* rowptr, const int* co
 }
 
 void launch_spmm_csr(cudaStream_t st, const int64_t* rowptr, const int* col, const float* val, const float* x,
-                     int64_t n_rows, int F, float* out, int accumulate) {
+                     int64_t n_rows, int F, float* out, int accumulate, const SpmmPlan* plan) {
   if (n_rows == 0) return;
+  if (!accumulate && plan_ok(plan, F)) {
+    if (plan->n_split > 0) {
+      count_launch();
+      zero_rows64_kernel<<<(plan->n_split * 16 + 255) / 256, 256, 0, st>>>(plan->split_rows, plan->n_split, out, F);
+    }
+    launch_items(st, *plan, col, val, LocalRows{x, F}, LocalOut{out, F, 0});
+    return;
+  }
   // rows without edges and rows shared between chunks start from zero
   if (!accumulate) cudaMemsetAsync(out, 0, static_cast<size_t>(n_rows) * F * sizeof(float), st);
   launch_chunked(st, rowptr, col, val, LocalRows{x, F}, n_rows, F, LocalOut{out, F, accumulate});
@@ -374,8 +466,17 @@ void launch_halo_pull(cudaStream_t st, const float* const* peers, const int* own
 // Aggregation over [this rank's rows | pulled halo rows] (columns remapped once
 // per graph: local sources -> their row in x, halo sources -> n_split + pull slot).
 void launch_spmm_two_tables(cudaStream_t st, const int64_t* rowptr, const int* col, const float* val, const float* x,
-                            int x_ld, const float* halo, int n_split, int64_t n_rows, int F, float* out) {
+                            int x_ld, const float* halo, int n_split, int64_t n_rows, int F, float* out,
+                            const SpmmPlan* plan) {
   if (n_rows == 0) return;
+  if (plan_ok(plan, F)) {
+    if (plan->n_split > 0) {
+      count_launch();
+      zero_rows64_kernel<<<(plan->n_split * 16 + 255) / 256, 256, 0, st>>>(plan->split_rows, plan->n_split, out, F);
+    }
+    launch_items(st, *plan, col, val, TwoTables{x, halo, n_split, F, x_ld}, LocalOut{out, F, 0});
+    return;
+  }
   cudaMemsetAsync(out, 0, static_cast<size_t>(n_rows) * F * sizeof(float), st);
   launch_chunked(st, rowptr, col, val, TwoTables{x, halo, n_split, F, x_ld}, n_rows, F, LocalOut{out, F, 0});
 }
@@ -384,8 +485,12 @@ void launch_spmm_two_tables(cudaStream_t st, const int64_t* rowptr, const int* c
 // gradient is pushed into the owner's gradient buffer with remote atomic adds.
 void launch_spmm_peer_push(cudaStream_t st, const int64_t* rowptr_t, const int* col_t, const float* val_t,
                            const float* grad_dst, int64_t n_src, int F, int ld, float* const* peers,
-                           const int* src_owner, const int* src_row) {
+                           const int* src_owner, const int* src_row, const SpmmPlan* plan) {
   if (n_src == 0) return;
+  if (plan_ok(plan, F)) {  // pushes are atomic adds into the owners' zeroed buffers
+    launch_items(st, *plan, col_t, val_t, LocalRows{grad_dst, F}, PeerPush{peers, src_owner, src_row, ld});
+    return;
+  }
   launch_chunked(st, rowptr_t, col_t, val_t, LocalRows{grad_dst, F}, n_src, F,
                  PeerPush{peers, src_owner, src_row, ld});
 }

@@ -141,8 +141,20 @@ void launch_rgru_bwd1(cudaStream_t st, const float* dhn, int dhn_ld, const float
 void launch_rgru_bwd2(cudaStream_t st, const float* drh, int drh_ld, const float* h, int h_ld, const float* r,
                       int64_t rows, int H, float* dzr, float* dh_acc);
 void launch_add_rows(cudaStream_t st, const float* a, const float* b, int b_ld, int64_t rows, int H, float* out);
+// Work plan of the item-based SpMM (F = 64): rows cut into items of at most a
+// fixed edge count, runs of items per warp of a fixed grid. Built on the device
+// once per CSR (starry_unigraph.data.partition.spmm_plan).
+struct SpmmPlan {
+  const int* items = nullptr;       // [3][n_items]: row (-row - 1 when split over items), first edge, end edge
+  int n_items = 0;
+  const int* warp_off = nullptr;    // [warps + 1] item offsets
+  int warps = 0;
+  const int* split_rows = nullptr;  // rows split over several items (zeroed before their atomic adds)
+  int n_split = 0;
+};
+int spmm_plan_warps(int device);
 void launch_spmm_csr(cudaStream_t st, const int64_t* rowptr, const int* col, const float* val, const float* x,
-                     int64_t n_rows, int F, float* out, int accumulate);
+                     int64_t n_rows, int F, float* out, int accumulate, const SpmmPlan* plan = nullptr);
 void launch_spmm_peer_gather(cudaStream_t st, const int64_t* rowptr, const int* col, const float* val,
                              const float* const* peers, const int* src_owner, const int* src_row, int64_t n_rows,
                              int F, float* out);
@@ -151,10 +163,11 @@ void launch_spmm_peer_gather(cudaStream_t st, const int64_t* rowptr, const int* 
 void launch_halo_pull(cudaStream_t st, const float* const* peers, const int* owner, const int* lrow,
                       const int* halo_src, int64_t n_halo, int F, int ld, float* out);
 void launch_spmm_two_tables(cudaStream_t st, const int64_t* rowptr, const int* col, const float* val, const float* x,
-                            int x_ld, const float* halo, int n_split, int64_t n_rows, int F, float* out);
+                            int x_ld, const float* halo, int n_split, int64_t n_rows, int F, float* out,
+                            const SpmmPlan* plan = nullptr);
 void launch_spmm_peer_push(cudaStream_t st, const int64_t* rowptr_t, const int* col_t, const float* val_t,
                            const float* grad_dst, int64_t n_src, int F, int ld, float* const* peers,
-                           const int* src_owner, const int* src_row);
+                           const int* src_owner, const int* src_row, const SpmmPlan* plan = nullptr);
 void launch_lstm_bwd(cudaStream_t st, const float* gates, const float* c_prev, const float* c_new, const float* dh,
                      int dh_ld, const float* dc, int dc_ld, int64_t rows, int H, float* dpre, float* dc_prev);
 // gate gradients written as the K-major image of dpre (the input-gradient GEMM's A)

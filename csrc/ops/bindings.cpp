@@ -93,7 +93,9 @@ void adam_flat(at::Tensor& p, const at::Tensor& g, at::Tensor& m, at::Tensor& v,
                double lr, double b1, double b2, double eps, double wd, double grad_scale);
 
 at::Tensor spmm_csr(const at::Tensor& rowptr, const at::Tensor& col, const at::Tensor& val, const at::Tensor& x,
-                    int64_t n_rows, const c10::optional<at::Tensor>& out_opt, bool accumulate);
+                    int64_t n_rows, const c10::optional<at::Tensor>& out_opt, bool accumulate,
+                    const c10::optional<std::vector<at::Tensor>>& plan);
+int64_t spmm_plan_warps_op();
 std::vector<at::Tensor> lstm_fwd(const at::Tensor& x, const c10::optional<at::Tensor>& h,
                                  const c10::optional<at::Tensor>& c, const at::Tensor& wi, const at::Tensor& bi,
                                  const at::Tensor& wf, const at::Tensor& bf, const at::Tensor& wg,
@@ -147,7 +149,8 @@ at::Tensor spmm_peer_gather(const at::Tensor& rowptr, const at::Tensor& col, con
 at::Tensor halo_pull(const at::Tensor& peers, const at::Tensor& src_owner, const at::Tensor& src_row,
                      const at::Tensor& halo_src, int64_t F, int64_t ld);
 at::Tensor spmm_two_tables(const at::Tensor& rowptr, const at::Tensor& col, const at::Tensor& val,
-                           const at::Tensor& x, const at::Tensor& halo, int64_t n_rows);
+                           const at::Tensor& x, const at::Tensor& halo, int64_t n_rows,
+                           const c10::optional<std::vector<at::Tensor>>& plan);
 std::vector<at::Tensor> rgru_fwd(const at::Tensor& xz, const at::Tensor& xr, const at::Tensor& xc,
                                  const c10::optional<at::Tensor>& h, const at::Tensor& wz, const at::Tensor& bz,
                                  const at::Tensor& wr, const at::Tensor& br, const at::Tensor& wc,
@@ -160,7 +163,7 @@ std::vector<at::Tensor> rgru_bwd(const at::Tensor& xz, const at::Tensor& xr, con
                                  at::Tensor& gbc);
 void spmm_peer_push(const at::Tensor& rowptr_t, const at::Tensor& col_t, const at::Tensor& val_t,
                     const at::Tensor& grad_dst, int64_t n_src, const at::Tensor& peers, const at::Tensor& src_owner,
-                    const at::Tensor& src_row, int64_t ld);
+                    const at::Tensor& src_row, int64_t ld, const c10::optional<std::vector<at::Tensor>>& plan);
 
 void tgn_rnn_memory_update(const at::Tensor& roots, const at::Tensor& n_roots, const at::Tensor& mailbox,
                            at::Tensor& memory, at::Tensor& memory_ts, const at::Tensor& ts_max,
@@ -225,16 +228,19 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("mem_prev"), py::arg("efeat"), py::arg("E"), py::arg("claim_ptrs"), py::arg("mail_ptrs") = py::none(),
         py::arg("mail_ts_ptrs") = py::none());
   m.def("peer_rs_adam_ag", &peer_rs_adam_ag);
-  m.def("spmm_csr", &spmm_csr);
+  m.def("spmm_csr", &spmm_csr, py::arg("rowptr"), py::arg("col"), py::arg("val"), py::arg("x"), py::arg("n_rows"),
+        py::arg("out") = py::none(), py::arg("accumulate") = false, py::arg("plan") = py::none());
+  m.def("spmm_plan_warps", &spmm_plan_warps_op, "warps of the item-based SpMM grid on the current device");
   m.def("spmm_peer_gather", &spmm_peer_gather);
   m.def("spmm_peer_push", &spmm_peer_push, py::arg("rowptr_t"), py::arg("col_t"), py::arg("val_t"),
         py::arg("grad_dst"), py::arg("n_src"), py::arg("peers"), py::arg("src_owner"), py::arg("src_row"),
-        py::arg("ld") = -1);
+        py::arg("ld") = -1, py::arg("plan") = py::none());
   m.def("halo_pull", &halo_pull, py::arg("peers"), py::arg("src_owner"), py::arg("src_row"), py::arg("halo_src"),
         py::arg("F"), py::arg("ld") = -1);
   m.def("rgru_fwd", &rgru_fwd);
   m.def("rgru_bwd", &rgru_bwd);
-  m.def("spmm_two_tables", &spmm_two_tables);
+  m.def("spmm_two_tables", &spmm_two_tables, py::arg("rowptr"), py::arg("col"), py::arg("val"), py::arg("x"),
+        py::arg("halo"), py::arg("n_rows"), py::arg("plan") = py::none());
   m.def("lstm_fwd", &lstm_fwd);
   m.def("lstm_bwd", &lstm_bwd);
 }

@@ -5,17 +5,20 @@
 
 using namespace su;
 
+int64_t spmm_plan_warps_op() { return spmm_plan_warps(at::cuda::current_device()); }
+
 at::Tensor spmm_csr(const at::Tensor& rowptr, const at::Tensor& col, const at::Tensor& val, const at::Tensor& x,
-                    int64_t n_rows, const c10::optional<at::Tensor>& out_opt, bool accumulate) {
+                    int64_t n_rows, const c10::optional<at::Tensor>& out_opt, bool accumulate,
+                    const c10::optional<std::vector<at::Tensor>>& plan_t) {
   SU_CHECK_I64(rowptr); SU_CHECK_I32(col); SU_CHECK_F32(val); SU_CHECK_F32(x); SU_CHECK_CONTIG(x);
   const int F = static_cast<int>(x.size(1));
   at::Tensor out = (out_opt.has_value() && out_opt->defined()) ? *out_opt : at::empty({n_rows, F}, x.options());
   TORCH_CHECK(out.is_contiguous() && out.size(1) == F, "bad output buffer");
-  if (accumulate == false && n_rows > 0 && rowptr.numel() == n_rows + 1) {
-    // every row is written by the kernel
-  }
+  SpmmPlan plan;
+  const bool planned = spmm_plan_from(plan_t, &plan).items != nullptr;
   launch_spmm_csr(cur_stream(), rowptr.data_ptr<int64_t>(), col.data_ptr<int>(), val.data_ptr<float>(),
-                  x.data_ptr<float>(), n_rows, F, out.data_ptr<float>(), accumulate ? 1 : 0);
+                  x.data_ptr<float>(), n_rows, F, out.data_ptr<float>(), accumulate ? 1 : 0,
+                  planned ? &plan : nullptr);
   SU_LAUNCH_CHECK();
   return out;
 }
@@ -273,7 +276,8 @@ at::Tensor halo_pull(const at::Tensor& peers, const at::Tensor& src_owner, const
 }
 
 at::Tensor spmm_two_tables(const at::Tensor& rowptr, const at::Tensor& col, const at::Tensor& val,
-                           const at::Tensor& x, const at::Tensor& halo, int64_t n_rows) {
+                           const at::Tensor& x, const at::Tensor& halo, int64_t n_rows,
+                           const c10::optional<std::vector<at::Tensor>>& plan_t) {
   SU_CHECK_I64(rowptr); SU_CHECK_I32(col); SU_CHECK_F32(val); SU_CHECK_F32(x);
   TORCH_CHECK(x.dim() == 2 && x.stride(1) == 1, "x must be a row-major matrix (any row stride)");
   SU_CHECK_F32(halo); SU_CHECK_CONTIG(halo);
@@ -282,9 +286,11 @@ at::Tensor spmm_two_tables(const at::Tensor& rowptr, const at::Tensor& col, cons
   TORCH_CHECK(F % 4 != 0 || (x.stride(0) % 4 == 0 && (reinterpret_cast<uintptr_t>(x.data_ptr()) & 15) == 0),
               "row-strided x needs 16-byte aligned rows");
   at::Tensor out = at::empty({n_rows, F}, x.options());
+  SpmmPlan plan;
   launch_spmm_two_tables(cur_stream(), rowptr.data_ptr<int64_t>(), col.data_ptr<int>(), val.data_ptr<float>(),
                          x.data_ptr<float>(), static_cast<int>(x.stride(0)), halo.numel() ? halo.data_ptr<float>() : nullptr,
-                         static_cast<int>(x.size(0)), n_rows, F, out.data_ptr<float>());
+                         static_cast<int>(x.size(0)), n_rows, F, out.data_ptr<float>(),
+                         spmm_plan_from(plan_t, &plan).items != nullptr ? &plan : nullptr);
   SU_LAUNCH_CHECK();
   return out;
 }
@@ -292,16 +298,17 @@ at::Tensor spmm_two_tables(const at::Tensor& rowptr, const at::Tensor& col, cons
 // `ld`: row stride of the owners' gradient buffers (-1: the gradient width)
 void spmm_peer_push(const at::Tensor& rowptr_t, const at::Tensor& col_t, const at::Tensor& val_t,
                     const at::Tensor& grad_dst, int64_t n_src, const at::Tensor& peers, const at::Tensor& src_owner,
-                    const at::Tensor& src_row, int64_t ld) {
+                    const at::Tensor& src_row, int64_t ld, const c10::optional<std::vector<at::Tensor>>& plan_t) {
   SU_CHECK_F32(grad_dst); SU_CHECK_CONTIG(grad_dst);
   TORCH_CHECK(peers.is_cuda() && peers.scalar_type() == at::kLong, "peer table must be cuda int64");
   const int F = static_cast<int>(grad_dst.size(1));
   if (ld < 0) ld = F;
   TORCH_CHECK(ld >= F, "gradient buffer rows narrower than the gradient");
+  SpmmPlan plan;
   launch_spmm_peer_push(cur_stream(), rowptr_t.data_ptr<int64_t>(), col_t.data_ptr<int>(), val_t.data_ptr<float>(),
                         grad_dst.data_ptr<float>(), n_src, F, static_cast<int>(ld),
                         reinterpret_cast<float* const*>(peers.data_ptr<int64_t>()), src_owner.data_ptr<int>(),
-                        src_row.data_ptr<int>());
+                        src_row.data_ptr<int>(), spmm_plan_from(plan_t, &plan).items != nullptr ? &plan : nullptr);
   SU_LAUNCH_CHECK();
 }
 

@@ -129,6 +129,27 @@ struct PeerDesc {
   const float* const* ts_peers = nullptr;
 };
 
+// (items [3 * n_items] int32, warp offsets [warps + 1] int32, split rows int32): the
+// item-based SpMM plan of one CSR; nullopt or an empty list keeps the edge-stream kernel
+inline SpmmPlan spmm_plan_from(const c10::optional<std::vector<at::Tensor>>& p, SpmmPlan* out) {
+  SpmmPlan plan;
+  if (!p.has_value() || p->empty()) return plan;
+  TORCH_CHECK(p->size() == 3, "SpMM plan: (items, warp_off, split_rows)");
+  const at::Tensor& items = (*p)[0];
+  const at::Tensor& woff = (*p)[1];
+  const at::Tensor& split = (*p)[2];
+  SU_CHECK_I32(items); SU_CHECK_I32(woff); SU_CHECK_I32(split);
+  TORCH_CHECK(items.numel() % 3 == 0 && woff.numel() >= 2, "malformed SpMM plan");
+  plan.items = items.data_ptr<int>();
+  plan.n_items = static_cast<int>(items.numel() / 3);
+  plan.warp_off = woff.data_ptr<int>();
+  plan.warps = static_cast<int>(woff.numel() - 1);
+  plan.split_rows = split.numel() ? split.data_ptr<int>() : nullptr;
+  plan.n_split = static_cast<int>(split.numel());
+  *out = plan;
+  return plan;
+}
+
 inline PeerDesc peer_desc(const c10::optional<at::Tensor>& t) {
   PeerDesc d;
   if (!t.has_value() || !t->defined()) return d;

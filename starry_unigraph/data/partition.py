@@ -128,6 +128,39 @@ class RouteData:
         return cls(send, recv, td.data, td.ptr)
 
 
+def spmm_plan(rowptr: Tensor, max_edges: int = 128, warps: int | None = None) -> list[Tensor]:
+    """Work plan of the item-based aggregation kernel over a CSR (device tensors):
+    every row cut into items of at most `max_edges` edges (a row without edges is
+    one empty item, which writes its zero row), items handed to the warps of a
+    fixed grid in runs of about equal edge count (8 edges of overhead per item).
+    Returns [items (row or -row-1 for rows split over several items, first edge,
+    end edge; int32, 3 x n_items), warp offsets (int32, warps + 1), split rows
+    (int32)]."""
+    from starry_unigraph.ops import cuda_ext
+
+    dev = rowptr.device
+    if warps is None:
+        warps = int(cuda_ext().spmm_plan_warps())
+    n = rowptr.numel() - 1
+    deg = rowptr[1:] - rowptr[:-1]
+    k = torch.clamp((deg + max_edges - 1) // max_edges, min=1)
+    row = torch.repeat_interleave(torch.arange(n, device=dev), k)
+    n_items = int(row.numel())
+    first = torch.cumsum(k, 0) - k
+    j = torch.arange(n_items, device=dev) - first[row]
+    e0 = rowptr[row] + j * max_edges
+    e1 = torch.minimum(e0 + max_edges, rowptr[row + 1])
+    split = k > 1
+    renc = torch.where(split[row], -row - 1, row)
+    cw = torch.cumsum(e1 - e0 + 8, 0)
+    targets = torch.arange(1, warps, device=dev, dtype=torch.int64) * int(cw[-1]) // warps
+    bounds = torch.searchsorted(cw, targets, right=True)
+    woff = torch.cat([torch.zeros(1, dtype=torch.int64, device=dev), bounds,
+                      torch.full((1,), n_items, dtype=torch.int64, device=dev)])
+    items = torch.stack([renc, e0, e1]).int().contiguous().view(-1)
+    return [items, woff.int().contiguous(), torch.nonzero(split).view(-1).int().contiguous()]
+
+
 @dataclass
 class SnapshotBlock:
     """Bipartite block of one snapshot on one partition."""
@@ -168,7 +201,9 @@ class SnapshotBlock:
 
     def csr(self) -> dict[str, Tensor]:
         """Destination-sorted CSR (forward aggregation) and source-sorted CSR
-        (backward aggregation), both with int32 columns and fp32 values."""
+        (backward aggregation), both with int32 columns and fp32 values; on the
+        GPU also the item plans of the 64-feature aggregation kernel for both
+        ("plan", "plan_t", see ``spmm_plan``)."""
         if self._csr is None:
             dst = self.edge_dst.long()
             src = self.edge_src.long()
@@ -182,6 +217,9 @@ class SnapshotBlock:
             self._csr = {"rowptr": rowptr, "col": src[order].int().contiguous(), "val": val[order].contiguous(),
                          "rowptr_t": rowptr_t, "col_t": dst[order_t].int().contiguous(),
                          "val_t": val[order_t].contiguous()}
+            if rowptr.is_cuda and int(rowptr[-1]) < 2 ** 31:
+                self._csr["plan"] = spmm_plan(rowptr)
+                self._csr["plan_t"] = spmm_plan(rowptr_t)
         return self._csr
 
     def local_scope(self):

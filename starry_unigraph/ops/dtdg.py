@@ -19,24 +19,24 @@ from starry_unigraph.ops import cuda_ext
 
 class _SpMM(torch.autograd.Function):
     @staticmethod
-    def forward(ctx, x_src, rowptr, col, val, rowptr_t, col_t, val_t, n_dst):
+    def forward(ctx, x_src, csr, n_dst):
         C = cuda_ext()
-        ctx.save_for_backward(rowptr_t, col_t, val_t)
+        ctx.csr = csr  # CSR and item plans of the block (cached on it)
         ctx.n_src = x_src.size(0)
-        return C.spmm_csr(rowptr, col, val, x_src.contiguous(), int(n_dst), None, False)
+        return C.spmm_csr(csr["rowptr"], csr["col"], csr["val"], x_src.contiguous(), int(n_dst), None, False,
+                          csr.get("plan"))
 
     @staticmethod
     def backward(ctx, g):
-        rowptr_t, col_t, val_t = ctx.saved_tensors
-        gx = cuda_ext().spmm_csr(rowptr_t, col_t, val_t, g.contiguous(), int(ctx.n_src), None, False)
-        return gx, None, None, None, None, None, None, None
+        c = ctx.csr
+        gx = cuda_ext().spmm_csr(c["rowptr_t"], c["col_t"], c["val_t"], g.contiguous(), int(ctx.n_src), None, False,
+                                 c.get("plan_t"))
+        return gx, None, None
 
 
 def gcn_aggregate(block, x_src: torch.Tensor) -> torch.Tensor:
     if x_src.is_cuda:
-        c = block.csr()
-        return _SpMM.apply(x_src.float(), c["rowptr"], c["col"], c["val"], c["rowptr_t"], c["col_t"], c["val_t"],
-                           block.num_dst_nodes)
+        return _SpMM.apply(x_src.float(), block.csr(), block.num_dst_nodes)
     norm = block.edge_norm()
     out = torch.zeros(block.num_dst_nodes, x_src.size(1), dtype=x_src.dtype, device=x_src.device)
     return out.index_add(0, block.edge_dst.long(), x_src[block.edge_src.long()] * norm.unsqueeze(1))

@@ -151,7 +151,8 @@ class _HaloAggregate(autograd.Function):
         if F % 4 == 0:
             halo_src, col = hc.pull_plan(graph, n_local)
             halo = C.halo_pull(hc.tables[buf], owner, row, halo_src, F, hc.F)
-            out = C.spmm_two_tables(csr["rowptr"], col, csr["val"], x_local, halo, graph.num_dst_nodes)
+            out = C.spmm_two_tables(csr["rowptr"], col, csr["val"], x_local, halo, graph.num_dst_nodes,
+                                    csr.get("plan"))
         else:  # F == hc.F (supports): per-edge peer reads at the staging stride
             out = C.spmm_peer_gather(csr["rowptr"], csr["col"], csr["val"], hc.tables[buf], owner, row,
                                      graph.num_dst_nodes, F)
@@ -169,7 +170,7 @@ class _HaloAggregate(autograd.Function):
         csr = ctx.graph.csr()
         F = grad.size(1)
         C.spmm_peer_push(csr["rowptr_t"], csr["col_t"], csr["val_t"], grad.contiguous(), ctx.graph.num_src_nodes,
-                         hc.tables[buf], owner, row, hc.F)
+                         hc.tables[buf], owner, row, hc.F, csr.get("plan_t"))
         hc.barrier()
         g = hc.arena[buf]
         gx = g[: ctx.n_local, :F].clone()

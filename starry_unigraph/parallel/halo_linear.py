@@ -38,7 +38,7 @@ class _HaloLinearAggregate(autograd.Function):
         owner, row = hc.src_maps(graph)
         halo_src, col = hc.pull_plan(graph, n_local)
         halo = C.halo_pull(hc.tables[buf], owner, row, halo_src, F, hc.F)
-        out = C.spmm_two_tables(csr["rowptr"], col, csr["val"], z, halo, graph.num_dst_nodes)
+        out = C.spmm_two_tables(csr["rowptr"], col, csr["val"], z, halo, graph.num_dst_nodes, csr.get("plan"))
         ctx.hc, ctx.graph, ctx.n_local, ctx.w_ref = hc, graph, n_local, w
         ctx.save_for_backward(x, w, owner, row)
         return out
@@ -55,11 +55,10 @@ class _HaloLinearAggregate(autograd.Function):
         csr = ctx.graph.csr()
         F = grad.size(1)
         C.spmm_peer_push(csr["rowptr_t"], csr["col_t"], csr["val_t"], grad.contiguous(), ctx.graph.num_src_nodes,
-                         hc.tables[buf], owner, row, hc.F)
+                         hc.tables[buf], owner, row, hc.F, csr.get("plan_t"))
         hc.barrier()
         g = hc.arena[buf]
-        gz = g[: ctx.n_local, :F].clone()
-        g[: ctx.n_local, :F].zero_()  # ready for its next use, two calls later
+        gz = g[: ctx.n_local, :F]  # read in place by both GEMMs (row stride hc.F), no copy
         gx = C.linear_dgrad(gz, w.contiguous()) if ctx.needs_input_grad[0] else None
         gw = None
         if ctx.needs_input_grad[1]:
@@ -67,6 +66,7 @@ class _HaloLinearAggregate(autograd.Function):
             target = sink if sink is not None else torch.zeros_like(w)
             C.linear_wgrad(gz, x.contiguous(), target, None, None)
             gw = None if sink is not None else target
+        gz.zero_()  # after both GEMMs (same stream): ready for its next use, two calls later
         return gx, gw, None, None
 
 

@@ -69,6 +69,15 @@ def test_spmm_csr_skewed_rows(F):
     acc = dev(base.clone())
     C.spmm_csr(dev(rowptr), dev(col), dev(val), dev(x), n_rows, acc, True)
     assert _rel(acc.cpu().double(), ref + base.double()) < 1e-6
+    # item plan (64 features): hubs split over items with atomic adds, empty rows as zero items;
+    # the output starts from garbage to show every row is written
+    from starry_unigraph.data.partition import spmm_plan
+
+    for max_edges, warps in ((128, None), (16, 37)):
+        plan = spmm_plan(dev(rowptr), max_edges, warps)
+        out = torch.full((n_rows, F), float("nan"), device="cuda")
+        C.spmm_csr(dev(rowptr), dev(col), dev(val), dev(x), n_rows, out, False, plan)
+        assert _rel(out.cpu().double(), ref) < 1e-6, (max_edges, warps)
 
 
 @pytest.mark.parametrize("H,FX,strided", [(64, 64, True), (128, 128, True), (32, 20, False)])
