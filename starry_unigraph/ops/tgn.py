@@ -101,6 +101,8 @@ class TGNCudaEngine:
         self.model = model
         self.updater = updater
         self.memory = memory
+        # multi-GPU write-back overlapped with the next step (reference ctdg.async_sync)
+        self.async_sync = bool(getattr(memory, "async_sync", True))
         dev = memory.memory.device
         self.device = dev
         D = memory.hidden_dim
@@ -377,6 +379,10 @@ class TGNCudaEngine:
                               float(o.betas[1]), float(o.eps), float(o.weight_decay), 1.0 / P.world)
         main.wait_stream(self._side)
         P.signal_end(C)
+        if not self.async_sync:
+            # ctdg.async_sync off: the step also waits for every peer's pushes, so the next
+            # step starts from fully written-back tables instead of overlapping them
+            P.drain(C)
 
     def _backward(self, gw: dict[str, torch.Tensor]) -> None:
         """Data gradients on the main stream; every weight-gradient GEMM forks onto a

@@ -66,6 +66,22 @@ def test_hash_partition_two_ranks_consistent(tmp_path, assign):
 
 
 @need2
+def test_async_sync_off_gives_the_same_steps(tmp_path):
+    """ctdg.async_sync false makes each step wait for every peer's write-back; the
+    overlapped default reads the same tables (the next step's remote reads wait
+    for the peers' end signals either way), so the runs agree."""
+    _run(tmp_path, 2, "--batch", "100", "--steps", "10", "--lr", "0", "--mode", "hash", port=29641)
+    _run(tmp_path, 2, "--batch", "100", "--steps", "10", "--lr", "0", "--mode", "hash", "--sync", "--tag", "_sync",
+         port=29642)
+    for r in (0, 1):
+        a = torch.load(tmp_path / f"w2_r{r}.pt")
+        b = torch.load(tmp_path / f"w2_r{r}_sync.pt")
+        torch.testing.assert_close(torch.tensor(b["losses"]), torch.tensor(a["losses"]), rtol=1e-6, atol=1e-7)
+        for k in ("memory", "memory_ts", "mailbox", "mailbox_ts"):
+            torch.testing.assert_close(b[k], a[k], rtol=1e-6, atol=1e-7, msg=k)
+
+
+@need2
 @pytest.mark.parametrize("decay", [False, True])
 def test_dtdg_nvlink_halo_matches_nccl_route(tmp_path, decay):
     """MPNN-LSTM over 2 partitions: halo read from peer memory inside the

@@ -28,6 +28,8 @@ def main():
     p.add_argument("--lr", type=float, default=1e-3)
     p.add_argument("--graphs", type=int, default=1)
     p.add_argument("--assign", default="balanced", choices=["balanced", "owner"])
+    p.add_argument("--sync", action="store_true", help="ctdg.async_sync false: each step waits for the write-backs")
+    p.add_argument("--tag", default="", help="suffix of the output files")
     a = p.parse_args()
     import torch
 
@@ -44,12 +46,12 @@ def main():
            "train": {"epochs": 1, "batch_size": a.batch, "lr": a.lr},
            "runtime": {"device": "cuda", "cuda_graphs": bool(a.graphs)},
            "ctdg": {"mailbox_slots": 1, "dim_time": 16, "num_head": 2, "dropout": 0.0, "att_dropout": 0.0,
-                    "event_partition": "owner" if a.mode == "owner0" else a.assign},
+                    "event_partition": "owner" if a.mode == "owner0" else a.assign, "async_sync": not a.sync},
            "sampling": {"neighbor_limit": [5], "strategy": "recent", "history": 1},
            "graph": {"partition": "round_robin"},
            "dist": {"backend": "nccl", "timeout_s": 120}}
     s = SchedulerSession.from_config(cfg)
-    s.ctx.artifact_root = Path(a.out) / f"art_w{world}_r{rank}"
+    s.ctx.artifact_root = Path(a.out) / f"art_w{world}_r{rank}{a.tag}"
     if world > 1:
         from starry_unigraph.distributed import initialize_distributed
 
@@ -78,7 +80,7 @@ def main():
     torch.save({"memory": mb.memory.cpu(), "memory_ts": mb.memory_ts.cpu(), "mailbox": mb.mailbox.cpu(),
                 "mailbox_ts": mb.mailbox_ts.cpu(), "params": eng.flat.data.cpu(), "losses": losses,
                 "owner": mb.owner.cpu(), "peer": eng.peer is not None, "sizes": sizes},
-               Path(a.out) / f"w{world}_r{rank}.pt")
+               Path(a.out) / f"w{world}_r{rank}{a.tag}.pt")
     if world > 1:
         eng.reset_graphs()
         from starry_unigraph.distributed import finalize_distributed
