@@ -461,10 +461,28 @@ def _ctdg_run(args, precision: str = "tf32") -> dict:
     e2e_s = time.perf_counter() - t0
     barrier()
 
+    phases = None
     if args.trace and hasattr(eng, "trace_step"):
-        b = e2e_batches[-1] if e2e_batches else timed[-1]
-        eng.load_batch(b.src, b.dst, b.ts, b.event_ids)
-        rows = eng.trace_step("train", True)
+        # per-op device times of eager steps (after the timed region), summed into the phases of
+        # the multi-GPU step; the wait phase absorbs the peers' lateness (load imbalance)
+        phase_of = {"tgn_peer_wait_claim": "end_wait_and_claims", "peer_barrier": "barrier_grads_complete",
+                    "tgn_peer_push": "writeback_push_side_stream", "peer_rs_adam_ag": "reduce_scatter_adam_allgather",
+                    "peer_signal": "end_signal"}
+        names = ["compute"] + list(phase_of.values())
+        acc = dict.fromkeys(names, 0.0)
+        src = (e2e_batches or timed)[-5:]
+        rows = []
+        for b in src:
+            eng.load_batch(b.src, b.dst, b.ts, b.event_ids)
+            rows = eng.trace_step("train", True)
+            for name, t in rows:
+                acc[phase_of.get(name, "compute")] += t
+        mine_p = torch.tensor([acc[n] / max(1, len(src)) for n in names], dtype=torch.float64, device="cuda")
+        gathered = [mine_p]
+        if world > 1:
+            gathered = [torch.empty_like(mine_p) for _ in range(world)]
+            dist.all_gather(gathered, mine_p)
+        phases = {n: [round(float(g[i]), 4) for g in gathered] for i, n in enumerate(names)}
         if rank == 0:
             print(f"# per-op device time, one eager step (rank 0): {sum(t for _, t in rows):.3f} ms summed",
                   file=sys.stderr)
@@ -524,6 +542,9 @@ def _ctdg_run(args, precision: str = "tf32") -> dict:
         cons["rows_written_on_non_owners"] = int(stray)
         cons["peer_path"] = eng.peer is not None
         line["consistency"] = cons
+    if phases is not None:
+        # --trace: device ms per step and phase (eager steps, CUDA events around every op), one value per rank
+        line["phases_ms_per_step"] = phases
     eng.reset_graphs()
     return line
 
