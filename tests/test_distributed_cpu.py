@@ -22,7 +22,7 @@ def _port() -> int:
         return s.getsockname()[1]
 
 
-def _launch(out, family, extra_env=None, *args, wall=240, nproc=2):
+def _launch(out, family, extra_env=None, *args, wall=420, nproc=2):
     env = dict(os.environ)
     env.pop("CUDA_VISIBLE_DEVICES", None)
     env.update(extra_env or {})

@@ -110,7 +110,12 @@ def _row_order_worker(rank: int, world: int, port: int, out: str):
 
 
 def test_set_row_order_publishes_every_ranks_order(tmp_path):
-    mp.spawn(_row_order_worker, args=(2, 29611, str(tmp_path)), nprocs=2, join=True)
+    import socket
+
+    with socket.socket() as sock:  # a free port for the rendezvous
+        sock.bind(("127.0.0.1", 0))
+        port = sock.getsockname()[1]
+    mp.spawn(_row_order_worker, args=(2, port, str(tmp_path)), nprocs=2, join=True)
     assert all(torch.load(tmp_path / f"r{r}.pt") for r in range(2))
 
 

@@ -19,7 +19,8 @@ def main():
     p = argparse.ArgumentParser()
     p.add_argument("--family", default="mpnn_lstm")
     p.add_argument("--out", required=True)
-    p.add_argument("--timeout", type=float, default=60.0)
+    # generous: on a cold machine the first torch import of each rank can take a minute
+    p.add_argument("--timeout", type=float, default=240.0)
     p.add_argument("--heartbeat", type=float, default=0.0)
     p.add_argument("--resume", action="store_true",
                    help="CTDG: train K1 + K2 steps, and K1 steps -> exact-resume checkpoint -> new session -> K2 steps")
