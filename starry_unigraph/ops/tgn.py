@@ -277,7 +277,11 @@ class TGNCudaEngine:
         C.tgn_link_loss(self.P, self.src_idx, self.dst_idx, self.neg_idx, self.n_ev, m.dst_fc.bias, m.out_fc.weight,
                         m.out_fc.bias, train, self.scores, self.loss, self.dP, gw["out_fc.weight"], gw["out_fc.bias"],
                         gw["dst_fc.bias"])
-        C.tgn_metrics(self.scores, self.n_ev, self.metrics)
+        # AP/AUC/MRR only feed reporting: computed on the side stream, overlapping the backward pass
+        main = torch.cuda.current_stream(self.device)
+        self._side.wait_stream(main)
+        with torch.cuda.stream(self._side):
+            C.tgn_metrics(self.scores, self.n_ev, self.metrics)
         if train:
             C.tgn_link_proj_bwd(self.dP, self.out, self.n_roots, m.src_fc.weight, m.dst_fc.weight,
                                 gw["src_fc.weight"], gw["src_fc.bias"], gw["dst_fc.weight"], gw["dst_fc.bias"],
@@ -289,6 +293,7 @@ class TGNCudaEngine:
                 if self.grad_sync is not None:
                     scale = self.grad_sync(self.flat.grad)
                 self.opt.step(grad_scale=scale)
+        main.wait_stream(self._side)
         if self.peer is not None:
             self._peer_sync(train)
 
