@@ -143,3 +143,42 @@ def test_route_volume_summary():
 
     v = plan_from_routes(_Routes())
     assert v["send_rows"] == [3, 0, 5] and v["max_recv"] == 4 and v["total_send"] == 8
+
+
+def test_store_memory_bank_and_state():
+    """runtime.store: ring-slot mail writes per node, versioned updates, and a
+    dense state view whose update / gather round-trip rows and mail."""
+    import torch
+
+    from starry_unigraph.runtime.store import MemoryBank, MemoryState, RNNState, TensorFeatureStore  # noqa: F401
+
+    bank = MemoryBank(num_nodes=6, hidden_dim=2, edge_feat_dim=1, mailbox_slots=2)
+    mails = torch.arange(4 * 5, dtype=torch.float32).view(4, 5)
+    bank.write_mail(torch.tensor([3, 1, 3, 3]), mails, torch.tensor([1.0, 2.0, 3.0, 4.0]))
+    # node 3 got three mails into two slots: slot 0 <- first, slot 1 <- second, slot 0 <- third
+    assert torch.equal(bank.mailbox[3, 0], mails[3]) and torch.equal(bank.mailbox[3, 1], mails[2])
+    assert torch.equal(bank.mailbox[1, 0], mails[1]) and int(bank.next_mail_pos[3]) == 1
+    assert bank.mailbox_ts[3].tolist() == [4.0, 3.0]
+    d = bank.describe()
+    assert d["memory_version"] == 1 and d["num_local_nodes"] == 6 and d["mailbox_slots"] == 2
+    st = MemoryState(6, 2, bank)
+    st.update(torch.tensor([0, 5]), torch.tensor([[1.0, 2.0], [3.0, 4.0]]), mails=torch.ones(2, 5))
+    rows, mb = st.gather(torch.tensor([5, 0]), mails=True)
+    assert rows.tolist() == [[3.0, 4.0], [1.0, 2.0]] and torch.equal(mb[:, 0], torch.ones(2, 5))
+
+
+def test_spatial_and_state_deps():
+    import torch
+
+    from starry_unigraph.runtime.route.comm_plan import SpatialDeps, StateDeps
+
+    # 2 ranks x 3 clusters; send index grouped by cluster
+    deps = SpatialDeps(torch.tensor([1, 2, 3, 4, 5, 6]), torch.tensor([6, 5, 4, 3, 2, 1]), torch.arange(10),
+                       torch.tensor([0, 3, 7, 10]))
+    r = deps.to_route([0, 2], num_clusters=3)
+    assert r.send_sizes == [1 + 3, 4 + 6] and r.recv_sizes == [6 + 4, 3 + 1]
+    assert r.send_index.tolist() == [0, 1, 2, 7, 8, 9]
+    s = StateDeps(torch.tensor([1, 2]), torch.tensor([0, 1]), torch.tensor([5, 6, 7]),
+                  [torch.tensor([0]), torch.tensor([1]), torch.tensor([0, 1])])
+    f = s.stale_filter(torch.tensor([True, False, True]))
+    assert f.write_notify.tolist() == [5, 7] and [t.tolist() for t in f.write_to_clusters] == [[0], [0, 1]]
