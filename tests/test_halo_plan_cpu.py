@@ -142,3 +142,36 @@ def test_halo_width_of_the_flare_models():
     assert halo_width(build_flare_model("mpnn_lstm", 64, 64, 1), 64) == 64
     assert halo_width(build_flare_model("evolvegcn", 128, 128, 2), 128) == 128  # no stack: the default
 
+
+
+def test_spmm_item_plan_covers_every_edge_once():
+    """The item plan of the 64-feature aggregation kernel, built on CPU tensors:
+    every row's edges are covered by its items exactly once and in order, a row
+    without edges is one empty item, rows longer than the item size are split
+    (and flagged, and listed for zeroing), and the warp offsets partition the
+    items with roughly equal edge counts."""
+    from starry_unigraph.data.partition import spmm_plan
+
+    g = torch.Generator().manual_seed(5)
+    deg = torch.randint(0, 6, (500,), generator=g)
+    deg[7], deg[100], deg[101] = 1000, 0, 129
+    rowptr = torch.zeros(501, dtype=torch.long)
+    rowptr[1:] = deg.cumsum(0)
+    max_edges, warps = 64, 13
+    items, woff, split = spmm_plan(rowptr, max_edges, warps)
+    it = items.view(3, -1).long()
+    renc, e0, e1 = it[0], it[1], it[2]
+    row = torch.where(renc >= 0, renc, -renc - 1)
+    assert bool((e1 - e0 <= max_edges).all()) and bool((e1 >= e0).all())
+    covered = torch.zeros(int(rowptr[-1]), dtype=torch.long)
+    for r, a, b in zip(row.tolist(), e0.tolist(), e1.tolist()):
+        assert int(rowptr[r]) <= a <= b <= int(rowptr[r + 1])
+        covered[a:b] += 1
+    assert bool((covered == 1).all())
+    per_row = torch.bincount(row, minlength=500)
+    assert bool((per_row >= 1).all())                       # empty rows have their zero item
+    assert int(per_row[100]) == 1 and int((e1 - e0)[row == 100].sum()) == 0
+    assert sorted(split.tolist()) == [7, 101]               # 1000 and 129 edges > 64
+    assert bool((renc[row == 7] < 0).all()) and bool((renc[row == 3] >= 0).all())
+    assert woff.numel() == warps + 1 and int(woff[0]) == 0 and int(woff[-1]) == it.size(1)
+    assert bool((woff[1:] >= woff[:-1]).all())
