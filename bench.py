@@ -44,9 +44,10 @@ def _args():
     p.add_argument("--events", type=int, default=None,
                    help="stream length (tgn config: 7,833,140; jodie config: 200,000,000)")
     p.add_argument("--batch", type=int, default=None, help="events per rank per step (tgn: 600, jodie: 4000)")
-    p.add_argument("--workload", default="tgn", choices=["tgn", "jodie", "mpnn_lstm", "tgcn", "evolvegcn"],
+    p.add_argument("--workload", default="tgn", choices=["tgn", "jodie", "mpnn_lstm", "tgcn", "evolvegcn", "tgn_cpu"],
                    help="tgn: TGN train events/sec (default, config 3); jodie: JODIE train events/sec (config 4); "
-                        "mpnn_lstm: MPNN-LSTM train snapshots/sec (config 2); tgcn / evolvegcn: config 5")
+                        "mpnn_lstm: MPNN-LSTM train snapshots/sec (config 2); tgcn / evolvegcn: config 5; "
+                        "tgn_cpu: TGN train events/sec in one CPU process (config 1), host-timed")
     p.add_argument("--snapshots", type=int, default=None, help="DTDG: snapshots generated (mpnn_lstm: 128, tgcn/evolvegcn: 32)")
     p.add_argument("--nodes", type=int, default=None, help="DTDG: nodes (mpnn_lstm: 200,000; tgcn/evolvegcn: 2,000,000)")
     p.add_argument("--edges", type=int, default=None,
@@ -549,10 +550,60 @@ def _ctdg_run(args, precision: str = "tf32") -> dict:
     return line
 
 
+def _tgn_cpu_run(args) -> int:
+    """TGN (1-layer attention, 2 heads, memory / time / embedding 100,
+    GRU updater, one mailbox slot, 10 recent neighbours) in one CPU process, fp32, on the
+    9,227-node / 157,474-event Zipf(1.1) stream with 172-dim edge features, batch 200, one
+    negative per event, 70/15/15 split. Steps go through the public per-batch API
+    (``SchedulerSession.ctdg_session.train_step``) and are timed with the host clock (no GPU
+    involved): W untimed steps, then K timed ones."""
+    import tempfile
+
+    import torch
+
+    sys.path.insert(0, str(ROOT))
+    from starry_unigraph import SchedulerSession
+
+    cfg = {"model": {"name": "tgn", "family": "tgn", "task": "temporal_link_prediction", "hidden_dim": 100},
+           "data": {"root": "./data", "name": "tgn_cpu", "format": "synthetic", "synthetic": {"preset": "tgn_cpu"}},
+           "train": {"epochs": 1, "batch_size": args.batch or 200, "lr": 1e-4},
+           "runtime": {"device": "cpu"},
+           "ctdg": {"mailbox_slots": 1, "dim_time": 100, "num_head": 2, "dropout": 0.1, "att_dropout": 0.1},
+           "sampling": {"neighbor_limit": [10], "strategy": "recent", "history": 1}}
+    session = SchedulerSession.from_config(cfg)
+    session.ctx.artifact_root = Path(tempfile.mkdtemp(prefix="su_tgn_cpu_"))
+    session.prepare_data()
+    session.build_runtime()
+    rt = session.ctdg_session.online_runtime
+    batches = []
+    for b in rt.iter_batches("train", args.batch or 200):
+        batches.append(b)
+        if len(batches) >= args.warmup + args.steps:
+            break
+    for b in batches[: args.warmup]:
+        session.ctdg_session.train_step(b)
+    timed = batches[args.warmup:]
+    events = sum(int(b.size) for b in timed)
+    t0 = time.perf_counter()
+    for b in timed:
+        session.ctdg_session.train_step(b)
+    wall = time.perf_counter() - t0
+    print(json.dumps({"metric": "TGN train events/sec (CPU, single process)", "value": events / wall,
+                      "unit": "events/s", "n_gpus": 0, "device": "cpu", "threads": torch.get_num_threads(),
+                      "steps": len(timed), "warmup": args.warmup, "ms_per_step": wall * 1000.0 / max(1, len(timed)),
+                      "higher_is_better": True, "scaling": "none", "vs_baseline": None, "dtype": "fp32",
+                      "data": "synthetic (random-init weights)", "timing": "host clock (perf_counter)",
+                      "config": {"model": "TGN (1-layer temporal attention, 2 heads), CPU", "global_batch": args.batch or 200,
+                                 "events": 157474, "nodes": 9227, "edge_dim": 172, "fanout": 10}}), flush=True)
+    return 0
+
+
 def main():
     args = _args()
     if args.impl == "reference":
         return _reference_arm(args)
+    if args.workload == "tgn_cpu":
+        return _tgn_cpu_run(args)
     if args.workload in DTDG_WORKLOADS:
         return _mpnn_main(args)
     sys.path.insert(0, str(ROOT))
