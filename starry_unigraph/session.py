@@ -279,8 +279,16 @@ class SchedulerSession:
         loss_sum = float(sum(losses))
         steps = len(losses) if split != "train" else len(outputs)
         tot_loss, tot_steps, max_elapsed = self._distributed_epoch_stats(loss_sum, steps, elapsed)
+        loss = tot_loss / tot_steps if tot_steps else 0.0
+        # "loss" keeps the reference's figure (sum over ranks / total steps). A DTDG rank's loss
+        # is already weighted by its share of the nodes, so that figure is the global mean
+        # divided by the world size; "global_loss" is the global mean itself.
+        shares = self.ctdg_session is None and self.runtime is not None and \
+            "part_loss_scale" in getattr(self.runtime, "state", {})
+        world = self.ctx.dist.world_size if self.ctx.dist.is_distributed and dist.is_initialized() else 1
         return {"split": split, "steps": tot_steps, "local_steps": steps,
-                "loss": tot_loss / tot_steps if tot_steps else 0.0, "local_loss": loss_sum / steps if steps else 0.0,
+                "loss": loss, "global_loss": loss * world if shares else loss,
+                "local_loss": loss_sum / steps if steps else 0.0,
                 "metrics": {k: float(sum(v) / len(v)) for k, v in metric_acc.items() if v},
                 "elapsed_s": max_elapsed, "local_elapsed_s": elapsed, "outputs": outputs}
 
