@@ -1,8 +1,10 @@
 """MemShare-style historical cache (reference backends/ctdg/runtime/cache.py:18-180).
 
 Caches the last value pushed for every shared (non-owned) node; a new update is
-only pushed when the cosine distance to the cached value exceeds 1 - alpha.
-``AdaParameter`` moves alpha with the sync/compute latency ratio.
+only pushed when the cosine distance to the cached value exceeds 1 - alpha, so a
+larger alpha pushes more rows. ``AdaParameter`` moves alpha with the ratio of a
+step's sync time to its compute time; the host runtime drives it after every
+training step when ``ctdg.ada_param_enabled`` is set.
 """
 from __future__ import annotations
 
@@ -20,10 +22,17 @@ class AdaParameter:
     _step: int = field(default=0, init=False, repr=False)
 
     def update_from_latency(self, sync_ms: float, compute_ms: float) -> None:
+        """Push fewer rows when sync outweighs compute, more when compute does.
+
+        alpha moves by 0.01 * (1 - sync / compute) per call, within [min_alpha,
+        max_alpha]. The reference (cache.py:26-37) adds 0.01 * (ratio - 1), which
+        raises alpha, and so the number of pushed rows, exactly when its own comment
+        says sync dominates and filtering should tighten; this keeps the documented
+        intent (the reference never calls the method)."""
         if compute_ms <= 0:
             return
         ratio = sync_ms / (compute_ms + 1e-9)
-        self.alpha = float(max(self.min_alpha, min(self.max_alpha, self.alpha + 0.01 * (ratio - 1.0))))
+        self.alpha = float(max(self.min_alpha, min(self.max_alpha, self.alpha + 0.01 * (1.0 - ratio))))
         self._step += 1
 
 

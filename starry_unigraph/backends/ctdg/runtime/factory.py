@@ -130,13 +130,15 @@ def build_ctdg_runtime(session_ctx: SessionContext, dataset: TGTemporalDataset |
                                      lr=lr)
     if dctx.is_distributed and node_parts is not None:
         shared = torch.nonzero(node_parts != dctx.rank).view(-1).to(device)
-        ada = AdaParameter(alpha=float(c.get("historical_alpha", 0.5))) if c.get("ada_param_enabled", True) else None
+        # the configured alpha holds either way; ada_param_enabled only lets the runtime move it
+        ada = AdaParameter(alpha=float(c.get("historical_alpha", 0.5)))
         if not bool(c.get("remote_fetch", True)):
             memory.historical_cache = CTDGHistoricalCache(shared.numel(), hidden, device, dataset.num_nodes, shared,
                                                           ada)
     online = CTDGOnlineRuntime(dataset=dataset, sampler=sampler, memory=memory, model=model, optimizer=optimizer,
                                route=route, device=device, dist_ctx=dctx, memory_updater=updater, engine=engine,
-                               memory_grad=bool(c.get("memory_grad", False)), seed=seed)
+                               memory_grad=bool(c.get("memory_grad", False)), seed=seed,
+                               adaptive_alpha=bool(c.get("ada_param_enabled", True)))
     online.broadcast_updater_params()
     bundle = RuntimeBundle(model=model, optimizer=optimizer,
                            state={"pipeline": "ctdg_online_native", "dataset": dataset.describe(),

@@ -61,7 +61,7 @@ class CTDGOnlineRuntime:
     def __init__(self, dataset: TGTemporalDataset, sampler: NativeTemporalSampler, memory: CTDGMemoryBank,
                  model: CTDGLinkPredictor, optimizer: Any, route: CTDGFeatureRoute, device: str,
                  dist_ctx: DistributedContext, memory_updater: torch.nn.Module | None = None, engine: Any = None,
-                 memory_grad: bool = False, seed: int = 0):
+                 memory_grad: bool = False, seed: int = 0, adaptive_alpha: bool = False):
         self.dataset = dataset
         self.sampler = sampler
         self.memory = memory
@@ -73,6 +73,8 @@ class CTDGOnlineRuntime:
         self.memory_updater = memory_updater
         self.engine = engine
         self.memory_grad = memory_grad
+        # with a historical cache: move its push threshold with each step's sync / compute time
+        self.adaptive_alpha = adaptive_alpha
         self._gen = torch.Generator().manual_seed(seed)
         self._dst_node_pool: torch.Tensor | None = None
         self._edge_feat_dev: torch.Tensor | None = None
@@ -245,12 +247,16 @@ class CTDGOnlineRuntime:
         t1 = time.perf_counter()
         self._submit_syncs(batch)
         submit_ms = (time.perf_counter() - t1) * 1000.0
+        step_ms = (time.perf_counter() - t0) * 1000.0
+        cache = self.memory.historical_cache
+        if cache is not None and self.adaptive_alpha:
+            cache.ada_param.update_from_latency(wait_ms + submit_ms, step_ms - wait_ms - submit_ms)
         return {"loss": float(loss.item()), "predictions": torch.sigmoid(pos).detach().cpu().tolist(),
                 "targets": [1] * batch.size,
                 "meta": {"split": batch.split, "batch_size": batch.size, "sample": prepared.sample.describe() if prepared.sample is not None else None,
                          "metrics": self._metric_dict(pos, neg), "memory": self.memory.describe(),
-                         "sync_wait_ms": wait_ms, "sync_submit_ms": submit_ms,
-                         "step_ms": (time.perf_counter() - t0) * 1000.0}}
+                         "sync_wait_ms": wait_ms, "sync_submit_ms": submit_ms, "step_ms": step_ms,
+                         "historical_alpha": cache.ada_param.alpha if cache is not None else None}}
 
     def eval_step(self, batch: CTDGDataBatch, split: str) -> dict[str, Any]:
         if self.engine is not None:

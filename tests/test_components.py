@@ -143,3 +143,29 @@ def test_chunk_artifacts_carry_routes_and_order(tmp_path):
     mine = [c.chunk_id for c in s.snapshot_core._splits["train"]]
     ranks = [order.index(tuple(c)) for c in mine]
     assert ranks == sorted(ranks)
+
+
+def test_historical_cache_threshold_and_adaptive_alpha():
+    """A shared node is pushed when its cosine distance to the last pushed row exceeds
+    1 - alpha; sync-heavy steps lower alpha (fewer pushes), compute-heavy steps raise it."""
+    from starry_unigraph.backends.ctdg.runtime.cache import AdaParameter, CTDGHistoricalCache
+
+    shared = torch.tensor([1, 3, 5])
+    cache = CTDGHistoricalCache(3, 2, "cpu", num_nodes=6, shared_node_ids=shared, ada_param=AdaParameter(alpha=0.5))
+    ids = torch.tensor([1, 3, 5, 0])
+    rows = torch.tensor([[1.0, 0.0], [1.0, 0.0], [1.0, 0.0], [1.0, 0.0]])
+    assert cache.historical_check(ids, rows).tolist() == [True, True, True, True]  # never cached / not shared
+    cache.update_cache(cache.slot_indices(ids[:3]), rows[:3], torch.zeros(3))
+    # cosine distances 0, 1 - cos(60 deg) = 0.5, 1 - cos(90 deg) = 1 against the threshold 0.5
+    new = torch.tensor([[1.0, 0.0], [0.5, 0.75 ** 0.5 + 1e-3], [0.0, 1.0], [1.0, 0.0]])
+    assert cache.historical_check(ids, new).tolist() == [False, True, True, True]
+    ada = cache.ada_param
+    ada.update_from_latency(sync_ms=30.0, compute_ms=10.0)  # sync dominates
+    assert ada.alpha < 0.5
+    assert cache.historical_check(ids, new).tolist() == [False, False, True, True]
+    for _ in range(1000):
+        ada.update_from_latency(sync_ms=0.0, compute_ms=10.0)
+    assert ada.alpha == ada.max_alpha
+    for _ in range(1000):
+        ada.update_from_latency(sync_ms=1e3, compute_ms=1.0)
+    assert ada.alpha == ada.min_alpha

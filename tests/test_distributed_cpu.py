@@ -63,6 +63,23 @@ def test_ctdg_two_ranks_memory_partition(tmp_path):
         assert torch.allclose(a, b, atol=1e-6)
 
 
+@pytest.mark.parametrize("adaptive", [True, False])
+def test_ctdg_historical_cache_alpha(tmp_path, adaptive):
+    """Remote reads off (the reference's push path): the historical cache filters the
+    pushed rows; with ada_param_enabled its alpha follows each step's sync / compute
+    time within its bounds, without it alpha stays at historical_alpha."""
+    over = json.dumps({"remote_fetch": False, "historical_alpha": 0.3, "ada_param_enabled": adaptive})
+    res = _launch(tmp_path, "tgn", None, "--ctdg-json", over)
+    assert res.returncode == 0, res.stdout[-2000:] + res.stderr[-4000:]
+    for r in range(2):
+        o = _outcome(tmp_path, r)
+        assert o["error"] is None and len(o["alphas"]) >= 2  # one per non-empty local step
+        if adaptive:
+            assert all(0.1 <= x <= 0.95 for x in o["alphas"]) and len(set(o["alphas"])) > 1
+        else:
+            assert set(o["alphas"]) == {0.3}
+
+
 def test_ctdg_exact_resume_two_ranks(tmp_path):
     """Each rank saves its own memory-bank rows, optimizer moments and random
     streams; a fresh session that loads them continues exactly like the

@@ -24,6 +24,7 @@ def main():
     p.add_argument("--heartbeat", type=float, default=0.0)
     p.add_argument("--resume", action="store_true",
                    help="CTDG: train K1 + K2 steps, and K1 steps -> exact-resume checkpoint -> new session -> K2 steps")
+    p.add_argument("--ctdg-json", default=None, help="JSON object merged into the config's ctdg section")
     a = p.parse_args()
     import torch
 
@@ -40,6 +41,8 @@ def main():
            "graph": {"storage": "events" if ctdg else "snapshots"},
            "ctdg": {"dim_time": 8, "mailbox_slots": 1},
            "dist": {"backend": "gloo", "timeout_s": a.timeout, "heartbeat_s": a.heartbeat}}
+    if a.ctdg_json:
+        cfg["ctdg"].update(json.loads(a.ctdg_json))
     s = SchedulerSession.from_config(cfg)
     s.ctx.artifact_root = Path(a.out) / f"art_r{rank}"
     initialize_distributed(s.ctx.dist)
@@ -55,6 +58,8 @@ def main():
         r = s.run_epoch("train")
         outcome["steps"] = r["steps"]
         outcome["loss"] = r["loss"]
+        outcome["alphas"] = [o["meta"].get("historical_alpha") for o in r["outputs"]
+                             if "historical_alpha" in o.get("meta", {})]
         model = s.runtime.model.module if hasattr(s.runtime.model, "module") else s.runtime.model
         torch.save({"params": [p.detach().clone() for p in model.parameters()], "losses":
                     [o.get("loss") for o in r["outputs"] if isinstance(o.get("loss"), float)]},
