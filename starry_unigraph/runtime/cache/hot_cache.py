@@ -18,16 +18,22 @@ class HotCache:
         self.misses = 0
 
     def lookup(self, node_ids: Tensor) -> tuple[Tensor, Tensor]:
-        ids = node_ids.to(self.ids.device).long()
-        match = ids.unsqueeze(1) == self.ids.unsqueeze(0) if self.capacity <= 65536 else None
-        if match is None:
-            return torch.zeros_like(ids, dtype=torch.bool), torch.zeros(ids.numel(), self.rows.size(1))
-        hit = match.any(1)
-        slot = match.float().argmax(1)
-        self.freq.index_add_(0, slot[hit], torch.ones_like(slot[hit]))
+        """(hit mask, rows): a sorted search of the resident ids, at any capacity; hits
+        count toward their slot's frequency, misses read as zero rows."""
+        ids = node_ids.to(self.ids.device).long().view(-1)
+        hit = torch.zeros(ids.numel(), dtype=torch.bool, device=ids.device)
+        out = torch.zeros(ids.numel(), self.rows.size(1), dtype=self.rows.dtype, device=self.rows.device)
+        occupied = torch.nonzero(self.ids >= 0).view(-1)
+        if occupied.numel() and ids.numel():
+            key, order = torch.sort(self.ids[occupied])
+            pos = torch.searchsorted(key, ids).clamp(max=key.numel() - 1)
+            hit = key[pos] == ids
+            slot = occupied[order[pos[hit]]]
+            out[hit] = self.rows[slot]
+            self.freq.index_add_(0, slot, torch.ones_like(slot))
         self.hits += int(hit.sum())
         self.misses += int((~hit).sum())
-        return hit, self.rows[slot]
+        return hit, out
 
     def insert(self, node_ids: Tensor, rows: Tensor) -> None:
         """Insert or refresh rows in one pass: ids already cached are updated in

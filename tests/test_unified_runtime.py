@@ -182,3 +182,15 @@ def test_spatial_and_state_deps():
                   [torch.tensor([0]), torch.tensor([1]), torch.tensor([0, 1])])
     f = s.stale_filter(torch.tensor([True, False, True]))
     assert f.write_notify.tolist() == [5, 7] and [t.tolist() for t in f.write_to_clusters] == [[0], [0, 1]]
+
+
+def test_hot_cache_lookup_at_large_capacity():
+    """A cache larger than a dense id-by-slot comparison would allow still hits."""
+    cache = HotCache(capacity=200_000, dim=2)
+    ids = torch.arange(0, 300_000, 2)
+    cache.insert(ids, torch.stack([ids.float(), -ids.float()], 1))
+    hit, got = cache.lookup(torch.tensor([4, 5, 299_998, 7]))
+    assert hit.tolist() == [True, False, True, False]
+    assert got[0].tolist() == [4.0, -4.0] and got[2].tolist() == [299_998.0, -299_998.0]
+    assert got[1].tolist() == [0.0, 0.0]
+    assert cache.describe()["hits"] == 2 and cache.describe()["misses"] == 2
