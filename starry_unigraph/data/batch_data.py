@@ -24,3 +24,4 @@ class BatchData:
     chunk_id: tuple | None = None
     local_node_mask: Tensor | None = None
     remote_manifest: dict[str, Any] | None = None
+    nbr_feat: Tensor | None = None  # [roots, k, F] feature rows of the sampled neighbours (ChunkAtomic.complete)

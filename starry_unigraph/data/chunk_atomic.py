@@ -5,7 +5,9 @@ A chunk holds its events in a temporal CSR over the cluster's master nodes
 (L1), the cross-cluster neighbours with their home clusters (L2) and
 scheduling metadata (L3). ``materialize`` samples the most recent neighbours of
 each event endpoint from the chunk's T-CSR and returns the local message-flow
-block plus the manifest of remote rows that must be fetched from other ranks.
+block plus the manifest of remote rows that must be fetched from other ranks;
+``complete`` assembles the neighbours' feature rows from the local feature store
+and the fetched remote rows.
 """
 from __future__ import annotations
 
@@ -106,10 +108,43 @@ class ChunkAtomic:
                           chunk_id=self.chunk_id, remote_manifest={"count": int(manifest.remote_node_ids.numel())})
         return batch, manifest
 
-    def complete(self, local_mfg: Any, remote_data: dict[str, Tensor] | None = None) -> Any:
-        """Phase 2: splice fetched remote rows into the materialised block."""
-        if remote_data:
-            if hasattr(local_mfg, "mfg") and local_mfg.mfg is not None:
-                local_mfg.remote_manifest = dict(local_mfg.remote_manifest or {}) | {"filled": True}
+    def complete(self, local_mfg: Any, remote_data: dict[str, Tensor] | None = None, local_store: Any = None,
+                 feat_name: str = "x") -> Any:
+        """Phase 2: the feature rows of every sampled neighbour slot, in the block's
+        [roots, k] layout (zero rows for empty slots), into ``batch.nbr_feat``.
+
+        Rows of nodes listed in ``remote_data`` (``{"node_ids": [R], "rows": [R, F]}``,
+        the answer to the phase-1 manifest) come from it; every other neighbour is
+        read from ``local_store`` (a ``FeatureStore`` of the rows this rank owns).
+        ``batch.local_node_mask`` marks the slots served locally. Without a store the
+        batch is returned as it is."""
+        block = getattr(local_mfg, "mfg", None)
+        if local_store is None or block is None or not hasattr(block, "nbr"):
             return local_mfg
+        nbr = block.nbr
+        valid = block.mask()
+        flat = nbr[valid]
+        is_remote = torch.zeros(flat.numel(), dtype=torch.bool)
+        rows = None
+        if remote_data and remote_data.get("node_ids") is not None and remote_data["node_ids"].numel():
+            key, order = torch.sort(remote_data["node_ids"].long())
+            pos = torch.searchsorted(key, flat).clamp(max=key.numel() - 1)
+            is_remote = key[pos] == flat
+            remote_rows = remote_data["rows"][order[pos[is_remote]]]
+            rows = torch.zeros(flat.numel(), remote_rows.size(1), dtype=remote_rows.dtype)
+            rows[is_remote] = remote_rows
+        local_rows = local_store.get_node_feat(flat[~is_remote], feat_name) if bool((~is_remote).any()) else None
+        width = local_store.feat_dim(feat_name)
+        if rows is None:
+            dtype = local_rows.dtype if local_rows is not None else torch.float32
+            rows = torch.zeros(flat.numel(), width, dtype=dtype)
+        if local_rows is not None:
+            rows[~is_remote] = local_rows.to(rows)
+        out = torch.zeros(*nbr.shape, width, dtype=rows.dtype)
+        out[valid] = rows
+        local_mask = torch.zeros(nbr.shape, dtype=torch.bool)
+        local_mask[valid] = ~is_remote
+        local_mfg.nbr_feat = out
+        local_mfg.local_node_mask = local_mask
+        local_mfg.remote_manifest = dict(local_mfg.remote_manifest or {}) | {"filled": int(is_remote.sum())}
         return local_mfg

@@ -155,12 +155,12 @@ def _load_from_ctdg_csv(dataset_dir: Path) -> RawTemporalEvents | None:
             return RawTemporalEvents(torch.empty(0, dtype=torch.long), torch.empty(0, dtype=torch.long), torch.empty(0),
                                      torch.empty(0), torch.empty(0, 1), nfeat.size if nfeat else 0, 0, str(edges_path), nfeat)
         return None
-    src = torch.as_tensor(frame["src"].to_numpy(dtype="int64"))
-    dst = torch.as_tensor(frame["dst"].to_numpy(dtype="int64"))
+    src = torch.as_tensor(frame["src"].to_numpy(dtype="int64", copy=True))
+    dst = torch.as_tensor(frame["dst"].to_numpy(dtype="int64", copy=True))
     ts_col = "time" if "time" in frame.columns else ("ts" if "ts" in frame.columns else frame.columns[-1])
-    ts = torch.as_tensor(frame[ts_col].to_numpy(dtype="float32"))
+    ts = torch.as_tensor(frame[ts_col].to_numpy(dtype="float32", copy=True))
     wcol = "w" if "w" in frame.columns else ("weight" if "weight" in frame.columns else None)
-    weight = torch.ones(src.numel()) if wcol is None else torch.as_tensor(frame[wcol].to_numpy(dtype="float32"))
+    weight = torch.ones(src.numel()) if wcol is None else torch.as_tensor(frame[wcol].to_numpy(dtype="float32", copy=True))
     num_nodes = int(max(int(src.max()), int(dst.max())) + 1) if src.numel() else 0
     if nfeat is not None and nfeat.size > 0:
         num_nodes = max(num_nodes, int(nfeat.node_ids.max()) + 1)

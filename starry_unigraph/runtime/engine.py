@@ -12,7 +12,12 @@ from starry_unigraph.data.batch_data import BatchData
 
 class PipelineEngine:
     def __init__(self, backend: Any, state_manager: Any, model: Any, task_adapter: Any, device: str = "cpu",
-                 optimizer: Any = None):
+                 optimizer: Any = None, feature_store: Any = None, fetch_remote: Any = None):
+        """`feature_store` (a ``FeatureStore`` of this rank's rows) makes every batch carry
+        its neighbours' feature rows (``BatchData.nbr_feat``); `fetch_remote(manifest)`
+        returns ``{"node_ids", "rows"}`` for the rows the manifest lists on other ranks."""
+        self.feature_store = feature_store
+        self.fetch_remote = fetch_remote
         self.backend = backend
         self.state_manager = state_manager
         self.model = model
@@ -21,7 +26,11 @@ class PipelineEngine:
         self.optimizer = optimizer
 
     def _materialize_batch(self, chunk: Any, sample_config: Any) -> BatchData:
-        batch, _manifest = chunk.materialize(sample_config)
+        batch, manifest = chunk.materialize(sample_config)
+        if self.feature_store is not None:
+            remote = self.fetch_remote(manifest) if self.fetch_remote is not None and \
+                manifest.remote_node_ids.numel() else None
+            batch = chunk.complete(batch, remote, self.feature_store)
         return batch
 
     def iter_batches_with_step(self, split: str = "train", batch_size: int = 64) -> Iterator[tuple[BatchData, Any]]:

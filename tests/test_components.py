@@ -1,6 +1,7 @@
 """Chunk mode, the unified pipeline engine, caches, comm engine and the stable
 library surface, on CPU (reference tests/test_chunk_pipeline.py,
 tests/test_lib_api.py, tests/test_engine.py)."""
+import pytest
 import torch
 
 from starry_unigraph import SchedulerSession
@@ -169,3 +170,89 @@ def test_historical_cache_threshold_and_adaptive_alpha():
     for _ in range(1000):
         ada.update_from_latency(sync_ms=1e3, compute_ms=1.0)
     assert ada.alpha == ada.min_alpha
+
+
+def test_feature_store_owned_rows_and_edges():
+    from starry_unigraph.data import TensorFeatureStore
+
+    owned = torch.tensor([7, 2, 9])
+    x = torch.arange(6, dtype=torch.float32).view(3, 2)
+    e = torch.arange(10, dtype=torch.float32).view(5, 2)
+    fs = TensorFeatureStore({"x": x, "h": -x}, {"edge_attr": e}, node_ids=owned)
+    assert torch.equal(fs.get_node_feat(torch.tensor([9, 7])), x[[2, 0]])
+    assert torch.equal(fs.get_node_feat(torch.tensor([2]), "h"), -x[[1]])
+    assert torch.equal(fs.get_edge_feat(torch.tensor([4, 0])), e[[4, 0]])
+    assert fs.num_nodes() == 3 and fs.feat_dim() == 2 and fs.feat_dim("edge_attr") == 2
+    with pytest.raises(IndexError):
+        fs.get_node_feat(torch.tensor([3]))
+    with pytest.raises(KeyError):
+        fs.get_node_feat(torch.tensor([7]), "y")
+    fs.put_node_feat(torch.tensor([2]), torch.tensor([[5.0, 5.0]]))
+    assert fs.pin_memory() is fs and torch.equal(fs.to("cpu").get_node_feat(torch.tensor([2])), torch.tensor([[5.0, 5.0]]))
+    assert torch.equal(TensorFeatureStore(x).get(torch.tensor([1])), x[[1]])  # row i is node i
+
+
+def test_global_csr_protocol_and_temporal_reads(tmp_path):
+    from starry_unigraph.data.global_csr import TemporalGlobalCSR
+
+    src, dst, ts, n = _stream(n_nodes=30, n_events=400, seed=5)
+    g = TemporalGlobalCSR(src, dst, ts, n)
+    assert g.num_nodes == n and g.num_edges == 400 and g.rowptr().numel() == n + 1 and g.col().numel() == 400
+    nodes = torch.tensor([4, 0, 17])
+    nbr, eid = g.neighbors(nodes)
+    expect = [i for v in nodes.tolist() for i in range(400) if int(dst[i]) == v]  # stream (time) order per node
+    assert eid.tolist() == expect and nbr.tolist() == src[expect].tolist()
+    # induced subgraph, renumbered to positions in the node list
+    keep = torch.tensor([3, 11, 5, 20, 8])
+    sub = g.subgraph(keep)
+    both = [i for i in range(400) if int(src[i]) in keep.tolist() and int(dst[i]) in keep.tolist()]
+    assert sub.num_nodes == 5 and sub.num_edges == len(both)
+    pos = {v: i for i, v in enumerate(keep.tolist())}
+    s_nbr, s_eid = sub.neighbors(torch.arange(5))
+    assert sorted(s_eid.tolist()) == both
+    assert all(pos[int(src[e])] == int(v) for v, e in zip(s_nbr.tolist(), s_eid.tolist()))
+    # strictly-earlier neighbours (int64-truncated timestamps, as the sampler)
+    t = float(ts[200])
+    b_nbr, b_ts, b_eid = g.neighbors_before(4, t)
+    assert b_eid.tolist() == [i for i in range(400) if int(dst[i]) == 4 and int(ts[i]) < int(t)]
+    # load from a dataset directory, whole and sharded by destination
+    d = tmp_path / "toy"
+    d.mkdir()
+    rows = ["src,dst,time"] + [f"{int(a)},{int(b)},{float(c):.3f}" for a, b, c in zip(src[:50], dst[:50], ts[:50])]
+    (d / "edges.csv").write_text("\n".join(rows) + "\n")
+    whole = TemporalGlobalCSR.load(d)
+    parts = [TemporalGlobalCSR.load(d, rank=r, world_size=2) for r in range(2)]
+    assert whole.num_edges == 50 and sum(p.num_edges for p in parts) == 50
+    for r, p in enumerate(parts):
+        deg = p.rowptr()[1:] - p.rowptr()[:-1]
+        assert bool((deg[torch.arange(p.num_nodes) % 2 != r] == 0).all())
+
+
+def test_chunk_complete_assembles_local_and_remote_rows():
+    """Phase 1 lists the neighbours owned elsewhere; phase 2 fills every sampled
+    slot from the local store or the fetched rows, equal to a gather from the
+    whole table."""
+    from starry_unigraph.backends.chunk.prepare import ChunkGenerator
+    from starry_unigraph.data import TensorFeatureStore
+    from starry_unigraph.data.sample_config import SampleConfig
+
+    src, dst, ts, n = _stream(n_nodes=40, n_events=600, seed=2)
+    table = torch.randn(n, 3)
+    owner = torch.arange(n) % 2
+    rank = 0
+    mine = torch.nonzero(owner == rank).view(-1)
+    store = TensorFeatureStore(table[mine], node_ids=mine)
+    chunks = ChunkGenerator(num_clusters=2, time_slices=3, adaptive=False).generate(src, dst, ts, n)["chunks"]
+    filled = 0
+    for ch in chunks:
+        batch, manifest = ch.materialize(SampleConfig(num_neighbors=[4]), owner=owner, rank=rank)
+        assert bool((owner[manifest.remote_node_ids] != rank).all())
+        remote = {"node_ids": manifest.remote_node_ids, "rows": table[manifest.remote_node_ids]}
+        out = ch.complete(batch, remote, store)
+        block = out.mfg
+        m = block.mask()
+        assert torch.equal(out.nbr_feat[m], table[block.nbr[m]])
+        assert bool((out.nbr_feat[~m] == 0).all())
+        assert torch.equal(out.local_node_mask[m], owner[block.nbr[m]] == rank)
+        filled += out.remote_manifest["filled"]
+    assert filled > 0
