@@ -45,14 +45,20 @@ class ChunkPreprocessor(GraphPreprocessor):
         ctx.provider_state["chunk_order"] = schedule(out["routes"])
         ctx.provider_state["chunk_builder"] = out["builder"] | {"num_clusters": out["num_clusters"],
                                                                 "cross_ratio": out["cross_ratio"]}
+        if W > 1:  # a node is owned by the rank that runs its cluster's chunks
+            node_parts = out["clusters"].long() % W
+            ctx.provider_state["node_parts"] = node_parts
+            ctx.provider_state["edge_parts"] = node_parts[ds.src.long()]
 
     def build_runtime_artifacts(self, ctx: SessionContext) -> PreparedArtifacts:
         parts = ctx.provider_state["chunk_parts"]
         ds = ctx.provider_state["chunk_dataset"]
         W = len(parts)
+        node_parts = ctx.provider_state.get("node_parts")
         meta: dict[str, Any] = {"graph_mode": "chunk", "artifact_version": ARTIFACT_VERSION, "num_parts": W,
                                 "num_nodes": ds.num_nodes, "num_edges": ds.num_edges,
-                                "builder": ctx.provider_state["chunk_builder"], "pipeline": "chunked"}
+                                "builder": ctx.provider_state["chunk_builder"], "pipeline": "chunked",
+                                "has_node_parts": node_parts is not None, "has_edge_parts": node_parts is not None}
         slices = sorted({ch.chunk_id[0] for p in parts for ch in p})
         routes = ctx.provider_state["chunk_routes"]
         outputs = [ArtifactOutput("partitions/manifest.json", {"num_parts": W, "partition_algo": "cluster_round_robin"}),
@@ -60,6 +66,9 @@ class ChunkPreprocessor(GraphPreprocessor):
                                                            "dependence_routes": [r.describe() for r in routes],
                                                            "order": [list(cid) for cid in ctx.provider_state["chunk_order"]]}),
                    ArtifactOutput("snapshots/manifest.json", {"time_slices": slices, "num_chunks": sum(map(len, parts))})]
+        if node_parts is not None:
+            outputs.append(ArtifactOutput("partitions/node_parts.pt", node_parts, "torch"))
+            outputs.append(ArtifactOutput("partitions/edge_parts.pt", ctx.provider_state["edge_parts"], "torch"))
         for p, chunks in enumerate(parts):
             outputs.append(ArtifactOutput(f"clusters/part_{p:03d}/cluster_manifest.json",
                                           {"part": p, "chunks": [list(c.chunk_id) for c in chunks],

@@ -489,15 +489,17 @@ class SchedulerSession:
         opt = self.runtime.optimizer
         # every rank: on the NVLink path the optimizer moments are sharded and gathered here
         opt_state = opt.state_dict() if opt is not None else None
-        if distributed and rank != 0:
-            return path  # one writer (all ranks hold identical parameters)
-        path.parent.mkdir(parents=True, exist_ok=True)
-        model = self.runtime.model.module if hasattr(self.runtime.model, "module") else self.runtime.model
-        payload = {"model_state": {k: v.detach().cpu() for k, v in model.state_dict().items()},
-                   "optimizer_state": opt_state,
-                   "scheduler_state": self.runtime.scheduler, "config": self.ctx.config,
-                   "epoch": self.current_epoch, "global_step": self.global_step}
-        return save_checkpoint(path, payload)
+        if rank == 0:  # one writer (all ranks hold identical parameters)
+            path.parent.mkdir(parents=True, exist_ok=True)
+            model = self.runtime.model.module if hasattr(self.runtime.model, "module") else self.runtime.model
+            payload = {"model_state": {k: v.detach().cpu() for k, v in model.state_dict().items()},
+                       "optimizer_state": opt_state,
+                       "scheduler_state": self.runtime.scheduler, "config": self.ctx.config,
+                       "epoch": self.current_epoch, "global_step": self.global_step}
+            save_checkpoint(path, payload)
+        if distributed:
+            dist.barrier()  # the file is complete before any rank goes on (and may read it)
+        return path
 
     def load_checkpoint(self, path: str | Path) -> dict[str, Any]:
         if self.ctdg_session is None and self.snapshot_core is None:

@@ -141,9 +141,9 @@ def test_chunk_artifacts_carry_routes_and_order(tmp_path):
     assert routes["dependence_routes"] and routes["order"]
     s.build_runtime()
     order = [tuple(c) for c in routes["order"]]
-    mine = [c.chunk_id for c in s.snapshot_core._splits["train"]]
-    ranks = [order.index(tuple(c)) for c in mine]
-    assert ranks == sorted(ranks)
+    mine = [c.chunk_id for c in s.snapshot_core.iter_chunks("train")]
+    keys = [(c[0], order.index(tuple(c))) for c in mine]  # slice by slice, the schedule's order inside one
+    assert mine and keys == sorted(keys)
 
 
 def test_historical_cache_threshold_and_adaptive_alpha():

@@ -80,6 +80,24 @@ def test_ctdg_historical_cache_alpha(tmp_path, adaptive):
             assert set(o["alphas"]) == {0.3}
 
 
+def test_chunk_mode_two_ranks_uneven_clusters(tmp_path):
+    """Three node clusters on two ranks: rank 0 runs two chunks per time slice, rank 1
+    one. Both take the same number of steps (rank 1 pads with empty steps), so their
+    collectives stay matched through train, validation, checkpoint and predict, and
+    the replicas stay identical."""
+    res = _launch(tmp_path, "tgn", None, "--chunk", "3")
+    assert res.returncode == 0, res.stdout[-2000:] + res.stderr[-4000:]
+    o0, o1 = _outcome(tmp_path, 0), _outcome(tmp_path, 1)
+    assert o0["error"] is None and o1["error"] is None
+    assert o0["local_steps"] == o1["local_steps"] and o0["val_steps"] == o1["val_steps"]
+    assert o0["own_chunks"] > o1["own_chunks"] > 0
+    assert o0["local_steps"] == o0["own_chunks"]  # the rank with the most chunks never pads
+    assert o0["predictions"] > 0
+    p0, p1 = torch.load(tmp_path / "r0.pt"), torch.load(tmp_path / "r1.pt")
+    for a, b in zip(p0["params"], p1["params"]):
+        assert torch.allclose(a, b, atol=1e-6)
+
+
 def test_ctdg_exact_resume_two_ranks(tmp_path):
     """Each rank saves its own memory-bank rows, optimizer moments and random
     streams; a fresh session that loads them continues exactly like the

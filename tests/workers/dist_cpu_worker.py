@@ -25,6 +25,8 @@ def main():
     p.add_argument("--resume", action="store_true",
                    help="CTDG: train K1 + K2 steps, and K1 steps -> exact-resume checkpoint -> new session -> K2 steps")
     p.add_argument("--ctdg-json", default=None, help="JSON object merged into the config's ctdg section")
+    p.add_argument("--chunk", type=int, default=0,
+                   help="> 0: chunk mode with this many node clusters on a synthetic stream, then predict")
     a = p.parse_args()
     import torch
 
@@ -43,8 +45,14 @@ def main():
            "dist": {"backend": "gloo", "timeout_s": a.timeout, "heartbeat_s": a.heartbeat}}
     if a.ctdg_json:
         cfg["ctdg"].update(json.loads(a.ctdg_json))
+    if a.chunk:
+        cfg["data"] = {"root": str(Path(a.out) / "data"), "name": "dist_chunk", "format": "synthetic",
+                       "graph_mode": "chunk", "synthetic": {"preset": "tgn_cpu", "num_events": 2000}}
+        cfg["chunk"] = {"node_clusters": a.chunk, "time_slices": 4}
+        cfg["train"]["batch_size"] = 64
     s = SchedulerSession.from_config(cfg)
-    s.ctx.artifact_root = Path(a.out) / f"art_r{rank}"
+    # chunk mode: one artifact set (rank 0 writes it) whose partition files every rank reads
+    s.ctx.artifact_root = Path(a.out) / ("art" if a.chunk else f"art_r{rank}")
     initialize_distributed(s.ctx.dist)
     if a.resume:
         _resume_check(a, cfg, s, rank)
@@ -53,9 +61,24 @@ def main():
     t0 = time.time()
     outcome = {"rank": rank, "error": None}
     try:
-        s.prepare_data()
+        if a.chunk:
+            import torch.distributed as dist
+
+            if rank == 0:
+                s.prepare_data()
+            dist.barrier()
+        else:
+            s.prepare_data()
         s.build_runtime()
         r = s.run_epoch("train")
+        if a.chunk:
+            outcome["local_steps"] = r["local_steps"]
+            outcome["own_chunks"] = len(list(s.snapshot_core.iter_chunks("train")))
+            outcome["val_steps"] = s.run_epoch("val")["local_steps"]
+            ckpt = Path(a.out) / "ckpt" / "chunk.pt"
+            s.save_checkpoint(ckpt)
+            s.load_checkpoint(ckpt)  # every rank reads the file rank 0 wrote
+            outcome["predictions"] = len(s.predict("test").predictions)
         outcome["steps"] = r["steps"]
         outcome["loss"] = r["loss"]
         outcome["alphas"] = [o["meta"].get("historical_alpha") for o in r["outputs"]
