@@ -77,23 +77,32 @@ def _build_session(args: argparse.Namespace):
 def _run_prepare(args) -> None:
     s = _build_session(args)
     _log(f"[prepare] artifact_root = {s.ctx.artifact_root}")
-    s.ctx.artifact_root.mkdir(parents=True, exist_ok=True)
-    t0 = time.perf_counter()
-    s.prepare_data()
-    _log(f"[prepare] done in {time.perf_counter() - t0:.1f}s")
+
+    def body():
+        # the artifacts do not depend on the rank: rank 0 writes them while the others wait,
+        # so no rank reads a file that another is still writing
+        t0 = time.perf_counter()
+        if _rank() == 0:
+            s.ctx.artifact_root.mkdir(parents=True, exist_ok=True)
+            s.prepare_data()
+        if int(os.environ.get("WORLD_SIZE", "1")) > 1:
+            import torch.distributed as dist
+
+            dist.barrier()
+        _log(f"[prepare] done in {time.perf_counter() - t0:.1f}s")
+
+    _with_dist(s, body)
 
 
 def _with_dist(s, fn):
-    from starry_unigraph.distributed import finalize_distributed, initialize_distributed
+    """Run `fn` with the process group up. One group serves every phase of the run (the
+    first phase creates it, later ones adopt it; ``main`` tears it down at the end):
+    re-creating it between phases costs a rendezvous and can stall."""
+    from starry_unigraph.distributed import initialize_distributed
 
-    multi = int(os.environ.get("WORLD_SIZE", "1")) > 1
-    if multi:
+    if int(os.environ.get("WORLD_SIZE", "1")) > 1:
         initialize_distributed(s.ctx.dist)
-    try:
-        return fn()
-    finally:
-        if multi:
-            finalize_distributed(s.ctx.dist)
+    return fn()
 
 
 def _run_train(args) -> None:
@@ -152,12 +161,18 @@ def _run_predict(args) -> None:
 def main(argv=None) -> None:
     args = _parse_args(argv)
     _log(f"config={args.config}  phase={args.phase}")
-    if args.phase in ("prepare", "all"):
-        _run_prepare(args)
-    if args.phase in ("train", "all"):
-        _run_train(args)
-    if args.phase in ("predict", "all"):
-        _run_predict(args)
+    try:
+        if args.phase in ("prepare", "all"):
+            _run_prepare(args)
+        if args.phase in ("train", "all"):
+            _run_train(args)
+        if args.phase in ("predict", "all"):
+            _run_predict(args)
+    finally:
+        import torch.distributed as dist
+
+        if dist.is_available() and dist.is_initialized():
+            dist.destroy_process_group()
 
 
 if __name__ == "__main__":

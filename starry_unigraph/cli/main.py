@@ -23,8 +23,14 @@ from starry_unigraph.distributed import finalize_distributed, initialize_distrib
 
 
 def _prepare(session: SchedulerSession, args: argparse.Namespace) -> dict[str, Any]:
-    prepared = session.prepare_data()
-    return {"artifacts": str(prepared.meta_path.parent.parent)}
+    """Rank 0 writes the artifacts (they do not depend on the rank); the others wait."""
+    import torch.distributed as dist
+
+    if session.ctx.dist.rank == 0:
+        session.prepare_data()
+    if dist.is_available() and dist.is_initialized():
+        dist.barrier()
+    return {"artifacts": str(session.ctx.artifact_root)}
 
 
 def _train(session: SchedulerSession, args: argparse.Namespace) -> dict[str, Any]:

@@ -170,3 +170,41 @@ def test_injected_exception_surfaces(tmp_path):
     assert o0["error"] == "InjectedFault"
     o1 = _outcome(tmp_path, 1)
     assert o1["error"] is not None  # the peer stops too (heartbeat or collective timeout)
+
+
+@pytest.mark.parametrize("mode", ["dtdg", "ctdg", "chunk"])
+def test_cli_all_phases_two_ranks(tmp_path, mode):
+    """`python -m starry_unigraph --phase all` under torchrun with two gloo ranks:
+    rank 0 writes the artifacts while the other waits, one process group serves
+    prepare, train and predict, and the checkpoint is complete before any rank
+    loads it."""
+    import yaml
+
+    family = "mpnn_lstm" if mode == "dtdg" else "tgn"
+    cfg = {"model": {"name": family, "family": family, "hidden_dim": 16,
+                     "task": "snapshot_node_regression" if mode == "dtdg" else "temporal_link_prediction"},
+           "data": {"root": str(tmp_path / "data"), "name": f"cli_{mode}", "format": "mock"},
+           "train": {"epochs": 2, "batch_size": 16, "snaps": 12},
+           "runtime": {"device": "cpu", "checkpoint": str(tmp_path / "ckpt" / "cli" / "latest.pt")},
+           "graph": {"storage": "snapshots" if mode == "dtdg" else "events"},
+           "ctdg": {"dim_time": 8, "mailbox_slots": 1},
+           "dist": {"backend": "gloo", "timeout_s": 120}}
+    if mode == "chunk":
+        cfg["data"].update({"format": "synthetic", "graph_mode": "chunk",
+                            "synthetic": {"preset": "tgn_cpu", "num_events": 2000}})
+        cfg["chunk"] = {"node_clusters": 3, "time_slices": 4}
+    path = tmp_path / "cfg.yaml"
+    path.write_text(yaml.safe_dump(cfg))
+    env = dict(os.environ, PYTHONPATH=str(ROOT))
+    env.pop("CUDA_VISIBLE_DEVICES", None)
+    for _ in range(3):  # a port picked free can be taken before the rendezvous binds it
+        res = subprocess.run(["timeout", "-k", "10", "300", sys.executable, "-m", "torch.distributed.run", "--nnodes=1",
+                              "--nproc-per-node=2", "--master-addr", "127.0.0.1", "--master-port", str(_port()),
+                              "-m", "starry_unigraph", "--config", str(path), "--phase", "all",
+                              "--artifact-root", str(tmp_path / "art")], cwd=tmp_path, env=env, capture_output=True,
+                             text=True, timeout=360)
+        if res.returncode == 0 or "Address already in use" not in res.stderr:
+            break
+    assert res.returncode == 0, res.stdout[-2000:] + res.stderr[-4000:]
+    assert res.stdout.count("epoch ") == 2 and "predict done" in res.stdout
+    assert (tmp_path / "ckpt" / "cli" / "latest.pt").exists()

@@ -174,3 +174,26 @@ def test_cli_prepare_train_predict(tmp_path):
                              cwd=tmp_path, env=env, timeout=300)
         assert out.returncode == 0, out.stderr[-2000:]
     assert "MAE=" in out.stdout
+
+
+def test_subcommand_cli(tmp_path, monkeypatch, capsys):
+    """`starry-unigraph --config CFG prepare|train|predict|resume` (reference cli/main.py)."""
+    import yaml
+
+    from starry_unigraph.cli.main import main as cli_main
+
+    monkeypatch.chdir(tmp_path)  # artifacts land under ./artifacts/<data.name>
+    cfg = make_config(tmp_path, family="tgn")
+    path = tmp_path / "cfg.yaml"
+    path.write_text(yaml.safe_dump(cfg))
+    for argv in (["prepare"], ["train"], ["predict", "--split", "val"]):
+        assert cli_main(["--config", str(path), *argv]) == 0
+    lines = [json.loads(x) for x in capsys.readouterr().out.splitlines() if x.startswith("{")]
+    assert [x["command"] for x in lines] == ["prepare", "train", "predict"]
+    assert lines[1]["epochs"] == 1 and lines[2]["predictions"] > 0
+    s = SchedulerSession.from_config(cfg)
+    s.build_runtime()
+    s.run_epoch("train")
+    ckpt = s.save_checkpoint(tmp_path / "ckpt" / "resume.pt")
+    assert cli_main(["--config", str(path), "resume", "--checkpoint", str(ckpt)]) == 0
+    assert json.loads(capsys.readouterr().out.splitlines()[-1])["command"] == "resume"
