@@ -73,6 +73,7 @@ class CTDGMemoryBank:
         self.historical_cache = None
         self.last_memory_sync: tuple | None = None
         self.last_mail_sync: tuple | None = None
+        self.pulled_rows = 0  # rows refreshed from their owners by pull_remote, cumulative
 
     # ------------------------------------------------------------------ reads
     @property
@@ -287,6 +288,7 @@ class CTDGMemoryBank:
         ans = torch.empty(sum(sc), width, dtype=torch.float32, device=dev)
         dist.all_to_all_single(ans.view(-1), rows.reshape(-1).contiguous(), [c * width for c in sc],
                                [c * width for c in rc])
+        self.pulled_rows += int(ids.numel())
         if ids.numel():
             i = ids.to(self._storage_device)
             a = ans.to(self._storage_device)

@@ -116,6 +116,18 @@ class CTDGOnlineRuntime:
         split = batch.split if batch.split != "predict" else "test"
         return CTDGPreparedBatch(batch, neg, self.sampler.sample(split, roots, ts), roots, root_ts)
 
+    def _pull(self, prepared: CTDGPreparedBatch | None) -> None:
+        """Remote reads (``ctdg.remote_fetch``, several ranks): refresh the rows this step
+        reads from their owners, the roots and every sampled neighbour. A collective:
+        every rank calls it once per step, with nothing to ask for on an empty step."""
+        if prepared is None:
+            ids = torch.empty(0, dtype=torch.long)
+        elif prepared.sample is not None:
+            ids = prepared.sample.sampled_nodes
+        else:
+            ids = prepared.roots
+        self.memory.pull_remote(self.dist_ctx, ids)
+
     def _edge_feats(self) -> torch.Tensor:
         if self._edge_feat_dev is None:
             ef = self.dataset.edge_feat.float()
@@ -224,6 +236,7 @@ class CTDGOnlineRuntime:
         self.memory.wait_pending_syncs()
         wait_ms = (time.perf_counter() - t0) * 1000.0
         if batch.is_empty:
+            self._pull(None)
             self.optimizer.zero_grad(set_to_none=False)
             zero = sum(p.sum() * 0.0 for p in self._core.parameters())
             zero.backward()
@@ -235,6 +248,7 @@ class CTDGOnlineRuntime:
             res["meta"].update(sync_wait_ms=wait_ms, sync_submit_ms=0.0, step_ms=(time.perf_counter() - t0) * 1e3)
             return res
         prepared = self._prepare(batch)
+        self._pull(prepared)
         self._update_memory(batch)
         pos, neg = self._scores(prepared)
         loss = F.binary_cross_entropy_with_logits(pos, torch.ones_like(pos)) + \
@@ -265,9 +279,11 @@ class CTDGOnlineRuntime:
         self.model.eval()
         with torch.no_grad():
             if batch.is_empty:
+                self._pull(None)
                 self._submit_syncs(batch)
                 return self._empty_result(split)
             prepared = self._prepare(batch)
+            self._pull(prepared)
             self._update_memory(batch)
             pos, neg = self._scores(prepared)
             loss = F.binary_cross_entropy_with_logits(pos, torch.ones_like(pos)) + \

@@ -80,6 +80,23 @@ def test_ctdg_historical_cache_alpha(tmp_path, adaptive):
             assert set(o["alphas"]) == {0.3}
 
 
+@pytest.mark.parametrize("remote_fetch", [True, False])
+def test_ctdg_host_path_remote_reads(tmp_path, remote_fetch):
+    """Remote reads on the host path: every step refreshes the rows it reads (roots and
+    sampled neighbours) from their owners, in the same collective order on a step with
+    no events; afterwards a pull of every remote row returns the owners' rows exactly.
+    Without remote reads nothing is pulled."""
+    res = _launch(tmp_path, "tgn", None, "--ctdg-json", json.dumps({"remote_fetch": remote_fetch}))
+    assert res.returncode == 0, res.stdout[-2000:] + res.stderr[-4000:]
+    for r in range(2):
+        o = _outcome(tmp_path, r)
+        assert o["error"] is None
+        if remote_fetch:
+            assert o["pulled"] > 0 and o["pull_exact"]
+        else:
+            assert o["pulled"] == 0
+
+
 def test_chunk_mode_two_ranks_uneven_clusters(tmp_path):
     """Three node clusters on two ranks: rank 0 runs two chunks per time slice, rank 1
     one. Both take the same number of steps (rank 1 pads with empty steps), so their

@@ -83,6 +83,8 @@ def main():
         outcome["loss"] = r["loss"]
         outcome["alphas"] = [o["meta"].get("historical_alpha") for o in r["outputs"]
                              if "historical_alpha" in o.get("meta", {})]
+        if ctdg and not a.chunk:
+            outcome.update(_pull_check(s))
         model = s.runtime.model.module if hasattr(s.runtime.model, "module") else s.runtime.model
         torch.save({"params": [p.detach().clone() for p in model.parameters()], "losses":
                     [o.get("loss") for o in r["outputs"] if isinstance(o.get("loss"), float)]},
@@ -95,6 +97,25 @@ def main():
     if outcome["error"] is None:
         finalize_distributed(s.ctx.dist)
     os._exit(0 if outcome["error"] is None else 3)
+
+
+def _pull_check(s):
+    """Rows pulled during the epoch, and whether pulling every remote row now returns
+    exactly the owners' rows (after all pushes have landed)."""
+    import torch
+    import torch.distributed as dist
+
+    mem = s.ctdg_session.online_runtime.memory
+    pulled = mem.pulled_rows
+    mem.wait_pending_syncs()
+    dist.barrier()
+    if not mem.remote_fetch:
+        return {"pulled": pulled}
+    mem.pull_remote(s.ctx.dist, torch.arange(mem.num_nodes))
+    tables = [torch.zeros_like(mem.memory) for _ in range(dist.get_world_size())]
+    dist.all_gather(tables, mem.memory)
+    owners_view = torch.stack(tables)[mem.owner, torch.arange(mem.num_nodes)]
+    return {"pulled": pulled, "pull_exact": bool(torch.equal(owners_view, mem.memory))}
 
 
 def _resume_check(a, cfg, s, rank):
