@@ -1,7 +1,7 @@
 """Communication engine of the unified runtime (reference runtime/comm/comm_engine.py:35-138,
 a protocol there): asynchronous owner-routed exchange of node rows, delta push /
 poll, remote fetch and gradient all-reduce with optional int8 compression
-(per-row absmax scaling)."""
+(one absmax scale shared by all ranks; int32 sums)."""
 from __future__ import annotations
 
 from dataclasses import dataclass

@@ -225,3 +225,23 @@ def test_cli_all_phases_two_ranks(tmp_path, mode):
     assert res.returncode == 0, res.stdout[-2000:] + res.stderr[-4000:]
     assert res.stdout.count("epoch ") == 2 and "predict done" in res.stdout
     assert (tmp_path / "ckpt" / "cli" / "latest.pt").exists()
+
+
+def test_comm_engine_two_ranks(tmp_path):
+    """CommEngine (runtime/comm) on two gloo ranks: rows reach their owners, fetched
+    rows equal the owners' rows, deltas are polled once, and the gradient all-reduce
+    is the exact mean (int8: within one quantisation step)."""
+    env = dict(os.environ)
+    env.pop("CUDA_VISIBLE_DEVICES", None)
+    worker = ROOT / "tests" / "workers" / "comm_engine_worker.py"
+    for _ in range(3):  # a port picked free can be taken before the rendezvous binds it
+        res = subprocess.run(["timeout", "-k", "10", "240", sys.executable, "-m", "torch.distributed.run", "--nnodes=1",
+                              "--nproc-per-node=2", "--master-addr", "127.0.0.1", "--master-port", str(_port()),
+                              str(worker), "--out", str(tmp_path)], cwd=ROOT, env=env, capture_output=True, text=True,
+                             timeout=300)
+        if res.returncode == 0 or "Address already in use" not in res.stderr:
+            break
+    assert res.returncode == 0, res.stdout[-2000:] + res.stderr[-4000:]
+    for r in range(2):
+        checks = json.loads((tmp_path / f"outcome_r{r}.json").read_text())
+        assert all(checks.values()), checks
