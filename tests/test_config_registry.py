@@ -106,3 +106,37 @@ def test_heads_and_wrapped_model():
     assert out["pos_score"].tolist() == [3.0]
     r = NodeRegressHead(3)(torch.ones(4, 3), BatchData(mfg=None, node_ids=torch.arange(4), target_nodes=torch.tensor([0, 2])))
     assert r["node_pred"].shape == (2, 1)
+
+
+def test_config_reference_covers_every_default_key():
+    """docs/config.md names every key of default.yaml (by dotted path, a `section.*`
+    wildcard, or its leaf name in its section's table)."""
+    from pathlib import Path
+
+    from starry_unigraph.config.schema import load_default_config
+
+    doc = (Path(__file__).resolve().parents[1] / "docs" / "config.md").read_text()
+    sections = {}
+    for block in doc.split("\n## ")[1:]:
+        title, _, body = block.partition("\n")
+        sections[title.strip()] = body
+
+    def leaves(d, prefix=""):
+        for k, v in d.items():
+            path = f"{prefix}{k}"
+            if isinstance(v, dict) and v:
+                yield from leaves(v, path + ".")
+            else:
+                yield path
+
+    missing = []
+    for path in leaves(load_default_config()):
+        top, leaf = path.split(".")[0], path.split(".")[-1]
+        wild = ".".join(path.split(".")[:2]) + ".*"
+        body = next((b for t, b in sections.items() if top in t.split()), "")
+        parts = path.split(".")
+        # the path below its section, or an ancestor of it, named in the section's table
+        named = any(f"`{'.'.join(parts[1:j])}`" in body for j in range(2, len(parts) + 1))
+        if path not in doc and wild not in doc and f"`{leaf}`" not in body and not named:
+            missing.append(path)
+    assert not missing, missing
