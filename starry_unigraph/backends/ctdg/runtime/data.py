@@ -58,6 +58,8 @@ class TGTemporalDataset:
         self.src = raw.src.long()
         self.dst = raw.dst.long()
         self.ts = raw.ts.float()
+        self.weight = raw.weight.float() if raw.weight is not None and raw.weight.numel() == raw.src.numel() \
+            else torch.ones(raw.src.numel())
         self.num_nodes = int(raw.num_nodes)
         self.num_edges = int(raw.num_edges)
         self.edge_feat = raw.edge_feat if raw.edge_feat.dtype == torch.bfloat16 else raw.edge_feat.float()
@@ -142,7 +144,7 @@ class TGTemporalDataset:
                 raise KeyError(f"Unsupported CTDG split: {split}")
             idx = torch.arange(0, end, dtype=torch.long)
             self._sampler_cache[split] = {"row": self.src[idx], "col": self.dst[idx], "eid": idx,
-                                          "ts": self.ts[idx].long()}
+                                          "ts": self.ts[idx].long(), "weight": self.weight[:end]}  # a view: no copy
         return self._sampler_cache[split]
 
     def describe(self) -> dict[str, int]:

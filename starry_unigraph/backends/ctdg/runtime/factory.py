@@ -36,6 +36,10 @@ def build_ctdg_runtime(session_ctx: SessionContext, dataset: TGTemporalDataset |
         device = "cpu"
     if device == "cuda":
         device = f"cuda:{session_ctx.dist.local_rank}" if session_ctx.dist.is_distributed else "cuda:0"
+    strategy = str(cfg["sampling"]["strategy"])
+    if device.startswith("cuda") and strategy not in ("recent", "uniform"):
+        raise ValueError(f"sampling.strategy {strategy!r} runs in the host sampler only; the CUDA step samples "
+                         "'recent' or 'uniform' (use runtime.device: cpu for the other policies)")
     hidden = int(cfg["model"]["hidden_dim"])
     dctx = session_ctx.dist
     c = cfg.get("ctdg", {})
@@ -81,9 +85,10 @@ def build_ctdg_runtime(session_ctx: SessionContext, dataset: TGTemporalDataset |
         p.requires_grad_(bool(c.get("memory_grad", False)))
     sampling = cfg["sampling"]
     fanout = list(sampling["neighbor_limit"])
-    sampler = NativeTemporalSampler(dataset, fanout=fanout, history=int(sampling["history"]),
-                                    strategy=str(sampling["strategy"]), workers=max(1, min(4, dctx.local_world_size)),
-                                    device=device)
+    strategy = str(sampling["strategy"])
+    sampler = NativeTemporalSampler(dataset, fanout=fanout, history=int(sampling["history"]), strategy=strategy,
+                                    workers=max(1, min(4, dctx.local_world_size)), device=device,
+                                    boundary_p=float(sampling.get("boundary_p", 1.0)))
     lr = float(cfg.get("train", {}).get("lr", 1e-3))
     route = CTDGFeatureRoute(route_type=str(cfg["graph"]["route"]), world_size=dctx.world_size)
     engine = None

@@ -12,6 +12,13 @@ time order inside each list). On CUDA the arrays live on the device and the
 sampler is the sm_100a warp-per-root kernel; the host C++ sampler
 (``starry_unigraph._native``) and the vectorised torch fallback serve CPU runs
 and act as the oracle.
+
+``recent`` and ``uniform`` run vectorised over the T-CSR (and in the CUDA step).
+The other policies of the native sampler, ``weighted`` (draws proportional to
+the events' weights), ``boundery_recent_uniform`` and ``boundery_recent_decay``
+(remote candidates, whose event or neighbour another rank owns, kept with a
+probability), run in the host sampler on CPU and come back in the same dense
+[roots, k] block layout; the CUDA step does not implement them.
 """
 from __future__ import annotations
 
@@ -111,14 +118,20 @@ class NativeTemporalSampler:
     """
 
     def __init__(self, dataset: TGTemporalDataset, fanout: list[int], history: int, strategy: str,
-                 workers: int = 1, device: str | torch.device = "cpu"):
+                 workers: int = 1, device: str | torch.device = "cpu", boundary_p: float = 1.0):
+        from starry_unigraph.native.bts_sampler import SAMPLER_POLICIES
+
+        if strategy not in SAMPLER_POLICIES:
+            raise ValueError(f"unknown sampling strategy {strategy!r} (one of {SAMPLER_POLICIES})")
         self.dataset = dataset
         self.fanout = list(fanout)
         self.history = int(history)
         self.strategy = str(strategy)
         self.workers = int(workers)
         self.device = torch.device(device)
+        self.boundary_p = float(boundary_p)
         self._csr: dict[str, TemporalCSR] = {}
+        self._native: dict[str, object] = {}
 
     def csr(self, split: str) -> TemporalCSR:
         split = "test" if split == "predict" else split
@@ -128,7 +141,53 @@ class NativeTemporalSampler:
                                                  self.device)
         return self._csr[split]
 
+    def _native_sampler(self, split: str):
+        from starry_unigraph.native.bts_sampler import BTSNativeSampler, build_temporal_neighbor_block
+
+        split = "test" if split == "predict" else split
+        if split not in self._native:
+            g = self.dataset.sampler_graph(split)
+            tnb = build_temporal_neighbor_block(f"su_{id(self)}_{split}", g["row"], g["col"], self.dataset.num_nodes,
+                                                g["eid"], edge_weight=g["weight"], timestamp=g["ts"])
+            ds = self.dataset
+            parts = getattr(ds, "node_parts", None)
+            kw = {}
+            if parts is not None and self.strategy.startswith("boundery"):
+                kw = {"local_part": int(ds.partition_rank), "node_part": parts,
+                      "edge_part": ds.edge_parts if ds.edge_parts is not None else parts[ds.src]}
+            self._native[split] = BTSNativeSampler(tnb, ds.num_nodes, ds.num_edges, self.history, self.fanout,
+                                                   workers=self.workers, policy=self.strategy,
+                                                   probability=self.boundary_p, **kw)
+        return self._native[split]
+
+    def _sample_native(self, split: str, root_nodes: torch.Tensor, timestamps: torch.Tensor) -> CTDGSampleOutput:
+        """Host sampler, its flat per-layer output laid out as [roots, k] blocks (k = the
+        layer's fanout, or more where a boundary policy kept more)."""
+        blocks_out = self._native_sampler(split).sample_from_nodes(root_nodes.long().cpu(), timestamps.long().cpu())
+        roots = root_nodes.long().cpu()
+        blocks: list[DenseBlock] = []
+        for layer, b in enumerate(blocks_out):
+            k = self.fanout[min(layer, len(self.fanout) - 1)]
+            src = b.src_index()
+            count = torch.bincount(src, minlength=roots.numel()) if src.numel() else \
+                torch.zeros(roots.numel(), dtype=torch.long)
+            width = max(k, int(count.max()) if count.numel() else 0)
+            first = torch.cumsum(count, 0) - count
+            col = torch.arange(src.numel()) - first[src] if src.numel() else src
+            nbr = torch.full((roots.numel(), width), -1, dtype=torch.long)
+            eid = nbr.clone()
+            dt = torch.zeros(roots.numel(), width)
+            nbr[src, col] = b.sample_nodes()
+            eid[src, col] = b.eid()
+            dt[src, col] = b.delta_ts().float()
+            blocks.append(DenseBlock(roots=roots, nbr=nbr.to(self.device), eid=eid.to(self.device),
+                                     dt=dt.to(self.device), count=count.int().to(self.device)))
+            roots = b.sample_nodes()
+        return CTDGSampleOutput(split=split, root_nodes=root_nodes.long(), timestamps=timestamps.float(), blocks=blocks)
+
     def sample(self, split: str, root_nodes: torch.Tensor, timestamps: torch.Tensor) -> CTDGSampleOutput:
+        if self.strategy not in ("recent", "uniform"):
+            return self._sample_native(split, root_nodes, timestamps)
         csr = self.csr(split)
         blocks: list[DenseBlock] = []
         roots, rts = root_nodes.long(), timestamps.long()

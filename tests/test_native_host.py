@@ -148,3 +148,81 @@ def test_utils():
     assert N.sparse_get_index(torch.tensor([7, 8, 9]), torch.tensor([9, 7])).tolist() == [1, -1, 0]
     m, s = N.get_norm_temporal(torch.tensor([0, 0, 0]), torch.tensor([1, 1, 1]), torch.tensor([0.0, 2.0, 4.0]), 2)
     assert abs(m - 2.0) < 1e-9 and abs(s) < 1e-9
+
+
+def _policy_dataset(n_nodes=30, n_events=600, seed=4):
+    from types import SimpleNamespace
+
+    g = torch.Generator().manual_seed(seed)
+    src = torch.randint(0, n_nodes, (n_events,), generator=g)
+    dst = torch.randint(0, n_nodes, (n_events,), generator=g)
+    ts = torch.sort(torch.randint(0, 10_000, (n_events,), generator=g)).values
+    weight = (torch.arange(n_events) % 2).float() * torch.rand(n_events, generator=g)  # odd events only
+    graph = {"row": src, "col": dst, "eid": torch.arange(n_events), "ts": ts, "weight": weight}
+    return SimpleNamespace(num_nodes=n_nodes, num_edges=n_events, src=src, node_parts=None, edge_parts=None,
+                           partition_rank=0, sampler_graph=lambda split: graph)
+
+
+def test_session_sampler_native_layout_matches_vectorised():
+    """The host sampler's flat blocks, laid out as [roots, k], equal the vectorised
+    recent sampler over two layers."""
+    from starry_unigraph.backends.ctdg.runtime.sampler import NativeTemporalSampler
+
+    ds = _policy_dataset()
+    s = NativeTemporalSampler(ds, fanout=[4, 3], history=2, strategy="recent")
+    roots, rts = torch.arange(30), torch.full((30,), 6000)
+    a, b = s.sample("train", roots, rts), s._sample_native("train", roots, rts)
+    for x, y in zip(a.blocks, b.blocks):
+        m = x.mask()
+        assert torch.equal(x.count.long(), y.count.long())
+        assert torch.equal(x.nbr[m], y.nbr[m]) and torch.equal(x.eid[m], y.eid[m]) and torch.equal(x.dt[m], y.dt[m])
+
+
+def test_session_sampler_weighted_and_boundary_policies():
+    from starry_unigraph.backends.ctdg.runtime.sampler import NativeTemporalSampler
+
+    ds = _policy_dataset()
+    roots, rts = torch.arange(30), torch.full((30,), 9000)
+    w = NativeTemporalSampler(ds, fanout=[8], history=1, strategy="weighted").sample("train", roots, rts).blocks[0]
+    picked = w.eid[w.mask()]
+    assert picked.numel() > 0 and bool((picked % 2 == 1).all())  # zero-weight events are never drawn
+    # boundary policy: with keep probability 0 no candidate owned by the other rank survives
+    ds.node_parts = torch.arange(30) % 2
+    ds.edge_parts = ds.node_parts[ds.src]
+    blk = NativeTemporalSampler(ds, fanout=[6], history=1, strategy="boundery_recent_uniform",
+                                boundary_p=0.0).sample("train", roots, rts).blocks[0]
+    m = blk.mask()
+    assert blk.nbr[m].numel() > 0
+    assert bool((ds.node_parts[blk.nbr[m]] == 0).all()) and bool((ds.edge_parts[blk.eid[m]] == 0).all())
+    # keep probability 1: the boundary policy takes the most recent candidates (newest first)
+    full = NativeTemporalSampler(ds, fanout=[6], history=1, strategy="boundery_recent_uniform",
+                                 boundary_p=1.0).sample("train", roots, rts).blocks[0]
+    rec = NativeTemporalSampler(ds, fanout=[6], history=1, strategy="recent").sample("train", roots, rts).blocks[0]
+    assert torch.equal(full.count, rec.count)
+    for i in range(roots.numel()):
+        n = int(rec.count[i])
+        assert sorted(full.eid[i, :n].tolist()) == sorted(rec.eid[i, :n].tolist())
+    with pytest.raises(ValueError):
+        NativeTemporalSampler(ds, fanout=[6], history=1, strategy="nearest")
+
+
+def test_session_trains_with_weighted_sampling_and_cuda_guard(tmp_path, monkeypatch):
+    from starry_unigraph import SchedulerSession
+
+    cfg = {"model": {"name": "tgn", "family": "tgn", "task": "temporal_link_prediction", "hidden_dim": 16},
+           "data": {"root": str(tmp_path / "d"), "name": "w", "format": "synthetic",
+                    "synthetic": {"preset": "tgn_cpu", "num_events": 1500}},
+           "train": {"epochs": 1, "batch_size": 100}, "runtime": {"device": "cpu"},
+           "ctdg": {"dim_time": 8, "mailbox_slots": 1}, "sampling": {"strategy": "weighted"}}
+    s = SchedulerSession.from_config(cfg)
+    s.ctx.artifact_root = tmp_path / "art"
+    s.prepare_data()
+    s.build_runtime()
+    assert s.run_epoch("train")["loss"] > 0
+    # the CUDA step samples recent / uniform only: other policies are refused there, not run as uniform
+    from starry_unigraph.backends.ctdg.runtime.factory import build_ctdg_runtime
+
+    monkeypatch.setattr(torch.cuda, "is_available", lambda: True)
+    s.ctx.config["runtime"]["device"] = "cuda"
+    with pytest.raises(ValueError, match="host sampler"):
+        build_ctdg_runtime(s.ctx)
