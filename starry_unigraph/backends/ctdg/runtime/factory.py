@@ -131,8 +131,9 @@ def build_ctdg_runtime(session_ctx: SessionContext, dataset: TGTemporalDataset |
                                precision=str(cfg["runtime"].get("precision", "tf32")))
         optimizer = engine.opt
     else:
+        # host path: torch's fused CPU Adam, one pass over all parameters instead of a loop of small ops
         optimizer = torch.optim.Adam(list(model.parameters()) + [p for p in updater.parameters() if p.requires_grad],
-                                     lr=lr)
+                                     lr=lr, fused=device == "cpu")
     if dctx.is_distributed and node_parts is not None:
         shared = torch.nonzero(node_parts != dctx.rank).view(-1).to(device)
         # the configured alpha holds either way; ada_param_enabled only lets the runtime move it

@@ -62,7 +62,7 @@ class FlareOptimizer:
 
                 self._allreduce = PeerAllReduceAdam(self.flat, self.opt, device)
         else:
-            self.opt = torch.optim.Adam(model.parameters(), lr=lr)
+            self.opt = torch.optim.Adam(model.parameters(), lr=lr, fused=device.type == "cpu")
         self.param_groups = self.opt.param_groups
 
     def zero_grad(self, set_to_none: bool = False) -> None:
