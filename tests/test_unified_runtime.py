@@ -2,6 +2,7 @@
 DTDG state managers, the runners driven through the session, the spatial /
 state communication plans and the route volume summary the DTDG session
 records."""
+import pytest
 import torch
 
 from starry_unigraph import SchedulerSession
@@ -194,3 +195,70 @@ def test_hot_cache_lookup_at_large_capacity():
     assert got[0].tolist() == [4.0, -4.0] and got[2].tolist() == [299_998.0, -299_998.0]
     assert got[1].tolist() == [0.0, 0.0]
     assert cache.describe()["hits"] == 2 and cache.describe()["misses"] == 2
+
+
+def test_backend_adapters_expose_every_mode_as_chunks(tmp_path):
+    """CTDG batches, Flare windows and chunk-mode chunks all come out of their
+    GraphBackend as ChunkAtomic units whose events and T-CSR rows are the
+    runtime's own (reference tests/test_orthogonal_separation.py::test_backend_adapters)."""
+    from starry_unigraph.runtime.backend_adapters import CTDGGraphBackend, ChunkGraphBackend, FlareGraphBackend
+    from test_session import _session
+
+    s = _session(tmp_path / "c", family="tgn")
+    s.prepare_data()
+    s.build_runtime()
+    rt = s.ctdg_session.online_runtime
+    back = CTDGGraphBackend(s.ctdg_session)
+    chunks = list(back.iter_batches("train", 8))
+    batches = list(rt.iter_batches("train", 8))
+    assert len(chunks) == len(batches) and back.describe()["backend"] == "ctdg_online"
+    csr = rt.sampler.csr("train")
+    for ch, b in zip(chunks, batches):
+        assert torch.equal(ch.events["src"], b.src) and torch.equal(ch.events["eid"], b.event_ids)
+        for i, v in enumerate(ch.node_set.tolist()):
+            a, e = int(ch.tcsr_rowptr[i]), int(ch.tcsr_rowptr[i + 1])
+            lo, hi = int(csr.rowptr[v]), int(csr.rowptr[v + 1])
+            assert torch.equal(ch.tcsr_edge_id[a:e], csr.eid[lo:hi].cpu())
+    d = _session(tmp_path / "d", family="mpnn_lstm")
+    d.prepare_data()
+    d.build_runtime()
+    windows = list(FlareGraphBackend(d.snapshot_core).iter_batches("train", 1))
+    assert windows and all(w.events["graph"].num_edges() > 0 for w in windows)
+    assert all(w.num_events == w.events["graph"].num_edges() for w in windows)
+    from test_components import _chunk_session
+
+    k = _chunk_session(tmp_path / "k")
+    k.prepare_data()
+    k.build_runtime()
+    units = list(ChunkGraphBackend(k.snapshot_core).iter_batches("train", 1))
+    assert [u.chunk_id for u in units] == [c.chunk_id for c in k.snapshot_core.iter_chunks("train")]
+
+
+def test_predict_result_has_one_shape_in_every_mode(tmp_path):
+    """predict() returns PredictionResult(predictions: list of floats, targets, meta with
+    split and graph_mode) in CTDG, DTDG and chunk mode alike."""
+    from starry_unigraph.types import PredictionResult
+    from test_components import _chunk_session
+    from test_session import _session
+
+    sessions = {"ctdg": _session(tmp_path / "c", family="tgn"), "dtdg": _session(tmp_path / "d", family="tgcn"),
+                "chunk": _chunk_session(tmp_path / "k")}
+    for mode, s in sessions.items():
+        s.prepare_data()
+        s.build_runtime()
+        r = s.predict("test")
+        assert isinstance(r, PredictionResult) and r.predictions
+        assert all(isinstance(x, float) for x in r.predictions)
+        assert r.meta["split"] == "test" and r.meta["graph_mode"] in ("ctdg", "dtdg")
+        assert r.targets is None or len(r.targets) == len(r.predictions)
+
+
+def test_missing_route_manifest_fails_early(tmp_path):
+    from test_session import _session
+
+    s = _session(tmp_path, family="mpnn_lstm")
+    s.prepare_data()
+    (s.ctx.artifact_root / "routes" / "manifest.json").unlink()
+    s.prepared = None
+    with pytest.raises(FileNotFoundError, match="route"):
+        s.build_runtime()
