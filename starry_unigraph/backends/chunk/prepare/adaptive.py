@@ -50,7 +50,8 @@ def cross_cluster_ratio(src: torch.Tensor, dst: torch.Tensor, cluster: torch.Ten
 class ChunkGenerator:
     def __init__(self, num_clusters: int | None = None, time_slices: int = 16, adaptive: bool = True,
                  nodes_per_cluster: int = 100_000, seed: int = 0, info_loss_threshold: float = 0.3,
-                 max_clusters: int = 1024, decay_base: float = 0.9):
+                 max_clusters: int = 1024, decay_base: float = 0.9, edge_share: float = 0.9):
+        self.edge_share = float(edge_share)  # cluster balance: see ChunkBuilder
         self.num_clusters = num_clusters
         self.time_slices = time_slices
         self.adaptive = adaptive
@@ -67,11 +68,13 @@ class ChunkGenerator:
                                 num_clusters: int | None = None) -> tuple[torch.Tensor, int, float]:
         """(cluster of every node, cluster count, cross-cluster event fraction)."""
         n = num_clusters or self.cluster_count(num_nodes)
-        cluster = ChunkBuilder(num_clusters=n, seed=self.seed).clusters(src.long(), dst.long(), num_nodes)
+        cluster = ChunkBuilder(num_clusters=n, seed=self.seed, edge_share=self.edge_share).clusters(
+            src.long(), dst.long(), num_nodes)
         ratio = cross_cluster_ratio(src, dst, cluster)
         if self.adaptive and ratio > self.info_loss_threshold and n < self.max_clusters:
             n = min(self.max_clusters, max(n + 1, math.ceil(n * ratio / self.info_loss_threshold)))
-            cluster = ChunkBuilder(num_clusters=n, seed=self.seed).clusters(src.long(), dst.long(), num_nodes)
+            cluster = ChunkBuilder(num_clusters=n, seed=self.seed, edge_share=self.edge_share).clusters(
+                src.long(), dst.long(), num_nodes)
             ratio = cross_cluster_ratio(src, dst, cluster)
         return cluster, n, ratio
 
@@ -102,7 +105,7 @@ class ChunkGenerator:
     def generate(self, src, dst, ts, num_nodes: int, neg_per_event: int = 1, eid=None) -> dict[str, Any]:
         src, dst = src.long(), dst.long()
         cluster, n_clusters, ratio = self.generate_graph_clusters(src, dst, num_nodes)
-        builder = ChunkBuilder(n_clusters, self.time_slices, self.adaptive, seed=self.seed)
+        builder = ChunkBuilder(n_clusters, self.time_slices, self.adaptive, seed=self.seed, edge_share=self.edge_share)
         slice_of_event = builder.slice_ids(src, dst, ts)
         chunks = builder.build(src, dst, ts, num_nodes, eid=eid, slice_ids=slice_of_event, clusters=cluster)
         g = torch.Generator().manual_seed(self.seed)
@@ -110,8 +113,10 @@ class ChunkGenerator:
         for ch in chunks:
             ch.events["neg"] = pool[torch.randint(0, pool.numel(), (ch.num_events * neg_per_event,), generator=g)]
         routes = self.build_routes([c.chunk_id for c in chunks], src, dst, slice_of_event, cluster)
+        load = torch.bincount(cluster[src], minlength=n_clusters).float() if src.numel() else torch.zeros(n_clusters)
         return {"chunks": chunks, "routes": routes, "clusters": cluster, "num_clusters": n_clusters,
-                "cross_ratio": ratio, "builder": builder.describe()}
+                "cross_ratio": ratio, "builder": builder.describe() | {
+                    "events_max_over_mean": round(float(load.max() / load.mean().clamp_min(1e-9)), 4)}}
 
 
 def schedule(routes: list[DependenceRoute]) -> list[tuple[int, int]]:

@@ -17,7 +17,11 @@ from .chunk_atomic import ChunkAtomic, SpatialDeps, StateDeps
 
 class ChunkBuilder:
     def __init__(self, num_clusters: int = 8, time_slices: int = 16, adaptive: bool = False,
-                 base_batch_size: int = 1000, graph_feature: float = 0.5, seed: int = 0):
+                 base_batch_size: int = 1000, graph_feature: float = 0.5, seed: int = 0, edge_share: float = 0.9):
+        """`edge_share`: share of the partitioner's vertex weight put on event endpoints (the
+        rest on nodes), so clusters carry similar event counts: a chunk's step costs its
+        events, and on a skewed stream node-balanced clusters leave most events in one."""
+        self.edge_share = float(edge_share)
         self.num_clusters = max(1, int(num_clusters))
         self.time_slices = max(1, int(time_slices))
         self.adaptive = adaptive
@@ -40,7 +44,8 @@ class ChunkBuilder:
     def clusters(self, src, dst, num_nodes: int) -> torch.Tensor:
         from starry_unigraph.backends.dtdg.dtdg_prepare import apply_partition
 
-        return apply_partition(torch.stack([src, dst]), num_nodes, self.num_clusters, self.seed)
+        return apply_partition(torch.stack([src, dst]), num_nodes, self.num_clusters, self.seed,
+                               edge_share=self.edge_share)
 
     def build(self, src, dst, ts, num_nodes: int, eid=None, slice_ids=None, clusters=None) -> list[ChunkAtomic]:
         """Chunks of the stream; `slice_ids` (per event) and `clusters` (per node)
@@ -81,4 +86,5 @@ class ChunkBuilder:
         return out
 
     def describe(self) -> dict[str, Any]:
-        return {"num_clusters": self.num_clusters, "time_slices": self.time_slices, "adaptive": self.adaptive}
+        return {"num_clusters": self.num_clusters, "time_slices": self.time_slices, "adaptive": self.adaptive,
+                "edge_share": self.edge_share}

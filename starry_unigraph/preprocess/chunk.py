@@ -35,7 +35,8 @@ class ChunkPreprocessor(GraphPreprocessor):
         c = ctx.config.get("chunk", {})
         gen = ChunkGenerator(num_clusters=int(c.get("node_clusters", 8)), time_slices=int(c.get("time_slices", 16)),
                              adaptive=bool(c.get("adaptive", False)),
-                             info_loss_threshold=float(c.get("info_loss_threshold", 0.3)))
+                             info_loss_threshold=float(c.get("info_loss_threshold", 0.3)),
+                             edge_share=float(c.get("edge_share", 0.9)))
         out = gen.generate(ds.src, ds.dst, ds.ts, ds.num_nodes, eid=ds.event_ids)
         chunks = out["chunks"]
         W = int(ctx.config["dist"]["world_size"])

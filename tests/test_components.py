@@ -256,3 +256,19 @@ def test_chunk_complete_assembles_local_and_remote_rows():
         assert torch.equal(out.local_node_mask[m], owner[block.nbr[m]] == rank)
         filled += out.remote_manifest["filled"]
     assert filled > 0
+
+
+def test_chunk_clusters_balance_event_load():
+    """On a Zipf stream, node-balanced clusters leave most events in one cluster; the
+    default edge share balances the events each cluster (and its rank) runs."""
+    from starry_unigraph.backends.chunk.prepare import ChunkGenerator
+    from starry_unigraph.data.synthetic import ctdg_preset
+
+    st = ctdg_preset("tgn_cpu", num_events=20000)
+    skew = {}
+    for share in (0.0, None):
+        kw = {} if share is None else {"edge_share": share}
+        out = ChunkGenerator(num_clusters=4, time_slices=4, adaptive=False, **kw).generate(
+            st["src"], st["dst"], st["ts"], st["num_nodes"])
+        skew[share] = out["builder"]["events_max_over_mean"]
+    assert skew[None] < 1.5 < skew[0.0]
