@@ -73,6 +73,7 @@ class ChunkPreprocessor(GraphPreprocessor):
         for p, chunks in enumerate(parts):
             outputs.append(ArtifactOutput(f"clusters/part_{p:03d}/cluster_manifest.json",
                                           {"part": p, "chunks": [list(c.chunk_id) for c in chunks],
+                                           "chunk_events": [c.num_events for c in chunks],
                                            "events": sum(c.num_events for c in chunks)}))
             outputs.append(ArtifactOutput(f"clusters/part_{p:03d}/chunks.pt", ChunkData(chunks), serializer="torch"))
         return self.emit_artifacts(ctx, ArtifactPayload(provider_meta=meta, outputs=outputs))

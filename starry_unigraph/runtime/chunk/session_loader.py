@@ -27,9 +27,12 @@ from starry_unigraph.runtime._split import normalize_split_ratio, split_bounds
 
 class ChunkRuntimeLoader:
     def __init__(self, chunks: ChunkData, manifest: dict[str, Any], config: dict[str, Any], device: str, rank: int,
-                 world_size: int, part_chunks: list[list[tuple[int, int]]] | None = None):
-        """`part_chunks[p]` lists the chunk ids of every rank p (default: this rank's
-        only, for one-rank runs)."""
+                 world_size: int, part_chunks: list[list[tuple[int, int]]] | None = None,
+                 part_events: list[list[int]] | None = None):
+        """`part_chunks[p]` lists the chunk ids of every rank p and `part_events[p]` their
+        event counts (default: this rank's only, for one-rank runs). A chunk runs as
+        steps of at most ``train.batch_size`` events in time order; without event counts
+        (artifacts written before they were recorded) each chunk is one step."""
         self.chunks = chunks
         self.chunk_manifest = manifest
         self.config = config
@@ -38,19 +41,34 @@ class ChunkRuntimeLoader:
         self.world_size = world_size
         self.cursor = 0
         self._ctdg = None
+        self.step_events = max(1, int(config.get("train", {}).get("batch_size", 0) or 1 << 62))
         # within a slice: the preprocessor's dependence-respecting schedule when recorded
         rank_of = {tuple(cid): i for i, cid in enumerate(manifest.get("order", []))}
         mine = sorted(chunks.chunks, key=lambda c: (c.chunk_id[0], rank_of.get(tuple(c.chunk_id), len(rank_of)),
                                                      c.chunk_id[1]))
-        parts = part_chunks if part_chunks is not None else [[tuple(c.chunk_id) for c in chunks.chunks]]
-        slices = sorted({int(cid[0]) for part in parts for cid in part})
-        steps_in = {t: max(sum(1 for cid in part if int(cid[0]) == t) for part in parts) for t in slices}
+        counted = part_events is not None or part_chunks is None
+        if part_chunks is None:
+            part_chunks = [[tuple(c.chunk_id) for c in chunks.chunks]]
+            part_events = [[c.num_events for c in chunks.chunks]]
+        if not counted:
+            part_events = [[1] * len(p) for p in part_chunks]
+        size = self.step_events if counted else 1 << 62
+
+        def pieces(n: int) -> int:
+            return max(1, -(-int(n) // size))
+
+        slices = sorted({int(cid[0]) for part in part_chunks for cid in part})
+        steps_in = {t: max(sum(pieces(n) for cid, n in zip(part, ev) if int(cid[0]) == t)
+                           for part, ev in zip(part_chunks, part_events)) for t in slices}
         ratio = normalize_split_ratio(config.get("data", {}).get("split_ratio"))
         self._splits: dict[str, list[Any]] = {}
         for split in ("train", "val", "test"):
             units: list[Any] = []
             for t in slices[slice(*split_bounds(len(slices), split, ratio))] if slices else []:
-                own = [c for c in mine if c.chunk_id[0] == t]
+                own = []
+                for c in (c for c in mine if c.chunk_id[0] == t):
+                    n = c.num_events
+                    own.extend((c, lo, min(n, lo + size)) for lo in range(0, max(n, 1), size))
                 units.extend(own + [None] * (steps_in[t] - len(own)))  # None: an empty step
             self._splits[split] = units
 
@@ -66,26 +84,36 @@ class ChunkRuntimeLoader:
         routes_path = Path(prepared_dir) / "routes" / "manifest.json"
         if routes_path.exists():
             manifest["order"] = json.loads(routes_path.read_text()).get("order", [])
-        part_chunks = [[tuple(cid) for cid in json.loads((clusters / f"part_{p:03d}" / "cluster_manifest.json")
-                                                          .read_text())["chunks"]] for p in range(world_size)]
-        return cls(chunks, manifest, config, device, rank, world_size, part_chunks)
+        parts = [json.loads((clusters / f"part_{p:03d}" / "cluster_manifest.json").read_text())
+                 for p in range(world_size)]
+        part_chunks = [[tuple(cid) for cid in m["chunks"]] for m in parts]
+        part_events = [m["chunk_events"] for m in parts] if all("chunk_events" in m for m in parts) else None
+        return cls(chunks, manifest, config, device, rank, world_size, part_chunks, part_events)
 
     def attach_ctdg(self, online_runtime: Any) -> None:
         self._ctdg = online_runtime
 
-    def _batch(self, chunk, split: str) -> CTDGDataBatch:
+    def _batch(self, unit, split: str) -> CTDGDataBatch:
+        """The step of `unit`: (chunk, first event, end event), or None for a padding step
+        that takes part in the step's collectives with no events."""
         ds = self._ctdg.dataset
-        if chunk is None:  # padding step: takes part in the step's collectives with no events
+        if unit is None:
             none = torch.zeros(0, dtype=torch.long)
             return CTDGDataBatch(index=-1, split=split, event_ids=none, src=none, dst=none, ts=torch.zeros(0),
                                  edge_feat=ds.edge_feat[none])
+        chunk, lo, hi = unit if isinstance(unit, tuple) else (unit, 0, unit.num_events)
         ev = chunk.events
-        return CTDGDataBatch(index=chunk.chunk_id[0], split=split, event_ids=ev["eid"], src=ev["src"], dst=ev["dst"],
-                             ts=ev["ts"], edge_feat=ds.edge_feat[ev["eid"]])
+        eid = ev["eid"][lo:hi]
+        return CTDGDataBatch(index=chunk.chunk_id[0], split=split, event_ids=eid, src=ev["src"][lo:hi],
+                             dst=ev["dst"][lo:hi], ts=ev["ts"][lo:hi], edge_feat=ds.edge_feat[eid])
 
     def iter_chunks(self, split: str) -> Iterable[Any]:
-        """This rank's chunks of the split (without the padding steps)."""
-        yield from (c for c in self._splits["test" if split == "predict" else split] if c is not None)
+        """This rank's chunks of the split, each once (without the padding steps)."""
+        last = None
+        for u in self._splits["test" if split == "predict" else split]:
+            if u is not None and u[0] is not last:
+                last = u[0]
+                yield last
 
     def iter_train(self, split: str = "train") -> Iterable[CTDGDataBatch]:
         for ch in self._splits["train"]:

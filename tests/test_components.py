@@ -272,3 +272,26 @@ def test_chunk_clusters_balance_event_load():
             st["src"], st["dst"], st["ts"], st["num_nodes"])
         skew[share] = out["builder"]["events_max_over_mean"]
     assert skew[None] < 1.5 < skew[0.0]
+
+
+def test_chunk_loader_runs_chunks_as_batch_size_steps(tmp_path):
+    """A chunk runs as time-ordered steps of at most train.batch_size events, every event
+    of the split's chunks exactly once (the CUDA step's buffers hold one batch)."""
+    cfg = make_config(tmp_path, family="tgn")
+    cfg["data"].update({"format": "synthetic", "graph_mode": "chunk",
+                        "synthetic": {"preset": "tgn_cpu", "num_events": 3000}})
+    cfg["chunk"] = {"node_clusters": 3, "time_slices": 4}
+    cfg["train"]["batch_size"] = 16
+    s = SchedulerSession.from_config(cfg)
+    s.ctx.artifact_root = tmp_path / "art"
+    s.prepare_data()
+    s.build_runtime()
+    loader = s.snapshot_core
+    batches = list(loader.iter_train())
+    assert batches and max(b.size for b in batches) <= 16
+    got = torch.cat([b.event_ids for b in batches])
+    want = torch.cat([c.events["eid"] for c in loader.iter_chunks("train")])
+    assert torch.equal(torch.sort(got).values, torch.sort(want).values)
+    assert any(c.num_events > 16 for c in loader.iter_chunks("train"))  # some chunk took several steps
+    for b in batches:
+        assert bool((b.ts[1:] >= b.ts[:-1]).all())
