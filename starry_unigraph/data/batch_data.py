@@ -25,3 +25,4 @@ class BatchData:
     local_node_mask: Tensor | None = None
     remote_manifest: dict[str, Any] | None = None
     nbr_feat: Tensor | None = None  # [roots, k, F] feature rows of the sampled neighbours (ChunkAtomic.complete)
+    source: Any = None  # the unit (ChunkAtomic) the batch was materialised from

@@ -35,11 +35,15 @@ def _events_chunk(idx: int, src: Tensor, dst: Tensor, ts: Tensor, eid: Tensor, c
 
 
 class CTDGGraphBackend(GraphBackend):
-    def __init__(self, ctdg_session: Any):
+    def __init__(self, ctdg_session: Any, max_batch: int | None = None):
+        """`max_batch`: cap on the events per unit (the CUDA step holds one configured batch)."""
         self.session = ctdg_session
+        self.max_batch = max_batch
 
     def iter_batches(self, split: str, batch_size: int) -> Iterator[ChunkAtomic]:
         rt = self.session.online_runtime
+        if self.max_batch is not None and rt.engine is not None:
+            batch_size = min(int(batch_size), int(self.max_batch))
         csr = rt.sampler.csr("test" if split == "predict" else split)
         csr_cpu = type(csr)(csr.rowptr.cpu(), csr.nbr.cpu(), csr.eid.cpu(), csr.ts.cpu(), csr.num_nodes)
         for b in rt.iter_batches(split, batch_size):
@@ -80,7 +84,19 @@ class ChunkGraphBackend(GraphBackend):
         self.loader = chunk_loader
 
     def iter_batches(self, split: str, batch_size: int) -> Iterator[ChunkAtomic]:
-        yield from self.loader.iter_chunks(split)
+        """The loader's steps in lock-step order: each a chunk restricted to the step's
+        events (its T-CSR kept), or an empty unit for a padding step."""
+        from dataclasses import replace
+
+        split = "test" if split == "predict" else split
+        for unit in self.loader._splits[split]:
+            if unit is None:
+                z = torch.zeros(0, dtype=torch.long)
+                yield _events_chunk(-1, z, z, torch.zeros(0), z)
+                continue
+            chunk, lo, hi = unit
+            ev = chunk.events
+            yield replace(chunk, events={k: ev[k][lo:hi] for k in ("src", "dst", "ts", "eid")})
 
     def reset(self) -> None:
         return None
@@ -107,3 +123,54 @@ class DummyStateManager(StateManager):
 
     def describe(self) -> dict[str, Any]:
         return {"manager": "dummy", "calls": self.calls}
+
+
+class RuntimeStepModel:
+    """The session's runtime as the unified engine's ``TemporalModel``.
+
+    ``predict(state, batch)`` runs the mode's own step on the unit the batch was
+    materialised from (``batch.source``): the CTDG step on the unit's events (the
+    fused sm_100a step on CUDA; chunk mode steps are CTDG steps too), or the Flare
+    window step of a DTDG unit. In train mode it is a training step (forward,
+    backward, optimizer). It returns the step result, whose loss is a float and whose
+    metrics sit under ``meta``: the task adapters read both from it, and the engine
+    takes no second backward or optimizer step.
+    """
+
+    def __init__(self, session: Any):
+        self.session = session
+        self.training = True
+        self.current_split = "train"
+
+    def train(self, mode: bool = True) -> "RuntimeStepModel":
+        """Set at the start of every engine epoch. An evaluation epoch of a DTDG session
+        starts from a fresh recurrent state, as the session's own evaluation does."""
+        self.training = bool(mode)
+        runtime = getattr(self.session, "runtime", None)
+        if not mode and self.session.ctdg_session is None and runtime is not None:
+            runtime.state.pop("eval_rnn_state", None)
+        return self
+
+    def eval(self) -> "RuntimeStepModel":
+        return self.train(False)
+
+    def _ctdg_runtime(self):
+        s = self.session
+        if s.ctdg_session is not None:
+            return s.ctdg_session.online_runtime
+        return getattr(s.snapshot_core, "_ctdg", None)
+
+    def predict(self, state: Any, batch: Any) -> dict[str, Any]:
+        from starry_unigraph.backends.ctdg.runtime.data import CTDGDataBatch
+
+        unit = batch.source
+        split = "test" if self.current_split == "predict" else self.current_split
+        ev = unit.events
+        if "item" in ev:  # a Flare window
+            loader, runtime = self.session.snapshot_core, self.session.runtime
+            return loader.run_train_step(runtime, ev["item"]) if self.training else \
+                loader.run_eval_step(runtime, ev["item"])
+        rt = self._ctdg_runtime()
+        b = CTDGDataBatch(index=unit.chunk_id[0], split=split, event_ids=ev["eid"], src=ev["src"], dst=ev["dst"],
+                          ts=ev["ts"], edge_feat=rt.dataset.edge_feat[ev["eid"]])
+        return rt.train_step(b) if self.training else rt.eval_step(b, split)

@@ -27,6 +27,7 @@ class PipelineEngine:
 
     def _materialize_batch(self, chunk: Any, sample_config: Any) -> BatchData:
         batch, manifest = chunk.materialize(sample_config)
+        batch.source = chunk
         if self.feature_store is not None:
             remote = self.fetch_remote(manifest) if self.fetch_remote is not None and \
                 manifest.remote_node_ids.numel() else None
@@ -42,26 +43,30 @@ class PipelineEngine:
         is_train = split == "train"
         if hasattr(self.model, "train"):
             self.model.train(is_train)
+        if hasattr(self.model, "current_split"):
+            self.model.current_split = split
         outputs, losses, metric_acc = [], [], {}
         for batch, chunk in self.iter_batches_with_step(split, batch_size):
             state = self.state_manager.prepare(node_ids=batch.node_ids, timestamps=batch.timestamps)
             predict = getattr(self.model, "predict", None)
             if not callable(predict):
-                continue
+                raise TypeError(f"{type(self.model).__name__} has no predict(state, batch) for the engine to call")
             with torch.set_grad_enabled(is_train):
                 out = predict(state, batch)
-            if is_train:
-                loss = self.task_adapter.compute_loss(out, batch)
-                if isinstance(loss, torch.Tensor) and loss.requires_grad:
-                    if self.optimizer is not None:
-                        self.optimizer.zero_grad()
-                    loss.backward()
-                    if self.optimizer is not None:
-                        self.optimizer.step()
-                losses.append(float(loss))
+            if isinstance(out, dict) and (not out or out.get("meta", {}).get("batch_size", 1) == 0):
+                continue  # a unit that only advanced state (lock-step padding, RNN warm-up): no loss
+            loss = self.task_adapter.compute_loss(out, batch)
+            if is_train and isinstance(loss, torch.Tensor) and loss.requires_grad:
+                if self.optimizer is not None:
+                    self.optimizer.zero_grad()
+                loss.backward()
+                if self.optimizer is not None:
+                    self.optimizer.step()
+            losses.append(float(loss))
             for k, v in self.task_adapter.compute_metrics(out, batch).items():
                 metric_acc.setdefault(k, []).append(float(v))
             self.state_manager.update(out, chunk)
             outputs.append(self.task_adapter.format_output(out, batch))
-        return {"split": split, "loss": sum(losses) / len(losses) if losses else 0.0, "num_batches": len(outputs),
-                "metrics": {k: sum(v) / len(v) for k, v in metric_acc.items()}, "outputs": outputs}
+        return {"split": split, "loss": sum(losses) / len(losses) if losses else 0.0, "losses": losses,
+                "num_batches": len(outputs), "metrics": {k: sum(v) / len(v) for k, v in metric_acc.items()},
+                "outputs": outputs}

@@ -193,8 +193,11 @@ class SchedulerSession:
         self.runtime.state["halo"] = {"transport": "nvlink_p2p", "world": hc.world, "features": hc.F}
 
     def build_pipeline_engine(self, model: Any = None):
+        """The unified engine over this session's backend. Without `model` it drives the
+        session's own runtime (``RuntimeStepModel``): its epochs train and evaluate
+        exactly as ``run_epoch`` does, unit by unit."""
         from starry_unigraph.runtime.backend_adapters import (ChunkGraphBackend, CTDGGraphBackend,
-                                                              DummyStateManager, FlareGraphBackend)
+                                                              DummyStateManager, FlareGraphBackend, RuntimeStepModel)
         from starry_unigraph.runtime.engine import PipelineEngine
 
         if self.prepared is None:
@@ -205,7 +208,7 @@ class SchedulerSession:
         if mode == "ctdg":
             from starry_unigraph.runtime.state import CTDGStateManager
 
-            backend = CTDGGraphBackend(self.ctdg_session)
+            backend = CTDGGraphBackend(self.ctdg_session, max_batch=int(self.ctx.config["train"]["batch_size"]))
             state_manager = CTDGStateManager(self.ctdg_session.online_runtime.memory)
         elif mode == "dtdg":
             from starry_unigraph.runtime.state import DTDGStateManager
@@ -216,7 +219,7 @@ class SchedulerSession:
             backend = ChunkGraphBackend(self.snapshot_core)
             state_manager = DummyStateManager()
         self.pipeline_engine = PipelineEngine(backend=backend, state_manager=state_manager,
-                                              model=model or self.runtime.model or self.model_spec,
+                                              model=model if model is not None else RuntimeStepModel(self),
                                               task_adapter=self.task_adapter, device=self._device(),
                                               optimizer=self.runtime.optimizer)
         return self.pipeline_engine

@@ -262,3 +262,33 @@ def test_missing_route_manifest_fails_early(tmp_path):
     s.prepared = None
     with pytest.raises(FileNotFoundError, match="route"):
         s.build_runtime()
+
+
+@pytest.mark.parametrize("mode", ["ctdg", "dtdg", "chunk"])
+def test_pipeline_engine_trains_like_the_session(tmp_path, mode):
+    """The unified engine over a session's own runtime trains: an engine epoch gives the
+    same losses as the session's run_epoch on a twin session, and moves the parameters
+    (reference architecture: PipelineEngine x GraphBackend x TaskAdapter x StateManager)."""
+    from test_components import _chunk_session
+    from test_session import _session
+
+    def make(sub):
+        s = _chunk_session(tmp_path / sub) if mode == "chunk" else \
+            _session(tmp_path / sub, family="tgn" if mode == "ctdg" else "mpnn_lstm")
+        s.prepare_data()
+        s.build_runtime()
+        return s
+
+    a, b = make("a"), make("b")
+    before = [p.detach().clone() for p in b.runtime.model.parameters()]
+    torch.manual_seed(1)  # dropout draws from the global stream: same start for both epochs
+    ref = a.run_epoch("train")
+    eng = b.build_pipeline_engine()
+    torch.manual_seed(1)
+    out = eng.run_epoch("train", batch_size=int(b.ctx.config["train"]["batch_size"]))
+    ref_losses = [float(o["loss"]) for o in ref["outputs"] if o.get("meta", {}).get("batch_size", 1) != 0]
+    got = out["losses"]
+    assert got == pytest.approx(ref_losses, rel=1e-5) and len(got) > 0
+    assert any(not torch.equal(x, y) for x, y in zip(before, b.runtime.model.parameters()))
+    val = eng.run_epoch("val", batch_size=int(b.ctx.config["train"]["batch_size"]))
+    assert val["num_batches"] > 0 and val["loss"] > 0
