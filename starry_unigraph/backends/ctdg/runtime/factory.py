@@ -25,6 +25,18 @@ def _load_parts(session_ctx: SessionContext, name: str, flag: str):
     return torch.load(path, weights_only=True) if path.exists() else None
 
 
+def _engine_bmax(session_ctx: SessionContext, batch_size: int, world_size: int, owner_events: bool) -> int:
+    """Events the CUDA step's static buffers hold. With the owner rule a rank's share of a
+    global window varies: the largest share, as the preprocessor recorded it (in this
+    process, or in the artifacts' metadata when another process prepared them)."""
+    if world_size <= 1 or not owner_events:
+        return batch_size
+    known = session_ctx.provider_state.get("max_local_batch")
+    if known is None and session_ctx.prepared_artifacts is not None:
+        known = session_ctx.prepared_artifacts.provider_meta.get("max_local_batch")
+    return max(batch_size, int(known)) if known else 2 * batch_size
+
+
 def build_ctdg_runtime(session_ctx: SessionContext, dataset: TGTemporalDataset | None = None):
     cfg = session_ctx.config
     root = session_ctx.dataset_path or Path(cfg["data"]["root"]).expanduser().resolve()
@@ -119,9 +131,8 @@ def build_ctdg_runtime(session_ctx: SessionContext, dataset: TGTemporalDataset |
                 dist.all_reduce(flat_grad)
                 return 1.0 / world
 
-        bmax = int(cfg["train"]["batch_size"])
-        if dctx.world_size > 1 and edge_parts is not None and assignment == "owner":
-            bmax = int(session_ctx.provider_state.get("max_local_batch", bmax * 2))
+        bmax = _engine_bmax(session_ctx, int(cfg["train"]["batch_size"]), dctx.world_size,
+                            edge_parts is not None and assignment == "owner")
         engine = TGNCudaEngine(model=model, updater=updater, memory=memory, edge_feat=dataset.edge_feat,
                                neg_pool=dataset.dst_pool(), csr_provider=sampler.csr, bmax=bmax, fanout=fanout[0],
                                policy=str(sampling["strategy"]), lr=lr, dropout=float(c.get("dropout", 0.1)),

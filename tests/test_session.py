@@ -197,3 +197,24 @@ def test_subcommand_cli(tmp_path, monkeypatch, capsys):
     ckpt = s.save_checkpoint(tmp_path / "ckpt" / "resume.pt")
     assert cli_main(["--config", str(path), "resume", "--checkpoint", str(ckpt)]) == 0
     assert json.loads(capsys.readouterr().out.splitlines()[-1])["command"] == "resume"
+
+
+def test_cuda_step_batch_capacity_from_artifacts(tmp_path):
+    """With the owner rule the CUDA step's buffers hold the largest per-rank share of a
+    global window: taken from the artifacts' metadata when another process prepared
+    them (a CLI train phase after its prepare phase), not guessed."""
+    from types import SimpleNamespace
+
+    from starry_unigraph.backends.ctdg.runtime.factory import _engine_bmax
+
+    meta = SimpleNamespace(provider_meta={"max_local_batch": 37})
+    ctx = SimpleNamespace(provider_state={}, prepared_artifacts=meta)
+    assert _engine_bmax(ctx, 20, 2, True) == 37
+    assert _engine_bmax(ctx, 20, 1, True) == 20 and _engine_bmax(ctx, 20, 2, False) == 20
+    ctx.provider_state["max_local_batch"] = 41
+    assert _engine_bmax(ctx, 20, 2, True) == 41
+    assert _engine_bmax(SimpleNamespace(provider_state={}, prepared_artifacts=None), 20, 2, True) == 40
+    # the preprocessor records it for several ranks
+    s = _session(tmp_path, family="tgn", dist={"world_size": 2})
+    prepared = s.prepare_data()
+    assert prepared.provider_meta["max_local_batch"] >= 1
