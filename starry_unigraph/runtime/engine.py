@@ -62,7 +62,7 @@ class PipelineEngine:
                 loss.backward()
                 if self.optimizer is not None:
                     self.optimizer.step()
-            losses.append(float(loss))
+            losses.append(float(loss.detach()) if isinstance(loss, torch.Tensor) else float(loss))
             for k, v in self.task_adapter.compute_metrics(out, batch).items():
                 metric_acc.setdefault(k, []).append(float(v))
             self.state_manager.update(out, chunk)

@@ -113,3 +113,15 @@ def test_dtdg_example_two_gloo_ranks_match_one_rank(tmp_path):
     l1, l2 = _train_losses(one.stdout), _train_losses(two.stdout)
     assert len(l1) == len(l2) == 2
     assert l1 == pytest.approx(l2, rel=1e-4)
+
+
+def test_custom_model_through_the_engine_learns(tmp_path, monkeypatch):
+    """A user model on materialised batches with neighbour feature rows (the engine given
+    a feature store) trains through PipelineEngine to a validation AUC above 0.6."""
+    monkeypatch.chdir(tmp_path)
+    torch = pytest.importorskip("torch")
+    torch.manual_seed(0)
+    res = _example("custom_model_engine").main(["--config", str(ROOT / "configs" / "tgn_large_nvlink.yaml"),
+                                                "--events", "8000", "--batch-size", "400", "--epochs", "3",
+                                                "--artifact-root", str(tmp_path / "art")])
+    assert res["train"] and res["val"]["metrics"]["auc"] > 0.6
