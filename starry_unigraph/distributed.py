@@ -166,6 +166,9 @@ def initialize_distributed(ctx: DistributedContext) -> DistributedContext:
     on_gpu = ctx.backend == "nccl" and torch.cuda.is_available()
     if on_gpu:
         torch.cuda.set_device(ctx.local_rank)
+        # a collective that fails or outlives dist.timeout_s aborts its communicator and raises in
+        # the caller (no process teardown), so the session's own error paths run
+        os.environ.setdefault("TORCH_NCCL_ASYNC_ERROR_HANDLING", "3")
     if not dist.is_initialized():
         extra = {"device_id": torch.device("cuda", ctx.local_rank)} if on_gpu else {}
         dist.init_process_group(backend=ctx.backend, init_method=ctx.init_method, rank=ctx.rank,
