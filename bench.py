@@ -604,6 +604,12 @@ def main():
         return _reference_arm(args)
     if args.workload == "tgn_cpu":
         return _tgn_cpu_run(args)
+    import torch
+
+    if not torch.cuda.is_available():
+        print(f"bench.py: the {args.workload} workload runs on CUDA devices and none is visible here "
+              "(--workload tgn_cpu measures the CPU configuration)", file=sys.stderr)
+        return 2
     if args.workload in DTDG_WORKLOADS:
         return _mpnn_main(args)
     sys.path.insert(0, str(ROOT))

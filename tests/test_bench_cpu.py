@@ -40,3 +40,13 @@ def test_cpu_workload_line():
         assert key in line, key
     assert line["value"] > 0 and line["steps"] == 3 and line["warmup"] == 3 and line["dtype"] == "fp32"
     assert line["config"]["events"] == 157474 and line["config"]["global_batch"] == 200
+
+
+def test_gpu_workload_without_a_gpu_says_so():
+    import pytest
+    import torch
+
+    if torch.cuda.is_available():
+        pytest.skip("a CUDA device is visible: the GPU workload would run")
+    res = _run("--steps", "3", "--warmup", "3", timeout=300)
+    assert res.returncode == 2 and "CUDA" in res.stderr and "Traceback" not in res.stderr
