@@ -109,6 +109,7 @@ def test_chunk_mode_two_ranks_uneven_clusters(tmp_path):
     assert o0["local_steps"] == o1["local_steps"] and o0["val_steps"] == o1["val_steps"]
     assert o0["own_chunks"] > o1["own_chunks"] > 0
     assert o0["local_steps"] >= o0["own_chunks"]  # a chunk runs as steps of at most batch_size events
+    assert 0 < o1["engine_losses"] <= o0["engine_losses"] == o0["local_steps"]  # padding units carry no loss
     assert o0["predictions"] > 0
     p0, p1 = torch.load(tmp_path / "r0.pt"), torch.load(tmp_path / "r1.pt")
     for a, b in zip(p0["params"], p1["params"]):

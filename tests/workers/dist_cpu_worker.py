@@ -75,6 +75,9 @@ def main():
             outcome["local_steps"] = r["local_steps"]
             outcome["own_chunks"] = len(list(s.snapshot_core.iter_chunks("train")))
             outcome["val_steps"] = s.run_epoch("val")["local_steps"]
+            # the unified engine over the same runtime walks the same lock-step units
+            eng = s.build_pipeline_engine()
+            outcome["engine_losses"] = len(eng.run_epoch("train", batch_size=64)["losses"])
             ckpt = Path(a.out) / "ckpt" / "chunk.pt"
             s.save_checkpoint(ckpt)
             s.load_checkpoint(ckpt)  # every rank reads the file rank 0 wrote
