@@ -469,7 +469,8 @@ class SchedulerSession:
         """Reference keys in `path` (rank 0 writes it: all ranks hold identical
         parameters). With ``exact_resume`` (CTDG) every rank also writes
         ``<path>.rank<r>`` with its own memory-bank rows, optimizer moments and
-        random streams; all ranks must call this then."""
+        random streams. On several ranks this is a collective: every rank calls it,
+        and it returns once the files are complete."""
         path = Path(path)
         distributed = self.ctx.dist.is_distributed and dist.is_initialized()
         rank = dist.get_rank() if distributed else 0
