@@ -39,6 +39,7 @@ from __future__ import annotations
 import argparse
 import json
 import os
+import sys
 
 import torch
 import torch.distributed as dist
@@ -415,6 +416,9 @@ def main() -> None:
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--paths", default="allreduce_adam,halo_gather,writeback,remote_fetch")
     args = ap.parse_args()
+    if not torch.cuda.is_available():
+        print("bench_fused.py: the fused NVLink paths need CUDA devices and none is visible here", file=sys.stderr)
+        sys.exit(2)
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
     torch.cuda.set_device(local_rank)
     dist.init_process_group("nccl", device_id=torch.device("cuda", local_rank))

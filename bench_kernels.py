@@ -113,6 +113,9 @@ def linear() -> dict:
 
 
 if __name__ == "__main__":
+    if not torch.cuda.is_available():
+        print("bench_kernels.py: the kernels run on a CUDA device and none is visible here", file=sys.stderr)
+        sys.exit(2)
     cases = {"spmm": spmm, "lstm": lstm, "linear": linear}
     for name in (sys.argv[1:] or list(cases)):
         print(json.dumps(cases[name]()), flush=True)
