@@ -125,3 +125,27 @@ def test_custom_model_through_the_engine_learns(tmp_path, monkeypatch):
                                                 "--events", "8000", "--batch-size", "400", "--epochs", "3",
                                                 "--artifact-root", str(tmp_path / "art")])
     assert res["train"] and res["val"]["metrics"]["auc"] > 0.6
+
+
+def test_multi_gpu_launcher_on_gloo_ranks(tmp_path):
+    """examples/run_multi_gpu.sh (one torchrun call over all phases) on two CPU ranks."""
+    import yaml
+
+    cfg = {"model": {"name": "mpnn_lstm", "family": "mpnn_lstm", "task": "snapshot_node_regression",
+                     "hidden_dim": 16},
+           "data": {"root": str(tmp_path / "data"), "name": "launcher", "format": "mock"},
+           "train": {"epochs": 1, "snaps": 12},
+           "runtime": {"device": "cpu", "checkpoint": str(tmp_path / "ckpt" / "x" / "latest.pt")},
+           "graph": {"storage": "snapshots"}, "dist": {"backend": "gloo", "timeout_s": 120}}
+    (tmp_path / "c.yaml").write_text(yaml.safe_dump(cfg))
+    env = dict(os.environ, LOG_DIR=str(tmp_path / "logs"), WALL_S="300")
+    env.pop("CUDA_VISIBLE_DEVICES", None)
+    for _ in range(3):  # a port picked free can be taken before the rendezvous binds it
+        env["PORT"] = str(_port())
+        res = subprocess.run(["bash", str(ROOT / "examples" / "run_multi_gpu.sh"), str(tmp_path / "c.yaml"), "2", "all",
+                              "--artifact-root", str(tmp_path / "art")], cwd=tmp_path, env=env, capture_output=True,
+                             text=True, timeout=360)
+        if res.returncode == 0 or "Address already in use" not in res.stdout + res.stderr:
+            break
+    assert res.returncode == 0, res.stdout[-2000:] + res.stderr[-2000:]
+    assert "predict done" in res.stdout and list((tmp_path / "logs").glob("*.log"))
