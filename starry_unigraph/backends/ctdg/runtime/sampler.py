@@ -39,6 +39,15 @@ class TemporalCSR:
     eid: torch.Tensor     # [E] int64
     ts: torch.Tensor      # [E] int64 (truncated)
     num_nodes: int
+    _keys: torch.Tensor | None = None  # (node << 40) | ts per entry, built on first use
+
+    def keys(self) -> torch.Tensor:
+        """Sorted (node, ts) search keys of every entry, computed once per T-CSR."""
+        if self._keys is None:
+            node_of = torch.repeat_interleave(torch.arange(self.num_nodes, device=self.rowptr.device),
+                                              self.rowptr[1:] - self.rowptr[:-1])
+            self._keys = (node_of << _KEY_SHIFT) | self.ts
+        return self._keys
 
     @classmethod
     def build(cls, row: torch.Tensor, col: torch.Tensor, eid: torch.Tensor, ts: torch.Tensor, num_nodes: int,
@@ -60,9 +69,7 @@ class TemporalCSR:
         rts = root_ts.to(dev).long()
         lo = self.rowptr[roots]
         hi = self.rowptr[roots + 1]
-        node_of = torch.repeat_interleave(torch.arange(self.num_nodes, device=dev), self.rowptr[1:] - self.rowptr[:-1])
-        keys = (node_of << _KEY_SHIFT) | self.ts
-        end = torch.searchsorted(keys, (roots << _KEY_SHIFT) | rts, side="left")
+        end = torch.searchsorted(self.keys(), (roots << _KEY_SHIFT) | rts, side="left")
         end = torch.minimum(torch.maximum(end, lo), hi)
         avail = end - lo
         j = torch.arange(k, device=dev).unsqueeze(0)
