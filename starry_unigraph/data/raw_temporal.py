@@ -224,7 +224,11 @@ def load_raw_temporal_events(root: Path | str, dataset_name: str, config: dict[s
     events = _load_from_ctdg_csv(dataset_dir)
     if events is None:
         events = _load_from_edge_file(dataset_dir, dataset_name)
-    if events is None:
+    if events is None:  # the reference's fallback, kept; said out loud so a missing dataset is noticed
+        import warnings
+
+        warnings.warn(f"no dataset found under {dataset_dir} (edges.csv, {dataset_name}.edges or edges.txt): "
+                      "using the mock ring stream", stacklevel=2)
         return _mock_events(dataset_name, config)
     return events
 
