@@ -319,10 +319,24 @@ def run_flare_eval_step(runtime: RuntimeBundle, batch: Any, kernel_output: dict[
     if loss is not None:
         out["loss"] = float(loss.detach().item())
         if targets is not None:
-            p = torch.tensor(preds)
-            t = torch.tensor(targets)
-            out["meta"]["metrics"] = {"mae": float((p - t).abs().mean()), "rmse": float((p - t).pow(2).mean().sqrt())}
+            out["meta"]["metrics"] = _eval_metrics(runtime.state.get("task"), torch.tensor(preds),
+                                                   torch.tensor(targets))
     return out
+
+
+def _eval_metrics(task: str | None, p: torch.Tensor, t: torch.Tensor) -> dict[str, float]:
+    """Regression: MAE / RMSE. Classification: accuracy (one logit per node: positive means
+    class 1; C logits per node: the arg-max)."""
+    if t.numel() == 0:
+        return {}
+    if task == "node_classification":
+        if p.numel() == t.numel():
+            hit = (p > 0).float() == t.float()
+        else:
+            hit = p.view(t.numel(), -1).argmax(1) == t.long()
+        return {"accuracy": float(hit.float().mean())}
+    p, t = p.float(), t.float()
+    return {"mae": float((p - t).abs().mean()), "rmse": float((p - t).pow(2).mean().sqrt())}
 
 
 def run_flare_predict_step(runtime: RuntimeBundle, batch: Any, kernel_output: dict[str, Any]) -> dict[str, Any]:

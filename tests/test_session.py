@@ -218,3 +218,22 @@ def test_cuda_step_batch_capacity_from_artifacts(tmp_path):
     s = _session(tmp_path, family="tgn", dist={"world_size": 2})
     prepared = s.prepare_data()
     assert prepared.provider_meta["max_local_batch"] >= 1
+
+
+def test_dtdg_eval_metrics_follow_the_task(tmp_path):
+    """Classification runs report accuracy, regression runs MAE / RMSE."""
+    from starry_unigraph.backends.dtdg.runtime.training import _eval_metrics
+
+    assert _eval_metrics("node_classification", torch.tensor([2.0, -1.0, 0.5]), torch.tensor([1, 0, 0])) == \
+        {"accuracy": pytest.approx(2 / 3)}
+    logits = torch.tensor([[0.1, 0.9], [0.8, 0.2]]).view(-1)
+    assert _eval_metrics("node_classification", logits, torch.tensor([1, 1]))["accuracy"] == pytest.approx(0.5)
+    m = _eval_metrics("snapshot_node_regression", torch.tensor([1.0, 3.0]), torch.tensor([2.0, 3.0]))
+    assert m["mae"] == pytest.approx(0.5) and m["rmse"] == pytest.approx(0.5 ** 0.5)
+    cfg = make_config(tmp_path, family="tgcn", task="node_classification")
+    s = SchedulerSession.from_config(cfg)
+    s.ctx.artifact_root = tmp_path / "art"
+    s.prepare_data()
+    s.build_runtime()
+    s.run_epoch("train")
+    assert "accuracy" in s.run_epoch("val")["metrics"]
