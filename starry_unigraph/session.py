@@ -271,7 +271,7 @@ class SchedulerSession:
     def _summarise(self, split: str, outputs: list[dict[str, Any]], losses: list[float], elapsed: float):
         res = self._summarise_impl(split, outputs, losses, elapsed)
         self._log_metrics(epoch=self.current_epoch, split=split, steps=res["steps"], loss=res["loss"],
-                          metrics=res["metrics"], elapsed_s=res["elapsed_s"])
+                          global_loss=res["global_loss"], metrics=res["metrics"], elapsed_s=res["elapsed_s"])
         return res
 
     def _summarise_impl(self, split: str, outputs: list[dict[str, Any]], losses: list[float], elapsed: float):
