@@ -237,3 +237,17 @@ def test_dtdg_eval_metrics_follow_the_task(tmp_path):
     s.build_runtime()
     s.run_epoch("train")
     assert "accuracy" in s.run_epoch("val")["metrics"]
+
+
+def test_metrics_jsonl(tmp_path):
+    """runtime.metrics_path: one JSON line per epoch summary with the losses and metrics."""
+    path = tmp_path / "m" / "metrics.jsonl"
+    s = _session(tmp_path, family="tgn", runtime={"metrics_path": str(path)})
+    s.prepare_data()
+    s.build_runtime()
+    s.run_epoch("train")
+    s.run_epoch("val")
+    rows = [json.loads(x) for x in path.read_text().splitlines()]
+    assert [r["split"] for r in rows] == ["train", "val"]
+    assert all({"epoch", "steps", "loss", "global_loss", "metrics", "elapsed_s"} <= set(r) for r in rows)
+    assert rows[0]["loss"] > 0 and "auc" in rows[1]["metrics"]
