@@ -39,13 +39,18 @@ class CTDGGraphBackend(GraphBackend):
         """`max_batch`: cap on the events per unit (the CUDA step holds one configured batch)."""
         self.session = ctdg_session
         self.max_batch = max_batch
+        self._csr_cpu: dict[str, Any] = {}  # host copy of each split's T-CSR, made once
 
     def iter_batches(self, split: str, batch_size: int) -> Iterator[ChunkAtomic]:
         rt = self.session.online_runtime
         if self.max_batch is not None and rt.engine is not None:
             batch_size = min(int(batch_size), int(self.max_batch))
-        csr = rt.sampler.csr("test" if split == "predict" else split)
-        csr_cpu = type(csr)(csr.rowptr.cpu(), csr.nbr.cpu(), csr.eid.cpu(), csr.ts.cpu(), csr.num_nodes)
+        split = "test" if split == "predict" else split
+        if split not in self._csr_cpu:
+            csr = rt.sampler.csr(split)
+            self._csr_cpu[split] = type(csr)(csr.rowptr.cpu(), csr.nbr.cpu(), csr.eid.cpu(), csr.ts.cpu(),
+                                             csr.num_nodes)
+        csr_cpu = self._csr_cpu[split]
         for b in rt.iter_batches(split, batch_size):
             yield _events_chunk(b.index, b.src, b.dst, b.ts, b.event_ids, csr_cpu)
 
