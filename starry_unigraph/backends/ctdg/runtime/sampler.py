@@ -103,8 +103,13 @@ class CTDGSampleOutput:
 
     @property
     def sampled_nodes(self) -> torch.Tensor:
-        parts = [self.root_nodes] + [b.nbr[b.mask()] for b in self.blocks]
-        return torch.unique(torch.cat(parts))
+        """Roots and every sampled neighbour, unique (computed once: read by the remote
+        pull and by the step's description)."""
+        cached = self.__dict__.get("_sampled_nodes")
+        if cached is None:
+            parts = [self.root_nodes] + [b.nbr[b.mask()] for b in self.blocks]
+            cached = self.__dict__["_sampled_nodes"] = torch.unique(torch.cat(parts))
+        return cached
 
     @property
     def sampled_eids(self) -> torch.Tensor:
