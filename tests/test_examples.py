@@ -149,3 +149,21 @@ def test_multi_gpu_launcher_on_gloo_ranks(tmp_path):
             break
     assert res.returncode == 0, res.stdout[-2000:] + res.stderr[-2000:]
     assert "predict done" in res.stdout and list((tmp_path / "logs").glob("*.log"))
+
+
+def test_tgn_example_two_gloo_ranks(tmp_path):
+    """The CTDG example under torchrun: rank 0 prepares, both ranks train, checkpoint and test."""
+    args = ["--config", str(ROOT / "configs" / "tgn_large_nvlink.yaml"), "--device", "cpu", "--backend", "gloo",
+            "--events", "4000", "--batch-size", "200", "--epochs", "1", "--artifact-root", str(tmp_path / "art")]
+    env = dict(os.environ, PYTHONPATH=str(ROOT))
+    env.pop("CUDA_VISIBLE_DEVICES", None)
+    for _ in range(3):  # a port picked free can be taken before the rendezvous binds it
+        res = subprocess.run(["timeout", "-k", "10", "420", sys.executable, "-m", "torch.distributed.run",
+                              "--nnodes=1", "--nproc-per-node=2", "--master-addr", "127.0.0.1", "--master-port",
+                              str(_port()), str(ROOT / "examples" / "train_tgn.py"), *args], cwd=tmp_path, env=env,
+                             capture_output=True, text=True, timeout=480)
+        if res.returncode == 0 or "Address already in use" not in res.stderr:
+            break
+    assert res.returncode == 0, res.stdout[-2000:] + res.stderr[-3000:]
+    assert "events/s" in res.stdout and "[test]" in res.stdout
+    assert (tmp_path / "checkpoints" / "tgn_large" / "latest.pt").exists()
