@@ -246,3 +246,16 @@ def test_comm_engine_two_ranks(tmp_path):
     for r in range(2):
         checks = json.loads((tmp_path / f"outcome_r{r}.json").read_text())
         assert all(checks.values()), checks
+
+
+def test_ctdg_balanced_events_on_the_host_path(tmp_path):
+    """event_partition: balanced on CPU ranks: each rank takes an equal share of every
+    window (nodes it does not own included), pulls their rows from the owners and pushes
+    the updates back; the replicas stay equal and the pulled rows match the owners'."""
+    res = _launch(tmp_path, "tgn", None, "--ctdg-json", json.dumps({"event_partition": "balanced"}))
+    assert res.returncode == 0, res.stdout[-2000:] + res.stderr[-4000:]
+    o0, o1 = _outcome(tmp_path, 0), _outcome(tmp_path, 1)
+    assert o0["error"] is None and o1["error"] is None and o0["pulled"] > 0 and o0["pull_exact"] and o1["pull_exact"]
+    p0, p1 = torch.load(tmp_path / "r0.pt"), torch.load(tmp_path / "r1.pt")
+    for a, b in zip(p0["params"], p1["params"]):
+        assert torch.allclose(a, b, atol=1e-6)
